@@ -1,0 +1,319 @@
+"""Benchmark of the Qwen2 token loop on B200.
+
+Workload (one GPU): Qwen2.5-0.5B-shaped decoder, INT8 per-row linears, BF16
+embedding/tied head and BF16 KV cache, random N(0, 0.02) weights (seed 1),
+a 128-token uniform prompt (seed 1 + rank), then greedy decode at batch 1.
+A step is one decode token.  W warm-up steps, then K timed steps.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+With N > 1 (torchrun, one process per GPU) every rank decodes its own
+independent sequence (data parallel, no collectives; weak scaling); the
+timed region is bracketed by a barrier and the max over ranks is reported.
+
+`value` is device-timed decode throughput (CUDA events on the session's
+stream around K back-to-back steps, each step's argmax feeding the next on
+the device).  `e2e` is the same metric through the public generation API
+(GenerationSession.next_token: per step a 16-byte host->device control copy
+from pinned memory and an 8-byte device->host result read).  The weights
+(631 MB) exceed the 126 MB L2, so no flush is needed between steps.
+
+--impl reference times the oracle -- the C restatement of the reference
+crate's CPU arithmetic (the Rust crate cannot be built here) -- on the
+host cores with OpenMP over output rows, on a bounded sample.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+PROMPT = 128
+SEED = 1
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="native", choices=["native", "reference"])
+    ap.add_argument("--config", default="int8", choices=["int8", "bf16"])
+    ap.add_argument("--cpu-steps", type=int, default=6)
+    return ap.parse_args()
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """Samples SM clocks and throttle reasons with nvidia-smi while running."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.samples = []
+        self._stop = threading.Event()
+        self._t = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", "-i", str(self.index), "--query-gpu=" + self.FIELDS,
+                                      "--format=csv,noheader,nounits"], capture_output=True, text=True,
+                                     timeout=5).stdout.strip()
+                if out:
+                    self.samples.append([v.strip() for v in out.split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        self._t.join(timeout=10)
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit()]
+        mx = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4)
+                          if len(s) > i + 2 and s[i + 2].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+def algorithmic_bytes(cfg, linear_format, kv_bytes_per_pos, L):
+    """HBM bytes one decode step must move: every weight once, the KV of
+    all L cached positions once, the new K/V and the logits row."""
+    h, kv, ff, V = cfg.hidden_dim, cfg.kv_dim, cfg.ff_dim, cfg.vocab_size
+    mats = h * h * 2 + kv * h * 2 + ff * h * 3
+    rows = h + 2 * kv + h + 2 * ff + h
+    if linear_format == "int8":
+        lin = mats + 4 * rows
+    else:
+        lin = 2 * mats
+    per_layer = lin + 4 * (2 * h) + 4 * (h + 2 * kv)
+    table = V * h * 2
+    return cfg.layers * per_layer + table + 4 * h + L * kv_bytes_per_pos + kv_bytes_per_pos + 4 * V
+
+
+def run_reference(args, rank, world):
+    """The oracle on the host cores (OpenMP over output rows)."""
+    import numpy as np
+    from llm_inference_edu_b200 import presets, synthetic
+    from oracle import oracle
+    if rank != 0:
+        return 0
+    cfg = presets.qwen_0_5b(PROMPT + 64)
+    lf = args.config
+    w = synthetic.weights(cfg, seed=SEED, dtype="bf16")
+    om = oracle.Model(cfg, oracle.int8_model_weights(cfg, w, lf))
+    prompt = synthetic.prompt(cfg.vocab_size, PROMPT, seed=SEED)
+    sess = oracle.Session(om, PROMPT + 64, kv_bf16=(lf == "int8"), budget=0)
+    # Bounded sample: 8 prompt tokens of serial prefill, then timed decode.
+    t0 = time.perf_counter()
+    s, lg = sess.prefill(prompt[:8])
+    t_prefill = time.perf_counter() - t0
+    tok = int(np.argmax(lg))
+    for _ in range(min(args.warmup, 1)):
+        s, lg = sess.step(tok)
+        tok = int(np.argmax(lg))
+    n = max(1, min(args.steps, args.cpu_steps))
+    t0 = time.perf_counter()
+    for _ in range(n):
+        s, lg = sess.step(tok)
+        tok = int(np.argmax(lg))
+    dt = time.perf_counter() - t0
+    value = n / dt
+    cores = oracle.threads()
+    line = {
+        "impl": "reference", "metric": "decode_tok_per_s", "value": value, "unit": "tok/s",
+        "n_gpus": world, "steps": n, "warmup": args.warmup, "ms_per_step": 1000 * dt / n,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+        "data": "synthetic: N(0,0.02) weights seed 1, uniform prompt seed 1",
+        "config": {"workload": f"qwen2.5-0.5b-shape {lf} batch-1 greedy decode", "batch": 1,
+                   "prompt": PROMPT, "cpu_sample": f"8-token prefill + {n} decode steps"},
+        "prefill_tok_per_s": 8 / t_prefill,
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "port",
+                         "sample": f"{n} decode steps after an 8-token prefill (oracle, C restatement)"},
+        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_native(args, rank, world, local_rank):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import llm_inference_edu_b200 as qb
+    from llm_inference_edu_b200 import presets, synthetic
+
+    torch.cuda.set_device(local_rank)
+    lf = args.config
+    kv = "bf16" if lf == "int8" else "f32"
+    cap = PROMPT + args.warmup + args.steps + args.warmup + args.steps + 8
+    cfg = presets.qwen_0_5b(cap)
+    w = synthetic.weights(cfg, seed=SEED, dtype="bf16")
+    model = qb.Decoder(cfg, w, linear_format=lf, table_format="bf16", device=local_rank)
+    del w
+    prompt = synthetic.prompt(cfg.vocab_size, PROMPT, seed=SEED + rank)
+    sess = qb.CachedSession(model, cap, kv_dtype=kv, budget=0)
+    stream = torch.cuda.ExternalStream(sess.stream())
+
+    # Prefill (serial steps through the decode kernel), timed separately.
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    ev0.record(stream)
+    first = sess.prefill_into(prompt, None)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    prefill_ms = ev0.elapsed_time(ev1)
+
+    tok = first
+    ids = sess.decode_greedy(tok, args.warmup)
+    tok = ids[-1]
+    L0 = sess.processed()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local_rank) as clocks:
+        ev0.record(stream)
+        ids = sess.decode_greedy(tok, args.steps)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    tok = ids[-1]
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+
+    # End to end through the public generation API (host buffers).
+    gen = qb.GenerationSession(model, cap, qb.Sampling.Greedy, [], args.warmup + args.steps + 1,
+                               kv_dtype=kv, budget=0)
+    gstream = None
+    gen.start(prompt)
+    for _ in range(args.warmup):
+        gen.next_token()
+    # The generation owns its own session stream; time with wall clock
+    # bracketed by device synchronization.
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    lat = []
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        a = time.perf_counter()
+        gen.next_token()
+        lat.append(time.perf_counter() - a)
+    torch.cuda.synchronize()
+    e2e_s = time.perf_counter() - t0
+    if world > 1:
+        t = torch.tensor([e2e_s], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+
+    if rank != 0:
+        return 0
+    peak, peak_kind = measured_peaks()
+    kv_pos = cfg.layers * 2 * cfg.kv_dim * (2 if kv == "bf16" else 4)
+    Lmean = L0 + (args.steps - 1) / 2.0
+    bytes_step = algorithmic_bytes(cfg, lf, kv_pos, Lmean)
+    step_s = ms / 1000.0 / args.steps
+    achieved = bytes_step / step_s / 1e9
+    value = world * args.steps / (ms / 1000.0)
+    line = {
+        "metric": "decode_tok_per_s", "value": value, "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp32-accumulate/int8-weights" if lf == "int8" else "fp32-accumulate/bf16-weights",
+        "data": "synthetic: N(0,0.02) weights seed 1, uniform prompts seed 1+rank",
+        "config": {"workload": f"qwen2.5-0.5b-shape {lf} batch-1 greedy decode (128-token prompt)",
+                   "batch_per_gpu": 1, "prompt": PROMPT, "kv": kv, "parallelism": f"dp{world}",
+                   "l2": "weights 631 MB > 126 MB L2; no flush"},
+        "prefill_tok_per_s": PROMPT / (prefill_ms / 1000.0),
+        "ms_per_token_p50": 1000.0 * statistics.median(lat),
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": None,
+                     "bytes_per_step": bytes_step, "peak_source": peak_kind},
+        "e2e": {"value": world * args.steps / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 16,
+                "d2h_bytes_per_step": 8},
+        "gpu_launches": args.steps,
+        "clocks": clocks.summary(),
+    }
+    if world == 1:
+        line["cpu_baseline"] = cpu_baseline(args)
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def cpu_baseline(args):
+    """The oracle on the host's cores, bounded sample (few decode steps)."""
+    r, w = os.pipe()
+    cmd = [sys.executable, os.path.abspath(__file__), "--impl", "reference", "--steps",
+           str(args.cpu_steps), "--warmup", "1", "--config", args.config,
+           "--cpu-steps", str(args.cpu_steps)]
+    env = dict(os.environ)
+    for k in ("RANK", "WORLD_SIZE", "LOCAL_RANK"):
+        env.pop(k, None)
+    try:
+        out = subprocess.run(cmd, capture_output=True, text=True, timeout=900, env=env).stdout
+        d = json.loads(out.strip().splitlines()[-1])
+        cb = d["cpu_baseline"]
+        cb["prefill_tok_per_s"] = d.get("prefill_tok_per_s")
+        return cb
+    except Exception as e:  # reported, never fatal
+        return {"value": None, "unit": "tok/s", "cores": None, "kind": "port", "sample": f"failed: {e}"}
+    finally:
+        os.close(r)
+        os.close(w)
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+    if world > 1:
+        import datetime
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+    try:
+        return run_native(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,321 @@
+/*
+ * qwen_b200.h -- C ABI of the B200 (sm_100a) Qwen2 token-loop library.
+ *
+ * The library replaces the hot path of the reference crate `llm_inference`
+ * (pshevskiy/llm_inference_edu): the linear kernels, INT8 scheme, RoPE,
+ * elementwise ops, KV-cached decode step, prefill and the greedy generation
+ * loop.  Each entry point below names the reference interface it replaces
+ * (path:line within that project).
+ *
+ * Conventions, following the reference's native bridge
+ * (apple/cpu_bridge/include/llm_cpu_bridge.h:8-13):
+ *   - every function returns a uint32_t status (QB_OK = 0);
+ *   - the caller owns every buffer; no foreign pointer is retained after a
+ *     call returns (model tensors are copied to the device);
+ *   - validate-before-write: an admission error leaves every output
+ *     untouched (src/lib.rs:46-50);
+ *   - models, sessions and generation states are opaque uint64_t handles,
+ *     never reused.
+ * Pointers documented as DEVICE must be device memory on the current CUDA
+ * device; HOST pointers are ordinary host memory.  `stream` is a
+ * cudaStream_t (NULL = the legacy default stream).
+ * Token ids are uint32_t (the bridge's id type, llm_cpu_bridge.h:32).
+ */
+#ifndef QWEN_B200_H
+#define QWEN_B200_H
+#include <stddef.h>
+#include <stdint.h>
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QB_ABI_VERSION 1u
+
+/* Status codes.  1..25 mirror the reference error enums LinearError
+ * (src/lib.rs:22-30), QuantError (src/quantization.rs:3-25), OpError
+ * (src/ops.rs:5-33), RopeError (src/rope.rs:3-20) and CacheError
+ * (src/kv_cache.rs:46-62); 26.. are the generation/bridge states
+ * (src/generation.rs:83-92, llm_cpu_bridge.h:14-18) and device errors. */
+enum {
+    QB_OK = 0,
+    QB_ZERO_DIMENSION = 1,
+    QB_DIMENSION_OVERFLOW = 2,
+    QB_INVALID_LENGTH = 3,
+    QB_INVALID_GROUP_SIZE = 4,
+    QB_INVALID_SHAPE = 5,
+    QB_NONFINITE_WEIGHT = 6,
+    QB_UNREPRESENTABLE_SCALE = 7,
+    QB_ALLOCATION = 8,
+    QB_INVALID_TOKEN = 9,
+    QB_INVALID_EPSILON = 10,
+    QB_NONFINITE = 11,
+    QB_ALL_MASKED = 12,
+    QB_ODD_HEAD_DIMENSION = 13,
+    QB_POSITION_OVERFLOW = 14,
+    QB_POSITION_OUT_OF_RANGE = 15,
+    QB_INVALID_BASE = 16,
+    QB_INVALID_ANGLE = 17,
+    QB_INVALID_CAPACITY = 18,
+    QB_RESOURCE_BUDGET = 19,
+    QB_INVALID_OUTPUT_LENGTH = 20,
+    QB_EMPTY_INPUT = 21,
+    QB_NOT_EMPTY = 22,
+    QB_FULL = 23,
+    QB_INVALID_STATE = 24,
+    QB_INVALID_CONFIG = 25,
+    QB_INVALID_HANDLE = 26,
+    QB_INVALID_PARAMETERS = 27,
+    QB_NOT_STARTED = 28,
+    QB_ALREADY_STARTED = 29,
+    QB_CANCELLED = 30,
+    QB_EMPTY_LOGITS = 31,
+    QB_CUDA_ERROR = 32,
+    QB_DEVICE_TIMEOUT = 33,
+    QB_CONTEXT_LIMIT = 34,
+    QB_TRACE_LIMIT = 35,
+    QB_EMPTY_PROMPT = 36,
+    QB_OUTPUT_LIMIT = 37,
+    QB_INVALID_LAYER_COUNT = 38,
+    QB_UNSUPPORTED = 39
+};
+
+/* Detail of the calling thread's last error: which buffer (argument order),
+ * expected and actual lengths, and the offending index or id -- the payload
+ * of the reference's InvalidLength/InvalidToken/NonFinite variants. */
+typedef struct {
+    size_t buffer;
+    size_t expected;
+    size_t actual;
+    size_t index;
+} qb_detail;
+
+uint32_t qb_abi_version(void);
+const char *qb_status_name(uint32_t status);
+void qb_last_detail(qb_detail *out);
+/* The last CUDA runtime error number seen by this thread (0 if none). */
+int qb_last_cuda_error(void);
+
+/* ------------------------------------------------------------------ */
+/* Linear kernels (DEVICE buffers; lengths are element counts)         */
+/* ------------------------------------------------------------------ */
+
+/* Y[t,o] = sum_i X[t,i] * W[o,i], all row-major FP32, FP32 accumulation.
+ * Replaces `linear`, src/lib.rs:51-73 (admission src/lib.rs:76-111: zero
+ * dimension, product overflow, then exact lengths of x, w, y). */
+uint32_t qb_linear_f32(const float *x, size_t x_len, const float *w, size_t w_len, float *y,
+                       size_t y_len, size_t tokens, size_t input_dim, size_t output_dim,
+                       void *stream);
+/* Same contract as qb_linear_f32.  Replaces `linear_lanes4`,
+ * src/kernels.rs:10-28 (the tied LM-head kernel). */
+uint32_t qb_linear_lanes4_f32(const float *x, size_t x_len, const float *w, size_t w_len,
+                              float *y, size_t y_len, size_t tokens, size_t input_dim,
+                              size_t output_dim, void *stream);
+/* BF16 weights (uint16 bit patterns, value = bits << 16 as in
+ * src/weights.rs:250-251), FP32 activations and accumulation. */
+uint32_t qb_linear_bf16(const float *x, size_t x_len, const uint16_t *w, size_t w_len, float *y,
+                        size_t y_len, size_t tokens, size_t input_dim, size_t output_dim,
+                        void *stream);
+
+/* ------------------------------------------------------------------ */
+/* INT8 weight-only scheme                                             */
+/* ------------------------------------------------------------------ */
+
+/* Quantizes W[output_dim, input_dim] (DEVICE FP32) into `values`
+ * [output_dim, input_dim] int8 and `scales` [output_dim, groups_per_row]
+ * FP32, groups_per_row = ceil(input_dim / group_size), bit-exact with
+ * GroupwiseInt8::quantize, src/quantization.rs:55-116 (encode :36-40).
+ * group_size is 1..=256 (the reference's range) or equal to input_dim
+ * (one scale per output row).  Synchronizes `stream`: non-finite weights
+ * and unrepresentable scales are found before any output is written. */
+uint32_t qb_quantize_int8(const float *w, size_t w_len, size_t output_dim, size_t input_dim,
+                          size_t group_size, int8_t *values, float *scales, void *stream);
+/* y = f32(q) * scale; replaces GroupwiseInt8::dequantize,
+ * src/quantization.rs:141-166. */
+uint32_t qb_dequantize_int8(const int8_t *values, const float *scales, size_t output_dim,
+                            size_t input_dim, size_t group_size, float *y, size_t y_len,
+                            void *stream);
+/* Fused dequantizing linear: y[t,o] = sum_i x[t,i] * (f32(q[o,i]) * s[o,g(i)]).
+ * Replaces linear_int8 / linear_int8_lanes4, src/quantization.rs:168-281. */
+uint32_t qb_linear_int8(const float *x, size_t x_len, const int8_t *values, const float *scales,
+                        size_t output_dim, size_t input_dim, size_t group_size, float *y,
+                        size_t y_len, size_t tokens, void *stream);
+
+/* ------------------------------------------------------------------ */
+/* Elementwise ops (DEVICE buffers; ids are HOST)                      */
+/* Checks that read values (finiteness, masks) synchronize `stream`    */
+/* before any output is written.                                       */
+/* ------------------------------------------------------------------ */
+
+/* Replaces `embedding`, src/ops.rs:67-91. */
+uint32_t qb_embedding(const uint32_t *ids, size_t count, const float *table, size_t table_len,
+                      float *y, size_t y_len, size_t vocab_size, size_t width, void *stream);
+/* Replaces `residual_add`, src/ops.rs:97-107. */
+uint32_t qb_residual_add(const float *x, size_t x_len, const float *residual, size_t residual_len,
+                         float *y, size_t y_len, void *stream);
+/* Scaled RMSNorm; replaces `rmsnorm`, src/ops.rs:119-152. */
+uint32_t qb_rmsnorm(const float *x, size_t x_len, const float *weight, size_t weight_len, float *y,
+                    size_t y_len, size_t rows, size_t width, float epsilon, void *stream);
+/* Replaces `silu`, src/ops.rs:158-173. */
+uint32_t qb_silu(const float *x, size_t x_len, float *y, size_t y_len, void *stream);
+/* Row softmax; `mask` (DEVICE uint8, nullable) selects masked_softmax.
+ * Replaces `softmax` / `masked_softmax`, src/ops.rs:179-257. */
+uint32_t qb_softmax(const float *logits, size_t logits_len, const uint8_t *mask, size_t mask_len,
+                    float *y, size_t y_len, size_t rows, size_t width, void *stream);
+/* Split-half RoPE at absolute positions; replaces `rope`,
+ * src/rope.rs:38-105.  Angles come from a host table computed with the
+ * C library's powf/sinf/cosf, the functions the reference calls. */
+uint32_t qb_rope(const float *x, size_t x_len, float *y, size_t y_len, size_t tokens,
+                 size_t heads, size_t head_dim, size_t start_position, float base, void *stream);
+
+/* ------------------------------------------------------------------ */
+/* Model: ModelConfig / Decoder (src/model.rs:12-25,191-273)           */
+/* ------------------------------------------------------------------ */
+
+typedef struct {
+    size_t vocab_size, layers, hidden_dim, query_heads, kv_heads, head_dim, ff_dim, max_tokens;
+    float rope_base, norm_epsilon;
+} qb_model_config;
+
+/* Storage of the seven per-layer linears on the device. */
+enum {
+    QB_LINEAR_F32 = 0,       /* FP32, the reference's WeightMatrix::Float */
+    QB_LINEAR_BF16 = 1,      /* BF16 values */
+    QB_LINEAR_INT8_ROW = 2   /* int8 with one FP32 absmax scale per output row */
+};
+/* Storage of the embedding table (tied LM head) and an untied head. */
+enum { QB_TABLE_F32 = 0, QB_TABLE_BF16 = 1 };
+/* Host source element type passed to qb_model_set_tensor. */
+enum { QB_HOST_F32 = 0, QB_HOST_BF16 = 1 };
+/* Tensor ids; HF Qwen2 names in comments (src/model.rs:296-316). */
+enum {
+    QB_T_EMBEDDING = 0,   /* model.embed_tokens.weight [V,h] */
+    QB_T_LM_HEAD = 1,     /* lm_head.weight [V,h]; absent = tied */
+    QB_T_FINAL_NORM = 2,  /* model.norm.weight [h] */
+    QB_T_ATTN_NORM = 3,   /* input_layernorm.weight [h] */
+    QB_T_Q = 4,           /* self_attn.q_proj.weight [h,h] */
+    QB_T_K = 5,           /* self_attn.k_proj.weight [kv,h] */
+    QB_T_V = 6,           /* self_attn.v_proj.weight [kv,h] */
+    QB_T_O = 7,           /* self_attn.o_proj.weight [h,h] */
+    QB_T_Q_BIAS = 8,      /* self_attn.q_proj.bias [h] (optional) */
+    QB_T_K_BIAS = 9,      /* self_attn.k_proj.bias [kv] (optional) */
+    QB_T_V_BIAS = 10,     /* self_attn.v_proj.bias [kv] (optional) */
+    QB_T_FFN_NORM = 11,   /* post_attention_layernorm.weight [h] */
+    QB_T_GATE = 12,       /* mlp.gate_proj.weight [ff,h] */
+    QB_T_UP = 13,         /* mlp.up_proj.weight [ff,h] */
+    QB_T_DOWN = 14        /* mlp.down_proj.weight [h,ff] */
+};
+
+/* Starts a model on `device` (config admission as Decoder::new,
+ * src/model.rs:191-230). */
+uint32_t qb_model_create(const qb_model_config *config, uint32_t linear_format,
+                         uint32_t table_format, int device, uint64_t *out_model);
+/* Copies one HOST tensor to the device (layer = -1 for embedding,
+ * lm_head and final_norm).  Lengths and finiteness are checked as in
+ * Decoder::new, src/model.rs:232-272. */
+uint32_t qb_model_set_tensor(uint64_t model, int64_t layer, uint32_t tensor, uint32_t host_dtype,
+                             const void *data, size_t elements);
+/* Checks completeness, quantizes INT8 linears on the device and builds the
+ * decode layout.  No tensor may be set afterwards. */
+uint32_t qb_model_finalize(uint64_t model);
+/* Logical stored payload in bytes; replaces Decoder::logical_weight_bytes,
+ * src/model.rs:347-385. */
+uint32_t qb_model_logical_weight_bytes(uint64_t model, size_t *out);
+/* Device copy of one quantized linear (int8 values and scales); for
+ * bit-exact checks of the on-device quantization. */
+uint32_t qb_model_read_int8(uint64_t model, int64_t layer, uint32_t tensor, int8_t *values,
+                            size_t values_len, float *scales, size_t scales_len);
+uint32_t qb_model_free(uint64_t model);
+
+/* ------------------------------------------------------------------ */
+/* CachedSession (src/kv_cache.rs:156-475)                              */
+/* ------------------------------------------------------------------ */
+
+enum { QB_KV_F32 = 0, QB_KV_BF16 = 1 };
+
+typedef struct {
+    size_t processed, capacity, logical_bytes, workspace_bytes;
+    int32_t valid;
+} qb_session_info;
+
+/* CachedSession::new, src/kv_cache.rs:167-200.  `budget_bytes` bounds the
+ * logical KV bytes plus workspace (the reference fixes 128 MiB,
+ * src/kv_cache.rs:184-190); 0 means unbounded. */
+uint32_t qb_session_create(uint64_t model, size_t capacity, uint32_t kv_dtype,
+                           size_t budget_bytes, uint64_t *out_session);
+/* step_into, src/kv_cache.rs:306-346.  `logits` (HOST, nullable) receives
+ * the vocabulary-width logits; `argmax` (HOST, nullable) the greedy id
+ * (lowest id on ties, src/sampling.rs:65-70).  Admission errors leave the
+ * state and outputs unchanged; execution errors invalidate the session. */
+uint32_t qb_session_step(uint64_t session, uint32_t token, float *logits, size_t logits_len,
+                         uint32_t *argmax);
+/* append_into / prefill_into (require_empty = 1), src/kv_cache.rs:249-294:
+ * the whole chunk is admitted first; only the last position's logits are
+ * returned. */
+uint32_t qb_session_append(uint64_t session, const uint32_t *tokens, size_t count, float *logits,
+                           size_t logits_len, uint32_t *argmax, int32_t require_empty);
+/* reset, src/kv_cache.rs:225-229. */
+uint32_t qb_session_reset(uint64_t session);
+uint32_t qb_session_info_get(uint64_t session, qb_session_info *out);
+/* Runs `steps` greedy decode steps back to back on the device, each feeding
+ * its own argmax to the next, starting from `token`; writes the emitted ids
+ * (HOST, `steps` entries).  Equivalent to `steps` rounds of step_into +
+ * greedy sample with no stop tokens. */
+uint32_t qb_session_decode_greedy(uint64_t session, uint32_t token, size_t steps, uint32_t *ids);
+/* The CUDA stream the session launches on (for event timing). */
+uint32_t qb_session_stream(uint64_t session, void **stream);
+uint32_t qb_session_free(uint64_t session);
+
+/* ------------------------------------------------------------------ */
+/* GenerationSession (src/generation.rs:98-338), greedy policy         */
+/* ------------------------------------------------------------------ */
+
+enum { QB_STOP_NONE = 0, QB_STOP_TOKEN = 1, QB_STOP_OUTPUT_LIMIT = 2 };
+
+typedef struct {
+    size_t processed, history_len, generated, max_new;
+    int32_t stop_reason, valid, logits_ready;
+} qb_generation_info;
+
+/* GenerationSession::new, src/generation.rs:111-138. */
+uint32_t qb_generation_create(uint64_t model, size_t capacity, const uint32_t *stops,
+                              size_t stop_count, size_t max_new, uint32_t kv_dtype,
+                              size_t budget_bytes, uint64_t *out_generation);
+/* start_with_cancel, src/generation.rs:145-170; `cancel` (HOST, nullable)
+ * is polled at token boundaries (nonzero = cancelled). */
+uint32_t qb_generation_start(uint64_t generation, const uint32_t *prompt, size_t count,
+                             const volatile int32_t *cancel);
+/* next_token, src/generation.rs:307-337: *has_token = 0 once stopped. */
+uint32_t qb_generation_next_token(uint64_t generation, const volatile int32_t *cancel,
+                                  uint32_t *token, int32_t *has_token);
+/* append_context, src/generation.rs:177-218. */
+uint32_t qb_generation_append_context(uint64_t generation, const uint32_t *suffix, size_t count,
+                                      size_t max_new, const volatile int32_t *cancel);
+/* replay_history, src/generation.rs:222-257. */
+uint32_t qb_generation_replay_history(uint64_t generation, const uint32_t *history, size_t count,
+                                      size_t max_new, const volatile int32_t *cancel);
+/* reset, src/generation.rs:294-301. */
+uint32_t qb_generation_reset(uint64_t generation);
+uint32_t qb_generation_info_get(uint64_t generation, qb_generation_info *out);
+/* history, src/generation.rs:275-277: copies min(len, capacity) ids. */
+uint32_t qb_generation_history(uint64_t generation, uint32_t *ids, size_t capacity, size_t *len);
+/* prefix_logits, src/generation.rs:281-283: QB_NOT_STARTED when None. */
+uint32_t qb_generation_prefix_logits(uint64_t generation, float *logits, size_t logits_len);
+uint32_t qb_generation_free(uint64_t generation);
+
+/* ------------------------------------------------------------------ */
+/* Synthetic inputs (host only; no GPU needed)                         */
+/* ------------------------------------------------------------------ */
+
+/* Fills `out` with n normal(0, stddev) draws of the documented counter-based
+ * generator (splitmix64 + Box-Muller) for (seed, stream).  out_dtype:
+ * QB_HOST_F32 (FP32) or QB_HOST_BF16 (FP32 rounded to BF16, nearest-even). */
+uint32_t qb_synthetic_normal(uint64_t seed, uint64_t stream, size_t n, double stddev,
+                             uint32_t out_dtype, void *out);
+/* n token ids uniform over [0, vocab) for (seed, stream). */
+uint32_t qb_synthetic_tokens(uint64_t seed, uint64_t stream, size_t n, uint32_t vocab,
+                             uint32_t *out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,536 @@
+"""Python mirror of the reference crate's token-loop API over the C ABI.
+
+Names, argument meaning and error behaviour follow the Rust crate
+(pshevskiy/llm_inference_edu):
+
+  linear / linear_lanes4        src/lib.rs:51, src/kernels.rs:10
+  GroupwiseInt8, linear_int8    src/quantization.rs:27-281
+  embedding, residual_add, rmsnorm, silu, softmax, masked_softmax
+                                src/ops.rs:67-257
+  rope                          src/rope.rs:38
+  Decoder                       src/model.rs:59-340
+  CachedSession                 src/kv_cache.rs:156-475
+  GenerationSession, Sampling   src/generation.rs:98-338, src/sampling.rs
+
+Operator entry points take CUDA tensors (device buffers) and write into a
+caller-owned output, with the reference's validate-before-write rule.
+Errors raise ``QbError`` subclasses named after the Rust error enums; the
+``kind`` attribute carries the variant name (``"InvalidLength"``, ...).
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+from typing import Optional, Sequence
+
+import numpy as np
+
+from . import _lib
+from ._lib import lib
+from .presets import ModelConfig
+
+# ----------------------------------------------------------------- errors --
+
+STATUS_NAMES = [
+    "Ok", "ZeroDimension", "DimensionOverflow", "InvalidLength", "InvalidGroupSize",
+    "InvalidShape", "NonFiniteWeight", "UnrepresentableScale", "Allocation", "InvalidToken",
+    "InvalidEpsilon", "NonFinite", "AllMasked", "OddHeadDimension", "PositionOverflow",
+    "PositionOutOfRange", "InvalidBase", "InvalidAngle", "InvalidCapacity", "ResourceBudget",
+    "InvalidOutputLength", "EmptyInput", "NotEmpty", "Full", "InvalidState", "InvalidConfig",
+    "InvalidHandle", "InvalidParameters", "NotStarted", "AlreadyStarted", "Cancelled",
+    "EmptyLogits", "CudaError", "DeviceTimeout", "ContextLimit", "TraceLimit", "EmptyPrompt",
+    "OutputLimit", "InvalidLayerCount", "Unsupported"]
+
+
+class QbError(Exception):
+    """A non-zero status from the library."""
+
+    def __init__(self, status: int, detail: Optional[_lib.Detail] = None):
+        self.status = int(status)
+        self.kind = STATUS_NAMES[status] if status < len(STATUS_NAMES) else f"Status{status}"
+        self.buffer = detail.buffer if detail else None
+        self.expected = detail.expected if detail else None
+        self.actual = detail.actual if detail else None
+        self.index = detail.index if detail else None
+        extra = ""
+        if self.kind == "CudaError":
+            extra = f" (cuda error {lib().qb_last_cuda_error()})"
+        super().__init__(f"{type(self).__name__}::{self.kind}{extra}")
+
+
+class LinearError(QbError):
+    pass
+
+
+class QuantError(QbError):
+    pass
+
+
+class OpError(QbError):
+    pass
+
+
+class RopeError(QbError):
+    pass
+
+
+class ModelError(QbError):
+    pass
+
+
+class CacheError(QbError):
+    pass
+
+
+class StateError(QbError):
+    pass
+
+
+def _check(status: int, cls=QbError):
+    if status:
+        d = _lib.Detail()
+        lib().qb_last_detail(C.byref(d))
+        raise cls(status, d)
+
+
+def _ptr(t):
+    """Device pointer of a CUDA tensor (None passes NULL)."""
+    if t is None:
+        return None
+    if not t.is_cuda:
+        raise ValueError("operator buffers must be CUDA tensors")
+    if not t.is_contiguous():
+        raise ValueError("operator buffers must be contiguous")
+    return C.c_void_p(t.data_ptr())
+
+
+def _stream(stream):
+    if stream is None:
+        import torch
+        return C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    return C.c_void_p(int(stream))
+
+
+# ------------------------------------------------------------ operators --
+
+def linear(x, w, y, tokens: int, input_dim: int, output_dim: int, stream=None):
+    """Y = X W^T with FP32 accumulation (src/lib.rs:51-73); BF16 weights
+    (torch.bfloat16 / int16 bit patterns) select the BF16 kernel."""
+    import torch
+    if w.dtype in (torch.bfloat16, torch.int16, torch.uint16):
+        f = lib().qb_linear_bf16
+    else:
+        f = lib().qb_linear_f32
+    _check(f(_ptr(x), x.numel(), _ptr(w), w.numel(), _ptr(y), y.numel(), tokens, input_dim,
+             output_dim, _stream(stream)), LinearError)
+
+
+def linear_lanes4(x, w, y, tokens: int, input_dim: int, output_dim: int, stream=None):
+    """Same contract as `linear` (src/kernels.rs:10-28)."""
+    _check(lib().qb_linear_lanes4_f32(_ptr(x), x.numel(), _ptr(w), w.numel(), _ptr(y), y.numel(),
+                                      tokens, input_dim, output_dim, _stream(stream)), LinearError)
+
+
+class GroupwiseInt8:
+    """Device INT8 weights + FP32 scales (src/quantization.rs:27-166).
+
+    group_size is 1..=256 as in the reference, or equal to input_dim for one
+    absmax scale per output row."""
+
+    def __init__(self, values, scales, output_dim, input_dim, group_size):
+        self.values, self.scales = values, scales
+        self._out, self._in, self._group = output_dim, input_dim, group_size
+
+    @classmethod
+    def quantize(cls, weights, output_dim: int, input_dim: int, group_size: int, stream=None):
+        import torch
+        gpr = -(-input_dim // group_size) if group_size else 0
+        n = output_dim * input_dim if output_dim and input_dim else 0
+        dev = weights.device if weights.is_cuda else torch.device("cuda")
+        values = torch.empty(max(n, 1), dtype=torch.int8, device=dev)
+        scales = torch.empty(max(output_dim * gpr, 1), dtype=torch.float32, device=dev)
+        _check(lib().qb_quantize_int8(_ptr(weights), weights.numel(), output_dim, input_dim,
+                                      group_size, _ptr(values), _ptr(scales), _stream(stream)),
+               QuantError)
+        return cls(values, scales, output_dim, input_dim, group_size)
+
+    def output_dim(self):
+        return self._out
+
+    def input_dim(self):
+        return self._in
+
+    def group_size(self):
+        return self._group
+
+    def groups_per_row(self):
+        return -(-self._in // self._group)
+
+    def logical_bytes(self):
+        return self._out * self._in + 4 * self._out * self.groups_per_row()
+
+    def dequantize(self, output, stream=None):
+        _check(lib().qb_dequantize_int8(_ptr(self.values), _ptr(self.scales), self._out, self._in,
+                                        self._group, _ptr(output), output.numel(), _stream(stream)),
+               QuantError)
+
+
+def linear_int8(x, weights: GroupwiseInt8, y, tokens: int, stream=None):
+    """Fused dequantizing linear (src/quantization.rs:168-215)."""
+    _check(lib().qb_linear_int8(_ptr(x), x.numel(), _ptr(weights.values), _ptr(weights.scales),
+                                weights._out, weights._in, weights._group, _ptr(y), y.numel(),
+                                tokens, _stream(stream)), QuantError)
+
+
+linear_int8_lanes4 = linear_int8
+
+
+def embedding(token_ids: Sequence[int], table, y, vocab_size: int, width: int, stream=None):
+    ids = np.ascontiguousarray(np.asarray(token_ids, dtype=np.uint64))
+    if ids.size and int(ids.max()) >= 2**32:
+        ids32 = np.full(ids.size, 0xFFFFFFFF, dtype=np.uint32)
+    else:
+        ids32 = ids.astype(np.uint32)
+    _check(lib().qb_embedding(ids32.ctypes.data_as(C.c_void_p), ids32.size, _ptr(table),
+                              table.numel(), _ptr(y), y.numel(), vocab_size, width,
+                              _stream(stream)), OpError)
+
+
+def residual_add(x, residual, y, stream=None):
+    _check(lib().qb_residual_add(_ptr(x), x.numel(), _ptr(residual), residual.numel(), _ptr(y),
+                                 y.numel(), _stream(stream)), OpError)
+
+
+def rmsnorm(x, weight, y, rows: int, width: int, epsilon: float, stream=None):
+    _check(lib().qb_rmsnorm(_ptr(x), x.numel(), _ptr(weight), weight.numel(), _ptr(y), y.numel(),
+                            rows, width, epsilon, _stream(stream)), OpError)
+
+
+def silu(x, y, stream=None):
+    _check(lib().qb_silu(_ptr(x), x.numel(), _ptr(y), y.numel(), _stream(stream)), OpError)
+
+
+def softmax(logits, y, rows: int, width: int, stream=None):
+    _check(lib().qb_softmax(_ptr(logits), logits.numel(), None, 0, _ptr(y), y.numel(), rows, width,
+                            _stream(stream)), OpError)
+
+
+def masked_softmax(logits, mask, y, rows: int, width: int, stream=None):
+    _check(lib().qb_softmax(_ptr(logits), logits.numel(), _ptr(mask), mask.numel(), _ptr(y),
+                            y.numel(), rows, width, _stream(stream)), OpError)
+
+
+def rope(x, y, tokens: int, heads: int, head_dim: int, start_position: int, base: float,
+         stream=None):
+    _check(lib().qb_rope(_ptr(x), x.numel(), _ptr(y), y.numel(), tokens, heads, head_dim,
+                         start_position, base, _stream(stream)), RopeError)
+
+
+# ---------------------------------------------------------------- model --
+
+LINEAR_FORMATS = {"f32": 0, "bf16": 1, "int8": 2}
+TABLE_FORMATS = {"f32": 0, "bf16": 1}
+_T = {"embedding": 0, "lm_head": 1, "final_norm": 2, "attn_norm": 3, "q": 4, "k": 5, "v": 6,
+      "o": 7, "q_bias": 8, "k_bias": 9, "v_bias": 10, "ffn_norm": 11, "gate": 12, "up": 13,
+      "down": 14}
+
+
+class Decoder:
+    """A device-resident model (src/model.rs:59-340).
+
+    ``weights`` is the host weight dictionary of ``synthetic.weights`` /
+    ``presets.tiny_r_weights``: matrices are float32 arrays or uint16 BF16
+    bit patterns.  ``linear_format`` stores the seven per-layer linears as
+    "f32", "bf16" or "int8" (per-row absmax, quantized on the device with the
+    reference's encode); ``table_format`` stores the embedding/LM-head table
+    as "f32" or "bf16"."""
+
+    def __init__(self, config: ModelConfig, weights: dict, linear_format: str = "f32",
+                 table_format: str = "f32", device: int = 0):
+        self.config = config
+        self.linear_format = linear_format
+        self.table_format = table_format
+        c = _lib.ModelConfigC(config.vocab_size, config.layers, config.hidden_dim,
+                              config.query_heads, config.kv_heads, config.head_dim, config.ff_dim,
+                              config.max_tokens, config.rope_base, config.norm_epsilon)
+        h = C.c_uint64()
+        _check(lib().qb_model_create(C.byref(c), LINEAR_FORMATS[linear_format],
+                                     TABLE_FORMATS[table_format], device, C.byref(h)), ModelError)
+        self.handle = h.value
+        try:
+            self._set(-1, "embedding", weights["embedding"])
+            if weights.get("lm_head") is not None:
+                self._set(-1, "lm_head", weights["lm_head"])
+            self._set(-1, "final_norm", weights["final_norm"])
+            for i, layer in enumerate(weights["layers"]):
+                for k, v in layer.items():
+                    if v is not None:
+                        self._set(i, k, v)
+            _check(lib().qb_model_finalize(self.handle), ModelError)
+        except Exception:
+            lib().qb_model_free(self.handle)
+            self.handle = None
+            raise
+
+    def _set(self, layer, name, arr):
+        a = np.ascontiguousarray(arr)
+        if a.dtype == np.uint16:
+            dt = 1
+        else:
+            a = np.ascontiguousarray(a, dtype=np.float32)
+            dt = 0
+        _check(lib().qb_model_set_tensor(self.handle, layer, _T[name], dt,
+                                         a.ctypes.data_as(C.c_void_p), a.size), ModelError)
+
+    def __del__(self):
+        if getattr(self, "handle", None):
+            lib().qb_model_free(self.handle)
+            self.handle = None
+
+    def logical_weight_bytes(self) -> int:
+        n = C.c_size_t()
+        _check(lib().qb_model_logical_weight_bytes(self.handle, C.byref(n)), ModelError)
+        return n.value
+
+    def read_int8(self, layer: int, name: str):
+        """Device INT8 values [rows, cols] and row scales of one linear."""
+        c = self.config
+        rows, cols = {"q": (c.hidden_dim, c.hidden_dim), "k": (c.kv_dim, c.hidden_dim),
+                      "v": (c.kv_dim, c.hidden_dim), "o": (c.hidden_dim, c.hidden_dim),
+                      "gate": (c.ff_dim, c.hidden_dim), "up": (c.ff_dim, c.hidden_dim),
+                      "down": (c.hidden_dim, c.ff_dim)}[name]
+        v = np.zeros(rows * cols, dtype=np.int8)
+        s = np.zeros(rows, dtype=np.float32)
+        _check(lib().qb_model_read_int8(self.handle, layer, _T[name], v.ctypes.data_as(C.c_void_p),
+                                        v.size, s.ctypes.data_as(C.c_void_p), s.size), ModelError)
+        return v.reshape(rows, cols), s
+
+
+# -------------------------------------------------------------- session --
+
+KV_DTYPES = {"f32": 0, "bf16": 1}
+REFERENCE_BUDGET = 128 * 1024 * 1024
+
+
+class CachedSession:
+    """KV-cached decoding state bound to one Decoder (src/kv_cache.rs:156-475).
+
+    ``budget`` bounds logical KV + workspace bytes like the reference's fixed
+    128 MiB (src/kv_cache.rs:184-190); pass 0 for no bound."""
+
+    def __init__(self, model: Decoder, capacity: int, kv_dtype: str = "f32",
+                 budget: int = REFERENCE_BUDGET):
+        self.model = model
+        h = C.c_uint64()
+        _check(lib().qb_session_create(model.handle, capacity, KV_DTYPES[kv_dtype], budget,
+                                       C.byref(h)), CacheError)
+        self.handle = h.value
+        self.vocab = model.config.vocab_size
+
+    def __del__(self):
+        if getattr(self, "handle", None):
+            lib().qb_session_free(self.handle)
+            self.handle = None
+
+    def _info(self):
+        i = _lib.SessionInfo()
+        _check(lib().qb_session_info_get(self.handle, C.byref(i)), CacheError)
+        return i
+
+    def processed(self) -> int:
+        return self._info().processed
+
+    def capacity(self) -> int:
+        return self._info().capacity
+
+    def is_valid(self) -> bool:
+        return bool(self._info().valid)
+
+    def logical_bytes(self) -> int:
+        return self._info().logical_bytes
+
+    def workspace_bytes(self) -> int:
+        return self._info().workspace_bytes
+
+    def reset(self):
+        _check(lib().qb_session_reset(self.handle), CacheError)
+
+    def step_into(self, token: int, logits: Optional[np.ndarray]) -> int:
+        """Evaluates one token; fills `logits` (float32, vocab width) if given
+        and returns the greedy id."""
+        am = C.c_uint32()
+        if token < 0 or token >= 2**32:
+            raise CacheError(9)
+        lp = None if logits is None else logits.ctypes.data_as(C.c_void_p)
+        _check(lib().qb_session_step(self.handle, token, lp, 0 if logits is None else logits.size,
+                                     C.byref(am)), CacheError)
+        return am.value
+
+    def step(self, token: int) -> np.ndarray:
+        logits = np.zeros(self.vocab, dtype=np.float32)
+        self.step_into(token, logits)
+        return logits
+
+    def append_into(self, tokens: Sequence[int], logits: Optional[np.ndarray],
+                    require_empty: bool = False) -> int:
+        ids = np.ascontiguousarray(np.asarray(list(tokens), dtype=np.int64))
+        if ids.size and (ids.min() < 0 or ids.max() >= 2**32):
+            raise CacheError(9)
+        ids = ids.astype(np.uint32)
+        am = C.c_uint32()
+        lp = None if logits is None else logits.ctypes.data_as(C.c_void_p)
+        _check(lib().qb_session_append(self.handle, ids.ctypes.data_as(C.c_void_p) if ids.size else None,
+                                       ids.size, lp, 0 if logits is None else logits.size,
+                                       C.byref(am), int(require_empty)), CacheError)
+        return am.value
+
+    def prefill_into(self, tokens, logits) -> int:
+        return self.append_into(tokens, logits, True)
+
+    def append(self, tokens) -> np.ndarray:
+        logits = np.zeros(self.vocab, dtype=np.float32)
+        self.append_into(tokens, logits)
+        return logits
+
+    def prefill(self, tokens) -> np.ndarray:
+        logits = np.zeros(self.vocab, dtype=np.float32)
+        self.append_into(tokens, logits, True)
+        return logits
+
+    def decode_greedy(self, token: int, steps: int) -> list:
+        """`steps` greedy steps on the device, each fed its own argmax."""
+        out = np.zeros(steps, dtype=np.uint32)
+        _check(lib().qb_session_decode_greedy(self.handle, token, steps,
+                                              out.ctypes.data_as(C.c_void_p)), CacheError)
+        return [int(v) for v in out]
+
+    def stream(self) -> int:
+        p = C.c_void_p()
+        _check(lib().qb_session_stream(self.handle, C.byref(p)), CacheError)
+        return p.value or 0
+
+
+# ----------------------------------------------------------- generation --
+
+class Sampling:
+    """Sampling policy.  The device token loop implements Greedy
+    (src/sampling.rs:57-70)."""
+    Greedy = "greedy"
+
+
+STOP_REASONS = {0: None, 1: "StopToken", 2: "OutputLimit"}
+
+
+class CancelFlag:
+    """Cooperative cancellation flag (the reference's &AtomicBool)."""
+
+    def __init__(self, value: bool = False):
+        self._v = C.c_int32(int(value))
+
+    def store(self, value: bool):
+        self._v.value = int(value)
+
+    def load(self) -> bool:
+        return bool(self._v.value)
+
+    def ref(self):
+        return C.byref(self._v)
+
+
+class GenerationSession:
+    """History plus KV-cached greedy generation (src/generation.rs:98-338)."""
+
+    def __init__(self, model: Decoder, capacity: int, policy=Sampling.Greedy,
+                 stops: Sequence[int] = (), max_new: int = 1, kv_dtype: str = "f32",
+                 budget: int = REFERENCE_BUDGET):
+        if policy != Sampling.Greedy:
+            raise StateError(27)
+        st = np.ascontiguousarray(np.asarray(list(stops), dtype=np.int64))
+        if st.size and (st.min() < 0 or st.max() >= 2**32):
+            raise StateError(27)
+        st = st.astype(np.uint32)
+        h = C.c_uint64()
+        _check(lib().qb_generation_create(model.handle, capacity,
+                                          st.ctypes.data_as(C.c_void_p) if st.size else None,
+                                          st.size, max_new, KV_DTYPES[kv_dtype], budget,
+                                          C.byref(h)), StateError)
+        self.handle = h.value
+        self.vocab = model.config.vocab_size
+
+    def __del__(self):
+        if getattr(self, "handle", None):
+            lib().qb_generation_free(self.handle)
+            self.handle = None
+
+    @staticmethod
+    def _ids(ids):
+        a = np.ascontiguousarray(np.asarray(list(ids), dtype=np.int64))
+        if a.size and (a.min() < 0 or a.max() >= 2**32):
+            a = np.full(a.size, 0xFFFFFFFF, dtype=np.int64)
+        return a.astype(np.uint32)
+
+    @staticmethod
+    def _cancel(cancel):
+        return None if cancel is None else cancel.ref()
+
+    def start(self, prompt):
+        self.start_with_cancel(prompt, None)
+
+    def start_with_cancel(self, prompt, cancel: Optional[CancelFlag]):
+        p = self._ids(prompt)
+        _check(lib().qb_generation_start(self.handle, p.ctypes.data_as(C.c_void_p) if p.size else None,
+                                         p.size, self._cancel(cancel)), StateError)
+
+    def next_token(self, cancel: Optional[CancelFlag] = None) -> Optional[int]:
+        tok, has = C.c_uint32(), C.c_int32()
+        _check(lib().qb_generation_next_token(self.handle, self._cancel(cancel), C.byref(tok),
+                                              C.byref(has)), StateError)
+        return tok.value if has.value else None
+
+    def append_context(self, suffix, max_new: int, cancel: Optional[CancelFlag] = None):
+        s = self._ids(suffix)
+        _check(lib().qb_generation_append_context(self.handle,
+                                                  s.ctypes.data_as(C.c_void_p) if s.size else None,
+                                                  s.size, max_new, self._cancel(cancel)), StateError)
+
+    def replay_history(self, history, max_new: int, cancel: Optional[CancelFlag] = None):
+        s = self._ids(history)
+        _check(lib().qb_generation_replay_history(self.handle,
+                                                  s.ctypes.data_as(C.c_void_p) if s.size else None,
+                                                  s.size, max_new, self._cancel(cancel)), StateError)
+
+    def reset(self):
+        _check(lib().qb_generation_reset(self.handle), StateError)
+
+    def _info(self):
+        i = _lib.GenerationInfo()
+        _check(lib().qb_generation_info_get(self.handle, C.byref(i)), StateError)
+        return i
+
+    def history(self) -> list:
+        n = C.c_size_t()
+        _check(lib().qb_generation_history(self.handle, None, 0, C.byref(n)), StateError)
+        out = np.zeros(max(n.value, 1), dtype=np.uint32)
+        _check(lib().qb_generation_history(self.handle, out.ctypes.data_as(C.c_void_p), n.value,
+                                           C.byref(n)), StateError)
+        return [int(v) for v in out[:n.value]]
+
+    def processed(self) -> int:
+        return self._info().processed
+
+    def generated(self) -> int:
+        return self._info().generated
+
+    def is_valid(self) -> bool:
+        return bool(self._info().valid)
+
+    def stop_reason(self):
+        return STOP_REASONS[self._info().stop_reason]
+
+    def prefix_logits(self) -> Optional[np.ndarray]:
+        out = np.zeros(self.vocab, dtype=np.float32)
+        st = lib().qb_generation_prefix_logits(self.handle, out.ctypes.data_as(C.c_void_p), out.size)
+        if st == 28:
+            return None
+        _check(st, StateError)
+        return out

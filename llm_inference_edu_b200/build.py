@@ -1,0 +1,68 @@
+"""Builds libqwen_b200.so in-tree with nvcc for sm_100a.
+
+    python -m llm_inference_edu_b200.build
+
+The library links the CUDA runtime statically, so loading it needs no GPU
+and no driver; only calls that touch the device do.
+"""
+from __future__ import annotations
+
+import os
+import subprocess
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+CSRC = os.path.join(HERE, "csrc")
+OUT = os.path.join(HERE, "libqwen_b200.so")
+SOURCES = ["ops.cu", "decode.cu", "runtime.cu", "synthetic.cpp"]
+HEADERS = ["common.cuh", "decode.cuh"]
+
+NVCC_FLAGS = [
+    "-gencode", "arch=compute_100a,code=sm_100a",
+    "-O3", "-lineinfo", "-std=c++17",
+    # Separate roundings for a*b+c unless fmaf() is written explicitly, so the
+    # elementwise arithmetic rounds like the reference's f32 expressions.
+    "-fmad=false",
+    "--cudart", "static",
+    "-Xcompiler", "-fPIC,-fopenmp,-ffp-contract=off",
+]
+
+
+def _stale():
+    if not os.path.exists(OUT):
+        return True
+    t = os.path.getmtime(OUT)
+    deps = [os.path.join(CSRC, f) for f in SOURCES + HEADERS]
+    deps.append(os.path.join(os.path.dirname(HERE), "include", "qwen_b200.h"))
+    return any(os.path.getmtime(d) > t for d in deps)
+
+
+def build(force: bool = False, verbose: bool = False) -> str:
+    if not force and not _stale():
+        return OUT
+    objdir = os.path.join(HERE, "_build")
+    os.makedirs(objdir, exist_ok=True)
+    objs, procs = [], []
+    for src in SOURCES:
+        obj = os.path.join(objdir, os.path.splitext(src)[0] + ".o")
+        cmd = ["nvcc", *NVCC_FLAGS, "-c", os.path.join(CSRC, src), "-o", obj]
+        if src.endswith(".cpp"):
+            cmd = ["nvcc", "-x", "cu", *NVCC_FLAGS, "-c", os.path.join(CSRC, src), "-o", obj]
+        if verbose:
+            print(" ".join(cmd), file=sys.stderr)
+        procs.append((cmd, subprocess.Popen(cmd)))
+        objs.append(obj)
+    for cmd, proc in procs:
+        if proc.wait() != 0:
+            raise subprocess.CalledProcessError(proc.returncode, cmd)
+    tmp = OUT + ".tmp"
+    cmd = ["nvcc", "-shared", "--cudart", "static", "-gencode", "arch=compute_100a,code=sm_100a",
+           *objs, "-o", tmp, "-Xcompiler", "-fopenmp", "-lgomp"]
+    subprocess.run(cmd, check=True)
+    os.replace(tmp, OUT)
+    return OUT
+
+
+if __name__ == "__main__":
+    build(force="--force" in sys.argv, verbose=True)
+    print(OUT)

@@ -1,0 +1,92 @@
+// Shared device/host helpers for the sm_100a Qwen2 token-loop library.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stddef.h>
+
+#include "../../include/qwen_b200.h"
+
+namespace qb {
+
+// ---------------------------------------------------------------- host ----
+
+// Thread-local error detail (qb_last_detail) and last CUDA error.
+void set_detail(size_t buffer, size_t expected, size_t actual, size_t index = 0);
+void clear_detail();
+uint32_t cuda_status(cudaError_t e);  // records e, returns QB_OK or QB_CUDA_ERROR
+
+#define QB_CUDA(expr)                                  \
+    do {                                               \
+        cudaError_t _e = (expr);                       \
+        if (_e != cudaSuccess) return ::qb::cuda_status(_e); \
+    } while (0)
+
+inline bool mul_ovf(size_t a, size_t b, size_t *out) {
+    if (a != 0 && b > SIZE_MAX / a) return true;
+    *out = a * b;
+    return false;
+}
+
+// Host-side scratch reused by the elementwise ops: a small device buffer per
+// device for error flags and per-call tables (grown on demand).
+struct DeviceScratch {
+    int device = -1;
+    void *ptr = nullptr;
+    size_t bytes = 0;
+};
+uint32_t scratch_get(size_t bytes, void **out);
+
+// ---------------------------------------------------------------- device ----
+
+__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+__device__ __forceinline__ float bf16_to_f32(uint16_t b) { return __uint_as_float((uint32_t)b << 16); }
+
+// Round-to-nearest-even FP32 -> BF16 bits.
+__device__ __forceinline__ uint16_t f32_to_bf16_rne(float x) {
+    uint32_t u = __float_as_uint(x);
+    if ((u & 0x7f800000u) == 0x7f800000u && (u & 0x007fffffu)) return (uint16_t)((u | 0x00400000u) >> 16);
+    uint32_t lsb = (u >> 16) & 1u;
+    return (uint16_t)((u + 0x7fffu + lsb) >> 16);
+}
+
+// Rust's f32::max: a NaN operand yields the other operand.
+__device__ __forceinline__ float rust_max(float a, float b) { return fmaxf(a, b); }
+
+__device__ __forceinline__ uint32_t ld_acquire_u32(const unsigned *p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void red_release_add_u32(unsigned *p, uint32_t v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Streaming 16-byte load that bypasses L1 allocation (weights are read once).
+__device__ __forceinline__ uint4 ld_stream_u4(const void *p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+// Bulk prefetch of [p, p+bytes) into L2 (p and bytes multiples of 16).
+__device__ __forceinline__ void prefetch_l2_bulk(const void *p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// Exact int8 -> FP32 for weights stored biased as u = q + 128 (1..255):
+// the byte is placed in the mantissa of 2^23 and 2^23 + 128 subtracted.
+__device__ __forceinline__ float u8b_to_f32(uint32_t word, int byte) {
+    uint32_t sel = 0x7650u | (uint32_t)byte;  // [b, 0, 0, 0x4B] little-endian
+    uint32_t f = __byte_perm(word, 0x4B000000u, sel);
+    return __uint_as_float(f) - 8388736.0f;   // 2^23 + 128
+}
+
+}  // namespace qb

@@ -1,0 +1,83 @@
+// Device layout and parameters of the persistent decode-step kernel.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stddef.h>
+
+namespace qb {
+
+// Storage of the seven per-layer linears (DecodeParams::wfmt).
+enum { WF_F32 = 0, WF_BF16 = 1, WF_I8 = 2 };
+
+// Error bits reported by the kernel in DecodeCtrl::error.
+enum { ERR_NONFINITE = 1u, ERR_TIMEOUT = 2u };
+
+// One layer's device tensors.  Every weight matrix is row-major with a row
+// stride padded to a multiple of 16 bytes (zero padding).  INT8 rows are
+// stored biased (u = q + 128) with one FP32 scale per output row.
+struct DecodeLayer {
+    const uint8_t *wqkv;  // [h + 2 kv, stride_h]: q rows, then k rows, then v rows
+    const float *sqkv;    // row scales (INT8) or null
+    const float *bqkv;    // [h + 2 kv] biases (zeros when the model has none)
+    const uint8_t *wo;    // head-blocked o_proj: [qh][h rows][stride_hd]
+    const float *so;      // [h] row scales (INT8) or null
+    const uint8_t *wg;    // [ff, stride_h]
+    const float *sg;
+    const uint8_t *wu;    // [ff, stride_h]
+    const float *su;
+    const uint8_t *wd;    // [h, stride_ff]
+    const float *sd;
+    const float *attn_norm;  // [h]
+    const float *ffn_norm;   // [h]
+    uint8_t *kc;          // [kv_heads][capacity][head_dim] rotated keys (FP32 or BF16)
+    uint8_t *vc;          // [kv_heads][capacity][head_dim] values
+};
+
+// Device-resident control block shared by the host and every step.
+struct DecodeCtrl {
+    int token;         // in: token evaluated by the next step
+    int pos;           // in: its absolute position (== processed)
+    int write_logits;  // in: nonzero = store the full logits row
+    int pad0;
+    int next_token;    // out: greedy argmax of this step
+    unsigned error;    // out: ERR_* bits, sticky until the host clears them
+    unsigned bar;      // grid barrier arrivals (reset by the last CTA)
+    unsigned ticket;   // end-of-step ticket (reset by the last CTA)
+};
+
+struct DecodeParams {
+    int V, L, h, qh, kvh, hd, ff, cap, group;
+    int wfmt, tfmt, kv_bf16;
+    float eps, sqrt_hd;
+    int ch, chd, cff, cemb;   // 16-byte chunks per row for K = h, hd, ff and the table
+    size_t sh, shd, sff, semb;  // row strides in bytes
+    int rqkv;                 // h + 2 * kv_heads * head_dim
+    int s_o;                  // CTAs per query head in the attention phase
+    const uint8_t *emb;       // [V, semb] embedding table (FP32 or BF16)
+    const uint8_t *head;      // LM head table (== emb when tied)
+    const float *final_norm;
+    const DecodeLayer *layers;  // device array [L]
+    const float2 *rope;       // [cap][hd/2] (cos, sin)
+    float *qkv;               // [rqkv]
+    float *part;              // [qh][h] per-head o_proj partial sums
+    float *act;               // [ff]
+    float *hidden;            // [h] residual stream
+    float *logits;            // [V]
+    float *amax_v;            // [grid] per-CTA argmax value
+    int *amax_i;              // [grid] per-CTA argmax index
+    int *emitted;             // [cap] greedy id emitted after each position (nullable)
+    DecodeCtrl *ctrl;
+    unsigned long long timeout_ns;
+    int prefetch;
+    // Shared-memory carve-up, in floats from the base (host-computed).
+    int sm_xs, sm_part, sm_h2, sm_q, sm_sc, sm_gu, sm_red, part_cap, sm_total;
+};
+
+// Shared-memory bytes the kernel needs for these parameters.
+size_t decode_smem_bytes(const DecodeParams &p);
+// Launches one decode step (cooperative, one CTA per SM).
+cudaError_t decode_launch(const DecodeParams &p, int grid, cudaStream_t stream);
+// Threads per CTA.
+constexpr int kDecodeThreads = 512;
+
+}  // namespace qb

@@ -1,0 +1,1097 @@
+// Host runtime behind the C ABI: device-resident models (Decoder,
+// src/model.rs:59-340), cached sessions (CachedSession, src/kv_cache.rs:
+// 156-475) and greedy generation state (GenerationSession,
+// src/generation.rs:98-338).
+//
+// A session owns its KV cache, activations, a device control block and a
+// CUDA graph that replays one decode step (control copy in, the persistent
+// decode kernel, result copy out).  Handles are opaque, never reused, and
+// every entry point validates before it writes.
+#include <math.h>
+#include <string.h>
+
+#include <algorithm>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <vector>
+
+#include "common.cuh"
+#include "decode.cuh"
+
+namespace qb {
+int decode_max_ctas(int wfmt, int kv_bf16, size_t smem);
+
+// ------------------------------------------------------ conversions ----
+
+__global__ void bf16_to_f32_kernel(const uint16_t *__restrict__ s, float *__restrict__ d, size_t n) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        d[i] = bf16_to_f32(s[i]);
+}
+
+__global__ void f32_to_bf16_kernel(const float *__restrict__ s, uint16_t *__restrict__ d, size_t n) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        d[i] = f32_to_bf16_rne(s[i]);
+}
+
+__global__ void nonfinite_any(const float *__restrict__ v, size_t n, unsigned long long *first) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        if (!isfinite(v[i])) atomicMin(first, (unsigned long long)i);
+}
+
+// Copies columns [c0, c0 + nc) of a row-major [rows, cols] FP32 matrix into
+// a padded row-major destination in format `fmt` (FP32, BF16 or biased u8
+// from int8 `q`).
+__global__ void relayout_kernel(const float *__restrict__ srcf, const int8_t *__restrict__ srcq,
+                                size_t rows, size_t cols, size_t c0, size_t nc, uint8_t *dst,
+                                size_t dst_stride, int fmt) {
+    size_t n = rows * nc;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        size_t r = i / nc, c = i % nc;
+        size_t s = r * cols + c0 + c;
+        uint8_t *row = dst + r * dst_stride;
+        if (fmt == WF_F32) ((float *)row)[c] = srcf[s];
+        else if (fmt == WF_BF16) ((uint16_t *)row)[c] = f32_to_bf16_rne(srcf[s]);
+        else row[c] = (uint8_t)((int)srcq[s] + 128);
+    }
+}
+
+__global__ void unbias_kernel(const uint8_t *__restrict__ src, size_t rows, size_t cols, size_t stride,
+                              int8_t *__restrict__ dst) {
+    size_t n = rows * cols;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        size_t r = i / cols, c = i % cols;
+        dst[i] = (int8_t)((int)src[r * stride + c] - 128);
+    }
+}
+
+static unsigned gridn(size_t n) {
+    size_t b = (n + 255) / 256;
+    return (unsigned)std::max<size_t>(1, std::min<size_t>(b, 16384));
+}
+
+static size_t round16(size_t b) { return (b + 15) & ~(size_t)15; }
+
+// RAII device buffer.
+struct DevBuf {
+    void *p = nullptr;
+    size_t bytes = 0;
+    DevBuf() = default;
+    DevBuf(const DevBuf &) = delete;
+    DevBuf &operator=(const DevBuf &) = delete;
+    DevBuf(DevBuf &&o) noexcept : p(o.p), bytes(o.bytes) { o.p = nullptr; o.bytes = 0; }
+    DevBuf &operator=(DevBuf &&o) noexcept {
+        if (this != &o) { release(); p = o.p; bytes = o.bytes; o.p = nullptr; o.bytes = 0; }
+        return *this;
+    }
+    ~DevBuf() { release(); }
+    void release() {
+        if (p) cudaFree(p);
+        p = nullptr;
+        bytes = 0;
+    }
+    uint32_t alloc(size_t n, bool zero = true) {
+        release();
+        if (n == 0) n = 16;
+        QB_CUDA(cudaMalloc(&p, n));
+        bytes = n;
+        if (zero) QB_CUDA(cudaMemset(p, 0, n));
+        return QB_OK;
+    }
+    template <class T> T *as() const { return (T *)p; }
+};
+
+// Makes `device` current for the scope.
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        cudaGetDevice(&prev);
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur;
+        if (cudaGetDevice(&cur) == cudaSuccess && prev >= 0 && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+// ------------------------------------------------------------ model ----
+
+struct Linear {  // one device linear in the decode layout
+    DevBuf w;       // padded rows
+    DevBuf scales;  // [rows] (INT8)
+    size_t rows = 0, cols = 0, stride = 0;
+    bool set = false;
+};
+
+struct LayerStore {
+    DevBuf wqkv, sqkv, bqkv, wo, so;
+    Linear gate, up, down;
+    DevBuf attn_norm, ffn_norm;
+    bool q = false, k = false, v = false, o = false, an = false, fn = false;
+};
+
+struct Model {
+    qb_model_config c{};
+    int device = 0;
+    uint32_t lin = QB_LINEAR_F32, tab = QB_TABLE_F32;
+    size_t sh = 0, shd = 0, sff = 0, semb = 0;
+    DevBuf emb, head, final_norm;
+    bool emb_set = false, head_set = false, fn_set = false, finalized = false;
+    std::vector<LayerStore> layers;
+    DevBuf dlayers;  // DecodeLayer[L] (weights only; sessions add KV pointers)
+    size_t logical_bytes = 0;
+    int wf() const { return lin == QB_LINEAR_INT8_ROW ? WF_I8 : (lin == QB_LINEAR_BF16 ? WF_BF16 : WF_F32); }
+    size_t esz() const { return lin == QB_LINEAR_INT8_ROW ? 1 : (lin == QB_LINEAR_BF16 ? 2 : 4); }
+    size_t tesz() const { return tab == QB_TABLE_BF16 ? 2 : 4; }
+    size_t kv() const { return c.kv_heads * c.head_dim; }
+};
+
+static std::mutex g_mu;
+static uint64_t g_next = 1;
+static std::map<uint64_t, std::shared_ptr<Model>> g_models;
+struct Session;
+struct Generation;
+static std::map<uint64_t, std::shared_ptr<Session>> g_sessions;
+static std::map<uint64_t, std::shared_ptr<Generation>> g_generations;
+
+static std::shared_ptr<Model> find_model(uint64_t h) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = g_models.find(h);
+    return it == g_models.end() ? nullptr : it->second;
+}
+
+// Converts a host tensor (FP32 or BF16) to a temporary device FP32 buffer.
+static uint32_t upload_f32(const void *data, size_t n, uint32_t dtype, DevBuf &out) {
+    uint32_t s = out.alloc(n * 4, false);
+    if (s) return s;
+    if (dtype == QB_HOST_F32) {
+        QB_CUDA(cudaMemcpy(out.p, data, n * 4, cudaMemcpyHostToDevice));
+    } else {
+        DevBuf tmp;
+        if ((s = tmp.alloc(n * 2, false))) return s;
+        QB_CUDA(cudaMemcpy(tmp.p, data, n * 2, cudaMemcpyHostToDevice));
+        bf16_to_f32_kernel<<<gridn(n), 256>>>(tmp.as<uint16_t>(), out.as<float>(), n);
+        QB_CUDA(cudaGetLastError());
+        QB_CUDA(cudaDeviceSynchronize());
+    }
+    return QB_OK;
+}
+
+static uint32_t check_finite_dev(const float *p, size_t n, size_t *index) {
+    void *sp;
+    uint32_t s = scratch_get(64, &sp);
+    if (s) return s;
+    unsigned long long *f = (unsigned long long *)sp;
+    QB_CUDA(cudaMemset(f, 0xff, 8));
+    nonfinite_any<<<gridn(n), 256>>>(p, n, f);
+    unsigned long long h;
+    QB_CUDA(cudaMemcpy(&h, f, 8, cudaMemcpyDeviceToHost));
+    if (h != ~0ull) {
+        *index = (size_t)h;
+        return QB_NONFINITE;
+    }
+    return QB_OK;
+}
+
+// Stores FP32 source rows into `dst` (padded rows), quantizing per row for
+// INT8 with the bit-exact scheme of qb_quantize_int8.  `scales` receives the
+// row scales.  Column window [c0, c0 + nc) of the source is stored.
+static uint32_t store_linear(const Model &m, const float *src, size_t rows, size_t cols, uint8_t *dst,
+                             size_t stride, float *scales, size_t row_base_dst) {
+    (void)row_base_dst;
+    const int wf = m.wf();
+    if (wf == WF_I8) {
+        DevBuf q, sc;
+        uint32_t s;
+        if ((s = q.alloc(rows * cols, false)) || (s = sc.alloc(rows * 4, false))) return s;
+        s = qb_quantize_int8(src, rows * cols, rows, cols, cols, q.as<int8_t>(), sc.as<float>(), nullptr);
+        if (s) return s == QB_NONFINITE_WEIGHT ? QB_NONFINITE : s;
+        relayout_kernel<<<gridn(rows * cols), 256>>>(nullptr, q.as<int8_t>(), rows, cols, 0, cols, dst, stride, WF_I8);
+        QB_CUDA(cudaGetLastError());
+        QB_CUDA(cudaMemcpy(scales, sc.p, rows * 4, cudaMemcpyDeviceToDevice));
+    } else {
+        size_t idx;
+        uint32_t s = check_finite_dev(src, rows * cols, &idx);
+        if (s) { set_detail(0, 0, 0, idx); return s; }
+        relayout_kernel<<<gridn(rows * cols), 256>>>(src, nullptr, rows, cols, 0, cols, dst, stride, wf);
+        QB_CUDA(cudaGetLastError());
+    }
+    QB_CUDA(cudaDeviceSynchronize());
+    return QB_OK;
+}
+
+// o_proj in head-blocked form: block hh holds columns [hh*hd, (hh+1)*hd) of
+// every row, so one head's partial product streams a contiguous block.
+static uint32_t store_o_proj(Model &m, LayerStore &L, const float *src) {
+    const size_t h = m.c.hidden_dim, hd = m.c.head_dim, qh = m.c.query_heads;
+    const int wf = m.wf();
+    uint32_t s;
+    if (wf == WF_I8) {
+        DevBuf q, sc;
+        if ((s = q.alloc(h * h, false)) || (s = sc.alloc(h * 4, false))) return s;
+        s = qb_quantize_int8(src, h * h, h, h, h, q.as<int8_t>(), sc.as<float>(), nullptr);
+        if (s) return s == QB_NONFINITE_WEIGHT ? QB_NONFINITE : s;
+        for (size_t hh = 0; hh < qh; ++hh)
+            relayout_kernel<<<gridn(h * hd), 256>>>(nullptr, q.as<int8_t>(), h, h, hh * hd, hd,
+                                                    L.wo.as<uint8_t>() + hh * h * m.shd, m.shd, WF_I8);
+        QB_CUDA(cudaMemcpy(L.so.p, sc.p, h * 4, cudaMemcpyDeviceToDevice));
+    } else {
+        size_t idx;
+        if ((s = check_finite_dev(src, h * h, &idx))) { set_detail(0, 0, 0, idx); return s; }
+        for (size_t hh = 0; hh < qh; ++hh)
+            relayout_kernel<<<gridn(h * hd), 256>>>(src, nullptr, h, h, hh * hd, hd,
+                                                    L.wo.as<uint8_t>() + hh * h * m.shd, m.shd, wf);
+    }
+    QB_CUDA(cudaGetLastError());
+    QB_CUDA(cudaDeviceSynchronize());
+    return QB_OK;
+}
+
+static uint32_t host_vector_finite(const void *data, size_t n, uint32_t dtype, std::vector<float> &out) {
+    out.resize(n);
+    for (size_t i = 0; i < n; ++i) {
+        float v;
+        if (dtype == QB_HOST_F32) v = ((const float *)data)[i];
+        else {
+            uint32_t u = (uint32_t)((const uint16_t *)data)[i] << 16;
+            memcpy(&v, &u, 4);
+        }
+        if (!isfinite(v)) {
+            set_detail(0, 0, 0, i);
+            return QB_NONFINITE;
+        }
+        out[i] = v;
+    }
+    return QB_OK;
+}
+
+// ---------------------------------------------------------- session ----
+
+struct Session {
+    std::shared_ptr<Model> m;
+    int device = 0;
+    size_t capacity = 0, processed = 0;
+    bool valid = true;
+    int kv_bf16 = 0;
+    size_t logical_bytes = 0, workspace_bytes = 0;
+    cudaStream_t stream = nullptr;
+    DevBuf kv, rope, qkv, part, act, hidden, logits, amax_v, amax_i, emitted, ctrl, dlayers;
+    DecodeCtrl *hctrl = nullptr;  // pinned mirror
+    DecodeParams params{};
+    int grid = 0;
+    cudaGraphExec_t g_host = nullptr;
+    bool logits_valid = false;
+    ~Session() {
+        DeviceGuard dg(device);
+        if (g_host) cudaGraphExecDestroy(g_host);
+        if (hctrl) cudaFreeHost(hctrl);
+        if (stream) cudaStreamDestroy(stream);
+    }
+};
+
+static std::shared_ptr<Session> find_session(uint64_t h) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = g_sessions.find(h);
+    return it == g_sessions.end() ? nullptr : it->second;
+}
+
+// workspace_bytes, src/kv_cache.rs:114-127 (the reference's resident vector
+// payload formula, kept so budgets and reports agree with the reference).
+static size_t ref_workspace_bytes(const qb_model_config &c, size_t capacity) {
+    return (c.hidden_dim * 8 + c.kv_heads * c.head_dim * 3 + c.ff_dim * 3 + capacity * 2) * 4;
+}
+
+static uint32_t session_build(Session &s) {
+    Model &m = *s.m;
+    const qb_model_config &c = m.c;
+    const size_t L = c.layers, kvh = c.kv_heads, hd = c.head_dim, cap = s.capacity;
+    const size_t esz = s.kv_bf16 ? 2 : 4;
+    const size_t per = kvh * cap * hd * esz;
+    uint32_t st;
+    QB_CUDA(cudaStreamCreateWithFlags(&s.stream, cudaStreamNonBlocking));
+    if ((st = s.kv.alloc(round16(per) * 2 * L))) return st;
+    // RoPE table: the reference's f32 powf/sin/cos per position (src/rope.rs:83-90).
+    const size_t half = hd / 2;
+    std::vector<float> tab(cap * half * 2);
+    std::vector<float> freq(half);
+    for (size_t j = 0; j < half; ++j) freq[j] = powf(c.rope_base, -((float)(2 * j)) / (float)hd);
+    for (size_t t = 0; t < cap; ++t) {
+        float pos = (float)t;
+        for (size_t j = 0; j < half; ++j) {
+            float a = pos * freq[j];
+            tab[(t * half + j) * 2] = cosf(a);
+            tab[(t * half + j) * 2 + 1] = sinf(a);
+        }
+    }
+    if ((st = s.rope.alloc(tab.size() * 4, false))) return st;
+    QB_CUDA(cudaMemcpy(s.rope.p, tab.data(), tab.size() * 4, cudaMemcpyHostToDevice));
+    const size_t rqkv = c.hidden_dim + 2 * kvh * hd;
+    int dev_sms = 0;
+    QB_CUDA(cudaDeviceGetAttribute(&dev_sms, cudaDevAttrMultiProcessorCount, s.device));
+    s.grid = dev_sms;
+    if ((st = s.qkv.alloc(rqkv * 4)) || (st = s.part.alloc(c.query_heads * c.hidden_dim * 4)) ||
+        (st = s.act.alloc(c.ff_dim * 4)) || (st = s.hidden.alloc(c.hidden_dim * 4)) ||
+        (st = s.logits.alloc(c.vocab_size * 4)) || (st = s.amax_v.alloc(s.grid * 4)) ||
+        (st = s.amax_i.alloc(s.grid * 4)) || (st = s.emitted.alloc(cap * 4)) ||
+        (st = s.ctrl.alloc(sizeof(DecodeCtrl))))
+        return st;
+    QB_CUDA(cudaMallocHost((void **)&s.hctrl, sizeof(DecodeCtrl)));
+    memset(s.hctrl, 0, sizeof(DecodeCtrl));
+    // Per-session layer table: the model's weights plus this session's KV.
+    std::vector<DecodeLayer> dl(L);
+    QB_CUDA(cudaMemcpy(dl.data(), m.dlayers.p, L * sizeof(DecodeLayer), cudaMemcpyDeviceToHost));
+    for (size_t l = 0; l < L; ++l) {
+        dl[l].kc = s.kv.as<uint8_t>() + round16(per) * (2 * l);
+        dl[l].vc = s.kv.as<uint8_t>() + round16(per) * (2 * l + 1);
+    }
+    if ((st = s.dlayers.alloc(L * sizeof(DecodeLayer), false))) return st;
+    QB_CUDA(cudaMemcpy(s.dlayers.p, dl.data(), L * sizeof(DecodeLayer), cudaMemcpyHostToDevice));
+
+    DecodeParams &p = s.params;
+    const int wf = m.wf();
+    const int epc = wf == WF_I8 ? 16 : (wf == WF_BF16 ? 8 : 4);
+    const int tepc = m.tab == QB_TABLE_BF16 ? 8 : 4;
+    p.V = (int)c.vocab_size; p.L = (int)L; p.h = (int)c.hidden_dim; p.qh = (int)c.query_heads;
+    p.kvh = (int)kvh; p.hd = (int)hd; p.ff = (int)c.ff_dim; p.cap = (int)cap;
+    p.group = (int)(c.query_heads / kvh);
+    p.wfmt = wf; p.tfmt = m.tab == QB_TABLE_BF16 ? WF_BF16 : WF_F32; p.kv_bf16 = s.kv_bf16;
+    p.eps = c.norm_epsilon;
+    p.sqrt_hd = sqrtf((float)hd);
+    p.sh = m.sh; p.shd = m.shd; p.sff = m.sff; p.semb = m.semb;
+    p.ch = (int)(m.sh / 16); p.chd = (int)(m.shd / 16); p.cff = (int)(m.sff / 16); p.cemb = (int)(m.semb / 16);
+    p.rqkv = (int)rqkv;
+    p.s_o = std::max(1, std::min(8, s.grid / std::max(1, p.qh)));
+    p.emb = m.emb.as<uint8_t>();
+    p.head = m.head_set ? m.head.as<uint8_t>() : m.emb.as<uint8_t>();
+    p.final_norm = m.final_norm.as<float>();
+    p.layers = s.dlayers.as<DecodeLayer>();
+    p.rope = s.rope.as<float2>();
+    p.qkv = s.qkv.as<float>(); p.part = s.part.as<float>(); p.act = s.act.as<float>();
+    p.hidden = s.hidden.as<float>(); p.logits = s.logits.as<float>();
+    p.amax_v = s.amax_v.as<float>(); p.amax_i = s.amax_i.as<int>(); p.emitted = s.emitted.as<int>();
+    p.ctrl = s.ctrl.as<DecodeCtrl>();
+    p.timeout_ns = 2000000000ull;
+    p.prefetch = 1;
+    // Shared-memory carve-up (floats).
+    int xs = std::max({p.ch * epc, p.chd * epc, p.cff * epc, p.cemb * tepc, p.h});
+    xs = (xs + 3) & ~3;
+    int part_cap = std::max({8192, p.ch, p.chd, p.cff, p.cemb, 512});
+    part_cap = (part_cap + 3) & ~3;
+    int h2 = (p.h + 3) & ~3;
+    int q = (3 * p.hd + std::max(p.hd, p.chd * epc) + 3) & ~3;
+    int sc = (p.cap + 3) & ~3;
+    int rows_per = (int)((std::max<size_t>({c.ff_dim, c.hidden_dim, rqkv}) + s.grid - 1) / s.grid);
+    int gu = (2 * rows_per + 4 + 3) & ~3;
+    int red = 128;
+    p.sm_xs = 0; p.sm_part = xs; p.sm_h2 = p.sm_part + part_cap; p.sm_q = p.sm_h2 + h2;
+    p.sm_sc = p.sm_q + q; p.sm_gu = p.sm_sc + sc; p.sm_red = p.sm_gu + gu;
+    p.sm_total = p.sm_red + red;
+    p.part_cap = part_cap;
+    size_t smem = decode_smem_bytes(p);
+    if (smem > 227 * 1024) return QB_UNSUPPORTED;
+    int maxc = decode_max_ctas(wf, s.kv_bf16, smem);
+    if (maxc < s.grid) return QB_UNSUPPORTED;
+
+    // Graph: control block in, one decode step, result out.
+    cudaGraph_t g = nullptr;
+    QB_CUDA(cudaStreamBeginCapture(s.stream, cudaStreamCaptureModeThreadLocal));
+    cudaError_t e1 = cudaMemcpyAsync(s.ctrl.p, s.hctrl, 16, cudaMemcpyHostToDevice, s.stream);
+    cudaError_t e2 = decode_launch(p, s.grid, s.stream);
+    cudaError_t e3 = cudaMemcpyAsync((char *)s.hctrl + 16, (char *)s.ctrl.p + 16, 8, cudaMemcpyDeviceToHost, s.stream);
+    cudaError_t e4 = cudaStreamEndCapture(s.stream, &g);
+    if (e1 == cudaSuccess && e2 == cudaSuccess && e3 == cudaSuccess && e4 == cudaSuccess) {
+        cudaError_t e5 = cudaGraphInstantiate(&s.g_host, g, 0);
+        if (e5 != cudaSuccess) s.g_host = nullptr;
+    } else {
+        s.g_host = nullptr;
+        cudaGetLastError();
+    }
+    if (g) cudaGraphDestroy(g);
+    s.logical_bytes = kvh * cap * hd * 2 * L * 4;  // the reference's FP32 KV count
+    s.workspace_bytes = ref_workspace_bytes(c, cap);
+    return QB_OK;
+}
+
+// One decode step with a host-supplied token (graph replay).
+static uint32_t session_launch(Session &s, uint32_t token, bool want_logits) {
+    s.hctrl->token = (int)token;
+    s.hctrl->pos = (int)s.processed;
+    s.hctrl->write_logits = want_logits ? 1 : 0;
+    if (s.g_host) {
+        QB_CUDA(cudaGraphLaunch(s.g_host, s.stream));
+    } else {
+        QB_CUDA(cudaMemcpyAsync(s.ctrl.p, s.hctrl, 16, cudaMemcpyHostToDevice, s.stream));
+        QB_CUDA(decode_launch(s.params, s.grid, s.stream));
+        QB_CUDA(cudaMemcpyAsync((char *)s.hctrl + 16, (char *)s.ctrl.p + 16, 8, cudaMemcpyDeviceToHost, s.stream));
+    }
+    return QB_OK;
+}
+
+// Execution error: invalidate (src/kv_cache.rs:335-345) and clear the
+// device control block so the next step starts from a clean barrier.
+static uint32_t session_fail(Session &s, uint32_t status) {
+    s.valid = false;
+    s.processed = 0;
+    s.logits_valid = false;
+    cudaMemsetAsync(s.ctrl.p, 0, sizeof(DecodeCtrl), s.stream);
+    cudaStreamSynchronize(s.stream);
+    memset(s.hctrl, 0, sizeof(DecodeCtrl));
+    return status;
+}
+
+static uint32_t session_finish(Session &s, float *logits, uint32_t *argmax) {
+    cudaError_t e = cudaStreamSynchronize(s.stream);
+    if (e != cudaSuccess) return session_fail(s, cuda_status(e));
+    unsigned err = s.hctrl->error;
+    if (err) return session_fail(s, (err & ERR_TIMEOUT) ? QB_DEVICE_TIMEOUT : QB_NONFINITE);
+    if (logits) {
+        e = cudaMemcpy(logits, s.logits.p, s.m->c.vocab_size * 4, cudaMemcpyDeviceToHost);
+        if (e != cudaSuccess) return session_fail(s, cuda_status(e));
+    }
+    if (argmax) *argmax = (uint32_t)s.hctrl->next_token;
+    s.processed += 1;
+    return QB_OK;
+}
+
+static uint32_t session_step(Session &s, uint32_t token, float *logits, size_t logits_len,
+                             uint32_t *argmax, bool keep_logits) {
+    if (!s.valid) return QB_INVALID_STATE;
+    if (logits && logits_len != s.m->c.vocab_size) return QB_INVALID_OUTPUT_LENGTH;
+    if (token >= s.m->c.vocab_size) return QB_INVALID_TOKEN;
+    if (s.processed == s.capacity) return QB_FULL;
+    DeviceGuard dg(s.device);
+    uint32_t st = session_launch(s, token, logits != nullptr || keep_logits);
+    if (st) return session_fail(s, st);
+    st = session_finish(s, logits, argmax);
+    if (!st) s.logits_valid = logits != nullptr || keep_logits;
+    return st;
+}
+
+// ------------------------------------------------------- generation ----
+
+struct Generation {
+    std::shared_ptr<Session> cache;
+    std::vector<uint32_t> history;
+    std::vector<uint32_t> stops;
+    size_t max_new = 0, generated = 0;
+    int stop = QB_STOP_NONE;
+    bool logits_ready = false;
+    uint32_t last_argmax = 0;
+    uint32_t vocab = 0;
+};
+
+static std::shared_ptr<Generation> find_generation(uint64_t h) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = g_generations.find(h);
+    return it == g_generations.end() ? nullptr : it->second;
+}
+
+static bool cancelled(const volatile int32_t *c) { return c && *c != 0; }
+
+// evaluate_pending, src/generation.rs:258-274.
+static uint32_t evaluate_pending(Generation &g, const volatile int32_t *cancel) {
+    Session &s = *g.cache;
+    while (s.processed < g.history.size()) {
+        if (cancelled(cancel)) return QB_CANCELLED;
+        uint32_t token = g.history[s.processed];
+        g.logits_ready = false;
+        uint32_t am = 0;
+        uint32_t st = session_step(s, token, nullptr, 0, &am, true);
+        if (st) return st;
+        g.last_argmax = am;
+        g.logits_ready = true;
+    }
+    if (cancelled(cancel)) return QB_CANCELLED;
+    return QB_OK;
+}
+
+static void generation_reset(Generation &g) {
+    g.cache->processed = 0;
+    g.cache->valid = true;
+    g.cache->logits_valid = false;
+    g.history.clear();
+    g.logits_ready = false;
+    g.generated = 0;
+    g.stop = QB_STOP_NONE;
+}
+
+}  // namespace qb
+
+using namespace qb;
+
+extern "C" {
+
+// ---------------------------------------------------------------- model ----
+
+uint32_t qb_model_create(const qb_model_config *cfg, uint32_t linear_format, uint32_t table_format,
+                         int device, uint64_t *out) {
+    clear_detail();
+    if (!cfg || !out) return QB_INVALID_PARAMETERS;
+    const qb_model_config c = *cfg;
+    // Decoder::new admission, src/model.rs:191-230.
+    if (!c.vocab_size || !c.layers || !c.hidden_dim || !c.query_heads || !c.kv_heads || !c.head_dim ||
+        !c.ff_dim || !c.max_tokens)
+        return QB_INVALID_CONFIG;
+    if (c.head_dim % 2 || c.query_heads % c.kv_heads) return QB_INVALID_CONFIG;
+    size_t qd;
+    if (mul_ovf(c.query_heads, c.head_dim, &qd)) return QB_DIMENSION_OVERFLOW;
+    if (qd != c.hidden_dim) return QB_INVALID_CONFIG;
+    if (!isfinite(c.rope_base) || c.rope_base <= 0 || !isfinite(c.norm_epsilon) || c.norm_epsilon <= 0)
+        return QB_INVALID_CONFIG;
+    if (c.max_tokens > ((size_t)1 << 24)) return QB_INVALID_CONFIG;
+    if (linear_format > QB_LINEAR_INT8_ROW || table_format > QB_TABLE_BF16) return QB_INVALID_PARAMETERS;
+    if (c.vocab_size > 0x7fffffff || c.hidden_dim > 0xffffff || c.ff_dim > 0xffffff || c.head_dim > 512)
+        return QB_UNSUPPORTED;
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev) {
+        cudaGetLastError();
+        return QB_CUDA_ERROR;
+    }
+    auto m = std::make_shared<Model>();
+    m->c = c;
+    m->device = device;
+    m->lin = linear_format;
+    m->tab = table_format;
+    m->sh = round16(c.hidden_dim * m->esz());
+    m->shd = round16(c.head_dim * m->esz());
+    m->sff = round16(c.ff_dim * m->esz());
+    m->semb = round16(c.hidden_dim * m->tesz());
+    m->layers.resize(c.layers);
+    DeviceGuard dg(device);
+    const size_t h = c.hidden_dim, kv = m->kv(), ff = c.ff_dim, rq = h + 2 * kv;
+    uint32_t s;
+    for (auto &L : m->layers) {
+        if ((s = L.wqkv.alloc(rq * m->sh)) || (s = L.sqkv.alloc(rq * 4)) || (s = L.bqkv.alloc(rq * 4)) ||
+            (s = L.wo.alloc(c.query_heads * h * m->shd)) || (s = L.so.alloc(h * 4)) ||
+            (s = L.gate.w.alloc(ff * m->sh)) || (s = L.gate.scales.alloc(ff * 4)) ||
+            (s = L.up.w.alloc(ff * m->sh)) || (s = L.up.scales.alloc(ff * 4)) ||
+            (s = L.down.w.alloc(h * m->sff)) || (s = L.down.scales.alloc(h * 4)) ||
+            (s = L.attn_norm.alloc(h * 4)) || (s = L.ffn_norm.alloc(h * 4)))
+            return s == QB_CUDA_ERROR ? QB_ALLOCATION : s;
+    }
+    if ((s = m->emb.alloc(c.vocab_size * m->semb)) || (s = m->final_norm.alloc(h * 4)))
+        return s == QB_CUDA_ERROR ? QB_ALLOCATION : s;
+    std::lock_guard<std::mutex> lk(g_mu);
+    uint64_t id = g_next++;
+    g_models[id] = m;
+    *out = id;
+    return QB_OK;
+}
+
+uint32_t qb_model_set_tensor(uint64_t model, int64_t layer, uint32_t tensor, uint32_t dtype,
+                             const void *data, size_t n) {
+    clear_detail();
+    auto m = find_model(model);
+    if (!m) return QB_INVALID_HANDLE;
+    if (m->finalized) return QB_INVALID_STATE;
+    if (!data || (dtype != QB_HOST_F32 && dtype != QB_HOST_BF16)) return QB_INVALID_PARAMETERS;
+    const qb_model_config &c = m->c;
+    const size_t h = c.hidden_dim, kv = m->kv(), ff = c.ff_dim, V = c.vocab_size;
+    DeviceGuard dg(m->device);
+    size_t expected = 0;
+    bool global = tensor <= QB_T_FINAL_NORM;
+    if (global != (layer < 0)) return QB_INVALID_PARAMETERS;
+    if (!global && (size_t)layer >= c.layers) return QB_INVALID_LAYER_COUNT;
+    switch (tensor) {
+    case QB_T_EMBEDDING: case QB_T_LM_HEAD: expected = V * h; break;
+    case QB_T_FINAL_NORM: case QB_T_ATTN_NORM: case QB_T_FFN_NORM: case QB_T_Q_BIAS: expected = h; break;
+    case QB_T_K_BIAS: case QB_T_V_BIAS: expected = kv; break;
+    case QB_T_Q: case QB_T_O: expected = h * h; break;
+    case QB_T_K: case QB_T_V: expected = kv * h; break;
+    case QB_T_GATE: case QB_T_UP: case QB_T_DOWN: expected = ff * h; break;
+    default: return QB_INVALID_PARAMETERS;
+    }
+    if (n != expected) {
+        set_detail(tensor, expected, n);
+        return QB_INVALID_LENGTH;
+    }
+    uint32_t s;
+    std::vector<float> hv;
+    if (tensor == QB_T_FINAL_NORM || tensor == QB_T_ATTN_NORM || tensor == QB_T_FFN_NORM ||
+        tensor == QB_T_Q_BIAS || tensor == QB_T_K_BIAS || tensor == QB_T_V_BIAS) {
+        if ((s = host_vector_finite(data, n, dtype, hv))) return s;
+        float *dst = nullptr;
+        if (tensor == QB_T_FINAL_NORM) { dst = m->final_norm.as<float>(); m->fn_set = true; }
+        else {
+            LayerStore &L = m->layers[layer];
+            if (tensor == QB_T_ATTN_NORM) { dst = L.attn_norm.as<float>(); L.an = true; }
+            else if (tensor == QB_T_FFN_NORM) { dst = L.ffn_norm.as<float>(); L.fn = true; }
+            else if (tensor == QB_T_Q_BIAS) dst = L.bqkv.as<float>();
+            else if (tensor == QB_T_K_BIAS) dst = L.bqkv.as<float>() + h;
+            else dst = L.bqkv.as<float>() + h + kv;
+        }
+        QB_CUDA(cudaMemcpy(dst, hv.data(), n * 4, cudaMemcpyHostToDevice));
+        return QB_OK;
+    }
+    DevBuf src;
+    if ((s = upload_f32(data, n, dtype, src))) return s;
+    if (tensor == QB_T_EMBEDDING || tensor == QB_T_LM_HEAD) {
+        size_t idx;
+        if ((s = check_finite_dev(src.as<float>(), n, &idx))) { set_detail(tensor, 0, 0, idx); return s; }
+        DevBuf *dst = tensor == QB_T_EMBEDDING ? &m->emb : &m->head;
+        if (tensor == QB_T_LM_HEAD && (s = m->head.alloc(V * m->semb))) return s;
+        relayout_kernel<<<gridn(n), 256>>>(src.as<float>(), nullptr, V, h, 0, h, dst->as<uint8_t>(), m->semb,
+                                           m->tab == QB_TABLE_BF16 ? WF_BF16 : WF_F32);
+        QB_CUDA(cudaGetLastError());
+        QB_CUDA(cudaDeviceSynchronize());
+        if (tensor == QB_T_EMBEDDING) m->emb_set = true; else m->head_set = true;
+        return QB_OK;
+    }
+    LayerStore &L = m->layers[layer];
+    switch (tensor) {
+    case QB_T_Q:
+        s = store_linear(*m, src.as<float>(), h, h, L.wqkv.as<uint8_t>(), m->sh, L.sqkv.as<float>(), 0);
+        if (!s) L.q = true;
+        break;
+    case QB_T_K:
+        s = store_linear(*m, src.as<float>(), kv, h, L.wqkv.as<uint8_t>() + h * m->sh, m->sh, L.sqkv.as<float>() + h, 0);
+        if (!s) L.k = true;
+        break;
+    case QB_T_V:
+        s = store_linear(*m, src.as<float>(), kv, h, L.wqkv.as<uint8_t>() + (h + kv) * m->sh, m->sh,
+                         L.sqkv.as<float>() + h + kv, 0);
+        if (!s) L.v = true;
+        break;
+    case QB_T_O:
+        s = store_o_proj(*m, L, src.as<float>());
+        if (!s) L.o = true;
+        break;
+    case QB_T_GATE:
+        s = store_linear(*m, src.as<float>(), ff, h, L.gate.w.as<uint8_t>(), m->sh, L.gate.scales.as<float>(), 0);
+        if (!s) L.gate.set = true;
+        break;
+    case QB_T_UP:
+        s = store_linear(*m, src.as<float>(), ff, h, L.up.w.as<uint8_t>(), m->sh, L.up.scales.as<float>(), 0);
+        if (!s) L.up.set = true;
+        break;
+    case QB_T_DOWN:
+        s = store_linear(*m, src.as<float>(), h, ff, L.down.w.as<uint8_t>(), m->sff, L.down.scales.as<float>(), 0);
+        if (!s) L.down.set = true;
+        break;
+    }
+    if (s == QB_NONFINITE) set_detail(tensor, 0, 0, 0);
+    return s;
+}
+
+uint32_t qb_model_finalize(uint64_t model) {
+    clear_detail();
+    auto m = find_model(model);
+    if (!m) return QB_INVALID_HANDLE;
+    if (m->finalized) return QB_OK;
+    if (!m->emb_set || !m->fn_set) return QB_INVALID_STATE;
+    for (auto &L : m->layers)
+        if (!(L.q && L.k && L.v && L.o && L.an && L.fn && L.gate.set && L.up.set && L.down.set))
+            return QB_INVALID_STATE;
+    DeviceGuard dg(m->device);
+    const bool i8 = m->wf() == WF_I8;
+    std::vector<DecodeLayer> dl(m->c.layers);
+    for (size_t l = 0; l < m->c.layers; ++l) {
+        LayerStore &L = m->layers[l];
+        DecodeLayer &d = dl[l];
+        d.wqkv = L.wqkv.as<uint8_t>(); d.sqkv = i8 ? L.sqkv.as<float>() : nullptr; d.bqkv = L.bqkv.as<float>();
+        d.wo = L.wo.as<uint8_t>(); d.so = i8 ? L.so.as<float>() : nullptr;
+        d.wg = L.gate.w.as<uint8_t>(); d.sg = i8 ? L.gate.scales.as<float>() : nullptr;
+        d.wu = L.up.w.as<uint8_t>(); d.su = i8 ? L.up.scales.as<float>() : nullptr;
+        d.wd = L.down.w.as<uint8_t>(); d.sd = i8 ? L.down.scales.as<float>() : nullptr;
+        d.attn_norm = L.attn_norm.as<float>(); d.ffn_norm = L.ffn_norm.as<float>();
+        d.kc = d.vc = nullptr;
+    }
+    uint32_t s;
+    if ((s = m->dlayers.alloc(dl.size() * sizeof(DecodeLayer), false))) return s;
+    QB_CUDA(cudaMemcpy(m->dlayers.p, dl.data(), dl.size() * sizeof(DecodeLayer), cudaMemcpyHostToDevice));
+    // Logical payload: matrices at their stored width (FP32 4 B, BF16 2 B,
+    // INT8 1 B + 4 B per row scale), plus FP32 norms and biases; the tied
+    // table counts once (src/model.rs:347-385).
+    const qb_model_config &c = m->c;
+    const size_t h = c.hidden_dim, kv = m->kv(), ff = c.ff_dim;
+    size_t mats = h * h * 2 + kv * h * 2 + ff * h * 3;
+    size_t rows = h + 2 * kv + h + 2 * ff + h;
+    size_t per = i8 ? mats + rows * 4 : mats * m->esz();
+    per += 2 * h * 4 + (h + 2 * kv) * 4;
+    size_t table = c.vocab_size * h * m->tesz();
+    m->logical_bytes = table * (m->head_set ? 2 : 1) + h * 4 + per * c.layers;
+    m->finalized = true;
+    return QB_OK;
+}
+
+uint32_t qb_model_logical_weight_bytes(uint64_t model, size_t *out) {
+    auto m = find_model(model);
+    if (!m) return QB_INVALID_HANDLE;
+    if (!m->finalized) return QB_INVALID_STATE;
+    *out = m->logical_bytes;
+    return QB_OK;
+}
+
+uint32_t qb_model_read_int8(uint64_t model, int64_t layer, uint32_t tensor, int8_t *values, size_t vl,
+                            float *scales, size_t sl) {
+    clear_detail();
+    auto m = find_model(model);
+    if (!m) return QB_INVALID_HANDLE;
+    if (m->wf() != WF_I8) return QB_UNSUPPORTED;
+    if (layer < 0 || (size_t)layer >= m->c.layers) return QB_INVALID_LAYER_COUNT;
+    const size_t h = m->c.hidden_dim, kv = m->kv(), ff = m->c.ff_dim;
+    LayerStore &L = m->layers[layer];
+    const uint8_t *src = nullptr;
+    const float *sc = nullptr;
+    size_t rows = 0, cols = h, stride = m->sh;
+    switch (tensor) {
+    case QB_T_Q: src = L.wqkv.as<uint8_t>(); sc = L.sqkv.as<float>(); rows = h; break;
+    case QB_T_K: src = L.wqkv.as<uint8_t>() + h * m->sh; sc = L.sqkv.as<float>() + h; rows = kv; break;
+    case QB_T_V: src = L.wqkv.as<uint8_t>() + (h + kv) * m->sh; sc = L.sqkv.as<float>() + h + kv; rows = kv; break;
+    case QB_T_GATE: src = L.gate.w.as<uint8_t>(); sc = L.gate.scales.as<float>(); rows = ff; break;
+    case QB_T_UP: src = L.up.w.as<uint8_t>(); sc = L.up.scales.as<float>(); rows = ff; break;
+    case QB_T_DOWN: src = L.down.w.as<uint8_t>(); sc = L.down.scales.as<float>(); rows = h; cols = ff; stride = m->sff; break;
+    case QB_T_O: rows = h; sc = L.so.as<float>(); break;
+    default: return QB_INVALID_PARAMETERS;
+    }
+    if (vl != rows * cols) { set_detail(0, rows * cols, vl); return QB_INVALID_LENGTH; }
+    if (sl != rows) { set_detail(1, rows, sl); return QB_INVALID_LENGTH; }
+    DeviceGuard dg(m->device);
+    DevBuf tmp;
+    uint32_t s;
+    if ((s = tmp.alloc(rows * cols, false))) return s;
+    if (tensor == QB_T_O) {
+        const size_t hd = m->c.head_dim;
+        std::vector<int8_t> blk(h * hd), out(h * h);
+        DevBuf b1;
+        if ((s = b1.alloc(h * hd, false))) return s;
+        for (size_t hh = 0; hh < m->c.query_heads; ++hh) {
+            unbias_kernel<<<gridn(h * hd), 256>>>(L.wo.as<uint8_t>() + hh * h * m->shd, h, hd, m->shd, b1.as<int8_t>());
+            QB_CUDA(cudaMemcpy(blk.data(), b1.p, h * hd, cudaMemcpyDeviceToHost));
+            for (size_t r = 0; r < h; ++r) memcpy(&out[r * h + hh * hd], &blk[r * hd], hd);
+        }
+        memcpy(values, out.data(), h * h);
+    } else {
+        unbias_kernel<<<gridn(rows * cols), 256>>>(src, rows, cols, stride, tmp.as<int8_t>());
+        QB_CUDA(cudaGetLastError());
+        QB_CUDA(cudaMemcpy(values, tmp.p, rows * cols, cudaMemcpyDeviceToHost));
+    }
+    QB_CUDA(cudaMemcpy(scales, sc, rows * 4, cudaMemcpyDeviceToHost));
+    return QB_OK;
+}
+
+uint32_t qb_model_free(uint64_t model) {
+    std::shared_ptr<Model> m;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        auto it = g_models.find(model);
+        if (it == g_models.end()) return QB_INVALID_HANDLE;
+        m = it->second;
+        g_models.erase(it);
+    }
+    DeviceGuard dg(m->device);
+    m.reset();  // sessions hold their own reference
+    return QB_OK;
+}
+
+// -------------------------------------------------------------- session ----
+
+static uint32_t session_create(uint64_t model, size_t capacity, uint32_t kv_dtype, size_t budget,
+                               std::shared_ptr<Session> &out) {
+    auto m = find_model(model);
+    if (!m) return QB_INVALID_HANDLE;
+    if (!m->finalized) return QB_INVALID_STATE;
+    const qb_model_config &c = m->c;
+    if (capacity == 0 || capacity > c.max_tokens) return QB_INVALID_CAPACITY;
+    if (kv_dtype > QB_KV_BF16) return QB_INVALID_PARAMETERS;
+    size_t per, logical;
+    if (mul_ovf(c.kv_heads, capacity, &per) || mul_ovf(per, c.head_dim, &per) || mul_ovf(per, 2, &logical) ||
+        mul_ovf(logical, c.layers, &logical) || mul_ovf(logical, 4, &logical))
+        return QB_DIMENSION_OVERFLOW;
+    size_t ws = ref_workspace_bytes(c, capacity);
+    if (budget && (logical > SIZE_MAX - ws || logical + ws > budget)) return QB_RESOURCE_BUDGET;
+    auto s = std::make_shared<Session>();
+    s->m = m;
+    s->device = m->device;
+    s->capacity = capacity;
+    s->kv_bf16 = kv_dtype == QB_KV_BF16;
+    DeviceGuard dg(m->device);
+    uint32_t st = session_build(*s);
+    if (st) return st == QB_CUDA_ERROR ? QB_ALLOCATION : st;
+    out = s;
+    return QB_OK;
+}
+
+uint32_t qb_session_create(uint64_t model, size_t capacity, uint32_t kv_dtype, size_t budget, uint64_t *out) {
+    clear_detail();
+    if (!out) return QB_INVALID_PARAMETERS;
+    std::shared_ptr<Session> s;
+    uint32_t st = session_create(model, capacity, kv_dtype, budget, s);
+    if (st) return st;
+    std::lock_guard<std::mutex> lk(g_mu);
+    uint64_t id = g_next++;
+    g_sessions[id] = s;
+    *out = id;
+    return QB_OK;
+}
+
+uint32_t qb_session_step(uint64_t session, uint32_t token, float *logits, size_t logits_len, uint32_t *argmax) {
+    clear_detail();
+    auto s = find_session(session);
+    if (!s) return QB_INVALID_HANDLE;
+    return session_step(*s, token, logits, logits_len, argmax, false);
+}
+
+uint32_t qb_session_append(uint64_t session, const uint32_t *tokens, size_t n, float *logits,
+                           size_t logits_len, uint32_t *argmax, int32_t require_empty) {
+    clear_detail();
+    auto s = find_session(session);
+    if (!s) return QB_INVALID_HANDLE;
+    Session &S = *s;
+    // append_into admission, src/kv_cache.rs:255-279.
+    if (!S.valid) return QB_INVALID_STATE;
+    if (require_empty && S.processed != 0) return QB_NOT_EMPTY;
+    if (n == 0 || !tokens) return QB_EMPTY_INPUT;
+    if (logits && logits_len != S.m->c.vocab_size) return QB_INVALID_OUTPUT_LENGTH;
+    for (size_t i = 0; i < n; ++i)
+        if (tokens[i] >= S.m->c.vocab_size) return QB_INVALID_TOKEN;
+    if (S.processed + n > S.capacity) return QB_FULL;
+    for (size_t i = 0; i < n; ++i) {
+        bool last = i + 1 == n;
+        uint32_t st = session_step(S, tokens[i], last ? logits : nullptr, logits_len, last ? argmax : nullptr, last);
+        if (st) return st;
+    }
+    return QB_OK;
+}
+
+uint32_t qb_session_reset(uint64_t session) {
+    auto s = find_session(session);
+    if (!s) return QB_INVALID_HANDLE;
+    s->processed = 0;
+    s->valid = true;
+    s->logits_valid = false;
+    return QB_OK;
+}
+
+uint32_t qb_session_info_get(uint64_t session, qb_session_info *out) {
+    auto s = find_session(session);
+    if (!s) return QB_INVALID_HANDLE;
+    if (!out) return QB_INVALID_PARAMETERS;
+    out->processed = s->processed;
+    out->capacity = s->capacity;
+    out->logical_bytes = s->logical_bytes;
+    out->workspace_bytes = s->workspace_bytes;
+    out->valid = s->valid ? 1 : 0;
+    return QB_OK;
+}
+
+uint32_t qb_session_decode_greedy(uint64_t session, uint32_t token, size_t steps, uint32_t *ids) {
+    clear_detail();
+    auto sp = find_session(session);
+    if (!sp) return QB_INVALID_HANDLE;
+    Session &s = *sp;
+    if (!s.valid) return QB_INVALID_STATE;
+    if (steps == 0 || !ids) return QB_EMPTY_INPUT;
+    if (token >= s.m->c.vocab_size) return QB_INVALID_TOKEN;
+    if (s.processed + steps > s.capacity) return QB_FULL;
+    DeviceGuard dg(s.device);
+    const size_t start = s.processed;
+    // The first launch takes the host token; each step then feeds its own
+    // argmax to the next through the device control block.
+    s.hctrl->token = (int)token;
+    s.hctrl->pos = (int)start;
+    s.hctrl->write_logits = 0;
+    cudaError_t e = cudaMemcpyAsync(s.ctrl.p, s.hctrl, 16, cudaMemcpyHostToDevice, s.stream);
+    for (size_t i = 0; i < steps && e == cudaSuccess; ++i) e = decode_launch(s.params, s.grid, s.stream);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync((char *)s.hctrl + 16, (char *)s.ctrl.p + 16, 8, cudaMemcpyDeviceToHost, s.stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s.stream);
+    if (e != cudaSuccess) return session_fail(s, cuda_status(e));
+    if (s.hctrl->error) return session_fail(s, (s.hctrl->error & ERR_TIMEOUT) ? QB_DEVICE_TIMEOUT : QB_NONFINITE);
+    std::vector<int> out(steps);
+    e = cudaMemcpy(out.data(), s.emitted.as<int>() + start, steps * 4, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return session_fail(s, cuda_status(e));
+    for (size_t i = 0; i < steps; ++i) ids[i] = (uint32_t)out[i];
+    s.processed += steps;
+    s.logits_valid = false;
+    return QB_OK;
+}
+
+uint32_t qb_session_stream(uint64_t session, void **stream) {
+    auto s = find_session(session);
+    if (!s) return QB_INVALID_HANDLE;
+    *stream = (void *)s->stream;
+    return QB_OK;
+}
+
+uint32_t qb_session_free(uint64_t session) {
+    std::shared_ptr<Session> s;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        auto it = g_sessions.find(session);
+        if (it == g_sessions.end()) return QB_INVALID_HANDLE;
+        s = it->second;
+        g_sessions.erase(it);
+    }
+    return QB_OK;
+}
+
+// ----------------------------------------------------------- generation ----
+
+uint32_t qb_generation_create(uint64_t model, size_t capacity, const uint32_t *stops, size_t nstops,
+                              size_t max_new, uint32_t kv_dtype, size_t budget, uint64_t *out) {
+    clear_detail();
+    if (!out) return QB_INVALID_PARAMETERS;
+    auto m = find_model(model);
+    if (!m) return QB_INVALID_HANDLE;
+    // GenerationSession::new, src/generation.rs:111-138.
+    if (max_new == 0 || max_new >= capacity) return QB_INVALID_PARAMETERS;
+    for (size_t i = 0; i < nstops; ++i)
+        if (stops[i] >= m->c.vocab_size) return QB_INVALID_PARAMETERS;
+    std::shared_ptr<Session> s;
+    uint32_t st = session_create(model, capacity, kv_dtype, budget, s);
+    if (st) return st;
+    auto g = std::make_shared<Generation>();
+    g->cache = s;
+    g->stops.assign(stops, stops + nstops);
+    g->max_new = max_new;
+    g->vocab = (uint32_t)m->c.vocab_size;
+    g->history.reserve(capacity);
+    std::lock_guard<std::mutex> lk(g_mu);
+    uint64_t id = g_next++;
+    g_generations[id] = g;
+    *out = id;
+    return QB_OK;
+}
+
+uint32_t qb_generation_start(uint64_t gen, const uint32_t *prompt, size_t n, const volatile int32_t *cancel) {
+    clear_detail();
+    auto gp = find_generation(gen);
+    if (!gp) return QB_INVALID_HANDLE;
+    Generation &g = *gp;
+    // start_with_cancel, src/generation.rs:145-170.
+    if (!g.history.empty()) return QB_ALREADY_STARTED;
+    if (n == 0 || !prompt) return QB_INVALID_PARAMETERS;
+    for (size_t i = 0; i < n; ++i)
+        if (prompt[i] >= g.vocab) return QB_INVALID_PARAMETERS;
+    if (n > SIZE_MAX - g.max_new || n + g.max_new > g.cache->capacity) return QB_INVALID_PARAMETERS;
+    if (cancelled(cancel)) return QB_CANCELLED;
+    if (!g.cache->valid) return QB_INVALID_STATE;
+    g.history.insert(g.history.end(), prompt, prompt + n);
+    return evaluate_pending(g, cancel);
+}
+
+uint32_t qb_generation_next_token(uint64_t gen, const volatile int32_t *cancel, uint32_t *token, int32_t *has) {
+    clear_detail();
+    auto gp = find_generation(gen);
+    if (!gp) return QB_INVALID_HANDLE;
+    Generation &g = *gp;
+    if (has) *has = 0;
+    // next_token, src/generation.rs:307-337.
+    if (cancelled(cancel)) return QB_CANCELLED;
+    if (!g.cache->valid) return QB_INVALID_STATE;
+    if (g.history.empty()) return QB_NOT_STARTED;
+    if (g.stop != QB_STOP_NONE) return QB_OK;
+    uint32_t st = evaluate_pending(g, cancel);
+    if (st) return st;
+    if (!g.logits_ready) return QB_NOT_STARTED;
+    uint32_t next = g.last_argmax;
+    g.history.push_back(next);
+    g.generated += 1;
+    g.logits_ready = false;
+    if (std::find(g.stops.begin(), g.stops.end(), next) != g.stops.end()) g.stop = QB_STOP_TOKEN;
+    else if (g.generated == g.max_new) g.stop = QB_STOP_OUTPUT_LIMIT;
+    if (token) *token = next;
+    if (has) *has = 1;
+    return QB_OK;
+}
+
+uint32_t qb_generation_append_context(uint64_t gen, const uint32_t *suffix, size_t n, size_t max_new,
+                                      const volatile int32_t *cancel) {
+    clear_detail();
+    auto gp = find_generation(gen);
+    if (!gp) return QB_INVALID_HANDLE;
+    Generation &g = *gp;
+    const size_t cap = g.cache->capacity;
+    // admit_context, src/generation.rs:183-218.
+    bool bad = g.history.empty() || g.stop == QB_STOP_NONE || n == 0 || !suffix || max_new == 0 || max_new >= cap;
+    if (!bad)
+        for (size_t i = 0; i < n; ++i)
+            if (suffix[i] >= g.vocab) bad = true;
+    if (!bad && (g.history.size() > SIZE_MAX - n || g.history.size() + n > SIZE_MAX - max_new ||
+                 g.history.size() + n + max_new > cap))
+        bad = true;
+    if (bad) return QB_INVALID_PARAMETERS;
+    if (!g.cache->valid) return QB_INVALID_STATE;
+    if (cancelled(cancel)) return QB_CANCELLED;
+    g.history.insert(g.history.end(), suffix, suffix + n);
+    g.max_new = max_new;
+    g.generated = 0;
+    g.stop = QB_STOP_NONE;
+    return evaluate_pending(g, cancel);
+}
+
+uint32_t qb_generation_replay_history(uint64_t gen, const uint32_t *hist, size_t n, size_t max_new,
+                                      const volatile int32_t *cancel) {
+    clear_detail();
+    auto gp = find_generation(gen);
+    if (!gp) return QB_INVALID_HANDLE;
+    Generation &g = *gp;
+    const size_t cap = g.cache->capacity;
+    // admit_replay, src/generation.rs:228-257.
+    bool bad = n == 0 || !hist || max_new == 0 || max_new >= cap;
+    if (!bad)
+        for (size_t i = 0; i < n; ++i)
+            if (hist[i] >= g.vocab) bad = true;
+    if (!bad && (n > SIZE_MAX - max_new || n + max_new > cap)) bad = true;
+    if (bad) return QB_INVALID_PARAMETERS;
+    if (cancelled(cancel)) return QB_CANCELLED;
+    std::vector<uint32_t> copy(hist, hist + n);  // `hist` may alias our history
+    generation_reset(g);
+    g.max_new = max_new;
+    g.history = copy;
+    return evaluate_pending(g, cancel);
+}
+
+uint32_t qb_generation_reset(uint64_t gen) {
+    auto gp = find_generation(gen);
+    if (!gp) return QB_INVALID_HANDLE;
+    generation_reset(*gp);
+    return QB_OK;
+}
+
+uint32_t qb_generation_info_get(uint64_t gen, qb_generation_info *out) {
+    auto gp = find_generation(gen);
+    if (!gp) return QB_INVALID_HANDLE;
+    if (!out) return QB_INVALID_PARAMETERS;
+    out->processed = gp->cache->processed;
+    out->history_len = gp->history.size();
+    out->generated = gp->generated;
+    out->max_new = gp->max_new;
+    out->stop_reason = gp->stop;
+    out->valid = gp->cache->valid ? 1 : 0;
+    out->logits_ready = gp->logits_ready ? 1 : 0;
+    return QB_OK;
+}
+
+uint32_t qb_generation_history(uint64_t gen, uint32_t *ids, size_t cap, size_t *len) {
+    auto gp = find_generation(gen);
+    if (!gp) return QB_INVALID_HANDLE;
+    size_t n = gp->history.size();
+    if (len) *len = n;
+    if (ids) memcpy(ids, gp->history.data(), std::min(n, cap) * 4);
+    return QB_OK;
+}
+
+uint32_t qb_generation_prefix_logits(uint64_t gen, float *logits, size_t n) {
+    clear_detail();
+    auto gp = find_generation(gen);
+    if (!gp) return QB_INVALID_HANDLE;
+    Session &s = *gp->cache;
+    // prefix_logits, src/generation.rs:281-283: valid cache and processed > 0.
+    if (!s.valid || s.processed == 0 || !s.logits_valid) return QB_NOT_STARTED;
+    if (n != s.m->c.vocab_size) return QB_INVALID_OUTPUT_LENGTH;
+    DeviceGuard dg(s.device);
+    QB_CUDA(cudaMemcpy(logits, s.logits.p, n * 4, cudaMemcpyDeviceToHost));
+    return QB_OK;
+}
+
+uint32_t qb_generation_free(uint64_t gen) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = g_generations.find(gen);
+    if (it == g_generations.end()) return QB_INVALID_HANDLE;
+    g_generations.erase(it);
+    return QB_OK;
+}
+
+}  // extern "C"

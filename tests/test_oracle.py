@@ -1,0 +1,445 @@
+"""Pins the CPU oracle to the reference's golden vectors and known answers.
+
+Each test names the reference test it restates.  The oracle is the checker
+for every GPU parity test, so it is validated here first, on CPU.
+"""
+import numpy as np
+import pytest
+
+from conftest import assert_close, golden
+from llm_inference_edu_b200 import presets
+
+
+def tiny_model(o, max_tokens=32, **mods):
+    w = presets.tiny_r_weights()
+    for layer in w["layers"]:
+        layer.update(mods)
+    return o.Model(presets.tiny_r(max_tokens), w), w
+
+
+# ------------------------------------------------------------- linear ----
+
+def test_linear_known_answers(oracle):
+    # tests/linear.rs:3-67
+    s, y, _ = oracle.linear([1, 2, 3, 4, 5, 6], [1, 0, -1, 2, 1, 0], 2, 3, 2)
+    assert s == 0 and list(y) == [-2, 4, -2, 13]
+    s, y, _ = oracle.linear([2, -1], [3, 4, -2, 5], 1, 2, 2)
+    assert list(y) == [2, -9]
+    s, y, _ = oracle.linear([1, 2, 3, 4, -1, 5], [1, 0, 0, 1, 1, 1, 2, -1], 3, 2, 4)
+    assert list(y) == [1, 2, 3, 0, 3, 4, 7, 2, -1, 5, 4, -7]
+    s, y, _ = oracle.linear([-2, 3, 1, -4], [-1, 2, 3, -2], 2, 2, 2)
+    assert list(y) == [8, -12, -9, 11]
+    s, y, _ = oracle.linear([1, 2, 3, 4, 5], [1, -1, 2, 0, -2], 1, 5, 1, lanes4=True)
+    assert list(y) == [-5]
+
+
+@pytest.mark.parametrize("xl,wl,yl,buf,exp", [(5, 6, 4, 0, 6), (7, 6, 4, 0, 6), (6, 5, 4, 1, 6),
+                                               (6, 7, 4, 1, 6), (6, 6, 3, 2, 4), (6, 6, 5, 2, 4)])
+def test_linear_lengths_leave_output_unchanged(oracle, xl, wl, yl, buf, exp):
+    # tests/linear.rs:69-100
+    s, y, d = oracle.linear(np.ones(xl), np.ones(wl), 2, 3, 2, y_len=yl)
+    assert s == oracle.INVALID_LENGTH and (d.buffer, d.expected) == (buf, exp)
+    assert np.all(y == 37.0)
+
+
+def test_linear_zero_and_overflow(oracle):
+    # tests/linear.rs:102-130
+    for t, i, o in [(0, 3, 2), (2, 0, 2), (2, 3, 0), (0, 0, 0)]:
+        s, y, _ = oracle.linear([], [], t, i, o, y_len=4)
+        assert s == oracle.ZERO_DIMENSION and np.all(y == 37)
+    big = 2**64 - 1
+    for t, i, o in [(big, 2, 1), (1, big, 2), (big, 1, 2)]:
+        s, y, _ = oracle.linear([], [], t, i, o, y_len=4)
+        assert s == oracle.DIMENSION_OVERFLOW and np.all(y == 37)
+
+
+def test_lanes_and_scalar_match_f64(oracle):
+    # tests/kernels.rs:29-60
+    for n in [1, 2, 3, 4, 5, 7, 8, 9, 31, 32, 33, 63, 64, 65, 127, 896, 4864]:
+        x = ((np.arange(3 * n) * 17 % 101) - 50.0).astype(np.float32) / np.float32(53)
+        w = ((np.arange(7 * n) * 23 % 97) - 48.0).astype(np.float32) / np.float32(61)
+        exp = x.reshape(3, n).astype(np.float64) @ w.reshape(7, n).astype(np.float64).T
+        for lanes in (False, True):
+            s, y, _ = oracle.linear(x, w, 3, n, 7, lanes4=lanes)
+            assert s == 0
+            assert_close(y, exp.ravel().astype(np.float32), name=f"n={n}")
+
+
+# --------------------------------------------------------------- int8 ----
+
+def test_encode_kat(oracle):
+    # src/quantization.rs:284-300
+    for w, q in [(-400, -127), (-127.5, -127), (-0.5, -1), (0, 0), (0.5, 1), (127.5, 127), (400, 127)]:
+        assert oracle.lib().or_encode(w, 1.0) == q
+
+
+def test_quantize_rounding_zero_groups_tail(oracle):
+    # tests/quantization.rs:3-24
+    s, q = oracle.quantize([127, 0.5, -0.5, 0, 254, 0, 0, 0, 0, 0], 2, 5, 4)
+    assert s == 0
+    assert list(q.values.ravel()) == [127, 1, -1, 0, 127, 0, 0, 0, 0, 0]
+    assert list(q.scales.ravel()) == [1, 2, 1, 1]
+    assert q.groups_per_row == 2 and q.logical_bytes == 10 + 16
+    assert list(oracle.dequantize(q)) == [127, 1, -1, 0, 254, 0, 0, 0, 0, 0]
+    s, y = oracle.linear_int8([0.5, 2, -1, 4, 0.25], q, 1)
+    assert list(y) == [130, 0]
+
+
+def test_quantize_matches_independent_equations_and_fused_dot(oracle):
+    # tests/quantization.rs:25-86
+    for width in [1, 3, 7, 32, 33, 65, 127, 896]:
+        for group in [1, 3, 4, 32, 64, 256]:
+            rows = 7
+            w = ((np.arange(rows * width) * 23 % 97) - 48.0).astype(np.float32) / np.float32(61)
+            x = ((np.arange(3 * width) * 17 % 101) - 50.0).astype(np.float32) / np.float32(53)
+            s, q = oracle.quantize(w, rows, width, group)
+            assert s == 0
+            wr = w.reshape(rows, width)
+            for o in range(rows):
+                for g in range(-(-width // group)):
+                    seg = wr[o, g * group:(g + 1) * group].astype(np.float64)
+                    m = np.abs(seg).max()
+                    es = np.float32(1.0) if m == 0 else np.float32(m / 127.0)
+                    assert q.scales[o, g] == es
+                    ratio = (seg / np.float64(es)).astype(np.float32).astype(np.float64)
+                    expq = np.clip(np.sign(ratio) * np.floor(np.abs(ratio) + 0.5), -127, 127)
+                    assert np.array_equal(q.values[o, g * group:(g + 1) * group], expq.astype(np.int8))
+            deq = oracle.dequantize(q)
+            s1, fused = oracle.linear_int8(x, q, 3)
+            s2, ref, _ = oracle.linear(x, deq, 3, width, rows)
+            assert np.array_equal(fused, ref)
+
+
+def test_quantize_admission(oracle):
+    # tests/quantization.rs:87-122
+    for g in [0, 257]:
+        assert oracle.quantize([], 1, 1, g)[0] == oracle.INVALID_GROUP_SIZE
+    for r, c in [(0, 1), (1, 0)]:
+        assert oracle.quantize([], r, c, 32)[0] == oracle.ZERO_DIMENSION
+    for n in (3, 5):
+        assert oracle.quantize(np.ones(n), 2, 2, 4)[0] == oracle.INVALID_LENGTH
+    for v in [np.nan, np.inf, -np.inf]:
+        assert oracle.quantize([1, v], 1, 2, 32)[0] == oracle.NONFINITE_WEIGHT
+    tiny = np.array([1], dtype=np.uint32).view(np.float32)
+    assert oracle.quantize(tiny, 1, 1, 32)[0] == oracle.UNREPRESENTABLE_SCALE
+
+
+def test_quantize_fp32_half_case_and_subnormal(oracle):
+    # tests/quantization.rs:150-178
+    mx = np.array([1061777744], dtype=np.uint32).view(np.float32)[0]
+    half = np.array([1053389136], dtype=np.uint32).view(np.float32)[0]
+    s, q = oracle.quantize([mx, half], 1, 2, 2)
+    assert q.scales.view(np.uint32)[0, 0] == 1003161439
+    assert list(q.values.ravel()) == [127, 64]
+    w = np.array([190], dtype=np.uint32).view(np.float32)
+    s, q = oracle.quantize(w, 1, 1, 32)
+    assert q.scales.view(np.uint32)[0, 0] == 1 and list(q.values.ravel()) == [127]
+    s, y = oracle.linear_int8([1.0], q, 1)
+    assert y.view(np.uint32)[0] == 127
+
+
+def test_per_row_group_equals_groupwise_arithmetic(oracle):
+    # Per-row (group == input_dim) reuses the per-group arithmetic of
+    # src/quantization.rs:91-101 with one group per row.
+    w = ((np.arange(5 * 300) * 23 % 97) - 48.0).astype(np.float32) / np.float32(61)
+    s, q = oracle.quantize(w, 5, 300, 300)
+    assert s == 0 and q.scales.shape == (5, 1)
+    for o in range(5):
+        m = np.abs(w[o * 300:(o + 1) * 300]).max()
+        assert q.scales[o, 0] == np.float32(m) / np.float32(127)
+
+
+# ---------------------------------------------------------------- ops ----
+
+def test_ops_match_t01(oracle):
+    # tests/basic_ops.rs against fixtures/t01-*
+    inp, exp = golden("t01-inputs.json"), golden("t01-expected.json")["outputs"]
+    c = inp["embedding"]
+    s, y = oracle.embedding(c["token_ids"], c["table"], c["vocab_size"], c["width"])
+    assert_close(y, exp["embedding"])
+    c = inp["residual_add"]
+    assert_close(oracle.residual_add(c["x"], c["residual"])[1], exp["residual_add"])
+    c = inp["rmsnorm"]
+    assert_close(oracle.rmsnorm(c["x"], c["weight"], c["rows"], c["width"], c["epsilon"])[1], exp["rmsnorm"])
+    assert_close(oracle.silu(inp["silu"]["x"])[1], exp["silu"])
+    c = inp["softmax"]
+    assert_close(oracle.softmax(c["logits"], c["rows"], c["width"])[1], exp["softmax"])
+    c = inp["masked_softmax"]
+    assert_close(oracle.softmax(c["logits"], c["rows"], c["width"], c["mask"])[1], exp["masked_softmax"])
+
+
+def test_softmax_admission(oracle):
+    # src/ops.rs:214-232: all rows admitted before writes; all-masked rows rejected
+    s, y = oracle.softmax([1, 2, 3, 4], 2, 2, mask=[1, 1, 0, 0])
+    assert s == oracle.ALL_MASKED
+    s, y = oracle.softmax([1, np.nan, 3, 4], 2, 2)
+    assert s == oracle.NONFINITE
+    s, y = oracle.softmax([np.nan, 0, 3, 4], 2, 2, mask=[0, 1, 1, 1])
+    assert s == 0
+
+
+def test_rope_matches_t02(oracle):
+    # tests/rope.rs:18-56
+    inp, exp = golden("t02-inputs.json"), golden("t02-expected.json")["outputs"]
+    for c in inp["cases"]:
+        s, y = oracle.rope(c["x"], c["tokens"], c["heads"], c["head_dim"], c["start_position"], c["base"])
+        assert s == 0
+        assert_close(y, exp[c["name"]], name=c["name"])
+
+
+def test_rope_identity_at_zero_and_offsets(oracle):
+    # tests/rope.rs:57-72
+    x = np.arange(16, dtype=np.float32)
+    s, y = oracle.rope(x, 1, 2, 8, 0, 10000.0)
+    assert np.array_equal(y, x)
+    x = np.arange(48, dtype=np.float32) / 7
+    _, whole = oracle.rope(x, 3, 2, 8, 5, 10000.0)
+    _, tail = oracle.rope(x[16:], 2, 2, 8, 6, 10000.0)
+    assert np.array_equal(tail, whole[16:])
+
+
+# -------------------------------------------------------------- model ----
+
+def test_decoder_matches_t04_every_activation(oracle):
+    # tests/model.rs:30-75
+    m, _ = tiny_model(oracle)
+    ids = golden("t04-inputs.json")["token_ids"]
+    exp = golden("t04-expected.json")["outputs"]
+    s, logits, trace = m.forward(ids, trace=True)
+    assert s == 0
+    for name, values in exp.items():
+        assert_close(trace[name], values, name=name)
+    assert np.array_equal(logits, trace["logits"][2 * 64:])
+    s, plain, _ = m.forward(ids)
+    assert np.array_equal(plain, logits)
+
+
+def test_attention_matches_t03(oracle):
+    # tests/attention.rs:25-73, as a one-layer model whose norms are identity
+    # on already-normalized rows is not available; use the decoder pieces:
+    inp, exp = golden("t03-inputs.json"), golden("t03-expected.json")["outputs"]
+    t, h, qh, kvh, d = (inp[k] for k in ["tokens", "hidden_dim", "query_heads", "kv_heads", "head_dim"])
+    x = np.asarray(inp["x"], np.float32)
+    _, q, _ = oracle.linear(x, inp["query"], t, h, qh * d)
+    _, k, _ = oracle.linear(x, inp["key"], t, h, kvh * d)
+    _, v, _ = oracle.linear(x, inp["value"], t, h, kvh * d)
+    assert_close(q, exp["query"]); assert_close(k, exp["key"]); assert_close(v, exp["value"])
+    _, qr = oracle.rope(q, t, qh, d, inp["start_position"], inp["rope_base"])
+    _, kr = oracle.rope(k, t, kvh, d, inp["start_position"], inp["rope_base"])
+    assert_close(qr, exp["rotated_query"]); assert_close(kr, exp["rotated_key"])
+
+
+def test_uncached_greedy_kat_and_stop(oracle):
+    # tests/generation.rs:7-18
+    m, _ = tiny_model(oracle)
+    s, ids = m.uncached_greedy([1, 5, 7], [], 4)
+    assert s == 0 and ids == [41, 53, 41, 50]
+    s, ids = m.uncached_greedy([1, 5, 7], [41], 4)
+    assert ids == [41]
+
+
+def test_uncached_greedy_admission(oracle):
+    # tests/generation.rs:19-49
+    m, _ = tiny_model(oracle)
+    assert m.uncached_greedy([], [], 1)[0] == 36
+    assert m.uncached_greedy([1], [], 0)[0] == 37
+    assert m.uncached_greedy([64], [], 1)[0] == oracle.INVALID_TOKEN
+    assert m.uncached_greedy([1], [64], 1)[0] == oracle.INVALID_TOKEN
+    assert m.uncached_greedy([1] * 32, [], 1)[0] == oracle.CONTEXT_LIMIT
+    s, ids = m.uncached_greedy([1] * 31, [], 1)
+    assert s == 0 and len(ids) == 1
+
+
+def test_ties_choose_lowest_id(oracle):
+    # tests/generation.rs:50-61: zero embeddings -> all logits equal -> id 0
+    w = presets.tiny_r_weights()
+    w["embedding"] = np.zeros_like(w["embedding"])
+    m = oracle.Model(presets.tiny_r(), w)
+    assert m.uncached_greedy([1], [], 1)[1] == [0]
+
+
+def test_cached_equals_uncached_bitwise(oracle):
+    # tests/kv_cache.rs:5-25
+    m, _ = tiny_model(oracle)
+    sess = oracle.Session(m, 8)
+    ids = [1, 5, 7, 7, 41, 53, 2, 63]
+    for p, t in enumerate(ids):
+        s, cached = sess.step(t)
+        assert s == 0
+        _, unc, _ = m.forward(ids[:p + 1])
+        assert np.array_equal(cached, unc), p
+        assert sess.processed == p + 1
+    assert sess.step(1)[0] == oracle.FULL
+    assert sess.logical_bytes == 2 * 2 * 8 * 8 * 2 * 4
+
+
+def test_cached_biases_match_uncached(oracle):
+    # tests/kv_cache.rs:118-137
+    m, _ = tiny_model(oracle, q_bias=np.full(32, 0.125, np.float32),
+                      k_bias=np.full(16, -0.25, np.float32), v_bias=np.full(16, 0.5, np.float32))
+    sess = oracle.Session(m, 3)
+    for p, t in enumerate([1, 5, 7]):
+        assert np.array_equal(sess.step(t)[1], m.forward([1, 5, 7][:p + 1])[1])
+
+
+def test_prefill_partitions_identical(oracle):
+    # tests/prefill.rs:7-33
+    m, _ = tiny_model(oracle)
+    ids = [1, 5, 7, 41, 53, 41, 50, 2]
+    expected = m.forward(ids)[1]
+    sess = oracle.Session(m, 8)
+    assert np.array_equal(sess.prefill(ids)[1], expected)
+    for parts in [[1, 7], [3, 5], [2, 2, 4], [1] * 8]:
+        sess.reset()
+        end = 0
+        for i, c in enumerate(parts):
+            b, end = end, end + c
+            s, lg = sess.prefill(ids[b:end]) if i == 0 else sess.append(ids[b:end])
+            assert s == 0 and np.array_equal(lg, m.forward(ids[:end])[1])
+        assert sess.append([1])[0] == oracle.FULL
+
+
+def fragile_model(oracle, max_tokens=2, embedding=(0.0, 0.0, 1.0, 1.0)):
+    # The degenerate model of tests/kv_cache.rs:67-110 (down = f32::MAX).
+    from llm_inference_edu_b200.presets import ModelConfig
+    cfg = ModelConfig(2, 1, 2, 1, 1, 2, 2, max_tokens, 10000.0, 1e-5)
+    fmax = np.finfo(np.float32).max
+    layer = dict(attn_norm=np.ones(2, np.float32), q=np.zeros(4, np.float32), k=np.zeros(4, np.float32),
+                 v=np.array([1, 0, 0, 1], np.float32), o=np.zeros(4, np.float32),
+                 ffn_norm=np.ones(2, np.float32), gate=np.ones(4, np.float32), up=np.ones(4, np.float32),
+                 down=np.full(4, fmax, np.float32))
+    w = dict(embedding=np.array(embedding, np.float32), layers=[layer], final_norm=np.ones(2, np.float32))
+    return oracle.Model(cfg, w), cfg, w
+
+
+def test_execution_failure_invalidates(oracle):
+    # tests/kv_cache.rs:67-110, tests/prefill.rs:59-108
+    m, _, _ = fragile_model(oracle)
+    sess = oracle.Session(m, 2)
+    assert sess.prefill([0, 1])[0] == oracle.NONFINITE
+    assert sess.processed == 0 and not sess.valid
+    assert sess.append([0])[0] == oracle.INVALID_STATE
+    sess.reset()
+    s, lg = sess.prefill([0])
+    assert s == 0 and list(lg) == [0, 0]
+
+
+def test_admission_errors_preserve_prefix(oracle):
+    # tests/kv_cache.rs:43-66, tests/prefill.rs:34-58
+    m, _ = tiny_model(oracle)
+    assert oracle.Session(m, 0).status == oracle.INVALID_CAPACITY
+    assert oracle.Session(m, 33).status == oracle.INVALID_CAPACITY
+    sess = oracle.Session(m, 4)
+    assert sess.prefill([1, 64])[0] == oracle.INVALID_TOKEN and sess.processed == 0
+    assert sess.prefill([])[0] == oracle.EMPTY_INPUT
+    sess.prefill([1, 5])
+    assert sess.prefill([7])[0] == oracle.NOT_EMPTY
+    assert sess.append([7, 7, 7])[0] == oracle.FULL
+    assert np.array_equal(sess.append([7, 41])[1], m.forward([1, 5, 7, 41])[1])
+
+
+def test_large_cache_rejected_by_budget(oracle):
+    # tests/kv_cache.rs:139-148
+    m, _ = tiny_model(oracle, max_tokens=1 << 24)
+    assert oracle.Session(m, 1 << 24).status == oracle.RESOURCE_BUDGET
+
+
+def test_workspace_bytes(oracle):
+    # tests/workspace.rs:25
+    m, _ = tiny_model(oracle)
+    assert oracle.Session(m, 8).workspace_bytes == (8 * 32 + 3 * 16 + 3 * 64 + 2 * 8) * 4
+
+
+def test_context_t28_128_positions(oracle):
+    # tests/context.rs:24-58
+    m, _ = tiny_model(oracle, max_tokens=128)
+    fx = golden("t28-tiny-context.json")
+    sess = oracle.Session(m, 128)
+    rows = {r["position"]: r for r in fx["positions"]}
+    for p, t in enumerate(fx["ids"]):
+        s, lg = sess.step(t)
+        assert s == 0
+        if p in rows:
+            assert_close(lg, rows[p]["logits"], name=f"pos {p}")
+            assert int(np.argmax(lg)) == rows[p]["greedy"]
+    assert sess.step(2)[0] == oracle.FULL
+
+
+def test_continuation_t25(oracle):
+    # src/generation.rs:365-394 against fixtures/t25-continuation.json
+    m, _ = tiny_model(oracle)
+    for case in golden("t25-continuation.json")["cases"]:
+        sess = oracle.Session(m, 32)
+        s, lg = sess.prefill(case["ids"])
+        assert_close(lg, case["logits"])
+        assert int(np.argmax(lg)) == case["greedy"]
+
+
+def test_cached_greedy_kat(oracle):
+    # tests/generation_state.rs:9-23: [1,5,7] -> [41,53,41,50]
+    m, _ = tiny_model(oracle)
+    sess = oracle.Session(m, 32)
+    assert sess.greedy([1, 5, 7], 4) == (0, [41, 53, 41, 50])
+    sess.reset()
+    assert sess.greedy([1, 5, 7], 4, stops=[41]) == (0, [41])
+
+
+def test_int8_decoder_logical_bytes(oracle):
+    # tests/quantized_model.rs:96-106: FP32 82560 B, INT8 G32 23680 B
+    w = presets.tiny_r_weights()
+    n = w["embedding"].size * 4 + w["final_norm"].size * 4
+    for layer in w["layers"]:
+        n += sum(v.size * 4 for v in layer.values())
+    assert n == 82560
+    total = w["final_norm"].size * 4
+    for name, (rows, cols) in [("embedding", (64, 32))]:
+        total += oracle.quantize(w["embedding"], rows, cols, 32)[1].logical_bytes
+    shapes = dict(q=(32, 32), k=(16, 32), v=(16, 32), o=(32, 32), gate=(64, 32), up=(64, 32), down=(32, 64))
+    for layer in w["layers"]:
+        total += (layer["attn_norm"].size + layer["ffn_norm"].size) * 4
+        for k, (r, c) in shapes.items():
+            total += oracle.quantize(layer[k], r, c, 32)[1].logical_bytes
+    assert total == 23680
+
+
+def test_int8_decoder_fused_equals_dequantized_reference(oracle):
+    # tests/quantized_model.rs:32-95: fused INT8 decode == once-dequantized
+    # FP32 decode, bit for bit, at every cached position.
+    w = presets.tiny_r_weights()
+    shapes = dict(q=(32, 32), k=(16, 32), v=(16, 32), o=(32, 32), gate=(64, 32), up=(64, 32), down=(32, 64))
+    for group in [3, 4, 32]:
+        qw = {"embedding": oracle.quantize(w["embedding"], 64, 32, group)[1], "final_norm": w["final_norm"],
+              "layers": []}
+        dw = {"embedding": oracle.dequantize(qw["embedding"]), "final_norm": w["final_norm"], "layers": []}
+        for layer in w["layers"]:
+            ql = {k: oracle.quantize(layer[k], *shapes[k], group)[1] for k in shapes}
+            ql.update(attn_norm=layer["attn_norm"], ffn_norm=layer["ffn_norm"])
+            dl = {k: (oracle.dequantize(v) if k in shapes else v) for k, v in ql.items()}
+            qw["layers"].append(ql)
+            dw["layers"].append(dl)
+        mq, md = oracle.Model(presets.tiny_r(), qw), oracle.Model(presets.tiny_r(), dw)
+        ids = [1, 5, 7, 7, 41, 53, 2, 63]
+        _, a, ta = mq.forward(ids, trace=True)
+        _, b, tb = md.forward(ids, trace=True)
+        for k in ta:
+            assert np.array_equal(ta[k], tb[k]), (group, k)
+        sess = oracle.Session(mq, 8)
+        for p, t in enumerate(ids):
+            assert np.array_equal(sess.step(t)[1], mq.forward(ids[:p + 1])[1])
+
+
+def test_tinyb_numpy_golden(oracle):
+    # Tiny-B logits and greedy ids from the reference's NumPy decoder
+    # (reference/decoder.py), generated by tests/golden/make_golden.py.
+    from llm_inference_edu_b200 import synthetic
+    fx = golden("tinyb-numpy.json")
+    cfg = presets.tiny_b()
+    w = synthetic.weights(cfg, seed=fx["weight_seed"], dtype="f32")
+    m = oracle.Model(cfg, w)
+    assert fx["prompt"] == synthetic.prompt(cfg.vocab_size, 8, seed=0)
+    sess = oracle.Session(m, 64)
+    s, ids = sess.greedy(fx["prompt"], 32)
+    assert s == 0 and ids == fx["greedy"]
+    for row in fx["positions"]:
+        _, lg, _ = m.forward(fx["history"][:row["position"] + 1])
+        assert_close(lg, row["logits"], name=f"pos {row['position']}")
