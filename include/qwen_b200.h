@@ -253,6 +253,15 @@ uint32_t qb_session_step(uint64_t session, uint32_t token, float *logits, size_t
  * returned. */
 uint32_t qb_session_append(uint64_t session, const uint32_t *tokens, size_t count, float *logits,
                            size_t logits_len, uint32_t *argmax, int32_t require_empty);
+/* step_profiled, src/kv_cache.rs:309-316: one step as qb_session_step that
+ * also records device timestamps (ns, %globaltimer) into `stamps`:
+ * [B][grid] barrier arrival times per CTA, then [B] barrier release times,
+ * then the step's start and end, where B = 4 * layers (QKV, attention,
+ * gate/up and down phases of every layer).  `*needed` receives the count;
+ * a short `stamps` buffer is an admission error (QB_INVALID_LENGTH). */
+uint32_t qb_session_step_profiled(uint64_t session, uint32_t token, float *logits,
+                                  size_t logits_len, uint32_t *argmax, uint64_t *stamps,
+                                  size_t stamps_len, size_t *needed);
 /* reset, src/kv_cache.rs:225-229. */
 uint32_t qb_session_reset(uint64_t session);
 uint32_t qb_session_info_get(uint64_t session, qb_session_info *out);

@@ -397,6 +397,43 @@ class CachedSession:
         self.append_into(tokens, logits, True)
         return logits
 
+    def step_profiled(self, token: int):
+        """One step with device timestamps (src/kv_cache.rs:309-316).
+
+        Returns (logits, profile).  profile["layers"][l] holds, for each of
+        the phases "qkv", "attention", "gate_up", "down": wall ns from the
+        previous barrier release to this phase's release ("ns"), the slowest
+        CTA's work ("slowest_ns"), the mean CTA's work ("mean_ns") and the
+        barrier latency after the last arrival ("barrier_ns")."""
+        need = C.c_size_t()
+        lib().qb_session_step_profiled(self.handle, 0, None, 0, None, None, 0, C.byref(need))
+        stamps = np.zeros(need.value, dtype=np.uint64)
+        logits = np.zeros(self.vocab, dtype=np.float32)
+        am = C.c_uint32()
+        _check(lib().qb_session_step_profiled(self.handle, token, logits.ctypes.data_as(C.c_void_p),
+                                              logits.size, C.byref(am),
+                                              stamps.ctypes.data_as(C.c_void_p), stamps.size,
+                                              C.byref(need)), CacheError)
+        L = self.model.config.layers
+        nb = 4 * L
+        grid = (stamps.size - nb - 2) // nb
+        arr = stamps[:nb * grid].reshape(nb, grid).astype(np.int64)
+        rel = stamps[nb * grid:nb * grid + nb].astype(np.int64)
+        start, end = int(stamps[-2]), int(stamps[-1])
+        names = ["qkv", "attention", "gate_up", "down"]
+        layers, prev = [], start
+        for l in range(L):
+            d = {}
+            for k, name in enumerate(names):
+                i = 4 * l + k
+                d[name] = {"ns": int(rel[i] - prev), "slowest_ns": int(arr[i].max() - prev),
+                           "mean_ns": float(arr[i].mean() - prev),
+                           "barrier_ns": int(rel[i] - arr[i].max())}
+                prev = int(rel[i])
+            layers.append(d)
+        profile = {"layers": layers, "logits_ns": end - prev, "total_ns": end - start, "argmax": am.value}
+        return logits, profile
+
     def decode_greedy(self, token: int, steps: int) -> list:
         """`steps` greedy steps on the device, each fed its own argmax."""
         out = np.zeros(steps, dtype=np.uint32)

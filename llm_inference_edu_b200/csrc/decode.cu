@@ -3,24 +3,32 @@
 // One cooperative launch evaluates one token through every layer and the LM
 // head (src/kv_cache.rs:347-475 with attend_one :479-590) and leaves the
 // greedy argmax (src/sampling.rs:65-70) in the control block.  The grid is
-// one 512-thread CTA per SM.  Phases are separated by a grid barrier whose
-// wait is bounded by a timeout (the kernel then reports ERR_TIMEOUT and
-// returns; it never spins forever):
+// one CTA per SM: 16 compute warps and one producer warp.  Compute phases
+// are separated by a grid barrier whose wait is bounded by a timeout (the
+// kernel then reports ERR_TIMEOUT, drains its own bulk copies and returns;
+// it never spins forever):
 //
 //   per layer:  QKV      RMSNorm (each CTA, redundantly) -> rows of [Wq;Wk;Wv]
 //                        + bias
-//               ATTN     per (query head, o_proj row split): RoPE from the host
+//               ATTN     per (query head, o_proj row range): RoPE from the host
 //                        cos/sin table, K/V write, softmax(q.K/sqrt d).V, then
-//                        that head's o_proj partial for a slice of rows
+//                        that head's o_proj partial for the row range
 //               GATE/UP  residual + sum of head partials, RMSNorm, rows of
 //                        gate and up, SiLU(gate)*up
 //               DOWN     rows of down + residual
 //   final:      LM HEAD  RMSNorm, rows of the (tied) table, logits, argmax;
 //                        the last CTA reduces the per-CTA argmaxes.
 //
-// Weights stream with 16-byte non-allocating loads; each CTA prefetches a
-// slice of the weights two phases ahead into L2 with cp.async.bulk.prefetch,
-// so HBM keeps streaming while the grid waits at a barrier.
+// Weight streaming.  Weights never depend on activations, so the producer
+// warp streams every row block the CTA will multiply -- all phases of the
+// step, in order -- through a shared-memory ring of `nslot` slots with 1-D
+// bulk copies (cp.async.bulk ... mbarrier::complete_tx), waiting only for
+// the compute warps to free a slot ("empty" mbarrier).  It never waits for
+// a grid barrier, so the next phases' weights are in shared memory before
+// the activations they meet exist, and no weight occupies a register.  The
+// producer also prefetches the rows a few phases ahead into L2.  The per-CTA
+// row ranges come precomputed from the host: the critical path has no
+// integer division and no long serial chain.
 #include <math.h>
 
 #include "common.cuh"
@@ -28,16 +36,19 @@
 
 namespace qb {
 
-constexpr int NT = kDecodeThreads;
-constexpr int NW = NT / 32;
-constexpr int ITEMS = 8;
+constexpr int NT = kDecodeThreads;  // compute threads
+constexpr int NW = NT / 32;         // compute warps
+constexpr int LOOKAHEAD = 3;        // L2 prefetch distance in phases
 
 template <int WF> struct Fmt;
-template <> struct Fmt<WF_F32> { static constexpr int EPC = 4; static constexpr int ESZ = 4; };
-template <> struct Fmt<WF_BF16> { static constexpr int EPC = 8; static constexpr int ESZ = 2; };
-template <> struct Fmt<WF_I8> { static constexpr int EPC = 16; static constexpr int ESZ = 1; };
+template <> struct Fmt<WF_F32> { static constexpr int EPC = 4; };
+template <> struct Fmt<WF_BF16> { static constexpr int EPC = 8; };
+template <> struct Fmt<WF_I8> { static constexpr int EPC = 16; };
 
 __device__ __forceinline__ float ldcg(const float *p) { return __ldcg(p); }
+
+// Barrier among the compute warps only (the producer warp never joins).
+__device__ __forceinline__ void csync() { asm volatile("bar.sync 1, %0;" ::"n"(NT) : "memory"); }
 
 // Dot product of one 16-byte weight chunk with EPC activations (FMA chain).
 template <int WF>
@@ -68,226 +79,358 @@ __device__ __forceinline__ float chunk_dot(const uint4 &w, const float *x) {
     return a;
 }
 
-// Block-wide reductions in a fixed order (warp xor tree, then warp partials
-// summed in warp order by thread 0), broadcast to every thread.
-__device__ __forceinline__ float block_sum(float v, float *red) {
-    int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+// Block reductions over the compute warps: warp xor trees, then warp 0 runs
+// one more tree over the warp partials -- a fixed order, broadcast to all.
+__device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int off = 16; off; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-    __syncthreads();
-    if (lane == 0) red[warp] = v;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        float s = red[0];
-        for (int i = 1; i < NW; ++i) s += red[i];
-        red[NW] = s;
-    }
-    __syncthreads();
-    return red[NW];
+    return v;
 }
-
-__device__ __forceinline__ float block_max(float v, float *red) {
-    int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+__device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
     for (int off = 16; off; off >>= 1) v = rust_max(v, __shfl_xor_sync(0xffffffffu, v, off));
-    __syncthreads();
+    return v;
+}
+__device__ __forceinline__ float block_sum(float v, float *red) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    v = warp_sum(v);
     if (lane == 0) red[warp] = v;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        float s = red[0];
-        for (int i = 1; i < NW; ++i) s = rust_max(s, red[i]);
-        red[NW] = s;
+    csync();
+    if (warp == 0) {
+        v = warp_sum(lane < NW ? red[lane] : 0.0f);
+        if (lane == 0) red[NW] = v;
     }
-    __syncthreads();
+    csync();
+    return red[NW];
+}
+__device__ __forceinline__ float block_max(float v, float *red) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    v = warp_max(v);
+    if (lane == 0) red[warp] = v;
+    csync();
+    if (warp == 0) {
+        v = warp_max(lane < NW ? red[lane] : -INFINITY);
+        if (lane == 0) red[NW] = v;
+    }
+    csync();
     return red[NW];
 }
 
 // Scaled RMSNorm of `in` (shared, width w) into `out` (shared, zero-padded
 // to `padded`), src/ops.rs:137-149.  The row scale is an exact maximum.
-__device__ void block_rmsnorm(const float *in, const float *__restrict__ gain, float *out, int w,
-                              int padded, float eps, float *red) {
+__device__ __forceinline__ void block_rmsnorm(const float *in, const float *gain, float *out, int w,
+                                              int padded, float eps, float *red) {
     const float se = sqrtf(eps);
     float m = se;
+#pragma unroll 1
     for (int i = threadIdx.x; i < w; i += NT) m = rust_max(m, fabsf(in[i]));
     m = block_max(m, red);
     float ss = 0.0f;
+#pragma unroll 1
     for (int i = threadIdx.x; i < w; i += NT) {
         float v = in[i] / m;
         ss = ss + v * v;
     }
     ss = block_sum(ss, red);
-    float seps = se / m;
-    float den = sqrtf(ss / (float)w + seps * seps);
+    const float seps = se / m;
+    const float den = sqrtf(ss / (float)w + seps * seps);
+#pragma unroll 1
     for (int i = threadIdx.x; i < padded; i += NT) out[i] = i < w ? (in[i] / m) / den * gain[i] : 0.0f;
-    __syncthreads();
-}
-
-// CTA matrix-vector product over R rows of C 16-byte chunks each.
-// rowp(r) gives row r's base; emit(r, y) runs once per row on lane 0 of a
-// warp.  When C <= NT every thread owns one chunk column (its activations in
-// registers) and walks rows; otherwise threads stride the chunks of each row.
-// Partial sums meet in shared memory and are reduced per row in a fixed order.
-template <int WF, class RowPtr, class Emit>
-__device__ void cta_gemv(RowPtr rowp, int R, int C, const float *xs, float *part, int part_cap,
-                         Emit emit) {
-    constexpr int EPC = Fmt<WF>::EPC;
-    if (R <= 0 || C <= 0) return;
-    const int t = threadIdx.x, lane = t & 31;
-    if (C <= NT) {
-        const int RS = NT / C;
-        const int c = t % C, rs = t / C;
-        const bool active = rs < RS;
-        float xr[EPC];
-#pragma unroll
-        for (int k = 0; k < EPC; ++k) xr[k] = active ? xs[c * EPC + k] : 0.0f;
-        int RR = part_cap / C;
-        if (RR < 1) RR = 1;
-        for (int row0 = 0; row0 < R; row0 += RR) {
-            const int rr = min(RR, R - row0);
-            if (active) {
-                for (int r = rs; r < rr; r += RS * ITEMS) {
-                    uint4 w[ITEMS];
-#pragma unroll
-                    for (int k = 0; k < ITEMS; ++k) {
-                        int rk = r + k * RS;
-                        if (rk < rr) w[k] = ld_stream_u4(rowp(row0 + rk) + (size_t)c * 16);
-                    }
-#pragma unroll
-                    for (int k = 0; k < ITEMS; ++k) {
-                        int rk = r + k * RS;
-                        if (rk < rr) part[rk * C + c] = chunk_dot<WF>(w[k], xr);
-                    }
-                }
-            }
-            __syncthreads();
-            for (int r = t >> 5; r < rr; r += NW) {
-                float s = 0.0f;
-                for (int cc = lane; cc < C; cc += 32) s += part[r * C + cc];
-#pragma unroll
-                for (int off = 16; off; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-                if (lane == 0) emit(row0 + r, s);
-            }
-            __syncthreads();
-        }
-    } else {
-        int RR = part_cap / NT;
-        if (RR < 1) RR = 1;
-        for (int row0 = 0; row0 < R; row0 += RR) {
-            const int rr = min(RR, R - row0);
-            for (int r = 0; r < rr; ++r) {
-                const uint8_t *row = rowp(row0 + r);
-                float acc = 0.0f;
-                for (int c0 = t; c0 < C; c0 += NT * ITEMS) {
-                    uint4 w[ITEMS];
-#pragma unroll
-                    for (int k = 0; k < ITEMS; ++k) {
-                        int c = c0 + k * NT;
-                        if (c < C) w[k] = ld_stream_u4(row + (size_t)c * 16);
-                    }
-#pragma unroll
-                    for (int k = 0; k < ITEMS; ++k) {
-                        int c = c0 + k * NT;
-                        if (c < C) acc += chunk_dot<WF>(w[k], xs + c * EPC);
-                    }
-                }
-                part[r * NT + t] = acc;
-            }
-            __syncthreads();
-            for (int r = t >> 5; r < rr; r += NW) {
-                float s = 0.0f;
-                for (int cc = lane; cc < NT; cc += 32) s += part[r * NT + cc];
-#pragma unroll
-                for (int off = 16; off; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-                if (lane == 0) emit(row0 + r, s);
-            }
-            __syncthreads();
-        }
-    }
-}
-
-// Grid barrier with a bounded wait.  Returns false (after recording
-// ERR_TIMEOUT) when the arrivals do not complete within the timeout or when
-// another CTA has already timed out.
-__device__ bool grid_barrier(DecodeCtrl *ctrl, unsigned target, unsigned long long timeout_ns,
-                             int *s_flag) {
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence();
-        red_release_add_u32(&ctrl->bar, 1u);
-        int ok = 1;
-        if (ld_acquire_u32(&ctrl->bar) < target) {
-            const uint64_t t0 = globaltimer_ns();
-            unsigned spins = 0;
-            while (ld_acquire_u32(&ctrl->bar) < target) {
-                if ((++spins & 255u) == 0) {
-                    if (*(volatile unsigned *)&ctrl->error & ERR_TIMEOUT) { ok = 0; break; }
-                    if (globaltimer_ns() - t0 > timeout_ns) {
-                        atomicOr(&ctrl->error, ERR_TIMEOUT);
-                        ok = 0;
-                        break;
-                    }
-                }
-            }
-        }
-        *s_flag = ok;
-    }
-    __syncthreads();
-    return *s_flag != 0;
+    csync();
 }
 
 __device__ __forceinline__ void flag_nonfinite(DecodeCtrl *ctrl, float v) {
     if (!isfinite(v)) atomicOr(&ctrl->error, ERR_NONFINITE);
 }
 
-// Prefetches this CTA's 1/G slice of [base, base+bytes) into L2.
-__device__ __forceinline__ void prefetch_slice(const void *base, size_t bytes, int b, int G) {
-    if (!base || bytes == 0) return;
-    size_t lo = (bytes * (size_t)b / (size_t)G) & ~(size_t)15;
-    size_t hi = (bytes * (size_t)(b + 1) / (size_t)G) & ~(size_t)15;
-    if (b == G - 1) hi = bytes & ~(size_t)15;
+// --------------------------------------------------------------- ring ----
+//
+// Chunk k of the CTA's stream lives in slot k % nslot during round
+// u = k / nslot.  full[slot] completes phase u when the copy lands; the
+// compute warps arrive on empty[slot] (phase u) once they have read it.
+
+struct Ring {
+    uint8_t *slots;
+    uint64_t *full, *empty;
+    int nslot, slot_bytes;
+};
+
+__device__ __forceinline__ Ring ring_of(const DecodeParams &p, float *sm) {
+    Ring r;
+    r.slots = (uint8_t *)(sm + p.sm_ring);
+    r.full = (uint64_t *)(sm + p.sm_bar);
+    r.empty = r.full + p.nslot;
+    r.nslot = p.nslot;
+    r.slot_bytes = p.slot_bytes;
+    return r;
+}
+
+// Bounded wait for `parity` on `bar`; on timeout (or when the CTA is already
+// aborting) records ERR_TIMEOUT, raises the abort flag and returns false.
+__device__ __noinline__ bool mbar_wait_slow(const DecodeParams &p, uint64_t *bar, uint32_t parity,
+                                            volatile int *s_abort) {
+    const uint64_t t0 = globaltimer_ns();
+    for (unsigned it = 1;; ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 63u) == 0 && (*s_abort || globaltimer_ns() - t0 > p.timeout_ns)) {
+            atomicOr(&p.ctrl->error, ERR_TIMEOUT);
+            *s_abort = 1;
+            return false;
+        }
+    }
+}
+__device__ __forceinline__ bool mbar_wait(const DecodeParams &p, uint64_t *bar, uint32_t parity,
+                                          volatile int *s_abort) {
+    return mbar_try_wait(bar, parity) || mbar_wait_slow(p, bar, parity, s_abort);
+}
+
+// Consumer cursor (identical in every compute thread).
+struct Cursor {
+    int slot, round;
+    __device__ __forceinline__ void advance(int nslot) {
+        if (++slot == nslot) { slot = 0; ++round; }
+    }
+};
+
+// --------------------------------------------------------------- producer ----
+
+struct Producer {
+    const DecodeParams &p;
+    Ring rg;
+    volatile int *s_abort;
+    int slot = 0, round = 0;
+    bool alive = true;
+
+    __device__ Producer(const DecodeParams &pp, const Ring &r, volatile int *a) : p(pp), rg(r), s_abort(a) {}
+
+    // Streams rows [0, n) of a block (stride bytes each) in ring chunks.
+    __device__ void block(const uint8_t *base, int n, const KindGeom &g) {
+#pragma unroll 1
+        for (int r = 0; r < n && alive; r += g.rpc) {
+            if (round > 0 && !mbar_wait(p, rg.empty + slot, (uint32_t)((round - 1) & 1), s_abort)) {
+                alive = false;
+                return;
+            }
+            const uint32_t bytes = (uint32_t)(min(g.rpc, n - r) * g.stride);
+            mbar_arrive_expect_tx(rg.full + slot, bytes);
+            bulk_copy_g2s(rg.slots + (size_t)slot * rg.slot_bytes, base + (size_t)r * g.stride, bytes,
+                          rg.full + slot);
+            if (++slot == rg.nslot) { slot = 0; ++round; }
+        }
+    }
+
+    // Waits (bounded) for every copy this producer issued, before exiting
+    // early.
+    __device__ void drain() {
+        const uint64_t t0 = globaltimer_ns();
+        for (int s = 0; s < rg.nslot; ++s) {
+            // Slot s was last filled in round (s < slot ? round : round - 1).
+            const int u = s < slot ? round : round - 1;
+            if (u < 0) continue;
+            while (!mbar_try_wait(rg.full + s, (uint32_t)(u & 1)))
+                if (globaltimer_ns() - t0 > p.timeout_ns) return;
+        }
+    }
+};
+
+// L2 prefetch of `bytes` at `base` by the producer warp's lanes.
+__device__ __forceinline__ void prefetch_rows(const uint8_t *base, size_t bytes) {
     const int lane = threadIdx.x & 31;
     const size_t piece = 16384;
-    for (size_t off = lo + (size_t)lane * piece; off < hi; off += 32 * piece) {
-        size_t n = hi - off < piece ? hi - off : piece;
-        prefetch_l2_bulk((const char *)base + off, (uint32_t)n);
+#pragma unroll 1
+    for (size_t off = (size_t)lane * piece; off < bytes; off += 32 * piece) {
+        const size_t n = bytes - off < piece ? bytes - off : piece;
+        if (n >= 16) prefetch_l2_bulk(base + off, (uint32_t)(n & ~(size_t)15));
     }
 }
 
-// Phase k in the step's sequence: 4 per layer (QKV, ATTN, GATE/UP, DOWN),
-// then the LM head.  Prefetch the weights phase k will stream.
-__device__ void prefetch_phase(const DecodeParams &p, int k, int pos, int b, int G) {
-    if (!p.prefetch || threadIdx.x >= 32) return;
-    if (k >= 4 * p.L) {
-        // LM head: the first rows of this CTA's own range (later rounds
-        // prefetch further ahead inside the phase).
-        int v0 = (int)((long long)p.V * b / G), v1 = (int)((long long)p.V * (b + 1) / G);
-        int n = min(v1 - v0, 64);
-        if (n > 0 && threadIdx.x == 0)
-            prefetch_l2_bulk(p.head + (size_t)v0 * p.semb, (uint32_t)((size_t)n * p.semb));
+// Prefetches into L2 everything phase k of this CTA will stream: its weight
+// rows and, for attention, the cached K/V rows of its heads.
+__device__ void prefetch_phase(const DecodeParams &p, const DecodeLayer *lay, const CtaGeom &cg, int k,
+                               int pos) {
+    if (!p.prefetch || k > 4 * p.L) return;
+    if (k == 4 * p.L) {
+        prefetch_rows(p.head + (size_t)cg.lm_v0 * p.semb, (size_t)min(cg.lm_n, 64) * p.semb);
         return;
     }
-    const DecodeLayer &Ly = p.layers[k >> 2];
-    const size_t kv = (size_t)p.kvh * p.hd;
+    const DecodeLayer &Ly = lay[k >> 2];
     switch (k & 3) {
-    case 0: prefetch_slice(Ly.wqkv, (size_t)p.rqkv * p.sh, b, G); break;
+    case 0: prefetch_rows(Ly.wqkv + (size_t)cg.qkv_r0 * p.sh, (size_t)cg.qkv_n * p.sh); break;
     case 1: {
-        prefetch_slice(Ly.wo, (size_t)p.qh * p.h * p.shd, b, G);
-        // Cached keys/values of earlier positions do not depend on this step.
         const size_t esz = p.kv_bf16 ? 2 : 4;
-        for (int g = 0; g < p.kvh; ++g) {
-            prefetch_slice(Ly.kc + (size_t)g * p.cap * p.hd * esz, (size_t)pos * p.hd * esz, b, G);
-            prefetch_slice(Ly.vc + (size_t)g * p.cap * p.hd * esz, (size_t)pos * p.hd * esz, b, G);
+        for (int a = 0; a < cg.natt; ++a) {
+            prefetch_rows(Ly.wo + ((size_t)cg.att_hh[a] * p.h + cg.att_r0[a]) * p.shd, (size_t)cg.att_n[a] * p.shd);
+            const int g = cg.att_hh[a] / p.group;
+            prefetch_rows(Ly.kc + (size_t)g * p.cap * p.hd * esz, (size_t)pos * p.hd * esz);
+            prefetch_rows(Ly.vc + (size_t)g * p.cap * p.hd * esz, (size_t)pos * p.hd * esz);
         }
-        (void)kv;
         break;
     }
     case 2:
-        prefetch_slice(Ly.wg, (size_t)p.ff * p.sh, b, G);
-        prefetch_slice(Ly.wu, (size_t)p.ff * p.sh, b, G);
+        prefetch_rows(Ly.wg + (size_t)cg.gu_f0 * p.sh, (size_t)cg.gu_n * p.sh);
+        prefetch_rows(Ly.wu + (size_t)cg.gu_f0 * p.sh, (size_t)cg.gu_n * p.sh);
         break;
-    case 3: prefetch_slice(Ly.wd, (size_t)p.h * p.sff, b, G); break;
+    default: prefetch_rows(Ly.wd + (size_t)cg.dn_r0 * p.sff, (size_t)cg.dn_n * p.sff); break;
     }
 }
+
+// The producer warp: the step's blocks in consumption order.
+__device__ void produce(const DecodeParams &p, const DecodeLayer *lay, const CtaGeom &cg, float *sm, int pos,
+                        volatile int *s_abort) {
+    Producer pr(p, ring_of(p, sm), s_abort);
+    const bool leader = (threadIdx.x & 31) == 0;
+    for (int k = 0; k < LOOKAHEAD; ++k) prefetch_phase(p, lay, cg, k, pos);
+#pragma unroll 1
+    for (int l = 0; l < p.L && pr.alive; ++l) {
+        const DecodeLayer &Ly = lay[l];
+        const int ph = 4 * l;
+        prefetch_phase(p, lay, cg, ph + LOOKAHEAD, pos);
+        if (leader) pr.block(Ly.wqkv + (size_t)cg.qkv_r0 * p.sh, cg.qkv_n, p.kind[K_QKV]);
+        prefetch_phase(p, lay, cg, ph + 1 + LOOKAHEAD, pos);
+        if (leader)
+            for (int a = 0; a < cg.natt; ++a)
+                pr.block(Ly.wo + ((size_t)cg.att_hh[a] * p.h + cg.att_r0[a]) * p.shd, cg.att_n[a], p.kind[K_O]);
+        prefetch_phase(p, lay, cg, ph + 2 + LOOKAHEAD, pos);
+        if (leader) {
+            pr.block(Ly.wg + (size_t)cg.gu_f0 * p.sh, cg.gu_n, p.kind[K_GU]);
+            pr.block(Ly.wu + (size_t)cg.gu_f0 * p.sh, cg.gu_n, p.kind[K_GU]);
+        }
+        prefetch_phase(p, lay, cg, ph + 3 + LOOKAHEAD, pos);
+        if (leader) pr.block(Ly.wd + (size_t)cg.dn_r0 * p.sff, cg.dn_n, p.kind[K_DN]);
+        pr.alive = __shfl_sync(0xffffffffu, (int)pr.alive, 0) != 0;
+    }
+    if (leader && pr.alive) pr.block(p.head + (size_t)cg.lm_v0 * p.semb, cg.lm_n, p.kind[K_LM]);
+    if (leader && !pr.alive) pr.drain();
+}
+
+// ------------------------------------------------------------ gemv ----
+//
+// y_r = dot(W_r, x) for the n rows of one block, weights from the ring.
+// When C <= NT thread t owns chunk column c = t % C (its activations stay in
+// registers) and walks rows rs, rs + RS, ... of each chunk; otherwise threads
+// stride the columns of each row.  Partials meet in shared memory and are
+// reduced per row in a fixed order into rowout[r].
+
+template <int WF>
+__device__ __noinline__ bool ring_gemv(const DecodeParams &p, const Ring &rg, Cursor &cur, const KindGeom &g, int n,
+                          const float *xs, float *part, volatile int *s_abort, float *rowout) {
+    constexpr int EPC = Fmt<WF>::EPC;
+    if (n <= 0) return true;
+    const int t = threadIdx.x, lane = t & 31;
+    const bool cols = g.RS > 0;
+    const int pcols = cols ? g.C : NT;
+    const int rs = cols ? (int)__umulhi((unsigned)t, g.magic) : 0;
+    const int c = cols ? t - rs * g.C : t;
+    const bool active = !cols || rs < g.RS;
+    float xr[EPC];
+    if (cols) {
+#pragma unroll
+        for (int k = 0; k < EPC; ++k) xr[k] = active ? xs[c * EPC + k] : 0.0f;
+    }
+    const int grows = g.rpc * g.group;  // rows per reduction group
+#pragma unroll 1
+    for (int r0 = 0; r0 < n; r0 += grows) {
+        const int rows_g = min(grows, n - r0);
+        const Cursor c0 = cur;
+#pragma unroll 1
+        for (int j = 0; j * g.rpc < rows_g; ++j) {
+            if (!mbar_wait(p, rg.full + cur.slot, (uint32_t)(cur.round & 1), s_abort)) break;
+            const uint8_t *slot = rg.slots + (size_t)cur.slot * rg.slot_bytes;
+            const int nr = min(g.rpc, rows_g - j * g.rpc);
+            const int pr0 = j * g.rpc;
+            if (cols) {
+                if (active)
+#pragma unroll 1
+                    for (int r = rs; r < nr; r += g.RS) {
+                        const uint4 w = *(const uint4 *)(slot + (size_t)r * g.stride + (size_t)c * 16);
+                        part[(pr0 + r) * g.C + c] = chunk_dot<WF>(w, xr);
+                    }
+            } else {
+#pragma unroll 1
+                for (int r = 0; r < nr; ++r) {
+                    float acc = 0.0f;
+#pragma unroll 1
+                    for (int cc = t; cc < g.C; cc += NT) {
+                        const uint4 w = *(const uint4 *)(slot + (size_t)r * g.stride + (size_t)cc * 16);
+                        acc += chunk_dot<WF>(w, xs + cc * EPC);
+                    }
+                    part[(pr0 + r) * NT + t] = acc;
+                }
+            }
+            cur.advance(rg.nslot);
+        }
+        csync();
+        if (*s_abort) return false;
+        // Every compute thread has read the group's slots: hand them back.
+        if (t == 0) {
+            fence_proxy_async_smem();
+            Cursor e = c0;
+            for (int j = 0; j * g.rpc < rows_g; ++j) {
+                mbar_arrive(rg.empty + e.slot);
+                e.advance(rg.nslot);
+            }
+        }
+#pragma unroll 1
+        for (int r = t >> 5; r < rows_g; r += NW) {
+            float s = 0.0f;
+#pragma unroll 1
+            for (int cc = lane; cc < pcols; cc += 32) s += part[r * pcols + cc];
+            s = warp_sum(s);
+            if (lane == 0) rowout[r0 + r] = s;
+        }
+        csync();
+    }
+    return true;
+}
+
+// ------------------------------------------------------------ barrier ----
+
+// Grid barrier in two halves (compute warps only).  barrier_arrive makes
+// the CTA's writes visible (csync, then thread 0's release reduction);
+// independent work can run before barrier_wait, which polls with relaxed
+// loads (bounded by the timeout) and ends with an acquire fence and csync.
+// barrier_wait returns false (after recording ERR_TIMEOUT and raising the
+// abort flag) when the arrivals do not complete in time or another CTA has
+// timed out.
+__device__ __forceinline__ void barrier_arrive(const DecodeParams &p, unsigned target) {
+    csync();
+    if (threadIdx.x == 0) {
+        if (p.trace) {
+            const int G = gridDim.x, idx = (int)(target / (unsigned)G) - 1;
+            p.trace[(size_t)idx * G + blockIdx.x] = globaltimer_ns();
+        }
+        red_release_add_u32(&p.ctrl->bar, 1u);
+    }
+}
+
+__device__ __noinline__ bool barrier_wait(const DecodeParams &p, unsigned target, volatile int *s_abort) {
+    DecodeCtrl *ctrl = p.ctrl;
+    if (threadIdx.x == 0) {
+        volatile unsigned *bar = &ctrl->bar;
+        if (*bar < target) {
+            const uint64_t t0 = globaltimer_ns();
+            unsigned spins = 0;
+            while (*bar < target) {
+                if ((++spins & 63u) == 0) {
+                    if ((*(volatile unsigned *)&ctrl->error & ERR_TIMEOUT) || globaltimer_ns() - t0 > p.timeout_ns) {
+                        atomicOr(&ctrl->error, ERR_TIMEOUT);
+                        *s_abort = 1;
+                        break;
+                    }
+                }
+            }
+        }
+        asm volatile("fence.acq_rel.gpu;" ::: "memory");
+        if (p.trace && blockIdx.x == 0) {
+            const int G = gridDim.x, idx = (int)(target / (unsigned)G) - 1;
+            p.trace[(size_t)4 * p.L * G + idx] = globaltimer_ns();
+        }
+    }
+    csync();
+    return *s_abort == 0;
+}
+
+// --------------------------------------------------------- elementwise ----
 
 __device__ __forceinline__ float round_bf16(float x) {
     return __uint_as_float((uint32_t)f32_to_bf16_rne(x) << 16);
@@ -302,17 +445,27 @@ __device__ __forceinline__ float resid_in(const DecodeParams &p, int l, int toke
 }
 
 // h' = x + o_proj(ctx): the head partials summed in head order, then the
-// residual added (src/kv_cache.rs:405-406).  Identical in every phase that
-// needs it.
+// residual added (src/kv_cache.rs:405-406).
 __device__ __forceinline__ float after_attention(const DecodeParams &p, int l, int token, int i) {
-    float o = ldcg(p.part + i);
-    for (int hh = 1; hh < p.qh; ++hh) o += ldcg(p.part + (size_t)hh * p.h + i);
+    // Eight heads' loads are in flight at a time; the sum runs in head order.
+    const float *base = p.part + i;
+    const size_t stride = (size_t)p.h;
+    float o = 0.0f;
+#pragma unroll 1
+    for (int h0 = 0; h0 < p.qh; h0 += 8) {
+        float v[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[k] = h0 + k < p.qh ? ldcg(base + (size_t)(h0 + k) * stride) : 0.0f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+            if (h0 + k < p.qh) o = (h0 + k == 0) ? v[k] : o + v[k];
+    }
     return resid_in(p, l, token, i) + o;
 }
 
 __device__ __forceinline__ float silu1(float v) {
     if (v >= 0.0f) return v / (1.0f + expf(-v));
-    float e = expf(v);
+    const float e = expf(v);
     return v * e / (1.0f + e);
 }
 
@@ -322,277 +475,381 @@ __device__ __forceinline__ float kv_load(const uint8_t *base, size_t idx) {
     return __ldcg((const float *)base + idx);
 }
 
-// Attention for query head hh at position pos, then its o_proj partial over
-// rows [r0, r1) (src/kv_cache.rs:550-585).
+// Attention for query head hh at position pos (src/kv_cache.rs:550-576),
+// leaving the context vector in shared memory (ctx, zero-padded).  The
+// first CTA of a KV group writes the new K (rotated) and V at `pos`.
 template <int WF, int KVBF16>
-__device__ void attention_head(const DecodeParams &p, const DecodeLayer &Ly, int hh, int sp,
-                               int pos, float *sm) {
+__device__ __noinline__ void attention_context(const DecodeParams &p, const DecodeLayer &Ly, int hh, bool writer, int pos,
+                                  float *sm) {
     const int hd = p.hd, half = hd / 2, g = hh / p.group;
     const size_t kvw = (size_t)p.kvh * hd;
     float *qs = sm + p.sm_q, *ks = qs + hd, *vs = ks + hd, *ctx = vs + hd;
     float *sc = sm + p.sm_sc, *red = sm + p.sm_red, *part = sm + p.sm_part;
     const float2 *rp = p.rope + (size_t)pos * half;
+#pragma unroll 1
     for (int j = threadIdx.x; j < half; j += NT) {
-        float2 cs = rp[j];
-        float a = ldcg(p.qkv + (size_t)hh * hd + j), b = ldcg(p.qkv + (size_t)hh * hd + j + half);
+        const float2 cs = rp[j];
+        const float a = ldcg(p.qkv + (size_t)hh * hd + j), b = ldcg(p.qkv + (size_t)hh * hd + j + half);
         qs[j] = a * cs.x - b * cs.y;
         qs[j + half] = b * cs.x + a * cs.y;
-        float ka = ldcg(p.qkv + p.h + (size_t)g * hd + j), kb = ldcg(p.qkv + p.h + (size_t)g * hd + j + half);
+        const float ka = ldcg(p.qkv + p.h + (size_t)g * hd + j), kb = ldcg(p.qkv + p.h + (size_t)g * hd + j + half);
         float k0 = ka * cs.x - kb * cs.y, k1 = kb * cs.x + ka * cs.y;
         if (KVBF16) { k0 = round_bf16(k0); k1 = round_bf16(k1); }
         ks[j] = k0;
         ks[j + half] = k1;
     }
+#pragma unroll 1
     for (int i = threadIdx.x; i < hd; i += NT) {
-        float v = ldcg(p.qkv + p.h + kvw + (size_t)g * hd + i);
+        const float v = ldcg(p.qkv + p.h + kvw + (size_t)g * hd + i);
         vs[i] = KVBF16 ? round_bf16(v) : v;
     }
     const int ctx_pad = p.chd * Fmt<WF>::EPC;
+#pragma unroll 1
     for (int i = hd + threadIdx.x; i < ctx_pad; i += NT) ctx[i] = 0.0f;
-    __syncthreads();
-    if (!isfinite(qs[threadIdx.x % hd]) || !isfinite(ks[threadIdx.x % hd])) atomicOr(&p.ctrl->error, ERR_NONFINITE);
+    csync();
+    if (threadIdx.x < hd && (!isfinite(qs[threadIdx.x]) || !isfinite(ks[threadIdx.x])))
+        atomicOr(&p.ctrl->error, ERR_NONFINITE);
     const size_t esz = KVBF16 ? 2 : 4;
     const uint8_t *K = Ly.kc + (size_t)g * p.cap * hd * esz;
     const uint8_t *Vc = Ly.vc + (size_t)g * p.cap * hd * esz;
-    if (sp == 0 && hh % p.group == 0) {
+    if (writer) {
+#pragma unroll 1
         for (int i = threadIdx.x; i < hd; i += NT) {
-            size_t idx = (size_t)pos * hd + i;
+            const size_t idx = (size_t)g * p.cap * hd + (size_t)pos * hd + i;
             if (KVBF16) {
-                ((uint16_t *)Ly.kc)[(size_t)g * p.cap * hd + idx] = f32_to_bf16_rne(ks[i]);
-                ((uint16_t *)Ly.vc)[(size_t)g * p.cap * hd + idx] = f32_to_bf16_rne(vs[i]);
+                ((uint16_t *)Ly.kc)[idx] = f32_to_bf16_rne(ks[i]);
+                ((uint16_t *)Ly.vc)[idx] = f32_to_bf16_rne(vs[i]);
             } else {
-                ((float *)Ly.kc)[(size_t)g * p.cap * hd + idx] = ks[i];
-                ((float *)Ly.vc)[(size_t)g * p.cap * hd + idx] = vs[i];
+                ((float *)Ly.kc)[idx] = ks[i];
+                ((float *)Ly.vc)[idx] = vs[i];
             }
         }
     }
     // scores: q.k / sqrt(d), one position per thread, increasing i.
+    const int row_bytes = hd * (int)esz;
+    const bool vec = (row_bytes & 15) == 0;
+    constexpr int KEPC = KVBF16 ? 8 : 4;  // cache elements per 16-byte chunk
+#pragma unroll 1
     for (int q = threadIdx.x; q <= pos; q += NT) {
         float s = 0.0f;
         if (q == pos) {
+#pragma unroll 1
             for (int i = 0; i < hd; ++i) s = s + qs[i] * ks[i];
+        } else if (vec) {
+            const uint8_t *row = K + (size_t)q * row_bytes;
+            const int nc = row_bytes >> 4;
+#pragma unroll 1
+            for (int c0 = 0; c0 < nc; c0 += 8) {
+                uint4 kc[8];
+#pragma unroll
+                for (int c = 0; c < 8; ++c)
+                    if (c0 + c < nc) kc[c] = __ldcg((const uint4 *)(row + (size_t)(c0 + c) * 16));
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    if (c0 + c < nc) {
+                        const uint32_t w4[4] = {kc[c].x, kc[c].y, kc[c].z, kc[c].w};
+                        const float *qq = qs + (c0 + c) * KEPC;
+#pragma unroll
+                        for (int e = 0; e < KEPC; ++e) {
+                            const float kv = KVBF16 ? ((e & 1) ? bf16_hi(w4[e >> 1]) : bf16_lo(w4[e >> 1]))
+                                                    : __uint_as_float(w4[e]);
+                            s = s + qq[e] * kv;
+                        }
+                    }
+                }
+            }
         } else {
+#pragma unroll 1
             for (int i = 0; i < hd; ++i) s = s + qs[i] * kv_load<KVBF16>(K, (size_t)q * hd + i);
         }
         sc[q] = s / p.sqrt_hd;
     }
-    __syncthreads();
+    csync();
     float m = -INFINITY;
+#pragma unroll 1
     for (int q = threadIdx.x; q <= pos; q += NT) m = rust_max(m, sc[q]);
     m = block_max(m, red);
     float se = 0.0f;
+#pragma unroll 1
     for (int q = threadIdx.x; q <= pos; q += NT) {
-        float e = expf(sc[q] - m);
+        const float e = expf(sc[q] - m);
         sc[q] = e;
         se += e;
     }
     se = block_sum(se, red);
+#pragma unroll 1
     for (int q = threadIdx.x; q <= pos; q += NT) sc[q] = sc[q] / se;
-    __syncthreads();
-    // context: thread (i, pg) sums positions pg, pg+PG, ... in order.
-    const int PG = NT / hd > 0 ? NT / hd : 1;
-    {
+    csync();
+    // context: position groups pg sum positions pg, pg+PG, ... in order;
+    // the groups then meet in group order.
+    int PG;
+    if (vec) {
+        const int nc = row_bytes >> 4;
+        PG = NT / nc;
+        const int c = threadIdx.x % nc, pg = threadIdx.x / nc;
+        if (pg < PG) {
+            float acc[KEPC];
+#pragma unroll
+            for (int e = 0; e < KEPC; ++e) acc[e] = 0.0f;
+#pragma unroll 1
+            for (int q0 = pg; q0 <= pos; q0 += 4 * PG) {
+                uint4 vc[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int q = q0 + u * PG;
+                    if (q < pos) vc[u] = __ldcg((const uint4 *)(Vc + (size_t)q * row_bytes + (size_t)c * 16));
+                }
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int q = q0 + u * PG;
+                    if (q <= pos) {
+                        const float pr = sc[q];
+                        const uint32_t w4[4] = {vc[u].x, vc[u].y, vc[u].z, vc[u].w};
+#pragma unroll
+                        for (int e = 0; e < KEPC; ++e) {
+                            const float v = q == pos ? vs[c * KEPC + e]
+                                                     : (KVBF16 ? ((e & 1) ? bf16_hi(w4[e >> 1]) : bf16_lo(w4[e >> 1]))
+                                                               : __uint_as_float(w4[e]));
+                            acc[e] = acc[e] + pr * v;
+                        }
+                    }
+                }
+            }
+#pragma unroll
+            for (int e = 0; e < KEPC; ++e) part[pg * hd + c * KEPC + e] = acc[e];
+        }
+    } else {
+        PG = NT / hd > 0 ? NT / hd : 1;
         const int i = threadIdx.x % hd, pg = threadIdx.x / hd;
         float acc = 0.0f;
         if (pg < PG && threadIdx.x < PG * hd) {
+#pragma unroll 1
             for (int q = pg; q <= pos; q += PG) {
-                float v = q == pos ? vs[i] : kv_load<KVBF16>(Vc, (size_t)q * hd + i);
+                const float v = q == pos ? vs[i] : kv_load<KVBF16>(Vc, (size_t)q * hd + i);
                 acc = acc + sc[q] * v;
             }
             part[pg * hd + i] = acc;
         }
     }
-    __syncthreads();
+    csync();
+#pragma unroll 1
     for (int i = threadIdx.x; i < hd; i += NT) {
         float s = part[i];
+#pragma unroll 1
         for (int k = 1; k < PG; ++k) s += part[k * hd + i];
         ctx[i] = s;
         flag_nonfinite(p.ctrl, s);
     }
-    __syncthreads();
-    // o_proj partial of this head for rows [r0, r1).
-    const int r0 = (int)((long long)p.h * sp / p.s_o), r1 = (int)((long long)p.h * (sp + 1) / p.s_o);
-    const uint8_t *wo = Ly.wo + (size_t)hh * p.h * p.shd;
-    const float *so = Ly.so;
-    float *outp = p.part + (size_t)hh * p.h;
-    DecodeCtrl *ctrl = p.ctrl;
-    const size_t shd = p.shd;
-    cta_gemv<WF>([=](int r) { return wo + (size_t)(r0 + r) * shd; }, r1 - r0, p.chd, ctx, part,
-                 p.part_cap, [=](int r, float v) {
-                     if (WF == WF_I8) v = v * so[r0 + r];
-                     outp[r0 + r] = v;
-                     flag_nonfinite(ctrl, v);
-                 });
+    csync();
+}
+
+// ------------------------------------------------------------ phases ----
+//
+// Each phase has a `prep` that stages its small vectors -- `gain` (norm
+// gains) and `rv` (row scales rv[0..R), biases or second scales rv[R..2R))
+// -- into shared memory before the grid barrier that precedes it, and a
+// `run` after the barrier.  The weights arrive through the ring.
+
+// Stages n floats of global memory into shared memory.
+__device__ __forceinline__ void stage(float *dst, const float *src, int n) {
+#pragma unroll 1
+    for (int i = threadIdx.x; i < n; i += NT) dst[i] = src[i];
+}
+
+template <int WF>
+__device__ __forceinline__ void prep_qkv(const DecodeParams &p, const DecodeLayer &Ly, const CtaGeom &cg,
+                                         float *sm) {
+    float *gain = sm + p.sm_gain, *rv = sm + p.sm_rv;
+    stage(gain, Ly.attn_norm, p.h);
+    if (WF == WF_I8) stage(rv, Ly.sqkv + cg.qkv_r0, cg.qkv_n);
+    stage(rv + cg.qkv_n, Ly.bqkv + cg.qkv_r0, cg.qkv_n);
+}
+
+template <int WF>
+__device__ __forceinline__ bool run_qkv(const DecodeParams &p, const CtaGeom &cg, int l, int token, float *sm,
+                                        const Ring &rg, Cursor &cur, volatile int *s_abort) {
+    constexpr int EPC = Fmt<WF>::EPC;
+    float *xs = sm + p.sm_xs, *part = sm + p.sm_part, *h2 = sm + p.sm_h2, *red = sm + p.sm_red;
+    const float *gain = sm + p.sm_gain, *rv = sm + p.sm_rv;
+#pragma unroll 1
+    for (int i = threadIdx.x; i < p.h; i += NT) h2[i] = resid_in(p, l, token, i);
+    csync();
+    block_rmsnorm(h2, gain, xs, p.h, p.ch * EPC, p.eps, red);
+    float *rows = sm + p.sm_gu;
+    if (!ring_gemv<WF>(p, rg, cur, p.kind[K_QKV], cg.qkv_n, xs, part, s_abort, rows)) return false;
+    const int R = cg.qkv_n;
+    float *out = p.qkv + cg.qkv_r0;
+#pragma unroll 1
+    for (int r = threadIdx.x; r < R; r += NT) {
+        float v = rows[r];
+        if (WF == WF_I8) v = v * rv[r];
+        v = v + rv[R + r];
+        out[r] = v;
+        flag_nonfinite(p.ctrl, v);
+    }
+    return true;
+}
+
+template <int WF>
+__device__ __forceinline__ void prep_attention(const DecodeParams &p, const DecodeLayer &Ly, const CtaGeom &cg,
+                                               float *sm) {
+    if (WF == WF_I8 && cg.natt > 0) stage(sm + p.sm_rv, Ly.so + cg.att_r0[0], cg.att_n[0]);
 }
 
 template <int WF, int KVBF16>
-__global__ void __launch_bounds__(NT, 1) decode_kernel(const __grid_constant__ DecodeParams p) {
-    extern __shared__ __align__(16) float sm[];
-    __shared__ int s_flag;
-    float *xs = sm + p.sm_xs, *part = sm + p.sm_part, *h2 = sm + p.sm_h2, *gu = sm + p.sm_gu;
-    float *red = sm + p.sm_red;
-    const int G = gridDim.x, b = blockIdx.x;
-    DecodeCtrl *ctrl = p.ctrl;
-    const int token = *(volatile int *)&ctrl->token;
-    const int pos = *(volatile int *)&ctrl->pos;
+__device__ __forceinline__ bool run_attention(const DecodeParams &p, const DecodeLayer &Ly, const CtaGeom &cg,
+                                              int pos, float *sm, const Ring &rg, Cursor &cur,
+                                              volatile int *s_abort) {
+    float *part = sm + p.sm_part, *ctx = sm + p.sm_q + 3 * p.hd;
+    const float *rv = sm + p.sm_rv;
+#pragma unroll 1
+    for (int a = 0; a < cg.natt; ++a) {
+        const int hh = cg.att_hh[a], r0 = cg.att_r0[a], n = cg.att_n[a];
+        attention_context<WF, KVBF16>(p, Ly, hh, r0 == 0 && hh % p.group == 0, pos, sm);
+        float *rows = sm + p.sm_gu;
+        if (!ring_gemv<WF>(p, rg, cur, p.kind[K_O], n, ctx, part, s_abort, rows)) return false;
+        float *outp = p.part + (size_t)hh * p.h + r0;
+#pragma unroll 1
+        for (int r = threadIdx.x; r < n; r += NT) {
+            float v = rows[r];
+            if (WF == WF_I8) v = v * (a == 0 ? rv[r] : Ly.so[r0 + r]);
+            outp[r] = v;
+            flag_nonfinite(p.ctrl, v);
+        }
+        csync();
+    }
+    return true;
+}
+
+template <int WF>
+__device__ __forceinline__ void prep_gate_up(const DecodeParams &p, const DecodeLayer &Ly, const CtaGeom &cg,
+                                             float *sm) {
+    float *gain = sm + p.sm_gain, *rv = sm + p.sm_rv;
+    stage(gain, Ly.ffn_norm, p.h);
+    if (WF == WF_I8) {
+        stage(rv, Ly.sg + cg.gu_f0, cg.gu_n);
+        stage(rv + cg.gu_n, Ly.su + cg.gu_f0, cg.gu_n);
+    }
+}
+
+template <int WF>
+__device__ __forceinline__ bool run_gate_up(const DecodeParams &p, const CtaGeom &cg, int l, int token, float *sm,
+                                            const Ring &rg, Cursor &cur, volatile int *s_abort) {
     constexpr int EPC = Fmt<WF>::EPC;
-    unsigned target = 0;
-    int phase = 0;
-    prefetch_phase(p, 0, pos, b, G);
-    prefetch_phase(p, 1, pos, b, G);
-
-    for (int l = 0; l < p.L; ++l) {
-        const DecodeLayer &Ly = p.layers[l];
-        // ---------------- QKV ----------------
-        prefetch_phase(p, phase + 2, pos, b, G);
-        for (int i = threadIdx.x; i < p.h; i += NT) h2[i] = resid_in(p, l, token, i);
-        __syncthreads();
-        block_rmsnorm(h2, Ly.attn_norm, xs, p.h, p.ch * EPC, p.eps, red);
-        {
-            const int r0 = (int)((long long)p.rqkv * b / G), r1 = (int)((long long)p.rqkv * (b + 1) / G);
-            const uint8_t *w = Ly.wqkv;
-            const float *s = Ly.sqkv, *bias = Ly.bqkv;
-            float *out = p.qkv;
-            const size_t sh = p.sh;
-            cta_gemv<WF>([=](int r) { return w + (size_t)(r0 + r) * sh; }, r1 - r0, p.ch, xs, part,
-                         p.part_cap, [=](int r, float v) {
-                             if (WF == WF_I8) v = v * s[r0 + r];
-                             v = v + bias[r0 + r];
-                             out[r0 + r] = v;
-                             flag_nonfinite(ctrl, v);
-                         });
-        }
-        target += G;
-        ++phase;
-        if (!grid_barrier(ctrl, target, p.timeout_ns, &s_flag)) return;
-        // ---------------- ATTENTION + o_proj partials ----------------
-        prefetch_phase(p, phase + 2, pos, b, G);
-        for (int wi = b; wi < p.qh * p.s_o; wi += G) {
-            attention_head<WF, KVBF16>(p, Ly, wi / p.s_o, wi % p.s_o, pos, sm);
-            __syncthreads();
-        }
-        target += G;
-        ++phase;
-        if (!grid_barrier(ctrl, target, p.timeout_ns, &s_flag)) return;
-        // ---------------- GATE / UP ----------------
-        prefetch_phase(p, phase + 2, pos, b, G);
-        for (int i = threadIdx.x; i < p.h; i += NT) {
-            float v = after_attention(p, l, token, i);
-            h2[i] = v;
-            if (b == 0) flag_nonfinite(ctrl, v);
-        }
-        __syncthreads();
-        block_rmsnorm(h2, Ly.ffn_norm, xs, p.h, p.ch * EPC, p.eps, red);
-        {
-            const int f0 = (int)((long long)p.ff * b / G), f1 = (int)((long long)p.ff * (b + 1) / G);
-            const int R = f1 - f0;
-            const uint8_t *wg = Ly.wg, *wu = Ly.wu;
-            const size_t sh = p.sh;
-            float *g = gu;
-            cta_gemv<WF>(
-                [=](int r) { return r < R ? wg + (size_t)(f0 + r) * sh : wu + (size_t)(f0 + r - R) * sh; },
-                2 * R, p.ch, xs, part, p.part_cap, [=](int r, float v) { g[r] = v; });
-            __syncthreads();
-            for (int r = threadIdx.x; r < R; r += NT) {
-                float gv = gu[r], uv = gu[R + r];
-                if (WF == WF_I8) {
-                    gv = gv * Ly.sg[f0 + r];
-                    uv = uv * Ly.su[f0 + r];
-                }
-                float a = silu1(gv) * uv;
-                p.act[f0 + r] = a;
-                flag_nonfinite(ctrl, gv);
-                flag_nonfinite(ctrl, a);
-            }
-        }
-        target += G;
-        ++phase;
-        if (!grid_barrier(ctrl, target, p.timeout_ns, &s_flag)) return;
-        // ---------------- DOWN ----------------
-        prefetch_phase(p, phase + 2, pos, b, G);
-        for (int i = threadIdx.x; i < p.cff * EPC; i += NT) xs[i] = i < p.ff ? ldcg(p.act + i) : 0.0f;
-        __syncthreads();
-        {
-            const int r0 = (int)((long long)p.h * b / G), r1 = (int)((long long)p.h * (b + 1) / G);
-            const uint8_t *w = Ly.wd;
-            const float *s = Ly.sd;
-            const size_t sff = p.sff;
-            const int lay = l, tok = token;
-            const DecodeParams *pp = &p;
-            cta_gemv<WF>([=](int r) { return w + (size_t)(r0 + r) * sff; }, r1 - r0, p.cff, xs, part,
-                         p.part_cap, [=](int r, float v) {
-                             if (WF == WF_I8) v = v * s[r0 + r];
-                             float o = after_attention(*pp, lay, tok, r0 + r) + v;
-                             pp->hidden[r0 + r] = o;
-                             flag_nonfinite(ctrl, o);
-                         });
-        }
-        target += G;
-        ++phase;
-        if (!grid_barrier(ctrl, target, p.timeout_ns, &s_flag)) return;
+    float *xs = sm + p.sm_xs, *part = sm + p.sm_part, *h2 = sm + p.sm_h2, *red = sm + p.sm_red;
+    float *gu = sm + p.sm_gu;
+    const float *gain = sm + p.sm_gain, *rv = sm + p.sm_rv;
+#pragma unroll 1
+    for (int i = threadIdx.x; i < p.h; i += NT) {
+        const float v = after_attention(p, l, token, i);
+        h2[i] = v;
+        if (blockIdx.x == 0) flag_nonfinite(p.ctrl, v);
     }
+    csync();
+    block_rmsnorm(h2, gain, xs, p.h, p.ch * EPC, p.eps, red);
+    const int R = cg.gu_n;
+    if (!ring_gemv<WF>(p, rg, cur, p.kind[K_GU], R, xs, part, s_abort, gu)) return false;
+    if (!ring_gemv<WF>(p, rg, cur, p.kind[K_GU], R, xs, part, s_abort, gu + R)) return false;
+#pragma unroll 1
+    for (int r = threadIdx.x; r < R; r += NT) {
+        float gv = gu[r], uv = gu[R + r];
+        if (WF == WF_I8) {
+            gv = gv * rv[r];
+            uv = uv * rv[R + r];
+        }
+        const float a = silu1(gv) * uv;
+        p.act[cg.gu_f0 + r] = a;
+        flag_nonfinite(p.ctrl, gv);
+        flag_nonfinite(p.ctrl, a);
+    }
+    csync();  // rv is restaged by the next prep
+    return true;
+}
 
-    // ---------------- LM HEAD + argmax ----------------
+template <int WF>
+__device__ __forceinline__ void prep_down(const DecodeParams &p, const DecodeLayer &Ly, const CtaGeom &cg,
+                                          float *sm) {
+    if (WF == WF_I8) stage(sm + p.sm_rv, Ly.sd + cg.dn_r0, cg.dn_n);
+}
+
+template <int WF>
+__device__ __forceinline__ bool run_down(const DecodeParams &p, const CtaGeom &cg, float *sm, const Ring &rg,
+                                         Cursor &cur, volatile int *s_abort) {
+    constexpr int EPC = Fmt<WF>::EPC;
+    float *xs = sm + p.sm_xs, *part = sm + p.sm_part;
+#pragma unroll 1
+    for (int i = threadIdx.x; i < p.cff * EPC; i += NT) xs[i] = i < p.ff ? ldcg(p.act + i) : 0.0f;
+    csync();
+    float *rows = sm + p.sm_gu;
+    if (!ring_gemv<WF>(p, rg, cur, p.kind[K_DN], cg.dn_n, xs, part, s_abort, rows)) return false;
+    // h' of this layer is still in shared memory from the gate/up phase of
+    // this same CTA (src/kv_cache.rs:437-443: x_next = h' + down(a)).
+    const float *h2 = sm + p.sm_h2 + cg.dn_r0, *rv = sm + p.sm_rv;
+    float *hidden = p.hidden + cg.dn_r0;
+#pragma unroll 1
+    for (int r = threadIdx.x; r < cg.dn_n; r += NT) {
+        float v = rows[r];
+        if (WF == WF_I8) v = v * rv[r];
+        const float o = h2[r] + v;
+        hidden[r] = o;
+        flag_nonfinite(p.ctrl, o);
+    }
+    return true;
+}
+
+// Final RMSNorm, this CTA's rows of the (tied) table, logits and the CTA's
+// argmax (lowest id on ties); the last CTA to finish reduces the grid.  The
+// logits of all the CTA's rows land in `rowv`; warp 0 scans them in row
+// order, so ties keep the lowest id.
+template <int TF>
+__device__ __forceinline__ bool run_lm_head(const DecodeParams &p, const CtaGeom &cg, int pos, float *sm,
+                                            const Ring &rg, Cursor &cur, volatile int *s_abort) {
+    constexpr int TEPC = Fmt<TF>::EPC;
+    const int G = gridDim.x, b = blockIdx.x;
+    float *xs = sm + p.sm_xs, *part = sm + p.sm_part, *h2 = sm + p.sm_h2, *red = sm + p.sm_red;
+    const float *gain = sm + p.sm_gain;
+    float *rowv = sm + p.sm_sc;
+    DecodeCtrl *ctrl = p.ctrl;
+#pragma unroll 1
     for (int i = threadIdx.x; i < p.h; i += NT) h2[i] = ldcg(p.hidden + i);
-    __syncthreads();
-    const int tEPC = p.tfmt == WF_BF16 ? 8 : 4;
-    block_rmsnorm(h2, p.final_norm, xs, p.h, p.cemb * tEPC, p.eps, red);
-    const int v0 = (int)((long long)p.V * b / G), v1 = (int)((long long)p.V * (b + 1) / G);
-    float best_v = -INFINITY;
-    int best_i = 0x7fffffff;
-    {
-        const uint8_t *tab = p.head;
-        const size_t semb = p.semb;
-        float *logits = ctrl->write_logits ? p.logits : nullptr;
-        float *bv = &best_v;
-        int *bi = &best_i;
-        auto emit = [=](int r, float v) {
-            const int id = v0 + r;
-            if (logits) logits[id] = v;
-            flag_nonfinite(ctrl, v);
-            if (v > *bv || (v == *bv && id < *bi)) { *bv = v; *bi = id; }
-        };
-        // Rows are streamed in blocks; each block prefetches the next into L2.
-        const int R = v1 - v0, BLK = 256;
-        for (int r0 = 0; r0 < R; r0 += BLK) {
-            if (p.prefetch && threadIdx.x == 0 && r0 + BLK < R) {
-                int n = min(BLK, R - r0 - BLK);
-                prefetch_l2_bulk(tab + (size_t)(v0 + r0 + BLK) * semb, (uint32_t)((size_t)n * semb));
-            }
-            const int n = min(BLK, R - r0);
-            const int base = v0 + r0;
-            auto rowp = [=](int r) { return tab + (size_t)(base + r) * semb; };
-            auto em = [=](int r, float v) { emit(r0 + r, v); };
-            if (p.tfmt == WF_BF16) cta_gemv<WF_BF16>(rowp, n, p.cemb, xs, part, p.part_cap, em);
-            else cta_gemv<WF_F32>(rowp, n, p.cemb, xs, part, p.part_cap, em);
-        }
+    csync();
+    block_rmsnorm(h2, gain, xs, p.h, p.cemb * TEPC, p.eps, red);
+    if (!ring_gemv<TF>(p, rg, cur, p.kind[K_LM], cg.lm_n, xs, part, s_abort, rowv)) return false;
+    // ring_gemv ends with a barrier, so every row's logit is in rowv.
+    if (ctrl->write_logits) {
+        float *lg = p.logits + cg.lm_v0;
+#pragma unroll 1
+        for (int r = threadIdx.x; r < cg.lm_n; r += NT) lg[r] = rowv[r];
     }
-    // CTA argmax over the warps' lane-0 bests (lowest id on ties).
-    {
-        const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-        int *redi = (int *)(red + 2 * NW + 4);
-        __syncthreads();
-        if (lane == 0) {
-            red[warp] = best_v;
-            redi[warp] = best_i;
+    if (threadIdx.x < 32) {
+        const int lane = threadIdx.x;
+        float bv = -INFINITY;
+        int bi = 0x7fffffff;
+#pragma unroll 1
+        for (int r = lane; r < cg.lm_n; r += 32) {
+            const float v = rowv[r];
+            if (!isfinite(v)) atomicOr(&ctrl->error, ERR_NONFINITE);
+            if (v > bv) { bv = v; bi = r; }
         }
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            float bv = red[0];
-            int bi = redi[0];
-            for (int k = 1; k < NW; ++k)
-                if (red[k] > bv || (red[k] == bv && redi[k] < bi)) { bv = red[k]; bi = redi[k]; }
+#pragma unroll
+        for (int off = 16; off; off >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+            if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+        }
+        if (lane == 0) {
             p.amax_v[b] = bv;
-            p.amax_i[b] = bi;
+            p.amax_i[b] = bi == 0x7fffffff ? bi : cg.lm_v0 + bi;
             __threadfence();
-            unsigned tk = atomicAdd(&ctrl->ticket, 1u);
+            const unsigned tk = atomicAdd(&ctrl->ticket, 1u);
             if (tk == (unsigned)G - 1) {
                 __threadfence();
                 float gv = __ldcg(p.amax_v);
                 int gi = __ldcg(p.amax_i);
+#pragma unroll 1
                 for (int k = 1; k < G; ++k) {
-                    float v = __ldcg(p.amax_v + k);
-                    int i = __ldcg(p.amax_i + k);
+                    const float v = __ldcg(p.amax_v + k);
+                    const int i = __ldcg(p.amax_i + k);
                     if (v > gv || (v == gv && i < gi)) { gv = v; gi = i; }
                 }
                 if (gi < 0 || gi >= p.V) gi = 0;
@@ -602,23 +859,99 @@ __global__ void __launch_bounds__(NT, 1) decode_kernel(const __grid_constant__ D
                 ctrl->pos = pos + 1;
                 ctrl->bar = 0;
                 ctrl->ticket = 0;
+                if (p.trace) p.trace[(size_t)4 * p.L * G + 4 * p.L + 1] = globaltimer_ns();
                 __threadfence();
             }
         }
     }
+    return true;
+}
+
+// ------------------------------------------------------------ kernel ----
+
+template <int WF, int TF, int KVBF16>
+__global__ void __launch_bounds__(kDecodeBlock, 1) decode_kernel(const __grid_constant__ DecodeParams p) {
+    extern __shared__ __align__(128) float sm[];
+    __shared__ int s_abort_storage;
+    volatile int *s_abort = &s_abort_storage;
+    const int G = gridDim.x, b = blockIdx.x;
+    DecodeCtrl *ctrl = p.ctrl;
+    const int token = *(volatile int *)&ctrl->token;
+    const int pos = *(volatile int *)&ctrl->pos;
+    const int NB = 4 * p.L;
+    const CtaGeom &cg = p.geom[b];
+    if (p.trace && b == 0 && threadIdx.x == 0) p.trace[(size_t)NB * G + NB] = globaltimer_ns();
+    // The layer table lives in shared memory for the whole step.
+    DecodeLayer *lay = (DecodeLayer *)(sm + p.sm_lay);
+    {
+        const uint32_t *src = (const uint32_t *)p.layers;
+        uint32_t *dst = (uint32_t *)lay;
+        const int words = p.L * (int)(sizeof(DecodeLayer) / 4);
+#pragma unroll 1
+        for (int i = threadIdx.x; i < words; i += kDecodeBlock) dst[i] = src[i];
+    }
+    const Ring rg = ring_of(p, sm);
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < p.nslot; ++i) {
+            mbar_init(rg.full + i, 1);
+            mbar_init(rg.empty + i, 1);
+        }
+        fence_mbar_init();
+        *s_abort = 0;
+    }
+    __syncthreads();  // the only all-thread barrier: roles split here
+
+    if (threadIdx.x >= NT) {  // producer warp
+        produce(p, lay, cg, sm, pos, s_abort);
+        return;
+    }
+
+    Cursor cur{0, 0};
+    prep_qkv<WF>(p, lay[0], cg, sm);
+    csync();
+    unsigned target = 0;
+    bool ok = true;
+    // Each phase: run, arrive at the grid barrier, stage the next phase's
+    // vectors while the other CTAs arrive, then wait.
+#pragma unroll 1
+    for (int l = 0; l < p.L && ok; ++l) {
+        const DecodeLayer &Ly = lay[l];
+        if (!(ok = run_qkv<WF>(p, cg, l, token, sm, rg, cur, s_abort))) break;
+        barrier_arrive(p, target += G);
+        prep_attention<WF>(p, Ly, cg, sm);
+        if (!(ok = barrier_wait(p, target, s_abort))) break;
+
+        if (!(ok = run_attention<WF, KVBF16>(p, Ly, cg, pos, sm, rg, cur, s_abort))) break;
+        barrier_arrive(p, target += G);
+        prep_gate_up<WF>(p, Ly, cg, sm);
+        if (!(ok = barrier_wait(p, target, s_abort))) break;
+
+        if (!(ok = run_gate_up<WF>(p, cg, l, token, sm, rg, cur, s_abort))) break;
+        barrier_arrive(p, target += G);
+        prep_down<WF>(p, Ly, cg, sm);
+        if (!(ok = barrier_wait(p, target, s_abort))) break;
+
+        if (!(ok = run_down<WF>(p, cg, sm, rg, cur, s_abort))) break;
+        barrier_arrive(p, target += G);
+        if (l + 1 < p.L) prep_qkv<WF>(p, lay[l + 1], cg, sm);
+        else stage(sm + p.sm_gain, p.final_norm, p.h);
+        if (!(ok = barrier_wait(p, target, s_abort))) break;
+    }
+    if (ok) ok = run_lm_head<TF>(p, cg, pos, sm, rg, cur, s_abort);
+    if (!ok && threadIdx.x == 0) *s_abort = 1;  // releases a producer waiting for a slot
 }
 
 size_t decode_smem_bytes(const DecodeParams &p) { return (size_t)p.sm_total * sizeof(float); }
 
-template <int WF, int KV>
+template <int WF, int TF, int KV>
 static cudaError_t launch_t(const DecodeParams &p, int grid, cudaStream_t stream) {
-    auto kern = decode_kernel<WF, KV>;
+    auto kern = decode_kernel<WF, TF, KV>;
     size_t smem = decode_smem_bytes(p);
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(NT);
+    cfg.blockDim = dim3(kDecodeBlock);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
@@ -629,23 +962,45 @@ static cudaError_t launch_t(const DecodeParams &p, int grid, cudaStream_t stream
     return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
+template <int WF, int TF, int KV>
+static const void *kernel_ptr() {
+    return (const void *)decode_kernel<WF, TF, KV>;
+}
+
+// Dispatch over (linear format, table format, KV type).
+template <class F>
+static auto dispatch(int wf, int tf, int kv, F f) {
+#define QB_CASE(W, T, K) \
+    if (wf == W && tf == T && kv == K) return f.template operator()<W, T, K>();
+    QB_CASE(WF_F32, WF_F32, 0) QB_CASE(WF_F32, WF_F32, 1) QB_CASE(WF_F32, WF_BF16, 0) QB_CASE(WF_F32, WF_BF16, 1)
+    QB_CASE(WF_BF16, WF_F32, 0) QB_CASE(WF_BF16, WF_F32, 1) QB_CASE(WF_BF16, WF_BF16, 0) QB_CASE(WF_BF16, WF_BF16, 1)
+    QB_CASE(WF_I8, WF_F32, 0) QB_CASE(WF_I8, WF_F32, 1) QB_CASE(WF_I8, WF_BF16, 0)
+#undef QB_CASE
+    return f.template operator()<WF_I8, WF_BF16, 1>();
+}
+
+struct LaunchOp {
+    const DecodeParams &p;
+    int grid;
+    cudaStream_t stream;
+    template <int W, int T, int K> cudaError_t operator()() const { return launch_t<W, T, K>(p, grid, stream); }
+};
+struct PtrOp {
+    template <int W, int T, int K> const void *operator()() const { return kernel_ptr<W, T, K>(); }
+};
+
 cudaError_t decode_launch(const DecodeParams &p, int grid, cudaStream_t stream) {
-    if (p.wfmt == WF_I8) return p.kv_bf16 ? launch_t<WF_I8, 1>(p, grid, stream) : launch_t<WF_I8, 0>(p, grid, stream);
-    if (p.wfmt == WF_BF16) return p.kv_bf16 ? launch_t<WF_BF16, 1>(p, grid, stream) : launch_t<WF_BF16, 0>(p, grid, stream);
-    return p.kv_bf16 ? launch_t<WF_F32, 1>(p, grid, stream) : launch_t<WF_F32, 0>(p, grid, stream);
+    return dispatch(p.wfmt, p.tfmt, p.kv_bf16, LaunchOp{p, grid, stream});
 }
 
 // Largest number of co-resident CTAs of the decode kernel on this device.
-int decode_max_ctas(int wfmt, int kv_bf16, size_t smem) {
+int decode_max_ctas(int wfmt, int tfmt, int kv_bf16, size_t smem) {
     int dev = 0, sms = 0, per = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const void *f;
-    if (wfmt == WF_I8) f = kv_bf16 ? (const void *)decode_kernel<WF_I8, 1> : (const void *)decode_kernel<WF_I8, 0>;
-    else if (wfmt == WF_BF16) f = kv_bf16 ? (const void *)decode_kernel<WF_BF16, 1> : (const void *)decode_kernel<WF_BF16, 0>;
-    else f = kv_bf16 ? (const void *)decode_kernel<WF_F32, 1> : (const void *)decode_kernel<WF_F32, 0>;
+    const void *f = dispatch(wfmt, tfmt, kv_bf16, PtrOp{});
     if (cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, f, NT, smem) != cudaSuccess) return 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, f, kDecodeBlock, smem) != cudaSuccess) return 0;
     return per * sms;
 }
 

@@ -45,6 +45,29 @@ struct DecodeCtrl {
     unsigned ticket;   // end-of-step ticket (reset by the last CTA)
 };
 
+// The weight kinds a CTA streams, and their host-computed geometry.
+enum { K_QKV = 0, K_O = 1, K_GU = 2, K_DN = 3, K_LM = 4, NKIND = 5 };
+struct KindGeom {
+    int stride;      // bytes per padded row
+    int C;           // 16-byte chunks per row
+    int rpc;         // rows per ring chunk (slot_bytes / stride, >= 1)
+    int RS;          // row lanes NT / C when C <= NT (thread t owns column t % C), else 0
+    unsigned magic;  // ceil(2^32 / C): t / C == umulhi(t, magic) for t < NT
+    int group;       // ring chunks reduced together (partials fit part_cap)
+};
+
+// The rows each CTA owns in every phase (host-computed, no division on the
+// device).  Attention items are (query head, o_proj row range) pairs.
+constexpr int kMaxAttItems = 4;
+struct CtaGeom {
+    int qkv_r0, qkv_n;  // rows of [Wq;Wk;Wv]
+    int gu_f0, gu_n;    // rows of gate and of up
+    int dn_r0, dn_n;    // rows of down (== hidden elements written)
+    int lm_v0, lm_n;    // rows of the LM-head table
+    int natt;
+    int att_hh[kMaxAttItems], att_r0[kMaxAttItems], att_n[kMaxAttItems];
+};
+
 struct DecodeParams {
     int V, L, h, qh, kvh, hd, ff, cap, group;
     int wfmt, tfmt, kv_bf16;
@@ -52,7 +75,8 @@ struct DecodeParams {
     int ch, chd, cff, cemb;   // 16-byte chunks per row for K = h, hd, ff and the table
     size_t sh, shd, sff, semb;  // row strides in bytes
     int rqkv;                 // h + 2 * kv_heads * head_dim
-    int s_o;                  // CTAs per query head in the attention phase
+    KindGeom kind[NKIND];
+    const CtaGeom *geom;      // [grid]
     const uint8_t *emb;       // [V, semb] embedding table (FP32 or BF16)
     const uint8_t *head;      // LM head table (== emb when tied)
     const float *final_norm;
@@ -67,17 +91,25 @@ struct DecodeParams {
     int *amax_i;              // [grid] per-CTA argmax index
     int *emitted;             // [cap] greedy id emitted after each position (nullable)
     DecodeCtrl *ctrl;
+    // Optional phase trace (globaltimer ns): [4L barriers][grid] arrival
+    // times, then [4L] barrier release times seen by CTA 0, then the kernel
+    // start (CTA 0) and the end of the final reduction.  Null = off.
+    unsigned long long *trace;
     unsigned long long timeout_ns;
-    int prefetch;
+    int prefetch;             // L2 prefetch of upcoming weights by the producer warp
     // Shared-memory carve-up, in floats from the base (host-computed).
-    int sm_xs, sm_part, sm_h2, sm_q, sm_sc, sm_gu, sm_red, part_cap, sm_total;
+    int sm_xs, sm_part, sm_h2, sm_q, sm_sc, sm_gu, sm_red, sm_gain, sm_rv, sm_lay, part_cap;
+    // Weight ring: nslot slots of slot_bytes at sm_ring (128-byte aligned) and
+    // their full/empty mbarriers at sm_bar (2 * nslot, 8-byte aligned).
+    int sm_bar, sm_ring, nslot, slot_bytes, sm_total;
 };
 
 // Shared-memory bytes the kernel needs for these parameters.
 size_t decode_smem_bytes(const DecodeParams &p);
 // Launches one decode step (cooperative, one CTA per SM).
 cudaError_t decode_launch(const DecodeParams &p, int grid, cudaStream_t stream);
-// Threads per CTA.
+// Compute threads per CTA; one more warp streams the weights.
 constexpr int kDecodeThreads = 512;
+constexpr int kDecodeBlock = kDecodeThreads + 32;
 
 }  // namespace qb

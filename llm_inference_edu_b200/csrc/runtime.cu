@@ -20,7 +20,7 @@
 #include "decode.cuh"
 
 namespace qb {
-int decode_max_ctas(int wfmt, int kv_bf16, size_t smem);
+int decode_max_ctas(int wfmt, int tfmt, int kv_bf16, size_t smem);
 
 // ------------------------------------------------------ conversions ----
 
@@ -275,7 +275,7 @@ struct Session {
     int kv_bf16 = 0;
     size_t logical_bytes = 0, workspace_bytes = 0;
     cudaStream_t stream = nullptr;
-    DevBuf kv, rope, qkv, part, act, hidden, logits, amax_v, amax_i, emitted, ctrl, dlayers;
+    DevBuf kv, rope, qkv, part, act, hidden, logits, amax_v, amax_i, emitted, ctrl, dlayers, geom;
     DecodeCtrl *hctrl = nullptr;  // pinned mirror
     DecodeParams params{};
     int grid = 0;
@@ -360,7 +360,7 @@ static uint32_t session_build(Session &s) {
     p.sh = m.sh; p.shd = m.shd; p.sff = m.sff; p.semb = m.semb;
     p.ch = (int)(m.sh / 16); p.chd = (int)(m.shd / 16); p.cff = (int)(m.sff / 16); p.cemb = (int)(m.semb / 16);
     p.rqkv = (int)rqkv;
-    p.s_o = std::max(1, std::min(8, s.grid / std::max(1, p.qh)));
+    const int s_o = std::max(1, std::min(8, s.grid / std::max(1, p.qh)));  // CTAs per query head
     p.emb = m.emb.as<uint8_t>();
     p.head = m.head_set ? m.head.as<uint8_t>() : m.emb.as<uint8_t>();
     p.final_norm = m.final_norm.as<float>();
@@ -372,24 +372,83 @@ static uint32_t session_build(Session &s) {
     p.ctrl = s.ctrl.as<DecodeCtrl>();
     p.timeout_ns = 2000000000ull;
     p.prefetch = 1;
+    // Rows each CTA owns in every phase (floor(n * b / G) splits), and its
+    // attention items: (query head, o_proj row range) pairs wi = b + m * G.
+    std::vector<CtaGeom> geo(s.grid);
+    auto lo = [&](long long n, int b) { return (int)(n * b / s.grid); };
+    int max_qkv = 0, max_gu = 0, max_dn = 0, max_lm = 0, max_att = 0;
+    for (int b = 0; b < s.grid; ++b) {
+        CtaGeom &g = geo[b];
+        memset(&g, 0, sizeof(g));
+        g.qkv_r0 = lo(p.rqkv, b); g.qkv_n = lo(p.rqkv, b + 1) - g.qkv_r0;
+        g.gu_f0 = lo(p.ff, b); g.gu_n = lo(p.ff, b + 1) - g.gu_f0;
+        g.dn_r0 = lo(p.h, b); g.dn_n = lo(p.h, b + 1) - g.dn_r0;
+        g.lm_v0 = lo(p.V, b); g.lm_n = lo(p.V, b + 1) - g.lm_v0;
+        for (int wi = b; wi < p.qh * s_o; wi += s.grid) {
+            if (g.natt == kMaxAttItems) return QB_UNSUPPORTED;
+            const int sp = wi % s_o;
+            const int r0 = (int)((long long)p.h * sp / s_o), r1 = (int)((long long)p.h * (sp + 1) / s_o);
+            g.att_hh[g.natt] = wi / s_o;
+            g.att_r0[g.natt] = r0;
+            g.att_n[g.natt] = r1 - r0;
+            max_att = std::max(max_att, r1 - r0);
+            ++g.natt;
+        }
+        max_qkv = std::max(max_qkv, g.qkv_n); max_gu = std::max(max_gu, g.gu_n);
+        max_dn = std::max(max_dn, g.dn_n); max_lm = std::max(max_lm, g.lm_n);
+    }
+    if ((size_t)p.V * s.grid >= (1ull << 31)) return QB_UNSUPPORTED;
+    if ((st = s.geom.alloc(geo.size() * sizeof(CtaGeom), false))) return st;
+    QB_CUDA(cudaMemcpy(s.geom.p, geo.data(), geo.size() * sizeof(CtaGeom), cudaMemcpyHostToDevice));
+    p.geom = s.geom.as<CtaGeom>();
+
     // Shared-memory carve-up (floats).
     int xs = std::max({p.ch * epc, p.chd * epc, p.cff * epc, p.cemb * tepc, p.h});
     xs = (xs + 3) & ~3;
-    int part_cap = std::max({8192, p.ch, p.chd, p.cff, p.cemb, 512});
+    int part_cap = std::max({8192, p.ch, p.chd, p.cff, p.cemb, kDecodeThreads});
     part_cap = (part_cap + 3) & ~3;
     int h2 = (p.h + 3) & ~3;
     int q = (3 * p.hd + std::max(p.hd, p.chd * epc) + 3) & ~3;
-    int sc = (p.cap + 3) & ~3;
-    int rows_per = (int)((std::max<size_t>({c.ff_dim, c.hidden_dim, rqkv}) + s.grid - 1) / s.grid);
-    int gu = (2 * rows_per + 4 + 3) & ~3;
+    // scores, or the logits of this CTA's LM-head rows
+    int sc = (std::max({p.cap, max_lm, 256}) + 3) & ~3;
+    int gu = (std::max({max_qkv, 2 * max_gu, max_dn, max_att}) + 4 + 3) & ~3;  // row results
     int red = 128;
+    int gain = h2;
+    int rv = (std::max({2 * max_qkv, 2 * max_gu, max_dn, max_att}) + 4 + 3) & ~3;
+    int lay = (int)((L * sizeof(DecodeLayer) / 4 + 3) & ~(size_t)3);
     p.sm_xs = 0; p.sm_part = xs; p.sm_h2 = p.sm_part + part_cap; p.sm_q = p.sm_h2 + h2;
     p.sm_sc = p.sm_q + q; p.sm_gu = p.sm_sc + sc; p.sm_red = p.sm_gu + gu;
-    p.sm_total = p.sm_red + red;
+    p.sm_gain = p.sm_red + red; p.sm_rv = p.sm_gain + gain; p.sm_lay = p.sm_rv + rv;
     p.part_cap = part_cap;
+    // Weight ring: slots of at least 16 KB holding whole rows, as many as
+    // fit the remaining shared memory (at most 16), 128-byte aligned; the
+    // full/empty mbarriers (2 per slot, 8 bytes each) precede it.
+    size_t max_row = std::max({m.sh, m.shd, m.sff, m.semb});
+    p.slot_bytes = (int)std::max<size_t>(16384, (max_row + 127) & ~(size_t)127);
+    p.sm_bar = (p.sm_lay + lay + 3) & ~3;
+    p.sm_ring = (p.sm_bar + 2 * 2 * 16 + 31) & ~31;
+    const size_t budget = 227 * 1024 - 1024;  // CTA limit less the static shared memory
+    const size_t used = (size_t)p.sm_ring * 4;
+    int nslot = used < budget ? (int)((budget - used) / p.slot_bytes) : 0;
+    if (nslot > 16) nslot = 16;
+    if (nslot < 2) return QB_UNSUPPORTED;
+    p.nslot = nslot;
+    p.sm_total = p.sm_ring + nslot * p.slot_bytes / 4;
+    // Per-kind geometry of the streamed blocks.
+    const size_t strides[NKIND] = {m.sh, m.shd, m.sh, m.sff, m.semb};
+    for (int k = 0; k < NKIND; ++k) {
+        KindGeom &g = p.kind[k];
+        g.stride = (int)strides[k];
+        g.C = (int)(strides[k] / 16);
+        g.rpc = std::max(1, p.slot_bytes / g.stride);
+        g.RS = g.C <= kDecodeThreads ? kDecodeThreads / g.C : 0;
+        g.magic = (unsigned)(((1ull << 32) + g.C - 1) / g.C);
+        const int pcols = g.RS ? g.C : kDecodeThreads;
+        g.group = std::max(1, std::min(nslot, part_cap / (g.rpc * pcols)));
+    }
     size_t smem = decode_smem_bytes(p);
     if (smem > 227 * 1024) return QB_UNSUPPORTED;
-    int maxc = decode_max_ctas(wf, s.kv_bf16, smem);
+    int maxc = decode_max_ctas(wf, p.tfmt, s.kv_bf16, smem);
     if (maxc < s.grid) return QB_UNSUPPORTED;
 
     // Graph: control block in, one decode step, result out.
@@ -851,6 +910,44 @@ uint32_t qb_session_append(uint64_t session, const uint32_t *tokens, size_t n, f
         uint32_t st = session_step(S, tokens[i], last ? logits : nullptr, logits_len, last ? argmax : nullptr, last);
         if (st) return st;
     }
+    return QB_OK;
+}
+
+uint32_t qb_session_step_profiled(uint64_t session, uint32_t token, float *logits, size_t logits_len,
+                                  uint32_t *argmax, uint64_t *stamps, size_t stamps_len, size_t *needed) {
+    clear_detail();
+    auto sp = find_session(session);
+    if (!sp) return QB_INVALID_HANDLE;
+    Session &s = *sp;
+    const size_t nb = 4 * s.m->c.layers;
+    const size_t need = nb * (size_t)s.grid + nb + 2;
+    if (needed) *needed = need;
+    if (!stamps || stamps_len < need) {
+        set_detail(5, need, stamps_len);
+        return QB_INVALID_LENGTH;
+    }
+    if (!s.valid) return QB_INVALID_STATE;
+    if (logits && logits_len != s.m->c.vocab_size) return QB_INVALID_OUTPUT_LENGTH;
+    if (token >= s.m->c.vocab_size) return QB_INVALID_TOKEN;
+    if (s.processed == s.capacity) return QB_FULL;
+    DeviceGuard dg(s.device);
+    DevBuf tr;
+    uint32_t st = tr.alloc(need * 8);
+    if (st) return st;
+    DecodeParams p = s.params;
+    p.trace = tr.as<unsigned long long>();
+    s.hctrl->token = (int)token;
+    s.hctrl->pos = (int)s.processed;
+    s.hctrl->write_logits = 1;
+    cudaError_t e = cudaMemcpyAsync(s.ctrl.p, s.hctrl, 16, cudaMemcpyHostToDevice, s.stream);
+    if (e == cudaSuccess) e = decode_launch(p, s.grid, s.stream);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync((char *)s.hctrl + 16, (char *)s.ctrl.p + 16, 8, cudaMemcpyDeviceToHost, s.stream);
+    if (e != cudaSuccess) return session_fail(s, cuda_status(e));
+    st = session_finish(s, logits, argmax);
+    if (st) return st;
+    s.logits_valid = true;
+    QB_CUDA(cudaMemcpy(stamps, tr.p, need * 8, cudaMemcpyDeviceToHost));
     return QB_OK;
 }
 

@@ -284,9 +284,20 @@ def _qwen_pair(oracle, linear_format, kv, seed=1, prompt_len=128, greedy=64, che
 
 
 def test_qwen05b_int8_parity(oracle):
-    # BASELINE config 3 shape: INT8 per-row linears, BF16 table and KV.
-    worst, dev_ids, or_ids = _qwen_pair(oracle, "int8", "bf16")
+    # 0.5B shape, INT8 per-row linears, BF16 table, FP32 KV (the reference's
+    # own cache type): FP32 logits tolerance max-abs 1e-3.
+    worst, dev_ids, or_ids = _qwen_pair(oracle, "int8", "f32")
     assert worst <= 1e-3, worst
+    assert dev_ids == or_ids
+
+
+def test_qwen05b_int8_bf16_kv_parity(oracle):
+    # The benchmarked 0.5B INT8 workload: BF16 table and BF16 KV.  A stored
+    # key or value whose FP32 input differs in the last bits (summation
+    # order) can round to the neighbouring BF16 value (2^-8 relative), so
+    # the BF16 logits tolerance max-abs 2e-2 applies; greedy ids must agree.
+    worst, dev_ids, or_ids = _qwen_pair(oracle, "int8", "bf16")
+    assert worst <= 2e-2, worst
     assert dev_ids == or_ids
 
 
