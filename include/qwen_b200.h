@@ -167,6 +167,34 @@ uint32_t qb_softmax(const float *logits, size_t logits_len, const uint8_t *mask,
 uint32_t qb_rope(const float *x, size_t x_len, float *y, size_t y_len, size_t tokens,
                  size_t heads, size_t head_dim, size_t start_position, float base, void *stream);
 
+/* qb_rope without any allocation.  No counterpart in the reference: it is
+ * qb_rope (same arguments, checks, results and error codes) for callers
+ * that must not allocate -- a serving process that has already divided
+ * device memory between weights and KV pages, where a late cudaMalloc can
+ * fail or fragment memory another allocator owns, and latency-bound code
+ * with work in flight on other streams, which cudaFree would wait for.
+ * It uses no cudaMalloc/cudaFree, no heap and no allocating library call:
+ * its device scratch (a flag word and the angle table) is one fixed static
+ * array of QB_ROPE_STATIC_SCRATCH_BYTES per device inside this library, and
+ * the host stages the table through a 16 KiB stack buffer.
+ *  - Limit: tokens * head_dim <= QB_ROPE_STATIC_MAX_TABLE.  A larger call
+ *    returns QB_RESOURCE_BUDGET before any device work, with qb_last_detail
+ *    expected = the limit and actual = tokens * head_dim.
+ *  - The first call on each device looks up the array's address with
+ *    cudaGetSymbolAddress; make that first call before any stream capture
+ *    starts on that device.
+ *  - Each call resets the flag word itself; the angle table needs no
+ *    starting value (each call writes all of it before the kernel reads it).
+ *  - All calls on one device share the one array, so calls that overlap in
+ *    time (several host threads) race and can return wrong results:
+ *    serialize them.  As with qb_rope, `stream` is synchronized before the
+ *    call returns, so consecutive calls from one thread never overlap. */
+#define QB_ROPE_STATIC_SCRATCH_BYTES 262144u
+#define QB_ROPE_STATIC_MAX_TABLE 65472u /* (262144 - 256) / 4 floats */
+uint32_t qb_rope_static(const float *x, size_t x_len, float *y, size_t y_len, size_t tokens,
+                        size_t heads, size_t head_dim, size_t start_position, float base,
+                        void *stream);
+
 /* ------------------------------------------------------------------ */
 /* Model: ModelConfig / Decoder (src/model.rs:12-25,191-273)           */
 /* ------------------------------------------------------------------ */

@@ -31,6 +31,7 @@ SIGNATURES = {
     "qb_silu": ([P, S, P, S, P], U32),
     "qb_softmax": ([P, S, P, S, P, S, S, S, P], U32),
     "qb_rope": ([P, S, P, S, S, S, S, S, F, P], U32),
+    "qb_rope_static": ([P, S, P, S, S, S, S, S, F, P], U32),
     "qb_model_create": ([P, U32, U32, C.c_int, P], U32),
     "qb_model_set_tensor": ([U64, C.c_int64, U32, U32, P, S], U32),
     "qb_model_finalize": ([U64], U32),

@@ -14,7 +14,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "libqwen_b200.so")
-SOURCES = ["ops.cu", "decode.cu", "runtime.cu", "synthetic.cpp"]
+SOURCES = ["ops.cu", "decode.cu", "runtime.cu", "static_scratch.cu", "synthetic.cpp"]
 HEADERS = ["common.cuh", "decode.cuh"]
 
 NVCC_FLAGS = [
