@@ -3,18 +3,17 @@
 // One cooperative launch evaluates one token through every layer and the LM
 // head (src/kv_cache.rs:347-475 with attend_one :479-590) and leaves the
 // greedy argmax (src/sampling.rs:65-70) in the control block.  The grid is
-// one CTA per SM: 16 compute warps and one producer warp.  Compute phases
+// one CTA per SM: 15 compute warps and one producer warp.  Compute phases
 // are separated by a grid barrier whose wait is bounded by a timeout (the
-// kernel then reports ERR_TIMEOUT, drains its own bulk copies and returns;
-// it never spins forever):
+// kernel then reports ERR_TIMEOUT and returns; it never spins forever):
 //
 //   per layer:  QKV      RMSNorm (each CTA, redundantly) -> rows of [Wq;Wk;Wv]
 //                        + bias
 //               ATTN     per (query head, o_proj row range): RoPE from the host
 //                        cos/sin table, K/V write, softmax(q.K/sqrt d).V, then
 //                        that head's o_proj partial for the row range
-//               GATE/UP  residual + sum of head partials, RMSNorm, rows of
-//                        gate and up, SiLU(gate)*up
+//               GATE/UP  residual + sum of head partials, RMSNorm, (gate, up)
+//                        row pairs, SiLU(gate)*up
 //               DOWN     rows of down + residual
 //   final:      LM HEAD  RMSNorm, rows of the (tied) table, logits, argmax;
 //                        the last CTA reduces the per-CTA argmaxes.
@@ -23,12 +22,18 @@
 // warp streams every row block the CTA will multiply -- all phases of the
 // step, in order -- through a shared-memory ring of `nslot` slots with 1-D
 // bulk copies (cp.async.bulk ... mbarrier::complete_tx), waiting only for
-// the compute warps to free a slot ("empty" mbarrier).  It never waits for
-// a grid barrier, so the next phases' weights are in shared memory before
-// the activations they meet exist, and no weight occupies a register.  The
-// producer also prefetches the rows a few phases ahead into L2.  The per-CTA
-// row ranges come precomputed from the host: the critical path has no
-// integer division and no long serial chain.
+// the compute warps to free a slot ("empty" mbarrier, one arrival per compute
+// warp).  It never waits for a grid barrier, so a phase's weights are in
+// shared memory before the activations they meet exist.
+//
+// Latency discipline.  Batch-1 decode moves ~1 MB per CTA per step; what
+// costs time is dependent latency, so the compute side is written to keep
+// every chain short: every helper is inlined (no stack frame, no local
+// memory), global loads are issued in batches before their first use, each
+// GEMV row is reduced by a team of threads with shuffles (no shared-memory
+// partials), reductions over a vector are done redundantly per warp instead
+// of across warps, and activations sit in shared memory in a layout whose
+// 16-byte reads never conflict.
 #include <math.h>
 
 #include "common.cuh"
@@ -39,6 +44,7 @@ namespace qb {
 constexpr int NT = kDecodeThreads;  // compute threads
 constexpr int NW = NT / 32;         // compute warps
 constexpr int LOOKAHEAD = 3;        // L2 prefetch distance in phases
+constexpr unsigned FULL = 0xffffffffu;
 
 template <int WF> struct Fmt;
 template <> struct Fmt<WF_F32> { static constexpr int EPC = 4; };
@@ -50,92 +56,87 @@ __device__ __forceinline__ float ldcg(const float *p) { return __ldcg(p); }
 // Barrier among the compute warps only (the producer warp never joins).
 __device__ __forceinline__ void csync() { asm volatile("bar.sync 1, %0;" ::"n"(NT) : "memory"); }
 
-// Dot product of one 16-byte weight chunk with EPC activations (FMA chain).
+// ------------------------------------------------------ activations ----
+//
+// An activation vector that meets rows of C 16-byte chunks (EPC elements
+// each) is kept "quad-major": element e, in chunk c = e / EPC at position
+// k = e % EPC, lives at float (k / 4 * C + c) * 4 + k % 4.  Chunk c's quads
+// are then C float4 apart and threads that read consecutive chunks read
+// consecutive 16-byte words.
+
+template <int EPC>
+__device__ __forceinline__ int xq(int e, int C) {
+    const int c = e / EPC, k = e % EPC;
+    return ((k >> 2) * C + c) * 4 + (k & 3);
+}
+
+// Dot product of one 16-byte weight chunk with its EPC activations (the
+// chunk's quads x[0..EPC/4)), one FMA chain in element order.
 template <int WF>
-__device__ __forceinline__ float chunk_dot(const uint4 &w, const float *x) {
+__device__ __forceinline__ float chunk_dot(const uint4 &w, const float4 *x) {
     float a = 0.0f;
     if (WF == WF_F32) {
-        a = fmaf(x[0], __uint_as_float(w.x), a);
-        a = fmaf(x[1], __uint_as_float(w.y), a);
-        a = fmaf(x[2], __uint_as_float(w.z), a);
-        a = fmaf(x[3], __uint_as_float(w.w), a);
+        a = fmaf(x[0].x, __uint_as_float(w.x), a);
+        a = fmaf(x[0].y, __uint_as_float(w.y), a);
+        a = fmaf(x[0].z, __uint_as_float(w.z), a);
+        a = fmaf(x[0].w, __uint_as_float(w.w), a);
     } else if (WF == WF_BF16) {
-        a = fmaf(x[0], bf16_lo(w.x), a);
-        a = fmaf(x[1], bf16_hi(w.x), a);
-        a = fmaf(x[2], bf16_lo(w.y), a);
-        a = fmaf(x[3], bf16_hi(w.y), a);
-        a = fmaf(x[4], bf16_lo(w.z), a);
-        a = fmaf(x[5], bf16_hi(w.z), a);
-        a = fmaf(x[6], bf16_lo(w.w), a);
-        a = fmaf(x[7], bf16_hi(w.w), a);
+        a = fmaf(x[0].x, bf16_lo(w.x), a);
+        a = fmaf(x[0].y, bf16_hi(w.x), a);
+        a = fmaf(x[0].z, bf16_lo(w.y), a);
+        a = fmaf(x[0].w, bf16_hi(w.y), a);
+        a = fmaf(x[1].x, bf16_lo(w.z), a);
+        a = fmaf(x[1].y, bf16_hi(w.z), a);
+        a = fmaf(x[1].z, bf16_lo(w.w), a);
+        a = fmaf(x[1].w, bf16_hi(w.w), a);
     } else {
         const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-#pragma unroll
-            for (int b = 0; b < 4; ++b) a = fmaf(x[4 * k + b], u8b_to_f32(ws[k], b), a);
+            a = fmaf(x[k].x, u8b_to_f32(ws[k], 0), a);
+            a = fmaf(x[k].y, u8b_to_f32(ws[k], 1), a);
+            a = fmaf(x[k].z, u8b_to_f32(ws[k], 2), a);
+            a = fmaf(x[k].w, u8b_to_f32(ws[k], 3), a);
         }
     }
     return a;
 }
 
-// Block reductions over the compute warps: warp xor trees, then warp 0 runs
-// one more tree over the warp partials -- a fixed order, broadcast to all.
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
-    for (int off = 16; off; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    for (int off = 16; off; off >>= 1) v += __shfl_xor_sync(FULL, v, off);
     return v;
 }
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
-    for (int off = 16; off; off >>= 1) v = rust_max(v, __shfl_xor_sync(0xffffffffu, v, off));
+    for (int off = 16; off; off >>= 1) v = rust_max(v, __shfl_xor_sync(FULL, v, off));
     return v;
 }
-__device__ __forceinline__ float block_sum(float v, float *red) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    v = warp_sum(v);
-    if (lane == 0) red[warp] = v;
-    csync();
-    if (warp == 0) {
-        v = warp_sum(lane < NW ? red[lane] : 0.0f);
-        if (lane == 0) red[NW] = v;
-    }
-    csync();
-    return red[NW];
-}
-__device__ __forceinline__ float block_max(float v, float *red) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    v = warp_max(v);
-    if (lane == 0) red[warp] = v;
-    csync();
-    if (warp == 0) {
-        v = warp_max(lane < NW ? red[lane] : -INFINITY);
-        if (lane == 0) red[NW] = v;
-    }
-    csync();
-    return red[NW];
-}
 
-// Scaled RMSNorm of `in` (shared, width w) into `out` (shared, zero-padded
-// to `padded`), src/ops.rs:137-149.  The row scale is an exact maximum.
-__device__ __forceinline__ void block_rmsnorm(const float *in, const float *gain, float *out, int w,
-                                              int padded, float eps, float *red) {
+// Scaled RMSNorm (src/ops.rs:137-149) of `in` (shared, width w) into the
+// quad-major layout for EPC/C, zero-padded to C * EPC.  Every warp computes
+// the row scale and the sum of squares itself, in the same order, so no
+// cross-warp reduction is needed; the scale is an exact maximum.
+template <int EPC>
+__device__ __forceinline__ void warp_rmsnorm(const float *in, const float *gain, float *xs, int w, int C,
+                                             float eps) {
+    const int t = threadIdx.x, lane = t & 31;
     const float se = sqrtf(eps);
     float m = se;
-#pragma unroll 1
-    for (int i = threadIdx.x; i < w; i += NT) m = rust_max(m, fabsf(in[i]));
-    m = block_max(m, red);
+#pragma unroll 4
+    for (int i = lane; i < w; i += 32) m = rust_max(m, fabsf(in[i]));
+    m = warp_max(m);
     float ss = 0.0f;
-#pragma unroll 1
-    for (int i = threadIdx.x; i < w; i += NT) {
-        float v = in[i] / m;
+#pragma unroll 4
+    for (int i = lane; i < w; i += 32) {
+        const float v = in[i] / m;
         ss = ss + v * v;
     }
-    ss = block_sum(ss, red);
+    ss = warp_sum(ss);
     const float seps = se / m;
     const float den = sqrtf(ss / (float)w + seps * seps);
-#pragma unroll 1
-    for (int i = threadIdx.x; i < padded; i += NT) out[i] = i < w ? (in[i] / m) / den * gain[i] : 0.0f;
+    const int padded = C * EPC;
+    for (int i = t; i < padded; i += NT) xs[xq<EPC>(i, C)] = i < w ? (in[i] / m) / den * gain[i] : 0.0f;
     csync();
 }
 
@@ -143,11 +144,48 @@ __device__ __forceinline__ void flag_nonfinite(DecodeCtrl *ctrl, float v) {
     if (!isfinite(v)) atomicOr(&ctrl->error, ERR_NONFINITE);
 }
 
+// dst[i] = src[i], i < n, with B loads in flight per thread (L2-coherent
+// loads: src was written earlier in this step by other CTAs).
+template <int B>
+__device__ __forceinline__ void stage_l2(float *dst, const float *src, int n) {
+    for (int base = threadIdx.x; base < n; base += B * NT) {
+        float v[B];
+#pragma unroll
+        for (int k = 0; k < B; ++k) {
+            const int i = base + k * NT;
+            v[k] = i < n ? ldcg(src + i) : 0.0f;
+        }
+#pragma unroll
+        for (int k = 0; k < B; ++k) {
+            const int i = base + k * NT;
+            if (i < n) dst[i] = v[k];
+        }
+    }
+}
+
+// The same for read-only model vectors (gains, scales, biases).
+template <int B>
+__device__ __forceinline__ void stage_ro(float *dst, const float *src, int n) {
+    for (int base = threadIdx.x; base < n; base += B * NT) {
+        float v[B];
+#pragma unroll
+        for (int k = 0; k < B; ++k) {
+            const int i = base + k * NT;
+            v[k] = i < n ? __ldg(src + i) : 0.0f;
+        }
+#pragma unroll
+        for (int k = 0; k < B; ++k) {
+            const int i = base + k * NT;
+            if (i < n) dst[i] = v[k];
+        }
+    }
+}
+
 // --------------------------------------------------------------- ring ----
 //
 // Chunk k of the CTA's stream lives in slot k % nslot during round
-// u = k / nslot.  full[slot] completes phase u when the copy lands; the
-// compute warps arrive on empty[slot] (phase u) once they have read it.
+// u = k / nslot.  full[slot] completes phase u when the copy lands; every
+// compute warp arrives on empty[slot] (phase u) once it has read it.
 
 struct Ring {
     uint8_t *slots;
@@ -165,11 +203,15 @@ __device__ __forceinline__ Ring ring_of(const DecodeParams &p, float *sm) {
     return r;
 }
 
-// Bounded wait for `parity` on `bar`; on timeout (or when the CTA is already
-// aborting) records ERR_TIMEOUT, raises the abort flag and returns false.
-__device__ __noinline__ bool mbar_wait_slow(const DecodeParams &p, uint64_t *bar, uint32_t parity,
-                                            volatile int *s_abort) {
+// Bounded wait for `parity` on `bar`.  On timeout (or when the CTA is
+// already aborting) records ERR_TIMEOUT, raises the abort flag and returns
+// false; callers carry on to their next CTA barrier, after which the abort
+// flag is tested uniformly.
+__device__ __forceinline__ bool mbar_wait(const DecodeParams &p, uint64_t *bar, uint32_t parity,
+                                          volatile int *s_abort) {
+    if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
+#pragma unroll 1
     for (unsigned it = 1;; ++it) {
         if (mbar_try_wait(bar, parity)) return true;
         if ((it & 63u) == 0 && (*s_abort || globaltimer_ns() - t0 > p.timeout_ns)) {
@@ -178,10 +220,6 @@ __device__ __noinline__ bool mbar_wait_slow(const DecodeParams &p, uint64_t *bar
             return false;
         }
     }
-}
-__device__ __forceinline__ bool mbar_wait(const DecodeParams &p, uint64_t *bar, uint32_t parity,
-                                          volatile int *s_abort) {
-    return mbar_try_wait(bar, parity) || mbar_wait_slow(p, bar, parity, s_abort);
 }
 
 // Consumer cursor (identical in every compute thread).
@@ -266,10 +304,7 @@ __device__ void prefetch_phase(const DecodeParams &p, const DecodeLayer *lay, co
         }
         break;
     }
-    case 2:
-        prefetch_rows(Ly.wg + (size_t)cg.gu_f0 * p.sh, (size_t)cg.gu_n * p.sh);
-        prefetch_rows(Ly.wu + (size_t)cg.gu_f0 * p.sh, (size_t)cg.gu_n * p.sh);
-        break;
+    case 2: prefetch_rows(Ly.wgu + (size_t)2 * cg.gu_f0 * p.sh, (size_t)2 * cg.gu_n * p.sh); break;
     default: prefetch_rows(Ly.wd + (size_t)cg.dn_r0 * p.sff, (size_t)cg.dn_n * p.sff); break;
     }
 }
@@ -291,13 +326,10 @@ __device__ void produce(const DecodeParams &p, const DecodeLayer *lay, const Cta
             for (int a = 0; a < cg.natt; ++a)
                 pr.block(Ly.wo + ((size_t)cg.att_hh[a] * p.h + cg.att_r0[a]) * p.shd, cg.att_n[a], p.kind[K_O]);
         prefetch_phase(p, lay, cg, ph + 2 + LOOKAHEAD, pos);
-        if (leader) {
-            pr.block(Ly.wg + (size_t)cg.gu_f0 * p.sh, cg.gu_n, p.kind[K_GU]);
-            pr.block(Ly.wu + (size_t)cg.gu_f0 * p.sh, cg.gu_n, p.kind[K_GU]);
-        }
+        if (leader) pr.block(Ly.wgu + (size_t)2 * cg.gu_f0 * p.sh, 2 * cg.gu_n, p.kind[K_GU]);
         prefetch_phase(p, lay, cg, ph + 3 + LOOKAHEAD, pos);
         if (leader) pr.block(Ly.wd + (size_t)cg.dn_r0 * p.sff, cg.dn_n, p.kind[K_DN]);
-        pr.alive = __shfl_sync(0xffffffffu, (int)pr.alive, 0) != 0;
+        pr.alive = __shfl_sync(FULL, (int)pr.alive, 0) != 0;
     }
     if (leader && pr.alive) pr.block(p.head + (size_t)cg.lm_v0 * p.semb, cg.lm_n, p.kind[K_LM]);
     if (leader && !pr.alive) pr.drain();
@@ -305,82 +337,84 @@ __device__ void produce(const DecodeParams &p, const DecodeLayer *lay, const Cta
 
 // ------------------------------------------------------------ gemv ----
 //
-// y_r = dot(W_r, x) for the n rows of one block, weights from the ring.
-// When C <= NT thread t owns chunk column c = t % C (its activations stay in
-// registers) and walks rows rs, rs + RS, ... of each chunk; otherwise threads
-// stride the columns of each row.  Partials meet in shared memory and are
-// reduced per row in a fixed order into rowout[r].
+// y_r = dot(W_r, x) for the n rows of one streamed block.  The block is
+// consumed in waves of up to g.wave ring slots: every thread waits for the
+// wave's slots, then teams of G threads take units of U rows round-robin;
+// a team's threads stride the row's chunks (c = lane-in-team + G * i),
+// accumulate in FP32 and meet in a shuffle butterfly, and the team's first
+// thread hands the U results to `epi(row, a0, a1)`.  Each warp frees the
+// wave's slots as soon as it is done with them.  A failed wait (timeout)
+// leaves the abort flag set; the caller tests it after its next CTA barrier.
 
-template <int WF>
-__device__ __noinline__ bool ring_gemv(const DecodeParams &p, const Ring &rg, Cursor &cur, const KindGeom &g, int n,
-                          const float *xs, float *part, volatile int *s_abort, float *rowout) {
-    constexpr int EPC = Fmt<WF>::EPC;
-    if (n <= 0) return true;
+template <int WF, int U, class Epi>
+__device__ __forceinline__ void team_gemv(const DecodeParams &p, const Ring &rg, Cursor &cur, const KindGeom &g,
+                                          int n, const float *xs, volatile int *s_abort, Epi &&epi) {
+    constexpr int Q = Fmt<WF>::EPC / 4;
     const int t = threadIdx.x, lane = t & 31;
-    const bool cols = g.RS > 0;
-    const int pcols = cols ? g.C : NT;
-    const int rs = cols ? (int)__umulhi((unsigned)t, g.magic) : 0;
-    const int c = cols ? t - rs * g.C : t;
-    const bool active = !cols || rs < g.RS;
-    float xr[EPC];
-    if (cols) {
+    const int lgG = g.lgG, G = 1 << lgG;
+    const int lt = t & (G - 1), tm = t >> lgG, T = NT >> lgG;
+    const int warp_team0 = (t & ~31) >> lgG;
+    const int C = g.C;
+    const float4 *x4 = reinterpret_cast<const float4 *>(xs);
+#pragma unroll 1
+    for (int r0 = 0; r0 < n;) {
+        const int rows = min(g.wave * g.rpc, n - r0);
+        const int ns = (rows + g.rpc - 1) / g.rpc;
+        {
+            Cursor c = cur;
+#pragma unroll 1
+            for (int j = 0; j < ns; ++j) {
+                mbar_wait(p, rg.full + c.slot, (uint32_t)(c.round & 1), s_abort);
+                c.advance(rg.nslot);
+            }
+        }
+        const int nu = rows / U;
+#pragma unroll 1
+        for (int ub = 0; ub < nu; ub += T) {
+            if (ub + warp_team0 >= nu) break;  // warp-uniform
+            const int u = ub + tm;
+            const bool act = u < nu;
+            float a0 = 0.0f, a1 = 0.0f;
+            if (act) {
+                const int row = u * U;
+                const int j = row / g.rpc;
+                int s = cur.slot + j;
+                if (s >= rg.nslot) s -= rg.nslot;
+                const uint8_t *w0 = rg.slots + (size_t)s * rg.slot_bytes + (size_t)(row - j * g.rpc) * g.stride;
+#pragma unroll 2
+                for (int c = lt; c < C; c += G) {
+                    float4 x[Q];
 #pragma unroll
-        for (int k = 0; k < EPC; ++k) xr[k] = active ? xs[c * EPC + k] : 0.0f;
-    }
-    const int grows = g.rpc * g.group;  // rows per reduction group
-#pragma unroll 1
-    for (int r0 = 0; r0 < n; r0 += grows) {
-        const int rows_g = min(grows, n - r0);
-        const Cursor c0 = cur;
-#pragma unroll 1
-        for (int j = 0; j * g.rpc < rows_g; ++j) {
-            if (!mbar_wait(p, rg.full + cur.slot, (uint32_t)(cur.round & 1), s_abort)) break;
-            const uint8_t *slot = rg.slots + (size_t)cur.slot * rg.slot_bytes;
-            const int nr = min(g.rpc, rows_g - j * g.rpc);
-            const int pr0 = j * g.rpc;
-            if (cols) {
-                if (active)
-#pragma unroll 1
-                    for (int r = rs; r < nr; r += g.RS) {
-                        const uint4 w = *(const uint4 *)(slot + (size_t)r * g.stride + (size_t)c * 16);
-                        part[(pr0 + r) * g.C + c] = chunk_dot<WF>(w, xr);
+                    for (int q = 0; q < Q; ++q) x[q] = x4[q * C + c];
+                    const uint4 w = *reinterpret_cast<const uint4 *>(w0 + (size_t)c * 16);
+                    a0 += chunk_dot<WF>(w, x);
+                    if (U == 2) {
+                        const uint4 w1 = *reinterpret_cast<const uint4 *>(w0 + g.stride + (size_t)c * 16);
+                        a1 += chunk_dot<WF>(w1, x);
                     }
-            } else {
-#pragma unroll 1
-                for (int r = 0; r < nr; ++r) {
-                    float acc = 0.0f;
-#pragma unroll 1
-                    for (int cc = t; cc < g.C; cc += NT) {
-                        const uint4 w = *(const uint4 *)(slot + (size_t)r * g.stride + (size_t)cc * 16);
-                        acc += chunk_dot<WF>(w, xs + cc * EPC);
-                    }
-                    part[(pr0 + r) * NT + t] = acc;
                 }
             }
-            cur.advance(rg.nslot);
+#pragma unroll 1
+            for (int off = G >> 1; off; off >>= 1) {
+                a0 += __shfl_xor_sync(FULL, a0, off);
+                if (U == 2) a1 += __shfl_xor_sync(FULL, a1, off);
+            }
+            if (act && lt == 0) epi(r0 + u * U, a0, a1);
         }
-        csync();
-        if (*s_abort) return false;
-        // Every compute thread has read the group's slots: hand them back.
-        if (t == 0) {
+        __syncwarp();
+        if (lane == 0) {
             fence_proxy_async_smem();
-            Cursor e = c0;
-            for (int j = 0; j * g.rpc < rows_g; ++j) {
-                mbar_arrive(rg.empty + e.slot);
-                e.advance(rg.nslot);
+            Cursor c = cur;
+#pragma unroll 1
+            for (int j = 0; j < ns; ++j) {
+                mbar_arrive(rg.empty + c.slot);
+                c.advance(rg.nslot);
             }
         }
 #pragma unroll 1
-        for (int r = t >> 5; r < rows_g; r += NW) {
-            float s = 0.0f;
-#pragma unroll 1
-            for (int cc = lane; cc < pcols; cc += 32) s += part[r * pcols + cc];
-            s = warp_sum(s);
-            if (lane == 0) rowout[r0 + r] = s;
-        }
-        csync();
+        for (int j = 0; j < ns; ++j) cur.advance(rg.nslot);
+        r0 += rows;
     }
-    return true;
 }
 
 // ------------------------------------------------------------ barrier ----
@@ -389,9 +423,9 @@ __device__ __noinline__ bool ring_gemv(const DecodeParams &p, const Ring &rg, Cu
 // the CTA's writes visible (csync, then thread 0's release reduction);
 // independent work can run before barrier_wait, which polls with relaxed
 // loads (bounded by the timeout) and ends with an acquire fence and csync.
-// barrier_wait returns false (after recording ERR_TIMEOUT and raising the
-// abort flag) when the arrivals do not complete in time or another CTA has
-// timed out.
+// barrier_wait returns false (uniformly, after recording ERR_TIMEOUT and
+// raising the abort flag) when the arrivals do not complete in time, when
+// another CTA has timed out, or when this CTA is already aborting.
 __device__ __forceinline__ void barrier_arrive(const DecodeParams &p, unsigned target) {
     csync();
     if (threadIdx.x == 0) {
@@ -403,7 +437,7 @@ __device__ __forceinline__ void barrier_arrive(const DecodeParams &p, unsigned t
     }
 }
 
-__device__ __noinline__ bool barrier_wait(const DecodeParams &p, unsigned target, volatile int *s_abort) {
+__device__ __forceinline__ bool barrier_wait(const DecodeParams &p, unsigned target, volatile int *s_abort) {
     DecodeCtrl *ctrl = p.ctrl;
     if (threadIdx.x == 0) {
         volatile unsigned *bar = &ctrl->bar;
@@ -444,23 +478,27 @@ __device__ __forceinline__ float resid_in(const DecodeParams &p, int l, int toke
     return p.tfmt == WF_BF16 ? bf16_to_f32(((const uint16_t *)row)[i]) : ((const float *)row)[i];
 }
 
-// h' = x + o_proj(ctx): the head partials summed in head order, then the
-// residual added (src/kv_cache.rs:405-406).
-__device__ __forceinline__ float after_attention(const DecodeParams &p, int l, int token, int i) {
-    // Eight heads' loads are in flight at a time; the sum runs in head order.
-    const float *base = p.part + i;
+// h2 = x + o_proj(ctx): the per-head partials summed in head order, then the
+// residual added (src/kv_cache.rs:405-406).  All of an element's loads are
+// issued before the first add.
+__device__ __forceinline__ void stage_after_attention(const DecodeParams &p, int l, int token, float *h2) {
+    constexpr int HB = 16;
     const size_t stride = (size_t)p.h;
-    float o = 0.0f;
+#pragma unroll 2
+    for (int i = threadIdx.x; i < p.h; i += NT) {
+        const float r = resid_in(p, l, token, i);
+        float o = 0.0f;
 #pragma unroll 1
-    for (int h0 = 0; h0 < p.qh; h0 += 8) {
-        float v[8];
+        for (int h0 = 0; h0 < p.qh; h0 += HB) {
+            float v[HB];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) v[k] = h0 + k < p.qh ? ldcg(base + (size_t)(h0 + k) * stride) : 0.0f;
+            for (int k = 0; k < HB; ++k) v[k] = h0 + k < p.qh ? ldcg(p.part + (size_t)(h0 + k) * stride + i) : 0.0f;
 #pragma unroll
-        for (int k = 0; k < 8; ++k)
-            if (h0 + k < p.qh) o = (h0 + k == 0) ? v[k] : o + v[k];
+            for (int k = 0; k < HB; ++k)
+                if (h0 + k < p.qh) o = (h0 + k == 0) ? v[k] : o + v[k];
+        }
+        h2[i] = r + o;
     }
-    return resid_in(p, l, token, i) + o;
 }
 
 __device__ __forceinline__ float silu1(float v) {
@@ -475,46 +513,55 @@ __device__ __forceinline__ float kv_load(const uint8_t *base, size_t idx) {
     return __ldcg((const float *)base + idx);
 }
 
-// Attention for query head hh at position pos (src/kv_cache.rs:550-576),
-// leaving the context vector in shared memory (ctx, zero-padded).  The
-// first CTA of a KV group writes the new K (rotated) and V at `pos`.
+// Attention for query head hh at position pos (src/kv_cache.rs:550-576).
+// Leaves the context vector in xs (quad-major for the o_proj rows,
+// zero-padded).  The first CTA of a KV group writes the new K (rotated) and
+// V at `pos`.  Scores keep the reference's order (q.k summed by increasing
+// index, then divided by sqrt(hd)); softmax subtracts the maximum and
+// divides by the sum.
 template <int WF, int KVBF16>
-__device__ __noinline__ void attention_context(const DecodeParams &p, const DecodeLayer &Ly, int hh, bool writer, int pos,
-                                  float *sm) {
+__device__ __forceinline__ void attention_context(const DecodeParams &p, const DecodeLayer &Ly, int hh, bool writer,
+                                                  int pos, float *sm) {
+    constexpr int EPC = Fmt<WF>::EPC;
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
     const int hd = p.hd, half = hd / 2, g = hh / p.group;
     const size_t kvw = (size_t)p.kvh * hd;
-    float *qs = sm + p.sm_q, *ks = qs + hd, *vs = ks + hd, *ctx = vs + hd;
-    float *sc = sm + p.sm_sc, *red = sm + p.sm_red, *part = sm + p.sm_part;
-    const float2 *rp = p.rope + (size_t)pos * half;
+    float *qs = sm + p.sm_q, *ks = qs + hd, *vs = ks + hd;
+    float *sc = sm + p.sm_sc, *red = sm + p.sm_red, *xs = sm + p.sm_xs;
+    // q and k rotated with the host table (threads [0, NT/2)), v (threads
+    // [NT/2, NT)); every load is issued before its first use.
+    if (t < NT / 2) {
+        const float2 *rp = p.rope + (size_t)pos * half;
 #pragma unroll 1
-    for (int j = threadIdx.x; j < half; j += NT) {
-        const float2 cs = rp[j];
-        const float a = ldcg(p.qkv + (size_t)hh * hd + j), b = ldcg(p.qkv + (size_t)hh * hd + j + half);
-        qs[j] = a * cs.x - b * cs.y;
-        qs[j + half] = b * cs.x + a * cs.y;
-        const float ka = ldcg(p.qkv + p.h + (size_t)g * hd + j), kb = ldcg(p.qkv + p.h + (size_t)g * hd + j + half);
-        float k0 = ka * cs.x - kb * cs.y, k1 = kb * cs.x + ka * cs.y;
-        if (KVBF16) { k0 = round_bf16(k0); k1 = round_bf16(k1); }
-        ks[j] = k0;
-        ks[j + half] = k1;
+        for (int j = t; j < half; j += NT / 2) {
+            const float2 cs = rp[j];
+            const float a = ldcg(p.qkv + (size_t)hh * hd + j), b = ldcg(p.qkv + (size_t)hh * hd + j + half);
+            const float ka = ldcg(p.qkv + p.h + (size_t)g * hd + j);
+            const float kb = ldcg(p.qkv + p.h + (size_t)g * hd + j + half);
+            qs[j] = a * cs.x - b * cs.y;
+            qs[j + half] = b * cs.x + a * cs.y;
+            float k0 = ka * cs.x - kb * cs.y, k1 = kb * cs.x + ka * cs.y;
+            if (KVBF16) { k0 = round_bf16(k0); k1 = round_bf16(k1); }
+            ks[j] = k0;
+            ks[j + half] = k1;
+        }
+    } else {
+#pragma unroll 1
+        for (int i = t - NT / 2; i < hd; i += NT / 2) {
+            const float v = ldcg(p.qkv + p.h + kvw + (size_t)g * hd + i);
+            vs[i] = KVBF16 ? round_bf16(v) : v;
+        }
     }
-#pragma unroll 1
-    for (int i = threadIdx.x; i < hd; i += NT) {
-        const float v = ldcg(p.qkv + p.h + kvw + (size_t)g * hd + i);
-        vs[i] = KVBF16 ? round_bf16(v) : v;
-    }
-    const int ctx_pad = p.chd * Fmt<WF>::EPC;
-#pragma unroll 1
-    for (int i = hd + threadIdx.x; i < ctx_pad; i += NT) ctx[i] = 0.0f;
     csync();
-    if (threadIdx.x < hd && (!isfinite(qs[threadIdx.x]) || !isfinite(ks[threadIdx.x])))
-        atomicOr(&p.ctrl->error, ERR_NONFINITE);
+#pragma unroll 1
+    for (int i = t; i < hd; i += NT)
+        if (!isfinite(qs[i]) || !isfinite(ks[i])) atomicOr(&p.ctrl->error, ERR_NONFINITE);
     const size_t esz = KVBF16 ? 2 : 4;
     const uint8_t *K = Ly.kc + (size_t)g * p.cap * hd * esz;
     const uint8_t *Vc = Ly.vc + (size_t)g * p.cap * hd * esz;
     if (writer) {
 #pragma unroll 1
-        for (int i = threadIdx.x; i < hd; i += NT) {
+        for (int i = t; i < hd; i += NT) {
             const size_t idx = (size_t)g * p.cap * hd + (size_t)pos * hd + i;
             if (KVBF16) {
                 ((uint16_t *)Ly.kc)[idx] = f32_to_bf16_rne(ks[i]);
@@ -525,19 +572,21 @@ __device__ __noinline__ void attention_context(const DecodeParams &p, const Deco
             }
         }
     }
-    // scores: q.k / sqrt(d), one position per thread, increasing i.
+    // Scores: one position per thread, its key row read as 16-byte chunks
+    // (eight in flight), the dot product by increasing index.
     const int row_bytes = hd * (int)esz;
+    const int nc = row_bytes >> 4;
     const bool vec = (row_bytes & 15) == 0;
     constexpr int KEPC = KVBF16 ? 8 : 4;  // cache elements per 16-byte chunk
+    float mt = -INFINITY;
 #pragma unroll 1
-    for (int q = threadIdx.x; q <= pos; q += NT) {
+    for (int q = t; q <= pos; q += NT) {
         float s = 0.0f;
         if (q == pos) {
-#pragma unroll 1
+#pragma unroll 4
             for (int i = 0; i < hd; ++i) s = s + qs[i] * ks[i];
         } else if (vec) {
             const uint8_t *row = K + (size_t)q * row_bytes;
-            const int nc = row_bytes >> 4;
 #pragma unroll 1
             for (int c0 = 0; c0 < nc; c0 += 8) {
                 uint4 kc[8];
@@ -562,239 +611,248 @@ __device__ __noinline__ void attention_context(const DecodeParams &p, const Deco
 #pragma unroll 1
             for (int i = 0; i < hd; ++i) s = s + qs[i] * kv_load<KVBF16>(K, (size_t)q * hd + i);
         }
-        sc[q] = s / p.sqrt_hd;
+        s = s / p.sqrt_hd;
+        sc[q] = s;
+        mt = rust_max(mt, s);
     }
+    // Softmax: maximum and sum each meet through one shared array of warp
+    // partials, read in warp order by every thread.
+    mt = warp_max(mt);
+    if (lane == 0) red[warp] = mt;
     csync();
-    float m = -INFINITY;
+    float m = red[0];
+#pragma unroll
+    for (int w = 1; w < NW; ++w) m = rust_max(m, red[w]);
+    float st = 0.0f;
 #pragma unroll 1
-    for (int q = threadIdx.x; q <= pos; q += NT) m = rust_max(m, sc[q]);
-    m = block_max(m, red);
-    float se = 0.0f;
-#pragma unroll 1
-    for (int q = threadIdx.x; q <= pos; q += NT) {
+    for (int q = t; q <= pos; q += NT) {
         const float e = expf(sc[q] - m);
         sc[q] = e;
-        se += e;
+        st += e;
     }
-    se = block_sum(se, red);
-#pragma unroll 1
-    for (int q = threadIdx.x; q <= pos; q += NT) sc[q] = sc[q] / se;
+    st = warp_sum(st);
+    if (lane == 0) red[NW + warp] = st;
     csync();
-    // context: position groups pg sum positions pg, pg+PG, ... in order;
-    // the groups then meet in group order.
-    int PG;
-    if (vec) {
-        const int nc = row_bytes >> 4;
-        PG = NT / nc;
-        const int c = threadIdx.x % nc, pg = threadIdx.x / nc;
-        if (pg < PG) {
-            float acc[KEPC];
+    float se = red[NW];
 #pragma unroll
-            for (int e = 0; e < KEPC; ++e) acc[e] = 0.0f;
+    for (int w = 1; w < NW; ++w) se += red[NW + w];
+    // Context: thread t takes chunk c = t % nc of the value rows of the
+    // positions q = pg, pg + PG, ... (pg = t / nc); the position groups meet
+    // by shuffles inside the warp, then across warps in warp order.
+    const int ctx_pad = p.chd * EPC;
+    if (vec && nc <= 32 && (nc & (nc - 1)) == 0) {
+        const int PG = NT / nc;
+        const int c = t & (nc - 1), pg = t / nc;
+        float acc[KEPC];
+#pragma unroll
+        for (int e = 0; e < KEPC; ++e) acc[e] = 0.0f;
 #pragma unroll 1
-            for (int q0 = pg; q0 <= pos; q0 += 4 * PG) {
-                uint4 vc[4];
+        for (int q0 = pg; q0 <= pos; q0 += 4 * PG) {
+            uint4 vc[4];
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const int q = q0 + u * PG;
-                    if (q < pos) vc[u] = __ldcg((const uint4 *)(Vc + (size_t)q * row_bytes + (size_t)c * 16));
-                }
+            for (int u = 0; u < 4; ++u) {
+                const int q = q0 + u * PG;
+                if (q < pos) vc[u] = __ldcg((const uint4 *)(Vc + (size_t)q * row_bytes + (size_t)c * 16));
+            }
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const int q = q0 + u * PG;
-                    if (q <= pos) {
-                        const float pr = sc[q];
-                        const uint32_t w4[4] = {vc[u].x, vc[u].y, vc[u].z, vc[u].w};
+            for (int u = 0; u < 4; ++u) {
+                const int q = q0 + u * PG;
+                if (q <= pos) {
+                    const float pr = sc[q] / se;
+                    const uint32_t w4[4] = {vc[u].x, vc[u].y, vc[u].z, vc[u].w};
 #pragma unroll
-                        for (int e = 0; e < KEPC; ++e) {
-                            const float v = q == pos ? vs[c * KEPC + e]
-                                                     : (KVBF16 ? ((e & 1) ? bf16_hi(w4[e >> 1]) : bf16_lo(w4[e >> 1]))
-                                                               : __uint_as_float(w4[e]));
-                            acc[e] = acc[e] + pr * v;
-                        }
+                    for (int e = 0; e < KEPC; ++e) {
+                        const float v = q == pos ? vs[c * KEPC + e]
+                                                 : (KVBF16 ? ((e & 1) ? bf16_hi(w4[e >> 1]) : bf16_lo(w4[e >> 1]))
+                                                           : __uint_as_float(w4[e]));
+                        acc[e] = acc[e] + pr * v;
                     }
                 }
             }
+        }
+#pragma unroll 1
+        for (int off = nc; off < 32; off <<= 1) {
 #pragma unroll
-            for (int e = 0; e < KEPC; ++e) part[pg * hd + c * KEPC + e] = acc[e];
+            for (int e = 0; e < KEPC; ++e) acc[e] += __shfl_xor_sync(FULL, acc[e], off);
+        }
+        if (lane < nc) {
+#pragma unroll
+            for (int e = 0; e < KEPC; ++e) red[2 * NW + warp * hd + c * KEPC + e] = acc[e];
+        }
+        csync();
+#pragma unroll 1
+        for (int i = t; i < ctx_pad; i += NT) {
+            float s = 0.0f;
+            if (i < hd) {
+                s = red[2 * NW + i];
+#pragma unroll
+                for (int w = 1; w < NW; ++w) s += red[2 * NW + w * hd + i];
+                flag_nonfinite(p.ctrl, s);
+            }
+            xs[xq<EPC>(i, p.chd)] = s;
         }
     } else {
-        PG = NT / hd > 0 ? NT / hd : 1;
-        const int i = threadIdx.x % hd, pg = threadIdx.x / hd;
-        float acc = 0.0f;
-        if (pg < PG && threadIdx.x < PG * hd) {
+        // General layout: one thread per output element, positions in order.
 #pragma unroll 1
-            for (int q = pg; q <= pos; q += PG) {
-                const float v = q == pos ? vs[i] : kv_load<KVBF16>(Vc, (size_t)q * hd + i);
-                acc = acc + sc[q] * v;
+        for (int i = t; i < ctx_pad; i += NT) {
+            float s = 0.0f;
+            if (i < hd) {
+#pragma unroll 1
+                for (int q = 0; q <= pos; ++q) {
+                    const float v = q == pos ? vs[i] : kv_load<KVBF16>(Vc, (size_t)q * hd + i);
+                    s = s + (sc[q] / se) * v;
+                }
+                flag_nonfinite(p.ctrl, s);
             }
-            part[pg * hd + i] = acc;
+            xs[xq<EPC>(i, p.chd)] = s;
         }
-    }
-    csync();
-#pragma unroll 1
-    for (int i = threadIdx.x; i < hd; i += NT) {
-        float s = part[i];
-#pragma unroll 1
-        for (int k = 1; k < PG; ++k) s += part[k * hd + i];
-        ctx[i] = s;
-        flag_nonfinite(p.ctrl, s);
     }
     csync();
 }
 
 // ------------------------------------------------------------ phases ----
 //
-// Each phase has a `prep` that stages its small vectors -- `gain` (norm
-// gains) and `rv` (row scales rv[0..R), biases or second scales rv[R..2R))
-// -- into shared memory before the grid barrier that precedes it, and a
-// `run` after the barrier.  The weights arrive through the ring.
-
-// Stages n floats of global memory into shared memory.
-__device__ __forceinline__ void stage(float *dst, const float *src, int n) {
-#pragma unroll 1
-    for (int i = threadIdx.x; i < n; i += NT) dst[i] = src[i];
-}
+// Each phase has a `prep` that stages its small read-only vectors -- `gain`
+// (norm gains) and `rv` (row scales and biases) -- into shared memory while
+// the grid barrier before it completes, and a `run` after the barrier.  The
+// weights arrive through the ring.
 
 template <int WF>
 __device__ __forceinline__ void prep_qkv(const DecodeParams &p, const DecodeLayer &Ly, const CtaGeom &cg,
                                          float *sm) {
     float *gain = sm + p.sm_gain, *rv = sm + p.sm_rv;
-    stage(gain, Ly.attn_norm, p.h);
-    if (WF == WF_I8) stage(rv, Ly.sqkv + cg.qkv_r0, cg.qkv_n);
-    stage(rv + cg.qkv_n, Ly.bqkv + cg.qkv_r0, cg.qkv_n);
+    stage_ro<2>(gain, Ly.attn_norm, p.h);
+    if (WF == WF_I8) stage_ro<1>(rv, Ly.sqkv + cg.qkv_r0, cg.qkv_n);
+    stage_ro<1>(rv + cg.qkv_n, Ly.bqkv + cg.qkv_r0, cg.qkv_n);
 }
 
 template <int WF>
-__device__ __forceinline__ bool run_qkv(const DecodeParams &p, const CtaGeom &cg, int l, int token, float *sm,
+__device__ __forceinline__ void run_qkv(const DecodeParams &p, const CtaGeom &cg, int l, int token, float *sm,
                                         const Ring &rg, Cursor &cur, volatile int *s_abort) {
     constexpr int EPC = Fmt<WF>::EPC;
-    float *xs = sm + p.sm_xs, *part = sm + p.sm_part, *h2 = sm + p.sm_h2, *red = sm + p.sm_red;
+    float *xs = sm + p.sm_xs, *h2 = sm + p.sm_h2;
     const float *gain = sm + p.sm_gain, *rv = sm + p.sm_rv;
-#pragma unroll 1
-    for (int i = threadIdx.x; i < p.h; i += NT) h2[i] = resid_in(p, l, token, i);
+    if (l > 0) {
+        stage_l2<2>(h2, p.hidden, p.h);
+    } else {
+#pragma unroll 2
+        for (int i = threadIdx.x; i < p.h; i += NT) h2[i] = resid_in(p, 0, token, i);
+    }
     csync();
-    block_rmsnorm(h2, gain, xs, p.h, p.ch * EPC, p.eps, red);
-    float *rows = sm + p.sm_gu;
-    if (!ring_gemv<WF>(p, rg, cur, p.kind[K_QKV], cg.qkv_n, xs, part, s_abort, rows)) return false;
+    warp_rmsnorm<EPC>(h2, gain, xs, p.h, p.ch, p.eps);
     const int R = cg.qkv_n;
     float *out = p.qkv + cg.qkv_r0;
-#pragma unroll 1
-    for (int r = threadIdx.x; r < R; r += NT) {
-        float v = rows[r];
+    DecodeCtrl *ctrl = p.ctrl;
+    team_gemv<WF, 1>(p, rg, cur, p.kind[K_QKV], R, xs, s_abort, [&](int r, float a, float) {
+        float v = a;
         if (WF == WF_I8) v = v * rv[r];
         v = v + rv[R + r];
         out[r] = v;
-        flag_nonfinite(p.ctrl, v);
-    }
-    return true;
+        flag_nonfinite(ctrl, v);
+    });
 }
 
 template <int WF>
 __device__ __forceinline__ void prep_attention(const DecodeParams &p, const DecodeLayer &Ly, const CtaGeom &cg,
                                                float *sm) {
-    if (WF == WF_I8 && cg.natt > 0) stage(sm + p.sm_rv, Ly.so + cg.att_r0[0], cg.att_n[0]);
+    if (WF == WF_I8 && cg.natt > 0) stage_ro<1>(sm + p.sm_rv, Ly.so + cg.att_r0[0], cg.att_n[0]);
 }
 
 template <int WF, int KVBF16>
-__device__ __forceinline__ bool run_attention(const DecodeParams &p, const DecodeLayer &Ly, const CtaGeom &cg,
+__device__ __forceinline__ void run_attention(const DecodeParams &p, const DecodeLayer &Ly, const CtaGeom &cg,
                                               int pos, float *sm, const Ring &rg, Cursor &cur,
                                               volatile int *s_abort) {
-    float *part = sm + p.sm_part, *ctx = sm + p.sm_q + 3 * p.hd;
-    const float *rv = sm + p.sm_rv;
+    const float *rv = sm + p.sm_rv, *xs = sm + p.sm_xs;
+    DecodeCtrl *ctrl = p.ctrl;
 #pragma unroll 1
     for (int a = 0; a < cg.natt; ++a) {
         const int hh = cg.att_hh[a], r0 = cg.att_r0[a], n = cg.att_n[a];
         attention_context<WF, KVBF16>(p, Ly, hh, r0 == 0 && hh % p.group == 0, pos, sm);
-        float *rows = sm + p.sm_gu;
-        if (!ring_gemv<WF>(p, rg, cur, p.kind[K_O], n, ctx, part, s_abort, rows)) return false;
         float *outp = p.part + (size_t)hh * p.h + r0;
-#pragma unroll 1
-        for (int r = threadIdx.x; r < n; r += NT) {
-            float v = rows[r];
-            if (WF == WF_I8) v = v * (a == 0 ? rv[r] : Ly.so[r0 + r]);
+        const float *so = Ly.so + r0;
+        team_gemv<WF, 1>(p, rg, cur, p.kind[K_O], n, xs, s_abort, [&](int r, float acc, float) {
+            float v = acc;
+            if (WF == WF_I8) v = v * (a == 0 ? rv[r] : __ldg(so + r));
             outp[r] = v;
-            flag_nonfinite(p.ctrl, v);
-        }
-        csync();
+            flag_nonfinite(ctrl, v);
+        });
+        if (a + 1 < cg.natt) csync();  // xs is rewritten by the next item
     }
-    return true;
 }
 
 template <int WF>
 __device__ __forceinline__ void prep_gate_up(const DecodeParams &p, const DecodeLayer &Ly, const CtaGeom &cg,
                                              float *sm) {
-    float *gain = sm + p.sm_gain, *rv = sm + p.sm_rv;
-    stage(gain, Ly.ffn_norm, p.h);
-    if (WF == WF_I8) {
-        stage(rv, Ly.sg + cg.gu_f0, cg.gu_n);
-        stage(rv + cg.gu_n, Ly.su + cg.gu_f0, cg.gu_n);
-    }
+    stage_ro<2>(sm + p.sm_gain, Ly.ffn_norm, p.h);
+    if (WF == WF_I8) stage_ro<1>(sm + p.sm_rv, Ly.sgu + 2 * cg.gu_f0, 2 * cg.gu_n);
 }
 
 template <int WF>
-__device__ __forceinline__ bool run_gate_up(const DecodeParams &p, const CtaGeom &cg, int l, int token, float *sm,
+__device__ __forceinline__ void run_gate_up(const DecodeParams &p, const CtaGeom &cg, int l, int token, float *sm,
                                             const Ring &rg, Cursor &cur, volatile int *s_abort) {
     constexpr int EPC = Fmt<WF>::EPC;
-    float *xs = sm + p.sm_xs, *part = sm + p.sm_part, *h2 = sm + p.sm_h2, *red = sm + p.sm_red;
-    float *gu = sm + p.sm_gu;
+    float *xs = sm + p.sm_xs, *h2 = sm + p.sm_h2;
     const float *gain = sm + p.sm_gain, *rv = sm + p.sm_rv;
-#pragma unroll 1
-    for (int i = threadIdx.x; i < p.h; i += NT) {
-        const float v = after_attention(p, l, token, i);
-        h2[i] = v;
-        if (blockIdx.x == 0) flag_nonfinite(p.ctrl, v);
-    }
+    stage_after_attention(p, l, token, h2);
     csync();
-    block_rmsnorm(h2, gain, xs, p.h, p.ch * EPC, p.eps, red);
-    const int R = cg.gu_n;
-    if (!ring_gemv<WF>(p, rg, cur, p.kind[K_GU], R, xs, part, s_abort, gu)) return false;
-    if (!ring_gemv<WF>(p, rg, cur, p.kind[K_GU], R, xs, part, s_abort, gu + R)) return false;
-#pragma unroll 1
-    for (int r = threadIdx.x; r < R; r += NT) {
-        float gv = gu[r], uv = gu[R + r];
+    if (blockIdx.x == 0)
+        for (int i = threadIdx.x; i < p.h; i += NT) flag_nonfinite(p.ctrl, h2[i]);
+    warp_rmsnorm<EPC>(h2, gain, xs, p.h, p.ch, p.eps);
+    float *act = p.act + cg.gu_f0;
+    DecodeCtrl *ctrl = p.ctrl;
+    team_gemv<WF, 2>(p, rg, cur, p.kind[K_GU], 2 * cg.gu_n, xs, s_abort, [&](int row, float g, float u) {
         if (WF == WF_I8) {
-            gv = gv * rv[r];
-            uv = uv * rv[R + r];
+            g = g * rv[row];
+            u = u * rv[row + 1];
         }
-        const float a = silu1(gv) * uv;
-        p.act[cg.gu_f0 + r] = a;
-        flag_nonfinite(p.ctrl, gv);
-        flag_nonfinite(p.ctrl, a);
-    }
-    csync();  // rv is restaged by the next prep
-    return true;
+        const float a = silu1(g) * u;
+        act[row >> 1] = a;
+        flag_nonfinite(ctrl, g);
+        flag_nonfinite(ctrl, a);
+    });
 }
 
 template <int WF>
 __device__ __forceinline__ void prep_down(const DecodeParams &p, const DecodeLayer &Ly, const CtaGeom &cg,
                                           float *sm) {
-    if (WF == WF_I8) stage(sm + p.sm_rv, Ly.sd + cg.dn_r0, cg.dn_n);
+    if (WF == WF_I8) stage_ro<1>(sm + p.sm_rv, Ly.sd + cg.dn_r0, cg.dn_n);
 }
 
 template <int WF>
-__device__ __forceinline__ bool run_down(const DecodeParams &p, const CtaGeom &cg, float *sm, const Ring &rg,
+__device__ __forceinline__ void run_down(const DecodeParams &p, const CtaGeom &cg, float *sm, const Ring &rg,
                                          Cursor &cur, volatile int *s_abort) {
     constexpr int EPC = Fmt<WF>::EPC;
-    float *xs = sm + p.sm_xs, *part = sm + p.sm_part;
+    constexpr int B = 16;
+    float *xs = sm + p.sm_xs;
+    const int padded = p.cff * EPC;
+    // act -> xs (quad-major, zero-padded), B loads in flight per thread.
 #pragma unroll 1
-    for (int i = threadIdx.x; i < p.cff * EPC; i += NT) xs[i] = i < p.ff ? ldcg(p.act + i) : 0.0f;
+    for (int base = threadIdx.x; base < padded; base += B * NT) {
+        float v[B];
+#pragma unroll
+        for (int k = 0; k < B; ++k) {
+            const int i = base + k * NT;
+            v[k] = i < p.ff ? ldcg(p.act + i) : 0.0f;
+        }
+#pragma unroll
+        for (int k = 0; k < B; ++k) {
+            const int i = base + k * NT;
+            if (i < padded) xs[xq<EPC>(i, p.cff)] = v[k];
+        }
+    }
     csync();
-    float *rows = sm + p.sm_gu;
-    if (!ring_gemv<WF>(p, rg, cur, p.kind[K_DN], cg.dn_n, xs, part, s_abort, rows)) return false;
     // h' of this layer is still in shared memory from the gate/up phase of
     // this same CTA (src/kv_cache.rs:437-443: x_next = h' + down(a)).
     const float *h2 = sm + p.sm_h2 + cg.dn_r0, *rv = sm + p.sm_rv;
     float *hidden = p.hidden + cg.dn_r0;
-#pragma unroll 1
-    for (int r = threadIdx.x; r < cg.dn_n; r += NT) {
-        float v = rows[r];
+    DecodeCtrl *ctrl = p.ctrl;
+    team_gemv<WF, 1>(p, rg, cur, p.kind[K_DN], cg.dn_n, xs, s_abort, [&](int r, float acc, float) {
+        float v = acc;
         if (WF == WF_I8) v = v * rv[r];
         const float o = h2[r] + v;
         hidden[r] = o;
-        flag_nonfinite(p.ctrl, o);
-    }
-    return true;
+        flag_nonfinite(ctrl, o);
+    });
 }
 
 // Final RMSNorm, this CTA's rows of the (tied) table, logits and the CTA's
@@ -802,30 +860,31 @@ __device__ __forceinline__ bool run_down(const DecodeParams &p, const CtaGeom &c
 // logits of all the CTA's rows land in `rowv`; warp 0 scans them in row
 // order, so ties keep the lowest id.
 template <int TF>
-__device__ __forceinline__ bool run_lm_head(const DecodeParams &p, const CtaGeom &cg, int pos, float *sm,
+__device__ __forceinline__ void run_lm_head(const DecodeParams &p, const CtaGeom &cg, int pos, float *sm,
                                             const Ring &rg, Cursor &cur, volatile int *s_abort) {
     constexpr int TEPC = Fmt<TF>::EPC;
     const int G = gridDim.x, b = blockIdx.x;
-    float *xs = sm + p.sm_xs, *part = sm + p.sm_part, *h2 = sm + p.sm_h2, *red = sm + p.sm_red;
+    float *xs = sm + p.sm_xs, *h2 = sm + p.sm_h2;
     const float *gain = sm + p.sm_gain;
     float *rowv = sm + p.sm_sc;
     DecodeCtrl *ctrl = p.ctrl;
-#pragma unroll 1
-    for (int i = threadIdx.x; i < p.h; i += NT) h2[i] = ldcg(p.hidden + i);
+    stage_l2<2>(h2, p.hidden, p.h);
     csync();
-    block_rmsnorm(h2, gain, xs, p.h, p.cemb * TEPC, p.eps, red);
-    if (!ring_gemv<TF>(p, rg, cur, p.kind[K_LM], cg.lm_n, xs, part, s_abort, rowv)) return false;
-    // ring_gemv ends with a barrier, so every row's logit is in rowv.
+    warp_rmsnorm<TEPC>(h2, gain, xs, p.h, p.cemb, p.eps);
+    team_gemv<TF, 1>(p, rg, cur, p.kind[K_LM], cg.lm_n, xs, s_abort,
+                     [&](int r, float acc, float) { rowv[r] = acc; });
+    csync();
+    if (*s_abort) return;
     if (ctrl->write_logits) {
         float *lg = p.logits + cg.lm_v0;
-#pragma unroll 1
+#pragma unroll 4
         for (int r = threadIdx.x; r < cg.lm_n; r += NT) lg[r] = rowv[r];
     }
     if (threadIdx.x < 32) {
         const int lane = threadIdx.x;
         float bv = -INFINITY;
         int bi = 0x7fffffff;
-#pragma unroll 1
+#pragma unroll 4
         for (int r = lane; r < cg.lm_n; r += 32) {
             const float v = rowv[r];
             if (!isfinite(v)) atomicOr(&ctrl->error, ERR_NONFINITE);
@@ -833,8 +892,8 @@ __device__ __forceinline__ bool run_lm_head(const DecodeParams &p, const CtaGeom
         }
 #pragma unroll
         for (int off = 16; off; off >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+            const float ov = __shfl_xor_sync(FULL, bv, off);
+            const int oi = __shfl_xor_sync(FULL, bi, off);
             if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
         }
         if (lane == 0) {
@@ -864,13 +923,13 @@ __device__ __forceinline__ bool run_lm_head(const DecodeParams &p, const CtaGeom
             }
         }
     }
-    return true;
 }
 
 // ------------------------------------------------------------ kernel ----
 
 template <int WF, int TF, int KVBF16>
-__global__ void __launch_bounds__(kDecodeBlock, 1) decode_kernel(const __grid_constant__ DecodeParams p) {
+// Four warps per sub-partition x 32 threads x 128 registers = its 16K registers.
+__global__ void __maxnreg__(128) decode_kernel(const __grid_constant__ DecodeParams p) {
     extern __shared__ __align__(128) float sm[];
     __shared__ int s_abort_storage;
     volatile int *s_abort = &s_abort_storage;
@@ -894,7 +953,7 @@ __global__ void __launch_bounds__(kDecodeBlock, 1) decode_kernel(const __grid_co
     if (threadIdx.x == 0) {
         for (int i = 0; i < p.nslot; ++i) {
             mbar_init(rg.full + i, 1);
-            mbar_init(rg.empty + i, 1);
+            mbar_init(rg.empty + i, NW);
         }
         fence_mbar_init();
         *s_abort = 0;
@@ -912,33 +971,33 @@ __global__ void __launch_bounds__(kDecodeBlock, 1) decode_kernel(const __grid_co
     unsigned target = 0;
     bool ok = true;
     // Each phase: run, arrive at the grid barrier, stage the next phase's
-    // vectors while the other CTAs arrive, then wait.
+    // vectors while the other CTAs arrive, then wait.  Every exit decision
+    // is taken after a CTA barrier, so all compute threads agree on it.
 #pragma unroll 1
     for (int l = 0; l < p.L && ok; ++l) {
         const DecodeLayer &Ly = lay[l];
-        if (!(ok = run_qkv<WF>(p, cg, l, token, sm, rg, cur, s_abort))) break;
+        run_qkv<WF>(p, cg, l, token, sm, rg, cur, s_abort);
         barrier_arrive(p, target += G);
         prep_attention<WF>(p, Ly, cg, sm);
         if (!(ok = barrier_wait(p, target, s_abort))) break;
 
-        if (!(ok = run_attention<WF, KVBF16>(p, Ly, cg, pos, sm, rg, cur, s_abort))) break;
+        run_attention<WF, KVBF16>(p, Ly, cg, pos, sm, rg, cur, s_abort);
         barrier_arrive(p, target += G);
         prep_gate_up<WF>(p, Ly, cg, sm);
         if (!(ok = barrier_wait(p, target, s_abort))) break;
 
-        if (!(ok = run_gate_up<WF>(p, cg, l, token, sm, rg, cur, s_abort))) break;
+        run_gate_up<WF>(p, cg, l, token, sm, rg, cur, s_abort);
         barrier_arrive(p, target += G);
         prep_down<WF>(p, Ly, cg, sm);
         if (!(ok = barrier_wait(p, target, s_abort))) break;
 
-        if (!(ok = run_down<WF>(p, cg, sm, rg, cur, s_abort))) break;
+        run_down<WF>(p, cg, sm, rg, cur, s_abort);
         barrier_arrive(p, target += G);
         if (l + 1 < p.L) prep_qkv<WF>(p, lay[l + 1], cg, sm);
-        else stage(sm + p.sm_gain, p.final_norm, p.h);
+        else stage_ro<2>(sm + p.sm_gain, p.final_norm, p.h);
         if (!(ok = barrier_wait(p, target, s_abort))) break;
     }
-    if (ok) ok = run_lm_head<TF>(p, cg, pos, sm, rg, cur, s_abort);
-    if (!ok && threadIdx.x == 0) *s_abort = 1;  // releases a producer waiting for a slot
+    if (ok) run_lm_head<TF>(p, cg, pos, sm, rg, cur, s_abort);
 }
 
 size_t decode_smem_bytes(const DecodeParams &p) { return (size_t)p.sm_total * sizeof(float); }

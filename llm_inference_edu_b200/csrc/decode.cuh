@@ -21,10 +21,8 @@ struct DecodeLayer {
     const float *bqkv;    // [h + 2 kv] biases (zeros when the model has none)
     const uint8_t *wo;    // head-blocked o_proj: [qh][h rows][stride_hd]
     const float *so;      // [h] row scales (INT8) or null
-    const uint8_t *wg;    // [ff, stride_h]
-    const float *sg;
-    const uint8_t *wu;    // [ff, stride_h]
-    const float *su;
+    const uint8_t *wgu;   // [2 ff, stride_h]: row 2f = gate row f, row 2f + 1 = up row f
+    const float *sgu;     // [2 ff] row scales in the same order (INT8) or null
     const uint8_t *wd;    // [h, stride_ff]
     const float *sd;
     const float *attn_norm;  // [h]
@@ -45,15 +43,17 @@ struct DecodeCtrl {
     unsigned ticket;   // end-of-step ticket (reset by the last CTA)
 };
 
-// The weight kinds a CTA streams, and their host-computed geometry.
+// The weight kinds a CTA streams, and their host-computed geometry.  A
+// "unit" is the U consecutive rows one team of G = 2^lgG threads multiplies
+// together (U = 2 pairs each gate row with its up row).
 enum { K_QKV = 0, K_O = 1, K_GU = 2, K_DN = 3, K_LM = 4, NKIND = 5 };
 struct KindGeom {
-    int stride;      // bytes per padded row
-    int C;           // 16-byte chunks per row
-    int rpc;         // rows per ring chunk (slot_bytes / stride, >= 1)
-    int RS;          // row lanes NT / C when C <= NT (thread t owns column t % C), else 0
-    unsigned magic;  // ceil(2^32 / C): t / C == umulhi(t, magic) for t < NT
-    int group;       // ring chunks reduced together (partials fit part_cap)
+    int stride;  // bytes per padded row
+    int C;       // 16-byte chunks per row
+    int rpc;     // rows per ring slot (a multiple of U)
+    int lgG;     // log2 of the threads per unit (0..5)
+    int U;       // rows per unit
+    int wave;    // ring slots waited for and released together (<= nslot / 2 or the block)
 };
 
 // The rows each CTA owns in every phase (host-computed, no division on the
@@ -98,7 +98,11 @@ struct DecodeParams {
     unsigned long long timeout_ns;
     int prefetch;             // L2 prefetch of upcoming weights by the producer warp
     // Shared-memory carve-up, in floats from the base (host-computed).
-    int sm_xs, sm_part, sm_h2, sm_q, sm_sc, sm_gu, sm_red, sm_gain, sm_rv, sm_lay, part_cap;
+    // xs: the current activation vector in the quad-major layout; h2: the
+    // residual stream; gain: norm gains; rv: per-row scales/biases; sc:
+    // attention scores or the CTA's logits; q: q, k, v of one head; red:
+    // cross-warp partials; lay: the layer table.
+    int sm_xs, sm_h2, sm_gain, sm_rv, sm_sc, sm_q, sm_red, sm_lay;
     // Weight ring: nslot slots of slot_bytes at sm_ring (128-byte aligned) and
     // their full/empty mbarriers at sm_bar (2 * nslot, 8-byte aligned).
     int sm_bar, sm_ring, nslot, slot_bytes, sm_total;
@@ -108,8 +112,10 @@ struct DecodeParams {
 size_t decode_smem_bytes(const DecodeParams &p);
 // Launches one decode step (cooperative, one CTA per SM).
 cudaError_t decode_launch(const DecodeParams &p, int grid, cudaStream_t stream);
-// Compute threads per CTA; one more warp streams the weights.
-constexpr int kDecodeThreads = 512;
+// Compute threads per CTA; one more warp streams the weights.  16 warps in
+// all put 4 on each SM sub-partition, whose 16K registers then allow 128
+// registers per thread.
+constexpr int kDecodeThreads = 480;
 constexpr int kDecodeBlock = kDecodeThreads + 32;
 
 }  // namespace qb

@@ -125,9 +125,10 @@ struct Linear {  // one device linear in the decode layout
 
 struct LayerStore {
     DevBuf wqkv, sqkv, bqkv, wo, so;
-    Linear gate, up, down;
+    DevBuf wgu, sgu;  // gate and up rows interleaved: row 2f = gate f, 2f + 1 = up f
+    Linear down;
     DevBuf attn_norm, ffn_norm;
-    bool q = false, k = false, v = false, o = false, an = false, fn = false;
+    bool q = false, k = false, v = false, o = false, an = false, fn = false, gate = false, up = false;
 };
 
 struct Model {
@@ -193,12 +194,11 @@ static uint32_t check_finite_dev(const float *p, size_t n, size_t *index) {
     return QB_OK;
 }
 
-// Stores FP32 source rows into `dst` (padded rows), quantizing per row for
-// INT8 with the bit-exact scheme of qb_quantize_int8.  `scales` receives the
-// row scales.  Column window [c0, c0 + nc) of the source is stored.
+// Stores FP32 source rows into `dst` (row r at dst + r * stride), quantizing
+// per row for INT8 with the bit-exact scheme of qb_quantize_int8.  Row r's
+// scale goes to scales[r * scale_stride].
 static uint32_t store_linear(const Model &m, const float *src, size_t rows, size_t cols, uint8_t *dst,
-                             size_t stride, float *scales, size_t row_base_dst) {
-    (void)row_base_dst;
+                             size_t stride, float *scales, size_t scale_stride) {
     const int wf = m.wf();
     if (wf == WF_I8) {
         DevBuf q, sc;
@@ -208,7 +208,8 @@ static uint32_t store_linear(const Model &m, const float *src, size_t rows, size
         if (s) return s == QB_NONFINITE_WEIGHT ? QB_NONFINITE : s;
         relayout_kernel<<<gridn(rows * cols), 256>>>(nullptr, q.as<int8_t>(), rows, cols, 0, cols, dst, stride, WF_I8);
         QB_CUDA(cudaGetLastError());
-        QB_CUDA(cudaMemcpy(scales, sc.p, rows * 4, cudaMemcpyDeviceToDevice));
+        if (scale_stride == 1) QB_CUDA(cudaMemcpy(scales, sc.p, rows * 4, cudaMemcpyDeviceToDevice));
+        else QB_CUDA(cudaMemcpy2D(scales, scale_stride * 4, sc.p, 4, 4, rows, cudaMemcpyDeviceToDevice));
     } else {
         size_t idx;
         uint32_t s = check_finite_dev(src, rows * cols, &idx);
@@ -403,27 +404,22 @@ static uint32_t session_build(Session &s) {
     p.geom = s.geom.as<CtaGeom>();
 
     // Shared-memory carve-up (floats).
-    int xs = std::max({p.ch * epc, p.chd * epc, p.cff * epc, p.cemb * tepc, p.h});
-    xs = (xs + 3) & ~3;
-    int part_cap = std::max({8192, p.ch, p.chd, p.cff, p.cemb, kDecodeThreads});
-    part_cap = (part_cap + 3) & ~3;
-    int h2 = (p.h + 3) & ~3;
-    int q = (3 * p.hd + std::max(p.hd, p.chd * epc) + 3) & ~3;
-    // scores, or the logits of this CTA's LM-head rows
-    int sc = (std::max({p.cap, max_lm, 256}) + 3) & ~3;
-    int gu = (std::max({max_qkv, 2 * max_gu, max_dn, max_att}) + 4 + 3) & ~3;  // row results
-    int red = 128;
-    int gain = h2;
-    int rv = (std::max({2 * max_qkv, 2 * max_gu, max_dn, max_att}) + 4 + 3) & ~3;
-    int lay = (int)((L * sizeof(DecodeLayer) / 4 + 3) & ~(size_t)3);
-    p.sm_xs = 0; p.sm_part = xs; p.sm_h2 = p.sm_part + part_cap; p.sm_q = p.sm_h2 + h2;
-    p.sm_sc = p.sm_q + q; p.sm_gu = p.sm_sc + sc; p.sm_red = p.sm_gu + gu;
-    p.sm_gain = p.sm_red + red; p.sm_rv = p.sm_gain + gain; p.sm_lay = p.sm_rv + rv;
-    p.part_cap = part_cap;
-    // Weight ring: slots of at least 16 KB holding whole rows, as many as
-    // fit the remaining shared memory (at most 16), 128-byte aligned; the
-    // full/empty mbarriers (2 per slot, 8 bytes each) precede it.
-    size_t max_row = std::max({m.sh, m.shd, m.sff, m.semb});
+    auto r4 = [](long long v) { return (int)((v + 3) & ~3LL); };
+    const int xs = r4(std::max({(long long)p.ch * epc, (long long)p.chd * epc, (long long)p.cff * epc,
+                                (long long)p.cemb * tepc}));
+    const int h4 = r4(p.h);
+    const int rv = r4(std::max({2 * max_qkv, 2 * max_gu, max_dn, max_att}) + 4);
+    const int sc = r4(std::max({(int)cap, max_lm, 64}));
+    const int q = r4(3 * p.hd);
+    const int red = r4(std::max(64, 2 * 16 + 16 * p.hd));  // softmax partials, then [warp][hd] context partials
+    const int lay = r4((long long)(L * sizeof(DecodeLayer) / 4));
+    p.sm_xs = 0; p.sm_h2 = xs; p.sm_gain = p.sm_h2 + h4; p.sm_rv = p.sm_gain + h4;
+    p.sm_sc = p.sm_rv + rv; p.sm_q = p.sm_sc + sc; p.sm_red = p.sm_q + q; p.sm_lay = p.sm_red + red;
+    // Weight ring: slots of at least 16 KB holding whole rows (and whole
+    // gate/up pairs), as many as fit the remaining shared memory (at most
+    // 16), 128-byte aligned; the full/empty mbarriers (2 per slot, 8 bytes
+    // each) precede it.
+    size_t max_row = std::max({2 * m.sh, m.shd, m.sff, m.semb});
     p.slot_bytes = (int)std::max<size_t>(16384, (max_row + 127) & ~(size_t)127);
     p.sm_bar = (p.sm_lay + lay + 3) & ~3;
     p.sm_ring = (p.sm_bar + 2 * 2 * 16 + 31) & ~31;
@@ -434,17 +430,27 @@ static uint32_t session_build(Session &s) {
     if (nslot < 2) return QB_UNSUPPORTED;
     p.nslot = nslot;
     p.sm_total = p.sm_ring + nslot * p.slot_bytes / 4;
-    // Per-kind geometry of the streamed blocks.
+    // Per-kind geometry of the streamed blocks.  The team size G = 2^lgG
+    // minimises the critical path ceil(units / (threads / G)) * ceil(C / G)
+    // chunk products, plus the butterfly's lgG steps.
     const size_t strides[NKIND] = {m.sh, m.shd, m.sh, m.sff, m.semb};
+    const int rows_max[NKIND] = {max_qkv, max_att, 2 * max_gu, max_dn, max_lm};
     for (int k = 0; k < NKIND; ++k) {
         KindGeom &g = p.kind[k];
         g.stride = (int)strides[k];
         g.C = (int)(strides[k] / 16);
-        g.rpc = std::max(1, p.slot_bytes / g.stride);
-        g.RS = g.C <= kDecodeThreads ? kDecodeThreads / g.C : 0;
-        g.magic = (unsigned)(((1ull << 32) + g.C - 1) / g.C);
-        const int pcols = g.RS ? g.C : kDecodeThreads;
-        g.group = std::max(1, std::min(nslot, part_cap / (g.rpc * pcols)));
+        g.U = k == K_GU ? 2 : 1;
+        g.rpc = std::max(g.U, (p.slot_bytes / g.stride) / g.U * g.U);
+        const int block_slots = std::max(1, (rows_max[k] + g.rpc - 1) / g.rpc);
+        g.wave = std::max(1, std::min(block_slots, nslot / 2));
+        const int units = std::max(1, std::min(rows_max[k], g.wave * g.rpc) / g.U);
+        long long best = -1;
+        for (int lg = 0; lg <= 5; ++lg) {
+            const int G = 1 << lg;
+            const long long cost = (long long)((units + (kDecodeThreads / G) - 1) / (kDecodeThreads / G)) *
+                                       ((g.C + G - 1) / G) * 4 * g.U + lg;
+            if (best < 0 || cost < best) { best = cost; g.lgG = lg; }
+        }
     }
     size_t smem = decode_smem_bytes(p);
     if (smem > 227 * 1024) return QB_UNSUPPORTED;
@@ -622,8 +628,7 @@ uint32_t qb_model_create(const qb_model_config *cfg, uint32_t linear_format, uin
     for (auto &L : m->layers) {
         if ((s = L.wqkv.alloc(rq * m->sh)) || (s = L.sqkv.alloc(rq * 4)) || (s = L.bqkv.alloc(rq * 4)) ||
             (s = L.wo.alloc(c.query_heads * h * m->shd)) || (s = L.so.alloc(h * 4)) ||
-            (s = L.gate.w.alloc(ff * m->sh)) || (s = L.gate.scales.alloc(ff * 4)) ||
-            (s = L.up.w.alloc(ff * m->sh)) || (s = L.up.scales.alloc(ff * 4)) ||
+            (s = L.wgu.alloc(2 * ff * m->sh)) || (s = L.sgu.alloc(2 * ff * 4)) ||
             (s = L.down.w.alloc(h * m->sff)) || (s = L.down.scales.alloc(h * 4)) ||
             (s = L.attn_norm.alloc(h * 4)) || (s = L.ffn_norm.alloc(h * 4)))
             return s == QB_CUDA_ERROR ? QB_ALLOCATION : s;
@@ -699,16 +704,16 @@ uint32_t qb_model_set_tensor(uint64_t model, int64_t layer, uint32_t tensor, uin
     LayerStore &L = m->layers[layer];
     switch (tensor) {
     case QB_T_Q:
-        s = store_linear(*m, src.as<float>(), h, h, L.wqkv.as<uint8_t>(), m->sh, L.sqkv.as<float>(), 0);
+        s = store_linear(*m, src.as<float>(), h, h, L.wqkv.as<uint8_t>(), m->sh, L.sqkv.as<float>(), 1);
         if (!s) L.q = true;
         break;
     case QB_T_K:
-        s = store_linear(*m, src.as<float>(), kv, h, L.wqkv.as<uint8_t>() + h * m->sh, m->sh, L.sqkv.as<float>() + h, 0);
+        s = store_linear(*m, src.as<float>(), kv, h, L.wqkv.as<uint8_t>() + h * m->sh, m->sh, L.sqkv.as<float>() + h, 1);
         if (!s) L.k = true;
         break;
     case QB_T_V:
         s = store_linear(*m, src.as<float>(), kv, h, L.wqkv.as<uint8_t>() + (h + kv) * m->sh, m->sh,
-                         L.sqkv.as<float>() + h + kv, 0);
+                         L.sqkv.as<float>() + h + kv, 1);
         if (!s) L.v = true;
         break;
     case QB_T_O:
@@ -716,15 +721,16 @@ uint32_t qb_model_set_tensor(uint64_t model, int64_t layer, uint32_t tensor, uin
         if (!s) L.o = true;
         break;
     case QB_T_GATE:
-        s = store_linear(*m, src.as<float>(), ff, h, L.gate.w.as<uint8_t>(), m->sh, L.gate.scales.as<float>(), 0);
-        if (!s) L.gate.set = true;
+        s = store_linear(*m, src.as<float>(), ff, h, L.wgu.as<uint8_t>(), 2 * m->sh, L.sgu.as<float>(), 2);
+        if (!s) L.gate = true;
         break;
     case QB_T_UP:
-        s = store_linear(*m, src.as<float>(), ff, h, L.up.w.as<uint8_t>(), m->sh, L.up.scales.as<float>(), 0);
-        if (!s) L.up.set = true;
+        s = store_linear(*m, src.as<float>(), ff, h, L.wgu.as<uint8_t>() + m->sh, 2 * m->sh,
+                         L.sgu.as<float>() + 1, 2);
+        if (!s) L.up = true;
         break;
     case QB_T_DOWN:
-        s = store_linear(*m, src.as<float>(), h, ff, L.down.w.as<uint8_t>(), m->sff, L.down.scales.as<float>(), 0);
+        s = store_linear(*m, src.as<float>(), h, ff, L.down.w.as<uint8_t>(), m->sff, L.down.scales.as<float>(), 1);
         if (!s) L.down.set = true;
         break;
     }
@@ -739,7 +745,7 @@ uint32_t qb_model_finalize(uint64_t model) {
     if (m->finalized) return QB_OK;
     if (!m->emb_set || !m->fn_set) return QB_INVALID_STATE;
     for (auto &L : m->layers)
-        if (!(L.q && L.k && L.v && L.o && L.an && L.fn && L.gate.set && L.up.set && L.down.set))
+        if (!(L.q && L.k && L.v && L.o && L.an && L.fn && L.gate && L.up && L.down.set))
             return QB_INVALID_STATE;
     DeviceGuard dg(m->device);
     const bool i8 = m->wf() == WF_I8;
@@ -749,8 +755,7 @@ uint32_t qb_model_finalize(uint64_t model) {
         DecodeLayer &d = dl[l];
         d.wqkv = L.wqkv.as<uint8_t>(); d.sqkv = i8 ? L.sqkv.as<float>() : nullptr; d.bqkv = L.bqkv.as<float>();
         d.wo = L.wo.as<uint8_t>(); d.so = i8 ? L.so.as<float>() : nullptr;
-        d.wg = L.gate.w.as<uint8_t>(); d.sg = i8 ? L.gate.scales.as<float>() : nullptr;
-        d.wu = L.up.w.as<uint8_t>(); d.su = i8 ? L.up.scales.as<float>() : nullptr;
+        d.wgu = L.wgu.as<uint8_t>(); d.sgu = i8 ? L.sgu.as<float>() : nullptr;
         d.wd = L.down.w.as<uint8_t>(); d.sd = i8 ? L.down.scales.as<float>() : nullptr;
         d.attn_norm = L.attn_norm.as<float>(); d.ffn_norm = L.ffn_norm.as<float>();
         d.kc = d.vc = nullptr;
@@ -792,13 +797,15 @@ uint32_t qb_model_read_int8(uint64_t model, int64_t layer, uint32_t tensor, int8
     LayerStore &L = m->layers[layer];
     const uint8_t *src = nullptr;
     const float *sc = nullptr;
-    size_t rows = 0, cols = h, stride = m->sh;
+    size_t rows = 0, cols = h, stride = m->sh, sstride = 1;
     switch (tensor) {
     case QB_T_Q: src = L.wqkv.as<uint8_t>(); sc = L.sqkv.as<float>(); rows = h; break;
     case QB_T_K: src = L.wqkv.as<uint8_t>() + h * m->sh; sc = L.sqkv.as<float>() + h; rows = kv; break;
     case QB_T_V: src = L.wqkv.as<uint8_t>() + (h + kv) * m->sh; sc = L.sqkv.as<float>() + h + kv; rows = kv; break;
-    case QB_T_GATE: src = L.gate.w.as<uint8_t>(); sc = L.gate.scales.as<float>(); rows = ff; break;
-    case QB_T_UP: src = L.up.w.as<uint8_t>(); sc = L.up.scales.as<float>(); rows = ff; break;
+    case QB_T_GATE: src = L.wgu.as<uint8_t>(); sc = L.sgu.as<float>(); rows = ff; stride = 2 * m->sh; sstride = 2; break;
+    case QB_T_UP:
+        src = L.wgu.as<uint8_t>() + m->sh; sc = L.sgu.as<float>() + 1; rows = ff; stride = 2 * m->sh; sstride = 2;
+        break;
     case QB_T_DOWN: src = L.down.w.as<uint8_t>(); sc = L.down.scales.as<float>(); rows = h; cols = ff; stride = m->sff; break;
     case QB_T_O: rows = h; sc = L.so.as<float>(); break;
     default: return QB_INVALID_PARAMETERS;
@@ -825,7 +832,7 @@ uint32_t qb_model_read_int8(uint64_t model, int64_t layer, uint32_t tensor, int8
         QB_CUDA(cudaGetLastError());
         QB_CUDA(cudaMemcpy(values, tmp.p, rows * cols, cudaMemcpyDeviceToHost));
     }
-    QB_CUDA(cudaMemcpy(scales, sc, rows * 4, cudaMemcpyDeviceToHost));
+    QB_CUDA(cudaMemcpy2D(scales, 4, sc, sstride * 4, 4, rows, cudaMemcpyDeviceToHost));
     return QB_OK;
 }
 
