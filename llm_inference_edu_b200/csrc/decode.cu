@@ -70,36 +70,57 @@ __device__ __forceinline__ int xq(int e, int C) {
     return ((k >> 2) * C + c) * 4 + (k & 3);
 }
 
+// Packed FP32 pairs (Blackwell f32x2 pipe): two FMAs or adds per
+// instruction, each lane rounded exactly like fmaf / __fadd_rn.
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+        "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return d;
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+        "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+
 // Dot product of one 16-byte weight chunk with its EPC activations (the
-// chunk's quads x[0..EPC/4)), one FMA chain in element order.
+// chunk's quads x[0..EPC/4)), accumulated into the pair `acc` (even and odd
+// elements in its two lanes; the caller adds the lanes at the end).  INT8
+// bytes become exact floats by a byte permute into 2^23 + u and one packed
+// subtract of 2^23 + 128.
 template <int WF>
-__device__ __forceinline__ float chunk_dot(const uint4 &w, const float4 *x) {
-    float a = 0.0f;
+__device__ __forceinline__ void chunk_dot2(const uint4 &w, const float4 *x, float2 &acc) {
     if (WF == WF_F32) {
-        a = fmaf(x[0].x, __uint_as_float(w.x), a);
-        a = fmaf(x[0].y, __uint_as_float(w.y), a);
-        a = fmaf(x[0].z, __uint_as_float(w.z), a);
-        a = fmaf(x[0].w, __uint_as_float(w.w), a);
+        acc = ffma2(make_float2(x[0].x, x[0].y), make_float2(__uint_as_float(w.x), __uint_as_float(w.y)), acc);
+        acc = ffma2(make_float2(x[0].z, x[0].w), make_float2(__uint_as_float(w.z), __uint_as_float(w.w)), acc);
     } else if (WF == WF_BF16) {
-        a = fmaf(x[0].x, bf16_lo(w.x), a);
-        a = fmaf(x[0].y, bf16_hi(w.x), a);
-        a = fmaf(x[0].z, bf16_lo(w.y), a);
-        a = fmaf(x[0].w, bf16_hi(w.y), a);
-        a = fmaf(x[1].x, bf16_lo(w.z), a);
-        a = fmaf(x[1].y, bf16_hi(w.z), a);
-        a = fmaf(x[1].z, bf16_lo(w.w), a);
-        a = fmaf(x[1].w, bf16_hi(w.w), a);
+        acc = ffma2(make_float2(x[0].x, x[0].y), make_float2(bf16_lo(w.x), bf16_hi(w.x)), acc);
+        acc = ffma2(make_float2(x[0].z, x[0].w), make_float2(bf16_lo(w.y), bf16_hi(w.y)), acc);
+        acc = ffma2(make_float2(x[1].x, x[1].y), make_float2(bf16_lo(w.z), bf16_hi(w.z)), acc);
+        acc = ffma2(make_float2(x[1].z, x[1].w), make_float2(bf16_lo(w.w), bf16_hi(w.w)), acc);
     } else {
         const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+        const float2 bias = make_float2(-8388736.0f, -8388736.0f);  // -(2^23 + 128)
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-            a = fmaf(x[k].x, u8b_to_f32(ws[k], 0), a);
-            a = fmaf(x[k].y, u8b_to_f32(ws[k], 1), a);
-            a = fmaf(x[k].z, u8b_to_f32(ws[k], 2), a);
-            a = fmaf(x[k].w, u8b_to_f32(ws[k], 3), a);
+            const float2 q01 = fadd2(make_float2(__uint_as_float(__byte_perm(ws[k], 0x4B000000u, 0x7650)),
+                                                 __uint_as_float(__byte_perm(ws[k], 0x4B000000u, 0x7651))),
+                                     bias);
+            const float2 q23 = fadd2(make_float2(__uint_as_float(__byte_perm(ws[k], 0x4B000000u, 0x7652)),
+                                                 __uint_as_float(__byte_perm(ws[k], 0x4B000000u, 0x7653))),
+                                     bias);
+            acc = ffma2(make_float2(x[k].x, x[k].y), q01, acc);
+            acc = ffma2(make_float2(x[k].z, x[k].w), q23, acc);
         }
     }
-    return a;
 }
 
 __device__ __forceinline__ float warp_sum(float v) {
@@ -115,28 +136,61 @@ __device__ __forceinline__ float warp_max(float v) {
 
 // Scaled RMSNorm (src/ops.rs:137-149) of `in` (shared, width w) into the
 // quad-major layout for EPC/C, zero-padded to C * EPC.  Every warp computes
-// the row scale and the sum of squares itself, in the same order, so no
-// cross-warp reduction is needed; the scale is an exact maximum.
+// the row scale s (an exact maximum) and the sum of squares of x/s itself,
+// in the same order, so no cross-warp reduction is needed; x/s is taken as
+// x times the one reciprocal 1/s (within an ulp of the division).
 template <int EPC>
 __device__ __forceinline__ void warp_rmsnorm(const float *in, const float *gain, float *xs, int w, int C,
                                              float eps) {
     const int t = threadIdx.x, lane = t & 31;
     const float se = sqrtf(eps);
-    float m = se;
+    float m = se, ss = 0.0f, r;
+    if ((w & 3) == 0) {
+        const float4 *in4 = reinterpret_cast<const float4 *>(in);
 #pragma unroll 4
-    for (int i = lane; i < w; i += 32) m = rust_max(m, fabsf(in[i]));
-    m = warp_max(m);
-    float ss = 0.0f;
+        for (int i = lane; i < w / 4; i += 32) {
+            const float4 v = in4[i];
+            m = rust_max(rust_max(m, fabsf(v.x)), rust_max(fabsf(v.y), rust_max(fabsf(v.z), fabsf(v.w))));
+        }
+        m = warp_max(m);
+        r = 1.0f / m;
 #pragma unroll 4
-    for (int i = lane; i < w; i += 32) {
-        const float v = in[i] / m;
-        ss = ss + v * v;
+        for (int i = lane; i < w / 4; i += 32) {
+            const float4 v = in4[i];
+            const float a = v.x * r, b = v.y * r, c = v.z * r, d = v.w * r;
+            ss = ss + a * a + b * b + c * c + d * d;
+        }
+    } else {
+#pragma unroll 4
+        for (int i = lane; i < w; i += 32) m = rust_max(m, fabsf(in[i]));
+        m = warp_max(m);
+        r = 1.0f / m;
+#pragma unroll 4
+        for (int i = lane; i < w; i += 32) {
+            const float v = in[i] * r;
+            ss = ss + v * v;
+        }
     }
     ss = warp_sum(ss);
-    const float seps = se / m;
-    const float den = sqrtf(ss / (float)w + seps * seps);
+    const float seps = se * r;
+    const float rd = 1.0f / sqrtf(ss / (float)w + seps * seps);
     const int padded = C * EPC;
-    for (int i = t; i < padded; i += NT) xs[xq<EPC>(i, C)] = i < w ? (in[i] / m) / den * gain[i] : 0.0f;
+    if ((w & 3) == 0) {
+        // Four consecutive elements are one quad of the layout.
+        float4 *x4 = reinterpret_cast<float4 *>(xs);
+        for (int e = 4 * t; e < padded; e += 4 * NT) {
+            float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (e < w) {
+                o.x = in[e] * r * rd * gain[e];
+                o.y = in[e + 1] * r * rd * gain[e + 1];
+                o.z = in[e + 2] * r * rd * gain[e + 2];
+                o.w = in[e + 3] * r * rd * gain[e + 3];
+            }
+            x4[((e % EPC) >> 2) * C + e / EPC] = o;
+        }
+    } else {
+        for (int i = t; i < padded; i += NT) xs[xq<EPC>(i, C)] = i < w ? in[i] * r * rd * gain[i] : 0.0f;
+    }
     csync();
 }
 
@@ -144,22 +198,17 @@ __device__ __forceinline__ void flag_nonfinite(DecodeCtrl *ctrl, float v) {
     if (!isfinite(v)) atomicOr(&ctrl->error, ERR_NONFINITE);
 }
 
-// dst[i] = src[i], i < n, with B loads in flight per thread (L2-coherent
-// loads: src was written earlier in this step by other CTAs).
-template <int B>
+// dst[i] = src[i], i < n (L2-coherent loads: src was written earlier in
+// this step by other CTAs), 16 bytes per load when n % 4 == 0.
 __device__ __forceinline__ void stage_l2(float *dst, const float *src, int n) {
-    for (int base = threadIdx.x; base < n; base += B * NT) {
-        float v[B];
-#pragma unroll
-        for (int k = 0; k < B; ++k) {
-            const int i = base + k * NT;
-            v[k] = i < n ? ldcg(src + i) : 0.0f;
-        }
-#pragma unroll
-        for (int k = 0; k < B; ++k) {
-            const int i = base + k * NT;
-            if (i < n) dst[i] = v[k];
-        }
+    if ((n & 3) == 0) {
+        const float4 *s4 = reinterpret_cast<const float4 *>(src);
+        float4 *d4 = reinterpret_cast<float4 *>(dst);
+#pragma unroll 2
+        for (int i = threadIdx.x; i < n / 4; i += NT) d4[i] = __ldcg(s4 + i);
+    } else {
+#pragma unroll 2
+        for (int i = threadIdx.x; i < n; i += NT) dst[i] = ldcg(src + i);
     }
 }
 
@@ -360,7 +409,9 @@ __device__ __forceinline__ void team_gemv(const DecodeParams &p, const Ring &rg,
     for (int r0 = 0; r0 < n;) {
         const int rows = min(g.wave * g.rpc, n - r0);
         const int ns = (rows + g.rpc - 1) / g.rpc;
-        {
+        // One lane per warp observes the copies' completion (acquire);
+        // __syncwarp orders the rest of the warp's reads after it.
+        if (lane == 0) {
             Cursor c = cur;
 #pragma unroll 1
             for (int j = 0; j < ns; ++j) {
@@ -368,32 +419,34 @@ __device__ __forceinline__ void team_gemv(const DecodeParams &p, const Ring &rg,
                 c.advance(rg.nslot);
             }
         }
+        __syncwarp();
         const int nu = rows / U;
 #pragma unroll 1
         for (int ub = 0; ub < nu; ub += T) {
             if (ub + warp_team0 >= nu) break;  // warp-uniform
             const int u = ub + tm;
             const bool act = u < nu;
-            float a0 = 0.0f, a1 = 0.0f;
+            float2 p0 = make_float2(0.0f, 0.0f), p1 = make_float2(0.0f, 0.0f);
             if (act) {
                 const int row = u * U;
                 const int j = row / g.rpc;
                 int s = cur.slot + j;
                 if (s >= rg.nslot) s -= rg.nslot;
                 const uint8_t *w0 = rg.slots + (size_t)s * rg.slot_bytes + (size_t)(row - j * g.rpc) * g.stride;
-#pragma unroll 2
+#pragma unroll 1
                 for (int c = lt; c < C; c += G) {
                     float4 x[Q];
 #pragma unroll
                     for (int q = 0; q < Q; ++q) x[q] = x4[q * C + c];
                     const uint4 w = *reinterpret_cast<const uint4 *>(w0 + (size_t)c * 16);
-                    a0 += chunk_dot<WF>(w, x);
+                    chunk_dot2<WF>(w, x, p0);
                     if (U == 2) {
                         const uint4 w1 = *reinterpret_cast<const uint4 *>(w0 + g.stride + (size_t)c * 16);
-                        a1 += chunk_dot<WF>(w1, x);
+                        chunk_dot2<WF>(w1, x, p1);
                     }
                 }
             }
+            float a0 = p0.x + p0.y, a1 = p1.x + p1.y;
 #pragma unroll 1
             for (int off = G >> 1; off; off >>= 1) {
                 a0 += __shfl_xor_sync(FULL, a0, off);
@@ -484,6 +537,35 @@ __device__ __forceinline__ float resid_in(const DecodeParams &p, int l, int toke
 __device__ __forceinline__ void stage_after_attention(const DecodeParams &p, int l, int token, float *h2) {
     constexpr int HB = 16;
     const size_t stride = (size_t)p.h;
+    if ((p.h & 3) == 0 && (l > 0 || p.tfmt == WF_F32)) {
+        // 16-byte loads: four consecutive elements per thread.
+        const int n4 = p.h >> 2;
+        const float4 *part4 = reinterpret_cast<const float4 *>(p.part);
+        const float4 *res4 = reinterpret_cast<const float4 *>(l > 0 ? p.hidden : (const float *)(p.emb + (size_t)token * p.semb));
+        float4 *h4 = reinterpret_cast<float4 *>(h2);
+#pragma unroll 1
+        for (int i = threadIdx.x; i < n4; i += NT) {
+            const float4 r = l > 0 ? __ldcg(res4 + i) : __ldg(res4 + i);
+            float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            constexpr int HB4 = 8;
+#pragma unroll 1
+            for (int h0 = 0; h0 < p.qh; h0 += HB4) {
+                float4 v[HB4];
+#pragma unroll
+                for (int k = 0; k < HB4; ++k)
+                    if (h0 + k < p.qh) v[k] = __ldcg(part4 + (size_t)(h0 + k) * (stride >> 2) + i);
+#pragma unroll
+                for (int k = 0; k < HB4; ++k) {
+                    if (h0 + k < p.qh) {
+                        if (h0 + k == 0) o = v[k];
+                        else { o.x = o.x + v[k].x; o.y = o.y + v[k].y; o.z = o.z + v[k].z; o.w = o.w + v[k].w; }
+                    }
+                }
+            }
+            h4[i] = make_float4(r.x + o.x, r.y + o.y, r.z + o.z, r.w + o.w);
+        }
+        return;
+    }
 #pragma unroll 2
     for (int i = threadIdx.x; i < p.h; i += NT) {
         const float r = resid_in(p, l, token, i);
@@ -572,29 +654,35 @@ __device__ __forceinline__ void attention_context(const DecodeParams &p, const D
             }
         }
     }
-    // Scores: one position per thread, its key row read as 16-byte chunks
-    // (eight in flight), the dot product by increasing index.
+    // Scores.  TP = max(1, chunks / 4) adjacent lanes share a position: each
+    // loads up to four 16-byte chunks of the key row (all in flight at
+    // once) and sums its part in index order; the parts meet by shuffles.
     const int row_bytes = hd * (int)esz;
     const int nc = row_bytes >> 4;
-    const bool vec = (row_bytes & 15) == 0;
+    const bool vec = (row_bytes & 15) == 0 && nc <= 128 && (nc & (nc - 1)) == 0;
     constexpr int KEPC = KVBF16 ? 8 : 4;  // cache elements per 16-byte chunk
+    const int tpl = vec && nc > 4 ? 31 - __clz(nc >> 2) : 0;
+    const int TP = 1 << tpl, sub = t & (TP - 1), PPP = NT >> tpl;
     float mt = -INFINITY;
 #pragma unroll 1
-    for (int q = t; q <= pos; q += NT) {
+    for (int qb = 0; qb <= pos; qb += PPP) {
+        const int q = qb + (t >> tpl);
         float s = 0.0f;
         if (q == pos) {
+            if (sub == 0) {
 #pragma unroll 4
-            for (int i = 0; i < hd; ++i) s = s + qs[i] * ks[i];
-        } else if (vec) {
-            const uint8_t *row = K + (size_t)q * row_bytes;
-#pragma unroll 1
-            for (int c0 = 0; c0 < nc; c0 += 8) {
-                uint4 kc[8];
+                for (int i = 0; i < hd; ++i) s = s + qs[i] * ks[i];
+            }
+        } else if (q < pos) {
+            if (vec) {
+                const uint8_t *row = K + (size_t)q * row_bytes;
+                const int c0 = sub * 4;
+                uint4 kc[4];
 #pragma unroll
-                for (int c = 0; c < 8; ++c)
+                for (int c = 0; c < 4; ++c)
                     if (c0 + c < nc) kc[c] = __ldcg((const uint4 *)(row + (size_t)(c0 + c) * 16));
 #pragma unroll
-                for (int c = 0; c < 8; ++c) {
+                for (int c = 0; c < 4; ++c) {
                     if (c0 + c < nc) {
                         const uint32_t w4[4] = {kc[c].x, kc[c].y, kc[c].z, kc[c].w};
                         const float *qq = qs + (c0 + c) * KEPC;
@@ -606,14 +694,18 @@ __device__ __forceinline__ void attention_context(const DecodeParams &p, const D
                         }
                     }
                 }
-            }
-        } else {
+            } else {
 #pragma unroll 1
-            for (int i = 0; i < hd; ++i) s = s + qs[i] * kv_load<KVBF16>(K, (size_t)q * hd + i);
+                for (int i = 0; i < hd; ++i) s = s + qs[i] * kv_load<KVBF16>(K, (size_t)q * hd + i);
+            }
         }
-        s = s / p.sqrt_hd;
-        sc[q] = s;
-        mt = rust_max(mt, s);
+#pragma unroll 1
+        for (int off = TP >> 1; off; off >>= 1) s += __shfl_xor_sync(FULL, s, off);
+        if (sub == 0 && q <= pos) {
+            s = s / p.sqrt_hd;
+            sc[q] = s;
+            mt = rust_max(mt, s);
+        }
     }
     // Softmax: maximum and sum each meet through one shared array of warp
     // partials, read in warp order by every thread.
@@ -733,7 +825,7 @@ __device__ __forceinline__ void run_qkv(const DecodeParams &p, const CtaGeom &cg
     float *xs = sm + p.sm_xs, *h2 = sm + p.sm_h2;
     const float *gain = sm + p.sm_gain, *rv = sm + p.sm_rv;
     if (l > 0) {
-        stage_l2<2>(h2, p.hidden, p.h);
+        stage_l2(h2, p.hidden, p.h);
     } else {
 #pragma unroll 2
         for (int i = threadIdx.x; i < p.h; i += NT) h2[i] = resid_in(p, 0, token, i);
@@ -825,7 +917,26 @@ __device__ __forceinline__ void run_down(const DecodeParams &p, const CtaGeom &c
     constexpr int B = 16;
     float *xs = sm + p.sm_xs;
     const int padded = p.cff * EPC;
-    // act -> xs (quad-major, zero-padded), B loads in flight per thread.
+    if ((p.ff & 3) == 0) {
+        // act -> xs: four consecutive elements are one quad of the layout.
+        const float4 *a4 = reinterpret_cast<const float4 *>(p.act);
+        float4 *x4 = reinterpret_cast<float4 *>(xs);
+        constexpr int B4 = 4;
+#pragma unroll 1
+        for (int base = threadIdx.x; base < padded / 4; base += B4 * NT) {
+            float4 v[B4];
+#pragma unroll
+            for (int k = 0; k < B4; ++k) {
+                const int e = 4 * (base + k * NT);
+                v[k] = e < p.ff ? __ldcg(a4 + (e >> 2)) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            }
+#pragma unroll
+            for (int k = 0; k < B4; ++k) {
+                const int e = 4 * (base + k * NT);
+                if (e < padded) x4[((e % EPC) >> 2) * p.cff + e / EPC] = v[k];
+            }
+        }
+    } else
 #pragma unroll 1
     for (int base = threadIdx.x; base < padded; base += B * NT) {
         float v[B];
@@ -868,7 +979,7 @@ __device__ __forceinline__ void run_lm_head(const DecodeParams &p, const CtaGeom
     const float *gain = sm + p.sm_gain;
     float *rowv = sm + p.sm_sc;
     DecodeCtrl *ctrl = p.ctrl;
-    stage_l2<2>(h2, p.hidden, p.h);
+    stage_l2(h2, p.hidden, p.h);
     csync();
     warp_rmsnorm<TEPC>(h2, gain, xs, p.h, p.cemb, p.eps);
     team_gemv<TF, 1>(p, rg, cur, p.kind[K_LM], cg.lm_n, xs, s_abort,
@@ -938,7 +1049,12 @@ __global__ void __maxnreg__(128) decode_kernel(const __grid_constant__ DecodePar
     const int token = *(volatile int *)&ctrl->token;
     const int pos = *(volatile int *)&ctrl->pos;
     const int NB = 4 * p.L;
-    const CtaGeom &cg = p.geom[b];
+    // This CTA's row ranges live in shared memory for the whole step (a
+    // global copy would be re-read from L2 on the critical path).
+    __shared__ CtaGeom s_cg;
+    const CtaGeom &cg = s_cg;
+    if (threadIdx.x < (int)(sizeof(CtaGeom) / 4))
+        ((int *)&s_cg)[threadIdx.x] = ((const int *)(p.geom + b))[threadIdx.x];
     if (p.trace && b == 0 && threadIdx.x == 0) p.trace[(size_t)NB * G + NB] = globaltimer_ns();
     // The layer table lives in shared memory for the whole step.
     DecodeLayer *lay = (DecodeLayer *)(sm + p.sm_lay);

@@ -442,7 +442,10 @@ static uint32_t session_build(Session &s) {
         g.U = k == K_GU ? 2 : 1;
         g.rpc = std::max(g.U, (p.slot_bytes / g.stride) / g.U * g.U);
         const int block_slots = std::max(1, (rows_max[k] + g.rpc - 1) / g.rpc);
-        g.wave = std::max(1, std::min(block_slots, nslot / 2));
+        // A per-layer block is consumed in one wave (its weights are already
+        // resident); a longer stream (the LM head) in waves of two slots, so
+        // the rest of the ring keeps copies in flight.
+        g.wave = block_slots <= nslot / 2 ? block_slots : std::max(1, std::min(2, nslot / 2));
         const int units = std::max(1, std::min(rows_max[k], g.wave * g.rpc) / g.U);
         long long best = -1;
         for (int lg = 0; lg <= 5; ++lg) {
