@@ -67,6 +67,14 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
     return t;
 }
 
+// Relaxed GPU-scope 64-bit load for polling a word another CTA writes (a
+// volatile asm, so repeated polls are never merged or hoisted).
+__device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p));
+    return v;
+}
+
 // Streaming 16-byte load that bypasses L1 allocation (weights are read once).
 __device__ __forceinline__ uint4 ld_stream_u4(const void *p) {
     uint4 v;
@@ -120,6 +128,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
         : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// As mbar_try_wait, but the thread may be suspended in hardware for up to
+// `suspend_ns` while the phase is incomplete (no issue slots are spent
+// polling).
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t *bar, uint32_t parity, uint32_t suspend_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity), "r"(suspend_ns)
         : "memory");
     return ok != 0;
 }

@@ -92,20 +92,20 @@ __device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
 }
 
 // Dot product of one 16-byte weight chunk with its EPC activations (the
-// chunk's quads x[0..EPC/4)), accumulated into the pair `acc` (even and odd
-// elements in its two lanes; the caller adds the lanes at the end).  INT8
+// chunk's quads x[0..EPC/4)), accumulated into two pairs of partial sums
+// (four independent FMA chains; the caller adds them at the end).  INT8
 // bytes become exact floats by a byte permute into 2^23 + u and one packed
 // subtract of 2^23 + 128.
 template <int WF>
-__device__ __forceinline__ void chunk_dot2(const uint4 &w, const float4 *x, float2 &acc) {
+__device__ __forceinline__ void chunk_dot2(const uint4 &w, const float4 *x, float2 &acc, float2 &acc2) {
     if (WF == WF_F32) {
         acc = ffma2(make_float2(x[0].x, x[0].y), make_float2(__uint_as_float(w.x), __uint_as_float(w.y)), acc);
-        acc = ffma2(make_float2(x[0].z, x[0].w), make_float2(__uint_as_float(w.z), __uint_as_float(w.w)), acc);
+        acc2 = ffma2(make_float2(x[0].z, x[0].w), make_float2(__uint_as_float(w.z), __uint_as_float(w.w)), acc2);
     } else if (WF == WF_BF16) {
         acc = ffma2(make_float2(x[0].x, x[0].y), make_float2(bf16_lo(w.x), bf16_hi(w.x)), acc);
-        acc = ffma2(make_float2(x[0].z, x[0].w), make_float2(bf16_lo(w.y), bf16_hi(w.y)), acc);
+        acc2 = ffma2(make_float2(x[0].z, x[0].w), make_float2(bf16_lo(w.y), bf16_hi(w.y)), acc2);
         acc = ffma2(make_float2(x[1].x, x[1].y), make_float2(bf16_lo(w.z), bf16_hi(w.z)), acc);
-        acc = ffma2(make_float2(x[1].z, x[1].w), make_float2(bf16_lo(w.w), bf16_hi(w.w)), acc);
+        acc2 = ffma2(make_float2(x[1].z, x[1].w), make_float2(bf16_lo(w.w), bf16_hi(w.w)), acc2);
     } else {
         const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
         const float2 bias = make_float2(-8388736.0f, -8388736.0f);  // -(2^23 + 128)
@@ -118,7 +118,7 @@ __device__ __forceinline__ void chunk_dot2(const uint4 &w, const float4 *x, floa
                                                  __uint_as_float(__byte_perm(ws[k], 0x4B000000u, 0x7653))),
                                      bias);
             acc = ffma2(make_float2(x[k].x, x[k].y), q01, acc);
-            acc = ffma2(make_float2(x[k].z, x[k].w), q23, acc);
+            acc2 = ffma2(make_float2(x[k].z, x[k].w), q23, acc2);
         }
     }
 }
@@ -290,11 +290,28 @@ struct Producer {
 
     __device__ Producer(const DecodeParams &pp, const Ring &r, volatile int *a) : p(pp), rg(r), s_abort(a) {}
 
+    // Bounded wait for a free slot.  The producer is usually far ahead of
+    // the compute warps, so it waits suspended in hardware (not spinning,
+    // which would take issue slots from the compute warps of its SM
+    // sub-partition).
+    __device__ bool wait_free(int s, uint32_t parity) {
+        const uint64_t t0 = globaltimer_ns();
+#pragma unroll 1
+        while (!mbar_try_wait_suspend(rg.empty + s, parity, 20000u)) {
+            if (*s_abort || globaltimer_ns() - t0 > p.timeout_ns) {
+                atomicOr(&p.ctrl->error, ERR_TIMEOUT);
+                *s_abort = 1;
+                return false;
+            }
+        }
+        return true;
+    }
+
     // Streams rows [0, n) of a block (stride bytes each) in ring chunks.
     __device__ void block(const uint8_t *base, int n, const KindGeom &g) {
 #pragma unroll 1
         for (int r = 0; r < n && alive; r += g.rpc) {
-            if (round > 0 && !mbar_wait(p, rg.empty + slot, (uint32_t)((round - 1) & 1), s_abort)) {
+            if (round > 0 && !wait_free(slot, (uint32_t)((round - 1) & 1))) {
                 alive = false;
                 return;
             }
@@ -385,30 +402,22 @@ __device__ void produce(const DecodeParams &p, const DecodeLayer *lay, const Cta
 }
 
 // ------------------------------------------------------------ gemv ----
-//
-// y_r = dot(W_r, x) for the n rows of one streamed block.  The block is
-// consumed in waves of up to g.wave ring slots: every thread waits for the
-// wave's slots, then teams of G threads take units of U rows round-robin;
-// a team's threads stride the row's chunks (c = lane-in-team + G * i),
-// accumulate in FP32 and meet in a shuffle butterfly, and the team's first
-// thread hands the U results to `epi(row, a0, a1)`.  Each warp frees the
-// wave's slots as soon as it is done with them.  A failed wait (timeout)
-// leaves the abort flag set; the caller tests it after its next CTA barrier.
 
-template <int WF, int U, class Epi>
-__device__ __forceinline__ void team_gemv(const DecodeParams &p, const Ring &rg, Cursor &cur, const KindGeom &g,
-                                          int n, const float *xs, volatile int *s_abort, Epi &&epi) {
+// team_gemv (below) with the team size G = 2^LG fixed at compile time.
+template <int WF, int U, int LG, class Epi>
+__device__ __forceinline__ void team_gemv_g(const DecodeParams &p, const Ring &rg, Cursor &cur, const KindGeom &g,
+                                            int n, const float *xs, volatile int *s_abort, Epi &epi) {
     constexpr int Q = Fmt<WF>::EPC / 4;
+    constexpr int G = 1 << LG, T = NT >> LG;
     const int t = threadIdx.x, lane = t & 31;
-    const int lgG = g.lgG, G = 1 << lgG;
-    const int lt = t & (G - 1), tm = t >> lgG, T = NT >> lgG;
-    const int warp_team0 = (t & ~31) >> lgG;
+    const int lt = t & (G - 1), tm = t >> LG;
+    const int warp_team0 = (t & ~31) >> LG;
     const int C = g.C;
     const float4 *x4 = reinterpret_cast<const float4 *>(xs);
 #pragma unroll 1
     for (int r0 = 0; r0 < n;) {
         const int rows = min(g.wave * g.rpc, n - r0);
-        const int ns = (rows + g.rpc - 1) / g.rpc;
+        const int ns = g.rpc == 1 ? rows : (int)__umulhi((unsigned)(rows + g.rpc - 1), g.rpc_magic);
         // One lane per warp observes the copies' completion (acquire);
         // __syncwarp orders the rest of the warp's reads after it.
         if (lane == 0) {
@@ -426,33 +435,53 @@ __device__ __forceinline__ void team_gemv(const DecodeParams &p, const Ring &rg,
             if (ub + warp_team0 >= nu) break;  // warp-uniform
             const int u = ub + tm;
             const bool act = u < nu;
-            float2 p0 = make_float2(0.0f, 0.0f), p1 = make_float2(0.0f, 0.0f);
+            // Four independent partial-sum chains per row: two per chunk,
+            // and alternate chunks in alternate pairs.
+            float2 a0 = make_float2(0.0f, 0.0f), b0 = a0, c0 = a0, d0 = a0;
+            float2 a1 = a0, b1 = a0, c1 = a0, d1 = a0;
             if (act) {
                 const int row = u * U;
-                const int j = row / g.rpc;
+                const int j = g.rpc == 1 ? row : (int)__umulhi((unsigned)row, g.rpc_magic);
                 int s = cur.slot + j;
                 if (s >= rg.nslot) s -= rg.nslot;
                 const uint8_t *w0 = rg.slots + (size_t)s * rg.slot_bytes + (size_t)(row - j * g.rpc) * g.stride;
+                int c = lt;
 #pragma unroll 1
-                for (int c = lt; c < C; c += G) {
+                for (; c + G < C; c += 2 * G) {
+                    float4 x[Q], y[Q];
+#pragma unroll
+                    for (int q = 0; q < Q; ++q) { x[q] = x4[q * C + c]; y[q] = x4[q * C + c + G]; }
+                    const uint4 w = *reinterpret_cast<const uint4 *>(w0 + (size_t)c * 16);
+                    const uint4 v = *reinterpret_cast<const uint4 *>(w0 + (size_t)(c + G) * 16);
+                    chunk_dot2<WF>(w, x, a0, b0);
+                    chunk_dot2<WF>(v, y, c0, d0);
+                    if (U == 2) {
+                        const uint4 w1 = *reinterpret_cast<const uint4 *>(w0 + g.stride + (size_t)c * 16);
+                        const uint4 v1 = *reinterpret_cast<const uint4 *>(w0 + g.stride + (size_t)(c + G) * 16);
+                        chunk_dot2<WF>(w1, x, a1, b1);
+                        chunk_dot2<WF>(v1, y, c1, d1);
+                    }
+                }
+                if (c < C) {
                     float4 x[Q];
 #pragma unroll
                     for (int q = 0; q < Q; ++q) x[q] = x4[q * C + c];
                     const uint4 w = *reinterpret_cast<const uint4 *>(w0 + (size_t)c * 16);
-                    chunk_dot2<WF>(w, x, p0);
+                    chunk_dot2<WF>(w, x, a0, b0);
                     if (U == 2) {
                         const uint4 w1 = *reinterpret_cast<const uint4 *>(w0 + g.stride + (size_t)c * 16);
-                        chunk_dot2<WF>(w1, x, p1);
+                        chunk_dot2<WF>(w1, x, a1, b1);
                     }
                 }
             }
-            float a0 = p0.x + p0.y, a1 = p1.x + p1.y;
-#pragma unroll 1
+            float s0 = ((a0.x + a0.y) + (b0.x + b0.y)) + ((c0.x + c0.y) + (d0.x + d0.y));
+            float s1 = ((a1.x + a1.y) + (b1.x + b1.y)) + ((c1.x + c1.y) + (d1.x + d1.y));
+#pragma unroll
             for (int off = G >> 1; off; off >>= 1) {
-                a0 += __shfl_xor_sync(FULL, a0, off);
-                if (U == 2) a1 += __shfl_xor_sync(FULL, a1, off);
+                s0 += __shfl_xor_sync(FULL, s0, off);
+                if (U == 2) s1 += __shfl_xor_sync(FULL, s1, off);
             }
-            if (act && lt == 0) epi(r0 + u * U, a0, a1);
+            if (act && lt == 0) epi(r0 + u * U, s0, s1);
         }
         __syncwarp();
         if (lane == 0) {
@@ -464,18 +493,43 @@ __device__ __forceinline__ void team_gemv(const DecodeParams &p, const Ring &rg,
                 c.advance(rg.nslot);
             }
         }
-#pragma unroll 1
-        for (int j = 0; j < ns; ++j) cur.advance(rg.nslot);
+        cur.slot += ns;
+        if (cur.slot >= rg.nslot) { cur.slot -= rg.nslot; ++cur.round; }
         r0 += rows;
     }
+}
+
+// y_r = dot(W_r, x) for the n rows of one streamed block.  The block is
+// consumed in waves of up to g.wave ring slots: every warp waits for the
+// wave's slots, then teams of G = 2^g.lgG threads take units of U rows
+// round-robin; a team's threads stride the row's chunks, accumulate in FP32
+// and meet in a shuffle butterfly, and the team's first thread hands the U
+// results to `epi(row, y0, y1)`.  Each warp frees the wave's slots as soon
+// as it is done with them.  A failed wait (timeout) leaves the abort flag
+// set; the caller tests it after its next CTA barrier.
+// Team sizes are restricted to G in {4, 8, 32} (the LM head: {8, 16, 32})
+// to bound the kernel's code size; the host picks among them.
+template <int WF, int U, class Epi>
+__device__ __forceinline__ void team_gemv(const DecodeParams &p, const Ring &rg, Cursor &cur, const KindGeom &g,
+                                          int n, const float *xs, volatile int *s_abort, Epi &&epi) {
+    if (g.lgG == 2) team_gemv_g<WF, U, 2>(p, rg, cur, g, n, xs, s_abort, epi);
+    else if (g.lgG == 3) team_gemv_g<WF, U, 3>(p, rg, cur, g, n, xs, s_abort, epi);
+    else team_gemv_g<WF, U, 5>(p, rg, cur, g, n, xs, s_abort, epi);
+}
+template <int WF, class Epi>
+__device__ __forceinline__ void team_gemv_lm(const DecodeParams &p, const Ring &rg, Cursor &cur, const KindGeom &g,
+                                             int n, const float *xs, volatile int *s_abort, Epi &&epi) {
+    if (g.lgG == 3) team_gemv_g<WF, 1, 3>(p, rg, cur, g, n, xs, s_abort, epi);
+    else if (g.lgG == 4) team_gemv_g<WF, 1, 4>(p, rg, cur, g, n, xs, s_abort, epi);
+    else team_gemv_g<WF, 1, 5>(p, rg, cur, g, n, xs, s_abort, epi);
 }
 
 // ------------------------------------------------------------ barrier ----
 
 // Grid barrier in two halves (compute warps only).  barrier_arrive makes
 // the CTA's writes visible (csync, then thread 0's release reduction);
-// independent work can run before barrier_wait, which polls with relaxed
-// loads (bounded by the timeout) and ends with an acquire fence and csync.
+// independent work can run before barrier_wait, which polls with acquire
+// loads (bounded by the timeout) and ends with a csync.
 // barrier_wait returns false (uniformly, after recording ERR_TIMEOUT and
 // raising the abort flag) when the arrivals do not complete in time, when
 // another CTA has timed out, or when this CTA is already aborting.
@@ -493,11 +547,13 @@ __device__ __forceinline__ void barrier_arrive(const DecodeParams &p, unsigned t
 __device__ __forceinline__ bool barrier_wait(const DecodeParams &p, unsigned target, volatile int *s_abort) {
     DecodeCtrl *ctrl = p.ctrl;
     if (threadIdx.x == 0) {
-        volatile unsigned *bar = &ctrl->bar;
-        if (*bar < target) {
+        // Acquire loads: the one that sees the final count synchronizes with
+        // every CTA's release reduction, and the CTA barrier below carries
+        // that ordering to the other compute threads.
+        if (ld_acquire_u32(&ctrl->bar) < target) {
             const uint64_t t0 = globaltimer_ns();
             unsigned spins = 0;
-            while (*bar < target) {
+            while (ld_acquire_u32(&ctrl->bar) < target) {
                 if ((++spins & 63u) == 0) {
                     if ((*(volatile unsigned *)&ctrl->error & ERR_TIMEOUT) || globaltimer_ns() - t0 > p.timeout_ns) {
                         atomicOr(&ctrl->error, ERR_TIMEOUT);
@@ -507,7 +563,6 @@ __device__ __forceinline__ bool barrier_wait(const DecodeParams &p, unsigned tar
                 }
             }
         }
-        asm volatile("fence.acq_rel.gpu;" ::: "memory");
         if (p.trace && blockIdx.x == 0) {
             const int G = gridDim.x, idx = (int)(target / (unsigned)G) - 1;
             p.trace[(size_t)4 * p.L * G + idx] = globaltimer_ns();
@@ -537,32 +592,33 @@ __device__ __forceinline__ float resid_in(const DecodeParams &p, int l, int toke
 __device__ __forceinline__ void stage_after_attention(const DecodeParams &p, int l, int token, float *h2) {
     constexpr int HB = 16;
     const size_t stride = (size_t)p.h;
-    if ((p.h & 3) == 0 && (l > 0 || p.tfmt == WF_F32)) {
-        // 16-byte loads: four consecutive elements per thread.
-        const int n4 = p.h >> 2;
-        const float4 *part4 = reinterpret_cast<const float4 *>(p.part);
-        const float4 *res4 = reinterpret_cast<const float4 *>(l > 0 ? p.hidden : (const float *)(p.emb + (size_t)token * p.semb));
-        float4 *h4 = reinterpret_cast<float4 *>(h2);
+    if ((p.h & 1) == 0 && (l > 0 || p.tfmt == WF_F32) && p.h <= 2 * NT) {
+        // 8-byte loads: two consecutive elements per thread, every head's
+        // partial in flight at once (up to 16 heads per batch).
+        constexpr int HB2 = 16;
+        const int n2 = p.h >> 1;
+        const float2 *part2 = reinterpret_cast<const float2 *>(p.part);
+        const float2 *res2 = reinterpret_cast<const float2 *>(l > 0 ? p.hidden : (const float *)(p.emb + (size_t)token * p.semb));
+        float2 *h2v = reinterpret_cast<float2 *>(h2);
+        const int i = threadIdx.x;
+        if (i < n2) {
+            const float2 r = l > 0 ? __ldcg(res2 + i) : __ldg(res2 + i);
+            float2 o = make_float2(0.0f, 0.0f);
 #pragma unroll 1
-        for (int i = threadIdx.x; i < n4; i += NT) {
-            const float4 r = l > 0 ? __ldcg(res4 + i) : __ldg(res4 + i);
-            float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            constexpr int HB4 = 8;
-#pragma unroll 1
-            for (int h0 = 0; h0 < p.qh; h0 += HB4) {
-                float4 v[HB4];
+            for (int h0 = 0; h0 < p.qh; h0 += HB2) {
+                float2 v[HB2];
 #pragma unroll
-                for (int k = 0; k < HB4; ++k)
-                    if (h0 + k < p.qh) v[k] = __ldcg(part4 + (size_t)(h0 + k) * (stride >> 2) + i);
+                for (int k = 0; k < HB2; ++k)
+                    if (h0 + k < p.qh) v[k] = __ldcg(part2 + (size_t)(h0 + k) * (stride >> 1) + i);
 #pragma unroll
-                for (int k = 0; k < HB4; ++k) {
+                for (int k = 0; k < HB2; ++k) {
                     if (h0 + k < p.qh) {
                         if (h0 + k == 0) o = v[k];
-                        else { o.x = o.x + v[k].x; o.y = o.y + v[k].y; o.z = o.z + v[k].z; o.w = o.w + v[k].w; }
+                        else { o.x = o.x + v[k].x; o.y = o.y + v[k].y; }
                     }
                 }
             }
-            h4[i] = make_float4(r.x + o.x, r.y + o.y, r.z + o.z, r.w + o.w);
+            h2v[i] = make_float2(r.x + o.x, r.y + o.y);
         }
         return;
     }
@@ -982,7 +1038,7 @@ __device__ __forceinline__ void run_lm_head(const DecodeParams &p, const CtaGeom
     stage_l2(h2, p.hidden, p.h);
     csync();
     warp_rmsnorm<TEPC>(h2, gain, xs, p.h, p.cemb, p.eps);
-    team_gemv<TF, 1>(p, rg, cur, p.kind[K_LM], cg.lm_n, xs, s_abort,
+    team_gemv_lm<TF>(p, rg, cur, p.kind[K_LM], cg.lm_n, xs, s_abort,
                      [&](int r, float acc, float) { rowv[r] = acc; });
     csync();
     if (*s_abort) return;

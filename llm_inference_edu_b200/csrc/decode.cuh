@@ -54,6 +54,7 @@ struct KindGeom {
     int lgG;     // log2 of the threads per unit (0..5)
     int U;       // rows per unit
     int wave;    // ring slots waited for and released together (<= nslot / 2 or the block)
+    unsigned rpc_magic;  // ceil(2^32 / rpc) when rpc > 1: r / rpc == umulhi(r, rpc_magic) for r < 2^16
 };
 
 // The rows each CTA owns in every phase (host-computed, no division on the

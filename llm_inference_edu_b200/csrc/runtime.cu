@@ -431,8 +431,8 @@ static uint32_t session_build(Session &s) {
     p.nslot = nslot;
     p.sm_total = p.sm_ring + nslot * p.slot_bytes / 4;
     // Per-kind geometry of the streamed blocks.  The team size G = 2^lgG
-    // minimises the critical path ceil(units / (threads / G)) * ceil(C / G)
-    // chunk products, plus the butterfly's lgG steps.
+    // minimises the critical path: rounds of units times (chunk products per
+    // lane plus a fixed cost per round for the butterfly and epilogue).
     const size_t strides[NKIND] = {m.sh, m.shd, m.sh, m.sff, m.semb};
     const int rows_max[NKIND] = {max_qkv, max_att, 2 * max_gu, max_dn, max_lm};
     for (int k = 0; k < NKIND; ++k) {
@@ -441,17 +441,20 @@ static uint32_t session_build(Session &s) {
         g.C = (int)(strides[k] / 16);
         g.U = k == K_GU ? 2 : 1;
         g.rpc = std::max(g.U, (p.slot_bytes / g.stride) / g.U * g.U);
+        g.rpc_magic = g.rpc > 1 ? (unsigned)(((1ull << 32) + g.rpc - 1) / g.rpc) : 0u;  // rpc == 1 divides directly
         const int block_slots = std::max(1, (rows_max[k] + g.rpc - 1) / g.rpc);
         // A per-layer block is consumed in one wave (its weights are already
         // resident); a longer stream (the LM head) in waves of two slots, so
         // the rest of the ring keeps copies in flight.
         g.wave = block_slots <= nslot / 2 ? block_slots : std::max(1, std::min(2, nslot / 2));
         const int units = std::max(1, std::min(rows_max[k], g.wave * g.rpc) / g.U);
+        static const int lm_set[3] = {3, 4, 5}, set[3] = {2, 3, 5};  // the device's instantiated sizes
+        const int *cand = k == K_LM ? lm_set : set;
         long long best = -1;
-        for (int lg = 0; lg <= 5; ++lg) {
-            const int G = 1 << lg;
-            const long long cost = (long long)((units + (kDecodeThreads / G) - 1) / (kDecodeThreads / G)) *
-                                       ((g.C + G - 1) / G) * 4 * g.U + lg;
+        for (int ci = 0; ci < 3; ++ci) {
+            const int lg = cand[ci], G = 1 << lg, teams = kDecodeThreads / G;
+            const long long rounds = (units + teams - 1) / teams;
+            const long long cost = rounds * ((long long)((g.C + G - 1) / G) * 4 * g.U + 20 + 2 * lg);
             if (best < 0 || cost < best) { best = cost; g.lgG = lg; }
         }
     }
