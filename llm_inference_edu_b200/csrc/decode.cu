@@ -135,43 +135,44 @@ __device__ __forceinline__ float warp_max(float v) {
 }
 
 // Scaled RMSNorm (src/ops.rs:137-149) of `in` (shared, width w) into the
-// quad-major layout for EPC/C, zero-padded to C * EPC.  Every warp computes
-// the row scale s (an exact maximum) and the sum of squares of x/s itself,
-// in the same order, so no cross-warp reduction is needed; x/s is taken as
-// x times the one reciprocal 1/s (within an ulp of the division).
+// quad-major layout for EPC/C, zero-padded to C * EPC.  Each warp reduces
+// its slice to a pair (m_w = max |x|, s_w = sum (x / m_w)^2) and leaves it in
+// red[2w, 2w + 1]; after one CTA barrier every thread combines the pairs in
+// warp order: s = max(sqrt(eps), max m_w), sum (x/s)^2 = sum s_w (m_w/s)^2.
+// Scaling by reciprocals keeps the result within a few ulps of the
+// reference's divisions.
 template <int EPC>
-__device__ __forceinline__ void warp_rmsnorm(const float *in, const float *gain, float *xs, int w, int C,
-                                             float eps) {
-    const int t = threadIdx.x, lane = t & 31;
+__device__ __forceinline__ void block_rmsnorm(const float *in, const float *gain, float *xs, int w, int C,
+                                              float eps, float *red) {
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
     const float se = sqrtf(eps);
-    float m = se, ss = 0.0f, r;
-    if ((w & 3) == 0) {
-        const float4 *in4 = reinterpret_cast<const float4 *>(in);
-#pragma unroll 4
-        for (int i = lane; i < w / 4; i += 32) {
-            const float4 v = in4[i];
-            m = rust_max(rust_max(m, fabsf(v.x)), rust_max(fabsf(v.y), rust_max(fabsf(v.z), fabsf(v.w))));
-        }
-        m = warp_max(m);
-        r = 1.0f / m;
-#pragma unroll 4
-        for (int i = lane; i < w / 4; i += 32) {
-            const float4 v = in4[i];
-            const float a = v.x * r, b = v.y * r, c = v.z * r, d = v.w * r;
-            ss = ss + a * a + b * b + c * c + d * d;
-        }
-    } else {
-#pragma unroll 4
-        for (int i = lane; i < w; i += 32) m = rust_max(m, fabsf(in[i]));
-        m = warp_max(m);
-        r = 1.0f / m;
-#pragma unroll 4
-        for (int i = lane; i < w; i += 32) {
-            const float v = in[i] * r;
-            ss = ss + v * v;
-        }
+    float mw = se;
+#pragma unroll 2
+    for (int i = t; i < w; i += NT) mw = rust_max(mw, fabsf(in[i]));
+    mw = warp_max(mw);
+    const float rw = 1.0f / mw;
+    float sw = 0.0f;
+#pragma unroll 2
+    for (int i = t; i < w; i += NT) {
+        const float v = in[i] * rw;
+        sw = sw + v * v;
     }
-    ss = warp_sum(ss);
+    sw = warp_sum(sw);
+    if (lane == 0) {
+        red[2 * warp] = mw;
+        red[2 * warp + 1] = sw;
+    }
+    csync();
+    float m = red[0];
+#pragma unroll
+    for (int k = 1; k < NW; ++k) m = rust_max(m, red[2 * k]);
+    const float r = 1.0f / m;
+    float ss = 0.0f;
+#pragma unroll
+    for (int k = 0; k < NW; ++k) {
+        const float f = red[2 * k] * r;
+        ss = ss + red[2 * k + 1] * (f * f);
+    }
     const float seps = se * r;
     const float rd = 1.0f / sqrtf(ss / (float)w + seps * seps);
     const int padded = C * EPC;
@@ -418,18 +419,20 @@ __device__ __forceinline__ void team_gemv_g(const DecodeParams &p, const Ring &r
     for (int r0 = 0; r0 < n;) {
         const int rows = min(g.wave * g.rpc, n - r0);
         const int ns = g.rpc == 1 ? rows : (int)__umulhi((unsigned)(rows + g.rpc - 1), g.rpc_magic);
-        // One lane per warp observes the copies' completion (acquire);
-        // __syncwarp orders the rest of the warp's reads after it.
-        if (lane == 0) {
-            Cursor c = cur;
+        // Lane j of each warp observes the completion of the wave's j-th
+        // copy (acquire); __syncwarp orders the rest of the warp's reads
+        // after all of them.
 #pragma unroll 1
-            for (int j = 0; j < ns; ++j) {
-                mbar_wait(p, rg.full + c.slot, (uint32_t)(c.round & 1), s_abort);
-                c.advance(rg.nslot);
-            }
+        for (int j = lane; j < ns; j += 32) {
+            int s = cur.slot + j, rd = cur.round;
+            while (s >= rg.nslot) { s -= rg.nslot; ++rd; }
+            mbar_wait(p, rg.full + s, (uint32_t)(rd & 1), s_abort);
         }
         __syncwarp();
-        const int nu = rows / U;
+        // With U = 2 an odd block (the LM head) ends in a half unit: its second
+        // row is read from the wave's last slot (stale, in bounds) and its
+        // result is discarded by the epilogue.
+        const int nu = (rows + U - 1) / U;
 #pragma unroll 1
         for (int ub = 0; ub < nu; ub += T) {
             if (ub + warp_team0 >= nu) break;  // warp-uniform
@@ -519,9 +522,9 @@ __device__ __forceinline__ void team_gemv(const DecodeParams &p, const Ring &rg,
 template <int WF, class Epi>
 __device__ __forceinline__ void team_gemv_lm(const DecodeParams &p, const Ring &rg, Cursor &cur, const KindGeom &g,
                                              int n, const float *xs, volatile int *s_abort, Epi &&epi) {
-    if (g.lgG == 3) team_gemv_g<WF, 1, 3>(p, rg, cur, g, n, xs, s_abort, epi);
-    else if (g.lgG == 4) team_gemv_g<WF, 1, 4>(p, rg, cur, g, n, xs, s_abort, epi);
-    else team_gemv_g<WF, 1, 5>(p, rg, cur, g, n, xs, s_abort, epi);
+    if (g.lgG == 3) team_gemv_g<WF, 2, 3>(p, rg, cur, g, n, xs, s_abort, epi);
+    else if (g.lgG == 4) team_gemv_g<WF, 2, 4>(p, rg, cur, g, n, xs, s_abort, epi);
+    else team_gemv_g<WF, 2, 5>(p, rg, cur, g, n, xs, s_abort, epi);
 }
 
 // ------------------------------------------------------------ barrier ----
@@ -887,7 +890,7 @@ __device__ __forceinline__ void run_qkv(const DecodeParams &p, const CtaGeom &cg
         for (int i = threadIdx.x; i < p.h; i += NT) h2[i] = resid_in(p, 0, token, i);
     }
     csync();
-    warp_rmsnorm<EPC>(h2, gain, xs, p.h, p.ch, p.eps);
+    block_rmsnorm<EPC>(h2, gain, xs, p.h, p.ch, p.eps, sm + p.sm_red);
     const int R = cg.qkv_n;
     float *out = p.qkv + cg.qkv_r0;
     DecodeCtrl *ctrl = p.ctrl;
@@ -945,7 +948,7 @@ __device__ __forceinline__ void run_gate_up(const DecodeParams &p, const CtaGeom
     csync();
     if (blockIdx.x == 0)
         for (int i = threadIdx.x; i < p.h; i += NT) flag_nonfinite(p.ctrl, h2[i]);
-    warp_rmsnorm<EPC>(h2, gain, xs, p.h, p.ch, p.eps);
+    block_rmsnorm<EPC>(h2, gain, xs, p.h, p.ch, p.eps, sm + p.sm_red);
     float *act = p.act + cg.gu_f0;
     DecodeCtrl *ctrl = p.ctrl;
     team_gemv<WF, 2>(p, rg, cur, p.kind[K_GU], 2 * cg.gu_n, xs, s_abort, [&](int row, float g, float u) {
@@ -1037,9 +1040,12 @@ __device__ __forceinline__ void run_lm_head(const DecodeParams &p, const CtaGeom
     DecodeCtrl *ctrl = p.ctrl;
     stage_l2(h2, p.hidden, p.h);
     csync();
-    warp_rmsnorm<TEPC>(h2, gain, xs, p.h, p.cemb, p.eps);
-    team_gemv_lm<TF>(p, rg, cur, p.kind[K_LM], cg.lm_n, xs, s_abort,
-                     [&](int r, float acc, float) { rowv[r] = acc; });
+    block_rmsnorm<TEPC>(h2, gain, xs, p.h, p.cemb, p.eps, sm + p.sm_red);
+    const int nlm = cg.lm_n;
+    team_gemv_lm<TF>(p, rg, cur, p.kind[K_LM], nlm, xs, s_abort, [&](int r, float a0, float a1) {
+        rowv[r] = a0;
+        if (r + 1 < nlm) rowv[r + 1] = a1;
+    });
     csync();
     if (*s_abort) return;
     if (ctrl->write_logits) {

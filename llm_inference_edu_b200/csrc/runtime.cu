@@ -439,14 +439,14 @@ static uint32_t session_build(Session &s) {
         KindGeom &g = p.kind[k];
         g.stride = (int)strides[k];
         g.C = (int)(strides[k] / 16);
-        g.U = k == K_GU ? 2 : 1;
+        g.U = (k == K_GU || k == K_LM) ? 2 : 1;  // gate/up pairs; LM rows two at a time
         g.rpc = std::max(g.U, (p.slot_bytes / g.stride) / g.U * g.U);
         g.rpc_magic = g.rpc > 1 ? (unsigned)(((1ull << 32) + g.rpc - 1) / g.rpc) : 0u;  // rpc == 1 divides directly
         const int block_slots = std::max(1, (rows_max[k] + g.rpc - 1) / g.rpc);
         // A per-layer block is consumed in one wave (its weights are already
-        // resident); a longer stream (the LM head) in waves of two slots, so
-        // the rest of the ring keeps copies in flight.
-        g.wave = block_slots <= nslot / 2 ? block_slots : std::max(1, std::min(2, nslot / 2));
+        // resident); a longer stream (the LM head) in waves of a third of the
+        // ring (at most three slots), so the rest keeps copies in flight.
+        g.wave = block_slots <= nslot / 2 ? block_slots : std::max(1, std::min(3, nslot / 3));
         const int units = std::max(1, std::min(rows_max[k], g.wave * g.rpc) / g.U);
         static const int lm_set[3] = {3, 4, 5}, set[3] = {2, 3, 5};  // the device's instantiated sizes
         const int *cand = k == K_LM ? lm_set : set;
