@@ -165,14 +165,13 @@ def run_reference(args, rank, world):
     return 0
 
 
-def run_native(args, rank, world, local_rank):
-    import numpy as np
+def run_native(args, topo):
     import torch
-    import torch.distributed as dist
 
     import llm_inference_edu_b200 as qb
-    from llm_inference_edu_b200 import presets, synthetic
+    from llm_inference_edu_b200 import dp, presets, synthetic
 
+    rank, world, local_rank = topo.rank, topo.world, topo.local_rank
     torch.cuda.set_device(local_rank)
     lf = args.config
     kv = "bf16" if lf == "int8" else "f32"
@@ -198,8 +197,7 @@ def run_native(args, rank, world, local_rank):
     ids = sess.decode_greedy(tok, args.warmup)
     tok = ids[-1]
     L0 = sess.processed()
-    if world > 1:
-        dist.barrier()
+    dp.barrier(topo)
     torch.cuda.synchronize()
     with ClockSampler(local_rank) as clocks:
         ev0.record(stream)
@@ -208,22 +206,17 @@ def run_native(args, rank, world, local_rank):
         torch.cuda.synchronize()
     ms = ev0.elapsed_time(ev1)
     tok = ids[-1]
-    if world > 1:
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = dp.max_over_ranks(topo, ms, device="cuda")
 
     # End to end through the public generation API (host buffers).
     gen = qb.GenerationSession(model, cap, qb.Sampling.Greedy, [], args.warmup + args.steps + 1,
                                kv_dtype=kv, budget=0)
-    gstream = None
     gen.start(prompt)
     for _ in range(args.warmup):
         gen.next_token()
     # The generation owns its own session stream; time with wall clock
     # bracketed by device synchronization.
-    if world > 1:
-        dist.barrier()
+    dp.barrier(topo)
     torch.cuda.synchronize()
     lat = []
     t0 = time.perf_counter()
@@ -232,11 +225,7 @@ def run_native(args, rank, world, local_rank):
         gen.next_token()
         lat.append(time.perf_counter() - a)
     torch.cuda.synchronize()
-    e2e_s = time.perf_counter() - t0
-    if world > 1:
-        t = torch.tensor([e2e_s], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_s = float(t.item())
+    e2e_s = dp.max_over_ranks(topo, time.perf_counter() - t0, device="cuda")
 
     if rank != 0:
         return 0
@@ -296,23 +285,15 @@ def cpu_baseline(args):
 
 def main():
     args = parse()
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    from llm_inference_edu_b200 import dp
+    topo = dp.topology_from_env()
     if args.impl == "reference":
-        return run_reference(args, rank, world)
-    if world > 1:
-        import datetime
-        import torch
-        import torch.distributed as dist
-        torch.cuda.set_device(local_rank)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+        return run_reference(args, topo.rank, topo.world)
+    dp.init(topo, "nccl", timeout_s=600.0)
     try:
-        return run_native(args, rank, world, local_rank)
+        return run_native(args, topo)
     finally:
-        if world > 1:
-            import torch.distributed as dist
-            dist.destroy_process_group()
+        dp.shutdown(topo)
 
 
 if __name__ == "__main__":
