@@ -18,6 +18,7 @@
 
 #include "common.cuh"
 #include "decode.cuh"
+#include "prefill.cuh"
 
 namespace qb {
 int decode_max_ctas(int wfmt, int tfmt, int kv_bf16, size_t smem);
@@ -278,6 +279,8 @@ struct Session {
     cudaStream_t stream = nullptr;
     DevBuf kv, rope, qkv, part, act, hidden, logits, amax_v, amax_i, emitted, ctrl, dlayers, geom;
     DecodeCtrl *hctrl = nullptr;  // pinned mirror
+    std::vector<DecodeLayer> hlayers;  // host copy of the layer table (chunked prompt path)
+    DevBuf pf;                         // chunked prompt workspace (allocated on first use)
     DecodeParams params{};
     int grid = 0;
     cudaGraphExec_t g_host = nullptr;
@@ -347,6 +350,7 @@ static uint32_t session_build(Session &s) {
     }
     if ((st = s.dlayers.alloc(L * sizeof(DecodeLayer), false))) return st;
     QB_CUDA(cudaMemcpy(s.dlayers.p, dl.data(), L * sizeof(DecodeLayer), cudaMemcpyHostToDevice));
+    s.hlayers = dl;
 
     DecodeParams &p = s.params;
     const int wf = m.wf();
@@ -904,6 +908,46 @@ uint32_t qb_session_step(uint64_t session, uint32_t token, float *logits, size_t
     return session_step(*s, token, logits, logits_len, argmax, false);
 }
 
+// Chunked evaluation of a run of prompt tokens (all but the last of an
+// append); fills the cache and advances `processed`.  Shapes the chunked
+// kernels do not cover return QB_UNSUPPORTED without touching the session.
+static constexpr int kPrefillChunk = 256;
+
+static uint32_t session_prefill_chunked(Session &s, const uint32_t *tokens, size_t n) {
+    const Model &m = *s.m;
+    const qb_model_config &c = m.c;
+    PrefillArgs a{};
+    a.V = (int)c.vocab_size; a.L = (int)c.layers; a.h = (int)c.hidden_dim; a.qh = (int)c.query_heads;
+    a.kvh = (int)c.kv_heads; a.hd = (int)c.head_dim; a.ff = (int)c.ff_dim; a.cap = (int)s.capacity;
+    a.group = (int)(c.query_heads / c.kv_heads);
+    a.wfmt = m.wf(); a.tfmt = m.tab == QB_TABLE_BF16 ? WF_BF16 : WF_F32; a.kv_bf16 = s.kv_bf16;
+    a.eps = c.norm_epsilon; a.sqrt_hd = sqrtf((float)c.head_dim);
+    a.sh = m.sh; a.shd = m.shd; a.sff = m.sff; a.semb = m.semb;
+    a.emb = m.emb.as<uint8_t>();
+    a.layers = s.hlayers.data();
+    a.rope = s.rope.as<float2>();
+    a.chunk = kPrefillChunk;
+    if (!prefill_supported(a)) return QB_UNSUPPORTED;
+    const size_t h = c.hidden_dim, ff = c.ff_dim, rq = h + 2 * m.kv(), ch = (size_t)a.chunk;
+    const size_t floats = ch * (4 * h + rq + ff) + ch /* ids */ + 64 /* flags */;
+    if (!s.pf.p) {
+        uint32_t st = s.pf.alloc(floats * 4);
+        if (st) return st;
+    }
+    float *f = s.pf.as<float>();
+    a.x = f; a.xn = a.x + ch * h; a.h2 = a.xn + ch * h; a.ctx = a.h2 + ch * h;
+    a.qkv = a.ctx + ch * h; a.act = a.qkv + ch * rq;
+    a.ids = (uint32_t *)(a.act + ch * ff);
+    a.err = (unsigned *)(a.ids + ch);
+    bool bad = false;
+    cudaError_t e = prefill_kv(a, tokens, (int)n, (int)s.processed, s.stream, &bad);
+    if (e != cudaSuccess) return session_fail(s, cuda_status(e));
+    if (bad) return session_fail(s, QB_NONFINITE);
+    s.processed += n;
+    s.logits_valid = false;
+    return QB_OK;
+}
+
 uint32_t qb_session_append(uint64_t session, const uint32_t *tokens, size_t n, float *logits,
                            size_t logits_len, uint32_t *argmax, int32_t require_empty) {
     clear_detail();
@@ -918,7 +962,14 @@ uint32_t qb_session_append(uint64_t session, const uint32_t *tokens, size_t n, f
     for (size_t i = 0; i < n; ++i)
         if (tokens[i] >= S.m->c.vocab_size) return QB_INVALID_TOKEN;
     if (S.processed + n > S.capacity) return QB_FULL;
-    for (size_t i = 0; i < n; ++i) {
+    size_t i0 = 0;
+    if (n >= 2) {
+        DeviceGuard dg(S.device);
+        const uint32_t st = session_prefill_chunked(S, tokens, n - 1);
+        if (st == QB_OK) i0 = n - 1;
+        else if (st != QB_UNSUPPORTED) return st;
+    }
+    for (size_t i = i0; i < n; ++i) {
         bool last = i + 1 == n;
         uint32_t st = session_step(S, tokens[i], last ? logits : nullptr, logits_len, last ? argmax : nullptr, last);
         if (st) return st;

@@ -322,3 +322,32 @@ def test_qwen05b_device_quantization_bit_exact(oracle):
             s, q = oracle.quantize(synthetic.as_f32(w["layers"][layer][name]), r, c, c)
             assert np.array_equal(values, q.values), (layer, name)
             assert np.array_equal(scales.view(np.uint32), q.scales.ravel().view(np.uint32)), (layer, name)
+
+
+@pytest.mark.parametrize("linear_format,kv,tol", [("int8", "f32", 1e-3), ("int8", "bf16", 2e-2), ("bf16", "f32", 1e-3)])
+def test_qwen05b_chunked_prefill_parity(oracle, linear_format, kv, tol):
+    # A 300-token prompt through prefill_into (chunks of the multi-token
+    # path, then one decode step): last-position logits against the oracle's
+    # serial evaluation, then 32 greedy tokens identical.
+    import llm_inference_edu_b200 as qb
+    from helpers import qwen_host_weights
+    n, greedy = 300, 32
+    cfg = presets.qwen_0_5b(n + greedy + 8)
+    w = qwen_host_weights("0.5b", 1, "bf16")
+    m = qb.Decoder(cfg, w, linear_format=linear_format, table_format="bf16")
+    om = oracle.Model(cfg, oracle_weights(oracle, cfg, w, linear_format))
+    prompt = synthetic.prompt(cfg.vocab_size, n, seed=3)
+    s = qb.CachedSession(m, n + greedy + 8, kv_dtype=kv, budget=0)
+    os_ = oracle.Session(om, n + greedy + 8, kv_bf16=(kv == "bf16"), budget=0)
+    got = s.prefill(prompt)
+    _, exp = os_.prefill(prompt)
+    assert s.processed() == n
+    assert max_abs(got, exp) <= tol, max_abs(got, exp)
+    first = int(np.argmax(exp))
+    assert int(np.argmax(got)) == first
+    dev_ids = [first] + s.decode_greedy(first, greedy - 1)
+    or_ids = [first]
+    for _ in range(greedy - 1):
+        _, lg = os_.step(or_ids[-1])
+        or_ids.append(int(np.argmax(lg)))
+    assert dev_ids == or_ids
