@@ -38,6 +38,11 @@ sys.path.insert(0, ROOT)
 
 PROMPT = 128
 SEED = 1
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one
+# decode_kernel launch of the INT8 workload, from an ncu capture of this
+# kernel (taken at cache position 2; every further cached position adds
+# 6,144 bytes of BF16 KV).
+NCU_TRAFFIC_BYTES_INT8 = 637_587_200
 
 
 def parse():
@@ -248,7 +253,8 @@ def run_native(args, topo):
         "prefill_tok_per_s": PROMPT / (prefill_ms / 1000.0),
         "ms_per_token_p50": 1000.0 * statistics.median(lat),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "traffic": None,
+                     "frac": achieved / peak,
+                     "traffic": NCU_TRAFFIC_BYTES_INT8 if lf == "int8" else None,
                      "bytes_per_step": bytes_step, "peak_source": peak_kind},
         "e2e": {"value": world * args.steps / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 16,
                 "d2h_bytes_per_step": 8},
