@@ -340,6 +340,38 @@ uint32_t qb_generation_prefix_logits(uint64_t generation, float *logits, size_t 
 uint32_t qb_generation_free(uint64_t generation);
 
 /* ------------------------------------------------------------------ */
+/* Batched greedy decode of independent sequences                      */
+/* ------------------------------------------------------------------ */
+/* No counterpart in the reference, which decodes one sequence per session
+ * (src/kv_cache.rs:186-215 is the per-token step each row here repeats).
+ * `sequences` rows advance in lockstep, each with its own KV cache of
+ * `capacity` positions; every row equals what a CachedSession fed the same
+ * tokens would compute (within FP32 reassociation).  Created on the
+ * model's device; the model must outlive it. */
+typedef struct {
+    size_t sequences, capacity, processed;
+    int32_t valid;
+} qb_batch_info;
+
+uint32_t qb_batch_create(uint64_t model, size_t sequences, size_t capacity, uint32_t kv_dtype,
+                         uint64_t *out_batch);
+/* prompts [sequences][prompt_len] (HOST); next_ids [sequences] (HOST,
+ * nullable) receives each row's greedy id after its last prompt token.
+ * QB_NOT_EMPTY unless the batch is empty. */
+uint32_t qb_batch_prefill(uint64_t batch, const uint32_t *prompts, size_t prompt_len,
+                          uint32_t *next_ids);
+/* Feeds tokens [sequences] (HOST), then each row's greedy id, for `steps`
+ * steps; ids [steps][sequences] (HOST, nullable) receives the greedy ids. */
+uint32_t qb_batch_decode_greedy(uint64_t batch, const uint32_t *tokens, size_t steps,
+                                uint32_t *ids);
+/* Logits of the last step, [sequences][vocab]. */
+uint32_t qb_batch_logits(uint64_t batch, float *logits, size_t logits_len);
+uint32_t qb_batch_info_get(uint64_t batch, qb_batch_info *out);
+uint32_t qb_batch_reset(uint64_t batch);
+uint32_t qb_batch_stream(uint64_t batch, void **stream);
+uint32_t qb_batch_free(uint64_t batch);
+
+/* ------------------------------------------------------------------ */
 /* Synthetic inputs (host only; no GPU needed)                         */
 /* ------------------------------------------------------------------ */
 

@@ -57,6 +57,14 @@ SIGNATURES = {
     "qb_generation_history": ([U64, P, S, P], U32),
     "qb_generation_prefix_logits": ([U64, P, S], U32),
     "qb_generation_free": ([U64], U32),
+    "qb_batch_create": ([U64, S, S, U32, P], U32),
+    "qb_batch_prefill": ([U64, P, S, P], U32),
+    "qb_batch_decode_greedy": ([U64, P, S, P], U32),
+    "qb_batch_logits": ([U64, P, S], U32),
+    "qb_batch_info_get": ([U64, P], U32),
+    "qb_batch_reset": ([U64], U32),
+    "qb_batch_stream": ([U64, P], U32),
+    "qb_batch_free": ([U64], U32),
     "qb_synthetic_normal": ([U64, U64, S, C.c_double, U32, P], U32),
     "qb_synthetic_tokens": ([U64, U64, S, U32, P], U32),
 }
@@ -98,3 +106,7 @@ class SessionInfo(C.Structure):
 class GenerationInfo(C.Structure):
     _fields_ = [("processed", S), ("history_len", S), ("generated", S), ("max_new", S),
                 ("stop_reason", I32), ("valid", I32), ("logits_ready", I32)]
+
+
+class BatchInfo(C.Structure):
+    _fields_ = [("sequences", S), ("capacity", S), ("processed", S), ("valid", I32)]

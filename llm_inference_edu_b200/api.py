@@ -447,6 +447,78 @@ class CachedSession:
         return p.value or 0
 
 
+# ---------------------------------------------------------------- batch --
+
+class BatchSession:
+    """`sequences` independent sequences decoded greedily in lockstep, each
+    with its own KV cache of `capacity` positions.  No counterpart in the
+    reference (one sequence per CachedSession); each row matches a
+    CachedSession fed the same tokens."""
+
+    def __init__(self, model: Decoder, sequences: int, capacity: int, kv_dtype: str = "f32"):
+        self.model = model
+        h = C.c_uint64()
+        _check(lib().qb_batch_create(model.handle, sequences, capacity, KV_DTYPES[kv_dtype],
+                                     C.byref(h)), CacheError)
+        self.handle = h.value
+        self.sequences = sequences
+        self.vocab = model.config.vocab_size
+
+    def __del__(self):
+        if getattr(self, "handle", None):
+            lib().qb_batch_free(self.handle)
+            self.handle = None
+
+    def _info(self):
+        i = _lib.BatchInfo()
+        _check(lib().qb_batch_info_get(self.handle, C.byref(i)), CacheError)
+        return i
+
+    def processed(self) -> int:
+        return self._info().processed
+
+    def capacity(self) -> int:
+        return self._info().capacity
+
+    def is_valid(self) -> bool:
+        return bool(self._info().valid)
+
+    def reset(self):
+        _check(lib().qb_batch_reset(self.handle), CacheError)
+
+    def prefill(self, prompts) -> np.ndarray:
+        """prompts [sequences][prompt_len]; returns each row's greedy id after
+        its last prompt token."""
+        p = np.ascontiguousarray(np.asarray(prompts, dtype=np.uint32))
+        if p.ndim != 2 or p.shape[0] != self.sequences:
+            raise ValueError(f"prompts must be [{self.sequences}][prompt_len]")
+        out = np.zeros(self.sequences, dtype=np.uint32)
+        _check(lib().qb_batch_prefill(self.handle, p.ctypes.data_as(C.c_void_p) if p.size else None,
+                                      p.shape[1], out.ctypes.data_as(C.c_void_p)), CacheError)
+        return out
+
+    def decode_greedy(self, tokens, steps: int) -> np.ndarray:
+        """Feeds tokens [sequences], then each row's greedy id; returns the
+        greedy ids [steps][sequences]."""
+        t = np.ascontiguousarray(np.asarray(tokens, dtype=np.uint32))
+        if t.shape != (self.sequences,):
+            raise ValueError(f"tokens must be [{self.sequences}]")
+        out = np.zeros((steps, self.sequences), dtype=np.uint32)
+        _check(lib().qb_batch_decode_greedy(self.handle, t.ctypes.data_as(C.c_void_p), steps,
+                                            out.ctypes.data_as(C.c_void_p)), CacheError)
+        return out
+
+    def logits(self) -> np.ndarray:
+        out = np.zeros((self.sequences, self.vocab), dtype=np.float32)
+        _check(lib().qb_batch_logits(self.handle, out.ctypes.data_as(C.c_void_p), out.size), CacheError)
+        return out
+
+    def stream(self) -> int:
+        p = C.c_void_p()
+        _check(lib().qb_batch_stream(self.handle, C.byref(p)), CacheError)
+        return p.value or 0
+
+
 # ----------------------------------------------------------- generation --
 
 class Sampling:

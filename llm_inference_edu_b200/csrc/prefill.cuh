@@ -1,5 +1,6 @@
-// Chunked prompt evaluation: fills the KV cache for a run of prompt tokens
-// with a few wide kernels per layer instead of one decode step per token.
+// Multi-token forward: many tokens per launch sequence instead of one
+// decode step per token.  Serves the chunked prompt path of a session
+// (KV fill) and batched greedy decoding of independent sequences.
 #pragma once
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -9,18 +10,24 @@
 
 namespace qb {
 
-// Everything the chunked path reads or writes (device pointers unless
-// noted).  The layer table is a host copy of the session's DecodeLayer
-// array (weights in the decode layout, KV pointers of this session).
+// Everything the multi-token kernels read or write (device pointers unless
+// noted).  The layer table is a host copy of a DecodeLayer array whose
+// weights are in the decode layout; its KV pointers are ignored: the cache
+// of sequence s, layer l is K at kv + s * kv_seq_bytes + 2 l kv_layer_bytes
+// and V right after it, each [kv_heads][cap][head_dim].
 struct PrefillArgs {
     int V, L, h, qh, kvh, hd, ff, cap, group;
     int wfmt, tfmt, kv_bf16;
     float eps, sqrt_hd;
     size_t sh, shd, sff, semb;
     const uint8_t *emb;           // [V, semb] embedding table
+    const uint8_t *head;          // LM-head table (== emb when tied)
+    const float *final_norm;      // [h]
     const DecodeLayer *layers;    // HOST array [L]
     const float2 *rope;           // [cap][hd/2] (cos, sin)
-    int chunk;                    // workspace rows (tokens per chunk)
+    uint8_t *kv;                  // cache base
+    size_t kv_layer_bytes, kv_seq_bytes;
+    int chunk;                    // workspace rows (tokens per launch sequence)
     // Workspace, `chunk` rows each.
     float *x;                     // [chunk][h] residual stream
     float *xn;                    // [chunk][h] normalized rows
@@ -28,20 +35,37 @@ struct PrefillArgs {
     float *qkv;                   // [chunk][h + 2 kv]
     float *ctx;                   // [chunk][h] attention context
     float *act;                   // [chunk][ff] SwiGLU output
+    float *part;                  // split-K partial sums, part_floats floats
+    size_t part_floats;
     uint32_t *ids;                // [chunk] token ids
+    int *pos;                     // [chunk] positions
+    int *seq;                     // [chunk] sequence indices
+    float *logits;                // [chunk][V] (null unless the LM head runs)
+    uint32_t *amax;               // [chunk] greedy ids (null unless the LM head runs)
     unsigned *err;                // error flags (ERR_NONFINITE)
 };
 
-// True when the shapes suit the chunked kernels (else callers evaluate the
-// tokens one decode step at a time).
+// True when the shapes suit the multi-token kernels (else callers evaluate
+// the tokens one decode step at a time).
 bool prefill_supported(const PrefillArgs &a);
 
-// Writes the K/V of every layer for tokens[0, n) at positions p0 .. p0+n-1
-// (tokens on the HOST).  The chunk's own attention is causal over the cache
-// plus the chunk.  The final layer's MLP is skipped: only the cache is
-// produced.  Errors: the CUDA status; *nonfinite set when any value was not
-// finite.
+// Runs n <= chunk tokens whose ids, positions and sequences are already in
+// a.ids / a.pos / a.seq; max_pos is the largest position among them.  Each
+// token attends to its own sequence's positions 0 .. pos (its own K/V
+// included).  With lm_head the final layer runs in full and a.logits /
+// a.amax receive each token's logits and greedy id (strict >, lowest id on
+// ties, src/sampling.rs:65-70); without it the final layer's MLP is skipped
+// (only the cache is produced).  Errors land in a.err (not cleared here).
+cudaError_t forward_tokens(const PrefillArgs &a, int n, int max_pos, bool lm_head, cudaStream_t st);
+
+// Chunked prompt path of one session (sequence 0): the K/V of tokens[0, n)
+// (HOST) at positions p0 .. p0+n-1.  *nonfinite is set when any value was
+// not finite.
 cudaError_t prefill_kv(const PrefillArgs &a, const uint32_t *tokens, int n, int p0, cudaStream_t st,
                        bool *nonfinite);
+
+// Advances every position in a.pos[0, n) by one and copies a.amax into
+// a.ids (the next step's tokens), on the device.
+cudaError_t advance_tokens(const PrefillArgs &a, int n, cudaStream_t st);
 
 }  // namespace qb

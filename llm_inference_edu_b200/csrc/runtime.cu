@@ -305,6 +305,64 @@ static size_t ref_workspace_bytes(const qb_model_config &c, size_t capacity) {
     return (c.hidden_dim * 8 + c.kv_heads * c.head_dim * 3 + c.ff_dim * 3 + capacity * 2) * 4;
 }
 
+// RoPE table [cap][hd/2] of (cos, sin): the reference's f32 powf/sin/cos per
+// position (src/rope.rs:83-90), computed on the host with the C library.
+static uint32_t build_rope(const qb_model_config &c, size_t cap, DevBuf &out) {
+    const size_t half = c.head_dim / 2;
+    std::vector<float> tab(cap * half * 2);
+    std::vector<float> freq(half);
+    for (size_t j = 0; j < half; ++j) freq[j] = powf(c.rope_base, -((float)(2 * j)) / (float)c.head_dim);
+    for (size_t t = 0; t < cap; ++t) {
+        float pos = (float)t;
+        for (size_t j = 0; j < half; ++j) {
+            float a = pos * freq[j];
+            tab[(t * half + j) * 2] = cosf(a);
+            tab[(t * half + j) * 2 + 1] = sinf(a);
+        }
+    }
+    uint32_t st = out.alloc(tab.size() * 4, false);
+    if (st) return st;
+    QB_CUDA(cudaMemcpy(out.p, tab.data(), tab.size() * 4, cudaMemcpyHostToDevice));
+    return QB_OK;
+}
+
+// The model-level fields of the multi-token arguments, for a cache of `cap`
+// positions per sequence.
+static void prefill_common(const Model &m, size_t cap, int kv_bf16, PrefillArgs &a) {
+    const qb_model_config &c = m.c;
+    a.V = (int)c.vocab_size; a.L = (int)c.layers; a.h = (int)c.hidden_dim; a.qh = (int)c.query_heads;
+    a.kvh = (int)c.kv_heads; a.hd = (int)c.head_dim; a.ff = (int)c.ff_dim; a.cap = (int)cap;
+    a.group = (int)(c.query_heads / c.kv_heads);
+    a.wfmt = m.wf(); a.tfmt = m.tab == QB_TABLE_BF16 ? WF_BF16 : WF_F32; a.kv_bf16 = kv_bf16;
+    a.eps = c.norm_epsilon; a.sqrt_hd = sqrtf((float)c.head_dim);
+    a.sh = m.sh; a.shd = m.shd; a.sff = m.sff; a.semb = m.semb;
+    a.emb = m.emb.as<uint8_t>();
+    a.head = m.head_set ? m.head.as<uint8_t>() : m.emb.as<uint8_t>();
+    a.final_norm = m.final_norm.as<float>();
+    a.kv_layer_bytes = round16(c.kv_heads * cap * c.head_dim * (kv_bf16 ? 2 : 4));
+    a.kv_seq_bytes = 2 * c.layers * a.kv_layer_bytes;
+}
+
+// Carves the multi-token workspace for `chunk` rows out of one buffer
+// (allocated on first use): activations, split-K partials, ids, positions,
+// sequences and the error word.
+static uint32_t prefill_workspace(const Model &m, int chunk, DevBuf &ws, PrefillArgs &a) {
+    const size_t h = m.c.hidden_dim, ff = m.c.ff_dim, rq = h + 2 * m.kv(), ch = (size_t)chunk;
+    const size_t part = 4 * ch * std::max(rq, h);
+    const size_t floats = ch * (4 * h + rq + ff) + part + 3 * ch + 64;
+    if (!ws.p) {
+        uint32_t st = ws.alloc(floats * 4);
+        if (st) return st;
+    }
+    float *f = ws.as<float>();
+    a.chunk = chunk;
+    a.x = f; a.xn = a.x + ch * h; a.h2 = a.xn + ch * h; a.ctx = a.h2 + ch * h;
+    a.qkv = a.ctx + ch * h; a.act = a.qkv + ch * rq; a.part = a.act + ch * ff; a.part_floats = part;
+    a.ids = (uint32_t *)(a.part + part); a.pos = (int *)(a.ids + ch); a.seq = a.pos + ch;
+    a.err = (unsigned *)(a.seq + ch);
+    return QB_OK;
+}
+
 static uint32_t session_build(Session &s) {
     Model &m = *s.m;
     const qb_model_config &c = m.c;
@@ -314,21 +372,7 @@ static uint32_t session_build(Session &s) {
     uint32_t st;
     QB_CUDA(cudaStreamCreateWithFlags(&s.stream, cudaStreamNonBlocking));
     if ((st = s.kv.alloc(round16(per) * 2 * L))) return st;
-    // RoPE table: the reference's f32 powf/sin/cos per position (src/rope.rs:83-90).
-    const size_t half = hd / 2;
-    std::vector<float> tab(cap * half * 2);
-    std::vector<float> freq(half);
-    for (size_t j = 0; j < half; ++j) freq[j] = powf(c.rope_base, -((float)(2 * j)) / (float)hd);
-    for (size_t t = 0; t < cap; ++t) {
-        float pos = (float)t;
-        for (size_t j = 0; j < half; ++j) {
-            float a = pos * freq[j];
-            tab[(t * half + j) * 2] = cosf(a);
-            tab[(t * half + j) * 2 + 1] = sinf(a);
-        }
-    }
-    if ((st = s.rope.alloc(tab.size() * 4, false))) return st;
-    QB_CUDA(cudaMemcpy(s.rope.p, tab.data(), tab.size() * 4, cudaMemcpyHostToDevice));
+    if ((st = build_rope(c, cap, s.rope))) return st;
     const size_t rqkv = c.hidden_dim + 2 * kvh * hd;
     int dev_sms = 0;
     QB_CUDA(cudaDeviceGetAttribute(&dev_sms, cudaDevAttrMultiProcessorCount, s.device));
@@ -563,9 +607,43 @@ static std::shared_ptr<Generation> find_generation(uint64_t h) {
 
 static bool cancelled(const volatile int32_t *c) { return c && *c != 0; }
 
+// Chunked evaluation of a run of prompt tokens (all but the last of an
+// append); fills the cache and advances `processed`.  Shapes the chunked
+// kernels do not cover return QB_UNSUPPORTED without touching the session.
+static constexpr int kPrefillChunk = 256;
+
+static uint32_t session_prefill_chunked(Session &s, const uint32_t *tokens, size_t n) {
+    const Model &m = *s.m;
+    PrefillArgs a{};
+    prefill_common(m, s.capacity, s.kv_bf16, a);
+    a.layers = s.hlayers.data();
+    a.rope = s.rope.as<float2>();
+    a.kv = s.kv.as<uint8_t>();
+    a.chunk = kPrefillChunk;
+    if (!prefill_supported(a)) return QB_UNSUPPORTED;
+    uint32_t st = prefill_workspace(m, kPrefillChunk, s.pf, a);
+    if (st) return st;
+    bool bad = false;
+    cudaError_t e = prefill_kv(a, tokens, (int)n, (int)s.processed, s.stream, &bad);
+    if (e != cudaSuccess) return session_fail(s, cuda_status(e));
+    if (bad) return session_fail(s, QB_NONFINITE);
+    s.processed += n;
+    s.logits_valid = false;
+    return QB_OK;
+}
+
 // evaluate_pending, src/generation.rs:258-274.
 static uint32_t evaluate_pending(Generation &g, const volatile int32_t *cancel) {
     Session &s = *g.cache;
+    // Without a cancel flag nothing can interrupt the evaluation between
+    // tokens, so all pending tokens but the last go through the chunked path.
+    if (!cancel && g.history.size() - s.processed >= 2) {
+        DeviceGuard dg(s.device);
+        const size_t n = g.history.size() - s.processed - 1;
+        const uint32_t st = session_prefill_chunked(s, g.history.data() + s.processed, n);
+        if (st != QB_OK && st != QB_UNSUPPORTED) return st;
+        if (st == QB_OK) g.logits_ready = false;
+    }
     while (s.processed < g.history.size()) {
         if (cancelled(cancel)) return QB_CANCELLED;
         uint32_t token = g.history[s.processed];
@@ -588,6 +666,61 @@ static void generation_reset(Generation &g) {
     g.logits_ready = false;
     g.generated = 0;
     g.stop = QB_STOP_NONE;
+}
+
+
+// ----------------------------------------------------------- batch ----
+
+// B independent sequences decoded in lockstep with the multi-token kernels
+// (one row per sequence per step).  Each sequence has its own KV cache of
+// `capacity` positions; all advance together.
+struct Batch {
+    std::shared_ptr<Model> m;
+    int device = 0;
+    size_t nseq = 0, capacity = 0, processed = 0;
+    bool valid = true;
+    int kv_bf16 = 0;
+    cudaStream_t stream = nullptr;
+    DevBuf kv, rope, ws, logits, amax, hist;
+    std::vector<DecodeLayer> hlayers;
+    PrefillArgs a{};
+    bool logits_valid = false;
+    ~Batch() {
+        DeviceGuard dg(device);
+        if (stream) cudaStreamDestroy(stream);
+    }
+};
+
+static std::map<uint64_t, std::shared_ptr<Batch>> g_batches;
+
+static std::shared_ptr<Batch> find_batch(uint64_t h) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = g_batches.find(h);
+    return it == g_batches.end() ? nullptr : it->second;
+}
+
+static uint32_t batch_fail(Batch &b, uint32_t status) {
+    b.valid = false;
+    b.processed = 0;
+    b.logits_valid = false;
+    cudaStreamSynchronize(b.stream);
+    return status;
+}
+
+// Runs n rows already in b.a.ids / pos / seq; checks the error word.
+static uint32_t batch_forward(Batch &b, int n, int max_pos, bool lm_head) {
+    cudaError_t e = forward_tokens(b.a, n, max_pos, lm_head, b.stream);
+    if (e != cudaSuccess) return batch_fail(b, cuda_status(e));
+    return QB_OK;
+}
+
+static uint32_t batch_check(Batch &b) {
+    unsigned herr = 0;
+    cudaError_t e = cudaMemcpyAsync(&herr, b.a.err, sizeof(unsigned), cudaMemcpyDeviceToHost, b.stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(b.stream);
+    if (e != cudaSuccess) return batch_fail(b, cuda_status(e));
+    if (herr) return batch_fail(b, QB_NONFINITE);
+    return QB_OK;
 }
 
 }  // namespace qb
@@ -908,46 +1041,6 @@ uint32_t qb_session_step(uint64_t session, uint32_t token, float *logits, size_t
     return session_step(*s, token, logits, logits_len, argmax, false);
 }
 
-// Chunked evaluation of a run of prompt tokens (all but the last of an
-// append); fills the cache and advances `processed`.  Shapes the chunked
-// kernels do not cover return QB_UNSUPPORTED without touching the session.
-static constexpr int kPrefillChunk = 256;
-
-static uint32_t session_prefill_chunked(Session &s, const uint32_t *tokens, size_t n) {
-    const Model &m = *s.m;
-    const qb_model_config &c = m.c;
-    PrefillArgs a{};
-    a.V = (int)c.vocab_size; a.L = (int)c.layers; a.h = (int)c.hidden_dim; a.qh = (int)c.query_heads;
-    a.kvh = (int)c.kv_heads; a.hd = (int)c.head_dim; a.ff = (int)c.ff_dim; a.cap = (int)s.capacity;
-    a.group = (int)(c.query_heads / c.kv_heads);
-    a.wfmt = m.wf(); a.tfmt = m.tab == QB_TABLE_BF16 ? WF_BF16 : WF_F32; a.kv_bf16 = s.kv_bf16;
-    a.eps = c.norm_epsilon; a.sqrt_hd = sqrtf((float)c.head_dim);
-    a.sh = m.sh; a.shd = m.shd; a.sff = m.sff; a.semb = m.semb;
-    a.emb = m.emb.as<uint8_t>();
-    a.layers = s.hlayers.data();
-    a.rope = s.rope.as<float2>();
-    a.chunk = kPrefillChunk;
-    if (!prefill_supported(a)) return QB_UNSUPPORTED;
-    const size_t h = c.hidden_dim, ff = c.ff_dim, rq = h + 2 * m.kv(), ch = (size_t)a.chunk;
-    const size_t floats = ch * (4 * h + rq + ff) + ch /* ids */ + 64 /* flags */;
-    if (!s.pf.p) {
-        uint32_t st = s.pf.alloc(floats * 4);
-        if (st) return st;
-    }
-    float *f = s.pf.as<float>();
-    a.x = f; a.xn = a.x + ch * h; a.h2 = a.xn + ch * h; a.ctx = a.h2 + ch * h;
-    a.qkv = a.ctx + ch * h; a.act = a.qkv + ch * rq;
-    a.ids = (uint32_t *)(a.act + ch * ff);
-    a.err = (unsigned *)(a.ids + ch);
-    bool bad = false;
-    cudaError_t e = prefill_kv(a, tokens, (int)n, (int)s.processed, s.stream, &bad);
-    if (e != cudaSuccess) return session_fail(s, cuda_status(e));
-    if (bad) return session_fail(s, QB_NONFINITE);
-    s.processed += n;
-    s.logits_valid = false;
-    return QB_OK;
-}
-
 uint32_t qb_session_append(uint64_t session, const uint32_t *tokens, size_t n, float *logits,
                            size_t logits_len, uint32_t *argmax, int32_t require_empty) {
     clear_detail();
@@ -1252,6 +1345,204 @@ uint32_t qb_generation_free(uint64_t gen) {
     auto it = g_generations.find(gen);
     if (it == g_generations.end()) return QB_INVALID_HANDLE;
     g_generations.erase(it);
+    return QB_OK;
+}
+
+
+// ----------------------------------------------------------- batch ABI ----
+
+uint32_t qb_batch_create(uint64_t model, size_t sequences, size_t capacity, uint32_t kv_dtype, uint64_t *out) {
+    clear_detail();
+    auto m = find_model(model);
+    if (!m) return QB_INVALID_HANDLE;
+    if (!m->finalized) return QB_INVALID_STATE;
+    if (!out) return QB_INVALID_PARAMETERS;
+    if (sequences == 0 || capacity == 0 || capacity > m->c.max_tokens) return QB_INVALID_CAPACITY;
+    if (kv_dtype > QB_KV_BF16) return QB_INVALID_PARAMETERS;
+    auto b = std::make_shared<Batch>();
+    b->m = m;
+    b->device = m->device;
+    b->nseq = sequences;
+    b->capacity = capacity;
+    b->kv_bf16 = kv_dtype == QB_KV_BF16;
+    DeviceGuard dg(b->device);
+    PrefillArgs &a = b->a;
+    prefill_common(*m, capacity, b->kv_bf16, a);
+    const int chunk = (int)std::max<size_t>(sequences, 256);
+    a.chunk = chunk;
+    if (!prefill_supported(a) || sequences > (1u << 20)) return QB_UNSUPPORTED;
+    size_t kvb;
+    if (mul_ovf(a.kv_seq_bytes, sequences, &kvb)) return QB_DIMENSION_OVERFLOW;
+    uint32_t st;
+    QB_CUDA(cudaStreamCreateWithFlags(&b->stream, cudaStreamNonBlocking));
+    if ((st = b->kv.alloc(kvb)) || (st = build_rope(m->c, capacity, b->rope)) ||
+        (st = prefill_workspace(*m, chunk, b->ws, a)) ||
+        (st = b->logits.alloc(sequences * m->c.vocab_size * 4, false)) || (st = b->amax.alloc(sequences * 4)))
+        return st == QB_CUDA_ERROR ? QB_ALLOCATION : st;
+    b->hlayers.resize(m->c.layers);
+    QB_CUDA(cudaMemcpy(b->hlayers.data(), m->dlayers.p, m->c.layers * sizeof(DecodeLayer), cudaMemcpyDeviceToHost));
+    a.layers = b->hlayers.data();
+    a.rope = b->rope.as<float2>();
+    a.kv = b->kv.as<uint8_t>();
+    a.logits = b->logits.as<float>();
+    a.amax = b->amax.as<uint32_t>();
+    std::lock_guard<std::mutex> lk(g_mu);
+    uint64_t id = g_next++;
+    g_batches[id] = b;
+    *out = id;
+    return QB_OK;
+}
+
+uint32_t qb_batch_prefill(uint64_t batch, const uint32_t *prompts, size_t prompt_len, uint32_t *next_ids) {
+    clear_detail();
+    auto bp = find_batch(batch);
+    if (!bp) return QB_INVALID_HANDLE;
+    Batch &b = *bp;
+    if (!b.valid) return QB_INVALID_STATE;
+    if (b.processed != 0) return QB_NOT_EMPTY;
+    if (prompt_len == 0 || !prompts) return QB_EMPTY_INPUT;
+    if (prompt_len > b.capacity) return QB_FULL;
+    const size_t V = b.m->c.vocab_size, B = b.nseq;
+    for (size_t i = 0; i < B * prompt_len; ++i)
+        if (prompts[i] >= V) { set_detail(0, V, prompts[i], i); return QB_INVALID_TOKEN; }
+    DeviceGuard dg(b.device);
+    PrefillArgs &a = b.a;
+    cudaError_t e = cudaMemsetAsync(a.err, 0, sizeof(unsigned), b.stream);
+    if (e != cudaSuccess) return batch_fail(b, cuda_status(e));
+    // K/V of every prompt token but each sequence's last, in chunks that mix
+    // sequences; then the last tokens together, with the LM head.
+    const size_t fill = prompt_len - 1, total = B * fill;
+    std::vector<uint32_t> hid(a.chunk);
+    std::vector<int> hpos(a.chunk), hseq(a.chunk);
+    for (size_t c0 = 0; c0 < total; c0 += a.chunk) {
+        const int nc = (int)std::min<size_t>(a.chunk, total - c0);
+        int maxp = 0;
+        for (int t = 0; t < nc; ++t) {
+            const size_t g = c0 + t, sq = g / fill, p = g % fill;
+            hid[t] = prompts[sq * prompt_len + p];
+            hpos[t] = (int)p;
+            hseq[t] = (int)sq;
+            maxp = std::max(maxp, (int)p);
+        }
+        if ((e = cudaMemcpyAsync(a.ids, hid.data(), nc * 4, cudaMemcpyHostToDevice, b.stream)) ||
+            (e = cudaMemcpyAsync(a.pos, hpos.data(), nc * 4, cudaMemcpyHostToDevice, b.stream)) ||
+            (e = cudaMemcpyAsync(a.seq, hseq.data(), nc * 4, cudaMemcpyHostToDevice, b.stream)))
+            return batch_fail(b, cuda_status(e));
+        uint32_t st = batch_forward(b, nc, maxp, false);
+        if (st) return st;
+        if ((e = cudaStreamSynchronize(b.stream)) != cudaSuccess) return batch_fail(b, cuda_status(e));
+    }
+    for (size_t sq = 0; sq < B; ++sq) {
+        hid[sq] = prompts[sq * prompt_len + fill];
+        hpos[sq] = (int)fill;
+        hseq[sq] = (int)sq;
+    }
+    if ((e = cudaMemcpyAsync(a.ids, hid.data(), B * 4, cudaMemcpyHostToDevice, b.stream)) ||
+        (e = cudaMemcpyAsync(a.pos, hpos.data(), B * 4, cudaMemcpyHostToDevice, b.stream)) ||
+        (e = cudaMemcpyAsync(a.seq, hseq.data(), B * 4, cudaMemcpyHostToDevice, b.stream)))
+        return batch_fail(b, cuda_status(e));
+    uint32_t st = batch_forward(b, (int)B, (int)fill, true);
+    if (st) return st;
+    if (next_ids && (e = cudaMemcpyAsync(next_ids, a.amax, B * 4, cudaMemcpyDeviceToHost, b.stream)))
+        return batch_fail(b, cuda_status(e));
+    if ((st = batch_check(b))) return st;
+    b.processed = prompt_len;
+    b.logits_valid = true;
+    return QB_OK;
+}
+
+uint32_t qb_batch_decode_greedy(uint64_t batch, const uint32_t *tokens, size_t steps, uint32_t *ids) {
+    clear_detail();
+    auto bp = find_batch(batch);
+    if (!bp) return QB_INVALID_HANDLE;
+    Batch &b = *bp;
+    if (!b.valid) return QB_INVALID_STATE;
+    if (!tokens || steps == 0) return QB_EMPTY_INPUT;
+    if (b.processed + steps > b.capacity) return QB_FULL;
+    const size_t V = b.m->c.vocab_size, B = b.nseq;
+    for (size_t i = 0; i < B; ++i)
+        if (tokens[i] >= V) { set_detail(0, V, tokens[i], i); return QB_INVALID_TOKEN; }
+    DeviceGuard dg(b.device);
+    PrefillArgs &a = b.a;
+    size_t hb;
+    if (mul_ovf(steps, B * 4, &hb)) return QB_DIMENSION_OVERFLOW;
+    if (b.hist.bytes < hb) {
+        uint32_t st = b.hist.alloc(hb, false);
+        if (st) return st;
+    }
+    std::vector<int> hpos(B, (int)b.processed), hseq(B);
+    for (size_t sq = 0; sq < B; ++sq) hseq[sq] = (int)sq;
+    cudaError_t e;
+    if ((e = cudaMemsetAsync(a.err, 0, sizeof(unsigned), b.stream)) ||
+        (e = cudaMemcpyAsync(a.ids, tokens, B * 4, cudaMemcpyHostToDevice, b.stream)) ||
+        (e = cudaMemcpyAsync(a.pos, hpos.data(), B * 4, cudaMemcpyHostToDevice, b.stream)) ||
+        (e = cudaMemcpyAsync(a.seq, hseq.data(), B * 4, cudaMemcpyHostToDevice, b.stream)))
+        return batch_fail(b, cuda_status(e));
+    for (size_t k = 0; k < steps; ++k) {
+        uint32_t st = batch_forward(b, (int)B, (int)(b.processed + k), true);
+        if (st) return st;
+        if ((e = cudaMemcpyAsync(b.hist.as<uint32_t>() + k * B, a.amax, B * 4, cudaMemcpyDeviceToDevice,
+                                 b.stream)) ||
+            (e = advance_tokens(a, (int)B, b.stream)))
+            return batch_fail(b, cuda_status(e));
+    }
+    if (ids && (e = cudaMemcpyAsync(ids, b.hist.p, steps * B * 4, cudaMemcpyDeviceToHost, b.stream)))
+        return batch_fail(b, cuda_status(e));
+    uint32_t st = batch_check(b);
+    if (st) return st;
+    b.processed += steps;
+    b.logits_valid = true;
+    return QB_OK;
+}
+
+uint32_t qb_batch_logits(uint64_t batch, float *logits, size_t logits_len) {
+    clear_detail();
+    auto bp = find_batch(batch);
+    if (!bp) return QB_INVALID_HANDLE;
+    Batch &b = *bp;
+    if (!b.valid || !b.logits_valid) return QB_NOT_STARTED;
+    if (logits_len != b.nseq * b.m->c.vocab_size) {
+        set_detail(0, b.nseq * b.m->c.vocab_size, logits_len);
+        return QB_INVALID_OUTPUT_LENGTH;
+    }
+    DeviceGuard dg(b.device);
+    QB_CUDA(cudaMemcpy(logits, b.logits.p, logits_len * 4, cudaMemcpyDeviceToHost));
+    return QB_OK;
+}
+
+uint32_t qb_batch_info_get(uint64_t batch, qb_batch_info *out) {
+    auto bp = find_batch(batch);
+    if (!bp) return QB_INVALID_HANDLE;
+    if (!out) return QB_INVALID_PARAMETERS;
+    out->sequences = bp->nseq;
+    out->capacity = bp->capacity;
+    out->processed = bp->processed;
+    out->valid = bp->valid ? 1 : 0;
+    return QB_OK;
+}
+
+uint32_t qb_batch_reset(uint64_t batch) {
+    auto bp = find_batch(batch);
+    if (!bp) return QB_INVALID_HANDLE;
+    bp->processed = 0;
+    bp->valid = true;
+    bp->logits_valid = false;
+    return QB_OK;
+}
+
+uint32_t qb_batch_stream(uint64_t batch, void **stream) {
+    auto bp = find_batch(batch);
+    if (!bp) return QB_INVALID_HANDLE;
+    if (!stream) return QB_INVALID_PARAMETERS;
+    *stream = (void *)bp->stream;
+    return QB_OK;
+}
+
+uint32_t qb_batch_free(uint64_t batch) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = g_batches.find(batch);
+    if (it == g_batches.end()) return QB_INVALID_HANDLE;
+    g_batches.erase(it);
     return QB_OK;
 }
 
