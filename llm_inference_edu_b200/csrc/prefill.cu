@@ -16,20 +16,14 @@
 #include <vector>
 
 #include "common.cuh"
+#include "multitoken.cuh"
 #include "prefill.cuh"
+#include "tc_gemm.cuh"
 
 namespace qb {
 namespace {
 
-__device__ __forceinline__ void flag_bad(unsigned *err, float v) {
-    if (!isfinite(v)) atomicOr(err, ERR_NONFINITE);
-}
-
-__device__ __forceinline__ float silu_ref(float v) {
-    if (v >= 0.0f) return v / (1.0f + expf(-v));
-    const float e = expf(v);
-    return v * e / (1.0f + e);
-}
+using namespace mt;
 
 __device__ float block_max(float v, float *red) {
     for (int off = 16; off; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
@@ -57,6 +51,8 @@ __device__ float block_sum(float v, float *red) {
 
 template <int TF>
 __global__ void embed_rows(const uint32_t *ids, int n, const uint8_t *emb, size_t semb, int h, float *x) {
+    pdl_trigger();
+    pdl_wait();
     for (int t = blockIdx.x; t < n; t += gridDim.x) {
         const uint8_t *row = emb + (size_t)ids[t] * semb;
         for (int i = threadIdx.x; i < h; i += blockDim.x)
@@ -65,12 +61,49 @@ __global__ void embed_rows(const uint32_t *ids, int n, const uint8_t *emb, size_
     }
 }
 
-// Scaled RMSNorm of each row (src/ops.rs:137-149), one CTA per row.
-__global__ void rmsnorm_rows(const float *x, const float *g, float *y, int n, int w, float eps, unsigned *err) {
+// Scaled RMSNorm of each row (src/ops.rs:137-149), one CTA per row; rows of
+// up to 16 x blockDim elements stay in registers between the passes.
+__global__ void rmsnorm_rows(const float *x, const float *g, float *y, Planes P, int n, int w, float eps,
+                             unsigned *err) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ float red[32];
+    constexpr int VPT = 16;
+    const float se = sqrtf(eps);
     for (int t = blockIdx.x; t < n; t += gridDim.x) {
         const float *xr = x + (size_t)t * w;
-        const float se = sqrtf(eps);
+        float *yr = y + (size_t)t * w;
+        if (w <= (int)blockDim.x * VPT) {
+            float v[VPT];
+            float m = se;
+#pragma unroll
+            for (int k = 0; k < VPT; ++k) {
+                const int i = threadIdx.x + k * blockDim.x;
+                v[k] = i < w ? xr[i] : 0.0f;
+                if (i < w) m = rust_max(m, fabsf(v[k]));
+            }
+            m = block_max(m, red);
+            float ss = 0.0f;
+#pragma unroll
+            for (int k = 0; k < VPT; ++k) {
+                const float q = v[k] / m;
+                if (threadIdx.x + k * blockDim.x < w) ss = ss + q * q;
+            }
+            ss = block_sum(ss, red);
+            const float seps = se / m;
+            const float den = sqrtf(ss / (float)w + seps * seps);
+#pragma unroll
+            for (int k = 0; k < VPT; ++k) {
+                const int i = threadIdx.x + k * blockDim.x;
+                if (i < w) {
+                    const float o = (v[k] / m) / den * g[i];
+                    yr[i] = o;
+                    if (P.p) store_planes(P, (size_t)t * w + i, o);
+                    flag_bad(err, o);
+                }
+            }
+            continue;
+        }
         float m = se;
         for (int i = threadIdx.x; i < w; i += blockDim.x) m = rust_max(m, fabsf(xr[i]));
         m = block_max(m, red);
@@ -84,7 +117,8 @@ __global__ void rmsnorm_rows(const float *x, const float *g, float *y, int n, in
         const float den = sqrtf(ss / (float)w + seps * seps);
         for (int i = threadIdx.x; i < w; i += blockDim.x) {
             const float o = (xr[i] / m) / den * g[i];
-            y[(size_t)t * w + i] = o;
+            yr[i] = o;
+            if (P.p) store_planes(P, (size_t)t * w + i, o);
             flag_bad(err, o);
         }
     }
@@ -97,16 +131,6 @@ __global__ void rmsnorm_rows(const float *x, const float *g, float *y, int n, in
 // s (of seg_len elements) starts at base + s * seg_stride + r * row_stride,
 // so the head-blocked o_proj is one segmented matrix.  K, seg_len and every
 // leading dimension are multiples of 4.
-
-enum { EPI_QKV = 0, EPI_RESID = 1, EPI_GU = 2, EPI_PLAIN = 3 };
-
-struct GemmW {
-    const uint8_t *base;
-    size_t row_stride, seg_stride;
-    int seg_len;
-    const float *scale;  // per row (INT8) or null
-    const float *bias;   // per row (EPI_QKV) or null
-};
 
 // Four consecutive elements k .. k+3 of row r (k % 4 == 0).
 template <int WF>
@@ -124,39 +148,14 @@ __device__ __forceinline__ float4 load4(const GemmW &w, int r, int k) {
 
 constexpr int BM = 64, BN = 64, BK = 32;
 
-// The epilogue of one output (t, r) (all kinds but the SwiGLU pairs).
-template <int EPI>
-__device__ __forceinline__ void epilogue1(const GemmW &w, int t, int r, float v, const float *R, int ldr, float *Y,
-                                          int ldy, unsigned *err) {
-    if (w.scale) v = v * w.scale[r];
-    if (EPI == EPI_QKV) {
-        if (w.bias) v = v + w.bias[r];
-    } else if (EPI == EPI_RESID) {
-        v = R[(size_t)t * ldr + r] + v;
-    }
-    Y[(size_t)t * ldy + r] = v;
-    flag_bad(err, v);
-}
-
-// The SwiGLU epilogue of a (gate, up) row pair r, r + 1.
-__device__ __forceinline__ void epilogue_gu(const GemmW &w, int t, int r, float g, float u, float *Y, int ldy,
-                                            unsigned *err) {
-    if (w.scale) {
-        g = g * w.scale[r];
-        u = u * w.scale[r + 1];
-    }
-    const float a = silu_ref(g) * u;
-    Y[(size_t)t * ldy + (r >> 1)] = a;
-    flag_bad(err, g);
-    flag_bad(err, a);
-}
-
 // grid.z = ksplit slices of K (each kper elements, a multiple of BK).  With
 // ksplit > 1 the raw sums go to part[z][t][r] and reduce_epilogue finishes.
 template <int WF, int EPI>
 __global__ void __launch_bounds__(256) gemm_rows(const float *X, int ldx, int n, int N, int K, GemmW w,
-                                                 const float *R, int ldr, float *Y, int ldy, unsigned *err,
-                                                 int kper, float *part) {
+                                                 const float *R, int ldr, float *Y, int ldy, Planes P,
+                                                 unsigned *err, int kper, float *part) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ __align__(16) float Xs[BK][BM + 4];
     __shared__ __align__(16) float Ws[BK][BN + 4];
     const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
@@ -220,7 +219,7 @@ __global__ void __launch_bounds__(256) gemm_rows(const float *X, int ldx, int n,
 #pragma unroll
             for (int jj = 0; jj < 2; ++jj) {
                 const int r = n0 + tx * 4 + 2 * jj;
-                if (r + 1 < N) epilogue_gu(w, t, r, acc[i][2 * jj], acc[i][2 * jj + 1], Y, ldy, err);
+                if (r + 1 < N) epilogue_gu(w, t, r, acc[i][2 * jj], acc[i][2 * jj + 1], Y, ldy, P, err);
             }
         } else {
 #pragma unroll
@@ -228,33 +227,6 @@ __global__ void __launch_bounds__(256) gemm_rows(const float *X, int ldx, int n,
                 const int r = n0 + tx * 4 + j;
                 if (r < N) epilogue1<EPI>(w, t, r, acc[i][j], R, ldr, Y, ldy, err);
             }
-        }
-    }
-}
-
-// Sums the ksplit partials of each output in slice order, then the
-// epilogue (SwiGLU outputs one value per row pair).
-template <int EPI>
-__global__ void reduce_epilogue(const float *part, int ks, int n, int N, GemmW w, const float *R, int ldr, float *Y,
-                                int ldy, unsigned *err) {
-    const size_t per = (size_t)n * N;
-    const size_t total = EPI == EPI_GU ? per / 2 : per;
-    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
-        if (EPI == EPI_GU) {
-            const size_t t = i / (N / 2);
-            const int r = (int)(i - t * (N / 2)) * 2;
-            float g = 0.0f, u = 0.0f;
-            for (int z = 0; z < ks; ++z) {
-                g += part[z * per + t * N + r];
-                u += part[z * per + t * N + r + 1];
-            }
-            epilogue_gu(w, (int)t, r, g, u, Y, ldy, err);
-        } else {
-            const size_t t = i / N;
-            const int r = (int)(i - t * N);
-            float v = 0.0f;
-            for (int z = 0; z < ks; ++z) v += part[z * per + i];
-            epilogue1<EPI>(w, (int)t, r, v, R, ldr, Y, ldy, err);
         }
     }
 }
@@ -272,6 +244,8 @@ __device__ __forceinline__ uint8_t *kv_k(uint8_t *kv, size_t seq_bytes, size_t l
 __global__ void rope_kv(float *qkv, int n, const int *pos, const int *seqs, int l, int h, int qh, int kvh, int hd,
                         const float2 *rope, int cap, uint8_t *kv, size_t seq_bytes, size_t layer_bytes, int kv_bf16,
                         unsigned *err) {
+    pdl_trigger();
+    pdl_wait();
     const int half = hd / 2, rq = h + 2 * kvh * hd;
     for (int t = blockIdx.x; t < n; t += gridDim.x) {
         const int p = pos[t];
@@ -330,7 +304,9 @@ __device__ __forceinline__ float kv_at(const uint8_t *base, size_t idx) {
 template <int KVBF16>
 __global__ void attention_rows(const float *qkv, int n, const int *pos, const int *seqs, int l, int max_pos, int h,
                                int qh, int kvh, int hd, int group, int cap, const uint8_t *kv, size_t seq_bytes,
-                               size_t layer_bytes, float sqrt_hd, float *ctx, unsigned *err) {
+                               size_t layer_bytes, float sqrt_hd, float *ctx, Planes P, unsigned *err) {
+    pdl_trigger();
+    pdl_wait();
     extern __shared__ float asm_[];
     const int t = blockIdx.x / qh, hh = blockIdx.x - t * qh, g = hh / group, p = pos[t];
     const int rq = h + 2 * kvh * hd;
@@ -361,13 +337,187 @@ __global__ void attention_rows(const float *qkv, int n, const int *pos, const in
 #pragma unroll 4
         for (int q = 0; q <= p; ++q) acc = acc + (sc[q] / se) * kv_at<KVBF16>(vc, kv0 + (size_t)q * hd + i);
         ctx[(size_t)t * h + (size_t)hh * hd + i] = acc;
+        if (P.p) store_planes(P, (size_t)t * h + (size_t)hh * hd + i, acc);
         flag_bad(err, acc);
+    }
+}
+
+// Grouped-query attention, one CTA per (token, KV head, position split):
+// the G <= 8 query heads sharing a KV head are served by one pass over its
+// K and V rows.  Per query head, as the reference (src/kv_cache.rs:555-575):
+// scores q.k / sqrt(hd) with the dot by increasing index, softmax with the
+// maximum subtracted and each weight divided by the sum, and the context as
+// the weighted sum of V rows.  Scores: one lane per position (the K row in
+// registers, q broadcast from shared memory).  Context: each warp sums a
+// contiguous run of positions in order (one lane per hd/32 dimensions);
+// the warps' sums are added in warp order.  A split covers at most AT_SPAN
+// positions; with several splits each writes its maximum, sum and
+// unnormalized context and attn_combine merges them (rescaled by
+// exp(m_z - m)).
+constexpr int AT_THREADS = 256, AT_WARPS = AT_THREADS / 32, AT_SPAN = 1024, AT_GMAX = 8;
+
+size_t attn_gqa_smem(int G, int hd, int span) {
+    return ((size_t)G * hd + (size_t)G * span + (size_t)AT_WARPS * G * hd + 2 * AT_GMAX) * sizeof(float);
+}
+
+// Eight consecutive cache elements as FP32.
+template <int KVBF16>
+__device__ __forceinline__ void kv_load8(const uint8_t *base, size_t idx, float (&f)[8]) {
+    if (KVBF16) {
+        const uint4 v = *(const uint4 *)(base + idx * 2);
+        f[0] = bf16_lo(v.x); f[1] = bf16_hi(v.x); f[2] = bf16_lo(v.y); f[3] = bf16_hi(v.y);
+        f[4] = bf16_lo(v.z); f[5] = bf16_hi(v.z); f[6] = bf16_lo(v.w); f[7] = bf16_hi(v.w);
+    } else {
+        const float4 a = *(const float4 *)(base + idx * 4), b = *(const float4 *)(base + idx * 4 + 16);
+        f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+    }
+}
+
+template <int KVBF16, int HD>
+__global__ void __launch_bounds__(AT_THREADS)
+    attn_gqa(const float *qkv, const int *pos, const int *seqs, int l, int h, int kvh, int G, int cap,
+             const uint8_t *kv, size_t seq_bytes, size_t layer_bytes, float sqrt_hd, int span, float *ctx, Planes P,
+             float *apart, unsigned *err) {
+    pdl_trigger();
+    pdl_wait();
+    constexpr int DPL = HD / 32;  // context dimensions per lane
+    extern __shared__ float asm_[];
+    const int t = blockIdx.x, g = blockIdx.y, z = blockIdx.z, nz = gridDim.z;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int lo = z * span, cnt = max(0, min(pos[t] + 1, lo + span) - lo);
+    const int rq = h + 2 * kvh * HD;
+    float *qs = asm_, *sc = qs + G * HD, *wsum = sc + (size_t)G * span, *red = wsum + AT_WARPS * G * HD;
+    const uint8_t *kc = kv + (size_t)seqs[t] * seq_bytes + (size_t)(2 * l) * layer_bytes, *vc = kc + layer_bytes;
+    const size_t kv0 = ((size_t)g * cap + lo) * HD;
+    for (int i = tid; i < G * HD; i += AT_THREADS) qs[i] = qkv[(size_t)t * rq + (size_t)g * G * HD + i];
+    __syncthreads();
+    // Scores: lane per position.
+    for (int q = tid; q < cnt; q += AT_THREADS) {
+        float s[AT_GMAX];
+#pragma unroll
+        for (int gi = 0; gi < AT_GMAX; ++gi) s[gi] = 0.0f;
+#pragma unroll 2
+        for (int i0 = 0; i0 < HD; i0 += 8) {
+            float k8[8];
+            kv_load8<KVBF16>(kc, kv0 + (size_t)q * HD + i0, k8);
+#pragma unroll
+            for (int gi = 0; gi < AT_GMAX; ++gi) {
+                if (gi < G) {
+                    const float4 qa = *(const float4 *)(qs + gi * HD + i0);
+                    const float4 qb = *(const float4 *)(qs + gi * HD + i0 + 4);
+                    float a = s[gi];
+                    a = a + qa.x * k8[0]; a = a + qa.y * k8[1]; a = a + qa.z * k8[2]; a = a + qa.w * k8[3];
+                    a = a + qb.x * k8[4]; a = a + qb.y * k8[5]; a = a + qb.z * k8[6]; a = a + qb.w * k8[7];
+                    s[gi] = a;
+                }
+            }
+        }
+#pragma unroll
+        for (int gi = 0; gi < AT_GMAX; ++gi)
+            if (gi < G) sc[(size_t)gi * span + q] = s[gi] / sqrt_hd;
+    }
+    __syncthreads();
+    // Softmax of each head (one warp per head).
+    for (int gi = warp; gi < G; gi += AT_WARPS) {
+        float *row = sc + (size_t)gi * span;
+        float mx = -INFINITY;
+        for (int q = lane; q < cnt; q += 32) mx = rust_max(mx, row[q]);
+        for (int off = 16; off; off >>= 1) mx = rust_max(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+        float se = 0.0f;
+        for (int q = lane; q < cnt; q += 32) {
+            const float e = expf(row[q] - mx);
+            row[q] = e;
+            se += e;
+        }
+        for (int off = 16; off; off >>= 1) se += __shfl_xor_sync(0xffffffffu, se, off);
+        if (nz == 1)
+            for (int q = lane; q < cnt; q += 32) row[q] = row[q] / se;
+        if (lane == 0) {
+            red[gi] = mx;
+            red[AT_GMAX + gi] = se;
+        }
+    }
+    __syncthreads();
+    // Context: warp w sums positions [w * per, (w + 1) * per) in order.
+    float acc[AT_GMAX][DPL];
+#pragma unroll
+    for (int gi = 0; gi < AT_GMAX; ++gi)
+#pragma unroll
+        for (int d = 0; d < DPL; ++d) acc[gi][d] = 0.0f;
+    const int per = (cnt + AT_WARPS - 1) / AT_WARPS, q0 = warp * per, q1 = min(cnt, q0 + per);
+#pragma unroll 4
+    for (int q = q0; q < q1; ++q) {
+        float v[DPL];
+        const size_t at = kv0 + (size_t)q * HD + lane * DPL;
+#pragma unroll
+        for (int d = 0; d < DPL; ++d) v[d] = kv_at<KVBF16>(vc, at + d);
+#pragma unroll
+        for (int gi = 0; gi < AT_GMAX; ++gi) {
+            if (gi < G) {
+                const float w = sc[(size_t)gi * span + q];
+#pragma unroll
+                for (int d = 0; d < DPL; ++d) acc[gi][d] = acc[gi][d] + w * v[d];
+            }
+        }
+    }
+#pragma unroll
+    for (int gi = 0; gi < AT_GMAX; ++gi)
+        if (gi < G)
+#pragma unroll
+            for (int d = 0; d < DPL; ++d) wsum[((size_t)warp * G + gi) * HD + lane * DPL + d] = acc[gi][d];
+    __syncthreads();
+    for (int task = tid; task < G * HD; task += AT_THREADS) {
+        float o = wsum[task];
+        for (int w = 1; w < AT_WARPS; ++w) o = o + wsum[(size_t)w * G * HD + task];
+        const int gi = task / HD, i = task - gi * HD;
+        if (nz == 1) {
+            const size_t at = (size_t)t * h + ((size_t)g * G + gi) * HD + i;
+            ctx[at] = o;
+            if (P.p) store_planes(P, at, o);
+            flag_bad(err, o);
+        } else {
+            float *pp = apart + (((size_t)t * kvh + g) * nz + z) * G * (HD + 2) + (size_t)gi * (HD + 2);
+            pp[i] = o;
+            if (i == 0) {
+                pp[HD] = red[gi];
+                pp[HD + 1] = red[AT_GMAX + gi];
+            }
+        }
+    }
+}
+
+// Merges the position splits of attn_gqa: m = max m_z, L = sum l_z e^(m_z - m),
+// context = sum o_z e^(m_z - m) / L.  One CTA per (token, KV head).
+__global__ void attn_combine(const float *apart, int nz, int h, int kvh, int hd, int G, float *ctx, Planes P,
+                             unsigned *err) {
+    pdl_trigger();
+    pdl_wait();
+    const int t = blockIdx.x, g = blockIdx.y;
+    const float *base = apart + ((size_t)t * kvh + g) * nz * G * (hd + 2);
+    for (int task = threadIdx.x; task < G * hd; task += blockDim.x) {
+        const int gi = task / hd, i = task - gi * hd;
+        float m = -INFINITY;
+        for (int z = 0; z < nz; ++z) m = rust_max(m, base[((size_t)z * G + gi) * (hd + 2) + hd]);
+        float L = 0.0f, o = 0.0f;
+        for (int z = 0; z < nz; ++z) {
+            const float *pp = base + ((size_t)z * G + gi) * (hd + 2);
+            const float f = pp[hd + 1] > 0.0f ? expf(pp[hd] - m) : 0.0f;
+            L += pp[hd + 1] * f;
+            o += pp[i] * f;
+        }
+        const float v = o / L;
+        const size_t at = (size_t)t * h + ((size_t)g * G + gi) * hd + i;
+        ctx[at] = v;
+        if (P.p) store_planes(P, at, v);
+        flag_bad(err, v);
     }
 }
 
 // Greedy id of each logits row: strict > over increasing ids keeps the
 // lowest id among equal maxima (src/sampling.rs:65-70).
 __global__ void argmax_rows(const float *logits, int n, int V, uint32_t *out, unsigned *err) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ float bvs[32];
     __shared__ int bis[32];
     for (int t = blockIdx.x; t < n; t += gridDim.x) {
@@ -398,7 +548,30 @@ __global__ void argmax_rows(const float *logits, int n, int V, uint32_t *out, un
     }
 }
 
+// Greedy id of each token from the LM head's per-tile partials (tiles are
+// disjoint id ranges; ties keep the lowest id).  One warp per token.
+__global__ void argmax_tiles(const float *amv, const int *ami, int tiles, int n, int V, uint32_t *out) {
+    pdl_trigger();
+    pdl_wait();
+    const int t = blockIdx.x, lane = threadIdx.x;
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int k = lane; k < tiles; k += 32) {
+        const float v = amv[(size_t)k * n + t];
+        const int i = ami[(size_t)k * n + t];
+        if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
+    }
+    for (int off = 16; off; off >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    if (lane == 0) out[t] = bi >= 0 && bi < V ? (uint32_t)bi : 0u;
+}
+
 __global__ void advance_kernel(const uint32_t *amax, uint32_t *ids, int *pos, int n) {
+    pdl_trigger();
+    pdl_wait();
     for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < n; t += gridDim.x * blockDim.x) {
         ids[t] = amax[t];
         pos[t] += 1;
@@ -420,44 +593,84 @@ int choose_split(int n, int N, int K, size_t part_floats) {
 
 template <int WF, int EPI>
 cudaError_t gemm(const PrefillArgs &a, const float *X, int ldx, int n, int N, int K, const GemmW &w, const float *R,
-                 int ldr, float *Y, int ldy, cudaStream_t st) {
+                 int ldr, float *Y, int ldy, const Planes &P, cudaStream_t st) {
     const int ks = choose_split(n, N, K, a.part_floats);
     const int kper = ((K + ks - 1) / ks + BK - 1) / BK * BK;
     const int ksn = (K + kper - 1) / kper;
     dim3 grid((N + BN - 1) / BN, (n + BM - 1) / BM, ksn);
-    gemm_rows<WF, EPI><<<grid, 256, 0, st>>>(X, ldx, n, N, K, w, R, ldr, Y, ldy, a.err, kper, a.part);
+    cudaError_t e = launch_pdl(gemm_rows<WF, EPI>, grid, dim3(256), 0, st, X, ldx, n, N, K, w, R, ldr, Y, ldy, P, a.err,
+                               kper, a.part);
+    if (e != cudaSuccess) return e;
     if (ksn > 1) {
         const size_t total = (size_t)n * N / (EPI == EPI_GU ? 2 : 1);
         const unsigned blocks = (unsigned)std::min<size_t>((total + 255) / 256, 4096);
-        reduce_epilogue<EPI><<<blocks, 256, 0, st>>>(a.part, ksn, n, N, w, R, ldr, Y, ldy, a.err);
+        return launch_pdl(reduce_epilogue<EPI>, dim3(blocks), dim3(256), 0, st, a.part, ksn, n, N, w, R, ldr, Y, ldy, P,
+                          a.err);
     }
     return cudaGetLastError();
 }
 
+Planes xn_planes(const PrefillArgs &a) { return Planes{a.xnp, (size_t)a.chunk * a.h, TC_NP}; }
+Planes ctx_planes(const PrefillArgs &a) { return Planes{a.ctxp, (size_t)a.chunk * a.h, TC_NP}; }
+Planes act_planes(const PrefillArgs &a) { return Planes{a.actp, (size_t)a.chunk * a.ff, TC_NP}; }
+
+// The four GEMMs of a layer: 0 QKV (+ bias), 1 o_proj (head-blocked K) +
+// residual, 2 (gate, up) pairs -> SwiGLU, 3 down + residual.
 template <int WF>
 cudaError_t layer_gemm(int which, const PrefillArgs &a, const DecodeLayer &Ly, int n, cudaStream_t st) {
     const int kv = a.kvh * a.hd, rq = a.h + 2 * kv;
+    const Planes none{nullptr, 0, TC_NP};
     switch (which) {
-    case 0: {  // QKV (+ bias)
+    case 0: {
         GemmW w{Ly.wqkv, a.sh, 0, a.h, Ly.sqkv, Ly.bqkv};
-        return gemm<WF, EPI_QKV>(a, a.xn, a.h, n, rq, a.h, w, nullptr, 0, a.qkv, rq, st);
+        return gemm<WF, EPI_QKV>(a, a.xn, a.h, n, rq, a.h, w, nullptr, 0, a.qkv, rq, none, st);
     }
-    case 1: {  // o_proj (head-blocked K) + residual
+    case 1: {
         GemmW w{Ly.wo, a.shd, (size_t)a.h * a.shd, a.hd, Ly.so, nullptr};
-        return gemm<WF, EPI_RESID>(a, a.ctx, a.h, n, a.h, a.qh * a.hd, w, a.x, a.h, a.h2, a.h, st);
+        return gemm<WF, EPI_RESID>(a, a.ctx, a.h, n, a.h, a.qh * a.hd, w, a.x, a.h, a.h2, a.h, none, st);
     }
-    case 2: {  // (gate, up) pairs -> SwiGLU
+    case 2: {
         GemmW w{Ly.wgu, a.sh, 0, a.h, Ly.sgu, nullptr};
-        return gemm<WF, EPI_GU>(a, a.xn, a.h, n, 2 * a.ff, a.h, w, nullptr, 0, a.act, a.ff, st);
+        return gemm<WF, EPI_GU>(a, a.xn, a.h, n, 2 * a.ff, a.h, w, nullptr, 0, a.act, a.ff, act_planes(a), st);
     }
-    default: {  // down + residual
+    default: {
         GemmW w{Ly.wd, a.sff, 0, a.ff, Ly.sd, nullptr};
-        return gemm<WF, EPI_RESID>(a, a.act, a.ff, n, a.h, a.ff, w, a.h2, a.h, a.x, a.h, st);
+        return gemm<WF, EPI_RESID>(a, a.act, a.ff, n, a.h, a.ff, w, a.h2, a.h, a.x, a.h, none, st);
     }
     }
 }
 
-cudaError_t run_gemm(int which, const PrefillArgs &a, const DecodeLayer &Ly, int n, cudaStream_t st) {
+// The same GEMMs on the tensor cores (weights in the layer's tensor maps,
+// inputs as BF16 planes).
+cudaError_t layer_gemm_tc(int which, const PrefillArgs &a, int l, int n, cudaStream_t st) {
+    const DecodeLayer &Ly = a.layers[l];
+    const TcLayerMaps &M = a.tc->layers[l];
+    const int kv = a.kvh * a.hd, rq = a.h + 2 * kv;
+    const Planes none{nullptr, 0, TC_NP};
+    TcJob j;
+    switch (which) {
+    case 0:
+        j = TcJob{EPI_QKV, n, rq, a.h, &M.qkv, &a.tc->xn, GemmW{nullptr, 0, 0, 0, Ly.sqkv, Ly.bqkv},
+                  nullptr, 0, a.qkv, rq, none};
+        break;
+    case 1:
+        j = TcJob{EPI_RESID, n, a.h, a.qh * a.hd, &M.o, &a.tc->ctx, GemmW{nullptr, 0, 0, 0, Ly.so, nullptr},
+                  a.x, a.h, a.h2, a.h, none};
+        break;
+    case 2:
+        j = TcJob{EPI_GU, n, 2 * a.ff, a.h, &M.gu, &a.tc->xn, GemmW{nullptr, 0, 0, 0, Ly.sgu, nullptr},
+                  nullptr, 0, a.act, a.ff, act_planes(a)};
+        break;
+    default:
+        j = TcJob{EPI_RESID, n, a.h, a.ff, &M.down, &a.tc->act, GemmW{nullptr, 0, 0, 0, Ly.sd, nullptr},
+                  a.h2, a.h, a.x, a.h, none};
+    }
+    return tc_gemm(j, a.err, st);
+}
+
+cudaError_t run_gemm(int which, const PrefillArgs &a, int l, int n, cudaStream_t st) {
+    if (a.tc && !a.tc->layers.empty()) return layer_gemm_tc(which, a, l, n, st);
+    const DecodeLayer &Ly = a.layers[l];
     if (a.wfmt == WF_I8) return layer_gemm<WF_I8>(which, a, Ly, n, st);
     if (a.wfmt == WF_BF16) return layer_gemm<WF_BF16>(which, a, Ly, n, st);
     return layer_gemm<WF_F32>(which, a, Ly, n, st);
@@ -465,11 +678,65 @@ cudaError_t run_gemm(int which, const PrefillArgs &a, const DecodeLayer &Ly, int
 
 size_t attention_smem(const PrefillArgs &a, int max_pos) { return ((size_t)a.hd + max_pos + 1 + 32) * sizeof(float); }
 
+bool gqa_supported(const PrefillArgs &a) { return a.group <= AT_GMAX && (a.hd == 64 || a.hd == 128); }
+
+// Position splits for the grouped-query kernel: enough that one split
+// covers at most AT_SPAN positions, more (each at least 256 positions) while
+// the (token, KV head) pairs leave SMs idle, bounded by the partial buffer.
+int attention_splits(const PrefillArgs &a, int n, int max_pos, int *span) {
+    const int len = max_pos + 1;
+    int nz = (len + AT_SPAN - 1) / AT_SPAN;
+    const int want = (2 * 148 + n * a.kvh - 1) / (n * a.kvh);
+    nz = std::max(nz, std::min(want, (len + 255) / 256));
+    const size_t per = (size_t)a.group * (a.hd + 2);
+    while (nz > 1 && (size_t)n * a.kvh * nz * per > a.apart_floats) --nz;
+    int sp = (len + nz - 1) / nz;
+    sp = (sp + 63) / 64 * 64;
+    *span = sp;
+    return (len + sp - 1) / sp;
+}
+
+cudaError_t attention(const PrefillArgs &a, int n, int l, int max_pos, cudaStream_t st) {
+    if (gqa_supported(a) && a.apart) {
+        int span = 0;
+        const int nz = attention_splits(a, n, max_pos, &span);
+        if (span <= AT_SPAN) {
+            const size_t sm = attn_gqa_smem(a.group, a.hd, span);
+            static int configured[4] = {0, 0, 0, 0};
+            const int which = a.kv_bf16 * 2 + (a.hd == 128);
+            auto kern = which == 3 ? attn_gqa<1, 128> : which == 2 ? attn_gqa<1, 64>
+                      : which == 1 ? attn_gqa<0, 128> : attn_gqa<0, 64>;
+            if (!configured[which]) {
+                cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                     (int)attn_gqa_smem(AT_GMAX, 128, AT_SPAN));
+                if (e != cudaSuccess) return e;
+                configured[which] = 1;
+            }
+            cudaError_t e = launch_pdl(kern, dim3(n, a.kvh, nz), dim3(AT_THREADS), sm, st, a.qkv, a.pos, a.seq, l, a.h,
+                                       a.kvh, a.group, a.cap, a.kv, a.kv_seq_bytes, a.kv_layer_bytes, a.sqrt_hd, span,
+                                       a.ctx, ctx_planes(a), a.apart, a.err);
+            if (e != cudaSuccess) return e;
+            if (nz > 1)
+                return launch_pdl(attn_combine, dim3(n, a.kvh), dim3(128), 0, st, a.apart, nz, a.h, a.kvh, a.hd,
+                                  a.group, a.ctx, ctx_planes(a), a.err);
+            return cudaSuccess;
+        }
+    }
+    const size_t sm = attention_smem(a, max_pos);
+    if (a.kv_bf16)
+        return launch_pdl(attention_rows<1>, dim3(n * a.qh), dim3(128), sm, st, a.qkv, n, a.pos, a.seq, l, max_pos,
+                          a.h, a.qh, a.kvh, a.hd, a.group, a.cap, a.kv, a.kv_seq_bytes, a.kv_layer_bytes, a.sqrt_hd,
+                          a.ctx, ctx_planes(a), a.err);
+    return launch_pdl(attention_rows<0>, dim3(n * a.qh), dim3(128), sm, st, a.qkv, n, a.pos, a.seq, l, max_pos, a.h,
+                      a.qh, a.kvh, a.hd, a.group, a.cap, a.kv, a.kv_seq_bytes, a.kv_layer_bytes, a.sqrt_hd, a.ctx,
+                      ctx_planes(a), a.err);
+}
+
 }  // namespace
 
 bool prefill_supported(const PrefillArgs &a) {
     if (a.chunk < 1 || a.h % 4 || a.ff % 4 || a.hd % 4 || a.hd < 2) return false;
-    return attention_smem(a, a.cap - 1) <= 48 * 1024;
+    return gqa_supported(a) || attention_smem(a, a.cap - 1) <= 48 * 1024;
 }
 
 cudaError_t forward_tokens(const PrefillArgs &a, int n, int max_pos, bool lm_head, cudaStream_t st) {
@@ -480,40 +747,48 @@ cudaError_t forward_tokens(const PrefillArgs &a, int n, int max_pos, bool lm_hea
     cudaError_t e = cudaGetLastError();
     for (int l = 0; l < a.L && e == cudaSuccess; ++l) {
         const DecodeLayer &Ly = a.layers[l];
-        rmsnorm_rows<<<rows_grid, 256, 0, st>>>(a.x, Ly.attn_norm, a.xn, n, a.h, a.eps, a.err);
-        if ((e = run_gemm(0, a, Ly, n, st)) != cudaSuccess) break;
-        rope_kv<<<rows_grid, 128, 0, st>>>(a.qkv, n, a.pos, a.seq, l, a.h, a.qh, a.kvh, a.hd, a.rope, a.cap, a.kv,
-                                           a.kv_seq_bytes, a.kv_layer_bytes, a.kv_bf16, a.err);
-        const size_t sm = attention_smem(a, max_pos);
-        if (a.kv_bf16)
-            attention_rows<1><<<n * a.qh, 128, sm, st>>>(a.qkv, n, a.pos, a.seq, l, max_pos, a.h, a.qh, a.kvh, a.hd,
-                                                         a.group, a.cap, a.kv, a.kv_seq_bytes, a.kv_layer_bytes,
-                                                         a.sqrt_hd, a.ctx, a.err);
-        else
-            attention_rows<0><<<n * a.qh, 128, sm, st>>>(a.qkv, n, a.pos, a.seq, l, max_pos, a.h, a.qh, a.kvh, a.hd,
-                                                         a.group, a.cap, a.kv, a.kv_seq_bytes, a.kv_layer_bytes,
-                                                         a.sqrt_hd, a.ctx, a.err);
+        if ((e = launch_pdl(rmsnorm_rows, dim3(rows_grid), dim3(256), 0, st, a.x, Ly.attn_norm, a.xn, xn_planes(a), n,
+                            a.h, a.eps, a.err)) != cudaSuccess)
+            break;
+        if ((e = run_gemm(0, a, l, n, st)) != cudaSuccess) break;
+        if ((e = launch_pdl(rope_kv, dim3(rows_grid), dim3(128), 0, st, a.qkv, n, a.pos, a.seq, l, a.h, a.qh, a.kvh,
+                            a.hd, a.rope, a.cap, a.kv, a.kv_seq_bytes, a.kv_layer_bytes, a.kv_bf16, a.err)) !=
+            cudaSuccess)
+            break;
+        if ((e = attention(a, n, l, max_pos, st)) != cudaSuccess) break;
         if ((e = cudaGetLastError()) != cudaSuccess) break;
         if (l + 1 == a.L && !lm_head) break;  // the last layer's MLP feeds only the logits
-        if ((e = run_gemm(1, a, Ly, n, st)) != cudaSuccess) break;
-        rmsnorm_rows<<<rows_grid, 256, 0, st>>>(a.h2, Ly.ffn_norm, a.xn, n, a.h, a.eps, a.err);
-        if ((e = run_gemm(2, a, Ly, n, st)) != cudaSuccess) break;
-        if ((e = run_gemm(3, a, Ly, n, st)) != cudaSuccess) break;
+        if ((e = run_gemm(1, a, l, n, st)) != cudaSuccess) break;
+        if ((e = launch_pdl(rmsnorm_rows, dim3(rows_grid), dim3(256), 0, st, a.h2, Ly.ffn_norm, a.xn, xn_planes(a),
+                            n, a.h, a.eps, a.err)) != cudaSuccess)
+            break;
+        if ((e = run_gemm(2, a, l, n, st)) != cudaSuccess) break;
+        if ((e = run_gemm(3, a, l, n, st)) != cudaSuccess) break;
     }
     if (e != cudaSuccess || !lm_head) return e;
     // Final norm, the LM head (tied table or untied head) and the argmax.
-    rmsnorm_rows<<<rows_grid, 256, 0, st>>>(a.x, a.final_norm, a.xn, n, a.h, a.eps, a.err);
-    GemmW w{a.head, a.semb, 0, a.h, nullptr, nullptr};
-    if (a.tfmt == WF_BF16) e = gemm<WF_BF16, EPI_PLAIN>(a, a.xn, a.h, n, a.V, a.h, w, nullptr, 0, a.logits, a.V, st);
-    else e = gemm<WF_F32, EPI_PLAIN>(a, a.xn, a.h, n, a.V, a.h, w, nullptr, 0, a.logits, a.V, st);
+    e = launch_pdl(rmsnorm_rows, dim3(rows_grid), dim3(256), 0, st, a.x, a.final_norm, a.xn, xn_planes(a), n, a.h,
+                   a.eps, a.err);
     if (e != cudaSuccess) return e;
-    argmax_rows<<<rows_grid, 256, 0, st>>>(a.logits, n, a.V, a.amax, a.err);
-    return cudaGetLastError();
+    const Planes none{nullptr, 0, TC_NP};
+    GemmW w{a.head, a.semb, 0, a.h, nullptr, nullptr};
+    int am_tiles = 0;
+    if (a.tc && a.tc->head.wf >= 0) {
+        const TcJob j{EPI_PLAIN, n, a.V, a.h, &a.tc->head, &a.tc->xn, w, nullptr, 0, a.logits, a.V, none,
+                      a.amv, a.ami};
+        e = tc_gemm(j, a.err, st, &am_tiles);
+    } else if (a.tfmt == WF_BF16) {
+        e = gemm<WF_BF16, EPI_PLAIN>(a, a.xn, a.h, n, a.V, a.h, w, nullptr, 0, a.logits, a.V, none, st);
+    } else {
+        e = gemm<WF_F32, EPI_PLAIN>(a, a.xn, a.h, n, a.V, a.h, w, nullptr, 0, a.logits, a.V, none, st);
+    }
+    if (e != cudaSuccess) return e;
+    if (am_tiles > 0) return launch_pdl(argmax_tiles, dim3(n), dim3(32), 0, st, a.amv, a.ami, am_tiles, n, a.V, a.amax);
+    return launch_pdl(argmax_rows, dim3(rows_grid), dim3(256), 0, st, a.logits, n, a.V, a.amax, a.err);
 }
 
 cudaError_t advance_tokens(const PrefillArgs &a, int n, cudaStream_t st) {
-    advance_kernel<<<(n + 255) / 256, 256, 0, st>>>(a.amax, a.ids, a.pos, n);
-    return cudaGetLastError();
+    return launch_pdl(advance_kernel, dim3((n + 255) / 256), dim3(256), 0, st, a.amax, a.ids, a.pos, n);
 }
 
 cudaError_t prefill_kv(const PrefillArgs &a, const uint32_t *tokens, int n, int p0, cudaStream_t st,

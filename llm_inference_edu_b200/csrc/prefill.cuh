@@ -10,6 +10,8 @@
 
 namespace qb {
 
+struct TcMaps;
+
 // Everything the multi-token kernels read or write (device pointers unless
 // noted).  The layer table is a host copy of a DecodeLayer array whose
 // weights are in the decode layout; its KV pointers are ignored: the cache
@@ -43,6 +45,17 @@ struct PrefillArgs {
     float *logits;                // [chunk][V] (null unless the LM head runs)
     uint32_t *amax;               // [chunk] greedy ids (null unless the LM head runs)
     unsigned *err;                // error flags (ERR_NONFINITE)
+    // Tensor-core path: BF16 planes [TC_NP][chunk][K] of the GEMM inputs
+    // (normalized rows, attention context, SwiGLU output) and the tensor
+    // maps (HOST; null: every GEMM runs on the CUDA cores).
+    uint16_t *xnp, *ctxp, *actp;
+    const TcMaps *tc;
+    // Attention position-split partials (apart_floats floats) and the LM
+    // head's per-tile greedy partials ([ceil(V / 128)][chunk]).
+    float *apart;
+    size_t apart_floats;
+    float *amv;
+    int *ami;
 };
 
 // True when the shapes suit the multi-token kernels (else callers evaluate

@@ -19,6 +19,7 @@
 #include "common.cuh"
 #include "decode.cuh"
 #include "prefill.cuh"
+#include "tc_gemm.cuh"
 
 namespace qb {
 int decode_max_ctas(int wfmt, int tfmt, int kv_bf16, size_t smem);
@@ -281,6 +282,7 @@ struct Session {
     DecodeCtrl *hctrl = nullptr;  // pinned mirror
     std::vector<DecodeLayer> hlayers;  // host copy of the layer table (chunked prompt path)
     DevBuf pf;                         // chunked prompt workspace (allocated on first use)
+    std::unique_ptr<TcMaps> tcm;       // its tensor maps (built with it)
     DecodeParams params{};
     int grid = 0;
     cudaGraphExec_t g_host = nullptr;
@@ -345,13 +347,22 @@ static void prefill_common(const Model &m, size_t cap, int kv_bf16, PrefillArgs 
 
 // Carves the multi-token workspace for `chunk` rows out of one buffer
 // (allocated on first use): activations, split-K partials, ids, positions,
-// sequences and the error word.
+// sequences, the error word and the BF16 input planes of the tensor-core
+// GEMMs.
 static uint32_t prefill_workspace(const Model &m, int chunk, DevBuf &ws, PrefillArgs &a) {
     const size_t h = m.c.hidden_dim, ff = m.c.ff_dim, rq = h + 2 * m.kv(), ch = (size_t)chunk;
     const size_t part = 4 * ch * std::max(rq, h);
     const size_t floats = ch * (4 * h + rq + ff) + part + 3 * ch + 64;
+    const size_t fbytes = round16(floats * 4);
+    const size_t hp = round16((size_t)TC_NP * ch * h * 2), fp = round16((size_t)TC_NP * ch * ff * 2);
+    // Attention split partials: every row's full-length splits plus room for
+    // the extra splits of small row counts; greedy partials per 128-row tile.
+    const size_t kvh = m.c.kv_heads, grp = m.c.query_heads / kvh, hd = m.c.head_dim;
+    const size_t apart = (ch * kvh * ((a.cap + 1023) / 1024) + 600) * grp * (hd + 2);
+    const size_t am = ((m.c.vocab_size + 127) / 128) * ch;
+    const size_t abytes = round16(apart * 4), ambytes = round16(am * 4);
     if (!ws.p) {
-        uint32_t st = ws.alloc(floats * 4);
+        uint32_t st = ws.alloc(fbytes + 2 * hp + fp + abytes + 2 * ambytes);
         if (st) return st;
     }
     float *f = ws.as<float>();
@@ -360,7 +371,44 @@ static uint32_t prefill_workspace(const Model &m, int chunk, DevBuf &ws, Prefill
     a.qkv = a.ctx + ch * h; a.act = a.qkv + ch * rq; a.part = a.act + ch * ff; a.part_floats = part;
     a.ids = (uint32_t *)(a.part + part); a.pos = (int *)(a.ids + ch); a.seq = a.pos + ch;
     a.err = (unsigned *)(a.seq + ch);
+    uint8_t *pl = ws.as<uint8_t>() + fbytes;
+    a.xnp = (uint16_t *)pl;
+    a.ctxp = (uint16_t *)(pl + hp);
+    a.actp = (uint16_t *)(pl + 2 * hp);
+    a.apart = (float *)(pl + 2 * hp + fp);
+    a.apart_floats = apart;
+    a.amv = (float *)(pl + 2 * hp + fp + abytes);
+    a.ami = (int *)(pl + 2 * hp + fp + abytes + ambytes);
     return QB_OK;
+}
+
+// Tensor maps of the tensor-core GEMMs over this workspace: the linears when
+// they are INT8 (per-row scales) or BF16 and every shape suits TMA, the LM
+// head when its table is BF16.  What is not covered runs on the CUDA cores.
+static void tc_prepare(const Model &m, PrefillArgs &a, TcMaps &maps) {
+    a.tc = nullptr;
+    maps.layers.clear();
+    maps.head.wf = -1;
+    if (!tc_encode_planes(maps.xn, a.xnp, a.h, a.chunk) || !tc_encode_planes(maps.ctx, a.ctxp, a.h, a.chunk) ||
+        !tc_encode_planes(maps.act, a.actp, a.ff, a.chunk) || a.qh * a.hd != a.h)
+        return;
+    const int wf = m.wf();
+    if (wf == WF_I8 || wf == WF_BF16) {
+        const size_t h = a.h, ff = a.ff, rq = h + 2 * (size_t)a.kvh * a.hd;
+        maps.layers.resize(a.L);
+        bool ok = true;
+        for (int l = 0; l < a.L && ok; ++l) {
+            const DecodeLayer &Ly = a.layers[l];
+            TcLayerMaps &M = maps.layers[l];
+            ok = tc_encode_weight(M.qkv, Ly.wqkv, wf, rq, h, a.sh, 1, 0) &&
+                 tc_encode_weight(M.o, Ly.wo, wf, h, a.hd, a.shd, a.qh, h * a.shd) &&
+                 tc_encode_weight(M.gu, Ly.wgu, wf, 2 * ff, h, a.sh, 1, 0) &&
+                 tc_encode_weight(M.down, Ly.wd, wf, h, ff, a.sff, 1, 0);
+        }
+        if (!ok) maps.layers.clear();
+    }
+    if (a.tfmt == WF_BF16) tc_encode_weight(maps.head, a.head, WF_BF16, a.V, a.h, a.semb, 1, 0);
+    a.tc = &maps;
 }
 
 static uint32_t session_build(Session &s) {
@@ -623,6 +671,11 @@ static uint32_t session_prefill_chunked(Session &s, const uint32_t *tokens, size
     if (!prefill_supported(a)) return QB_UNSUPPORTED;
     uint32_t st = prefill_workspace(m, kPrefillChunk, s.pf, a);
     if (st) return st;
+    if (!s.tcm) {
+        s.tcm.reset(new TcMaps());
+        tc_prepare(m, a, *s.tcm);
+    }
+    a.tc = s.tcm.get();
     bool bad = false;
     cudaError_t e = prefill_kv(a, tokens, (int)n, (int)s.processed, s.stream, &bad);
     if (e != cudaSuccess) return session_fail(s, cuda_status(e));
@@ -683,6 +736,7 @@ struct Batch {
     cudaStream_t stream = nullptr;
     DevBuf kv, rope, ws, logits, amax, hist;
     std::vector<DecodeLayer> hlayers;
+    TcMaps tcm;
     PrefillArgs a{};
     bool logits_valid = false;
     ~Batch() {
@@ -1382,6 +1436,7 @@ uint32_t qb_batch_create(uint64_t model, size_t sequences, size_t capacity, uint
     b->hlayers.resize(m->c.layers);
     QB_CUDA(cudaMemcpy(b->hlayers.data(), m->dlayers.p, m->c.layers * sizeof(DecodeLayer), cudaMemcpyDeviceToHost));
     a.layers = b->hlayers.data();
+    tc_prepare(*m, a, b->tcm);
     a.rope = b->rope.as<float2>();
     a.kv = b->kv.as<uint8_t>();
     a.logits = b->logits.as<float>();
