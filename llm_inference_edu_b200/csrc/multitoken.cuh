@@ -72,13 +72,20 @@ struct Planes {
     int np;
 };
 
+// FP32 -> BF16, round to nearest even (the hardware conversion).
+__device__ __forceinline__ uint16_t bf16_rn(float x) {
+    uint16_t r;
+    asm("cvt.rn.bf16.f32 %0, %1;" : "=h"(r) : "f"(x));
+    return r;
+}
+
 __device__ __forceinline__ void store_planes(const Planes &P, size_t i, float v) {
-    const uint16_t b0 = f32_to_bf16_rne(v);
+    const uint16_t b0 = bf16_rn(v);
     const float r0 = v - bf16_to_f32(b0);
-    const uint16_t b1 = f32_to_bf16_rne(r0);
+    const uint16_t b1 = bf16_rn(r0);
     P.p[i] = b0;
     P.p[P.plane + i] = b1;
-    if (P.np > 2) P.p[2 * P.plane + i] = f32_to_bf16_rne(r0 - bf16_to_f32(b1));
+    if (P.np > 2) P.p[2 * P.plane + i] = bf16_rn(r0 - bf16_to_f32(b1));
 }
 
 // The epilogue of one output (t, r) (all kinds but the SwiGLU pairs).

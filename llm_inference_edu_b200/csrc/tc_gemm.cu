@@ -173,20 +173,62 @@ __device__ __forceinline__ void u8x4_to_bf16x4(uint32_t w, uint32_t &lo, uint32_
     hi = __byte_perm(__float_as_uint(f2), __float_as_uint(f3), 0x7632u);
 }
 
-// Row-wise epilogue of output (t, r) = v (the lanes of a warp hold 32
-// consecutive rows r of one token t; SwiGLU pairs neighbouring lanes).
+// Row-wise epilogue of outputs (t + k, r) = v[k], k < cnt (the lanes of a
+// warp hold 32 consecutive rows r; SwiGLU pairs neighbouring lanes).  Four
+// tokens at a time, their loads issued before any store, for ILP.  The
+// arithmetic is epilogue1 / epilogue_gu's.
 template <int EPI>
-__device__ __forceinline__ void epi_row(const TcArgs &g, int t, int r, float v, int lane) {
+__device__ __forceinline__ void epi_rows4(const TcArgs &g, int t, int r, const float (&v)[4], int cnt, int lane) {
+    const bool rv = r < g.N;
     if (EPI == EPI_GU) {
-        const float u = __shfl_down_sync(0xffffffffu, v, 1);
-        if (!(lane & 1) && r + 1 < g.N) epilogue_gu(g.w, t, r, v, u, g.Y, g.ldy, g.P, g.err);
-    } else if (r < g.N) {
-        epilogue1<EPI>(g.w, t, r, v, g.R, g.ldr, g.Y, g.ldy, g.err);
+        float u[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) u[k] = __shfl_down_sync(0xffffffffu, v[k], 1);
+        if (!(lane & 1) && r + 1 < g.N) {
+            const float sg = g.w.scale ? g.w.scale[r] : 1.0f, su = g.w.scale ? g.w.scale[r + 1] : 1.0f;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                if (k >= cnt) break;
+                float gg = v[k], uu = u[k];
+                if (g.w.scale) {
+                    gg = gg * sg;
+                    uu = uu * su;
+                }
+                const float a = silu_ref(gg) * uu;
+                const size_t i = (size_t)(t + k) * g.ldy + (r >> 1);
+                g.Y[i] = a;
+                if (g.P.p) store_planes(g.P, i, a);
+                flag_bad(g.err, gg);
+                flag_bad(g.err, a);
+            }
+        }
+    } else if (rv) {
+        float rr[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        if (EPI == EPI_RESID) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                if (k < cnt) rr[k] = g.R[(size_t)(t + k) * g.ldr + r];
+        }
+        const float sc = g.w.scale ? g.w.scale[r] : 1.0f;
+        const float b = EPI == EPI_QKV && g.w.bias ? g.w.bias[r] : 0.0f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            if (k >= cnt) break;
+            float x = v[k];
+            if (g.w.scale) x = x * sc;
+            if (EPI == EPI_QKV) {
+                if (g.w.bias) x = x + b;
+            } else if (EPI == EPI_RESID) {
+                x = rr[k] + x;
+            }
+            g.Y[(size_t)(t + k) * g.ldy + r] = x;
+            flag_bad(g.err, x);
+        }
     }
 }
 
 template <int WF, int EPI>
-__global__ void __launch_bounds__(TC_THREADS, 1)
+__global__ void __launch_bounds__(TC_THREADS, 2)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx, const TcArgs g) {
     extern __shared__ uint8_t tc_raw[];
     uint8_t *base = (uint8_t *)(((uintptr_t)tc_raw + 1023) & ~(uintptr_t)1023);
@@ -340,28 +382,41 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     for (int j = 0; j < tn; ++j) red[(c + j) * TC_BM + ct] = tile[j * 33 + lane];
                 } else {
 #pragma unroll 1
-                    for (int j = 0; j < tn; ++j) {
-                        const float v = tile[j * 33 + lane];
-                        epi_row<EPI>(g, t0 + c + j, r, v, lane);
+                    for (int j = 0; j < tn; j += 4) {
+                        float v[4];
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) v[k] = tile[min(j + k, 15) * 33 + lane];
+                        const int cnt = min(4, tn - j);
+                        epi_rows4<EPI>(g, t0 + c + j, r, v, cnt, lane);
                         if (am) {
-                            // The warp's greedy row for this token: strict >,
+                            // The warp's greedy row for each token: strict >,
                             // lowest id on ties (a NaN never wins; it is
                             // flagged by the epilogue).
-                            float bv = r < g.N && v == v ? v : -INFINITY;
-                            int bi = r < g.N && v == v ? r : 0x7fffffff;
+                            float bv[4];
+                            int bi[4];
 #pragma unroll
-                            for (int off = 16; off; off >>= 1) {
-                                const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
-                                const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
-                                if (ov > bv || (ov == bv && oi < bi)) {
-                                    bv = ov;
-                                    bi = oi;
+                            for (int k = 0; k < 4; ++k) {
+                                bv[k] = r < g.N && v[k] == v[k] ? v[k] : -INFINITY;
+                                bi[k] = r < g.N && v[k] == v[k] ? r : 0x7fffffff;
+                            }
+#pragma unroll
+                            for (int off = 16; off; off >>= 1)
+#pragma unroll
+                                for (int k = 0; k < 4; ++k) {
+                                    const float ov = __shfl_xor_sync(0xffffffffu, bv[k], off);
+                                    const int oi = __shfl_xor_sync(0xffffffffu, bi[k], off);
+                                    if (ov > bv[k] || (ov == bv[k] && oi < bi[k])) {
+                                        bv[k] = ov;
+                                        bi[k] = oi;
+                                    }
                                 }
-                            }
-                            if (lane == 0) {
-                                s_amv[q * NT + c + j] = bv;
-                                s_ami[q * NT + c + j] = bi;
-                            }
+                            if (lane == 0)
+#pragma unroll
+                                for (int k = 0; k < 4; ++k)
+                                    if (k < cnt) {
+                                        s_amv[q * NT + c + j + k] = bv[k];
+                                        s_ami[q * NT + c + j + k] = bi[k];
+                                    }
                         }
                     }
                 }
@@ -398,12 +453,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             const bool run = __all_sync(0xffffffffu, !*abort_);
             const int tn = min(NT, g.n - t0), ks = (int)gridDim.y, tper = (tn + ks - 1) / ks;
             const uint32_t mine = smem_addr(red);
+            const int j1 = min(tn, (z + 1) * tper);
 #pragma unroll 1
-            for (int j = z * tper; j < min(tn, (z + 1) * tper); ++j) {
-                float v = 0.0f;
+            for (int j = z * tper; j < j1; j += 4) {
+                float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll 1
-                for (int zz = 0; zz < ks; ++zz) v += ld_dsmem_f32(mapa_rank(mine + (uint32_t)(j * TC_BM + ct) * 4u, zz));
-                if (run) epi_row<EPI>(g, t0 + j, r, v, lane);
+                for (int zz = 0; zz < ks; ++zz)
+#pragma unroll
+                    for (int k = 0; k < 4; ++k)
+                        if (j + k < j1) v[k] += ld_dsmem_f32(mapa_rank(mine + (uint32_t)((j + k) * TC_BM + ct) * 4u, zz));
+                if (run) epi_rows4<EPI>(g, t0 + j, r, v, min(4, j1 - j), lane);
             }
         }
         // No CTA may exit while another still reads its shared memory.
@@ -528,15 +587,22 @@ cudaError_t tc_gemm(const TcJob &j, unsigned *err, cudaStream_t st, int *am_tile
     const int nt = j.n <= 80 ? (j.n + 15) / 16 * 16 : 64;
     const int ttiles = (j.n + nt - 1) / nt, rtiles = (j.N + TC_BM - 1) / TC_BM;
     const int nkb = (j.K + TC_BK - 1) / TC_BK;
-    // Split K (clusters of up to 8 CTAs) while the output tiles leave SMs
-    // idle, staying in one wave and keeping at least two K blocks a split.
+    // Two CTAs per SM when two or more stages fit in half the shared memory
+    // (one CTA's conversion and epilogue then overlap the other's copies),
+    // else one CTA with up to eight stages.
+    const size_t per = tc_stage_bytes(j.w->wf, nt);
+    int stages = (int)std::min<size_t>(8, (112 * 1024 - tc_fixed_bytes(nt, 8)) / per), slots = 2 * 148;
+    if (stages < 2) {
+        stages = (int)std::min<size_t>(8, std::max<size_t>(2, (227 * 1024 - tc_fixed_bytes(nt, 8)) / per));
+        slots = 148;
+    }
+    // Split K (clusters of up to 8 CTAs) while the output tiles leave CTA
+    // slots idle, staying in one wave and keeping at least two K blocks a
+    // split.
     int ks = 1;
-    while (rtiles * ttiles * ks * 2 <= 148 && nkb >= ks * 2 * 2 && ks * 2 <= 8) ks *= 2;
+    while (rtiles * ttiles * ks * 2 <= slots && nkb >= ks * 2 * 2 && ks * 2 <= 8) ks *= 2;
     const int kb_per = (nkb + ks - 1) / ks;
     ks = (nkb + kb_per - 1) / kb_per;
-    const size_t per = tc_stage_bytes(j.w->wf, nt);
-    const int stages =
-        (int)std::min<size_t>(8, std::max<size_t>(2, (227 * 1024 - tc_fixed_bytes(nt, 8)) / per));
     const bool am = j.epi == EPI_PLAIN && j.amv && j.ami && ks == 1;
     TcArgs g{j.n, j.N, nkb, kb_per, nt, stages, j.w->seg_kb, j.gw, j.R, j.ldr, j.Y, j.ldy, j.P, err,
              am ? j.amv : nullptr, am ? j.ami : nullptr};
