@@ -660,9 +660,40 @@ __device__ __forceinline__ float kv_load(const uint8_t *base, size_t idx) {
 // V at `pos`.  Scores keep the reference's order (q.k summed by increasing
 // index, then divided by sqrt(hd)); softmax subtracts the maximum and
 // divides by the sum.
+// Per-head barrier of the attention splits: every split has written its
+// partial before any reads them (release/acquire like the grid barrier;
+// bounded by the timeout).  Returns false when aborting.
+__device__ __forceinline__ bool head_barrier(const DecodeParams &p, int hh, unsigned target, volatile int *s_abort) {
+    csync();
+    if (threadIdx.x == 0) {
+        red_release_add_u32(p.hbar + hh, 1u);
+        if (ld_acquire_u32(p.hbar + hh) < target) {
+            const uint64_t t0 = globaltimer_ns();
+            unsigned spins = 0;
+            while (ld_acquire_u32(p.hbar + hh) < target) {
+                if ((++spins & 63u) == 0) {
+                    if ((*(volatile unsigned *)&p.ctrl->error & ERR_TIMEOUT) || globaltimer_ns() - t0 > p.timeout_ns) {
+                        atomicOr(&p.ctrl->error, ERR_TIMEOUT);
+                        *s_abort = 1;
+                        break;
+                    }
+                }
+            }
+        }
+    }
+    csync();
+    return *s_abort == 0;
+}
+
+// Attention of query head hh over positions [lo, hi) of 0..pos.  Without a
+// split (lo = 0, hi = pos + 1) the weights are divided by the sum and the
+// context lands in xs.  With a split (vectorised layouts only) the warps'
+// unnormalized context sums stay in red[2 NW + w hd + i], with the maximum
+// at red[2 NW + NW hd] and the sum after it, for split_exchange.
 template <int WF, int KVBF16>
 __device__ __forceinline__ void attention_context(const DecodeParams &p, const DecodeLayer &Ly, int hh, bool writer,
-                                                  int pos, float *sm) {
+                                                  int pos, float *sm, int lo, int hi) {
+    const bool split = hi - lo < pos + 1;
     constexpr int EPC = Fmt<WF>::EPC;
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
     const int hd = p.hd, half = hd / 2, g = hh / p.group;
@@ -724,10 +755,11 @@ __device__ __forceinline__ void attention_context(const DecodeParams &p, const D
     const int TP = 1 << tpl, sub = t & (TP - 1), PPP = NT >> tpl;
     float mt = -INFINITY;
 #pragma unroll 1
-    for (int qb = 0; qb <= pos; qb += PPP) {
+    for (int qb = lo; qb < hi; qb += PPP) {
         const int q = qb + (t >> tpl);
         float s = 0.0f;
-        if (q == pos) {
+        if (q >= hi) {
+        } else if (q == pos) {
             if (sub == 0) {
 #pragma unroll 4
                 for (int i = 0; i < hd; ++i) s = s + qs[i] * ks[i];
@@ -760,7 +792,7 @@ __device__ __forceinline__ void attention_context(const DecodeParams &p, const D
         }
 #pragma unroll 1
         for (int off = TP >> 1; off; off >>= 1) s += __shfl_xor_sync(FULL, s, off);
-        if (sub == 0 && q <= pos) {
+        if (sub == 0 && q < hi) {
             s = s / p.sqrt_hd;
             sc[q] = s;
             mt = rust_max(mt, s);
@@ -776,7 +808,7 @@ __device__ __forceinline__ void attention_context(const DecodeParams &p, const D
     for (int w = 1; w < NW; ++w) m = rust_max(m, red[w]);
     float st = 0.0f;
 #pragma unroll 1
-    for (int q = t; q <= pos; q += NT) {
+    for (int q = lo + t; q < hi; q += NT) {
         const float e = expf(sc[q] - m);
         sc[q] = e;
         st += e;
@@ -798,18 +830,18 @@ __device__ __forceinline__ void attention_context(const DecodeParams &p, const D
 #pragma unroll
         for (int e = 0; e < KEPC; ++e) acc[e] = 0.0f;
 #pragma unroll 1
-        for (int q0 = pg; q0 <= pos; q0 += 4 * PG) {
+        for (int q0 = lo + pg; q0 < hi; q0 += 4 * PG) {
             uint4 vc[4];
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
                 const int q = q0 + u * PG;
-                if (q < pos) vc[u] = __ldcg((const uint4 *)(Vc + (size_t)q * row_bytes + (size_t)c * 16));
+                if (q < pos && q < hi) vc[u] = __ldcg((const uint4 *)(Vc + (size_t)q * row_bytes + (size_t)c * 16));
             }
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
                 const int q = q0 + u * PG;
-                if (q <= pos) {
-                    const float pr = sc[q] / se;
+                if (q < hi) {
+                    const float pr = split ? sc[q] : sc[q] / se;
                     const uint32_t w4[4] = {vc[u].x, vc[u].y, vc[u].z, vc[u].w};
 #pragma unroll
                     for (int e = 0; e < KEPC; ++e) {
@@ -831,6 +863,14 @@ __device__ __forceinline__ void attention_context(const DecodeParams &p, const D
             for (int e = 0; e < KEPC; ++e) red[2 * NW + warp * hd + c * KEPC + e] = acc[e];
         }
         csync();
+        if (split) {
+            if (t == 0) {
+                red[2 * NW + NW * hd] = m;
+                red[2 * NW + NW * hd + 1] = se;
+            }
+            csync();
+            return;
+        }
 #pragma unroll 1
         for (int i = t; i < ctx_pad; i += NT) {
             float s = 0.0f;
@@ -903,6 +943,56 @@ __device__ __forceinline__ void run_qkv(const DecodeParams &p, const CtaGeom &cg
     });
 }
 
+// The position-split exchange of head hh (split sp of nsp, layer l): this
+// split's partial (context sums, maximum, sum) to its slot, the head
+// barrier, then every split combines all slots in slot order, rescaled by
+// exp(m_j - m), into xs.  Returns false when aborting.
+template <int WF>
+__device__ __noinline__ bool split_exchange(const DecodeParams &p, int hh, int sp, int nsp, int l, float *sm,
+                                            volatile int *s_abort) {
+    constexpr int EPC = Fmt<WF>::EPC;
+    const int t = threadIdx.x, hd = p.hd;
+    const float *red = sm + p.sm_red;
+    float *xs = sm + p.sm_xs;
+    float *mine = p.apart + ((size_t)hh * nsp + sp) * (hd + 2);
+#pragma unroll 1
+    for (int i = t; i < hd + 2; i += NT) {
+        float v;
+        if (i < hd) {
+            v = red[2 * NW + i];
+#pragma unroll
+            for (int w = 1; w < NW; ++w) v += red[2 * NW + w * hd + i];
+        } else {
+            v = red[2 * NW + NW * hd + (i - hd)];
+        }
+        mine[i] = v;
+    }
+    if (!head_barrier(p, hh, (unsigned)((l + 1) * nsp), s_abort)) return false;
+    const float *all = p.apart + (size_t)hh * nsp * (hd + 2);
+    float M = -INFINITY;
+    for (int j = 0; j < nsp; ++j) M = rust_max(M, __ldcg(all + (size_t)j * (hd + 2) + hd));
+    const int ctx_pad = p.chd * EPC;
+#pragma unroll 1
+    for (int i = t; i < ctx_pad; i += NT) {
+        float s = 0.0f;
+        if (i < hd) {
+            float Lsum = 0.0f, o = 0.0f;
+            for (int j = 0; j < nsp; ++j) {
+                const float *pj = all + (size_t)j * (hd + 2);
+                const float lj = __ldcg(pj + hd + 1);
+                const float f = lj > 0.0f ? expf(__ldcg(pj + hd) - M) : 0.0f;
+                Lsum += lj * f;
+                o += __ldcg(pj + i) * f;
+            }
+            s = o / Lsum;
+            flag_nonfinite(p.ctrl, s);
+        }
+        xs[xq<EPC>(i, p.chd)] = s;
+    }
+    csync();
+    return true;
+}
+
 template <int WF>
 __device__ __forceinline__ void prep_attention(const DecodeParams &p, const DecodeLayer &Ly, const CtaGeom &cg,
                                                float *sm) {
@@ -910,7 +1000,7 @@ __device__ __forceinline__ void prep_attention(const DecodeParams &p, const Deco
 }
 
 template <int WF, int KVBF16>
-__device__ __forceinline__ void run_attention(const DecodeParams &p, const DecodeLayer &Ly, const CtaGeom &cg,
+__device__ __forceinline__ void run_attention(const DecodeParams &p, const DecodeLayer &Ly, const CtaGeom &cg, int l,
                                               int pos, float *sm, const Ring &rg, Cursor &cur,
                                               volatile int *s_abort) {
     const float *rv = sm + p.sm_rv, *xs = sm + p.sm_xs;
@@ -918,7 +1008,12 @@ __device__ __forceinline__ void run_attention(const DecodeParams &p, const Decod
 #pragma unroll 1
     for (int a = 0; a < cg.natt; ++a) {
         const int hh = cg.att_hh[a], r0 = cg.att_r0[a], n = cg.att_n[a];
-        attention_context<WF, KVBF16>(p, Ly, hh, r0 == 0 && hh % p.group == 0, pos, sm);
+        const int nsp = p.att_splits > 1 && pos + 1 >= p.att_split_min ? p.att_splits : 1;
+        const int sp = cg.att_sp[a];
+        const int lo = nsp > 1 ? (int)((long long)(pos + 1) * sp / nsp) : 0;
+        const int hi = nsp > 1 ? (int)((long long)(pos + 1) * (sp + 1) / nsp) : pos + 1;
+        attention_context<WF, KVBF16>(p, Ly, hh, r0 == 0 && hh % p.group == 0, pos, sm, lo, hi);
+        if (nsp > 1 && !split_exchange<WF>(p, hh, sp, nsp, l, sm, s_abort)) return;
         float *outp = p.part + (size_t)hh * p.h + r0;
         const float *so = Ly.so + r0;
         team_gemv<WF, 1>(p, rg, cur, p.kind[K_O], n, xs, s_abort, [&](int r, float acc, float) {
@@ -1091,6 +1186,8 @@ __device__ __forceinline__ void run_lm_head(const DecodeParams &p, const CtaGeom
                 ctrl->pos = pos + 1;
                 ctrl->bar = 0;
                 ctrl->ticket = 0;
+                if (p.hbar)
+                    for (int k = 0; k < p.qh; ++k) p.hbar[k] = 0u;
                 if (p.trace) p.trace[(size_t)4 * p.L * G + 4 * p.L + 1] = globaltimer_ns();
                 __threadfence();
             }
@@ -1159,7 +1256,7 @@ __global__ void __maxnreg__(128) decode_kernel(const __grid_constant__ DecodePar
         prep_attention<WF>(p, Ly, cg, sm);
         if (!(ok = barrier_wait(p, target, s_abort))) break;
 
-        run_attention<WF, KVBF16>(p, Ly, cg, pos, sm, rg, cur, s_abort);
+        run_attention<WF, KVBF16>(p, Ly, cg, l, pos, sm, rg, cur, s_abort);
         barrier_arrive(p, target += G);
         prep_gate_up<WF>(p, Ly, cg, sm);
         if (!(ok = barrier_wait(p, target, s_abort))) break;

@@ -67,6 +67,7 @@ struct CtaGeom {
     int lm_v0, lm_n;    // rows of the LM-head table
     int natt;
     int att_hh[kMaxAttItems], att_r0[kMaxAttItems], att_n[kMaxAttItems];
+    int att_sp[kMaxAttItems];  // index of the item among its head's att_splits items
 };
 
 struct DecodeParams {
@@ -98,6 +99,14 @@ struct DecodeParams {
     unsigned long long *trace;
     unsigned long long timeout_ns;
     int prefetch;             // L2 prefetch of upcoming weights by the producer warp
+    // Long-context attention: with att_splits > 1 and at least att_split_min
+    // cached positions, the att_splits CTAs of a query head each take one
+    // position range, exchange (max, sum, context) partials through apart
+    // [qh][att_splits][hd + 2] and meet at a per-head barrier (hbar[qh],
+    // arrivals reset by the last CTA of the step).
+    int att_splits, att_split_min;
+    float *apart;
+    unsigned *hbar;
     // Shared-memory carve-up, in floats from the base (host-computed).
     // xs: the current activation vector in the quad-major layout; h2: the
     // residual stream; gain: norm gains; rv: per-row scales/biases; sc:

@@ -278,7 +278,7 @@ struct Session {
     int kv_bf16 = 0;
     size_t logical_bytes = 0, workspace_bytes = 0;
     cudaStream_t stream = nullptr;
-    DevBuf kv, rope, qkv, part, act, hidden, logits, amax_v, amax_i, emitted, ctrl, dlayers, geom;
+    DevBuf kv, rope, qkv, part, act, hidden, logits, amax_v, amax_i, emitted, ctrl, dlayers, geom, apart, hbar;
     DecodeCtrl *hctrl = nullptr;  // pinned mirror
     std::vector<DecodeLayer> hlayers;  // host copy of the layer table (chunked prompt path)
     DevBuf pf;                         // chunked prompt workspace (allocated on first use)
@@ -486,6 +486,7 @@ static uint32_t session_build(Session &s) {
             const int sp = wi % s_o;
             const int r0 = (int)((long long)p.h * sp / s_o), r1 = (int)((long long)p.h * (sp + 1) / s_o);
             g.att_hh[g.natt] = wi / s_o;
+            g.att_sp[g.natt] = sp;
             g.att_r0[g.natt] = r0;
             g.att_n[g.natt] = r1 - r0;
             max_att = std::max(max_att, r1 - r0);
@@ -495,6 +496,22 @@ static uint32_t session_build(Session &s) {
         max_dn = std::max(max_dn, g.dn_n); max_lm = std::max(max_lm, g.lm_n);
     }
     if ((size_t)p.V * s.grid >= (1ull << 31)) return QB_UNSUPPORTED;
+    // Position-split attention for long contexts: each head's s_o CTAs take
+    // a range of positions and combine through a per-head barrier.  Only
+    // when every CTA has at most one attention item (no CTA waits on a head
+    // whose other members are busy with another head) and the key rows
+    // suit the vectorised path.
+    {
+        const size_t row_bytes = hd * (s.kv_bf16 ? 2 : 4), nc = row_bytes / 16;
+        const bool vec = row_bytes % 16 == 0 && nc <= 32 && (nc & (nc - 1)) == 0;
+        p.att_splits = (p.qh * s_o <= s.grid && s_o > 1 && vec) ? s_o : 1;
+        p.att_split_min = 512;
+        if ((st = s.apart.alloc((size_t)p.qh * s_o * (hd + 2) * 4, false)) ||
+            (st = s.hbar.alloc((size_t)p.qh * 4)))
+            return st;
+        p.apart = s.apart.as<float>();
+        p.hbar = s.hbar.as<unsigned>();
+    }
     if ((st = s.geom.alloc(geo.size() * sizeof(CtaGeom), false))) return st;
     QB_CUDA(cudaMemcpy(s.geom.p, geo.data(), geo.size() * sizeof(CtaGeom), cudaMemcpyHostToDevice));
     p.geom = s.geom.as<CtaGeom>();

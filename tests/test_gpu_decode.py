@@ -351,3 +351,33 @@ def test_qwen05b_chunked_prefill_parity(oracle, linear_format, kv, tol):
         _, lg = os_.step(or_ids[-1])
         or_ids.append(int(np.argmax(lg)))
     assert dev_ids == or_ids
+
+
+@pytest.mark.parametrize("kv,tol", [("f32", 1e-3), ("bf16", 2e-2)])
+def test_qwen05b_long_context_split_attention(oracle, kv, tol):
+    # Past 512 cached positions the decode kernel splits each head's
+    # attention over its CTAs and combines the partials through a per-head
+    # barrier: a 640-token prompt, then 8 decode steps against the oracle's
+    # serial evaluation (logits within tolerance, greedy ids identical).
+    import llm_inference_edu_b200 as qb
+    from helpers import qwen_host_weights
+    n, steps = 640, 8
+    cfg = presets.qwen_0_5b(n + steps + 8)
+    w = qwen_host_weights("0.5b", 1, "bf16")
+    m = qb.Decoder(cfg, w, linear_format="int8", table_format="bf16")
+    om = oracle.Model(cfg, oracle_weights(oracle, cfg, w, "int8"))
+    prompt = synthetic.prompt(cfg.vocab_size, n, seed=5)
+    s = qb.CachedSession(m, n + steps + 8, kv_dtype=kv, budget=0)
+    os_ = oracle.Session(om, n + steps + 8, kv_bf16=(kv == "bf16"), budget=0)
+    got = s.prefill(prompt)
+    _, exp = os_.prefill(prompt)
+    worst = max_abs(got, exp)
+    tok = int(np.argmax(exp))
+    assert int(np.argmax(got)) == tok
+    for _ in range(steps):
+        g = s.step(tok)
+        _, e = os_.step(tok)
+        worst = max(worst, max_abs(g, e))
+        assert int(np.argmax(g)) == int(np.argmax(e))
+        tok = int(np.argmax(e))
+    assert worst <= tol, worst
