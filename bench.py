@@ -20,7 +20,8 @@ from pinned memory and an 8-byte device->host result read).  The weights
 
 `batched` is the same model decoding 64 independent sequences per GPU in
 lockstep (BatchSession: one multi-token forward per step on the tensor
-cores), device-timed, with its prompt evaluation rate.
+cores), device-timed, with its prompt evaluation rate.  `long_context` is
+an 8,192-token prompt (chunked) then greedy decode at that depth.
 
 --impl reference times the oracle -- the C restatement of the reference
 crate's CPU arithmetic (the Rust crate cannot be built here) -- on the
@@ -238,6 +239,8 @@ def run_native(args, topo):
     e2e_s = dp.max_over_ranks(topo, time.perf_counter() - t0, device="cuda")
 
     batched = run_batched(args, topo, model, cfg, kv)
+    del model
+    long_ctx = run_long_context(args, topo, kv) if lf == "int8" else None
 
     if rank != 0:
         return 0
@@ -268,6 +271,7 @@ def run_native(args, topo):
         "gpu_launches": args.steps,
         "clocks": clocks.summary(),
         "batched": batched,
+        "long_context": long_ctx,
     }
     if world == 1:
         line["cpu_baseline"] = cpu_baseline(args)
@@ -316,6 +320,48 @@ def run_batched(args, topo, model, cfg, kv):
             "unit": "tok/s", "ms_per_step": ms / steps,
             "prefill_tok_per_s": BATCH * PROMPT / (prefill_ms / 1000.0),
             "h2d_bytes_per_call": BATCH * 4, "d2h_bytes_per_call": BATCH * 4 * steps}
+
+
+LONG_PROMPT = 8192
+LONG_STEPS = 128
+
+
+def run_long_context(args, topo, kv):
+    """The long-context variant: an 8,192-token prompt through the chunked
+    multi-token path, then 128 greedy tokens through the decode kernel
+    (position-split attention), device-timed."""
+    import torch
+
+    import llm_inference_edu_b200 as qb
+    from llm_inference_edu_b200 import dp, presets, synthetic
+
+    cap = LONG_PROMPT + LONG_STEPS + 8
+    cfg = presets.qwen_0_5b(cap)
+    w = synthetic.weights(cfg, seed=SEED, dtype="bf16")
+    model = qb.Decoder(cfg, w, linear_format="int8", table_format="bf16", device=topo.local_rank)
+    del w
+    prompt = synthetic.prompt(cfg.vocab_size, LONG_PROMPT, seed=2000 + topo.rank)
+    sess = qb.CachedSession(model, cap, kv_dtype=kv, budget=0)
+    stream = torch.cuda.ExternalStream(sess.stream())
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    ev0.record(stream)
+    first = sess.prefill_into(prompt, None)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    prefill_ms = dp.max_over_ranks(topo, ev0.elapsed_time(ev1), device="cuda")
+    ids = sess.decode_greedy(first, 8)
+    dp.barrier(topo)
+    torch.cuda.synchronize()
+    ev0.record(stream)
+    sess.decode_greedy(ids[-1], LONG_STEPS - 8)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    ms = dp.max_over_ranks(topo, ev0.elapsed_time(ev1), device="cuda")
+    return {"prompt": LONG_PROMPT, "steps": LONG_STEPS - 8,
+            "prefill_tok_per_s": topo.world * LONG_PROMPT / (prefill_ms / 1000.0),
+            "value": topo.world * (LONG_STEPS - 8) / (ms / 1000.0), "unit": "tok/s",
+            "ms_per_token": ms / (LONG_STEPS - 8)}
 
 
 def cpu_baseline(args):

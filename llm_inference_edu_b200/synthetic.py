@@ -56,32 +56,53 @@ def prompt(vocab: int, n: int, seed: int, stream: int = 7) -> list:
 
 
 def weights(cfg: ModelConfig, seed: int, dtype: str = "bf16", bias_std: float = 0.0,
-            norm_std: float = 0.0) -> dict:
+            norm_std: float = 0.0, lazy: bool = False) -> dict:
     """Host weight dictionary for `cfg` (see module docstring).
 
     bias_std / norm_std > 0 draw non-trivial biases and norm gains
-    (1 + N(0, norm_std)) for tests that must exercise those paths.
+    (1 + N(0, norm_std)) for tests that must exercise those paths.  With
+    lazy=True, "layers" is a sequence that draws each layer when it is
+    visited (host memory of one layer at a time, for 7B-sized models).
     """
-    h, kv, ff, V = cfg.hidden_dim, cfg.kv_dim, cfg.ff_dim, cfg.vocab_size
-    shapes = {"q": h * h, "k": kv * h, "v": kv * h, "o": h * h, "gate": ff * h, "up": ff * h,
-              "down": h * ff}
+    h, V = cfg.hidden_dim, cfg.vocab_size
     out = {"embedding": normal(seed, 1, V * h, STD, dtype)}
     if not cfg.tied:
         out["lm_head"] = normal(seed, 2, V * h, STD, dtype)
     out["final_norm"] = _gain(seed, 3, h, norm_std)
-    layers = []
-    for l in range(cfg.layers):
-        base = 100 + 16 * l
-        layer = {k: normal(seed, base + i, shapes[k], STD, dtype) for k, i in _MAT.items()}
-        layer["attn_norm"] = _gain(seed, base + 10, h, norm_std)
-        layer["ffn_norm"] = _gain(seed, base + 11, h, norm_std)
-        if cfg.qkv_bias or bias_std > 0:
-            for name, i, n in (("q_bias", 7, h), ("k_bias", 8, kv), ("v_bias", 9, kv)):
-                layer[name] = (normal(seed, base + i, n, bias_std, "f32") if bias_std > 0
-                               else np.zeros(n, dtype=np.float32))
-        layers.append(layer)
-    out["layers"] = layers
+    layers = _Layers(cfg, seed, dtype, bias_std, norm_std)
+    out["layers"] = layers if lazy else list(layers)
     return out
+
+
+class _Layers:
+    """The layers of `weights`, each drawn when it is visited."""
+
+    def __init__(self, cfg, seed, dtype, bias_std, norm_std):
+        self.cfg, self.seed, self.dtype, self.bias_std, self.norm_std = cfg, seed, dtype, bias_std, norm_std
+
+    def __len__(self):
+        return self.cfg.layers
+
+    def __getitem__(self, l):
+        if not 0 <= l < self.cfg.layers:
+            raise IndexError(l)
+        cfg, seed = self.cfg, self.seed
+        h, kv, ff = cfg.hidden_dim, cfg.kv_dim, cfg.ff_dim
+        shapes = {"q": h * h, "k": kv * h, "v": kv * h, "o": h * h, "gate": ff * h, "up": ff * h,
+                  "down": h * ff}
+        base = 100 + 16 * l
+        layer = {k: normal(seed, base + i, shapes[k], STD, self.dtype) for k, i in _MAT.items()}
+        layer["attn_norm"] = _gain(seed, base + 10, h, self.norm_std)
+        layer["ffn_norm"] = _gain(seed, base + 11, h, self.norm_std)
+        if cfg.qkv_bias or self.bias_std > 0:
+            for name, i, n in (("q_bias", 7, h), ("k_bias", 8, kv), ("v_bias", 9, kv)):
+                layer[name] = (normal(seed, base + i, n, self.bias_std, "f32") if self.bias_std > 0
+                               else np.zeros(n, dtype=np.float32))
+        return layer
+
+    def __iter__(self):
+        for l in range(len(self)):
+            yield self[l]
 
 
 def _gain(seed, stream, n, std):
