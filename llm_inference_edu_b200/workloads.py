@@ -1,0 +1,128 @@
+"""Small fixed workloads for profiling and examples (synthetic weights).
+
+    python -m llm_inference_edu_b200.workloads batched [--sequences 64] [--prompt 2] [--steps 4]
+    python -m llm_inference_edu_b200.workloads decode [--prompt 128] [--steps 8] [--profile]
+    python -m llm_inference_edu_b200.workloads long [--prompt 8192] [--steps 128]
+    python -m llm_inference_edu_b200.workloads qwen7b [--prompt 512] [--steps 64]
+
+Each builds the model on cuda:0 (0.5B INT8 with a BF16 table and KV unless
+noted), runs the workload through the public API and prints one line of
+timings.  `decode --profile` prints the per-phase device timestamps of the
+decode kernel (CachedSession.step_profiled).
+"""
+from __future__ import annotations
+
+import argparse
+import time
+
+import numpy as np
+
+from . import presets, synthetic
+
+
+def _model(cfg, seed=1):
+    from . import api
+    w = synthetic.weights(cfg, seed=seed, dtype="bf16", lazy=True)
+    return api.Decoder(cfg, w, linear_format="int8", table_format="bf16")
+
+
+def _sync():
+    import torch
+    torch.cuda.synchronize()
+
+
+def batched(sequences: int, prompt: int, steps: int) -> None:
+    from . import api
+    cap = prompt + steps + 8
+    cfg = presets.qwen_0_5b(cap)
+    m = _model(cfg)
+    prompts = np.stack([synthetic.prompt(cfg.vocab_size, prompt, seed=100 + r)
+                        for r in range(sequences)]).astype(np.uint32)
+    b = api.BatchSession(m, sequences, cap, kv_dtype="bf16")
+    _sync()
+    t0 = time.perf_counter()
+    first = b.prefill(prompts)
+    _sync()
+    t1 = time.perf_counter()
+    b.decode_greedy(first, steps)
+    _sync()
+    t2 = time.perf_counter()
+    print(f"batched: {sequences} sequences, prompt {prompt}: prefill {sequences * prompt / (t1 - t0):.0f} tok/s, "
+          f"decode {(t2 - t1) * 1e3 / steps:.3f} ms/step (wall)")
+
+
+def decode(prompt: int, steps: int, profile: bool) -> None:
+    from . import api
+    cap = prompt + steps + 8
+    cfg = presets.qwen_0_5b(cap)
+    m = _model(cfg)
+    s = api.CachedSession(m, cap, kv_dtype="bf16", budget=0)
+    tok = s.prefill_into(synthetic.prompt(cfg.vocab_size, prompt, seed=1), None)
+    if not profile:
+        _sync()
+        t0 = time.perf_counter()
+        s.decode_greedy(tok, steps)
+        _sync()
+        print(f"decode: {(time.perf_counter() - t0) * 1e6 / steps:.1f} us/token (wall)")
+        return
+    acc = {k: np.zeros(3) for k in ("qkv", "attention", "gate_up", "down")}
+    tot = []
+    for i in range(steps):
+        _, prof = s.step_profiled(tok)
+        tok = prof["argmax"]
+        if i < 2:
+            continue
+        tot.append((prof["total_ns"], prof["logits_ns"]))
+        for L in prof["layers"]:
+            for k, v in L.items():
+                acc[k] += np.array([v["ns"], v["mean_ns"], v["barrier_ns"]])
+    n = (steps - 2) * cfg.layers
+    print(f"decode at position ~{prompt}: step {np.mean([t[0] for t in tot]) / 1e3:.1f} us, "
+          f"LM head {np.mean([t[1] for t in tot]) / 1e3:.1f} us")
+    for k, v in acc.items():
+        print(f"  {k:9s} per layer: phase {v[0] / n / 1e3:.2f} us, mean CTA work {v[1] / n / 1e3:.2f} us, "
+              f"barrier after the last arrival {v[2] / n / 1e3:.2f} us")
+
+
+def long(prompt: int, steps: int) -> None:
+    decode(prompt, steps, profile=False)
+
+
+def qwen7b(prompt: int, steps: int) -> None:
+    from . import api
+    cap = prompt + steps + 8
+    cfg = presets.qwen_7b(cap)
+    m = _model(cfg, seed=2)
+    s = api.CachedSession(m, cap, kv_dtype="bf16", budget=0)
+    _sync()
+    t0 = time.perf_counter()
+    tok = s.prefill_into(synthetic.prompt(cfg.vocab_size, prompt, seed=3), None)
+    _sync()
+    t1 = time.perf_counter()
+    s.decode_greedy(tok, steps)
+    _sync()
+    t2 = time.perf_counter()
+    print(f"qwen7b: prefill {prompt / (t1 - t0):.0f} tok/s, decode {(t2 - t1) * 1e3 / steps:.2f} ms/token (wall)")
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("workload", choices=["batched", "decode", "long", "qwen7b"])
+    ap.add_argument("--sequences", type=int, default=64)
+    ap.add_argument("--prompt", type=int, default=None)
+    ap.add_argument("--steps", type=int, default=None)
+    ap.add_argument("--profile", action="store_true")
+    a = ap.parse_args(argv)
+    if a.workload == "batched":
+        batched(a.sequences, a.prompt or 2, a.steps or 4)
+    elif a.workload == "decode":
+        decode(a.prompt or 128, a.steps or 8, a.profile)
+    elif a.workload == "long":
+        long(a.prompt or 8192, a.steps or 128)
+    else:
+        qwen7b(a.prompt or 512, a.steps or 64)
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())
