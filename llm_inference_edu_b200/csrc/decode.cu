@@ -213,19 +213,24 @@ __device__ __forceinline__ void stage_l2(float *dst, const float *src, int n) {
     }
 }
 
-// The same for read-only model vectors (gains, scales, biases).
+// The same for read-only model vectors (gains, scales, biases), by the
+// compute warps other than warp 0: the next phase's vectors are staged while
+// the grid barrier completes, and warp 0 (whose thread 0 polls the barrier)
+// must not wait for these loads before it starts polling.
 template <int B>
 __device__ __forceinline__ void stage_ro(float *dst, const float *src, int n) {
-    for (int base = threadIdx.x; base < n; base += B * NT) {
+    constexpr int NS = NT - 32;
+    if (threadIdx.x < 32) return;
+    for (int base = threadIdx.x - 32; base < n; base += B * NS) {
         float v[B];
 #pragma unroll
         for (int k = 0; k < B; ++k) {
-            const int i = base + k * NT;
+            const int i = base + k * NS;
             v[k] = i < n ? __ldg(src + i) : 0.0f;
         }
 #pragma unroll
         for (int k = 0; k < B; ++k) {
-            const int i = base + k * NT;
+            const int i = base + k * NS;
             if (i < n) dst[i] = v[k];
         }
     }
