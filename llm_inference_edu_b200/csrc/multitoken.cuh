@@ -118,6 +118,49 @@ __device__ __forceinline__ void epilogue_gu(const GemmW &w, int t, int r, float 
     flag_bad(err, a);
 }
 
+// RoPE and the KV write fused into the QKV epilogue: everything rope_kv
+// needs (per-token positions and sequences, the host cos/sin table and the
+// cache geometry).  hd is a power of two >= 64.
+struct RopeKv {
+    const int *pos, *seq;
+    const float2 *rope;  // [cap][hd / 2]
+    uint8_t *kv;         // cache base: sequence s, layer l: K at kv + s seq_bytes + 2 l layer_bytes, V after it
+    size_t seq_bytes, layer_bytes;
+    int l, h, kvh, hd, cap, kv_bf16;
+};
+
+// Output row r of token t of the QKV projection, y (after scale and bias),
+// with yp the same token's row r ^ (hd / 2) (the RoPE partner): q rows are
+// rotated in place, k rows rotated into the cache, v rows copied into the
+// cache (BF16 round-to-nearest-even when the cache is BF16) -- rope_kv's
+// arithmetic (src/rope.rs:83-105 with the host table).
+__device__ __forceinline__ void qkv_rope_store(const RopeKv &k, float *qkv, int ldq, int t, int r, float y, float yp,
+                                               unsigned *err) {
+    const int half = k.hd >> 1, kvw = k.kvh * k.hd;
+    const int p = k.pos[t];
+    flag_bad(err, y);
+    uint8_t *kc = k.kv + (size_t)k.seq[t] * k.seq_bytes + (size_t)(2 * k.l) * k.layer_bytes;
+    if (r < k.h + kvw) {
+        const int rr = r < k.h ? r : r - k.h, d = rr & (k.hd - 1);
+        const float2 cs = k.rope[(size_t)p * half + (d & (half - 1))];
+        const float o = d < half ? y * cs.x - yp * cs.y : y * cs.x + yp * cs.y;
+        flag_bad(err, o);
+        if (r < k.h) {
+            qkv[(size_t)t * ldq + r] = o;
+            return;
+        }
+        const size_t at = ((size_t)(rr / k.hd) * k.cap + p) * k.hd + d;
+        if (k.kv_bf16) ((uint16_t *)kc)[at] = bf16_rn(o);
+        else ((float *)kc)[at] = o;
+    } else {
+        const int rr = r - k.h - kvw, d = rr & (k.hd - 1);
+        const size_t at = ((size_t)(rr / k.hd) * k.cap + p) * k.hd + d;
+        uint8_t *vc = kc + k.layer_bytes;
+        if (k.kv_bf16) ((uint16_t *)vc)[at] = bf16_rn(y);
+        else ((float *)vc)[at] = y;
+    }
+}
+
 // Sums the ks split-K partials part[z][t][r] of each output in slice order,
 // then the epilogue (SwiGLU outputs one value per row pair).
 template <int EPI>

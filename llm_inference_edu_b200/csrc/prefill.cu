@@ -640,6 +640,12 @@ cudaError_t layer_gemm(int which, const PrefillArgs &a, const DecodeLayer &Ly, i
     }
 }
 
+// RoPE and the KV write run in the QKV GEMM's epilogue when that GEMM is on
+// the tensor cores and the RoPE partner rows (r ^ hd/2) share a 128-row tile.
+bool rope_fused(const PrefillArgs &a) {
+    return a.tc && !a.tc->layers.empty() && (a.hd == 64 || a.hd == 128);
+}
+
 // The same GEMMs on the tensor cores (weights in the layer's tensor maps,
 // inputs as BF16 planes).
 cudaError_t layer_gemm_tc(int which, const PrefillArgs &a, int l, int n, cudaStream_t st) {
@@ -648,10 +654,16 @@ cudaError_t layer_gemm_tc(int which, const PrefillArgs &a, int l, int n, cudaStr
     const int kv = a.kvh * a.hd, rq = a.h + 2 * kv;
     const Planes none{nullptr, 0, TC_NP};
     TcJob j;
+    RopeKv rk;
     switch (which) {
     case 0:
         j = TcJob{EPI_QKV, n, rq, a.h, &M.qkv, &a.tc->xn, GemmW{nullptr, 0, 0, 0, Ly.sqkv, Ly.bqkv},
                   nullptr, 0, a.qkv, rq, none};
+        if (rope_fused(a)) {
+            rk = RopeKv{a.pos, a.seq, a.rope, a.kv, a.kv_seq_bytes, a.kv_layer_bytes, l, a.h, a.kvh, a.hd, a.cap,
+                        a.kv_bf16};
+            j.rk = &rk;
+        }
         break;
     case 1:
         j = TcJob{EPI_RESID, n, a.h, a.qh * a.hd, &M.o, &a.tc->ctx, GemmW{nullptr, 0, 0, 0, Ly.so, nullptr},
@@ -751,9 +763,10 @@ cudaError_t forward_tokens(const PrefillArgs &a, int n, int max_pos, bool lm_hea
                             a.h, a.eps, a.err)) != cudaSuccess)
             break;
         if ((e = run_gemm(0, a, l, n, st)) != cudaSuccess) break;
-        if ((e = launch_pdl(rope_kv, dim3(rows_grid), dim3(128), 0, st, a.qkv, n, a.pos, a.seq, l, a.h, a.qh, a.kvh,
+        if (!rope_fused(a) &&
+            (e = launch_pdl(rope_kv, dim3(rows_grid), dim3(128), 0, st, a.qkv, n, a.pos, a.seq, l, a.h, a.qh, a.kvh,
                             a.hd, a.rope, a.cap, a.kv, a.kv_seq_bytes, a.kv_layer_bytes, a.kv_bf16, a.err)) !=
-            cudaSuccess)
+                cudaSuccess)
             break;
         if ((e = attention(a, n, l, max_pos, st)) != cudaSuccess) break;
         if ((e = cudaGetLastError()) != cudaSuccess) break;

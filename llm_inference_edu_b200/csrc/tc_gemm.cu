@@ -53,7 +53,29 @@ struct TcArgs {
     unsigned *err;
     float *amv;
     int *ami;
+    RopeKv rk;
+    int rope;
 };
+
+// AND of v over the 128 epilogue threads (named barrier 1).
+__device__ __forceinline__ bool bar_and_128(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 q, %1, 0;\n\tbar.red.and.pred p, 1, 128, q;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)v)
+        : "memory");
+    return r != 0;
+}
+
+// The QKV value of row r from its raw accumulator (epilogue1's arithmetic).
+__device__ __forceinline__ float qkv_value(const GemmW &w, int r, float acc) {
+    float v = acc;
+    if (w.scale) v = v * w.scale[r];
+    if (w.bias) v = v + w.bias[r];
+    return v;
+}
 
 __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *m, int c0, int c1, int c2,
                                             uint64_t *bar) {
@@ -359,8 +381,11 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
         const int q = warp & 3, r = row0 + 32 * q + lane;
         const bool split = gridDim.y > 1;
         const bool am = EPI == EPI_PLAIN && g.amv && !split;
-        const bool run = __all_sync(0xffffffffu, ok && !*abort_);
+        // Uniform over the epilogue warps (the RoPE exchange below uses
+        // named barriers).
+        const bool run = bar_and_128(ok && !*abort_);
         float *tile = s_epi + q * (16 * 33);
+        const bool rope = EPI == EPI_QKV && g.rope;
         if (run) {
             const uint32_t lanes = (uint32_t)(32 * q) << 16;
 #pragma unroll 1
@@ -380,6 +405,18 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
                 if (split) {
 #pragma unroll 1
                     for (int j = 0; j < tn; ++j) red[(c + j) * TC_BM + ct] = tile[j * 33 + lane];
+                } else if (rope) {
+                    // The RoPE partner row r ^ (hd / 2) sits in another
+                    // warp's tile, same lane.
+                    asm volatile("bar.sync 1, 128;" ::: "memory");
+                    const int rp = r ^ (g.rk.hd >> 1);
+                    const float *ptile = s_epi + (((32 * q + lane) ^ (g.rk.hd >> 1)) >> 5) * (16 * 33);
+#pragma unroll 1
+                    for (int j = 0; j < tn; ++j)
+                        if (r < g.N)
+                            qkv_rope_store(g.rk, g.Y, g.ldy, t0 + c + j, r, qkv_value(g.w, r, tile[j * 33 + lane]),
+                                           qkv_value(g.w, rp, ptile[j * 33 + lane]), g.err);
+                    asm volatile("bar.sync 1, 128;" ::: "memory");
                 } else {
 #pragma unroll 1
                     for (int j = 0; j < tn; j += 4) {
@@ -454,6 +491,20 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
             const int tn = min(NT, g.n - t0), ks = (int)gridDim.y, tper = (tn + ks - 1) / ks;
             const uint32_t mine = smem_addr(red);
             const int j1 = min(tn, (z + 1) * tper);
+            if (EPI == EPI_QKV && g.rope) {
+                const int hl = g.rk.hd >> 1, rp = r ^ hl;
+#pragma unroll 1
+                for (int j = z * tper; j < j1; ++j) {
+                    float v = 0.0f, vp = 0.0f;
+#pragma unroll 1
+                    for (int zz = 0; zz < ks; ++zz) {
+                        v += ld_dsmem_f32(mapa_rank(mine + (uint32_t)(j * TC_BM + ct) * 4u, zz));
+                        vp += ld_dsmem_f32(mapa_rank(mine + (uint32_t)(j * TC_BM + (ct ^ hl)) * 4u, zz));
+                    }
+                    if (run && r < g.N)
+                        qkv_rope_store(g.rk, g.Y, g.ldy, t0 + j, r, qkv_value(g.w, r, v), qkv_value(g.w, rp, vp), g.err);
+                }
+            } else
 #pragma unroll 1
             for (int j = z * tper; j < j1; j += 4) {
                 float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
@@ -605,7 +656,11 @@ cudaError_t tc_gemm(const TcJob &j, unsigned *err, cudaStream_t st, int *am_tile
     ks = (nkb + kb_per - 1) / kb_per;
     const bool am = j.epi == EPI_PLAIN && j.amv && j.ami && ks == 1;
     TcArgs g{j.n, j.N, nkb, kb_per, nt, stages, j.w->seg_kb, j.gw, j.R, j.ldr, j.Y, j.ldy, j.P, err,
-             am ? j.amv : nullptr, am ? j.ami : nullptr};
+             am ? j.amv : nullptr, am ? j.ami : nullptr, RopeKv{}, 0};
+    if (j.epi == EPI_QKV && j.rk) {
+        g.rk = *j.rk;
+        g.rope = 1;
+    }
     if (am && am_tiles) *am_tiles = rtiles;
     const dim3 grid(rtiles, ks, ttiles);
     return j.w->wf == WF_I8 ? launch_epi<WF_I8>(j, g, grid, st) : launch_epi<WF_BF16>(j, g, grid, st);

@@ -52,6 +52,9 @@ struct TcJob {
     // ([ceil(N / 128)][n]; null: not wanted).
     float *amv;
     int *ami;
+    // EPI_QKV: RoPE and the KV write fused into the epilogue (null: the
+    // plain QKV epilogue).
+    const mt::RopeKv *rk;
 };
 
 // Builds a weight map; false when the layout does not suit TMA.
