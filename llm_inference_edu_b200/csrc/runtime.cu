@@ -618,6 +618,7 @@ static uint32_t session_fail(Session &s, uint32_t status) {
     s.processed = 0;
     s.logits_valid = false;
     cudaMemsetAsync(s.ctrl.p, 0, sizeof(DecodeCtrl), s.stream);
+    if (s.hbar.p) cudaMemsetAsync(s.hbar.p, 0, s.hbar.bytes, s.stream);
     cudaStreamSynchronize(s.stream);
     memset(s.hctrl, 0, sizeof(DecodeCtrl));
     return status;

@@ -560,6 +560,9 @@ cudaError_t launch(const TcJob &j, const TcArgs &g, dim3 grid, cudaStream_t st) 
         cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<WF, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)std::max<size_t>(smem, 200 * 1024));
         if (e != cudaSuccess) return e;
+        // Clusters of up to 16 CTAs (K splits of one output tile).
+        e = cudaFuncSetAttribute(tc_gemm_kernel<WF, EPI>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        if (e != cudaSuccess) return e;
         configured = std::max<size_t>(smem, 200 * 1024);
     }
     // Dependent launch; the K splits of an output tile form one cluster.
@@ -647,11 +650,11 @@ cudaError_t tc_gemm(const TcJob &j, unsigned *err, cudaStream_t st, int *am_tile
         stages = (int)std::min<size_t>(8, std::max<size_t>(2, (227 * 1024 - tc_fixed_bytes(nt, 8)) / per));
         slots = 148;
     }
-    // Split K (clusters of up to 8 CTAs) while the output tiles leave CTA
+    // Split K (clusters of up to 16 CTAs) while the output tiles leave CTA
     // slots idle, staying in one wave and keeping at least two K blocks a
     // split.
     int ks = 1;
-    while (rtiles * ttiles * ks * 2 <= slots && nkb >= ks * 2 * 2 && ks * 2 <= 8) ks *= 2;
+    while (rtiles * ttiles * ks * 2 <= slots && nkb >= ks * 2 * 2 && ks * 2 <= 16) ks *= 2;
     const int kb_per = (nkb + ks - 1) / ks;
     ks = (nkb + kb_per - 1) / kb_per;
     const bool am = j.epi == EPI_PLAIN && j.amv && j.ami && ks == 1;
