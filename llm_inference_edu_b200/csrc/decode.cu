@@ -532,6 +532,67 @@ __device__ __forceinline__ void team_gemv_lm(const DecodeParams &p, const Ring &
     else team_gemv_g<WF, 2, 5>(p, rg, cur, g, n, xs, s_abort, epi);
 }
 
+// The LM head's stream: the CTA's table rows arrive slot by slot, and each
+// slot (whole row pairs) is taken by one warp alone -- warp w < W reads
+// slots w, w + W, ... -- so the slots' latencies overlap instead of every
+// warp meeting at each wave.  W = min(NW, nslot): a warp then reaches a
+// ring slot only after its previous use was filled, so the parity wait
+// cannot match a phase two rounds old.  The warp frees its slot with all NW
+// arrivals at once.  Per row pair: lanes stride the 16-byte chunks with four FP32
+// chains, a shuffle butterfly, then lane 0 runs epi(row, y0, y1) (y1 of an
+// odd tail row is discarded by the epilogue).
+template <int TF, class Epi>
+__device__ __forceinline__ void lm_stream(const DecodeParams &p, const Ring &rg, Cursor &cur, const KindGeom &g,
+                                          int n, const float *xs, volatile int *s_abort, Epi &&epi) {
+    constexpr int Q = Fmt<TF>::EPC / 4;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int C = g.C, rpc = g.rpc;
+    const int nslots = (n + rpc - 1) / rpc, W = min(NW, rg.nslot);
+    const float4 *x4 = reinterpret_cast<const float4 *>(xs);
+#pragma unroll 1
+    for (int k = warp; k < nslots && warp < W; k += W) {
+        int s = cur.slot + k, rd = cur.round;
+        while (s >= rg.nslot) { s -= rg.nslot; ++rd; }
+        int ok = 1;
+        if (lane == 0) ok = mbar_wait(p, rg.full + s, (uint32_t)(rd & 1), s_abort) ? 1 : 0;
+        ok = __shfl_sync(FULL, ok, 0);
+        __syncwarp();  // the rest of the warp reads after lane 0's acquire
+        if (ok) {
+            const uint8_t *base = rg.slots + (size_t)s * rg.slot_bytes;
+            const int r0 = k * rpc, rows = min(rpc, n - r0);
+#pragma unroll 1
+            for (int u = 0; u < rows; u += 2) {
+                const uint8_t *w0 = base + (size_t)u * g.stride;
+                float2 a0 = make_float2(0.0f, 0.0f), b0 = a0, a1 = a0, b1 = a0;
+#pragma unroll 2
+                for (int c = lane; c < C; c += 32) {
+                    float4 x[Q];
+#pragma unroll
+                    for (int q = 0; q < Q; ++q) x[q] = x4[q * C + c];
+                    const uint4 w = *reinterpret_cast<const uint4 *>(w0 + (size_t)c * 16);
+                    const uint4 w1 = *reinterpret_cast<const uint4 *>(w0 + g.stride + (size_t)c * 16);
+                    chunk_dot2<TF>(w, x, a0, b0);
+                    chunk_dot2<TF>(w1, x, a1, b1);
+                }
+                float s0 = (a0.x + a0.y) + (b0.x + b0.y), s1 = (a1.x + a1.y) + (b1.x + b1.y);
+#pragma unroll
+                for (int off = 16; off; off >>= 1) {
+                    s0 += __shfl_xor_sync(FULL, s0, off);
+                    s1 += __shfl_xor_sync(FULL, s1, off);
+                }
+                if (lane == 0) epi(r0 + u, s0, s1);
+            }
+        }
+        __syncwarp();
+        if (lane == 0) {
+            fence_proxy_async_smem();
+            mbar_arrive_cnt(rg.empty + s, NW);
+        }
+    }
+    cur.slot += nslots;
+    while (cur.slot >= rg.nslot) { cur.slot -= rg.nslot; ++cur.round; }
+}
+
 // ------------------------------------------------------------ barrier ----
 
 // Grid barrier in two halves (compute warps only).  barrier_arrive makes
@@ -1142,7 +1203,7 @@ __device__ __forceinline__ void run_lm_head(const DecodeParams &p, const CtaGeom
     csync();
     block_rmsnorm<TEPC>(h2, gain, xs, p.h, p.cemb, p.eps, sm + p.sm_red);
     const int nlm = cg.lm_n;
-    team_gemv_lm<TF>(p, rg, cur, p.kind[K_LM], nlm, xs, s_abort, [&](int r, float a0, float a1) {
+    lm_stream<TF>(p, rg, cur, p.kind[K_LM], nlm, xs, s_abort, [&](int r, float a0, float a1) {
         rowv[r] = a0;
         if (r + 1 < nlm) rowv[r + 1] = a1;
     });

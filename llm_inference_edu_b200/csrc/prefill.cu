@@ -13,6 +13,7 @@
 #include <math.h>
 
 #include <algorithm>
+#include <atomic>
 #include <vector>
 
 #include "common.cuh"
@@ -714,15 +715,19 @@ cudaError_t attention(const PrefillArgs &a, int n, int l, int max_pos, cudaStrea
         const int nz = attention_splits(a, n, max_pos, &span);
         if (span <= AT_SPAN) {
             const size_t sm = attn_gqa_smem(a.group, a.hd, span);
-            static int configured[4] = {0, 0, 0, 0};
+            // Attribute set once per (instantiation, device): bit `which` of
+            // the device's mask.
+            static std::atomic<unsigned> configured[64];
+            int dev = 0;
+            if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
             const int which = a.kv_bf16 * 2 + (a.hd == 128);
             auto kern = which == 3 ? attn_gqa<1, 128> : which == 2 ? attn_gqa<1, 64>
                       : which == 1 ? attn_gqa<0, 128> : attn_gqa<0, 64>;
-            if (!configured[which]) {
+            if (!(configured[dev].load() & (1u << which))) {
                 cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                      (int)attn_gqa_smem(AT_GMAX, 128, AT_SPAN));
                 if (e != cudaSuccess) return e;
-                configured[which] = 1;
+                configured[dev].fetch_or(1u << which);
             }
             cudaError_t e = launch_pdl(kern, dim3(n, a.kvh, nz), dim3(AT_THREADS), sm, st, a.qkv, a.pos, a.seq, l, a.h,
                                        a.kvh, a.group, a.cap, a.kv, a.kv_seq_bytes, a.kv_layer_bytes, a.sqrt_hd, span,

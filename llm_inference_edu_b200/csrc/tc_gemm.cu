@@ -28,6 +28,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 
 #include "tc_gemm.cuh"
@@ -41,6 +42,7 @@ constexpr int TC_THREADS = 256, TC_BM = 128, TC_BK = 64;
 constexpr uint32_t A_BYTES = TC_BM * TC_BK * 2;   // BF16 operand tile, 16 KB
 constexpr uint32_t S_BYTES = TC_BM * TC_BK;       // INT8 staging, 8 KB
 constexpr unsigned long long TC_TIMEOUT_NS = 2000000000ull;
+constexpr int kMaxDevices = 64;
 
 struct TcArgs {
     int n, N, nkb, kb_per, nt, stages, seg_kb;
@@ -555,15 +557,21 @@ size_t tc_smem_bytes(int wf, int nt, int stages) { return tc_fixed_bytes(nt, sta
 template <int WF, int EPI>
 cudaError_t launch(const TcJob &j, const TcArgs &g, dim3 grid, cudaStream_t st) {
     const size_t smem = tc_smem_bytes(WF, g.nt, g.stages);
-    static size_t configured = 0;  // largest size set for this instantiation
-    if (smem > configured) {
+    // Largest size set for this instantiation, per device (function
+    // attributes apply to the current device).
+    static std::atomic<size_t> configured[kMaxDevices];
+    int dev = 0;
+    cudaError_t de = cudaGetDevice(&dev);
+    if (de != cudaSuccess) return de;
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    if (smem > configured[dev].load()) {
         cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<WF, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)std::max<size_t>(smem, 200 * 1024));
         if (e != cudaSuccess) return e;
         // Clusters of up to 16 CTAs (K splits of one output tile).
         e = cudaFuncSetAttribute(tc_gemm_kernel<WF, EPI>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
         if (e != cudaSuccess) return e;
-        configured = std::max<size_t>(smem, 200 * 1024);
+        configured[dev].store(std::max<size_t>(smem, 200 * 1024));
     }
     // Dependent launch; the K splits of an output tile form one cluster.
     cudaLaunchConfig_t cfg = {};
