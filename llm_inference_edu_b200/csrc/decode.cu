@@ -36,6 +36,8 @@
 // 16-byte reads never conflict.
 #include <math.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 #include "decode.cuh"
 
@@ -564,7 +566,7 @@ __device__ __forceinline__ void lm_stream(const DecodeParams &p, const Ring &rg,
             for (int u = 0; u < rows; u += 2) {
                 const uint8_t *w0 = base + (size_t)u * g.stride;
                 float2 a0 = make_float2(0.0f, 0.0f), b0 = a0, a1 = a0, b1 = a0;
-#pragma unroll 2
+#pragma unroll 1
                 for (int c = lane; c < C; c += 32) {
                     float4 x[Q];
 #pragma unroll
@@ -1065,7 +1067,7 @@ __device__ __forceinline__ void prep_attention(const DecodeParams &p, const Deco
     if (WF == WF_I8 && cg.natt > 0) stage_ro<1>(sm + p.sm_rv, Ly.so + cg.att_r0[0], cg.att_n[0]);
 }
 
-template <int WF, int KVBF16>
+template <int WF, int KVBF16, int SPLIT>
 __device__ __forceinline__ void run_attention(const DecodeParams &p, const DecodeLayer &Ly, const CtaGeom &cg, int l,
                                               int pos, float *sm, const Ring &rg, Cursor &cur,
                                               volatile int *s_abort) {
@@ -1074,12 +1076,12 @@ __device__ __forceinline__ void run_attention(const DecodeParams &p, const Decod
 #pragma unroll 1
     for (int a = 0; a < cg.natt; ++a) {
         const int hh = cg.att_hh[a], r0 = cg.att_r0[a], n = cg.att_n[a];
-        const int nsp = p.att_splits > 1 && pos + 1 >= p.att_split_min ? p.att_splits : 1;
+        const int nsp = SPLIT && p.att_splits > 1 && pos + 1 >= p.att_split_min ? p.att_splits : 1;
         const int sp = cg.att_sp[a];
         const int lo = nsp > 1 ? (int)((long long)(pos + 1) * sp / nsp) : 0;
         const int hi = nsp > 1 ? (int)((long long)(pos + 1) * (sp + 1) / nsp) : pos + 1;
         attention_context<WF, KVBF16>(p, Ly, hh, r0 == 0 && hh % p.group == 0, pos, sm, lo, hi);
-        if (nsp > 1 && !split_exchange<WF>(p, hh, sp, nsp, l, sm, s_abort)) return;
+        if (SPLIT && nsp > 1 && !split_exchange<WF>(p, hh, sp, nsp, l, sm, s_abort)) return;
         float *outp = p.part + (size_t)hh * p.h + r0;
         const float *so = Ly.so + r0;
         team_gemv<WF, 1>(p, rg, cur, p.kind[K_O], n, xs, s_abort, [&](int r, float acc, float) {
@@ -1263,7 +1265,7 @@ __device__ __forceinline__ void run_lm_head(const DecodeParams &p, const CtaGeom
 
 // ------------------------------------------------------------ kernel ----
 
-template <int WF, int TF, int KVBF16>
+template <int WF, int TF, int KVBF16, int SPLIT>
 // Four warps per sub-partition x 32 threads x 128 registers = its 16K registers.
 __global__ void __maxnreg__(128) decode_kernel(const __grid_constant__ DecodeParams p) {
     extern __shared__ __align__(128) float sm[];
@@ -1322,7 +1324,7 @@ __global__ void __maxnreg__(128) decode_kernel(const __grid_constant__ DecodePar
         prep_attention<WF>(p, Ly, cg, sm);
         if (!(ok = barrier_wait(p, target, s_abort))) break;
 
-        run_attention<WF, KVBF16>(p, Ly, cg, l, pos, sm, rg, cur, s_abort);
+        run_attention<WF, KVBF16, SPLIT>(p, Ly, cg, l, pos, sm, rg, cur, s_abort);
         barrier_arrive(p, target += G);
         prep_gate_up<WF>(p, Ly, cg, sm);
         if (!(ok = barrier_wait(p, target, s_abort))) break;
@@ -1344,8 +1346,8 @@ __global__ void __maxnreg__(128) decode_kernel(const __grid_constant__ DecodePar
 size_t decode_smem_bytes(const DecodeParams &p) { return (size_t)p.sm_total * sizeof(float); }
 
 template <int WF, int TF, int KV>
-static cudaError_t launch_t(const DecodeParams &p, int grid, cudaStream_t stream) {
-    auto kern = decode_kernel<WF, TF, KV>;
+static cudaError_t launch_t(const DecodeParams &p, int grid, cudaStream_t stream, bool split) {
+    auto kern = split ? decode_kernel<WF, TF, KV, 1> : decode_kernel<WF, TF, KV, 0>;
     size_t smem = decode_smem_bytes(p);
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
@@ -1363,8 +1365,8 @@ static cudaError_t launch_t(const DecodeParams &p, int grid, cudaStream_t stream
 }
 
 template <int WF, int TF, int KV>
-static const void *kernel_ptr() {
-    return (const void *)decode_kernel<WF, TF, KV>;
+static const void *kernel_ptr(bool split) {
+    return split ? (const void *)decode_kernel<WF, TF, KV, 1> : (const void *)decode_kernel<WF, TF, KV, 0>;
 }
 
 // Dispatch over (linear format, table format, KV type).
@@ -1383,14 +1385,16 @@ struct LaunchOp {
     const DecodeParams &p;
     int grid;
     cudaStream_t stream;
-    template <int W, int T, int K> cudaError_t operator()() const { return launch_t<W, T, K>(p, grid, stream); }
+    bool split;
+    template <int W, int T, int K> cudaError_t operator()() const { return launch_t<W, T, K>(p, grid, stream, split); }
 };
 struct PtrOp {
-    template <int W, int T, int K> const void *operator()() const { return kernel_ptr<W, T, K>(); }
+    bool split;
+    template <int W, int T, int K> const void *operator()() const { return kernel_ptr<W, T, K>(split); }
 };
 
-cudaError_t decode_launch(const DecodeParams &p, int grid, cudaStream_t stream) {
-    return dispatch(p.wfmt, p.tfmt, p.kv_bf16, LaunchOp{p, grid, stream});
+cudaError_t decode_launch(const DecodeParams &p, int grid, cudaStream_t stream, bool split) {
+    return dispatch(p.wfmt, p.tfmt, p.kv_bf16, LaunchOp{p, grid, stream, split});
 }
 
 // Largest number of co-resident CTAs of the decode kernel on this device.
@@ -1398,10 +1402,14 @@ int decode_max_ctas(int wfmt, int tfmt, int kv_bf16, size_t smem) {
     int dev = 0, sms = 0, per = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const void *f = dispatch(wfmt, tfmt, kv_bf16, PtrOp{});
-    if (cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, f, kDecodeBlock, smem) != cudaSuccess) return 0;
-    return per * sms;
+    int lowest = 1 << 30;
+    for (int split = 0; split < 2; ++split) {
+        const void *f = dispatch(wfmt, tfmt, kv_bf16, PtrOp{split != 0});
+        if (cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, f, kDecodeBlock, smem) != cudaSuccess) return 0;
+        lowest = std::min(lowest, per * sms);
+    }
+    return lowest;
 }
 
 }  // namespace qb

@@ -121,7 +121,9 @@ struct DecodeParams {
 // Shared-memory bytes the kernel needs for these parameters.
 size_t decode_smem_bytes(const DecodeParams &p);
 // Launches one decode step (cooperative, one CTA per SM).
-cudaError_t decode_launch(const DecodeParams &p, int grid, cudaStream_t stream);
+// split: the instantiation with the long-context position-split attention
+// (used from att_split_min cached positions on; the other one never splits).
+cudaError_t decode_launch(const DecodeParams &p, int grid, cudaStream_t stream, bool split);
 // Compute threads per CTA; one more warp streams the weights.  16 warps in
 // all put 4 on each SM sub-partition, whose 16K registers then allow 128
 // registers per thread.

@@ -285,11 +285,14 @@ struct Session {
     std::unique_ptr<TcMaps> tcm;       // its tensor maps (built with it)
     DecodeParams params{};
     int grid = 0;
-    cudaGraphExec_t g_host = nullptr;
+    // One-step graphs: the decode kernel without, and with, the long-context
+    // position-split attention.
+    cudaGraphExec_t g_host = nullptr, g_host_split = nullptr;
     bool logits_valid = false;
     ~Session() {
         DeviceGuard dg(device);
         if (g_host) cudaGraphExecDestroy(g_host);
+        if (g_host_split) cudaGraphExecDestroy(g_host_split);
         if (hctrl) cudaFreeHost(hctrl);
         if (stream) cudaStreamDestroy(stream);
     }
@@ -576,24 +579,34 @@ static uint32_t session_build(Session &s) {
     int maxc = decode_max_ctas(wf, p.tfmt, s.kv_bf16, smem);
     if (maxc < s.grid) return QB_UNSUPPORTED;
 
-    // Graph: control block in, one decode step, result out.
-    cudaGraph_t g = nullptr;
-    QB_CUDA(cudaStreamBeginCapture(s.stream, cudaStreamCaptureModeThreadLocal));
-    cudaError_t e1 = cudaMemcpyAsync(s.ctrl.p, s.hctrl, 16, cudaMemcpyHostToDevice, s.stream);
-    cudaError_t e2 = decode_launch(p, s.grid, s.stream);
-    cudaError_t e3 = cudaMemcpyAsync((char *)s.hctrl + 16, (char *)s.ctrl.p + 16, 8, cudaMemcpyDeviceToHost, s.stream);
-    cudaError_t e4 = cudaStreamEndCapture(s.stream, &g);
-    if (e1 == cudaSuccess && e2 == cudaSuccess && e3 == cudaSuccess && e4 == cudaSuccess) {
-        cudaError_t e5 = cudaGraphInstantiate(&s.g_host, g, 0);
-        if (e5 != cudaSuccess) s.g_host = nullptr;
-    } else {
-        s.g_host = nullptr;
-        cudaGetLastError();
+    // Graphs: control block in, one decode step, result out.
+    for (int split = 0; split < 2; ++split) {
+        cudaGraphExec_t &gx = split ? s.g_host_split : s.g_host;
+        cudaGraph_t g = nullptr;
+        QB_CUDA(cudaStreamBeginCapture(s.stream, cudaStreamCaptureModeThreadLocal));
+        cudaError_t e1 = cudaMemcpyAsync(s.ctrl.p, s.hctrl, 16, cudaMemcpyHostToDevice, s.stream);
+        cudaError_t e2 = decode_launch(p, s.grid, s.stream, split != 0);
+        cudaError_t e3 =
+            cudaMemcpyAsync((char *)s.hctrl + 16, (char *)s.ctrl.p + 16, 8, cudaMemcpyDeviceToHost, s.stream);
+        cudaError_t e4 = cudaStreamEndCapture(s.stream, &g);
+        if (e1 == cudaSuccess && e2 == cudaSuccess && e3 == cudaSuccess && e4 == cudaSuccess) {
+            cudaError_t e5 = cudaGraphInstantiate(&gx, g, 0);
+            if (e5 != cudaSuccess) gx = nullptr;
+        } else {
+            gx = nullptr;
+            cudaGetLastError();
+        }
+        if (g) cudaGraphDestroy(g);
     }
-    if (g) cudaGraphDestroy(g);
     s.logical_bytes = kvh * cap * hd * 2 * L * 4;  // the reference's FP32 KV count
     s.workspace_bytes = ref_workspace_bytes(c, cap);
     return QB_OK;
+}
+
+// Whether the step at cached position `pos` takes the decode kernel with the
+// position-split attention (from att_split_min cached positions on).
+static bool split_at(const Session &s, size_t pos) {
+    return s.params.att_splits > 1 && pos + 1 >= (size_t)s.params.att_split_min;
 }
 
 // One decode step with a host-supplied token (graph replay).
@@ -601,11 +614,13 @@ static uint32_t session_launch(Session &s, uint32_t token, bool want_logits) {
     s.hctrl->token = (int)token;
     s.hctrl->pos = (int)s.processed;
     s.hctrl->write_logits = want_logits ? 1 : 0;
-    if (s.g_host) {
-        QB_CUDA(cudaGraphLaunch(s.g_host, s.stream));
+    const bool split = split_at(s, s.processed);
+    cudaGraphExec_t gx = split ? s.g_host_split : s.g_host;
+    if (gx) {
+        QB_CUDA(cudaGraphLaunch(gx, s.stream));
     } else {
         QB_CUDA(cudaMemcpyAsync(s.ctrl.p, s.hctrl, 16, cudaMemcpyHostToDevice, s.stream));
-        QB_CUDA(decode_launch(s.params, s.grid, s.stream));
+        QB_CUDA(decode_launch(s.params, s.grid, s.stream, split));
         QB_CUDA(cudaMemcpyAsync((char *)s.hctrl + 16, (char *)s.ctrl.p + 16, 8, cudaMemcpyDeviceToHost, s.stream));
     }
     return QB_OK;
@@ -1169,7 +1184,7 @@ uint32_t qb_session_step_profiled(uint64_t session, uint32_t token, float *logit
     s.hctrl->pos = (int)s.processed;
     s.hctrl->write_logits = 1;
     cudaError_t e = cudaMemcpyAsync(s.ctrl.p, s.hctrl, 16, cudaMemcpyHostToDevice, s.stream);
-    if (e == cudaSuccess) e = decode_launch(p, s.grid, s.stream);
+    if (e == cudaSuccess) e = decode_launch(p, s.grid, s.stream, split_at(s, s.processed));
     if (e == cudaSuccess)
         e = cudaMemcpyAsync((char *)s.hctrl + 16, (char *)s.ctrl.p + 16, 8, cudaMemcpyDeviceToHost, s.stream);
     if (e != cudaSuccess) return session_fail(s, cuda_status(e));
@@ -1218,7 +1233,8 @@ uint32_t qb_session_decode_greedy(uint64_t session, uint32_t token, size_t steps
     s.hctrl->pos = (int)start;
     s.hctrl->write_logits = 0;
     cudaError_t e = cudaMemcpyAsync(s.ctrl.p, s.hctrl, 16, cudaMemcpyHostToDevice, s.stream);
-    for (size_t i = 0; i < steps && e == cudaSuccess; ++i) e = decode_launch(s.params, s.grid, s.stream);
+    for (size_t i = 0; i < steps && e == cudaSuccess; ++i)
+        e = decode_launch(s.params, s.grid, s.stream, split_at(s, start + i));
     if (e == cudaSuccess)
         e = cudaMemcpyAsync((char *)s.hctrl + 16, (char *)s.ctrl.p + 16, 8, cudaMemcpyDeviceToHost, s.stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s.stream);
