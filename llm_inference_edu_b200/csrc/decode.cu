@@ -1016,7 +1016,7 @@ __device__ __forceinline__ void run_qkv(const DecodeParams &p, const CtaGeom &cg
 // barrier, then every split combines all slots in slot order, rescaled by
 // exp(m_j - m), into xs.  Returns false when aborting.
 template <int WF>
-__device__ __noinline__ bool split_exchange(const DecodeParams &p, int hh, int sp, int nsp, int l, float *sm,
+__device__ __forceinline__ bool split_exchange(const DecodeParams &p, int hh, int sp, int nsp, int l, float *sm,
                                             volatile int *s_abort) {
     constexpr int EPC = Fmt<WF>::EPC;
     const int t = threadIdx.x, hd = p.hd;
