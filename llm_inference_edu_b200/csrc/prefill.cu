@@ -125,6 +125,81 @@ __global__ void rmsnorm_rows(const float *x, const float *g, float *y, Planes P,
     }
 }
 
+// The same RMSNorm with one warp per row (rows of w <= 1024 elements, w a
+// multiple of 4): the row stays in registers and both reductions are warp
+// shuffles, with no CTA barrier.  Eight rows per 256-thread CTA.
+__global__ void rmsnorm_rows_warp(const float *x, const float *g, float *y, Planes P, int n, int w, float eps,
+                                  unsigned *err) {
+    pdl_trigger();
+    pdl_wait();
+    constexpr int V4 = 8;  // float4 per lane: w <= 32 * 4 * 8
+    const int lane = threadIdx.x & 31;
+    const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (t >= n) return;
+    const float4 *xr = reinterpret_cast<const float4 *>(x + (size_t)t * w);
+    const int w4 = w >> 2;
+    const float se = sqrtf(eps);
+    float4 v[V4];
+    float m = se;
+#pragma unroll
+    for (int k = 0; k < V4; ++k) {
+        const int i = lane + 32 * k;
+        v[k] = i < w4 ? xr[i] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (i < w4)
+            m = rust_max(rust_max(rust_max(rust_max(m, fabsf(v[k].x)), fabsf(v[k].y)), fabsf(v[k].z)), fabsf(v[k].w));
+    }
+    for (int off = 16; off; off >>= 1) m = rust_max(m, __shfl_xor_sync(0xffffffffu, m, off));
+    float ss = 0.0f;
+#pragma unroll
+    for (int k = 0; k < V4; ++k) {
+        if (lane + 32 * k < w4) {
+            const float a = v[k].x / m, b = v[k].y / m, c = v[k].z / m, d = v[k].w / m;
+            ss = ss + a * a;
+            ss = ss + b * b;
+            ss = ss + c * c;
+            ss = ss + d * d;
+        }
+    }
+    for (int off = 16; off; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    const float seps = se / m;
+    const float den = sqrtf(ss / (float)w + seps * seps);
+    float4 *yr = reinterpret_cast<float4 *>(y + (size_t)t * w);
+    const float4 *g4 = reinterpret_cast<const float4 *>(g);
+#pragma unroll
+    for (int k = 0; k < V4; ++k) {
+        const int i = lane + 32 * k;
+        if (i < w4) {
+            const float4 gg = g4[i];
+            float4 o;
+            o.x = (v[k].x / m) / den * gg.x;
+            o.y = (v[k].y / m) / den * gg.y;
+            o.z = (v[k].z / m) / den * gg.z;
+            o.w = (v[k].w / m) / den * gg.w;
+            yr[i] = o;
+            if (P.p) {
+                const size_t at = (size_t)t * w + 4 * (size_t)i;
+                store_planes(P, at, o.x);
+                store_planes(P, at + 1, o.y);
+                store_planes(P, at + 2, o.z);
+                store_planes(P, at + 3, o.w);
+            }
+            flag_bad(err, o.x);
+            flag_bad(err, o.y);
+            flag_bad(err, o.z);
+            flag_bad(err, o.w);
+        }
+    }
+}
+
+// Row RMSNorm launch: the warp-per-row kernel when the row fits it.
+cudaError_t rmsnorm(const float *x, const float *g, float *y, Planes P, int n, int w, float eps, unsigned *err,
+                    cudaStream_t st) {
+    if (w % 4 == 0 && w <= 32 * 4 * 8 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)y & 15) == 0 &&
+        ((uintptr_t)g & 15) == 0)
+        return launch_pdl(rmsnorm_rows_warp, dim3((n + 7) / 8), dim3(256), 0, st, x, g, y, P, n, w, eps, err);
+    return launch_pdl(rmsnorm_rows, dim3(std::min(n, 4096)), dim3(256), 0, st, x, g, y, P, n, w, eps, err);
+}
+
 // ----------------------------------------------------------------- gemm ----
 //
 // Y[t][r] = epilogue(sum_k X[t][k] W[r][k]) for t < n tokens and r < N rows,
@@ -764,8 +839,7 @@ cudaError_t forward_tokens(const PrefillArgs &a, int n, int max_pos, bool lm_hea
     cudaError_t e = cudaGetLastError();
     for (int l = 0; l < a.L && e == cudaSuccess; ++l) {
         const DecodeLayer &Ly = a.layers[l];
-        if ((e = launch_pdl(rmsnorm_rows, dim3(rows_grid), dim3(256), 0, st, a.x, Ly.attn_norm, a.xn, xn_planes(a), n,
-                            a.h, a.eps, a.err)) != cudaSuccess)
+        if ((e = rmsnorm(a.x, Ly.attn_norm, a.xn, xn_planes(a), n, a.h, a.eps, a.err, st)) != cudaSuccess)
             break;
         if ((e = run_gemm(0, a, l, n, st)) != cudaSuccess) break;
         if (!rope_fused(a) &&
@@ -777,16 +851,14 @@ cudaError_t forward_tokens(const PrefillArgs &a, int n, int max_pos, bool lm_hea
         if ((e = cudaGetLastError()) != cudaSuccess) break;
         if (l + 1 == a.L && !lm_head) break;  // the last layer's MLP feeds only the logits
         if ((e = run_gemm(1, a, l, n, st)) != cudaSuccess) break;
-        if ((e = launch_pdl(rmsnorm_rows, dim3(rows_grid), dim3(256), 0, st, a.h2, Ly.ffn_norm, a.xn, xn_planes(a),
-                            n, a.h, a.eps, a.err)) != cudaSuccess)
+        if ((e = rmsnorm(a.h2, Ly.ffn_norm, a.xn, xn_planes(a), n, a.h, a.eps, a.err, st)) != cudaSuccess)
             break;
         if ((e = run_gemm(2, a, l, n, st)) != cudaSuccess) break;
         if ((e = run_gemm(3, a, l, n, st)) != cudaSuccess) break;
     }
     if (e != cudaSuccess || !lm_head) return e;
     // Final norm, the LM head (tied table or untied head) and the argmax.
-    e = launch_pdl(rmsnorm_rows, dim3(rows_grid), dim3(256), 0, st, a.x, a.final_norm, a.xn, xn_planes(a), n, a.h,
-                   a.eps, a.err);
+    e = rmsnorm(a.x, a.final_norm, a.xn, xn_planes(a), n, a.h, a.eps, a.err, st);
     if (e != cudaSuccess) return e;
     const Planes none{nullptr, 0, TC_NP};
     GemmW w{a.head, a.semb, 0, a.h, nullptr, nullptr};
