@@ -517,21 +517,14 @@ __device__ __forceinline__ void team_gemv_g(const DecodeParams &p, const Ring &r
 // results to `epi(row, y0, y1)`.  Each warp frees the wave's slots as soon
 // as it is done with them.  A failed wait (timeout) leaves the abort flag
 // set; the caller tests it after its next CTA barrier.
-// Team sizes are restricted to G in {4, 8, 32} (the LM head: {8, 16, 32})
-// to bound the kernel's code size; the host picks among them.
+// Team sizes are restricted to G in {4, 8, 32} to bound the kernel's code
+// size; the host picks among them.  (The LM head streams through lm_stream.)
 template <int WF, int U, class Epi>
 __device__ __forceinline__ void team_gemv(const DecodeParams &p, const Ring &rg, Cursor &cur, const KindGeom &g,
                                           int n, const float *xs, volatile int *s_abort, Epi &&epi) {
     if (g.lgG == 2) team_gemv_g<WF, U, 2>(p, rg, cur, g, n, xs, s_abort, epi);
     else if (g.lgG == 3) team_gemv_g<WF, U, 3>(p, rg, cur, g, n, xs, s_abort, epi);
     else team_gemv_g<WF, U, 5>(p, rg, cur, g, n, xs, s_abort, epi);
-}
-template <int WF, class Epi>
-__device__ __forceinline__ void team_gemv_lm(const DecodeParams &p, const Ring &rg, Cursor &cur, const KindGeom &g,
-                                             int n, const float *xs, volatile int *s_abort, Epi &&epi) {
-    if (g.lgG == 3) team_gemv_g<WF, 2, 3>(p, rg, cur, g, n, xs, s_abort, epi);
-    else if (g.lgG == 4) team_gemv_g<WF, 2, 4>(p, rg, cur, g, n, xs, s_abort, epi);
-    else team_gemv_g<WF, 2, 5>(p, rg, cur, g, n, xs, s_abort, epi);
 }
 
 // The LM head's stream: the CTA's table rows arrive slot by slot, and each
