@@ -283,9 +283,10 @@ uint32_t qb_session_append(uint64_t session, const uint32_t *tokens, size_t coun
                            size_t logits_len, uint32_t *argmax, int32_t require_empty);
 /* step_profiled, src/kv_cache.rs:309-316: one step as qb_session_step that
  * also records device timestamps (ns, %globaltimer) into `stamps`:
- * [B][grid] barrier arrival times per CTA, then [B] barrier release times,
- * then the step's start and end, where B = 4 * layers (QKV, attention,
- * gate/up and down phases of every layer).  `*needed` receives the count;
+ * [B][grid] times at which each CTA finished each phase, then [B] times at
+ * which CTA 0 held the inputs of the phase after it, then the step's start
+ * and end, where B = 4 * layers (QKV, attention, gate/up and down phases of
+ * every layer).  `*needed` receives the count;
  * a short `stamps` buffer is an admission error (QB_INVALID_LENGTH). */
 uint32_t qb_session_step_profiled(uint64_t session, uint32_t token, float *logits,
                                   size_t logits_len, uint32_t *argmax, uint64_t *stamps,

@@ -402,9 +402,11 @@ class CachedSession:
 
         Returns (logits, profile).  profile["layers"][l] holds, for each of
         the phases "qkv", "attention", "gate_up", "down": wall ns from the
-        previous barrier release to this phase's release ("ns"), the slowest
-        CTA's work ("slowest_ns"), the mean CTA's work ("mean_ns") and the
-        barrier latency after the last arrival ("barrier_ns")."""
+        moment CTA 0 held this phase's inputs to the moment it held the next
+        phase's ("ns"), the slowest CTA's work ("slowest_ns"), the mean CTA's
+        work ("mean_ns") and the hand-over latency from the last CTA's finish
+        to CTA 0 holding its next inputs ("barrier_ns"; negative when CTA 0's
+        inputs did not wait for the last CTA)."""
         need = C.c_size_t()
         lib().qb_session_step_profiled(self.handle, 0, None, 0, None, None, 0, C.byref(need))
         stamps = np.zeros(need.value, dtype=np.uint64)

@@ -75,6 +75,30 @@ __device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long
     return v;
 }
 
+// Relaxed GPU-scope loads and store of words that other CTAs of the same
+// grid write or read while this one runs (volatile asm: polls are never
+// merged or hoisted).  Each 32-bit word is single-copy atomic.
+__device__ __forceinline__ uint32_t ld_relaxed_b32(const void *p) {
+    uint32_t v;
+    asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint2 ld_relaxed_v2(const void *p) {
+    uint2 v;
+    asm volatile("ld.relaxed.gpu.global.v2.b32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint4 ld_relaxed_v4(const void *p) {
+    uint4 v;
+    asm volatile("ld.relaxed.gpu.global.v4.b32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+__device__ __forceinline__ void st_relaxed_b32(void *p, uint32_t v) {
+    asm volatile("st.relaxed.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 // Streaming 16-byte load that bypasses L1 allocation (weights are read once).
 __device__ __forceinline__ uint4 ld_stream_u4(const void *p) {
     uint4 v;

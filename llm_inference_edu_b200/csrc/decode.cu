@@ -3,8 +3,9 @@
 // One cooperative launch evaluates one token through every layer and the LM
 // head (src/kv_cache.rs:347-475 with attend_one :479-590) and leaves the
 // greedy argmax (src/sampling.rs:65-70) in the control block.  The grid is
-// one CTA per SM: 15 compute warps and one producer warp.  Compute phases
-// are separated by a grid barrier whose wait is bounded by a timeout (the
+// one CTA per SM: 15 compute warps and one producer warp.  A phase's
+// outputs reach the next phase through exchange vectors that consumers poll
+// word by word (no grid barrier); every poll is bounded by a timeout (the
 // kernel then reports ERR_TIMEOUT and returns; it never spins forever):
 //
 //   per layer:  QKV      RMSNorm (each CTA, redundantly) -> rows of [Wq;Wk;Wv]
@@ -23,7 +24,7 @@
 // step, in order -- through a shared-memory ring of `nslot` slots with 1-D
 // bulk copies (cp.async.bulk ... mbarrier::complete_tx), waiting only for
 // the compute warps to free a slot ("empty" mbarrier, one arrival per compute
-// warp).  It never waits for a grid barrier, so a phase's weights are in
+// warp).  It never waits for another CTA, so a phase's weights are in
 // shared memory before the activations they meet exist.
 //
 // Latency discipline.  Batch-1 decode moves ~1 MB per CTA per step; what
@@ -201,24 +202,9 @@ __device__ __forceinline__ void flag_nonfinite(DecodeCtrl *ctrl, float v) {
     if (!isfinite(v)) atomicOr(&ctrl->error, ERR_NONFINITE);
 }
 
-// dst[i] = src[i], i < n (L2-coherent loads: src was written earlier in
-// this step by other CTAs), 16 bytes per load when n % 4 == 0.
-__device__ __forceinline__ void stage_l2(float *dst, const float *src, int n) {
-    if ((n & 3) == 0) {
-        const float4 *s4 = reinterpret_cast<const float4 *>(src);
-        float4 *d4 = reinterpret_cast<float4 *>(dst);
-#pragma unroll 2
-        for (int i = threadIdx.x; i < n / 4; i += NT) d4[i] = __ldcg(s4 + i);
-    } else {
-#pragma unroll 2
-        for (int i = threadIdx.x; i < n; i += NT) dst[i] = ldcg(src + i);
-    }
-}
-
-// The same for read-only model vectors (gains, scales, biases), by the
-// compute warps other than warp 0: the next phase's vectors are staged while
-// the grid barrier completes, and warp 0 (whose thread 0 polls the barrier)
-// must not wait for these loads before it starts polling.
+// dst[i] = src[i], i < n, for read-only model vectors (gains, scales,
+// biases), by the compute warps other than warp 0 (which starts polling the
+// phase's inputs without waiting for these loads).
 template <int B>
 __device__ __forceinline__ void stage_ro(float *dst, const float *src, int n) {
     constexpr int NS = NT - 32;
@@ -588,52 +574,133 @@ __device__ __forceinline__ void lm_stream(const DecodeParams &p, const Ring &rg,
     while (cur.slot >= rg.nslot) { cur.slot -= rg.nslot; ++cur.round; }
 }
 
-// ------------------------------------------------------------ barrier ----
+// ----------------------------------------------------------- exchange ----
+//
+// Phases hand their outputs to the CTAs that need them through exchange
+// vectors instead of a grid barrier: each output word is published once per
+// step with a relaxed store, and a consumer polls exactly the words it reads
+// until none is kNotReady.  A 32-bit word is single-copy atomic, so a word
+// that is not kNotReady is the producer's value; no fence or counter sits on
+// the path.  Every CTA is co-resident (cooperative launch) and every phase
+// only waits for outputs of the phase before it, so the polls end; each is
+// bounded by the timeout all the same.
 
-// Grid barrier in two halves (compute warps only).  barrier_arrive makes
-// the CTA's writes visible (csync, then thread 0's release reduction);
-// independent work can run before barrier_wait, which polls with acquire
-// loads (bounded by the timeout) and ends with a csync.
-// barrier_wait returns false (uniformly, after recording ERR_TIMEOUT and
-// raising the abort flag) when the arrivals do not complete in time, when
-// another CTA has timed out, or when this CTA is already aborting.
-__device__ __forceinline__ void barrier_arrive(const DecodeParams &p, unsigned target) {
-    csync();
-    if (threadIdx.x == 0) {
-        if (p.trace) {
-            const int G = gridDim.x, idx = (int)(target / (unsigned)G) - 1;
-            p.trace[(size_t)idx * G + blockIdx.x] = globaltimer_ns();
+// Vector `off` of layer l in this step's exchange (xcur: its parity).
+__device__ __forceinline__ float *xv(const DecodeParams &p, float *xcur, int l, int off) {
+    return xcur + (size_t)l * p.xl + off;
+}
+
+// Publishes v in an exchange slot of this step.
+__device__ __forceinline__ void publish(float *slot, float v) {
+    uint32_t b = __float_as_uint(v);
+    if (b == kNotReady) b = 0x7fffffffu;
+    st_relaxed_b32(slot, b);
+}
+
+// Resets this CTA's share of the other parity (the next step's exchange)
+// to kNotReady; nothing reads or writes that parity during this step.  Run
+// by the producer warp, off the compute path.
+__device__ __forceinline__ void reset_next(const DecodeParams &p, unsigned par) {
+    const size_t words = (size_t)p.L * p.xl;  // a multiple of 4
+    uint4 *nx = reinterpret_cast<uint4 *>(p.xch + (size_t)(par ^ 1u) * words);
+    const size_t n4 = words >> 2, G = gridDim.x, b = blockIdx.x;
+    const size_t lo = n4 * b / G, hi = n4 * (b + 1) / G;
+    const uint4 nr = make_uint4(kNotReady, kNotReady, kNotReady, kNotReady);
+#pragma unroll 4
+    for (size_t i = lo + (threadIdx.x & 31); i < hi; i += 32) nx[i] = nr;
+}
+
+// Poll bookkeeping of one thread: again() is true while the thread may poll
+// once more; false after the timeout (ERR_TIMEOUT recorded, abort raised) or
+// once this CTA or another one is aborting.  The clock and the flags are
+// read every 64 polls.
+struct Poll {
+    uint64_t t0 = 0;
+    unsigned it = 0;
+    __device__ __forceinline__ bool again(const DecodeParams &p, volatile int *s_abort) {
+        if (it++ == 0) {
+            t0 = globaltimer_ns();
+            return true;
         }
-        red_release_add_u32(&p.ctrl->bar, 1u);
+        if ((it & 63u) != 0) return true;
+        if (*s_abort || (*(volatile unsigned *)&p.ctrl->error & ERR_TIMEOUT) ||
+            globaltimer_ns() - t0 > p.timeout_ns) {
+            atomicOr(&p.ctrl->error, ERR_TIMEOUT);
+            *s_abort = 1;
+            return false;
+        }
+        return true;
+    }
+};
+
+__device__ __forceinline__ bool ready2(const uint2 &v) { return v.x != kNotReady && v.y != kNotReady; }
+__device__ __forceinline__ bool ready4(const uint4 &v) {
+    return v.x != kNotReady && v.y != kNotReady && v.z != kNotReady && v.w != kNotReady;
+}
+
+// One exchange word, polled until ready.
+__device__ __forceinline__ float await1(const DecodeParams &p, const float *a, volatile int *s_abort) {
+    uint32_t v = ld_relaxed_b32(a);
+    Poll pl;
+#pragma unroll 1
+    while (v == kNotReady && pl.again(p, s_abort)) v = ld_relaxed_b32(a);
+    return __uint_as_float(v);
+}
+
+// Four exchange words, all loads in flight at once; a pass reloads only the
+// words still missing.
+__device__ __forceinline__ void await4(const DecodeParams &p, const float *a0, const float *a1, const float *a2,
+                                       const float *a3, float &o0, float &o1, float &o2, float &o3,
+                                       volatile int *s_abort) {
+    uint32_t v0 = ld_relaxed_b32(a0), v1 = ld_relaxed_b32(a1), v2 = ld_relaxed_b32(a2), v3 = ld_relaxed_b32(a3);
+    Poll pl;
+#pragma unroll 1
+    while ((v0 == kNotReady || v1 == kNotReady || v2 == kNotReady || v3 == kNotReady) && pl.again(p, s_abort)) {
+        if (v0 == kNotReady) v0 = ld_relaxed_b32(a0);
+        if (v1 == kNotReady) v1 = ld_relaxed_b32(a1);
+        if (v2 == kNotReady) v2 = ld_relaxed_b32(a2);
+        if (v3 == kNotReady) v3 = ld_relaxed_b32(a3);
+    }
+    o0 = __uint_as_float(v0);
+    o1 = __uint_as_float(v1);
+    o2 = __uint_as_float(v2);
+    o3 = __uint_as_float(v3);
+}
+
+// dst[i] = src[i], i < n, from an exchange vector (16 bytes per load when
+// n % 4 == 0 and src is 16-byte aligned).
+__device__ __forceinline__ void await_stage(const DecodeParams &p, float *dst, const float *src, int n,
+                                            volatile int *s_abort) {
+    if ((n & 3) == 0 && ((uintptr_t)src & 15) == 0) {
+        const uint4 *s4 = reinterpret_cast<const uint4 *>(src);
+        uint4 *d4 = reinterpret_cast<uint4 *>(dst);
+#pragma unroll 1
+        for (int i = threadIdx.x; i < (n >> 2); i += NT) {
+            uint4 v = ld_relaxed_v4(s4 + i);
+            Poll pl;
+#pragma unroll 1
+            while (!ready4(v) && pl.again(p, s_abort)) v = ld_relaxed_v4(s4 + i);
+            d4[i] = v;
+        }
+    } else {
+#pragma unroll 1
+        for (int i = threadIdx.x; i < n; i += NT) dst[i] = await1(p, src + i, s_abort);
     }
 }
 
-__device__ __forceinline__ bool barrier_wait(const DecodeParams &p, unsigned target, volatile int *s_abort) {
-    DecodeCtrl *ctrl = p.ctrl;
-    if (threadIdx.x == 0) {
-        // Acquire loads: the one that sees the final count synchronizes with
-        // every CTA's release reduction, and the CTA barrier below carries
-        // that ordering to the other compute threads.
-        if (ld_acquire_u32(&ctrl->bar) < target) {
-            const uint64_t t0 = globaltimer_ns();
-            unsigned spins = 0;
-            while (ld_acquire_u32(&ctrl->bar) < target) {
-                if ((++spins & 63u) == 0) {
-                    if ((*(volatile unsigned *)&ctrl->error & ERR_TIMEOUT) || globaltimer_ns() - t0 > p.timeout_ns) {
-                        atomicOr(&ctrl->error, ERR_TIMEOUT);
-                        *s_abort = 1;
-                        break;
-                    }
-                }
-            }
-        }
-        if (p.trace && blockIdx.x == 0) {
-            const int G = gridDim.x, idx = (int)(target / (unsigned)G) - 1;
-            p.trace[(size_t)4 * p.L * G + idx] = globaltimer_ns();
-        }
-    }
+// End of a phase: every compute thread is done with the phase's shared
+// vectors (the next phase's prep overwrites them), and the trace records
+// the CTA's finish.  False when aborting (uniform after the CTA barrier).
+__device__ __forceinline__ bool phase_end(const DecodeParams &p, int idx, volatile int *s_abort) {
     csync();
+    if (p.trace && threadIdx.x == 0) p.trace[(size_t)idx * gridDim.x + blockIdx.x] = globaltimer_ns();
     return *s_abort == 0;
+}
+
+// Trace mark: CTA 0 holds the inputs of the phase after phase idx.
+__device__ __forceinline__ void mark_ready(const DecodeParams &p, int idx) {
+    if (p.trace && idx >= 0 && blockIdx.x == 0 && threadIdx.x == 0)
+        p.trace[(size_t)4 * p.L * gridDim.x + idx] = globaltimer_ns();
 }
 
 // --------------------------------------------------------- elementwise ----
@@ -642,64 +709,71 @@ __device__ __forceinline__ float round_bf16(float x) {
     return __uint_as_float((uint32_t)f32_to_bf16_rne(x) << 16);
 }
 
-// Residual-stream input of layer l at element i: the embedding row for
-// layer 0, the previous layer's output otherwise.
-__device__ __forceinline__ float resid_in(const DecodeParams &p, int l, int token, int i) {
-    if (l > 0) return ldcg(p.hidden + i);
+// Element i of the token's embedding row (the residual input of layer 0).
+__device__ __forceinline__ float emb_in(const DecodeParams &p, int token, int i) {
     const uint8_t *row = p.emb + (size_t)token * p.semb;
     return p.tfmt == WF_BF16 ? bf16_to_f32(((const uint16_t *)row)[i]) : ((const float *)row)[i];
 }
 
-// h2 = x + o_proj(ctx): the per-head partials summed in head order, then the
-// residual added (src/kv_cache.rs:405-406).  All of an element's loads are
-// issued before the first add.
-__device__ __forceinline__ void stage_after_attention(const DecodeParams &p, int l, int token, float *h2) {
-    constexpr int HB = 16;
+// h2 = x + o_proj(ctx) (src/kv_cache.rs:405-406): h2 already holds the
+// layer's input x (staged by the QKV phase); the per-head partials are
+// polled from the exchange, summed in head order, then added.  All of a
+// batch's partials are in flight at once; a pass reloads only the missing.
+__device__ __forceinline__ void stage_after_attention(const DecodeParams &p, float *xcur, int l, float *h2,
+                                                      volatile int *s_abort) {
+    const float *part = xv(p, xcur, l, p.x_part);
     const size_t stride = (size_t)p.h;
-    if ((p.h & 1) == 0 && (l > 0 || p.tfmt == WF_F32) && p.h <= 2 * NT) {
-        // 8-byte loads: two consecutive elements per thread, every head's
-        // partial in flight at once (up to 16 heads per batch).
-        constexpr int HB2 = 16;
-        const int n2 = p.h >> 1;
-        const float2 *part2 = reinterpret_cast<const float2 *>(p.part);
-        const float2 *res2 = reinterpret_cast<const float2 *>(l > 0 ? p.hidden : (const float *)(p.emb + (size_t)token * p.semb));
-        float2 *h2v = reinterpret_cast<float2 *>(h2);
-        const int i = threadIdx.x;
-        if (i < n2) {
-            const float2 r = l > 0 ? __ldcg(res2 + i) : __ldg(res2 + i);
+    if ((p.h & 1) == 0) {
+        // 8-byte loads: two consecutive elements per thread and pass, up to
+        // 14 heads per batch (more would spill registers).
+        constexpr int HB = 14;
+#pragma unroll 1
+        for (int i = threadIdx.x; i < (p.h >> 1); i += NT) {
+            const uint2 *part2 = reinterpret_cast<const uint2 *>(part) + i;
+            const int s2 = p.h >> 1;
             float2 o = make_float2(0.0f, 0.0f);
 #pragma unroll 1
-            for (int h0 = 0; h0 < p.qh; h0 += HB2) {
-                float2 v[HB2];
+            for (int h0 = 0; h0 < p.qh; h0 += HB) {
+                uint2 v[HB];
 #pragma unroll
-                for (int k = 0; k < HB2; ++k)
-                    if (h0 + k < p.qh) v[k] = __ldcg(part2 + (size_t)(h0 + k) * (stride >> 1) + i);
+                for (int k = 0; k < HB; ++k)
+                    if (h0 + k < p.qh) v[k] = ld_relaxed_v2(part2 + (h0 + k) * s2);
+                Poll pl;
+#pragma unroll 1
+                for (;;) {
+                    bool all = true;
 #pragma unroll
-                for (int k = 0; k < HB2; ++k) {
+                    for (int k = 0; k < HB; ++k)
+                        if (h0 + k < p.qh && !ready2(v[k])) {
+                            all = false;
+                            v[k] = ld_relaxed_v2(part2 + (h0 + k) * s2);
+                        }
+                    if (all || !pl.again(p, s_abort)) break;
+                }
+#pragma unroll
+                for (int k = 0; k < HB; ++k) {
                     if (h0 + k < p.qh) {
-                        if (h0 + k == 0) o = v[k];
-                        else { o.x = o.x + v[k].x; o.y = o.y + v[k].y; }
+                        const float2 f = make_float2(__uint_as_float(v[k].x), __uint_as_float(v[k].y));
+                        if (h0 + k == 0) o = f;
+                        else { o.x = o.x + f.x; o.y = o.y + f.y; }
                     }
                 }
             }
-            h2v[i] = make_float2(r.x + o.x, r.y + o.y);
+            float2 *h2v = reinterpret_cast<float2 *>(h2) + i;
+            const float2 r = *h2v;
+            *h2v = make_float2(r.x + o.x, r.y + o.y);
         }
         return;
     }
-#pragma unroll 2
+#pragma unroll 1
     for (int i = threadIdx.x; i < p.h; i += NT) {
-        const float r = resid_in(p, l, token, i);
         float o = 0.0f;
 #pragma unroll 1
-        for (int h0 = 0; h0 < p.qh; h0 += HB) {
-            float v[HB];
-#pragma unroll
-            for (int k = 0; k < HB; ++k) v[k] = h0 + k < p.qh ? ldcg(p.part + (size_t)(h0 + k) * stride + i) : 0.0f;
-#pragma unroll
-            for (int k = 0; k < HB; ++k)
-                if (h0 + k < p.qh) o = (h0 + k == 0) ? v[k] : o + v[k];
+        for (int hh = 0; hh < p.qh; ++hh) {
+            const float v = await1(p, part + (size_t)hh * stride + i, s_abort);
+            o = hh == 0 ? v : o + v;
         }
-        h2[i] = r + o;
+        h2[i] = h2[i] + o;
     }
 }
 
@@ -751,9 +825,12 @@ __device__ __forceinline__ bool head_barrier(const DecodeParams &p, int hh, unsi
 // context lands in xs.  With a split (vectorised layouts only) the warps'
 // unnormalized context sums stay in red[2 NW + w hd + i], with the maximum
 // at red[2 NW + NW hd] and the sum after it, for split_exchange.
+// q, k and v come from the exchange (qkv: this layer's QKV outputs); `mark`
+// is the trace index recorded once they are staged (-1: none).
 template <int WF, int KVBF16>
-__device__ __forceinline__ void attention_context(const DecodeParams &p, const DecodeLayer &Ly, int hh, bool writer,
-                                                  int pos, float *sm, int lo, int hi) {
+__device__ __forceinline__ void attention_context(const DecodeParams &p, const DecodeLayer &Ly, const float *qkv,
+                                                  int hh, bool writer, int pos, float *sm, int lo, int hi, int mark,
+                                                  volatile int *s_abort) {
     const bool split = hi - lo < pos + 1;
     constexpr int EPC = Fmt<WF>::EPC;
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
@@ -768,9 +845,9 @@ __device__ __forceinline__ void attention_context(const DecodeParams &p, const D
 #pragma unroll 1
         for (int j = t; j < half; j += NT / 2) {
             const float2 cs = rp[j];
-            const float a = ldcg(p.qkv + (size_t)hh * hd + j), b = ldcg(p.qkv + (size_t)hh * hd + j + half);
-            const float ka = ldcg(p.qkv + p.h + (size_t)g * hd + j);
-            const float kb = ldcg(p.qkv + p.h + (size_t)g * hd + j + half);
+            const float *qa = qkv + (size_t)hh * hd + j, *kq = qkv + p.h + (size_t)g * hd + j;
+            float a, b, ka, kb;
+            await4(p, qa, qa + half, kq, kq + half, a, b, ka, kb, s_abort);
             qs[j] = a * cs.x - b * cs.y;
             qs[j + half] = b * cs.x + a * cs.y;
             float k0 = ka * cs.x - kb * cs.y, k1 = kb * cs.x + ka * cs.y;
@@ -781,11 +858,12 @@ __device__ __forceinline__ void attention_context(const DecodeParams &p, const D
     } else {
 #pragma unroll 1
         for (int i = t - NT / 2; i < hd; i += NT / 2) {
-            const float v = ldcg(p.qkv + p.h + kvw + (size_t)g * hd + i);
+            const float v = await1(p, qkv + p.h + kvw + (size_t)g * hd + i, s_abort);
             vs[i] = KVBF16 ? round_bf16(v) : v;
         }
     }
     csync();
+    mark_ready(p, mark);
 #pragma unroll 1
     for (int i = t; i < hd; i += NT)
         if (!isfinite(qs[i]) || !isfinite(ks[i])) atomicOr(&p.ctrl->error, ERR_NONFINITE);
@@ -979,27 +1057,29 @@ __device__ __forceinline__ void prep_qkv(const DecodeParams &p, const DecodeLaye
 }
 
 template <int WF>
-__device__ __forceinline__ void run_qkv(const DecodeParams &p, const CtaGeom &cg, int l, int token, float *sm,
-                                        const Ring &rg, Cursor &cur, volatile int *s_abort) {
+__device__ __forceinline__ void run_qkv(const DecodeParams &p, const CtaGeom &cg, float *xcur, int l, int token,
+                                        float *sm, const Ring &rg, Cursor &cur, volatile int *s_abort) {
     constexpr int EPC = Fmt<WF>::EPC;
     float *xs = sm + p.sm_xs, *h2 = sm + p.sm_h2;
     const float *gain = sm + p.sm_gain, *rv = sm + p.sm_rv;
     if (l > 0) {
-        stage_l2(h2, p.hidden, p.h);
+        await_stage(p, h2, xv(p, xcur, l - 1, p.x_hid), p.h, s_abort);
     } else {
 #pragma unroll 2
-        for (int i = threadIdx.x; i < p.h; i += NT) h2[i] = resid_in(p, 0, token, i);
+        for (int i = threadIdx.x; i < p.h; i += NT) h2[i] = emb_in(p, token, i);
     }
     csync();
+    mark_ready(p, 4 * l - 1);
+    if (*s_abort) return;
     block_rmsnorm<EPC>(h2, gain, xs, p.h, p.ch, p.eps, sm + p.sm_red);
     const int R = cg.qkv_n;
-    float *out = p.qkv + cg.qkv_r0;
+    float *out = xv(p, xcur, l, p.x_qkv) + cg.qkv_r0;
     DecodeCtrl *ctrl = p.ctrl;
     team_gemv<WF, 1>(p, rg, cur, p.kind[K_QKV], R, xs, s_abort, [&](int r, float a, float) {
         float v = a;
         if (WF == WF_I8) v = v * rv[r];
         v = v + rv[R + r];
-        out[r] = v;
+        publish(out + r, v);
         flag_nonfinite(ctrl, v);
     });
 }
@@ -1061,8 +1141,8 @@ __device__ __forceinline__ void prep_attention(const DecodeParams &p, const Deco
 }
 
 template <int WF, int KVBF16, int SPLIT>
-__device__ __forceinline__ void run_attention(const DecodeParams &p, const DecodeLayer &Ly, const CtaGeom &cg, int l,
-                                              int pos, float *sm, const Ring &rg, Cursor &cur,
+__device__ __forceinline__ void run_attention(const DecodeParams &p, const DecodeLayer &Ly, const CtaGeom &cg,
+                                              float *xcur, int l, int pos, float *sm, const Ring &rg, Cursor &cur,
                                               volatile int *s_abort) {
     const float *rv = sm + p.sm_rv, *xs = sm + p.sm_xs;
     DecodeCtrl *ctrl = p.ctrl;
@@ -1073,14 +1153,15 @@ __device__ __forceinline__ void run_attention(const DecodeParams &p, const Decod
         const int sp = cg.att_sp[a];
         const int lo = nsp > 1 ? (int)((long long)(pos + 1) * sp / nsp) : 0;
         const int hi = nsp > 1 ? (int)((long long)(pos + 1) * (sp + 1) / nsp) : pos + 1;
-        attention_context<WF, KVBF16>(p, Ly, hh, r0 == 0 && hh % p.group == 0, pos, sm, lo, hi);
+        attention_context<WF, KVBF16>(p, Ly, xv(p, xcur, l, p.x_qkv), hh, r0 == 0 && hh % p.group == 0, pos, sm,
+                                      lo, hi, a == 0 ? 4 * l : -1, s_abort);
         if (SPLIT && nsp > 1 && !split_exchange<WF>(p, hh, sp, nsp, l, sm, s_abort)) return;
-        float *outp = p.part + (size_t)hh * p.h + r0;
+        float *outp = xv(p, xcur, l, p.x_part) + (size_t)hh * p.h + r0;
         const float *so = Ly.so + r0;
         team_gemv<WF, 1>(p, rg, cur, p.kind[K_O], n, xs, s_abort, [&](int r, float acc, float) {
             float v = acc;
             if (WF == WF_I8) v = v * (a == 0 ? rv[r] : __ldg(so + r));
-            outp[r] = v;
+            publish(outp + r, v);
             flag_nonfinite(ctrl, v);
         });
         if (a + 1 < cg.natt) csync();  // xs is rewritten by the next item
@@ -1095,17 +1176,19 @@ __device__ __forceinline__ void prep_gate_up(const DecodeParams &p, const Decode
 }
 
 template <int WF>
-__device__ __forceinline__ void run_gate_up(const DecodeParams &p, const CtaGeom &cg, int l, int token, float *sm,
+__device__ __forceinline__ void run_gate_up(const DecodeParams &p, const CtaGeom &cg, float *xcur, int l, float *sm,
                                             const Ring &rg, Cursor &cur, volatile int *s_abort) {
     constexpr int EPC = Fmt<WF>::EPC;
     float *xs = sm + p.sm_xs, *h2 = sm + p.sm_h2;
     const float *gain = sm + p.sm_gain, *rv = sm + p.sm_rv;
-    stage_after_attention(p, l, token, h2);
+    stage_after_attention(p, xcur, l, h2, s_abort);
     csync();
+    mark_ready(p, 4 * l + 1);
+    if (*s_abort) return;
     if (blockIdx.x == 0)
         for (int i = threadIdx.x; i < p.h; i += NT) flag_nonfinite(p.ctrl, h2[i]);
     block_rmsnorm<EPC>(h2, gain, xs, p.h, p.ch, p.eps, sm + p.sm_red);
-    float *act = p.act + cg.gu_f0;
+    float *act = xv(p, xcur, l, p.x_act) + cg.gu_f0;
     DecodeCtrl *ctrl = p.ctrl;
     team_gemv<WF, 2>(p, rg, cur, p.kind[K_GU], 2 * cg.gu_n, xs, s_abort, [&](int row, float g, float u) {
         if (WF == WF_I8) {
@@ -1113,7 +1196,7 @@ __device__ __forceinline__ void run_gate_up(const DecodeParams &p, const CtaGeom
             u = u * rv[row + 1];
         }
         const float a = silu1(g) * u;
-        act[row >> 1] = a;
+        publish(act + (row >> 1), a);
         flag_nonfinite(ctrl, g);
         flag_nonfinite(ctrl, a);
     });
@@ -1126,24 +1209,38 @@ __device__ __forceinline__ void prep_down(const DecodeParams &p, const DecodeLay
 }
 
 template <int WF>
-__device__ __forceinline__ void run_down(const DecodeParams &p, const CtaGeom &cg, float *sm, const Ring &rg,
-                                         Cursor &cur, volatile int *s_abort) {
+__device__ __forceinline__ void run_down(const DecodeParams &p, const CtaGeom &cg, float *xcur, int l, float *sm,
+                                         const Ring &rg, Cursor &cur, volatile int *s_abort) {
     constexpr int EPC = Fmt<WF>::EPC;
-    constexpr int B = 16;
     float *xs = sm + p.sm_xs;
     const int padded = p.cff * EPC;
+    const float *actv = xv(p, xcur, l, p.x_act);
     if ((p.ff & 3) == 0) {
         // act -> xs: four consecutive elements are one quad of the layout.
-        const float4 *a4 = reinterpret_cast<const float4 *>(p.act);
-        float4 *x4 = reinterpret_cast<float4 *>(xs);
+        const uint4 *a4 = reinterpret_cast<const uint4 *>(actv);
+        uint4 *x4 = reinterpret_cast<uint4 *>(xs);
         constexpr int B4 = 4;
 #pragma unroll 1
         for (int base = threadIdx.x; base < padded / 4; base += B4 * NT) {
-            float4 v[B4];
+            uint4 v[B4];
 #pragma unroll
             for (int k = 0; k < B4; ++k) {
                 const int e = 4 * (base + k * NT);
-                v[k] = e < p.ff ? __ldcg(a4 + (e >> 2)) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                v[k] = e < p.ff ? ld_relaxed_v4(a4 + (e >> 2)) : make_uint4(0u, 0u, 0u, 0u);
+            }
+            Poll pl;
+#pragma unroll 1
+            for (;;) {
+                bool all = true;
+#pragma unroll
+                for (int k = 0; k < B4; ++k) {
+                    const int e = 4 * (base + k * NT);
+                    if (e < p.ff && !ready4(v[k])) {
+                        all = false;
+                        v[k] = ld_relaxed_v4(a4 + (e >> 2));
+                    }
+                }
+                if (all || !pl.again(p, s_abort)) break;
             }
 #pragma unroll
             for (int k = 0; k < B4; ++k) {
@@ -1151,32 +1248,23 @@ __device__ __forceinline__ void run_down(const DecodeParams &p, const CtaGeom &c
                 if (e < padded) x4[((e % EPC) >> 2) * p.cff + e / EPC] = v[k];
             }
         }
-    } else
+    } else {
 #pragma unroll 1
-    for (int base = threadIdx.x; base < padded; base += B * NT) {
-        float v[B];
-#pragma unroll
-        for (int k = 0; k < B; ++k) {
-            const int i = base + k * NT;
-            v[k] = i < p.ff ? ldcg(p.act + i) : 0.0f;
-        }
-#pragma unroll
-        for (int k = 0; k < B; ++k) {
-            const int i = base + k * NT;
-            if (i < padded) xs[xq<EPC>(i, p.cff)] = v[k];
-        }
+        for (int i = threadIdx.x; i < padded; i += NT) xs[xq<EPC>(i, p.cff)] = i < p.ff ? await1(p, actv + i, s_abort) : 0.0f;
     }
     csync();
+    mark_ready(p, 4 * l + 2);
+    if (*s_abort) return;
     // h' of this layer is still in shared memory from the gate/up phase of
     // this same CTA (src/kv_cache.rs:437-443: x_next = h' + down(a)).
     const float *h2 = sm + p.sm_h2 + cg.dn_r0, *rv = sm + p.sm_rv;
-    float *hidden = p.hidden + cg.dn_r0;
+    float *hid = xv(p, xcur, l, p.x_hid) + cg.dn_r0;
     DecodeCtrl *ctrl = p.ctrl;
     team_gemv<WF, 1>(p, rg, cur, p.kind[K_DN], cg.dn_n, xs, s_abort, [&](int r, float acc, float) {
         float v = acc;
         if (WF == WF_I8) v = v * rv[r];
         const float o = h2[r] + v;
-        hidden[r] = o;
+        publish(hid + r, o);
         flag_nonfinite(ctrl, o);
     });
 }
@@ -1186,16 +1274,18 @@ __device__ __forceinline__ void run_down(const DecodeParams &p, const CtaGeom &c
 // logits of all the CTA's rows land in `rowv`; warp 0 scans them in row
 // order, so ties keep the lowest id.
 template <int TF>
-__device__ __forceinline__ void run_lm_head(const DecodeParams &p, const CtaGeom &cg, int pos, float *sm,
-                                            const Ring &rg, Cursor &cur, volatile int *s_abort) {
+__device__ __forceinline__ void run_lm_head(const DecodeParams &p, const CtaGeom &cg, float *xcur, int pos,
+                                            float *sm, const Ring &rg, Cursor &cur, volatile int *s_abort) {
     constexpr int TEPC = Fmt<TF>::EPC;
     const int G = gridDim.x, b = blockIdx.x;
     float *xs = sm + p.sm_xs, *h2 = sm + p.sm_h2;
     const float *gain = sm + p.sm_gain;
     float *rowv = sm + p.sm_sc;
     DecodeCtrl *ctrl = p.ctrl;
-    stage_l2(h2, p.hidden, p.h);
+    await_stage(p, h2, xv(p, xcur, p.L - 1, p.x_hid), p.h, s_abort);
     csync();
+    mark_ready(p, 4 * p.L - 1);
+    if (*s_abort) return;
     block_rmsnorm<TEPC>(h2, gain, xs, p.h, p.cemb, p.eps, sm + p.sm_red);
     const int nlm = cg.lm_n;
     lm_stream<TF>(p, rg, cur, p.kind[K_LM], nlm, xs, s_abort, [&](int r, float a0, float a1) {
@@ -1245,7 +1335,7 @@ __device__ __forceinline__ void run_lm_head(const DecodeParams &p, const CtaGeom
                 if (p.emitted) p.emitted[pos] = gi;
                 ctrl->token = gi;
                 ctrl->pos = pos + 1;
-                ctrl->bar = 0;
+                ctrl->epoch = ctrl->epoch + 1u;
                 ctrl->ticket = 0;
                 if (p.hbar)
                     for (int k = 0; k < p.qh; ++k) p.hbar[k] = 0u;
@@ -1268,6 +1358,8 @@ __global__ void __maxnreg__(128) decode_kernel(const __grid_constant__ DecodePar
     DecodeCtrl *ctrl = p.ctrl;
     const int token = *(volatile int *)&ctrl->token;
     const int pos = *(volatile int *)&ctrl->pos;
+    const unsigned par = *(volatile unsigned *)&ctrl->epoch & 1u;
+    float *const xcur = p.xch + (size_t)par * p.L * p.xl;
     const int NB = 4 * p.L;
     // This CTA's row ranges live in shared memory for the whole step (a
     // global copy would be re-read from L2 on the critical path).
@@ -1297,43 +1389,35 @@ __global__ void __maxnreg__(128) decode_kernel(const __grid_constant__ DecodePar
     __syncthreads();  // the only all-thread barrier: roles split here
 
     if (threadIdx.x >= NT) {  // producer warp
+        reset_next(p, par);
         produce(p, lay, cg, sm, pos, s_abort);
         return;
     }
 
     Cursor cur{0, 0};
     prep_qkv<WF>(p, lay[0], cg, sm);
-    csync();
-    unsigned target = 0;
     bool ok = true;
-    // Each phase: run, arrive at the grid barrier, stage the next phase's
-    // vectors while the other CTAs arrive, then wait.  Every exit decision
-    // is taken after a CTA barrier, so all compute threads agree on it.
+    // Each phase: stage the phase's small read-only vectors, poll its inputs
+    // from the exchange, run, publish.  Every exit decision is taken right
+    // after a CTA barrier, so all compute threads agree on it.
 #pragma unroll 1
     for (int l = 0; l < p.L && ok; ++l) {
         const DecodeLayer &Ly = lay[l];
-        run_qkv<WF>(p, cg, l, token, sm, rg, cur, s_abort);
-        barrier_arrive(p, target += G);
+        run_qkv<WF>(p, cg, xcur, l, token, sm, rg, cur, s_abort);
+        if (!(ok = phase_end(p, 4 * l, s_abort))) break;
         prep_attention<WF>(p, Ly, cg, sm);
-        if (!(ok = barrier_wait(p, target, s_abort))) break;
-
-        run_attention<WF, KVBF16, SPLIT>(p, Ly, cg, l, pos, sm, rg, cur, s_abort);
-        barrier_arrive(p, target += G);
+        run_attention<WF, KVBF16, SPLIT>(p, Ly, cg, xcur, l, pos, sm, rg, cur, s_abort);
+        if (!(ok = phase_end(p, 4 * l + 1, s_abort))) break;
         prep_gate_up<WF>(p, Ly, cg, sm);
-        if (!(ok = barrier_wait(p, target, s_abort))) break;
-
-        run_gate_up<WF>(p, cg, l, token, sm, rg, cur, s_abort);
-        barrier_arrive(p, target += G);
+        run_gate_up<WF>(p, cg, xcur, l, sm, rg, cur, s_abort);
+        if (!(ok = phase_end(p, 4 * l + 2, s_abort))) break;
         prep_down<WF>(p, Ly, cg, sm);
-        if (!(ok = barrier_wait(p, target, s_abort))) break;
-
-        run_down<WF>(p, cg, sm, rg, cur, s_abort);
-        barrier_arrive(p, target += G);
+        run_down<WF>(p, cg, xcur, l, sm, rg, cur, s_abort);
+        if (!(ok = phase_end(p, 4 * l + 3, s_abort))) break;
         if (l + 1 < p.L) prep_qkv<WF>(p, lay[l + 1], cg, sm);
         else stage_ro<2>(sm + p.sm_gain, p.final_norm, p.h);
-        if (!(ok = barrier_wait(p, target, s_abort))) break;
     }
-    if (ok) run_lm_head<TF>(p, cg, pos, sm, rg, cur, s_abort);
+    if (ok) run_lm_head<TF>(p, cg, xcur, pos, sm, rg, cur, s_abort);
 }
 
 size_t decode_smem_bytes(const DecodeParams &p) { return (size_t)p.sm_total * sizeof(float); }

@@ -6,6 +6,11 @@
 
 namespace qb {
 
+// Word of an exchange slot that has not received its value (a NaN that no
+// producer stores: a computed value with this bit pattern is stored as
+// 0x7fffffff and reported as non-finite).
+constexpr uint32_t kNotReady = 0xffffffffu;
+
 // Storage of the seven per-layer linears (DecodeParams::wfmt).
 enum { WF_F32 = 0, WF_BF16 = 1, WF_I8 = 2 };
 
@@ -39,7 +44,7 @@ struct DecodeCtrl {
     int pad0;
     int next_token;    // out: greedy argmax of this step
     unsigned error;    // out: ERR_* bits, sticky until the host clears them
-    unsigned bar;      // grid barrier arrivals (reset by the last CTA)
+    unsigned epoch;    // steps completed; its parity selects the exchange buffers
     unsigned ticket;   // end-of-step ticket (reset by the last CTA)
 };
 
@@ -84,18 +89,25 @@ struct DecodeParams {
     const float *final_norm;
     const DecodeLayer *layers;  // device array [L]
     const float2 *rope;       // [cap][hd/2] (cos, sin)
-    float *qkv;               // [rqkv]
-    float *part;              // [qh][h] per-head o_proj partial sums
-    float *act;               // [ff]
-    float *hidden;            // [h] residual stream
+    // Exchange vectors between the CTAs: [2 parities][L][xl] floats; per
+    // layer the QKV outputs at x_qkv ([rqkv]), the per-head o_proj partial
+    // sums at x_part ([qh][h]), the SwiGLU activations at x_act ([ff]) and
+    // the layer's output at x_hid ([h]), each 16-byte aligned.  A step uses
+    // the parity of ctrl->epoch: every slot of it starts as kNotReady and
+    // receives exactly one value, while the step resets the other parity to
+    // kNotReady for the next step.  Consumers poll their inputs until no
+    // word is kNotReady (no grid barrier).
+    float *xch;
+    int xl, x_qkv, x_part, x_act, x_hid;
     float *logits;            // [V]
     float *amax_v;            // [grid] per-CTA argmax value
     int *amax_i;              // [grid] per-CTA argmax index
     int *emitted;             // [cap] greedy id emitted after each position (nullable)
     DecodeCtrl *ctrl;
-    // Optional phase trace (globaltimer ns): [4L barriers][grid] arrival
-    // times, then [4L] barrier release times seen by CTA 0, then the kernel
-    // start (CTA 0) and the end of the final reduction.  Null = off.
+    // Optional phase trace (globaltimer ns): [4L phases][grid] times at which
+    // each CTA finished the phase, then [4L] times at which CTA 0 held the
+    // inputs of the next phase, then the kernel start (CTA 0) and the end of
+    // the final reduction.  Null = off.
     unsigned long long *trace;
     unsigned long long timeout_ns;
     int prefetch;             // L2 prefetch of upcoming weights by the producer warp

@@ -278,7 +278,7 @@ struct Session {
     int kv_bf16 = 0;
     size_t logical_bytes = 0, workspace_bytes = 0;
     cudaStream_t stream = nullptr;
-    DevBuf kv, rope, qkv, part, act, hidden, logits, amax_v, amax_i, emitted, ctrl, dlayers, geom, apart, hbar;
+    DevBuf kv, rope, xch, logits, amax_v, amax_i, emitted, ctrl, dlayers, geom, apart, hbar;
     DecodeCtrl *hctrl = nullptr;  // pinned mirror
     std::vector<DecodeLayer> hlayers;  // host copy of the layer table (chunked prompt path)
     DevBuf pf;                         // chunked prompt workspace (allocated on first use)
@@ -428,9 +428,16 @@ static uint32_t session_build(Session &s) {
     int dev_sms = 0;
     QB_CUDA(cudaDeviceGetAttribute(&dev_sms, cudaDevAttrMultiProcessorCount, s.device));
     s.grid = dev_sms;
-    if ((st = s.qkv.alloc(rqkv * 4)) || (st = s.part.alloc(c.query_heads * c.hidden_dim * 4)) ||
-        (st = s.act.alloc(c.ff_dim * 4)) || (st = s.hidden.alloc(c.hidden_dim * 4)) ||
-        (st = s.logits.alloc(c.vocab_size * 4)) || (st = s.amax_v.alloc(s.grid * 4)) ||
+    // Exchange vectors: per layer qkv, per-head o_proj partials, SwiGLU
+    // activations and the layer output, each 16-byte aligned, in two
+    // parities, every word starting as kNotReady (all bits set).
+    auto al4 = [](size_t v) { return (v + 3) & ~(size_t)3; };
+    const size_t x_part = al4(rqkv), x_act = x_part + al4(c.query_heads * c.hidden_dim);
+    const size_t x_hid = x_act + al4(c.ff_dim), xl = x_hid + al4(c.hidden_dim);
+    if (2 * L * xl >= (1ull << 31)) return QB_UNSUPPORTED;
+    if ((st = s.xch.alloc(2 * L * xl * 4, false))) return st;
+    QB_CUDA(cudaMemset(s.xch.p, 0xff, s.xch.bytes));
+    if ((st = s.logits.alloc(c.vocab_size * 4)) || (st = s.amax_v.alloc(s.grid * 4)) ||
         (st = s.amax_i.alloc(s.grid * 4)) || (st = s.emitted.alloc(cap * 4)) ||
         (st = s.ctrl.alloc(sizeof(DecodeCtrl))))
         return st;
@@ -466,8 +473,9 @@ static uint32_t session_build(Session &s) {
     p.final_norm = m.final_norm.as<float>();
     p.layers = s.dlayers.as<DecodeLayer>();
     p.rope = s.rope.as<float2>();
-    p.qkv = s.qkv.as<float>(); p.part = s.part.as<float>(); p.act = s.act.as<float>();
-    p.hidden = s.hidden.as<float>(); p.logits = s.logits.as<float>();
+    p.xch = s.xch.as<float>();
+    p.xl = (int)xl; p.x_qkv = 0; p.x_part = (int)x_part; p.x_act = (int)x_act; p.x_hid = (int)x_hid;
+    p.logits = s.logits.as<float>();
     p.amax_v = s.amax_v.as<float>(); p.amax_i = s.amax_i.as<int>(); p.emitted = s.emitted.as<int>();
     p.ctrl = s.ctrl.as<DecodeCtrl>();
     p.timeout_ns = 2000000000ull;
@@ -627,13 +635,15 @@ static uint32_t session_launch(Session &s, uint32_t token, bool want_logits) {
 }
 
 // Execution error: invalidate (src/kv_cache.rs:335-345) and clear the
-// device control block so the next step starts from a clean barrier.
+// device control block and the exchange so the next step starts clean.
 static uint32_t session_fail(Session &s, uint32_t status) {
     s.valid = false;
     s.processed = 0;
     s.logits_valid = false;
     cudaMemsetAsync(s.ctrl.p, 0, sizeof(DecodeCtrl), s.stream);
     if (s.hbar.p) cudaMemsetAsync(s.hbar.p, 0, s.hbar.bytes, s.stream);
+    // Epoch 0 again: both parities of the exchange start not ready.
+    if (s.xch.p) cudaMemsetAsync(s.xch.p, 0xff, s.xch.bytes, s.stream);
     cudaStreamSynchronize(s.stream);
     memset(s.hctrl, 0, sizeof(DecodeCtrl));
     return status;

@@ -81,7 +81,7 @@ def decode(prompt: int, steps: int, profile: bool) -> None:
           f"LM head {np.mean([t[1] for t in tot]) / 1e3:.1f} us")
     for k, v in acc.items():
         print(f"  {k:9s} per layer: phase {v[0] / n / 1e3:.2f} us, mean CTA work {v[1] / n / 1e3:.2f} us, "
-              f"barrier after the last arrival {v[2] / n / 1e3:.2f} us")
+              f"hand-over after the last finish {v[2] / n / 1e3:.2f} us")
 
 
 def long(prompt: int, steps: int) -> None:
