@@ -1315,21 +1315,35 @@ __device__ __forceinline__ void run_lm_head(const DecodeParams &p, const CtaGeom
             const int oi = __shfl_xor_sync(FULL, bi, off);
             if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
         }
+        unsigned tk = 0;
         if (lane == 0) {
             p.amax_v[b] = bv;
             p.amax_i[b] = bi == 0x7fffffff ? bi : cg.lm_v0 + bi;
             __threadfence();
-            const unsigned tk = atomicAdd(&ctrl->ticket, 1u);
-            if (tk == (unsigned)G - 1) {
-                __threadfence();
-                float gv = __ldcg(p.amax_v);
-                int gi = __ldcg(p.amax_i);
-#pragma unroll 1
-                for (int k = 1; k < G; ++k) {
-                    const float v = __ldcg(p.amax_v + k);
-                    const int i = __ldcg(p.amax_i + k);
-                    if (v > gv || (v == gv && i < gi)) { gv = v; gi = i; }
-                }
+            tk = atomicAdd(&ctrl->ticket, 1u);
+        }
+        tk = __shfl_sync(FULL, tk, 0);
+        if (tk == (unsigned)G - 1) {
+            // The last CTA: its warp 0 reduces the per-CTA partials, every
+            // lane's loads in flight at once, then a butterfly (the maximum,
+            // the lowest id among equal values).
+            __syncwarp();
+            __threadfence();
+            float gv = -INFINITY;
+            int gi = 0x7fffffff;
+#pragma unroll 4
+            for (int k = lane; k < G; k += 32) {
+                const float v = __ldcg(p.amax_v + k);
+                const int i = __ldcg(p.amax_i + k);
+                if (v > gv || (v == gv && i < gi)) { gv = v; gi = i; }
+            }
+#pragma unroll
+            for (int off = 16; off; off >>= 1) {
+                const float ov = __shfl_xor_sync(FULL, gv, off);
+                const int oi = __shfl_xor_sync(FULL, gi, off);
+                if (ov > gv || (ov == gv && oi < gi)) { gv = ov; gi = oi; }
+            }
+            if (lane == 0) {
                 if (gi < 0 || gi >= p.V) gi = 0;
                 ctrl->next_token = gi;
                 if (p.emitted) p.emitted[pos] = gi;
