@@ -1110,21 +1110,38 @@ __device__ __forceinline__ bool split_exchange(const DecodeParams &p, int hh, in
     }
     if (!head_barrier(p, hh, (unsigned)((l + 1) * nsp), s_abort)) return false;
     const float *all = p.apart + (size_t)hh * nsp * (hd + 2);
-    float M = -INFINITY;
-    for (int j = 0; j < nsp; ++j) M = rust_max(M, __ldcg(all + (size_t)j * (hd + 2) + hd));
+    // Lane j of every warp loads split j's (maximum, sum) (nsp <=
+    // kMaxSplits <= 32); the rescale factors exp(m_j - M) and the combined
+    // sum follow in split order.
+    const int lane = t & 31;
+    float mj = -INFINITY, lj = 0.0f;
+    if (lane < nsp) {
+        mj = __ldcg(all + (size_t)lane * (hd + 2) + hd);
+        lj = __ldcg(all + (size_t)lane * (hd + 2) + hd + 1);
+    }
+    const float M = warp_max(mj);
+    const float f = lane < nsp && lj > 0.0f ? expf(mj - M) : 0.0f;
+    float fj[kMaxSplits];
+    float Lsum = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kMaxSplits; ++j) {
+        fj[j] = __shfl_sync(FULL, f, j);
+        const float l = __shfl_sync(FULL, lj, j);
+        if (j < nsp) Lsum += l * fj[j];
+    }
     const int ctx_pad = p.chd * EPC;
 #pragma unroll 1
     for (int i = t; i < ctx_pad; i += NT) {
         float s = 0.0f;
         if (i < hd) {
-            float Lsum = 0.0f, o = 0.0f;
-            for (int j = 0; j < nsp; ++j) {
-                const float *pj = all + (size_t)j * (hd + 2);
-                const float lj = __ldcg(pj + hd + 1);
-                const float f = lj > 0.0f ? expf(__ldcg(pj + hd) - M) : 0.0f;
-                Lsum += lj * f;
-                o += __ldcg(pj + i) * f;
-            }
+            float oj[kMaxSplits];
+#pragma unroll
+            for (int j = 0; j < kMaxSplits; ++j)
+                if (j < nsp) oj[j] = __ldcg(all + (size_t)j * (hd + 2) + i);
+            float o = 0.0f;
+#pragma unroll
+            for (int j = 0; j < kMaxSplits; ++j)
+                if (j < nsp) o += oj[j] * fj[j];
             s = o / Lsum;
             flag_nonfinite(p.ctrl, s);
         }

@@ -65,6 +65,8 @@ struct KindGeom {
 // The rows each CTA owns in every phase (host-computed, no division on the
 // device).  Attention items are (query head, o_proj row range) pairs.
 constexpr int kMaxAttItems = 4;
+// At most this many CTAs per query head (and position splits of a head).
+constexpr int kMaxSplits = 8;
 struct CtaGeom {
     int qkv_r0, qkv_n;  // rows of [Wq;Wk;Wv]
     int gu_f0, gu_n;    // rows of gate and of up

@@ -467,7 +467,7 @@ static uint32_t session_build(Session &s) {
     p.sh = m.sh; p.shd = m.shd; p.sff = m.sff; p.semb = m.semb;
     p.ch = (int)(m.sh / 16); p.chd = (int)(m.shd / 16); p.cff = (int)(m.sff / 16); p.cemb = (int)(m.semb / 16);
     p.rqkv = (int)rqkv;
-    const int s_o = std::max(1, std::min(8, s.grid / std::max(1, p.qh)));  // CTAs per query head
+    const int s_o = std::max(1, std::min(kMaxSplits, s.grid / std::max(1, p.qh)));  // CTAs per query head
     p.emb = m.emb.as<uint8_t>();
     p.head = m.head_set ? m.head.as<uint8_t>() : m.emb.as<uint8_t>();
     p.final_norm = m.final_norm.as<float>();
