@@ -291,6 +291,12 @@ uint32_t qb_session_append(uint64_t session, const uint32_t *tokens, size_t coun
 uint32_t qb_session_step_profiled(uint64_t session, uint32_t token, float *logits,
                                   size_t logits_len, uint32_t *argmax, uint64_t *stamps,
                                   size_t stamps_len, size_t *needed);
+/* Fault-path test hook with no counterpart in the reference: one decode
+ * step in which CTA 0 withholds its first-layer QKV outputs, so the polls
+ * that wait for them run out after `timeout_ns` (1 ns .. 2 s).  Expected
+ * result: QB_DEVICE_TIMEOUT, the session invalidated (as after any
+ * execution error) until qb_session_reset; the device stays usable. */
+uint32_t qb_session_step_withheld(uint64_t session, uint32_t token, uint64_t timeout_ns);
 /* reset, src/kv_cache.rs:225-229. */
 uint32_t qb_session_reset(uint64_t session);
 uint32_t qb_session_info_get(uint64_t session, qb_session_info *out);

@@ -42,6 +42,7 @@ SIGNATURES = {
     "qb_session_step": ([U64, U32, P, S, P], U32),
     "qb_session_append": ([U64, P, S, P, S, P, I32], U32),
     "qb_session_step_profiled": ([U64, U32, P, S, P, P, S, P], U32),
+    "qb_session_step_withheld": ([U64, U32, U64], U32),
     "qb_session_reset": ([U64], U32),
     "qb_session_info_get": ([U64, P], U32),
     "qb_session_decode_greedy": ([U64, U32, S, P], U32),

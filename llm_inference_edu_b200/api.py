@@ -355,6 +355,14 @@ class CachedSession:
     def reset(self):
         _check(lib().qb_session_reset(self.handle), CacheError)
 
+    def step_withheld(self, token: int, timeout_ns: int) -> None:
+        """Fault-path test hook (no counterpart in the reference): one step in
+        which the first CTA withholds its first-layer QKV outputs, so the
+        polls waiting for them run out after `timeout_ns`.  Raises
+        CacheError("DeviceTimeout") and leaves the session invalid until
+        reset()."""
+        _check(lib().qb_session_step_withheld(self.handle, token, timeout_ns), CacheError)
+
     def step_into(self, token: int, logits: Optional[np.ndarray]) -> int:
         """Evaluates one token; fills `logits` (float32, vocab width) if given
         and returns the greedy id."""

@@ -1074,12 +1074,13 @@ __device__ __forceinline__ void run_qkv(const DecodeParams &p, const CtaGeom &cg
     block_rmsnorm<EPC>(h2, gain, xs, p.h, p.ch, p.eps, sm + p.sm_red);
     const int R = cg.qkv_n;
     float *out = xv(p, xcur, l, p.x_qkv) + cg.qkv_r0;
+    const bool pub = !(p.withhold && l == 0 && blockIdx.x == 0);
     DecodeCtrl *ctrl = p.ctrl;
     team_gemv<WF, 1>(p, rg, cur, p.kind[K_QKV], R, xs, s_abort, [&](int r, float a, float) {
         float v = a;
         if (WF == WF_I8) v = v * rv[r];
         v = v + rv[R + r];
-        publish(out + r, v);
+        if (pub) publish(out + r, v);
         flag_nonfinite(ctrl, v);
     });
 }

@@ -113,6 +113,10 @@ struct DecodeParams {
     unsigned long long *trace;
     unsigned long long timeout_ns;
     int prefetch;             // L2 prefetch of upcoming weights by the producer warp
+    // Fault-path test hook: nonzero = CTA 0 does not publish its layer-0 QKV
+    // outputs, so the polls that read them run out (ERR_TIMEOUT).  0 in
+    // every normal step.
+    int withhold;
     // Long-context attention: with att_splits > 1 and at least att_split_min
     // cached positions, the att_splits CTAs of a query head each take one
     // position range, exchange (max, sum, context) partials through apart

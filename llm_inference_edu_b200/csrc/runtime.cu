@@ -480,6 +480,7 @@ static uint32_t session_build(Session &s) {
     p.ctrl = s.ctrl.as<DecodeCtrl>();
     p.timeout_ns = 2000000000ull;
     p.prefetch = 1;
+    p.withhold = 0;
     // Rows each CTA owns in every phase (floor(n * b / G) splits), and its
     // attention items: (query head, o_proj row range) pairs wi = b + m * G.
     std::vector<CtaGeom> geo(s.grid);
@@ -1203,6 +1204,30 @@ uint32_t qb_session_step_profiled(uint64_t session, uint32_t token, float *logit
     s.logits_valid = true;
     QB_CUDA(cudaMemcpy(stamps, tr.p, need * 8, cudaMemcpyDeviceToHost));
     return QB_OK;
+}
+
+uint32_t qb_session_step_withheld(uint64_t session, uint32_t token, uint64_t timeout_ns) {
+    clear_detail();
+    auto sp = find_session(session);
+    if (!sp) return QB_INVALID_HANDLE;
+    Session &s = *sp;
+    if (!s.valid) return QB_INVALID_STATE;
+    if (token >= s.m->c.vocab_size) return QB_INVALID_TOKEN;
+    if (s.processed == s.capacity) return QB_FULL;
+    if (timeout_ns == 0 || timeout_ns > 2000000000ull) return QB_INVALID_LENGTH;
+    DeviceGuard dg(s.device);
+    DecodeParams p = s.params;
+    p.withhold = 1;
+    p.timeout_ns = timeout_ns;
+    s.hctrl->token = (int)token;
+    s.hctrl->pos = (int)s.processed;
+    s.hctrl->write_logits = 0;
+    cudaError_t e = cudaMemcpyAsync(s.ctrl.p, s.hctrl, 16, cudaMemcpyHostToDevice, s.stream);
+    if (e == cudaSuccess) e = decode_launch(p, s.grid, s.stream, split_at(s, s.processed));
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync((char *)s.hctrl + 16, (char *)s.ctrl.p + 16, 8, cudaMemcpyDeviceToHost, s.stream);
+    if (e != cudaSuccess) return session_fail(s, cuda_status(e));
+    return session_finish(s, nullptr, nullptr);
 }
 
 uint32_t qb_session_reset(uint64_t session) {

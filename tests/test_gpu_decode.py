@@ -146,6 +146,38 @@ def test_nonfinite_invalidates_until_reset():
     assert s.is_valid() and s.processed() == 1
 
 
+def test_withheld_exchange_times_out_and_recovers():
+    # Fault path of the decode kernel, made on purpose without a GPU fault:
+    # the first CTA withholds its first-layer QKV outputs, so the bounded
+    # polls that wait for them run out (20 ms).  The step reports
+    # DeviceTimeout and invalidates the session; after reset the same prompt
+    # decodes exactly as before (the exchange buffers were re-marked), and a
+    # second session on the device is unaffected.
+    import llm_inference_edu_b200 as qb
+    from helpers import qwen_host_weights
+    cap = 48
+    cfg = presets.qwen_0_5b(cap)
+    m = qb.Decoder(cfg, qwen_host_weights("0.5b", 1, "bf16"), linear_format="int8", table_format="bf16")
+    prompt = synthetic.prompt(cfg.vocab_size, 16, seed=5)
+    s = qb.CachedSession(m, cap, kv_dtype="bf16", budget=0)
+    first = int(np.argmax(s.prefill(prompt)))
+    ref = [first] + s.decode_greedy(first, 8)
+    s.reset()
+    assert int(np.argmax(s.prefill(prompt))) == first
+    with pytest.raises(qb.CacheError) as e:
+        s.step_withheld(first, 20_000_000)
+    assert e.value.kind == "DeviceTimeout" and not s.is_valid()
+    with pytest.raises(qb.CacheError) as e:
+        s.step(first)
+    assert e.value.kind == "InvalidState"
+    s.reset()
+    again = int(np.argmax(s.prefill(prompt)))
+    assert [again] + s.decode_greedy(again, 8) == ref
+    other = qb.CachedSession(m, cap, kv_dtype="bf16", budget=0)
+    f2 = int(np.argmax(other.prefill(prompt)))
+    assert [f2] + other.decode_greedy(f2, 8) == ref
+
+
 def test_generation_failure_and_replay():
     # tests/generation_state.rs:102-171
     import llm_inference_edu_b200 as qb
