@@ -127,7 +127,10 @@ __global__ void rmsnorm_rows(const float *x, const float *g, float *y, Planes P,
 
 // The same RMSNorm with one warp per row (rows of w <= 1024 elements, w a
 // multiple of 4): the row stays in registers and both reductions are warp
-// shuffles, with no CTA barrier.  Eight rows per 256-thread CTA.
+// shuffles, with no CTA barrier.  Eight rows per 256-thread CTA.  The two
+// divisions per element become multiplications by the reciprocals of the
+// row maximum and of the denominator (as in the decode kernel's RMSNorm:
+// within a few ulps of the divisions).
 __global__ void rmsnorm_rows_warp(const float *x, const float *g, float *y, Planes P, int n, int w, float eps,
                                   unsigned *err) {
     pdl_trigger();
@@ -149,11 +152,12 @@ __global__ void rmsnorm_rows_warp(const float *x, const float *g, float *y, Plan
             m = rust_max(rust_max(rust_max(rust_max(m, fabsf(v[k].x)), fabsf(v[k].y)), fabsf(v[k].z)), fabsf(v[k].w));
     }
     for (int off = 16; off; off >>= 1) m = rust_max(m, __shfl_xor_sync(0xffffffffu, m, off));
+    const float r = 1.0f / m;
     float ss = 0.0f;
 #pragma unroll
     for (int k = 0; k < V4; ++k) {
         if (lane + 32 * k < w4) {
-            const float a = v[k].x / m, b = v[k].y / m, c = v[k].z / m, d = v[k].w / m;
+            const float a = v[k].x * r, b = v[k].y * r, c = v[k].z * r, d = v[k].w * r;
             ss = ss + a * a;
             ss = ss + b * b;
             ss = ss + c * c;
@@ -161,8 +165,8 @@ __global__ void rmsnorm_rows_warp(const float *x, const float *g, float *y, Plan
         }
     }
     for (int off = 16; off; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-    const float seps = se / m;
-    const float den = sqrtf(ss / (float)w + seps * seps);
+    const float seps = se * r;
+    const float rd = 1.0f / sqrtf(ss / (float)w + seps * seps);
     float4 *yr = reinterpret_cast<float4 *>(y + (size_t)t * w);
     const float4 *g4 = reinterpret_cast<const float4 *>(g);
 #pragma unroll
@@ -171,10 +175,10 @@ __global__ void rmsnorm_rows_warp(const float *x, const float *g, float *y, Plan
         if (i < w4) {
             const float4 gg = g4[i];
             float4 o;
-            o.x = (v[k].x / m) / den * gg.x;
-            o.y = (v[k].y / m) / den * gg.y;
-            o.z = (v[k].z / m) / den * gg.z;
-            o.w = (v[k].w / m) / den * gg.w;
+            o.x = v[k].x * r * rd * gg.x;
+            o.y = v[k].y * r * rd * gg.y;
+            o.z = v[k].z * r * rd * gg.z;
+            o.w = v[k].w * r * rd * gg.w;
             yr[i] = o;
             if (P.p) {
                 const size_t at = (size_t)t * w + 4 * (size_t)i;
