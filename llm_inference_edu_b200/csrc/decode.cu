@@ -796,8 +796,8 @@ __device__ __forceinline__ float kv_load(const uint8_t *base, size_t idx) {
 // index, then divided by sqrt(hd)); softmax subtracts the maximum and
 // divides by the sum.
 // Per-head barrier of the attention splits: every split has written its
-// partial before any reads them (release/acquire like the grid barrier;
-// bounded by the timeout).  Returns false when aborting.
+// partial before any reads them (a release reduction on a per-head counter,
+// acquire polling bounded by the timeout).  Returns false when aborting.
 __device__ __forceinline__ bool head_barrier(const DecodeParams &p, int hh, unsigned target, volatile int *s_abort) {
     csync();
     if (threadIdx.x == 0) {
@@ -1043,9 +1043,9 @@ __device__ __forceinline__ void attention_context(const DecodeParams &p, const D
 // ------------------------------------------------------------ phases ----
 //
 // Each phase has a `prep` that stages its small read-only vectors -- `gain`
-// (norm gains) and `rv` (row scales and biases) -- into shared memory while
-// the grid barrier before it completes, and a `run` after the barrier.  The
-// weights arrive through the ring.
+// (norm gains) and `rv` (row scales and biases) -- into shared memory, and a
+// `run` that polls the phase's inputs from the exchange, computes and
+// publishes.  The weights arrive through the ring.
 
 template <int WF>
 __device__ __forceinline__ void prep_qkv(const DecodeParams &p, const DecodeLayer &Ly, const CtaGeom &cg,
