@@ -47,6 +47,7 @@ namespace qb {
 constexpr int NT = kDecodeThreads;  // compute threads
 constexpr int NW = NT / 32;         // compute warps
 constexpr int LOOKAHEAD = 3;        // L2 prefetch distance in phases
+constexpr int LM_PREFETCH = 8;      // LM-head rows: L2 prefetch distance in ring chunks
 constexpr unsigned FULL = 0xffffffffu;
 
 template <int WF> struct Fmt;
@@ -302,9 +303,17 @@ struct Producer {
     }
 
     // Streams rows [0, n) of a block (stride bytes each) in ring chunks.
-    __device__ void block(const uint8_t *base, int n, const KindGeom &g) {
+    // With pf > 0 the chunk pf chunks ahead is prefetched into L2 as each
+    // chunk is issued (the LM head, a stream much longer than the ring), so
+    // more DRAM reads are in flight than the ring's slots hold.
+    __device__ void block(const uint8_t *base, int n, const KindGeom &g, int pf = 0) {
 #pragma unroll 1
         for (int r = 0; r < n && alive; r += g.rpc) {
+            if (pf > 0) {
+                const int rp = r + pf * g.rpc;
+                if (rp < n)
+                    prefetch_l2_bulk(base + (size_t)rp * g.stride, (uint32_t)(min(g.rpc, n - rp) * g.stride) & ~15u);
+            }
             if (round > 0 && !wait_free(slot, (uint32_t)((round - 1) & 1))) {
                 alive = false;
                 return;
@@ -348,7 +357,7 @@ __device__ void prefetch_phase(const DecodeParams &p, const DecodeLayer *lay, co
                                int pos) {
     if (!p.prefetch || k > 4 * p.L) return;
     if (k == 4 * p.L) {
-        prefetch_rows(p.head + (size_t)cg.lm_v0 * p.semb, (size_t)min(cg.lm_n, 64) * p.semb);
+        prefetch_rows(p.head + (size_t)cg.lm_v0 * p.semb, (size_t)min(cg.lm_n, LM_PREFETCH * p.kind[K_LM].rpc) * p.semb);
         return;
     }
     const DecodeLayer &Ly = lay[k >> 2];
@@ -391,7 +400,7 @@ __device__ void produce(const DecodeParams &p, const DecodeLayer *lay, const Cta
         if (leader) pr.block(Ly.wd + (size_t)cg.dn_r0 * p.sff, cg.dn_n, p.kind[K_DN]);
         pr.alive = __shfl_sync(FULL, (int)pr.alive, 0) != 0;
     }
-    if (leader && pr.alive) pr.block(p.head + (size_t)cg.lm_v0 * p.semb, cg.lm_n, p.kind[K_LM]);
+    if (leader && pr.alive) pr.block(p.head + (size_t)cg.lm_v0 * p.semb, cg.lm_n, p.kind[K_LM], LM_PREFETCH);
     if (leader && !pr.alive) pr.drain();
 }
 
