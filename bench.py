@@ -23,9 +23,11 @@ lockstep (BatchSession: one multi-token forward per step on the tensor
 cores), device-timed, with its prompt evaluation rate.  `long_context` is
 an 8,192-token prompt (chunked) then greedy decode at that depth.
 
---impl reference times the oracle -- the C restatement of the reference
-crate's CPU arithmetic (the Rust crate cannot be built here) -- on the
-host cores with OpenMP over output rows, on a bounded sample.
+--impl reference times the reference's CPU token loop on the host: the
+oracle (the C restatement of the crate's scalar FP32 arithmetic; the Rust
+crate cannot be built here), single-threaded like the crate, on the same
+prompt, warm-up and step count as the native arm.  It loads no library of
+the product (the oracle draws the same seeded weights itself).
 """
 from __future__ import annotations
 
@@ -46,7 +48,7 @@ SEED = 1
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one
 # decode_kernel launch of the INT8 workload, from an ncu capture of this
 # kernel (taken at cache position 134; every further cached position adds
-# 6,144 bytes of BF16 KV).
+# 12,288 bytes of BF16 KV: 24 layers x K and V x 2 KV heads x 64 x 2 B).
 NCU_TRAFFIC_BYTES_INT8 = 643_108_608
 
 
@@ -130,45 +132,84 @@ def algorithmic_bytes(cfg, linear_format, kv_bytes_per_pos, L):
     return cfg.layers * per_layer + table + 4 * h + L * kv_bytes_per_pos + kv_bytes_per_pos + 4 * V
 
 
+def native_config(lf, world):
+    """The `config` object of the line (shared by both arms)."""
+    kv = "bf16" if lf == "int8" else "f32"
+    return {"workload": f"qwen2.5-0.5b-shape {lf} batch-1 greedy decode (128-token prompt)",
+            "batch_per_gpu": 1, "prompt": PROMPT, "kv": kv, "parallelism": f"dp{world}",
+            "l2": "weights 631 MB > 126 MB L2; no flush"}
+
+
+def ref_decode_rate(token_times):
+    """The reference's decode throughput (src/benchmark.rs:85-91): N tokens
+    emitted at token_times[0..N); (N - 1) / (t_last - t_first)."""
+    if len(token_times) < 2 or token_times[-1] <= token_times[0]:
+        return None
+    return (len(token_times) - 1) / (token_times[-1] - token_times[0])
+
+
 def run_reference(args, rank, world):
-    """The oracle on the host cores (OpenMP over output rows)."""
-    import numpy as np
-    from llm_inference_edu_b200 import presets, synthetic
-    from oracle import oracle
+    """The reference's CPU token loop on this host's cores.
+
+    The Rust crate cannot be built in this image, so its arithmetic runs as
+    the oracle (oracle/qwen_oracle.c, the C restatement of the crate's scalar
+    FP32 path; nothing of the product is loaded: the oracle draws the same
+    seeded weights and prompt itself).  Same workload as the native arm: the
+    0.5B model (INT8 per-row linears quantized by the oracle, BF16 table and
+    KV), the same 128-token prompt, W warm-up then K timed greedy decode
+    steps.  The reference is single-threaded (src/kernels.rs:8), so the
+    decode steps run on one thread (`value`); the prompt is evaluated with
+    every host thread (not part of the metric) to keep the run short, and
+    a few steps on every host thread are reported beside the value."""
     if rank != 0:
         return 0
-    cfg = presets.qwen_0_5b(PROMPT + 64)
+    import numpy as np
+
+    from oracle import oracle
     lf = args.config
-    w = synthetic.weights(cfg, seed=SEED, dtype="bf16")
-    om = oracle.Model(cfg, oracle.int8_model_weights(cfg, w, lf))
-    prompt = synthetic.prompt(cfg.vocab_size, PROMPT, seed=SEED)
-    sess = oracle.Session(om, PROMPT + 64, kv_bf16=(lf == "int8"), budget=0)
-    # Bounded sample: 8 prompt tokens of serial prefill, then timed decode.
+    cap = PROMPT + args.warmup + args.steps + 16
+    cfg = oracle.qwen_0_5b_config(cap)
+    all_threads = oracle.threads()
+    om = oracle.Model(cfg, oracle.int8_model_weights(cfg, oracle.synthetic_weights(cfg, SEED, "bf16"), lf))
+    prompt = oracle.synthetic_prompt(cfg.vocab_size, PROMPT, SEED)
+    sess = oracle.Session(om, cap, kv_bf16=(lf == "int8"), budget=0)
     t0 = time.perf_counter()
-    s, lg = sess.prefill(prompt[:8])
+    s, lg = sess.prefill(prompt)
     t_prefill = time.perf_counter() - t0
+    if s:
+        raise RuntimeError(f"oracle prefill failed: {s}")
     tok = int(np.argmax(lg))
-    for _ in range(min(args.warmup, 1)):
-        s, lg = sess.step(tok)
+    oracle.set_threads(1)
+    for _ in range(args.warmup):
+        sess.step(tok, lg)
         tok = int(np.argmax(lg))
-    n = max(1, min(args.steps, args.cpu_steps))
+    times = [time.perf_counter()]
+    for _ in range(args.steps):
+        sess.step(tok, lg)
+        tok = int(np.argmax(lg))
+        times.append(time.perf_counter())
+    dt = times[-1] - times[0]
+    value = args.steps / dt
+    steps_all = min(args.steps, 8)
+    oracle.set_threads(all_threads)
     t0 = time.perf_counter()
-    for _ in range(n):
-        s, lg = sess.step(tok)
+    for _ in range(steps_all):
+        sess.step(tok, lg)
         tok = int(np.argmax(lg))
-    dt = time.perf_counter() - t0
-    value = n / dt
-    cores = oracle.threads()
+    rate_all = steps_all / (time.perf_counter() - t0)
+    sample = (f"{args.steps} timed greedy decode steps on 1 thread after the 128-token prompt and "
+              f"{args.warmup} warm-up steps (oracle: C restatement of the crate's FP32 path)")
     line = {
         "impl": "reference", "metric": "decode_tok_per_s", "value": value, "unit": "tok/s",
-        "n_gpus": world, "steps": n, "warmup": args.warmup, "ms_per_step": 1000 * dt / n,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
-        "data": "synthetic: N(0,0.02) weights seed 1, uniform prompt seed 1",
-        "config": {"workload": f"qwen2.5-0.5b-shape {lf} batch-1 greedy decode", "batch": 1,
-                   "prompt": PROMPT, "cpu_sample": f"8-token prefill + {n} decode steps"},
-        "prefill_tok_per_s": 8 / t_prefill,
-        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "port",
-                         "sample": f"{n} decode steps after an 8-token prefill (oracle, C restatement)"},
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * dt / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp32-accumulate/int8-weights" if lf == "int8" else "fp32-accumulate/bf16-weights",
+        "data": "synthetic: N(0,0.02) weights seed 1, uniform prompts seed 1+rank",
+        "config": native_config(lf, world),
+        "decode_tok_per_s_reference_definition": ref_decode_rate(times),
+        "prefill_tok_per_s": PROMPT / t_prefill, "prefill_threads": all_threads,
+        "value_all_threads": rate_all, "all_threads": all_threads,
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": 1, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -231,12 +272,15 @@ def run_native(args, topo):
     torch.cuda.synchronize()
     lat = []
     t0 = time.perf_counter()
+    times = [t0]
     for _ in range(args.steps):
         a = time.perf_counter()
         gen.next_token()
-        lat.append(time.perf_counter() - a)
+        times.append(time.perf_counter())
+        lat.append(times[-1] - a)
     torch.cuda.synchronize()
     e2e_s = dp.max_over_ranks(topo, time.perf_counter() - t0, device="cuda")
+    ref_rate = ref_decode_rate(times)
 
     batched = run_batched(args, topo, model, cfg, kv)
     del model
@@ -257,11 +301,10 @@ def run_native(args, topo):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "fp32-accumulate/int8-weights" if lf == "int8" else "fp32-accumulate/bf16-weights",
         "data": "synthetic: N(0,0.02) weights seed 1, uniform prompts seed 1+rank",
-        "config": {"workload": f"qwen2.5-0.5b-shape {lf} batch-1 greedy decode (128-token prompt)",
-                   "batch_per_gpu": 1, "prompt": PROMPT, "kv": kv, "parallelism": f"dp{world}",
-                   "l2": "weights 631 MB > 126 MB L2; no flush"},
+        "config": native_config(lf, world),
         "prefill_tok_per_s": PROMPT / (prefill_ms / 1000.0),
         "ms_per_token_p50": 1000.0 * statistics.median(lat),
+        "decode_tok_per_s_reference_definition": ref_rate,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak,
                      "traffic": NCU_TRAFFIC_BYTES_INT8 if lf == "int8" else None,

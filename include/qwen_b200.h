@@ -99,19 +99,23 @@ int qb_last_cuda_error(void);
 /* Linear kernels (DEVICE buffers; lengths are element counts)         */
 /* ------------------------------------------------------------------ */
 
-/* Y[t,o] = sum_i X[t,i] * W[o,i], all row-major FP32, FP32 accumulation.
- * Replaces `linear`, src/lib.rs:51-73 (admission src/lib.rs:76-111: zero
- * dimension, product overflow, then exact lengths of x, w, y). */
+/* Y[t,o] = sum_i X[t,i] * W[o,i], all row-major FP32, FP32 accumulation in
+ * increasing i (bit-identical to the crate).  Replaces `linear`,
+ * src/lib.rs:51-73 (admission src/lib.rs:76-111: zero dimension, product
+ * overflow, then exact lengths of x, w, y). */
 uint32_t qb_linear_f32(const float *x, size_t x_len, const float *w, size_t w_len, float *y,
                        size_t y_len, size_t tokens, size_t input_dim, size_t output_dim,
                        void *stream);
-/* Same contract as qb_linear_f32.  Replaces `linear_lanes4`,
- * src/kernels.rs:10-28 (the tied LM-head kernel). */
+/* Same contract as qb_linear_f32, in the four-lane order of dot_lanes4
+ * (lanes i % 4, ((s0 + s1) + s2) + s3, then the tail; bit-identical to the
+ * crate).  Replaces `linear_lanes4`, src/kernels.rs:10-46 (the tied LM-head
+ * kernel). */
 uint32_t qb_linear_lanes4_f32(const float *x, size_t x_len, const float *w, size_t w_len,
                               float *y, size_t y_len, size_t tokens, size_t input_dim,
                               size_t output_dim, void *stream);
 /* BF16 weights (uint16 bit patterns, value = bits << 16 as in
- * src/weights.rs:250-251), FP32 activations and accumulation. */
+ * src/weights.rs:250-251), FP32 activations and accumulation in `linear`'s
+ * order. */
 uint32_t qb_linear_bf16(const float *x, size_t x_len, const uint16_t *w, size_t w_len, float *y,
                         size_t y_len, size_t tokens, size_t input_dim, size_t output_dim,
                         void *stream);
@@ -134,11 +138,20 @@ uint32_t qb_quantize_int8(const float *w, size_t w_len, size_t output_dim, size_
 uint32_t qb_dequantize_int8(const int8_t *values, const float *scales, size_t output_dim,
                             size_t input_dim, size_t group_size, float *y, size_t y_len,
                             void *stream);
-/* Fused dequantizing linear: y[t,o] = sum_i x[t,i] * (f32(q[o,i]) * s[o,g(i)]).
- * Replaces linear_int8 / linear_int8_lanes4, src/quantization.rs:168-281. */
+/* Fused dequantizing linear: y[t,o] = sum_i x[t,i] * (f32(q[o,i]) * s[o,g(i)]),
+ * summed in increasing i (bit-identical to the crate).  Replaces
+ * linear_int8, src/quantization.rs:168-215. */
 uint32_t qb_linear_int8(const float *x, size_t x_len, const int8_t *values, const float *scales,
                         size_t output_dim, size_t input_dim, size_t group_size, float *y,
                         size_t y_len, size_t tokens, void *stream);
+/* The same product in the four-lane order (lanes i % 4 over the first
+ * input_dim - input_dim % 4 elements, ((s0 + s1) + s2) + s3, then the tail
+ * in order; bit-identical to the crate).  Replaces linear_int8_lanes4,
+ * src/quantization.rs:218-281. */
+uint32_t qb_linear_int8_lanes4(const float *x, size_t x_len, const int8_t *values,
+                               const float *scales, size_t output_dim, size_t input_dim,
+                               size_t group_size, float *y, size_t y_len, size_t tokens,
+                               void *stream);
 
 /* ------------------------------------------------------------------ */
 /* Elementwise ops (DEVICE buffers; ids are HOST)                      */
@@ -180,9 +193,10 @@ uint32_t qb_rope(const float *x, size_t x_len, float *y, size_t y_len, size_t to
  *  - Limit: tokens * head_dim <= QB_ROPE_STATIC_MAX_TABLE.  A larger call
  *    returns QB_RESOURCE_BUDGET before any device work, with qb_last_detail
  *    expected = the limit and actual = tokens * head_dim.
+ *  - Like qb_rope, the call synchronizes `stream` before it returns.
  *  - The first call on each device looks up the array's address with
- *    cudaGetSymbolAddress; make that first call before any stream capture
- *    starts on that device.
+ *    cudaGetSymbolAddress (not a stream operation); make that first call
+ *    before any stream capture begins on that device.
  *  - Each call resets the flag word itself; the angle table needs no
  *    starting value (each call writes all of it before the kernel reads it).
  *  - All calls on one device share the one array, so calls that overlap in
@@ -283,9 +297,10 @@ uint32_t qb_session_append(uint64_t session, const uint32_t *tokens, size_t coun
                            size_t logits_len, uint32_t *argmax, int32_t require_empty);
 /* step_profiled, src/kv_cache.rs:309-316: one step as qb_session_step that
  * also records device timestamps (ns, %globaltimer) into `stamps`:
- * [B][grid] times at which each CTA finished each phase, then [B] times at
- * which CTA 0 held the inputs of the phase after it, then the step's start
- * and end, where B = 4 * layers (QKV, attention, gate/up and down phases of
+ * [B][grid] times at which each CTA finished each phase, then [B][grid]
+ * times at which each CTA held that phase's outputs as the inputs of its
+ * next phase (0 where the CTA had no work in it), then the step's start and
+ * end, where B = 4 * layers (QKV, attention, gate/up and down phases of
  * every layer).  `*needed` receives the count;
  * a short `stamps` buffer is an admission error (QB_INVALID_LENGTH). */
 uint32_t qb_session_step_profiled(uint64_t session, uint32_t token, float *logits,
@@ -293,9 +308,11 @@ uint32_t qb_session_step_profiled(uint64_t session, uint32_t token, float *logit
                                   size_t stamps_len, size_t *needed);
 /* Fault-path test hook with no counterpart in the reference: one decode
  * step in which CTA 0 withholds its first-layer QKV outputs, so the polls
- * that wait for them run out after `timeout_ns` (1 ns .. 2 s).  Expected
- * result: QB_DEVICE_TIMEOUT, the session invalidated (as after any
- * execution error) until qb_session_reset; the device stays usable. */
+ * that wait for them run out after `timeout_ns` (1 ns .. 2 s; outside that
+ * range: QB_INVALID_PARAMETERS, with qb_last_detail expected = 2e9 and
+ * actual = timeout_ns, and nothing runs).  Expected result:
+ * QB_DEVICE_TIMEOUT, the session invalidated (as after any execution
+ * error) until qb_session_reset; the device stays usable. */
 uint32_t qb_session_step_withheld(uint64_t session, uint32_t token, uint64_t timeout_ns);
 /* reset, src/kv_cache.rs:225-229. */
 uint32_t qb_session_reset(uint64_t session);

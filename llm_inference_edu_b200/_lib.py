@@ -25,6 +25,7 @@ SIGNATURES = {
     "qb_quantize_int8": ([P, S, S, S, S, P, P, P], U32),
     "qb_dequantize_int8": ([P, P, S, S, S, P, S, P], U32),
     "qb_linear_int8": ([P, S, P, P, S, S, S, P, S, S, P], U32),
+    "qb_linear_int8_lanes4": ([P, S, P, P, S, S, S, P, S, S, P], U32),
     "qb_embedding": ([P, S, P, S, P, S, S, S, P], U32),
     "qb_residual_add": ([P, S, P, S, P, S, P], U32),
     "qb_rmsnorm": ([P, S, P, S, P, S, S, S, F, P], U32),

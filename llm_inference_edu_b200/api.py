@@ -182,7 +182,11 @@ def linear_int8(x, weights: GroupwiseInt8, y, tokens: int, stream=None):
                                 tokens, _stream(stream)), QuantError)
 
 
-linear_int8_lanes4 = linear_int8
+def linear_int8_lanes4(x, weights: GroupwiseInt8, y, tokens: int, stream=None):
+    """Fused dequantizing linear in the four-lane order (src/quantization.rs:218-281)."""
+    _check(lib().qb_linear_int8_lanes4(_ptr(x), x.numel(), _ptr(weights.values), _ptr(weights.scales),
+                                       weights._out, weights._in, weights._group, _ptr(y), y.numel(),
+                                       tokens, _stream(stream)), QuantError)
 
 
 def embedding(token_ids: Sequence[int], table, y, vocab_size: int, width: int, stream=None):
@@ -414,7 +418,10 @@ class CachedSession:
         phase's ("ns"), the slowest CTA's work ("slowest_ns"), the mean CTA's
         work ("mean_ns") and the hand-over latency from the last CTA's finish
         to CTA 0 holding its next inputs ("barrier_ns"; negative when CTA 0's
-        inputs did not wait for the last CTA)."""
+        inputs did not wait for the last CTA).  Per CTA: "ready_ns" (mean
+        over the CTAs of the time from the phase's start to holding its
+        inputs), "compute_ns" (mean time from holding the inputs to the
+        finish) and "last_ready_ns" (the latest CTA to hold its inputs)."""
         need = C.c_size_t()
         lib().qb_session_step_profiled(self.handle, 0, None, 0, None, None, 0, C.byref(need))
         stamps = np.zeros(need.value, dtype=np.uint64)
@@ -426,9 +433,9 @@ class CachedSession:
                                               C.byref(need)), CacheError)
         L = self.model.config.layers
         nb = 4 * L
-        grid = (stamps.size - nb - 2) // nb
-        arr = stamps[:nb * grid].reshape(nb, grid).astype(np.int64)
-        rel = stamps[nb * grid:nb * grid + nb].astype(np.int64)
+        grid = (stamps.size - 2) // (2 * nb)
+        fin = stamps[:nb * grid].reshape(nb, grid).astype(np.int64)
+        rdy = stamps[nb * grid:2 * nb * grid].reshape(nb, grid).astype(np.int64)
         start, end = int(stamps[-2]), int(stamps[-1])
         names = ["qkv", "attention", "gate_up", "down"]
         layers, prev = [], start
@@ -436,12 +443,20 @@ class CachedSession:
             d = {}
             for k, name in enumerate(names):
                 i = 4 * l + k
-                d[name] = {"ns": int(rel[i] - prev), "slowest_ns": int(arr[i].max() - prev),
-                           "mean_ns": float(arr[i].mean() - prev),
-                           "barrier_ns": int(rel[i] - arr[i].max())}
-                prev = int(rel[i])
+                # inputs of phase i are the outputs of phase i - 1
+                r = rdy[i - 1] if i > 0 else np.full(grid, start, dtype=np.int64)
+                act = r > 0
+                rel = int(rdy[i, 0])
+                d[name] = {"ns": int(rel - prev), "slowest_ns": int(fin[i].max() - prev),
+                           "mean_ns": float(fin[i].mean() - prev),
+                           "barrier_ns": int(rel - fin[i].max()),
+                           "ready_ns": float((r[act] - prev).mean()) if act.any() else 0.0,
+                           "last_ready_ns": float((r[act] - prev).max()) if act.any() else 0.0,
+                           "compute_ns": float((fin[i][act] - r[act]).mean()) if act.any() else 0.0}
+                prev = rel
             layers.append(d)
-        profile = {"layers": layers, "logits_ns": end - prev, "total_ns": end - start, "argmax": am.value}
+        profile = {"layers": layers, "logits_ns": end - prev, "total_ns": end - start, "argmax": am.value,
+                   "finish": fin, "ready": rdy, "start": start, "end": end}
         return logits, profile
 
     def decode_greedy(self, token: int, steps: int) -> list:

@@ -42,16 +42,23 @@ def build(force: bool = False, verbose: bool = False) -> str:
         return OUT
     objdir = os.path.join(HERE, "_build")
     os.makedirs(objdir, exist_ok=True)
+    # An object is rebuilt when its source, or any shared header, is newer.
+    hdrs = [os.path.join(CSRC, f) for f in HEADERS]
+    hdrs.append(os.path.join(os.path.dirname(HERE), "include", "qwen_b200.h"))
+    t_hdr = max(os.path.getmtime(h) for h in hdrs)
     objs, procs = [], []
     for src in SOURCES:
         obj = os.path.join(objdir, os.path.splitext(src)[0] + ".o")
-        cmd = ["nvcc", *NVCC_FLAGS, "-c", os.path.join(CSRC, src), "-o", obj]
+        objs.append(obj)
+        path = os.path.join(CSRC, src)
+        if not force and os.path.exists(obj) and os.path.getmtime(obj) > max(t_hdr, os.path.getmtime(path)):
+            continue
+        cmd = ["nvcc", *NVCC_FLAGS, "-c", path, "-o", obj]
         if src.endswith(".cpp"):
-            cmd = ["nvcc", "-x", "cu", *NVCC_FLAGS, "-c", os.path.join(CSRC, src), "-o", obj]
+            cmd = ["nvcc", "-x", "cu", *NVCC_FLAGS, "-c", path, "-o", obj]
         if verbose:
             print(" ".join(cmd), file=sys.stderr)
         procs.append((cmd, subprocess.Popen(cmd)))
-        objs.append(obj)
     for cmd, proc in procs:
         if proc.wait() != 0:
             raise subprocess.CalledProcessError(proc.returncode, cmd)

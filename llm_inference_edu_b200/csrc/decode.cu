@@ -144,7 +144,8 @@ __device__ __forceinline__ float warp_max(float v) {
 // red[2w, 2w + 1]; after one CTA barrier every thread combines the pairs in
 // warp order: s = max(sqrt(eps), max m_w), sum (x/s)^2 = sum s_w (m_w/s)^2.
 // Scaling by reciprocals keeps the result within a few ulps of the
-// reference's divisions.
+// reference's divisions; a maximum of 2^125 or more (whose reciprocal would
+// be subnormal) keeps the divisions.
 template <int EPC>
 __device__ __forceinline__ void block_rmsnorm(const float *in, const float *gain, float *xs, int w, int C,
                                               float eps, float *red) {
@@ -154,11 +155,12 @@ __device__ __forceinline__ void block_rmsnorm(const float *in, const float *gain
 #pragma unroll 2
     for (int i = t; i < w; i += NT) mw = rust_max(mw, fabsf(in[i]));
     mw = warp_max(mw);
+    const bool bigw = mw >= 0x1p125f;  // warp-uniform
     const float rw = 1.0f / mw;
     float sw = 0.0f;
 #pragma unroll 2
     for (int i = t; i < w; i += NT) {
-        const float v = in[i] * rw;
+        const float v = bigw ? in[i] / mw : in[i] * rw;
         sw = sw + v * v;
     }
     sw = warp_sum(sw);
@@ -170,15 +172,17 @@ __device__ __forceinline__ void block_rmsnorm(const float *in, const float *gain
     float m = red[0];
 #pragma unroll
     for (int k = 1; k < NW; ++k) m = rust_max(m, red[2 * k]);
+    const bool big = m >= 0x1p125f;  // CTA-uniform
     const float r = 1.0f / m;
     float ss = 0.0f;
 #pragma unroll
     for (int k = 0; k < NW; ++k) {
-        const float f = red[2 * k] * r;
+        const float f = big ? red[2 * k] / m : red[2 * k] * r;
         ss = ss + red[2 * k + 1] * (f * f);
     }
-    const float seps = se * r;
+    const float seps = big ? se / m : se * r;
     const float rd = 1.0f / sqrtf(ss / (float)w + seps * seps);
+#define QB_XS(v) ((big ? (v) / m : (v) * r) * rd)
     const int padded = C * EPC;
     if ((w & 3) == 0) {
         // Four consecutive elements are one quad of the layout.
@@ -186,16 +190,17 @@ __device__ __forceinline__ void block_rmsnorm(const float *in, const float *gain
         for (int e = 4 * t; e < padded; e += 4 * NT) {
             float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
             if (e < w) {
-                o.x = in[e] * r * rd * gain[e];
-                o.y = in[e + 1] * r * rd * gain[e + 1];
-                o.z = in[e + 2] * r * rd * gain[e + 2];
-                o.w = in[e + 3] * r * rd * gain[e + 3];
+                o.x = QB_XS(in[e]) * gain[e];
+                o.y = QB_XS(in[e + 1]) * gain[e + 1];
+                o.z = QB_XS(in[e + 2]) * gain[e + 2];
+                o.w = QB_XS(in[e + 3]) * gain[e + 3];
             }
             x4[((e % EPC) >> 2) * C + e / EPC] = o;
         }
     } else {
-        for (int i = t; i < padded; i += NT) xs[xq<EPC>(i, C)] = i < w ? in[i] * r * rd * gain[i] : 0.0f;
+        for (int i = t; i < padded; i += NT) xs[xq<EPC>(i, C)] = i < w ? QB_XS(in[i]) * gain[i] : 0.0f;
     }
+#undef QB_XS
     csync();
 }
 
@@ -326,16 +331,24 @@ struct Producer {
         }
     }
 
-    // Waits (bounded) for every copy this producer issued, before exiting
-    // early.
+    // Waits (bounded, each slot with its own limit) for every copy this
+    // producer issued, before the CTA exits early, so no bulk copy still
+    // writes this CTA's shared memory after it is gone.  A copy that has
+    // not landed within the limit means the memory system itself has
+    // stalled for seconds; the producer then records ERR_TIMEOUT (the host
+    // fails the step and invalidates the session) and stops waiting rather
+    // than hold the SM forever.
     __device__ void drain() {
-        const uint64_t t0 = globaltimer_ns();
         for (int s = 0; s < rg.nslot; ++s) {
             // Slot s was last filled in round (s < slot ? round : round - 1).
             const int u = s < slot ? round : round - 1;
             if (u < 0) continue;
+            const uint64_t t0 = globaltimer_ns();
             while (!mbar_try_wait(rg.full + s, (uint32_t)(u & 1)))
-                if (globaltimer_ns() - t0 > p.timeout_ns) return;
+                if (globaltimer_ns() - t0 > p.timeout_ns) {
+                    atomicOr(&p.ctrl->error, ERR_TIMEOUT);
+                    return;
+                }
         }
     }
 };
@@ -706,10 +719,10 @@ __device__ __forceinline__ bool phase_end(const DecodeParams &p, int idx, volati
     return *s_abort == 0;
 }
 
-// Trace mark: CTA 0 holds the inputs of the phase after phase idx.
+// Trace mark: this CTA holds the inputs of the phase after phase idx.
 __device__ __forceinline__ void mark_ready(const DecodeParams &p, int idx) {
-    if (p.trace && idx >= 0 && blockIdx.x == 0 && threadIdx.x == 0)
-        p.trace[(size_t)4 * p.L * gridDim.x + idx] = globaltimer_ns();
+    if (p.trace && idx >= 0 && threadIdx.x == 0)
+        p.trace[((size_t)4 * p.L + idx) * gridDim.x + blockIdx.x] = globaltimer_ns();
 }
 
 // --------------------------------------------------------- elementwise ----
@@ -1380,7 +1393,7 @@ __device__ __forceinline__ void run_lm_head(const DecodeParams &p, const CtaGeom
                 ctrl->ticket = 0;
                 if (p.hbar)
                     for (int k = 0; k < p.qh; ++k) p.hbar[k] = 0u;
-                if (p.trace) p.trace[(size_t)4 * p.L * G + 4 * p.L + 1] = globaltimer_ns();
+                if (p.trace) p.trace[(size_t)8 * p.L * G + 1] = globaltimer_ns();
                 __threadfence();
             }
         }
@@ -1408,7 +1421,7 @@ __global__ void __maxnreg__(128) decode_kernel(const __grid_constant__ DecodePar
     const CtaGeom &cg = s_cg;
     if (threadIdx.x < (int)(sizeof(CtaGeom) / 4))
         ((int *)&s_cg)[threadIdx.x] = ((const int *)(p.geom + b))[threadIdx.x];
-    if (p.trace && b == 0 && threadIdx.x == 0) p.trace[(size_t)NB * G + NB] = globaltimer_ns();
+    if (p.trace && b == 0 && threadIdx.x == 0) p.trace[(size_t)2 * NB * G] = globaltimer_ns();
     // The layer table lives in shared memory for the whole step.
     DecodeLayer *lay = (DecodeLayer *)(sm + p.sm_lay);
     {

@@ -107,9 +107,10 @@ struct DecodeParams {
     int *emitted;             // [cap] greedy id emitted after each position (nullable)
     DecodeCtrl *ctrl;
     // Optional phase trace (globaltimer ns): [4L phases][grid] times at which
-    // each CTA finished the phase, then [4L] times at which CTA 0 held the
-    // inputs of the next phase, then the kernel start (CTA 0) and the end of
-    // the final reduction.  Null = off.
+    // each CTA finished the phase, then [4L phases][grid] times at which each
+    // CTA held the outputs of the phase it consumes next (0: the CTA had no
+    // work in that phase), then the kernel start (CTA 0) and the end of the
+    // final reduction.  Null = off.
     unsigned long long *trace;
     unsigned long long timeout_ns;
     int prefetch;             // L2 prefetch of upcoming weights by the producer warp

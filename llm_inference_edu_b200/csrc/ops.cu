@@ -62,34 +62,71 @@ uint32_t scratch_get(size_t bytes, void **out) {
 
 // ------------------------------------------------------------- linear ----
 
-// One warp per (token, output row); lanes stride the input dimension and the
-// partial sums meet in a fixed shuffle tree (FP32 accumulation).
+// One thread per (token, output row), each dot product in the reference's
+// exact FP32 order, so the results are bit-identical to the crate's:
+//   LANES = 0: sum += x[i] * w[i] for increasing i (linear, src/lib.rs:63-69;
+//              linear_int8, src/quantization.rs:200-212, with w[i] =
+//              f32(q[i]) * scale rounded first);
+//   LANES = 1: four lanes sums[i % 4] += x[i] * w[i] over the first
+//              in - in % 4 elements, then ((s0 + s1) + s2) + s3, then the
+//              tail added in order (dot_lanes4, src/kernels.rs:31-46;
+//              linear_int8_lanes4, src/quantization.rs:246-276).
+// A CTA owns 128 consecutive rows of one token; 32-column tiles of those
+// rows and of x are staged in shared memory by coalesced loads (row stride
+// 33 floats: no bank conflicts when each thread walks its own row).
+// Every operation is an explicitly rounded FP32 multiply or add.
+constexpr int kLinRows = 128, kLinCols = 32;
+
 template <int KIND>  // 0 f32, 1 bf16, 2 int8 (groupwise)
-__global__ void linear_kernel(const float *__restrict__ x, const void *__restrict__ w,
-                              const float *__restrict__ scales, float *__restrict__ y,
-                              size_t tokens, size_t in, size_t out, size_t group) {
-    size_t warp = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    int lane = threadIdx.x & 31;
-    if (warp >= tokens * out) return;
-    size_t t = warp / out, o = warp % out;
+__device__ __forceinline__ float lin_weight(const void *w, const float *scales, size_t o, size_t i, size_t in,
+                                            size_t group, size_t gpr) {
+    if (KIND == 0) return ((const float *)w)[o * in + i];
+    if (KIND == 1) return bf16_to_f32(((const uint16_t *)w)[o * in + i]);
+    return __fmul_rn((float)((const int8_t *)w)[o * in + i], scales[o * gpr + i / group]);
+}
+
+template <int KIND, int LANES>
+__global__ void __launch_bounds__(kLinRows) linear_kernel(const float *__restrict__ x, const void *__restrict__ w,
+                                                          const float *__restrict__ scales, float *__restrict__ y,
+                                                          size_t tokens, size_t in, size_t out, size_t group) {
+    __shared__ float ws[kLinRows][kLinCols + 1];
+    __shared__ float xs[kLinCols];
+    const size_t o0 = (size_t)blockIdx.x * kLinRows;
+    const int tid = threadIdx.x;
+    const size_t o = o0 + tid;
+    const size_t gpr = KIND == 2 ? (in + group - 1) / group : 1;
+    const size_t bulk = LANES ? in - in % 4 : in;
+  for (size_t t = blockIdx.y; t < tokens; t += gridDim.y) {
     const float *xr = x + t * in;
-    float sum = 0.0f;
-    if (KIND == 0) {
-        const float *wr = (const float *)w + o * in;
-        for (size_t i = lane; i < in; i += 32) sum = fmaf(xr[i], wr[i], sum);
-    } else if (KIND == 1) {
-        const uint16_t *wr = (const uint16_t *)w + o * in;
-        for (size_t i = lane; i < in; i += 32) sum = fmaf(xr[i], bf16_to_f32(wr[i]), sum);
-    } else {
-        const int8_t *wr = (const int8_t *)w + o * in;
-        size_t gpr = (in + group - 1) / group;
-        const float *sr = scales + o * gpr;
-        for (size_t i = lane; i < in; i += 32)
-            sum = fmaf(xr[i], __fmul_rn((float)wr[i], sr[i / group]), sum);
+    float sum = 0.0f, s4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    for (size_t i0 = 0; i0 < bulk; i0 += kLinCols) {
+        const int n = (int)(bulk - i0 < (size_t)kLinCols ? bulk - i0 : (size_t)kLinCols);
+        __syncthreads();
+        // Rows [o0, o0 + 128) x columns [i0, i0 + n): element e = r * 32 + c.
+        for (int e = tid; e < kLinRows * kLinCols; e += kLinRows) {
+            const int r = e / kLinCols, c = e % kLinCols;
+            if (o0 + r < out && c < n) ws[r][c] = lin_weight<KIND>(w, scales, o0 + r, i0 + c, in, group, gpr);
+        }
+        if (tid < n) xs[tid] = xr[i0 + tid];
+        __syncthreads();
+        if (o < out) {
+            if (LANES) {
+                // i0 is a multiple of 4, so lane k of this tile is lane k of the row.
+                for (int c = 0; c < n; ++c) s4[c & 3] = __fadd_rn(s4[c & 3], __fmul_rn(xs[c], ws[tid][c]));
+            } else {
+                for (int c = 0; c < n; ++c) sum = __fadd_rn(sum, __fmul_rn(xs[c], ws[tid][c]));
+            }
+        }
     }
-#pragma unroll
-    for (int off = 16; off; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-    if (lane == 0) y[t * out + o] = sum;
+    if (o < out) {
+        if (LANES) {
+            sum = __fadd_rn(__fadd_rn(__fadd_rn(s4[0], s4[1]), s4[2]), s4[3]);
+            for (size_t i = bulk; i < in; ++i)
+                sum = __fadd_rn(sum, __fmul_rn(xr[i], lin_weight<KIND>(w, scales, o, i, in, group, gpr)));
+        }
+        y[t * out + o] = sum;
+    }
+  }
 }
 
 static uint32_t validate_linear(size_t xl, size_t wl, size_t yl, size_t t, size_t in, size_t out) {
@@ -107,14 +144,13 @@ static uint32_t validate_linear(size_t xl, size_t wl, size_t yl, size_t t, size_
     return QB_OK;
 }
 
-template <int KIND>
+template <int KIND, int LANES = 0>
 static uint32_t launch_linear(const float *x, const void *w, const float *scales, float *y,
                               size_t t, size_t in, size_t out, size_t group, void *stream) {
-    size_t warps = t * out;
-    size_t blocks = (warps + 7) / 8;
-    if (blocks > 0x7fffffffu) return QB_DIMENSION_OVERFLOW;
-    linear_kernel<KIND><<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(x, w, scales, y, t,
-                                                                            in, out, group);
+    const size_t bx = (out + kLinRows - 1) / kLinRows;
+    if (bx > 0x7fffffffu) return QB_DIMENSION_OVERFLOW;
+    const dim3 grid((unsigned)bx, (unsigned)(t < 65535 ? t : 65535));
+    linear_kernel<KIND, LANES><<<grid, kLinRows, 0, (cudaStream_t)stream>>>(x, w, scales, y, t, in, out, group);
     QB_CUDA(cudaGetLastError());
     return QB_OK;
 }
@@ -400,7 +436,9 @@ uint32_t qb_linear_f32(const float *x, size_t xl, const float *w, size_t wl, flo
 
 uint32_t qb_linear_lanes4_f32(const float *x, size_t xl, const float *w, size_t wl, float *y,
                               size_t yl, size_t t, size_t in, size_t out, void *stream) {
-    return qb_linear_f32(x, xl, w, wl, y, yl, t, in, out, stream);
+    uint32_t s = validate_linear(xl, wl, yl, t, in, out);
+    if (s) return s;
+    return launch_linear<0, 1>(x, w, nullptr, y, t, in, out, 1, stream);
 }
 
 uint32_t qb_linear_bf16(const float *x, size_t xl, const uint16_t *w, size_t wl, float *y,
@@ -463,9 +501,7 @@ uint32_t qb_dequantize_int8(const int8_t *values, const float *scales, size_t ou
     return QB_OK;
 }
 
-uint32_t qb_linear_int8(const float *x, size_t xl, const int8_t *values, const float *scales,
-                        size_t out, size_t in, size_t group, float *y, size_t yl, size_t t,
-                        void *stream) {
+static uint32_t validate_linear_int8(size_t xl, size_t out, size_t in, size_t group, size_t yl, size_t t) {
     clear_detail();
     if (t == 0) return QB_ZERO_DIMENSION;
     if (out == 0 || in == 0 || group == 0) return QB_ZERO_DIMENSION;
@@ -479,7 +515,23 @@ uint32_t qb_linear_int8(const float *x, size_t xl, const int8_t *values, const f
         set_detail(2, yn, yl);
         return QB_INVALID_LENGTH;
     }
+    return QB_OK;
+}
+
+uint32_t qb_linear_int8(const float *x, size_t xl, const int8_t *values, const float *scales,
+                        size_t out, size_t in, size_t group, float *y, size_t yl, size_t t,
+                        void *stream) {
+    uint32_t s = validate_linear_int8(xl, out, in, group, yl, t);
+    if (s) return s;
     return launch_linear<2>(x, values, scales, y, t, in, out, group, stream);
+}
+
+uint32_t qb_linear_int8_lanes4(const float *x, size_t xl, const int8_t *values, const float *scales,
+                               size_t out, size_t in, size_t group, float *y, size_t yl, size_t t,
+                               void *stream) {
+    uint32_t s = validate_linear_int8(xl, out, in, group, yl, t);
+    if (s) return s;
+    return launch_linear<2, 1>(x, values, scales, y, t, in, out, group, stream);
 }
 
 uint32_t qb_embedding(const uint32_t *ids, size_t count, const float *table, size_t tl, float *y,

@@ -130,7 +130,10 @@ __global__ void rmsnorm_rows(const float *x, const float *g, float *y, Planes P,
 // shuffles, with no CTA barrier.  Eight rows per 256-thread CTA.  The two
 // divisions per element become multiplications by the reciprocals of the
 // row maximum and of the denominator (as in the decode kernel's RMSNorm:
-// within a few ulps of the divisions).
+// within a few ulps of the divisions).  A row maximum of 2^125 or more
+// would make its reciprocal subnormal (lost precision), so such rows keep
+// the division by the maximum; the denominator lies in [w^-1/2, 2^1/2],
+// whose reciprocal is always normal.
 __global__ void rmsnorm_rows_warp(const float *x, const float *g, float *y, Planes P, int n, int w, float eps,
                                   unsigned *err) {
     pdl_trigger();
@@ -152,12 +155,25 @@ __global__ void rmsnorm_rows_warp(const float *x, const float *g, float *y, Plan
             m = rust_max(rust_max(rust_max(rust_max(m, fabsf(v[k].x)), fabsf(v[k].y)), fabsf(v[k].z)), fabsf(v[k].w));
     }
     for (int off = 16; off; off >>= 1) m = rust_max(m, __shfl_xor_sync(0xffffffffu, m, off));
+    const bool big = m >= 0x1p125f;  // warp-uniform
     const float r = 1.0f / m;
+    if (big) {
+#pragma unroll
+        for (int k = 0; k < V4; ++k) {
+            v[k].x = v[k].x / m; v[k].y = v[k].y / m; v[k].z = v[k].z / m; v[k].w = v[k].w / m;
+        }
+    } else {
+#pragma unroll
+        for (int k = 0; k < V4; ++k) {
+            v[k].x = v[k].x * r; v[k].y = v[k].y * r; v[k].z = v[k].z * r; v[k].w = v[k].w * r;
+        }
+    }
+    // v now holds x / m.
     float ss = 0.0f;
 #pragma unroll
     for (int k = 0; k < V4; ++k) {
         if (lane + 32 * k < w4) {
-            const float a = v[k].x * r, b = v[k].y * r, c = v[k].z * r, d = v[k].w * r;
+            const float a = v[k].x, b = v[k].y, c = v[k].z, d = v[k].w;
             ss = ss + a * a;
             ss = ss + b * b;
             ss = ss + c * c;
@@ -165,7 +181,7 @@ __global__ void rmsnorm_rows_warp(const float *x, const float *g, float *y, Plan
         }
     }
     for (int off = 16; off; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-    const float seps = se * r;
+    const float seps = big ? se / m : se * r;
     const float rd = 1.0f / sqrtf(ss / (float)w + seps * seps);
     float4 *yr = reinterpret_cast<float4 *>(y + (size_t)t * w);
     const float4 *g4 = reinterpret_cast<const float4 *>(g);
@@ -175,10 +191,10 @@ __global__ void rmsnorm_rows_warp(const float *x, const float *g, float *y, Plan
         if (i < w4) {
             const float4 gg = g4[i];
             float4 o;
-            o.x = v[k].x * r * rd * gg.x;
-            o.y = v[k].y * r * rd * gg.y;
-            o.z = v[k].z * r * rd * gg.z;
-            o.w = v[k].w * r * rd * gg.w;
+            o.x = v[k].x * rd * gg.x;
+            o.y = v[k].y * rd * gg.y;
+            o.z = v[k].z * rd * gg.z;
+            o.w = v[k].w * rd * gg.w;
             yr[i] = o;
             if (P.p) {
                 const size_t at = (size_t)t * w + 4 * (size_t)i;

@@ -1175,7 +1175,7 @@ uint32_t qb_session_step_profiled(uint64_t session, uint32_t token, float *logit
     if (!sp) return QB_INVALID_HANDLE;
     Session &s = *sp;
     const size_t nb = 4 * s.m->c.layers;
-    const size_t need = nb * (size_t)s.grid + nb + 2;
+    const size_t need = 2 * nb * (size_t)s.grid + 2;
     if (needed) *needed = need;
     if (!stamps || stamps_len < need) {
         set_detail(5, need, stamps_len);
@@ -1214,7 +1214,10 @@ uint32_t qb_session_step_withheld(uint64_t session, uint32_t token, uint64_t tim
     if (!s.valid) return QB_INVALID_STATE;
     if (token >= s.m->c.vocab_size) return QB_INVALID_TOKEN;
     if (s.processed == s.capacity) return QB_FULL;
-    if (timeout_ns == 0 || timeout_ns > 2000000000ull) return QB_INVALID_LENGTH;
+    if (timeout_ns == 0 || timeout_ns > 2000000000ull) {
+        set_detail(0, 2000000000ull, (size_t)timeout_ns);
+        return QB_INVALID_PARAMETERS;
+    }
     DeviceGuard dg(s.device);
     DecodeParams p = s.params;
     p.withhold = 1;

@@ -65,7 +65,8 @@ def decode(prompt: int, steps: int, profile: bool) -> None:
         _sync()
         print(f"decode: {(time.perf_counter() - t0) * 1e6 / steps:.1f} us/token (wall)")
         return
-    acc = {k: np.zeros(3) for k in ("qkv", "attention", "gate_up", "down")}
+    keys = ("ns", "mean_ns", "barrier_ns", "ready_ns", "last_ready_ns", "compute_ns")
+    acc = {k: np.zeros(len(keys)) for k in ("qkv", "attention", "gate_up", "down")}
     tot = []
     for i in range(steps):
         _, prof = s.step_profiled(tok)
@@ -75,13 +76,15 @@ def decode(prompt: int, steps: int, profile: bool) -> None:
         tot.append((prof["total_ns"], prof["logits_ns"]))
         for L in prof["layers"]:
             for k, v in L.items():
-                acc[k] += np.array([v["ns"], v["mean_ns"], v["barrier_ns"]])
+                acc[k] += np.array([v[x] for x in keys])
     n = (steps - 2) * cfg.layers
     print(f"decode at position ~{prompt}: step {np.mean([t[0] for t in tot]) / 1e3:.1f} us, "
           f"LM head {np.mean([t[1] for t in tot]) / 1e3:.1f} us")
     for k, v in acc.items():
-        print(f"  {k:9s} per layer: phase {v[0] / n / 1e3:.2f} us, mean CTA work {v[1] / n / 1e3:.2f} us, "
-              f"hand-over after the last finish {v[2] / n / 1e3:.2f} us")
+        v = v / n / 1e3
+        print(f"  {k:9s} per layer: phase {v[0]:.2f} us, mean CTA work {v[1]:.2f} us, "
+              f"hand-over after the last finish {v[2]:.2f} us; per CTA: inputs held after {v[3]:.2f} us "
+              f"(last {v[4]:.2f} us), then computes {v[5]:.2f} us")
 
 
 def long(prompt: int, steps: int) -> None:

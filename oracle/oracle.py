@@ -109,6 +109,8 @@ def lib():
             ("or_set_threads", [C.c_int], None),
             ("or_get_threads", [], C.c_int),
             ("or_round_bf16", [C.c_float], C.c_float),
+            ("or_synthetic_normal", [C.c_uint64, C.c_uint64, S, C.c_double, C.c_int, P], C.c_int),
+            ("or_synthetic_tokens", [C.c_uint64, C.c_uint64, S, C.c_uint32, P], C.c_int),
         ]:
             f = getattr(L, name)
             f.argtypes = args
@@ -437,3 +439,85 @@ def int8_model_weights(cfg, w, linear_format):
             ql[k] = q
         out["layers"].append(ql)
     return out
+
+
+# --------------------------------------------------- synthetic inputs ----
+#
+# The benchmark workloads' seeded weights and prompts, generated by the
+# oracle library itself (or_synthetic_*), so that a CPU-only run (the
+# reference arm of bench.py) maps no library of the product.  The stream
+# ids and shapes follow the package's synthetic weight dictionary:
+# embedding 1, lm_head 2, final_norm 3, layer l: 100 + 16 l + {q 0, k 1,
+# v 2, o 3, gate 4, up 5, down 6, q_bias 7, k_bias 8, v_bias 9,
+# attn_norm 10, ffn_norm 11}; norm gains 1.0 and biases 0.
+
+STD = 0.02
+
+
+@dataclass(frozen=True)
+class WorkloadConfig:
+    """The model shape fields the oracle reads (src/model.rs:12-25)."""
+    vocab_size: int
+    layers: int
+    hidden_dim: int
+    query_heads: int
+    kv_heads: int
+    head_dim: int
+    ff_dim: int
+    max_tokens: int
+    rope_base: float
+    norm_epsilon: float
+    tied: bool = True
+    qkv_bias: bool = False
+
+    @property
+    def kv_dim(self):
+        return self.kv_heads * self.head_dim
+
+
+def qwen_0_5b_config(max_tokens):
+    return WorkloadConfig(151936, 24, 896, 14, 2, 64, 4864, max_tokens, 1e6, 1e-6, True, True)
+
+
+def qwen_7b_config(max_tokens):
+    return WorkloadConfig(152064, 28, 3584, 28, 4, 128, 18944, max_tokens, 1e6, 1e-6, False, True)
+
+
+def synthetic_normal(seed, stream, n, std=STD, dtype="f32"):
+    out = np.empty(n, dtype=np.float32 if dtype == "f32" else np.uint16)
+    s = lib().or_synthetic_normal(seed, stream, n, std, 0 if dtype == "f32" else 1, _p(out))
+    if s:
+        raise ValueError(f"or_synthetic_normal failed: {s}")
+    return out
+
+
+def synthetic_prompt(vocab, n, seed, stream=7):
+    out = np.empty(n, dtype=np.uint32)
+    s = lib().or_synthetic_tokens(seed, stream, n, vocab, _p(out))
+    if s:
+        raise ValueError(f"or_synthetic_tokens failed: {s}")
+    return [int(v) for v in out]
+
+
+def synthetic_layer(cfg, seed, l, dtype="bf16"):
+    h, kv, ff = cfg.hidden_dim, cfg.kv_dim, cfg.ff_dim
+    shapes = {"q": h * h, "k": kv * h, "v": kv * h, "o": h * h, "gate": ff * h, "up": ff * h, "down": h * ff}
+    base = 100 + 16 * l
+    layer = {k: synthetic_normal(seed, base + i, shapes[k], STD, dtype)
+             for i, k in enumerate(("q", "k", "v", "o", "gate", "up", "down"))}
+    layer["attn_norm"] = np.ones(h, dtype=np.float32)
+    layer["ffn_norm"] = np.ones(h, dtype=np.float32)
+    if cfg.qkv_bias:
+        for name, n in (("q_bias", h), ("k_bias", kv), ("v_bias", kv)):
+            layer[name] = np.zeros(n, dtype=np.float32)
+    return layer
+
+
+def synthetic_weights(cfg, seed, dtype="bf16"):
+    h, V = cfg.hidden_dim, cfg.vocab_size
+    w = {"embedding": synthetic_normal(seed, 1, V * h, STD, dtype),
+         "final_norm": np.ones(h, dtype=np.float32),
+         "layers": [synthetic_layer(cfg, seed, l, dtype) for l in range(cfg.layers)]}
+    if not cfg.tied:
+        w["lm_head"] = synthetic_normal(seed, 2, V * h, STD, dtype)
+    return w

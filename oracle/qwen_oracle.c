@@ -957,3 +957,63 @@ long or_uncached_greedy(const or_model *m, const size_t *prompt, size_t n, const
     free(logits);
     return (long)g;
 }
+
+/* ------------------------------------------------------------------ */
+/* Synthetic inputs (not a reference function).  Every value is a pure  */
+/* function of (seed, stream, index):                                   */
+/*   mix(z)   = splitmix64 finalizer of z + 0x9E3779B97F4A7C15          */
+/*   base     = mix(seed * 0x100000001B3 ^ mix(stream))                  */
+/*   pair k   : a = mix(base + 2k), b = mix(base + 2k + 1),              */
+/*              u1 = ((a >> 11) + 1) 2^-53, u2 = (b >> 11) 2^-53,        */
+/*              r = sqrt(-2 ln u1), z0 = r cos(2 pi u2), z1 = r sin(..)  */
+/*   element 2k + e = (float)(z_e * stddev) (then BF16 nearest-even)     */
+/*   token i  : mix(base + i) mod vocab                                  */
+/* ------------------------------------------------------------------ */
+
+static uint64_t syn_mix(uint64_t z) {
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+static uint64_t syn_base(uint64_t seed, uint64_t stream) {
+    return syn_mix(seed * 0x100000001B3ull ^ syn_mix(stream));
+}
+
+int or_synthetic_normal(uint64_t seed, uint64_t stream, size_t n, double stddev, int out_dtype,
+                        void *out) {
+    if ((!out && n) || (out_dtype != 0 && out_dtype != 1)) return OR_INVALID_LENGTH;
+    const uint64_t base = syn_base(seed, stream);
+    const long long pairs = (long long)((n + 1) / 2);
+    const double two_pi = 6.283185307179586476925286766559;
+#pragma omp parallel for schedule(static) num_threads(or_get_threads())
+    for (long long k = 0; k < pairs; ++k) {
+        uint64_t a = syn_mix(base + 2 * (uint64_t)k), b = syn_mix(base + 2 * (uint64_t)k + 1);
+        double u1 = (double)((a >> 11) + 1) * (1.0 / 9007199254740992.0);
+        double u2 = (double)(b >> 11) * (1.0 / 9007199254740992.0);
+        double r = sqrt(-2.0 * log(u1));
+        double z[2] = {r * cos(two_pi * u2), r * sin(two_pi * u2)};
+        for (int e = 0; e < 2; ++e) {
+            size_t i = 2 * (size_t)k + e;
+            if (i >= n) break;
+            float v = (float)(z[e] * stddev);
+            if (out_dtype == 0) {
+                ((float *)out)[i] = v;
+            } else {
+                float r16 = or_round_bf16(v);
+                uint32_t u;
+                memcpy(&u, &r16, 4);
+                ((uint16_t *)out)[i] = (uint16_t)(u >> 16);
+            }
+        }
+    }
+    return OR_OK;
+}
+
+int or_synthetic_tokens(uint64_t seed, uint64_t stream, size_t n, uint32_t vocab, uint32_t *out) {
+    if (vocab == 0 || (!out && n)) return OR_INVALID_LENGTH;
+    const uint64_t base = syn_base(seed, stream);
+    for (size_t i = 0; i < n; ++i) out[i] = (uint32_t)(syn_mix(base + i) % vocab);
+    return OR_OK;
+}

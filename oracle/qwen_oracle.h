@@ -134,6 +134,15 @@ long or_greedy(or_session *s, const size_t *prompt, size_t n, const size_t *stop
 long or_uncached_greedy(const or_model *m, const size_t *prompt, size_t n, const size_t *stops,
                         size_t nstops, size_t max_new, size_t *out);
 
+/* Seeded synthetic inputs for the benchmark workloads: the documented
+ * counter-based generator (splitmix64 finalizer + Box-Muller) that the
+ * library's qb_synthetic_normal / qb_synthetic_tokens also implement, so the
+ * oracle can build the same weights and prompts without loading the
+ * library.  out_dtype 0 = FP32, 1 = BF16 bits (nearest-even). */
+int or_synthetic_normal(uint64_t seed, uint64_t stream, size_t n, double stddev, int out_dtype,
+                        void *out);
+int or_synthetic_tokens(uint64_t seed, uint64_t stream, size_t n, uint32_t vocab, uint32_t *out);
+
 #ifdef __cplusplus
 }
 #endif

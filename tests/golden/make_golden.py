@@ -89,7 +89,9 @@ def tinyb_vectors(ref):
 
 
 def main():
-    ref = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py <reference checkout>")
+    ref = sys.argv[1]
     copy_reference_vectors(ref)
     tinyb_vectors(ref)
     print("golden fixtures written to", HERE)

@@ -164,6 +164,10 @@ def test_withheld_exchange_times_out_and_recovers():
     ref = [first] + s.decode_greedy(first, 8)
     s.reset()
     assert int(np.argmax(s.prefill(prompt))) == first
+    for bad in (0, 2_000_000_001):  # out of range: refused before anything runs
+        with pytest.raises(qb.CacheError) as e:
+            s.step_withheld(first, bad)
+        assert e.value.kind == "InvalidParameters" and s.is_valid() and s.processed() == len(prompt)
     with pytest.raises(qb.CacheError) as e:
         s.step_withheld(first, 20_000_000)
     assert e.value.kind == "DeviceTimeout" and not s.is_valid()

@@ -29,6 +29,7 @@ def host(t):
 
 def test_linear_known_answers_and_f64():
     import llm_inference_edu_b200 as qb
+    from oracle import oracle
     y = zeros(4)
     qb.linear(dev(np.float32([1, 2, 3, 4, 5, 6])), dev(np.float32([1, 0, -1, 2, 1, 0])), y, 2, 3, 2)
     assert list(host(y)) == [-2, 4, -2, 13]
@@ -36,10 +37,31 @@ def test_linear_known_answers_and_f64():
         x = (((np.arange(3 * n) * 17 % 101) - 50.0) / 53).astype(np.float32)
         w = (((np.arange(7 * n) * 23 % 97) - 48.0) / 61).astype(np.float32)
         exp = x.reshape(3, n).astype(np.float64) @ w.reshape(7, n).astype(np.float64).T
-        for fn in (qb.linear, qb.linear_lanes4):
+        for lanes, fn in ((False, qb.linear), (True, qb.linear_lanes4)):
             y = zeros(21)
             fn(dev(x), dev(w), y, 3, n, 7)
             assert_close(host(y), exp.ravel(), name=f"n={n}")
+            # the reference's own summation order: bit-identical
+            _, ref, _ = oracle.linear(x, w, 3, n, 7, lanes4=lanes)
+            assert np.array_equal(host(y).view(np.uint32), ref.view(np.uint32)), (n, lanes)
+
+
+def test_linear_bit_exact_at_model_shapes():
+    # Every standalone linear follows the crate's order (scalar, or the four
+    # lanes of dot_lanes4), so outputs are bit-identical to the oracle's
+    # restatement at the 0.5B shapes, including tails (in % 4 != 0) and
+    # more rows than one CTA holds.
+    import llm_inference_edu_b200 as qb
+    from oracle import oracle
+    rng = np.random.default_rng(11)
+    for t, n, o in [(1, 896, 1152), (3, 4864, 130), (2, 1003, 257)]:
+        x = rng.standard_normal(t * n).astype(np.float32)
+        w = (rng.standard_normal(o * n) * 0.02).astype(np.float32)
+        for lanes, fn in ((False, qb.linear), (True, qb.linear_lanes4)):
+            y = zeros(t * o)
+            fn(dev(x), dev(w), y, t, n, o)
+            _, ref, _ = oracle.linear(x, w, t, n, o, lanes4=lanes)
+            assert np.array_equal(host(y).view(np.uint32), ref.view(np.uint32)), (t, n, o, lanes)
 
 
 def test_linear_admission_leaves_output_unchanged():
@@ -62,7 +84,7 @@ def test_linear_bf16_weights():
     y = zeros(600)
     qb.linear(dev(x), dev(w16.view(np.int16)).view(torch.int16), y, 2, 896, 300)
     _, ref, _ = oracle.linear(x, synthetic.as_f32(w16), 2, 896, 300)
-    assert np.max(np.abs(host(y) - ref)) < 1e-5
+    assert np.array_equal(host(y).view(np.uint32), ref.view(np.uint32))
 
 
 def test_quantize_bit_exact_and_kats():
@@ -86,10 +108,12 @@ def test_quantize_bit_exact_and_kats():
         assert np.array_equal(host(q.values), ref.values.ravel())
         assert np.array_equal(host(q.scales).view(np.uint32), ref.scales.ravel().view(np.uint32))
         x = rng.standard_normal(2 * width).astype(np.float32)
-        y = zeros(2 * rows)
-        qb.linear_int8(dev(x), q, y, 2)
-        _, yr = oracle.linear_int8(x, ref, 2)
-        assert_close(host(y), yr, atol=1e-4, rtol=1e-4)
+        for lanes, fn in ((False, qb.linear_int8), (True, qb.linear_int8_lanes4)):
+            y = zeros(2 * rows)
+            fn(dev(x), q, y, 2)
+            _, yr = oracle.linear_int8(x, ref, 2, lanes4=lanes)
+            # x * (f32(q) * scale) summed in the crate's order: bit-identical
+            assert np.array_equal(host(y).view(np.uint32), yr.view(np.uint32)), (rows, width, group, lanes)
 
 
 def test_quantize_admission_writes_nothing():

@@ -443,3 +443,30 @@ def test_tinyb_numpy_golden(oracle):
     for row in fx["positions"]:
         _, lg, _ = m.forward(fx["history"][:row["position"] + 1])
         assert_close(lg, row["logits"], name=f"pos {row['position']}")
+
+
+# ------------------------------------------------- synthetic inputs ----
+
+def test_oracle_generator_matches_library(oracle):
+    # The reference arm of bench.py builds its weights with the oracle's own
+    # generator (it must map no product library); it has to draw exactly the
+    # library's values.
+    from llm_inference_edu_b200 import synthetic
+    for seed, stream, n, dtype in ((1, 1, 4097, "bf16"), (2, 107, 1001, "f32"), (0, 3, 1, "bf16")):
+        a = oracle.synthetic_normal(seed, stream, n, 0.02, dtype)
+        b = synthetic.normal(seed, stream, n, 0.02, dtype)
+        assert np.array_equal(a.view(np.uint16 if dtype == "bf16" else np.uint32),
+                              b.view(np.uint16 if dtype == "bf16" else np.uint32))
+    assert oracle.synthetic_prompt(151936, 128, 1) == synthetic.prompt(151936, 128, 1)
+    cfg = presets.tiny_b()
+    ocfg = oracle.WorkloadConfig(256, 2, 64, 4, 2, 16, 128, 64, 1e4, 1e-6, True, True)
+    w1, w2 = synthetic.weights(cfg.__class__(**{**cfg.__dict__, "qkv_bias": True}), 0, "bf16"), \
+        oracle.synthetic_weights(ocfg, 0, "bf16")
+    assert np.array_equal(w1["embedding"], w2["embedding"])
+    for l1, l2 in zip(w1["layers"], w2["layers"]):
+        assert sorted(l1) == sorted(l2)
+        for k in l1:
+            assert np.array_equal(l1[k], l2[k]), k
+    q = oracle.qwen_0_5b_config(64)
+    p = presets.qwen_0_5b(64)
+    assert all(getattr(q, f) == getattr(p, f) for f in p.__dataclass_fields__)

@@ -6,6 +6,9 @@ request beyond its fixed scratch is refused before any device work.
 Named to be collected last, so it also runs after every other GPU test has
 used the library's allocating paths."""
 import ctypes as C
+import os
+import subprocess
+import sys
 
 import numpy as np
 import pytest
@@ -71,3 +74,43 @@ def test_rope_static_matches_rope_on_consecutive_calls():
     st, y = run(L.qb_rope_static, x, 4, 2, 8, 0, 1e4)
     s_ref, y_ref = run(L.qb_rope, x, 4, 2, 8, 0, 1e4)
     assert st == 0 and s_ref == 0 and np.array_equal(y.view(np.uint32), y_ref.view(np.uint32))
+
+
+_NO_ALLOC_PROBE = r"""
+import ctypes as C, sys
+sys.path.insert(0, sys.argv[1])
+import torch
+from llm_inference_edu_b200._lib import lib
+L = lib()
+torch.cuda.init()
+x = torch.randn(1023 * 14 * 64, device="cuda")
+y = torch.empty_like(x)
+stream = torch.cuda.current_stream().cuda_stream
+
+def call(tokens, heads, hd, start):
+    n = tokens * heads * hd
+    st = L.qb_rope_static(C.c_void_p(x.data_ptr()), n, C.c_void_p(y.data_ptr()), n, tokens, heads, hd,
+                          start, 1e6, C.c_void_p(stream))
+    assert st == 0, st
+
+call(16, 2, 64, 0)  # the first call loads the library's device code and its static array
+torch.cuda.synchronize()
+free0 = torch.cuda.mem_get_info()[0]
+for args in [(1023, 14, 64, 5), (37, 2, 128, 100000), (1, 1, 2, 0), (1023, 14, 64, 7)]:
+    call(*args)
+torch.cuda.synchronize()
+free1 = torch.cuda.mem_get_info()[0]
+print(free0, free1)
+assert free0 == free1, (free0, free1)
+"""
+
+
+@pytest.mark.gpu
+def test_rope_static_allocates_no_device_memory():
+    # In a fresh process (so nothing else of the library has run): once the
+    # first call has loaded the device code, further calls of several sizes
+    # leave the device's free memory unchanged -- no cudaMalloc, no pool.
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, "-c", _NO_ALLOC_PROBE, root], capture_output=True, text=True,
+                       timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
