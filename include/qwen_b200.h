@@ -281,7 +281,11 @@ typedef struct {
 
 /* CachedSession::new, src/kv_cache.rs:167-200.  `budget_bytes` bounds the
  * logical KV bytes plus workspace (the reference fixes 128 MiB,
- * src/kv_cache.rs:184-190); 0 means unbounded. */
+ * src/kv_cache.rs:184-190); 0 means unbounded.  The device cache is paged:
+ * per layer a K and a V pool of 16-position pages, each page
+ * [kv_heads][16][head_dim] (FP32 or BF16), allocated for the whole
+ * capacity at creation and reached through the session's page table; the
+ * reported byte counts stay the reference's (FP32, unpaged). */
 uint32_t qb_session_create(uint64_t model, size_t capacity, uint32_t kv_dtype,
                            size_t budget_bytes, uint64_t *out_session);
 /* step_into, src/kv_cache.rs:306-346.  `logits` (HOST, nullable) receives
@@ -370,8 +374,10 @@ uint32_t qb_generation_free(uint64_t generation);
  * (src/kv_cache.rs:186-215 is the per-token step each row here repeats).
  * `sequences` rows advance in lockstep, each with its own KV cache of
  * `capacity` positions; every row equals what a CachedSession fed the same
- * tokens would compute (within FP32 reassociation).  Created on the
- * model's device; the model must outlive it. */
+ * tokens would compute (within FP32 reassociation).  The sequences' caches
+ * share one page pool per layer (16-position pages; sequence s's page j is
+ * pool page j * sequences + s).  Created on the model's device; the model
+ * must outlive it. */
 typedef struct {
     size_t sequences, capacity, processed;
     int32_t valid;

@@ -141,8 +141,9 @@ __device__ __forceinline__ float warp_max(float v) {
 // Scaled RMSNorm (src/ops.rs:137-149) of `in` (shared, width w) into the
 // quad-major layout for EPC/C, zero-padded to C * EPC.  Each warp reduces
 // its slice to a pair (m_w = max |x|, s_w = sum (x / m_w)^2) and leaves it in
-// red[2w, 2w + 1]; after one CTA barrier every thread combines the pairs in
-// warp order: s = max(sqrt(eps), max m_w), sum (x/s)^2 = sum s_w (m_w/s)^2.
+// red[2w, 2w + 1]; after one CTA barrier every warp combines the pairs,
+// lane k taking warp k's: s = max(sqrt(eps), max m_w), sum (x/s)^2 =
+// sum s_w (m_w/s)^2 (shuffle trees; no serial chain of loads).
 // Scaling by reciprocals keeps the result within a few ulps of the
 // reference's divisions; a maximum of 2^125 or more (whose reciprocal would
 // be subnormal) keeps the divisions.
@@ -169,18 +170,19 @@ __device__ __forceinline__ void block_rmsnorm(const float *in, const float *gain
         red[2 * warp + 1] = sw;
     }
     csync();
-    float m = red[0];
-#pragma unroll
-    for (int k = 1; k < NW; ++k) m = rust_max(m, red[2 * k]);
+    const float2 pr = lane < NW ? *reinterpret_cast<const float2 *>(red + 2 * lane) : make_float2(se, 0.0f);
+    const float m = warp_max(pr.x);
     const bool big = m >= 0x1p125f;  // CTA-uniform
     const float r = 1.0f / m;
-    float ss = 0.0f;
-#pragma unroll
-    for (int k = 0; k < NW; ++k) {
-        const float f = big ? red[2 * k] / m : red[2 * k] * r;
-        ss = ss + red[2 * k + 1] * (f * f);
+    float f, seps;
+    if (big) {
+        f = pr.x / m;
+        seps = se / m;
+    } else {
+        f = pr.x * r;
+        seps = se * r;
     }
-    const float seps = big ? se / m : se * r;
+    const float ss = warp_sum(pr.y * (f * f));
     const float rd = 1.0f / sqrtf(ss / (float)w + seps * seps);
 #define QB_XS(v) ((big ? (v) / m : (v) * r) * rd)
     const int padded = C * EPC;
@@ -367,7 +369,7 @@ __device__ __forceinline__ void prefetch_rows(const uint8_t *base, size_t bytes)
 // Prefetches into L2 everything phase k of this CTA will stream: its weight
 // rows and, for attention, the cached K/V rows of its heads.
 __device__ void prefetch_phase(const DecodeParams &p, const DecodeLayer *lay, const CtaGeom &cg, int k,
-                               int pos) {
+                               int pos, const float *sm) {
     if (!p.prefetch || k > 4 * p.L) return;
     if (k == 4 * p.L) {
         prefetch_rows(p.head + (size_t)cg.lm_v0 * p.semb, (size_t)min(cg.lm_n, LM_PREFETCH * p.kind[K_LM].rpc) * p.semb);
@@ -381,8 +383,16 @@ __device__ void prefetch_phase(const DecodeParams &p, const DecodeLayer *lay, co
         for (int a = 0; a < cg.natt; ++a) {
             prefetch_rows(Ly.wo + ((size_t)cg.att_hh[a] * p.h + cg.att_r0[a]) * p.shd, (size_t)cg.att_n[a] * p.shd);
             const int g = cg.att_hh[a] / p.group;
-            prefetch_rows(Ly.kc + (size_t)g * p.cap * p.hd * esz, (size_t)pos * p.hd * esz);
-            prefetch_rows(Ly.vc + (size_t)g * p.cap * p.hd * esz, (size_t)pos * p.hd * esz);
+            // The group's block of every page that holds cached positions.
+            const int *ptab = (const int *)(sm + p.sm_ptab);
+            const size_t blk = (size_t)kPageTokens * p.hd * esz;
+            const int np = (pos + kPageTokens - 1) / kPageTokens;
+#pragma unroll 1
+            for (int j = threadIdx.x & 31; j < np; j += 32) {
+                const size_t off = ((size_t)ptab[j] * p.kvh + g) * blk;
+                prefetch_l2_bulk(Ly.kc + off, (uint32_t)blk);
+                prefetch_l2_bulk(Ly.vc + off, (uint32_t)blk);
+            }
         }
         break;
     }
@@ -396,20 +406,20 @@ __device__ void produce(const DecodeParams &p, const DecodeLayer *lay, const Cta
                         volatile int *s_abort) {
     Producer pr(p, ring_of(p, sm), s_abort);
     const bool leader = (threadIdx.x & 31) == 0;
-    for (int k = 0; k < LOOKAHEAD; ++k) prefetch_phase(p, lay, cg, k, pos);
+    for (int k = 0; k < LOOKAHEAD; ++k) prefetch_phase(p, lay, cg, k, pos, sm);
 #pragma unroll 1
     for (int l = 0; l < p.L && pr.alive; ++l) {
         const DecodeLayer &Ly = lay[l];
         const int ph = 4 * l;
-        prefetch_phase(p, lay, cg, ph + LOOKAHEAD, pos);
+        prefetch_phase(p, lay, cg, ph + LOOKAHEAD, pos, sm);
         if (leader) pr.block(Ly.wqkv + (size_t)cg.qkv_r0 * p.sh, cg.qkv_n, p.kind[K_QKV]);
-        prefetch_phase(p, lay, cg, ph + 1 + LOOKAHEAD, pos);
+        prefetch_phase(p, lay, cg, ph + 1 + LOOKAHEAD, pos, sm);
         if (leader)
             for (int a = 0; a < cg.natt; ++a)
                 pr.block(Ly.wo + ((size_t)cg.att_hh[a] * p.h + cg.att_r0[a]) * p.shd, cg.att_n[a], p.kind[K_O]);
-        prefetch_phase(p, lay, cg, ph + 2 + LOOKAHEAD, pos);
+        prefetch_phase(p, lay, cg, ph + 2 + LOOKAHEAD, pos, sm);
         if (leader) pr.block(Ly.wgu + (size_t)2 * cg.gu_f0 * p.sh, 2 * cg.gu_n, p.kind[K_GU]);
-        prefetch_phase(p, lay, cg, ph + 3 + LOOKAHEAD, pos);
+        prefetch_phase(p, lay, cg, ph + 3 + LOOKAHEAD, pos, sm);
         if (leader) pr.block(Ly.wd + (size_t)cg.dn_r0 * p.sff, cg.dn_n, p.kind[K_DN]);
         pr.alive = __shfl_sync(FULL, (int)pr.alive, 0) != 0;
     }
@@ -805,6 +815,12 @@ __device__ __forceinline__ float silu1(float v) {
     return v * e / (1.0f + e);
 }
 
+// Element offset of the row of (KV head g, position q) in a layer's page
+// pool; `ptab` is the page table staged in shared memory.
+__device__ __forceinline__ size_t kv_row(const DecodeParams &p, const int *ptab, int g, int q) {
+    return (((size_t)ptab[q / kPageTokens] * p.kvh + g) * kPageTokens + (q % kPageTokens)) * (size_t)p.hd;
+}
+
 template <int KVBF16>
 __device__ __forceinline__ float kv_load(const uint8_t *base, size_t idx) {
     if (KVBF16) return bf16_to_f32(__ldcg((const unsigned short *)base + idx));
@@ -890,12 +906,12 @@ __device__ __forceinline__ void attention_context(const DecodeParams &p, const D
     for (int i = t; i < hd; i += NT)
         if (!isfinite(qs[i]) || !isfinite(ks[i])) atomicOr(&p.ctrl->error, ERR_NONFINITE);
     const size_t esz = KVBF16 ? 2 : 4;
-    const uint8_t *K = Ly.kc + (size_t)g * p.cap * hd * esz;
-    const uint8_t *Vc = Ly.vc + (size_t)g * p.cap * hd * esz;
+    const int *ptab = (const int *)(sm + p.sm_ptab);
+    const uint8_t *K = Ly.kc, *Vc = Ly.vc;  // page pools; rows at kv_row()
     if (writer) {
 #pragma unroll 1
         for (int i = t; i < hd; i += NT) {
-            const size_t idx = (size_t)g * p.cap * hd + (size_t)pos * hd + i;
+            const size_t idx = kv_row(p, ptab, g, pos) + i;
             if (KVBF16) {
                 ((uint16_t *)Ly.kc)[idx] = f32_to_bf16_rne(ks[i]);
                 ((uint16_t *)Ly.vc)[idx] = f32_to_bf16_rne(vs[i]);
@@ -927,7 +943,7 @@ __device__ __forceinline__ void attention_context(const DecodeParams &p, const D
             }
         } else if (q < pos) {
             if (vec) {
-                const uint8_t *row = K + (size_t)q * row_bytes;
+                const uint8_t *row = K + kv_row(p, ptab, g, q) * esz;
                 const int c0 = sub * 4;
                 uint4 kc[4];
 #pragma unroll
@@ -948,7 +964,7 @@ __device__ __forceinline__ void attention_context(const DecodeParams &p, const D
                 }
             } else {
 #pragma unroll 1
-                for (int i = 0; i < hd; ++i) s = s + qs[i] * kv_load<KVBF16>(K, (size_t)q * hd + i);
+                for (int i = 0; i < hd; ++i) s = s + qs[i] * kv_load<KVBF16>(K, kv_row(p, ptab, g, q) + i);
             }
         }
 #pragma unroll 1
@@ -996,7 +1012,7 @@ __device__ __forceinline__ void attention_context(const DecodeParams &p, const D
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
                 const int q = q0 + u * PG;
-                if (q < pos && q < hi) vc[u] = __ldcg((const uint4 *)(Vc + (size_t)q * row_bytes + (size_t)c * 16));
+                if (q < pos && q < hi) vc[u] = __ldcg((const uint4 *)(Vc + kv_row(p, ptab, g, q) * esz + (size_t)c * 16));
             }
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
@@ -1051,7 +1067,7 @@ __device__ __forceinline__ void attention_context(const DecodeParams &p, const D
             if (i < hd) {
 #pragma unroll 1
                 for (int q = 0; q <= pos; ++q) {
-                    const float v = q == pos ? vs[i] : kv_load<KVBF16>(Vc, (size_t)q * hd + i);
+                    const float v = q == pos ? vs[i] : kv_load<KVBF16>(Vc, kv_row(p, ptab, g, q) + i);
                     s = s + (sc[q] / se) * v;
                 }
                 flag_nonfinite(p.ctrl, s);
@@ -1430,6 +1446,13 @@ __global__ void __maxnreg__(128) decode_kernel(const __grid_constant__ DecodePar
         const int words = p.L * (int)(sizeof(DecodeLayer) / 4);
 #pragma unroll 1
         for (int i = threadIdx.x; i < words; i += kDecodeBlock) dst[i] = src[i];
+    }
+    // The page table entries of the pages that hold positions 0 .. pos.
+    {
+        int *sp = (int *)(sm + p.sm_ptab);
+        const int np = pos / kPageTokens + 1;
+#pragma unroll 1
+        for (int i = threadIdx.x; i < np; i += kDecodeBlock) sp[i] = __ldg(p.ptab + i);
     }
     const Ring rg = ring_of(p, sm);
     if (threadIdx.x == 0) {

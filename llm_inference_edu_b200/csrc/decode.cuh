@@ -17,6 +17,12 @@ enum { WF_F32 = 0, WF_BF16 = 1, WF_I8 = 2 };
 // Error bits reported by the kernel in DecodeCtrl::error.
 enum { ERR_NONFINITE = 1u, ERR_TIMEOUT = 2u };
 
+// Positions per KV-cache page.  A layer's cache is a pool of pages, each
+// [kv_heads][kPageTokens][head_dim] (K and V in separate pools); a page
+// table maps a sequence's page j (positions 16 j .. 16 j + 15) to a page of
+// the pool.
+constexpr int kPageTokens = 16;
+
 // One layer's device tensors.  Every weight matrix is row-major with a row
 // stride padded to a multiple of 16 bytes (zero padding).  INT8 rows are
 // stored biased (u = q + 128) with one FP32 scale per output row.
@@ -32,8 +38,8 @@ struct DecodeLayer {
     const float *sd;
     const float *attn_norm;  // [h]
     const float *ffn_norm;   // [h]
-    uint8_t *kc;          // [kv_heads][capacity][head_dim] rotated keys (FP32 or BF16)
-    uint8_t *vc;          // [kv_heads][capacity][head_dim] values
+    uint8_t *kc;          // K page pool: [pages][kv_heads][16][head_dim] rotated keys (FP32 or BF16)
+    uint8_t *vc;          // V page pool, same layout
 };
 
 // Device-resident control block shared by the host and every step.
@@ -83,6 +89,7 @@ struct DecodeParams {
     float eps, sqrt_hd;
     int ch, chd, cff, cemb;   // 16-byte chunks per row for K = h, hd, ff and the table
     size_t sh, shd, sff, semb;  // row strides in bytes
+    const int *ptab;          // page table of the session: [ceil(cap / 16)] pool pages
     int rqkv;                 // h + 2 * kv_heads * head_dim
     KindGeom kind[NKIND];
     const CtaGeom *geom;      // [grid]
@@ -132,6 +139,8 @@ struct DecodeParams {
     // attention scores or the CTA's logits; q: q, k, v of one head; red:
     // cross-warp partials; lay: the layer table.
     int sm_xs, sm_h2, sm_gain, sm_rv, sm_sc, sm_q, sm_red, sm_lay;
+    // The page table's first ceil(cap / 16) entries, staged by every step.
+    int sm_ptab;
     // Weight ring: nslot slots of slot_bytes at sm_ring (128-byte aligned) and
     // their full/empty mbarriers at sm_bar (2 * nslot, 8-byte aligned).
     int sm_bar, sm_ring, nslot, slot_bytes, sm_total;

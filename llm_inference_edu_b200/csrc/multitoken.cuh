@@ -9,6 +9,7 @@
 
 #include "common.cuh"
 #include "decode.cuh"
+#include "prefill.cuh"
 
 namespace qb {
 namespace mt {
@@ -124,9 +125,8 @@ __device__ __forceinline__ void epilogue_gu(const GemmW &w, int t, int r, float 
 struct RopeKv {
     const int *pos, *seq;
     const float2 *rope;  // [cap][hd / 2]
-    uint8_t *kv;         // cache base: sequence s, layer l: K at kv + s seq_bytes + 2 l layer_bytes, V after it
-    size_t seq_bytes, layer_bytes;
-    int l, h, kvh, hd, cap, kv_bf16;
+    KvPages kv;          // the paged cache
+    int l, h, kvh, hd, kv_bf16;
 };
 
 // Output row r of token t of the QKV projection, y (after scale and bias),
@@ -139,7 +139,6 @@ __device__ __forceinline__ void qkv_rope_store(const RopeKv &k, float *qkv, int 
     const int half = k.hd >> 1, kvw = k.kvh * k.hd;
     const int p = k.pos[t];
     flag_bad(err, y);
-    uint8_t *kc = k.kv + (size_t)k.seq[t] * k.seq_bytes + (size_t)(2 * k.l) * k.layer_bytes;
     if (r < k.h + kvw) {
         const int rr = r < k.h ? r : r - k.h, d = rr & (k.hd - 1);
         const float2 cs = k.rope[(size_t)p * half + (d & (half - 1))];
@@ -149,13 +148,14 @@ __device__ __forceinline__ void qkv_rope_store(const RopeKv &k, float *qkv, int 
             qkv[(size_t)t * ldq + r] = o;
             return;
         }
-        const size_t at = ((size_t)(rr / k.hd) * k.cap + p) * k.hd + d;
+        uint8_t *kc = k.kv.k(k.l);
+        const size_t at = k.kv.row(k.seq[t], rr / k.hd, p) + d;
         if (k.kv_bf16) ((uint16_t *)kc)[at] = bf16_rn(o);
         else ((float *)kc)[at] = o;
     } else {
         const int rr = r - k.h - kvw, d = rr & (k.hd - 1);
-        const size_t at = ((size_t)(rr / k.hd) * k.cap + p) * k.hd + d;
-        uint8_t *vc = kc + k.layer_bytes;
+        uint8_t *vc = k.kv.v(k.l);
+        const size_t at = k.kv.row(k.seq[t], rr / k.hd, p) + d;
         if (k.kv_bf16) ((uint16_t *)vc)[at] = bf16_rn(y);
         else ((float *)vc)[at] = y;
     }

@@ -329,23 +329,17 @@ __global__ void __launch_bounds__(256) gemm_rows(const float *X, int ldx, int n,
 
 // -------------------------------------------------------------- attention ----
 
-// K (layer l) of sequence `seq`; V follows at + kv_layer_bytes.
-__device__ __forceinline__ uint8_t *kv_k(uint8_t *kv, size_t seq_bytes, size_t layer_bytes, int seq, int l) {
-    return kv + (size_t)seq * seq_bytes + (size_t)(2 * l) * layer_bytes;
-}
-
 // RoPE of every query and key head of each token (at its own position) with
 // the host table, in place, and the K (rotated) and V write into its
 // sequence's cache -- BF16 round-to-nearest-even when the cache is BF16.
 __global__ void rope_kv(float *qkv, int n, const int *pos, const int *seqs, int l, int h, int qh, int kvh, int hd,
-                        const float2 *rope, int cap, uint8_t *kv, size_t seq_bytes, size_t layer_bytes, int kv_bf16,
-                        unsigned *err) {
+                        const float2 *rope, KvPages kv, int kv_bf16, unsigned *err) {
     pdl_trigger();
     pdl_wait();
     const int half = hd / 2, rq = h + 2 * kvh * hd;
     for (int t = blockIdx.x; t < n; t += gridDim.x) {
         const int p = pos[t];
-        uint8_t *kc = kv_k(kv, seq_bytes, layer_bytes, seqs[t], l), *vc = kc + layer_bytes;
+        uint8_t *kc = kv.k(l), *vc = kv.v(l);
         float *row = qkv + (size_t)t * rq;
         const float2 *rp = rope + (size_t)p * half;
         for (int idx = threadIdx.x; idx < qh * half; idx += blockDim.x) {
@@ -367,7 +361,7 @@ __global__ void rope_kv(float *qkv, int n, const int *pos, const int *seqs, int 
             const float k0 = a * cs.x - b * cs.y, k1 = b * cs.x + a * cs.y;
             flag_bad(err, k0);
             flag_bad(err, k1);
-            const size_t base = ((size_t)g * cap + p) * hd;
+            const size_t base = kv.row(seqs[t], g, p);
             if (kv_bf16) {
                 ((uint16_t *)kc)[base + j] = f32_to_bf16_rne(k0);
                 ((uint16_t *)kc)[base + j + half] = f32_to_bf16_rne(k1);
@@ -379,7 +373,7 @@ __global__ void rope_kv(float *qkv, int n, const int *pos, const int *seqs, int 
         for (int idx = threadIdx.x; idx < kvh * hd; idx += blockDim.x) {
             const int g = idx / hd, i = idx - g * hd;
             const float v = row[h + (size_t)kvh * hd + (size_t)g * hd + i];
-            const size_t at = ((size_t)g * cap + p) * hd + i;
+            const size_t at = kv.row(seqs[t], g, p) + i;
             if (kv_bf16) ((uint16_t *)vc)[at] = f32_to_bf16_rne(v);
             else ((float *)vc)[at] = v;
         }
@@ -399,21 +393,21 @@ __device__ __forceinline__ float kv_at(const uint8_t *base, size_t idx) {
 // scores [max_pos + 1], 32 floats of reduction space.
 template <int KVBF16>
 __global__ void attention_rows(const float *qkv, int n, const int *pos, const int *seqs, int l, int max_pos, int h,
-                               int qh, int kvh, int hd, int group, int cap, const uint8_t *kv, size_t seq_bytes,
-                               size_t layer_bytes, float sqrt_hd, float *ctx, Planes P, unsigned *err) {
+                               int qh, int kvh, int hd, int group, KvPages kv, float sqrt_hd, float *ctx, Planes P,
+                               unsigned *err) {
     pdl_trigger();
     pdl_wait();
     extern __shared__ float asm_[];
     const int t = blockIdx.x / qh, hh = blockIdx.x - t * qh, g = hh / group, p = pos[t];
     const int rq = h + 2 * kvh * hd;
-    const uint8_t *kc = kv + (size_t)seqs[t] * seq_bytes + (size_t)(2 * l) * layer_bytes, *vc = kc + layer_bytes;
+    const uint8_t *kc = kv.k(l), *vc = kv.v(l);
+    const int sq = seqs[t];
     float *qs = asm_, *sc = qs + hd, *red = sc + (max_pos + 1);
     for (int i = threadIdx.x; i < hd; i += blockDim.x) qs[i] = qkv[(size_t)t * rq + (size_t)hh * hd + i];
     __syncthreads();
-    const size_t kv0 = (size_t)g * cap * hd;
     float m = -INFINITY;
     for (int q = threadIdx.x; q <= p; q += blockDim.x) {
-        const size_t row = kv0 + (size_t)q * hd;
+        const size_t row = kv.row(sq, g, q);
         float s = 0.0f;
         for (int i = 0; i < hd; ++i) s = s + qs[i] * kv_at<KVBF16>(kc, row + i);
         s = s / sqrt_hd;
@@ -431,7 +425,7 @@ __global__ void attention_rows(const float *qkv, int n, const int *pos, const in
     for (int i = threadIdx.x; i < hd; i += blockDim.x) {
         float acc = 0.0f;
 #pragma unroll 4
-        for (int q = 0; q <= p; ++q) acc = acc + (sc[q] / se) * kv_at<KVBF16>(vc, kv0 + (size_t)q * hd + i);
+        for (int q = 0; q <= p; ++q) acc = acc + (sc[q] / se) * kv_at<KVBF16>(vc, kv.row(sq, g, q) + i);
         ctx[(size_t)t * h + (size_t)hh * hd + i] = acc;
         if (P.p) store_planes(P, (size_t)t * h + (size_t)hh * hd + i, acc);
         flag_bad(err, acc);
@@ -471,9 +465,8 @@ __device__ __forceinline__ void kv_load8(const uint8_t *base, size_t idx, float 
 
 template <int KVBF16, int HD>
 __global__ void __launch_bounds__(AT_THREADS)
-    attn_gqa(const float *qkv, const int *pos, const int *seqs, int l, int h, int kvh, int G, int cap,
-             const uint8_t *kv, size_t seq_bytes, size_t layer_bytes, float sqrt_hd, int span, float *ctx, Planes P,
-             float *apart, unsigned *err) {
+    attn_gqa(const float *qkv, const int *pos, const int *seqs, int l, int h, int kvh, int G, KvPages kv,
+             float sqrt_hd, int span, float *ctx, Planes P, float *apart, unsigned *err) {
     pdl_trigger();
     pdl_wait();
     constexpr int DPL = HD / 32;  // context dimensions per lane
@@ -483,8 +476,8 @@ __global__ void __launch_bounds__(AT_THREADS)
     const int lo = z * span, cnt = max(0, min(pos[t] + 1, lo + span) - lo);
     const int rq = h + 2 * kvh * HD;
     float *qs = asm_, *sc = qs + G * HD, *wsum = sc + (size_t)G * span, *red = wsum + AT_WARPS * G * HD;
-    const uint8_t *kc = kv + (size_t)seqs[t] * seq_bytes + (size_t)(2 * l) * layer_bytes, *vc = kc + layer_bytes;
-    const size_t kv0 = ((size_t)g * cap + lo) * HD;
+    const uint8_t *kc = kv.k(l), *vc = kv.v(l);
+    const int sq = seqs[t];
     for (int i = tid; i < G * HD; i += AT_THREADS) qs[i] = qkv[(size_t)t * rq + (size_t)g * G * HD + i];
     __syncthreads();
     // Scores: lane per position.
@@ -492,10 +485,11 @@ __global__ void __launch_bounds__(AT_THREADS)
         float s[AT_GMAX];
 #pragma unroll
         for (int gi = 0; gi < AT_GMAX; ++gi) s[gi] = 0.0f;
+        const size_t krow = kv.row(sq, g, lo + q);
 #pragma unroll 2
         for (int i0 = 0; i0 < HD; i0 += 8) {
             float k8[8];
-            kv_load8<KVBF16>(kc, kv0 + (size_t)q * HD + i0, k8);
+            kv_load8<KVBF16>(kc, krow + i0, k8);
 #pragma unroll
             for (int gi = 0; gi < AT_GMAX; ++gi) {
                 if (gi < G) {
@@ -544,7 +538,7 @@ __global__ void __launch_bounds__(AT_THREADS)
 #pragma unroll 4
     for (int q = q0; q < q1; ++q) {
         float v[DPL];
-        const size_t at = kv0 + (size_t)q * HD + lane * DPL;
+        const size_t at = kv.row(sq, g, lo + q) + lane * DPL;
 #pragma unroll
         for (int d = 0; d < DPL; ++d) v[d] = kv_at<KVBF16>(vc, at + d);
 #pragma unroll
@@ -756,8 +750,7 @@ cudaError_t layer_gemm_tc(int which, const PrefillArgs &a, int l, int n, cudaStr
         j = TcJob{EPI_QKV, n, rq, a.h, &M.qkv, &a.tc->xn, GemmW{nullptr, 0, 0, 0, Ly.sqkv, Ly.bqkv},
                   nullptr, 0, a.qkv, rq, none};
         if (rope_fused(a)) {
-            rk = RopeKv{a.pos, a.seq, a.rope, a.kv, a.kv_seq_bytes, a.kv_layer_bytes, l, a.h, a.kvh, a.hd, a.cap,
-                        a.kv_bf16};
+            rk = RopeKv{a.pos, a.seq, a.rope, a.kv, l, a.h, a.kvh, a.hd, a.kv_bf16};
             j.rk = &rk;
         }
         break;
@@ -825,8 +818,7 @@ cudaError_t attention(const PrefillArgs &a, int n, int l, int max_pos, cudaStrea
                 configured[dev].fetch_or(1u << which);
             }
             cudaError_t e = launch_pdl(kern, dim3(n, a.kvh, nz), dim3(AT_THREADS), sm, st, a.qkv, a.pos, a.seq, l, a.h,
-                                       a.kvh, a.group, a.cap, a.kv, a.kv_seq_bytes, a.kv_layer_bytes, a.sqrt_hd, span,
-                                       a.ctx, ctx_planes(a), a.apart, a.err);
+                                       a.kvh, a.group, a.kv, a.sqrt_hd, span, a.ctx, ctx_planes(a), a.apart, a.err);
             if (e != cudaSuccess) return e;
             if (nz > 1)
                 return launch_pdl(attn_combine, dim3(n, a.kvh), dim3(128), 0, st, a.apart, nz, a.h, a.kvh, a.hd,
@@ -837,11 +829,9 @@ cudaError_t attention(const PrefillArgs &a, int n, int l, int max_pos, cudaStrea
     const size_t sm = attention_smem(a, max_pos);
     if (a.kv_bf16)
         return launch_pdl(attention_rows<1>, dim3(n * a.qh), dim3(128), sm, st, a.qkv, n, a.pos, a.seq, l, max_pos,
-                          a.h, a.qh, a.kvh, a.hd, a.group, a.cap, a.kv, a.kv_seq_bytes, a.kv_layer_bytes, a.sqrt_hd,
-                          a.ctx, ctx_planes(a), a.err);
+                          a.h, a.qh, a.kvh, a.hd, a.group, a.kv, a.sqrt_hd, a.ctx, ctx_planes(a), a.err);
     return launch_pdl(attention_rows<0>, dim3(n * a.qh), dim3(128), sm, st, a.qkv, n, a.pos, a.seq, l, max_pos, a.h,
-                      a.qh, a.kvh, a.hd, a.group, a.cap, a.kv, a.kv_seq_bytes, a.kv_layer_bytes, a.sqrt_hd, a.ctx,
-                      ctx_planes(a), a.err);
+                      a.qh, a.kvh, a.hd, a.group, a.kv, a.sqrt_hd, a.ctx, ctx_planes(a), a.err);
 }
 
 }  // namespace
@@ -864,7 +854,7 @@ cudaError_t forward_tokens(const PrefillArgs &a, int n, int max_pos, bool lm_hea
         if ((e = run_gemm(0, a, l, n, st)) != cudaSuccess) break;
         if (!rope_fused(a) &&
             (e = launch_pdl(rope_kv, dim3(rows_grid), dim3(128), 0, st, a.qkv, n, a.pos, a.seq, l, a.h, a.qh, a.kvh,
-                            a.hd, a.rope, a.cap, a.kv, a.kv_seq_bytes, a.kv_layer_bytes, a.kv_bf16, a.err)) !=
+                            a.hd, a.rope, a.kv, a.kv_bf16, a.err)) !=
                 cudaSuccess)
             break;
         if ((e = attention(a, n, l, max_pos, st)) != cudaSuccess) break;

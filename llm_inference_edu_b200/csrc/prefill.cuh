@@ -12,11 +12,28 @@ namespace qb {
 
 struct TcMaps;
 
+// The paged KV cache of one or more sequences: per layer l a K pool at
+// pool + 2 l layer_bytes and a V pool right after it, each a pool of pages
+// [kv_heads][16][head_dim]; sequence s's page j is pool page ptab[s pps + j].
+struct KvPages {
+    uint8_t *pool;
+    size_t layer_bytes;
+    const int *ptab;
+    int pps;  // pages per sequence (table row length)
+    int kvh, hd;
+    // Element offset of the row of (sequence s, KV head g, position p) in a pool.
+    __device__ __forceinline__ size_t row(int s, int g, int p) const {
+        const int page = ptab[(size_t)s * pps + p / kPageTokens];
+        return (((size_t)page * kvh + g) * kPageTokens + (p % kPageTokens)) * (size_t)hd;
+    }
+    __device__ __forceinline__ uint8_t *k(int l) const { return pool + (size_t)(2 * l) * layer_bytes; }
+    __device__ __forceinline__ uint8_t *v(int l) const { return pool + (size_t)(2 * l + 1) * layer_bytes; }
+};
+
 // Everything the multi-token kernels read or write (device pointers unless
 // noted).  The layer table is a host copy of a DecodeLayer array whose
 // weights are in the decode layout; its KV pointers are ignored: the cache
-// of sequence s, layer l is K at kv + s * kv_seq_bytes + 2 l kv_layer_bytes
-// and V right after it, each [kv_heads][cap][head_dim].
+// is `kv`.
 struct PrefillArgs {
     int V, L, h, qh, kvh, hd, ff, cap, group;
     int wfmt, tfmt, kv_bf16;
@@ -27,8 +44,7 @@ struct PrefillArgs {
     const float *final_norm;      // [h]
     const DecodeLayer *layers;    // HOST array [L]
     const float2 *rope;           // [cap][hd/2] (cos, sin)
-    uint8_t *kv;                  // cache base
-    size_t kv_layer_bytes, kv_seq_bytes;
+    KvPages kv;                   // the paged cache
     int chunk;                    // workspace rows (tokens per launch sequence)
     // Workspace, `chunk` rows each.
     float *x;                     // [chunk][h] residual stream

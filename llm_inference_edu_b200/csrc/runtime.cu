@@ -277,8 +277,9 @@ struct Session {
     bool valid = true;
     int kv_bf16 = 0;
     size_t logical_bytes = 0, workspace_bytes = 0;
+    size_t kv_layer_bytes = 0;  // bytes of one layer's K (or V) page pool
     cudaStream_t stream = nullptr;
-    DevBuf kv, rope, xch, logits, amax_v, amax_i, emitted, ctrl, dlayers, geom, apart, hbar;
+    DevBuf kv, ptab, rope, xch, logits, amax_v, amax_i, emitted, ctrl, dlayers, geom, apart, hbar;
     DecodeCtrl *hctrl = nullptr;  // pinned mirror
     std::vector<DecodeLayer> hlayers;  // host copy of the layer table (chunked prompt path)
     DevBuf pf;                         // chunked prompt workspace (allocated on first use)
@@ -344,8 +345,8 @@ static void prefill_common(const Model &m, size_t cap, int kv_bf16, PrefillArgs 
     a.emb = m.emb.as<uint8_t>();
     a.head = m.head_set ? m.head.as<uint8_t>() : m.emb.as<uint8_t>();
     a.final_norm = m.final_norm.as<float>();
-    a.kv_layer_bytes = round16(c.kv_heads * cap * c.head_dim * (kv_bf16 ? 2 : 4));
-    a.kv_seq_bytes = 2 * c.layers * a.kv_layer_bytes;
+    a.kv.kvh = (int)c.kv_heads;
+    a.kv.hd = (int)c.head_dim;
 }
 
 // Carves the multi-token workspace for `chunk` rows out of one buffer
@@ -414,15 +415,33 @@ static void tc_prepare(const Model &m, PrefillArgs &a, TcMaps &maps) {
     a.tc = &maps;
 }
 
+// KV-cache pages of a cache of `cap` positions per sequence: 16 positions
+// each, ceil(cap / 16) per sequence.
+static size_t pages_per_seq(size_t cap) { return (cap + kPageTokens - 1) / kPageTokens; }
+
 static uint32_t session_build(Session &s) {
     Model &m = *s.m;
     const qb_model_config &c = m.c;
     const size_t L = c.layers, kvh = c.kv_heads, hd = c.head_dim, cap = s.capacity;
     const size_t esz = s.kv_bf16 ? 2 : 4;
-    const size_t per = kvh * cap * hd * esz;
+    // The KV cache is a pool of 16-position pages per layer (K and V pools),
+    // each page [kv_heads][16][head_dim]; the session's page table maps its
+    // page j (positions 16 j .. 16 j + 15) to a pool page.  The pool is
+    // allocated whole at creation (the reference's capacity is fixed too)
+    // and the table hands the pages out last to first, so every access goes
+    // through the table.
+    const size_t npages = pages_per_seq(cap);
+    const size_t per = npages * kvh * kPageTokens * hd * esz;
     uint32_t st;
     QB_CUDA(cudaStreamCreateWithFlags(&s.stream, cudaStreamNonBlocking));
-    if ((st = s.kv.alloc(round16(per) * 2 * L))) return st;
+    s.kv_layer_bytes = round16(per);
+    if ((st = s.kv.alloc(s.kv_layer_bytes * 2 * L))) return st;
+    {
+        std::vector<int> tab(npages);
+        for (size_t j = 0; j < npages; ++j) tab[j] = (int)(npages - 1 - j);
+        if ((st = s.ptab.alloc(npages * 4, false))) return st;
+        QB_CUDA(cudaMemcpy(s.ptab.p, tab.data(), npages * 4, cudaMemcpyHostToDevice));
+    }
     if ((st = build_rope(c, cap, s.rope))) return st;
     const size_t rqkv = c.hidden_dim + 2 * kvh * hd;
     int dev_sms = 0;
@@ -467,6 +486,7 @@ static uint32_t session_build(Session &s) {
     p.sh = m.sh; p.shd = m.shd; p.sff = m.sff; p.semb = m.semb;
     p.ch = (int)(m.sh / 16); p.chd = (int)(m.shd / 16); p.cff = (int)(m.sff / 16); p.cemb = (int)(m.semb / 16);
     p.rqkv = (int)rqkv;
+    p.ptab = s.ptab.as<int>();
     const int s_o = std::max(1, std::min(kMaxSplits, s.grid / std::max(1, p.qh)));  // CTAs per query head
     p.emb = m.emb.as<uint8_t>();
     p.head = m.head_set ? m.head.as<uint8_t>() : m.emb.as<uint8_t>();
@@ -538,15 +558,17 @@ static uint32_t session_build(Session &s) {
     const int q = r4(3 * p.hd);
     const int red = r4(std::max(64, 2 * 16 + 16 * p.hd));  // softmax partials, then [warp][hd] context partials
     const int lay = r4((long long)(L * sizeof(DecodeLayer) / 4));
+    const int ptb = r4((long long)pages_per_seq(cap + 1));  // staged page table (one int per page)
     p.sm_xs = 0; p.sm_h2 = xs; p.sm_gain = p.sm_h2 + h4; p.sm_rv = p.sm_gain + h4;
     p.sm_sc = p.sm_rv + rv; p.sm_q = p.sm_sc + sc; p.sm_red = p.sm_q + q; p.sm_lay = p.sm_red + red;
+    p.sm_ptab = p.sm_lay + lay;
     // Weight ring: slots of at least 16 KB holding whole rows (and whole
     // gate/up pairs), as many as fit the remaining shared memory (at most
     // 16), 128-byte aligned; the full/empty mbarriers (2 per slot, 8 bytes
     // each) precede it.
     size_t max_row = std::max({2 * m.sh, m.shd, m.sff, m.semb});
     p.slot_bytes = (int)std::max<size_t>(16384, (max_row + 127) & ~(size_t)127);
-    p.sm_bar = (p.sm_lay + lay + 3) & ~3;
+    p.sm_bar = (p.sm_ptab + ptb + 3) & ~3;
     p.sm_ring = (p.sm_bar + 2 * 2 * 16 + 31) & ~31;
     const size_t budget = 227 * 1024 - 1024;  // CTA limit less the static shared memory
     const size_t used = (size_t)p.sm_ring * 4;
@@ -702,7 +724,7 @@ static bool cancelled(const volatile int32_t *c) { return c && *c != 0; }
 // Chunked evaluation of a run of prompt tokens (all but the last of an
 // append); fills the cache and advances `processed`.  Shapes the chunked
 // kernels do not cover return QB_UNSUPPORTED without touching the session.
-static constexpr int kPrefillChunk = 256;
+static constexpr int kPrefillChunk = 512;
 
 static uint32_t session_prefill_chunked(Session &s, const uint32_t *tokens, size_t n) {
     const Model &m = *s.m;
@@ -710,7 +732,10 @@ static uint32_t session_prefill_chunked(Session &s, const uint32_t *tokens, size
     prefill_common(m, s.capacity, s.kv_bf16, a);
     a.layers = s.hlayers.data();
     a.rope = s.rope.as<float2>();
-    a.kv = s.kv.as<uint8_t>();
+    a.kv.pool = s.kv.as<uint8_t>();
+    a.kv.layer_bytes = s.kv_layer_bytes;
+    a.kv.ptab = s.ptab.as<int>();
+    a.kv.pps = (int)pages_per_seq(s.capacity);
     a.chunk = kPrefillChunk;
     if (!prefill_supported(a)) return QB_UNSUPPORTED;
     uint32_t st = prefill_workspace(m, kPrefillChunk, s.pf, a);
@@ -778,7 +803,7 @@ struct Batch {
     bool valid = true;
     int kv_bf16 = 0;
     cudaStream_t stream = nullptr;
-    DevBuf kv, rope, ws, logits, amax, hist;
+    DevBuf kv, ptab, rope, ws, logits, amax, hist;
     std::vector<DecodeLayer> hlayers;
     TcMaps tcm;
     PrefillArgs a{};
@@ -1497,10 +1522,23 @@ uint32_t qb_batch_create(uint64_t model, size_t sequences, size_t capacity, uint
     const int chunk = (int)std::max<size_t>(sequences, 256);
     a.chunk = chunk;
     if (!prefill_supported(a) || sequences > (1u << 20)) return QB_UNSUPPORTED;
-    size_t kvb;
-    if (mul_ovf(a.kv_seq_bytes, sequences, &kvb)) return QB_DIMENSION_OVERFLOW;
+    // One page pool per layer for all sequences; the table interleaves the
+    // sequences' pages (sequence s's page j is pool page j B + s).
+    const size_t pps = pages_per_seq(capacity), npages = pps * sequences;
+    const size_t kv_esz = b->kv_bf16 ? 2 : 4;
+    size_t layer_bytes, kvb;
+    if (mul_ovf(npages, m->c.kv_heads * kPageTokens * m->c.head_dim * kv_esz, &layer_bytes) ||
+        mul_ovf(round16(layer_bytes), 2 * m->c.layers, &kvb) || npages > 0x7fffffffu)
+        return QB_DIMENSION_OVERFLOW;
     uint32_t st;
     QB_CUDA(cudaStreamCreateWithFlags(&b->stream, cudaStreamNonBlocking));
+    {
+        std::vector<int> tab(npages);
+        for (size_t sq = 0; sq < sequences; ++sq)
+            for (size_t j = 0; j < pps; ++j) tab[sq * pps + j] = (int)(j * sequences + sq);
+        if ((st = b->ptab.alloc(npages * 4, false))) return st == QB_CUDA_ERROR ? QB_ALLOCATION : st;
+        QB_CUDA(cudaMemcpy(b->ptab.p, tab.data(), npages * 4, cudaMemcpyHostToDevice));
+    }
     if ((st = b->kv.alloc(kvb)) || (st = build_rope(m->c, capacity, b->rope)) ||
         (st = prefill_workspace(*m, chunk, b->ws, a)) ||
         (st = b->logits.alloc(sequences * m->c.vocab_size * 4, false)) || (st = b->amax.alloc(sequences * 4)))
@@ -1510,7 +1548,10 @@ uint32_t qb_batch_create(uint64_t model, size_t sequences, size_t capacity, uint
     a.layers = b->hlayers.data();
     tc_prepare(*m, a, b->tcm);
     a.rope = b->rope.as<float2>();
-    a.kv = b->kv.as<uint8_t>();
+    a.kv.pool = b->kv.as<uint8_t>();
+    a.kv.layer_bytes = round16(layer_bytes);
+    a.kv.ptab = b->ptab.as<int>();
+    a.kv.pps = (int)pps;
     a.logits = b->logits.as<float>();
     a.amax = b->amax.as<uint32_t>();
     std::lock_guard<std::mutex> lk(g_mu);

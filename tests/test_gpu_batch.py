@@ -146,23 +146,38 @@ def test_qwen05b_batch64_matches_sessions():
     assert mismatched == 0, mismatched
 
 
-def test_qwen7b_decode_kernel_matches_multitoken_path():
-    # The 7B shape (hd 128, 4 KV heads, untied head) on one GPU: a 64-token
-    # prompt, then 16 greedy ids from the persistent decode kernel and from
-    # the tensor-core multi-token path must agree (two independent
-    # implementations of the same arithmetic); the last logits agree within
-    # the BF16-KV tolerance.
+def test_qwen7b_decode_kernel_matches_multitoken_path(oracle):
+    # The 7B shape (hd 128, 4 KV heads, untied head, INT8 per-row linears,
+    # BF16 tables and KV) on one GPU: a 64-token prompt, then 16 greedy ids.
+    # Against the oracle (INT8 values and row scales held in host memory,
+    # the crate's x * (f32(q) * s) order): the prompt's last logits within
+    # the BF16-KV tolerance and the 16 ids identical.  The persistent decode
+    # kernel and the tensor-core multi-token path must also agree with each
+    # other.
     import llm_inference_edu_b200 as qb
     P, steps = 64, 16
     cap = P + steps + 8
     cfg = presets.qwen_7b(cap)
     w = synthetic.weights(cfg, seed=2, dtype="bf16", lazy=True)
     m = qb.Decoder(cfg, w, linear_format="int8", table_format="bf16")
+    # The oracle quantizes each lazily drawn layer itself and keeps only the
+    # INT8 values and scales (~6.5 GB) plus the two BF16 tables.
+    om = oracle.Model(cfg, oracle.int8_model_weights(cfg, w, "int8"))
     del w
     prompt = synthetic.prompt(cfg.vocab_size, P, seed=3)
     s = qb.CachedSession(m, cap, kv_dtype="bf16", budget=0)
-    first = int(np.argmax(s.prefill(prompt)))
+    got = s.prefill(prompt)
+    first = int(np.argmax(got))
+    os_ = oracle.Session(om, cap, kv_bf16=True, budget=0)
+    _, exp = os_.prefill(prompt)
+    assert max_abs(got, exp) <= 2e-2, max_abs(got, exp)
+    assert int(np.argmax(exp)) == first
+    or_ids = [first]
+    for _ in range(steps - 1):
+        _, lg = os_.step(or_ids[-1])
+        or_ids.append(int(np.argmax(lg)))
     dev = [first] + s.decode_greedy(first, steps - 1)
+    assert dev == or_ids
     b = qb.BatchSession(m, 1, cap, kv_dtype="bf16")
     f = b.prefill(np.asarray(prompt, np.uint32)[None, :])
     g = b.decode_greedy(f, steps - 1)

@@ -338,8 +338,9 @@ def test_qwen05b_int8_bf16_kv_parity(oracle):
 
 
 def test_qwen05b_bf16_parity(oracle):
-    # BASELINE config 2 shape: BF16 linears, FP32 accumulation and KV.
-    worst, dev_ids, or_ids = _qwen_pair(oracle, "bf16", "f32", prompt_len=64, greedy=64)
+    # The BF16-linear configuration as benchmarked: BF16 linears, FP32
+    # accumulation and KV, the 128-token prompt, then 64 greedy ids.
+    worst, dev_ids, or_ids = _qwen_pair(oracle, "bf16", "f32", prompt_len=128, greedy=64)
     assert worst <= 1e-3, worst
     assert dev_ids == or_ids
 
@@ -417,3 +418,37 @@ def test_qwen05b_long_context_split_attention(oracle, kv, tol):
         assert int(np.argmax(g)) == int(np.argmax(e))
         tok = int(np.argmax(e))
     assert worst <= tol, worst
+
+
+def test_qwen05b_8192_token_context(oracle):
+    # The long-context configuration at its full size: an 8,192-token prompt
+    # through prefill_into (512-token chunks of the multi-token path, then
+    # one decode step), then 8 greedy decode steps through the decode
+    # kernel's position-split attention, against the oracle's serial
+    # evaluation of all 8,200 positions (BF16 KV: max-abs 2e-2, ids
+    # identical).
+    import llm_inference_edu_b200 as qb
+    from helpers import qwen_host_weights
+    n, steps = 8192, 8
+    cap = n + steps + 8
+    cfg = presets.qwen_0_5b(cap)
+    w = qwen_host_weights("0.5b", 1, "bf16")
+    m = qb.Decoder(cfg, w, linear_format="int8", table_format="bf16")
+    om = oracle.Model(cfg, oracle_weights(oracle, cfg, w, "int8"))
+    prompt = synthetic.prompt(cfg.vocab_size, n, seed=2000)
+    s = qb.CachedSession(m, cap, kv_dtype="bf16", budget=0)
+    os_ = oracle.Session(om, cap, kv_bf16=True, budget=0)
+    got = s.prefill(prompt)
+    _, exp = os_.prefill(prompt)
+    worst = max_abs(got, exp)
+    tok = int(np.argmax(exp))
+    assert int(np.argmax(got)) == tok
+    dev_ids, or_ids = [tok], [tok]
+    for _ in range(steps):
+        g = s.step(dev_ids[-1])
+        _, e = os_.step(or_ids[-1])
+        worst = max(worst, max_abs(g, e))
+        dev_ids.append(int(np.argmax(g)))
+        or_ids.append(int(np.argmax(e)))
+    assert dev_ids == or_ids
+    assert worst <= 2e-2, worst
