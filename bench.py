@@ -283,8 +283,11 @@ def run_native(args, topo):
     ref_rate = ref_decode_rate(times)
 
     batched = run_batched(args, topo, model, cfg, kv)
+    batched_split = run_batched(args, topo, model, cfg, kv, per_gpu=max(1, BATCH // topo.world))
     del model
     long_ctx = run_long_context(args, topo, kv) if lf == "int8" else None
+    bf16 = run_decode_config(args, topo, "bf16") if lf == "int8" else None
+    qwen7b = run_qwen7b(args, topo) if lf == "int8" else None
 
     if rank != 0:
         return 0
@@ -314,7 +317,10 @@ def run_native(args, topo):
         "gpu_launches": args.steps,
         "clocks": clocks.summary(),
         "batched": batched,
+        "batched_split": batched_split,
         "long_context": long_ctx,
+        "bf16": bf16,
+        "qwen7b": qwen7b,
     }
     if world == 1:
         line["cpu_baseline"] = cpu_baseline(args)
@@ -325,12 +331,13 @@ def run_native(args, topo):
 BATCH = 64
 
 
-def run_batched(args, topo, model, cfg, kv):
-    """Batched greedy decode (BatchSession): BATCH independent sequences per
-    GPU with their own 128-token prompts, one multi-token forward per step
-    (tensor-core GEMMs).  Device-timed with CUDA events on the batch's
-    stream; each decode_greedy call copies its tokens host->device and its
-    ids device->host inside the timed region."""
+def run_batched(args, topo, model, cfg, kv, per_gpu=BATCH):
+    """Batched greedy decode (BatchSession): `per_gpu` independent sequences
+    per GPU (BATCH each, weak scaling; or BATCH // N each, the 64-sequence
+    batch split over the N GPUs) with their own 128-token prompts, one
+    multi-token forward per step (tensor-core GEMMs).  Device-timed with
+    CUDA events on the batch's stream; each decode_greedy call copies its
+    tokens host->device and its ids device->host inside the timed region."""
     import numpy as np
     import torch
 
@@ -339,9 +346,10 @@ def run_batched(args, topo, model, cfg, kv):
 
     steps = max(1, args.steps // 4)
     cap = PROMPT + args.warmup + steps + 1
-    prompts = np.stack([synthetic.prompt(cfg.vocab_size, PROMPT, seed=1000 + topo.rank * BATCH + s)
-                        for s in range(BATCH)]).astype(np.uint32)
-    b = qb.BatchSession(model, BATCH, cap, kv_dtype=kv)
+    B = per_gpu
+    prompts = np.stack([synthetic.prompt(cfg.vocab_size, PROMPT, seed=1000 + topo.rank * B + s)
+                        for s in range(B)]).astype(np.uint32)
+    b = qb.BatchSession(model, B, cap, kv_dtype=kv)
     stream = torch.cuda.ExternalStream(b.stream())
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
@@ -359,10 +367,12 @@ def run_batched(args, topo, model, cfg, kv):
     torch.cuda.synchronize()
     ms = dp.max_over_ranks(topo, ev0.elapsed_time(ev1), device="cuda")
     del b
-    return {"sequences_per_gpu": BATCH, "steps": steps, "value": topo.world * BATCH * steps / (ms / 1000.0),
+    return {"sequences_per_gpu": B, "sequences_total": topo.world * B, "steps": steps,
+            "value": topo.world * B * steps / (ms / 1000.0),
             "unit": "tok/s", "ms_per_step": ms / steps,
-            "prefill_tok_per_s": BATCH * PROMPT / (prefill_ms / 1000.0),
-            "h2d_bytes_per_call": BATCH * 4, "d2h_bytes_per_call": BATCH * 4 * steps}
+            "scaling": "weak" if B == BATCH else "strong",
+            "prefill_tok_per_s": topo.world * B * PROMPT / (prefill_ms / 1000.0),
+            "h2d_bytes_per_call": B * 4, "d2h_bytes_per_call": B * 4 * steps}
 
 
 LONG_PROMPT = 8192
@@ -405,6 +415,89 @@ def run_long_context(args, topo, kv):
             "prefill_tok_per_s": topo.world * LONG_PROMPT / (prefill_ms / 1000.0),
             "value": topo.world * (LONG_STEPS - 8) / (ms / 1000.0), "unit": "tok/s",
             "ms_per_token": ms / (LONG_STEPS - 8)}
+
+
+def decode_timed(sess, tok, steps, topo):
+    """K greedy decode steps on the device, timed with CUDA events on the
+    session's stream (max over ranks); returns (ms, first cached position)."""
+    import torch
+
+    from llm_inference_edu_b200 import dp
+    stream = torch.cuda.ExternalStream(sess.stream())
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    L0 = sess.processed()
+    dp.barrier(topo)
+    torch.cuda.synchronize()
+    ev0.record(stream)
+    sess.decode_greedy(tok, steps)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    return dp.max_over_ranks(topo, ev0.elapsed_time(ev1), device="cuda"), L0
+
+
+def run_decode_config(args, topo, lf):
+    """Batch-1 greedy decode of the 0.5B shape with BF16 linears (FP32 KV,
+    the reference's cache type): the 128-token prompt, W warm-up then K
+    device-timed steps, with its roofline (~988 MB of weights per step)."""
+    import llm_inference_edu_b200 as qb
+    from llm_inference_edu_b200 import presets, synthetic
+    cap = PROMPT + 2 * args.warmup + args.steps + 8
+    cfg = presets.qwen_0_5b(cap)
+    w = synthetic.weights(cfg, seed=SEED, dtype="bf16")
+    model = qb.Decoder(cfg, w, linear_format=lf, table_format="bf16", device=topo.local_rank)
+    del w
+    kv = "f32"
+    sess = qb.CachedSession(model, cap, kv_dtype=kv, budget=0)
+    first = sess.prefill_into(synthetic.prompt(cfg.vocab_size, PROMPT, seed=SEED + topo.rank), None)
+    ids = sess.decode_greedy(first, args.warmup)
+    ms, L0 = decode_timed(sess, ids[-1], args.steps, topo)
+    peak, peak_kind = measured_peaks()
+    kv_pos = cfg.layers * 2 * cfg.kv_dim * 4
+    bytes_step = algorithmic_bytes(cfg, lf, kv_pos, L0 + (args.steps - 1) / 2.0)
+    achieved = bytes_step / (ms / 1000.0 / args.steps) / 1e9
+    return {"workload": f"qwen2.5-0.5b-shape {lf} linears batch-1 greedy decode (128-token prompt, f32 KV)",
+            "steps": args.steps, "value": topo.world * args.steps / (ms / 1000.0), "unit": "tok/s",
+            "ms_per_step": ms / args.steps,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "bytes_per_step": bytes_step, "peak_source": peak_kind}}
+
+
+QWEN7B_PROMPT = 512
+
+
+def run_qwen7b(args, topo):
+    """The Qwen2.5-7B shape (INT8 per-row linears, untied BF16 head, BF16 KV)
+    on one GPU per rank: batch-1 greedy decode after a 512-token prompt
+    (device-timed decode kernel steps, roofline ~7.1 GB per step)."""
+    import llm_inference_edu_b200 as qb
+    from llm_inference_edu_b200 import presets, synthetic
+    steps = max(4, args.steps // 2)
+    cap = QWEN7B_PROMPT + args.warmup + steps + 8
+    cfg = presets.qwen_7b(cap)
+    w = synthetic.weights(cfg, seed=2, dtype="bf16", lazy=True)
+    model = qb.Decoder(cfg, w, linear_format="int8", table_format="bf16", device=topo.local_rank)
+    del w
+    sess = qb.CachedSession(model, cap, kv_dtype="bf16", budget=0)
+    import torch
+    stream = torch.cuda.ExternalStream(sess.stream())
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    ev0.record(stream)
+    first = sess.prefill_into(synthetic.prompt(cfg.vocab_size, QWEN7B_PROMPT, seed=3 + topo.rank), None)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    prefill_ms = ev0.elapsed_time(ev1)
+    ids = sess.decode_greedy(first, args.warmup)
+    ms, L0 = decode_timed(sess, ids[-1], steps, topo)
+    peak, peak_kind = measured_peaks()
+    kv_pos = cfg.layers * 2 * cfg.kv_dim * 2
+    bytes_step = algorithmic_bytes(cfg, "int8", kv_pos, L0 + (steps - 1) / 2.0)
+    achieved = bytes_step / (ms / 1000.0 / steps) / 1e9
+    return {"workload": "qwen2.5-7b-shape int8 batch-1 greedy decode (512-token prompt, bf16 KV), tp1 per rank",
+            "steps": steps, "value": topo.world * steps / (ms / 1000.0), "unit": "tok/s",
+            "ms_per_step": ms / steps, "prefill_tok_per_s": QWEN7B_PROMPT / (prefill_ms / 1000.0),
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "bytes_per_step": bytes_step, "peak_source": peak_kind}}
 
 
 def cpu_baseline(args):

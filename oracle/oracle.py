@@ -103,6 +103,8 @@ def lib():
             ("or_session_reset", [P], None),
             ("or_session_step", [P, S, P, S], C.c_int),
             ("or_session_append", [P, P, S, P, S, C.c_int], C.c_int),
+            ("or_session_append_chunked", [P, P, S, P, S, C.c_int, S], C.c_int),
+            ("or_set_fast", [C.c_int], None),
             ("or_argmax", [P, S], S),
             ("or_greedy", [P, P, S, P, S, S, P], C.c_long),
             ("or_uncached_greedy", [P, P, S, P, S, S, P], C.c_long),
@@ -242,6 +244,12 @@ def round_bf16(a):
     u = a.view(np.uint32).astype(np.uint64)
     r = ((u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000).astype(np.uint32)
     return r.view(np.float32)
+
+
+def set_fast(on=True):
+    """Interleaved row evaluation (bit-identical outputs, faster): for the
+    parity tests; the timed CPU baseline keeps it off."""
+    lib().or_set_fast(int(on))
 
 
 def set_threads(n):
@@ -387,6 +395,18 @@ class Session:
 
     def prefill(self, tokens, logits=None):
         return self.append(tokens, True, logits)
+
+    def append_chunked(self, tokens, require_empty=False, logits=None, chunk=64):
+        """append / prefill evaluated layer-major over chunks of `chunk`
+        tokens: the same per-token values, only the last token's logits (the
+        long prompts of the parity tests)."""
+        t = ids_array(tokens)
+        V = self.model.config.vocab_size
+        if logits is None:
+            logits = np.zeros(V, dtype=np.float32)
+        s = lib().or_session_append_chunked(self.h, _p(t), t.size, _p(logits), logits.size,
+                                            int(require_empty), chunk)
+        return s, logits
 
     def reset(self):
         lib().or_session_reset(self.h)

@@ -481,9 +481,153 @@ int or_rope(const float *x, size_t xl, float *y, size_t yl, size_t tokens, size_
 /* weight matrices (src/matrix.rs)                                      */
 /* ------------------------------------------------------------------ */
 
+/* Interleaved evaluation (test speed only): OR_IL output rows are summed
+ * side by side, each in its own accumulator and in increasing index order,
+ * so every output is bit-identical to the one-row-at-a-time dot; the CPU
+ * overlaps the independent chains.  Off by default (the timed CPU baseline
+ * keeps the reference's one-row-at-a-time loop); or_set_fast turns it on. */
+static int g_fast = 0;
+void or_set_fast(int on) { g_fast = on; }
+#define OR_IL 8
+
+static void project_il(const or_matrix *m, const float *x, float *y, size_t t, size_t in, size_t out) {
+    long long nb = (long long)(out / OR_IL);
+#pragma omp parallel for schedule(static) num_threads(or_get_threads()) if (nb * (long long)t * (long long)in > 65536)
+    for (long long b = 0; b < nb; ++b) {
+        size_t o0 = (size_t)b * OR_IL;
+        for (size_t tt = 0; tt < t; ++tt) {
+            const float *xr = x + tt * in;
+            float acc[OR_IL];
+#pragma GCC unroll 8
+            for (int r = 0; r < OR_IL; ++r) acc[r] = 0.0f;
+            if (m->kind == OR_MAT_F32) {
+                const float *w = m->f32 + o0 * in;
+                for (size_t i = 0; i < in; ++i) {
+                    float xi = xr[i];
+#pragma GCC unroll 8
+                    for (int r = 0; r < OR_IL; ++r) acc[r] += xi * w[r * in + i];
+                }
+            } else if (m->kind == OR_MAT_BF16) {
+                const uint16_t *w = m->bf16 + o0 * in;
+                for (size_t i = 0; i < in; ++i) {
+                    float xi = xr[i];
+#pragma GCC unroll 8
+                    for (int r = 0; r < OR_IL; ++r) acc[r] += xi * bf16_to_f32(w[r * in + i]);
+                }
+            } else {
+                size_t group = m->group, gpr = in / group + (in % group != 0);
+                const int8_t *q = m->q + o0 * in;
+                const float *sc = m->scales + o0 * gpr;
+                for (size_t g = 0; g < gpr; ++g) {
+                    float scale[OR_IL];
+                    for (int r = 0; r < OR_IL; ++r) scale[r] = sc[r * gpr + g];
+                    size_t start = g * group, end = start + group < in ? start + group : in;
+                    for (size_t i = start; i < end; ++i) {
+                        float xi = xr[i];
+#pragma GCC unroll 8
+                        for (int r = 0; r < OR_IL; ++r) acc[r] += xi * ((float)q[r * in + i] * scale[r]);
+                    }
+                }
+            }
+            for (int r = 0; r < OR_IL; ++r) y[tt * out + o0 + r] = acc[r];
+        }
+    }
+}
+
+/* Token-vectorised evaluation (test speed only, several tokens): for each
+ * output row, OR_IL tokens are summed side by side from a transposed copy
+ * of their inputs, each token's sum in increasing index order, so every
+ * output is bit-identical to the one-row-at-a-time dot. */
+static void project_tv(const or_matrix *m, const float *x, float *y, size_t t, size_t in, size_t out) {
+    enum { RB = 4, KB = 512 };
+    size_t nb = (t + OR_IL - 1) / OR_IL, nrb = (out + RB - 1) / RB;
+    float *xt = (float *)calloc(nb * in * OR_IL, sizeof(float));
+    for (size_t tt = 0; tt < t; ++tt)
+        for (size_t i = 0; i < in; ++i) xt[((tt / OR_IL) * in + i) * OR_IL + tt % OR_IL] = x[tt * in + i];
+    size_t group = m->kind == OR_MAT_INT8 ? m->group : in, gpr = in / group + (in % group != 0);
+    /* Tiles: RB rows x OR_IL tokens, the reduction in KB-element pieces, so
+     * the inputs and weights of a piece stay in L1; each accumulator still
+     * runs over its row in increasing index order. */
+#pragma omp parallel for schedule(dynamic, 4) num_threads(or_get_threads()) if ((long long)out * (long long)t * (long long)in > 65536)
+    for (long long rbb = 0; rbb < (long long)(nrb * nb); ++rbb) {
+        size_t rb = (size_t)rbb / nb, b = (size_t)rbb % nb;
+        size_t o0 = rb * RB, nr = out - o0 < RB ? out - o0 : RB;
+        const float *xb = xt + b * in * OR_IL;
+        float acc[RB][OR_IL];
+        for (int r = 0; r < RB; ++r)
+            for (int j = 0; j < OR_IL; ++j) acc[r][j] = 0.0f;
+        for (size_t i0 = 0; i0 < in; i0 += KB) {
+            size_t i1 = i0 + KB < in ? i0 + KB : in;
+            for (size_t r = 0; r < nr; ++r) {
+                size_t o = o0 + r;
+                float *a = acc[r];
+                if (m->kind == OR_MAT_F32) {
+                    const float *w = m->f32 + o * in;
+                    for (size_t i = i0; i < i1; ++i) {
+                        float wi = w[i];
+#pragma GCC unroll 8
+                        for (int j = 0; j < OR_IL; ++j) a[j] += xb[i * OR_IL + j] * wi;
+                    }
+                } else if (m->kind == OR_MAT_BF16) {
+                    const uint16_t *w = m->bf16 + o * in;
+                    for (size_t i = i0; i < i1; ++i) {
+                        float wi = bf16_to_f32(w[i]);
+#pragma GCC unroll 8
+                        for (int j = 0; j < OR_IL; ++j) a[j] += xb[i * OR_IL + j] * wi;
+                    }
+                } else {
+                    const int8_t *q = m->q + o * in;
+                    const float *sc = m->scales + o * gpr;
+                    for (size_t i = i0; i < i1;) {
+                        size_t g = i / group, ge = (g + 1) * group < i1 ? (g + 1) * group : i1;
+                        float scale = sc[g];
+                        for (; i < ge; ++i) {
+                            float wi = (float)q[i] * scale;
+#pragma GCC unroll 8
+                            for (int j = 0; j < OR_IL; ++j) a[j] += xb[i * OR_IL + j] * wi;
+                        }
+                    }
+                }
+            }
+        }
+        for (size_t r = 0; r < nr; ++r)
+            for (int j = 0; j < OR_IL; ++j)
+                if (b * OR_IL + j < t) y[(b * OR_IL + j) * out + o0 + r] = acc[r][j];
+    }
+    free(xt);
+}
+
 /* MatrixRef::project, src/matrix.rs:153-187, extended with a BF16 kind. */
 static void project(const or_matrix *m, const float *x, float *y, size_t t, size_t in,
                     size_t out, int lanes) {
+    if (g_fast && !lanes && t >= 4) {
+        project_tv(m, x, y, t, in, out);
+        return;
+    }
+    if (g_fast && !lanes && out >= OR_IL) {
+        /* whole blocks interleaved, the tail rows below one at a time */
+        project_il(m, x, y, t, in, out);
+        size_t done = out / OR_IL * OR_IL;
+        if (done == out) return;
+        for (size_t tt = 0; tt < t; ++tt) {
+            const float *xr = x + tt * in;
+            for (size_t o = done; o < out; ++o) {
+                float r;
+                if (m->kind == OR_MAT_F32) {
+                    r = dot_scalar(xr, m->f32 + o * in, in);
+                } else if (m->kind == OR_MAT_BF16) {
+                    const uint16_t *w = m->bf16 + o * in;
+                    r = 0.0f;
+                    for (size_t i = 0; i < in; ++i) r += xr[i] * bf16_to_f32(w[i]);
+                } else {
+                    size_t gpr = in / m->group + (in % m->group != 0);
+                    r = dot_int8(xr, m->q + o * in, m->scales + o * gpr, in, m->group);
+                }
+                y[tt * out + o] = r;
+            }
+        }
+        return;
+    }
     long long n = (long long)(t * out);
 #pragma omp parallel for schedule(static) num_threads(or_get_threads()) if (n * (long long)in > 65536)
     for (long long k = 0; k < n; ++k) {
@@ -779,53 +923,96 @@ size_t or_session_workspace_bytes(const or_session *s) { return s->workspace_byt
 /* CachedSession::reset, src/kv_cache.rs:225-229. */
 void or_session_reset(or_session *s) { s->processed = 0; s->valid = 1; }
 
+/* The per-token body of attend_one after the q/k/v projections
+ * (src/kv_cache.rs:505-576): biases, RoPE at `pos`, the cache write at
+ * `pos`, then scores, softmax and context over positions 0..pos.  q, k, v
+ * hold this token's projections (biases added in place); qr, kr are
+ * scratch; the context lands in ctx [h]. */
+static int attend_core(or_session *s, size_t li, size_t pos, float *q, float *k, float *v, float *qr,
+                       float *kr, float *ctx) {
+    const or_model *m = s->m;
+    const or_config *c = &m->c;
+    const or_layer *l = &m->layers[li];
+    size_t h = c->hidden, d = c->head_dim, kv = c->kv_heads * d, cap = s->capacity;
+    if (l->qb) for (size_t i = 0; i < h; ++i) q[i] += l->qb[i];
+    if (!finite_all(q, h)) return OR_NONFINITE;
+    if (l->kb) for (size_t i = 0; i < kv; ++i) k[i] += l->kb[i];
+    if (!finite_all(k, kv)) return OR_NONFINITE;
+    if (l->vb) for (size_t i = 0; i < kv; ++i) v[i] += l->vb[i];
+    if (!finite_all(v, kv)) return OR_NONFINITE;
+    int st;
+    if ((st = or_rope(q, h, qr, h, 1, c->query_heads, d, pos, c->rope_base, NULL))) return st;
+    if ((st = or_rope(k, kv, kr, kv, 1, c->kv_heads, d, pos, c->rope_base, NULL))) return st;
+    if (!finite_all(qr, h) || !finite_all(kr, kv)) return OR_NONFINITE;
+    float *K = s->key + li * c->kv_heads * cap * d, *Vc = s->value + li * c->kv_heads * cap * d;
+    for (size_t hh = 0; hh < c->kv_heads; ++hh) {
+        size_t off = (hh * cap + pos) * d;
+        for (size_t i = 0; i < d; ++i) {
+            float kk = kr[hh * d + i], vv = v[hh * d + i];
+            K[off + i] = s->kv_bf16 ? or_round_bf16(kk) : kk;
+            Vc[off + i] = s->kv_bf16 ? or_round_bf16(vv) : vv;
+        }
+    }
+    memset(ctx, 0, h * 4);
+    size_t group = c->query_heads / c->kv_heads;
+    float scale = sqrtf((float)d);
+    if (g_fast && pos >= 256) {
+        /* heads in parallel (each head's sums unchanged), own score buffers */
+        int bad = 0;
+        float *buf = (float *)malloc(2 * (pos + 1) * c->query_heads * sizeof(float));
+#pragma omp parallel for schedule(static) num_threads(or_get_threads())
+        for (long long qi = 0; qi < (long long)c->query_heads; ++qi) {
+            size_t qh = (size_t)qi, kvh = qh / group;
+            float *sc = buf + 2 * (pos + 1) * qh, *pr = sc + (pos + 1);
+            for (size_t p = 0; p <= pos; ++p) {
+                size_t off = (kvh * cap + p) * d;
+                float sum = 0.0f;
+                for (size_t i = 0; i < d; ++i) sum += qr[qh * d + i] * K[off + i];
+                sc[p] = sum / scale;
+            }
+            if (or_softmax(sc, pos + 1, NULL, 0, pr, pos + 1, 1, pos + 1, NULL)) {
+#pragma omp atomic write
+                bad = 1;
+                continue;
+            }
+            for (size_t p = 0; p <= pos; ++p) {
+                size_t off = (kvh * cap + p) * d;
+                for (size_t i = 0; i < d; ++i) ctx[qh * d + i] += pr[p] * Vc[off + i];
+            }
+        }
+        free(buf);
+        if (bad) return OR_NONFINITE;
+    } else {
+        for (size_t qh = 0; qh < c->query_heads; ++qh) {
+            size_t kvh = qh / group;
+            for (size_t p = 0; p <= pos; ++p) {
+                size_t off = (kvh * cap + p) * d;
+                float sum = 0.0f;
+                for (size_t i = 0; i < d; ++i) sum += qr[qh * d + i] * K[off + i];
+                s->scores[p] = sum / scale;
+            }
+            if ((st = or_softmax(s->scores, pos + 1, NULL, 0, s->probs, pos + 1, 1, pos + 1, NULL))) return st;
+            for (size_t p = 0; p <= pos; ++p) {
+                size_t off = (kvh * cap + p) * d;
+                for (size_t i = 0; i < d; ++i) ctx[qh * d + i] += s->probs[p] * Vc[off + i];
+            }
+        }
+    }
+    if (!finite_all(ctx, h)) return OR_NONFINITE;
+    return OR_OK;
+}
+
 /* attend_one, src/kv_cache.rs:479-590. */
 static int attend_one(or_session *s, size_t li, const float *x) {
     const or_model *m = s->m;
     const or_config *c = &m->c;
     const or_layer *l = &m->layers[li];
-    size_t h = c->hidden, d = c->head_dim, kv = c->kv_heads * d, cap = s->capacity;
-    size_t pos = s->processed;
+    size_t h = c->hidden, kv = c->kv_heads * c->head_dim;
     project(&l->q, x, s->q, 1, h, h, 0);
     project(&l->k, x, s->k, 1, h, kv, 0);
     project(&l->v, x, s->v, 1, h, kv, 0);
-    if (l->qb) for (size_t i = 0; i < h; ++i) s->q[i] += l->qb[i];
-    if (!finite_all(s->q, h)) return OR_NONFINITE;
-    if (l->kb) for (size_t i = 0; i < kv; ++i) s->k[i] += l->kb[i];
-    if (!finite_all(s->k, kv)) return OR_NONFINITE;
-    if (l->vb) for (size_t i = 0; i < kv; ++i) s->v[i] += l->vb[i];
-    if (!finite_all(s->v, kv)) return OR_NONFINITE;
-    int st;
-    if ((st = or_rope(s->q, h, s->qr, h, 1, c->query_heads, d, pos, c->rope_base, NULL))) return st;
-    if ((st = or_rope(s->k, kv, s->kr, kv, 1, c->kv_heads, d, pos, c->rope_base, NULL))) return st;
-    if (!finite_all(s->qr, h) || !finite_all(s->kr, kv)) return OR_NONFINITE;
-    float *K = s->key + li * c->kv_heads * cap * d, *Vc = s->value + li * c->kv_heads * cap * d;
-    for (size_t hh = 0; hh < c->kv_heads; ++hh) {
-        size_t off = (hh * cap + pos) * d;
-        for (size_t i = 0; i < d; ++i) {
-            float kk = s->kr[hh * d + i], vv = s->v[hh * d + i];
-            K[off + i] = s->kv_bf16 ? or_round_bf16(kk) : kk;
-            Vc[off + i] = s->kv_bf16 ? or_round_bf16(vv) : vv;
-        }
-    }
-    memset(s->ctx, 0, h * 4);
-    size_t group = c->query_heads / c->kv_heads;
-    float scale = sqrtf((float)d);
-    for (size_t qh = 0; qh < c->query_heads; ++qh) {
-        size_t kvh = qh / group;
-        for (size_t p = 0; p <= pos; ++p) {
-            size_t off = (kvh * cap + p) * d;
-            float sum = 0.0f;
-            for (size_t i = 0; i < d; ++i) sum += s->qr[qh * d + i] * K[off + i];
-            s->scores[p] = sum / scale;
-        }
-        if ((st = or_softmax(s->scores, pos + 1, NULL, 0, s->probs, pos + 1, 1, pos + 1, NULL))) return st;
-        for (size_t p = 0; p <= pos; ++p) {
-            size_t off = (kvh * cap + p) * d;
-            for (size_t i = 0; i < d; ++i) s->ctx[qh * d + i] += s->probs[p] * Vc[off + i];
-        }
-    }
-    if (!finite_all(s->ctx, h)) return OR_NONFINITE;
+    int st = attend_core(s, li, s->processed, s->q, s->k, s->v, s->qr, s->kr, s->ctx);
+    if (st) return st;
     project(&l->o, s->ctx, s->out, 1, h, h, 0);
     if (!finite_all(s->out, h)) return OR_NONFINITE;
     return OR_OK;
@@ -893,6 +1080,76 @@ int or_session_append(or_session *s, const size_t *tokens, size_t n, float *logi
         if (st) return st;
     }
     return OR_OK;
+}
+
+/* The same evaluation as or_session_append (every per-token value
+ * bit-identical: the same dots, norms and attention in the same order),
+ * organised layer-major over chunks of up to `chunk` tokens so each weight
+ * row is read once per chunk, for the long prompts of the parity tests.
+ * Differences: intermediate tokens' logits are not computed (only the last
+ * token's), and any non-finite value makes the chunk run again token by
+ * token through or_session_step, whose error semantics then apply. */
+int or_session_append_chunked(or_session *s, const size_t *tokens, size_t n, float *logits,
+                              size_t logits_len, int require_empty, size_t chunk) {
+    if (!s->valid) return OR_INVALID_STATE;
+    if (require_empty && s->processed != 0) return OR_NOT_EMPTY;
+    if (n == 0) return OR_EMPTY_INPUT;
+    if (logits_len != s->m->c.vocab) return OR_INVALID_OUTPUT_LENGTH;
+    for (size_t i = 0; i < n; ++i) if (tokens[i] >= s->m->c.vocab) return OR_INVALID_TOKEN;
+    if (s->processed + n > s->capacity) return OR_FULL;
+    if (chunk == 0) chunk = 64;
+    const or_model *m = s->m;
+    const or_config *c = &m->c;
+    size_t h = c->hidden, kv = c->kv_heads * c->head_dim, ff = c->ff, T = chunk < n ? chunk : n;
+    float *H = (float *)malloc(T * h * 4), *N = (float *)malloc(T * h * 4), *R = (float *)malloc(T * h * 4);
+    float *Q = (float *)malloc(T * h * 4), *K = (float *)malloc(T * kv * 4), *Vv = (float *)malloc(T * kv * 4);
+    float *X = (float *)malloc(T * h * 4), *O = (float *)malloc(T * h * 4);
+    float *G = (float *)malloc(T * ff * 4), *U = (float *)malloc(T * ff * 4), *A = (float *)malloc(T * ff * 4);
+    int status = OR_OK;
+    for (size_t c0 = 0; c0 < n && !status; c0 += T) {
+        size_t nt = n - c0 < T ? n - c0 : T, pos0 = s->processed;
+        int bad = 0;
+        for (size_t t = 0; t < nt; ++t) gather_row(&m->embedding, tokens[c0 + t], h, H + t * h);
+        for (size_t li = 0; li < c->layers && !bad; ++li) {
+            const or_layer *l = &m->layers[li];
+            if (!finite_all(H, nt * h)) { bad = 1; break; }
+            for (size_t t = 0; t < nt; ++t) rms_row(H + t * h, l->attn_norm, N + t * h, h, c->norm_eps);
+            project(&l->q, N, Q, nt, h, h, 0);
+            project(&l->k, N, K, nt, h, kv, 0);
+            project(&l->v, N, Vv, nt, h, kv, 0);
+            for (size_t t = 0; t < nt && !bad; ++t)
+                bad = attend_core(s, li, pos0 + t, Q + t * h, K + t * kv, Vv + t * kv, s->qr, s->kr, X + t * h) != OR_OK;
+            if (bad) break;
+            project(&l->o, X, O, nt, h, h, 0);
+            if (!finite_all(O, nt * h)) { bad = 1; break; }
+            for (size_t i = 0; i < nt * h; ++i) R[i] = H[i] + O[i];
+            if (!finite_all(R, nt * h)) { bad = 1; break; }
+            for (size_t t = 0; t < nt; ++t) rms_row(R + t * h, l->ffn_norm, N + t * h, h, c->norm_eps);
+            project(&l->gate, N, G, nt, h, ff, 0);
+            project(&l->up, N, U, nt, h, ff, 0);
+            if (!finite_all(G, nt * ff)) { bad = 1; break; }
+            for (size_t i = 0; i < nt * ff; ++i) A[i] = silu1(G[i]);
+            for (size_t i = 0; i < nt * ff; ++i) A[i] *= U[i];
+            if (!finite_all(A, nt * ff)) { bad = 1; break; }
+            project(&l->down, A, O, nt, ff, h, 0);
+            for (size_t i = 0; i < nt * h; ++i) H[i] = R[i] + O[i];
+            if (!finite_all(H, nt * h)) { bad = 1; break; }
+        }
+        if (!bad && c0 + nt == n) {
+            rms_row(H + (nt - 1) * h, m->final_norm, N, h, c->norm_eps);
+            project(head_matrix(m), N, logits, 1, h, c->vocab, 1);
+            bad = !finite_all(logits, c->vocab);
+        }
+        if (bad) {
+            /* the serial path, from the same state (processed is unchanged) */
+            for (size_t t = 0; t < nt && !status; ++t)
+                status = or_session_step(s, tokens[c0 + t], logits, logits_len);
+        } else {
+            s->processed += nt;
+        }
+    }
+    free(H); free(N); free(R); free(Q); free(K); free(Vv); free(X); free(O); free(G); free(U); free(A);
+    return status;
 }
 
 /* Greedy argmax with a strict `>`, so the lowest id wins ties

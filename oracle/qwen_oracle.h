@@ -128,6 +128,9 @@ void or_session_reset(or_session *s);
 int or_session_step(or_session *s, size_t token, float *logits, size_t logits_len);
 int or_session_append(or_session *s, const size_t *tokens, size_t n, float *logits,
                       size_t logits_len, int require_empty);
+int or_session_append_chunked(or_session *s, const size_t *tokens, size_t n, float *logits,
+                              size_t logits_len, int require_empty, size_t chunk);
+void or_set_fast(int on);
 size_t or_argmax(const float *logits, size_t n);
 long or_greedy(or_session *s, const size_t *prompt, size_t n, const size_t *stops, size_t nstops,
                size_t max_new, size_t *out);

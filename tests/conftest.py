@@ -36,7 +36,16 @@ def assert_close(actual, expected, atol=ATOL, rtol=RTOL, name=""):
 
 
 @pytest.fixture(scope="session")
-def oracle():
+def oracle_lib():
     from oracle import oracle as o
     o.build()
     return o
+
+
+@pytest.fixture
+def oracle(oracle_lib):
+    # Interleaved evaluation: bit-identical to the one-row-at-a-time loop
+    # (tests/test_oracle.py::test_interleaved_and_chunked_paths_bit_identical)
+    # and several times faster for the model-sized parity tests.
+    oracle_lib.set_fast(True)
+    return oracle_lib

@@ -169,7 +169,7 @@ def test_qwen7b_decode_kernel_matches_multitoken_path(oracle):
     got = s.prefill(prompt)
     first = int(np.argmax(got))
     os_ = oracle.Session(om, cap, kv_bf16=True, budget=0)
-    _, exp = os_.prefill(prompt)
+    _, exp = os_.append_chunked(prompt, True)
     assert max_abs(got, exp) <= 2e-2, max_abs(got, exp)
     assert int(np.argmax(exp)) == first
     or_ids = [first]

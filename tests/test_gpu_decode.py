@@ -377,7 +377,7 @@ def test_qwen05b_chunked_prefill_parity(oracle, linear_format, kv, tol):
     s = qb.CachedSession(m, n + greedy + 8, kv_dtype=kv, budget=0)
     os_ = oracle.Session(om, n + greedy + 8, kv_bf16=(kv == "bf16"), budget=0)
     got = s.prefill(prompt)
-    _, exp = os_.prefill(prompt)
+    _, exp = os_.append_chunked(prompt, True)
     assert s.processed() == n
     assert max_abs(got, exp) <= tol, max_abs(got, exp)
     first = int(np.argmax(exp))
@@ -407,7 +407,7 @@ def test_qwen05b_long_context_split_attention(oracle, kv, tol):
     s = qb.CachedSession(m, n + steps + 8, kv_dtype=kv, budget=0)
     os_ = oracle.Session(om, n + steps + 8, kv_bf16=(kv == "bf16"), budget=0)
     got = s.prefill(prompt)
-    _, exp = os_.prefill(prompt)
+    _, exp = os_.append_chunked(prompt, True)
     worst = max_abs(got, exp)
     tok = int(np.argmax(exp))
     assert int(np.argmax(got)) == tok
@@ -439,7 +439,7 @@ def test_qwen05b_8192_token_context(oracle):
     s = qb.CachedSession(m, cap, kv_dtype="bf16", budget=0)
     os_ = oracle.Session(om, cap, kv_bf16=True, budget=0)
     got = s.prefill(prompt)
-    _, exp = os_.prefill(prompt)
+    _, exp = os_.append_chunked(prompt, True)
     worst = max_abs(got, exp)
     tok = int(np.argmax(exp))
     assert int(np.argmax(got)) == tok

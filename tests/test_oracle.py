@@ -470,3 +470,39 @@ def test_oracle_generator_matches_library(oracle):
     q = oracle.qwen_0_5b_config(64)
     p = presets.qwen_0_5b(64)
     assert all(getattr(q, f) == getattr(p, f) for f in p.__dataclass_fields__)
+
+
+# ---------------------------------------------- fast evaluation paths ----
+
+@pytest.mark.parametrize("fmt", ["f32", "bf16", "int8"])
+def test_interleaved_and_chunked_paths_bit_identical(oracle, fmt):
+    # The long-prompt and 7B parity tests evaluate prompts layer-major
+    # (append_chunked) with interleaved rows (set_fast); both must give the
+    # serial one-token-at-a-time path's values bit for bit, including the
+    # cache they leave behind (checked through the steps that follow).
+    from llm_inference_edu_b200 import synthetic
+    cfg = presets.tiny_b(300)
+    cfg = cfg.__class__(**{**cfg.__dict__, "qkv_bias": True})
+    w = synthetic.weights(cfg, seed=3, dtype="bf16" if fmt != "f32" else "f32", bias_std=0.02, norm_std=0.1)
+    ow = oracle.int8_model_weights(cfg, w, "int8" if fmt == "int8" else fmt)
+    m = oracle.Model(cfg, ow)
+    prompt = synthetic.prompt(cfg.vocab_size, 270, seed=9)
+    outs = []
+    for fast, chunked in ((False, False), (True, False), (True, True)):
+        oracle.set_fast(fast)
+        try:
+            s = oracle.Session(m, 290, kv_bf16=(fmt == "bf16"), budget=0)
+            st, lg = (s.append_chunked(prompt, True, chunk=37) if chunked else s.prefill(prompt))
+            assert st == 0 and s.processed == 270
+            seq = [lg.copy()]
+            tok = oracle.lib().or_argmax(oracle._p(lg), lg.size)
+            for _ in range(5):
+                st, lg = s.step(tok)
+                assert st == 0
+                seq.append(lg.copy())
+                tok = oracle.lib().or_argmax(oracle._p(lg), lg.size)
+            outs.append(np.stack(seq))
+        finally:
+            oracle.set_fast(True)
+    for o in outs[1:]:
+        assert np.array_equal(o.view(np.uint32), outs[0].view(np.uint32))
