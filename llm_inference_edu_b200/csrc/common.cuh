@@ -186,6 +186,19 @@ __device__ __forceinline__ void bulk_copy_g2s(void *dst, const void *src, uint32
         : "memory");
 }
 
+// Per-thread asynchronous global -> shared copies of 4 or 16 bytes
+// (cp.async): issued, then committed as a group; cp_async_wait_all waits for
+// every group this thread committed.  The data is visible to other threads
+// after their own wait and a CTA barrier.
+__device__ __forceinline__ void cp_async4(void *dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 // Exact int8 -> FP32 for weights stored biased as u = q + 128 (1..255):
 // the byte is placed in the mantissa of 2^23 and 2^23 + 128 subtracted.
 __device__ __forceinline__ float u8b_to_f32(uint32_t word, int byte) {

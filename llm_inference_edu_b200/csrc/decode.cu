@@ -211,24 +211,17 @@ __device__ __forceinline__ void flag_nonfinite(DecodeCtrl *ctrl, float v) {
 }
 
 // dst[i] = src[i], i < n, for read-only model vectors (gains, scales,
-// biases), by the compute warps other than warp 0 (which starts polling the
-// phase's inputs without waiting for these loads).
-template <int B>
-__device__ __forceinline__ void stage_ro(float *dst, const float *src, int n) {
-    constexpr int NS = NT - 32;
-    if (threadIdx.x < 32) return;
-    for (int base = threadIdx.x - 32; base < n; base += B * NS) {
-        float v[B];
-#pragma unroll
-        for (int k = 0; k < B; ++k) {
-            const int i = base + k * NS;
-            v[k] = i < n ? __ldg(src + i) : 0.0f;
-        }
-#pragma unroll
-        for (int k = 0; k < B; ++k) {
-            const int i = base + k * NS;
-            if (i < n) dst[i] = v[k];
-        }
+// biases): asynchronous copies issued by every compute thread (16 bytes at a
+// time when both sides are 16-byte aligned and n % 4 == 0), completed by
+// the next cp_async_wait_all.  A phase's vectors are issued at the start of
+// the phase before it, so their latency is off the critical path.
+__device__ __forceinline__ void stage_async(float *dst, const float *src, int n) {
+    if ((n & 3) == 0 && ((uintptr_t)src & 15) == 0 && ((uintptr_t)dst & 15) == 0) {
+#pragma unroll 1
+        for (int i = threadIdx.x; i < (n >> 2); i += NT) cp_async16(dst + 4 * i, src + 4 * i);
+    } else {
+#pragma unroll 1
+        for (int i = threadIdx.x; i < n; i += NT) cp_async4(dst + i, src + i);
     }
 }
 
@@ -401,6 +394,13 @@ __device__ void prefetch_phase(const DecodeParams &p, const DecodeLayer *lay, co
     }
 }
 
+// Query-head splits of this step's attention (1 below att_split_min cached
+// positions or in the kernel without the split path).
+template <int SPLIT>
+__device__ __forceinline__ int att_nsp(const DecodeParams &p, int pos) {
+    return SPLIT && p.att_splits > 1 && pos + 1 >= p.att_split_min ? p.att_splits : 1;
+}
+
 // The producer warp: the step's blocks in consumption order.
 __device__ void produce(const DecodeParams &p, const DecodeLayer *lay, const CtaGeom &cg, float *sm, int pos,
                         volatile int *s_abort) {
@@ -429,17 +429,75 @@ __device__ void produce(const DecodeParams &p, const DecodeLayer *lay, const Cta
 
 // ------------------------------------------------------------ gemv ----
 
-// team_gemv (below) with the team size G = 2^LG fixed at compile time.
-template <int WF, int U, int LG, class Epi>
-__device__ __forceinline__ void team_gemv_g(const DecodeParams &p, const Ring &rg, Cursor &cur, const KindGeom &g,
-                                            int n, const float *xs, volatile int *s_abort, Epi &epi) {
+// Publishes v in an exchange slot of this step.
+__device__ __forceinline__ void publish(float *slot, float v) {
+    uint32_t b = __float_as_uint(v);
+    if (b == kNotReady) b = 0x7fffffffu;
+    st_relaxed_b32(slot, b);
+}
+
+// SiLU with the reference's sign branch (src/ops.rs:158-173).
+__device__ __forceinline__ float silu1(float v) {
+    if (v >= 0.0f) return v / (1.0f + expf(-v));
+    const float e = expf(v);
+    return v * e / (1.0f + e);
+}
+
+// Epilogues of the per-layer GEMVs, chosen by a run-time kind (the
+// kernel's hot code must stay small: instruction-cache misses were its
+// largest stall when every phase carried three specialised GEMV copies).
+enum { EPI_QKV = 0, EPI_O = 1, EPI_GU = 2, EPI_DN = 3 };
+struct Epi {
+    float *out;         // exchange slots, by row (EPI_GU: by row pair)
+    const float *rv;    // row scales (INT8; any memory space) and, for EPI_QKV, biases at rv + n
+    const float *res;   // EPI_DN: the residual rows (shared memory)
+    int kind;
+    int pub;            // 0: EPI_QKV withholds its outputs (the fault-path hook)
+};
+
+__device__ __forceinline__ void epi_row(const Epi &e, int WFi8, int n, int r, float v, DecodeCtrl *ctrl) {
+    if (e.kind == EPI_QKV) {
+        if (WFi8) v = v * e.rv[r];
+        v = v + e.rv[n + r];
+        if (e.pub) publish(e.out + r, v);
+    } else if (e.kind == EPI_O) {
+        if (WFi8) v = v * e.rv[r];
+        publish(e.out + r, v);
+    } else {  // EPI_DN
+        if (WFi8) v = v * e.rv[r];
+        v = e.res[r] + v;
+        publish(e.out + r, v);
+    }
+    flag_nonfinite(ctrl, v);
+}
+
+// y_r = dot(W_r, x) for the n rows of one streamed block, rows taken in
+// pairs (2u, 2u + 1) when g.U == 2 (gate/up pairs, or two independent rows
+// that share the activation loads; the host pairs rows only where two fit
+// a ring slot) or one at a time when g.U == 1.  The block is consumed in waves of up to g.wave ring
+// slots: every warp waits for the wave's slots, then teams of G = 2^g.lgG
+// threads (G chosen by the host, a run-time value) take row pairs
+// round-robin; a team's threads stride the rows' 16-byte chunks with four
+// FP32 chains per row, meet in a shuffle butterfly, and the team's first
+// thread runs the epilogue.  Each warp frees the wave's slots as soon as it
+// is done with them.  A failed wait (timeout) leaves the abort flag set;
+// the caller tests it after its next CTA barrier.  An odd block's last pair
+// reads a stale (in-bounds) row of its slot, whose result is discarded.
+// Inlined (a call costs more than the code it saves: the kernel parameters
+// become generic loads and live registers spill around it); the team size
+// is a run-time value, so each phase holds one copy of the loop.  Returns
+// the advanced cursor.
+template <int WF>
+__device__ __forceinline__ Cursor gemv_pairs(const DecodeParams &p, const Ring rg, Cursor cur, const KindGeom &g,
+                                          int n, const float *xs, volatile int *s_abort, const Epi e) {
     constexpr int Q = Fmt<WF>::EPC / 4;
-    constexpr int G = 1 << LG, T = NT >> LG;
+    const int lg = g.lgG, G = 1 << lg, T = NT >> lg;
     const int t = threadIdx.x, lane = t & 31;
-    const int lt = t & (G - 1), tm = t >> LG;
-    const int warp_team0 = (t & ~31) >> LG;
+    const int lt = t & (G - 1), tm = t >> lg;
+    const int warp_team0 = (t & ~31) >> lg;
     const int C = g.C;
     const float4 *x4 = reinterpret_cast<const float4 *>(xs);
+    DecodeCtrl *ctrl = p.ctrl;
 #pragma unroll 1
     for (int r0 = 0; r0 < n;) {
         const int rows = min(g.wave * g.rpc, n - r0);
@@ -454,10 +512,8 @@ __device__ __forceinline__ void team_gemv_g(const DecodeParams &p, const Ring &r
             mbar_wait(p, rg.full + s, (uint32_t)(rd & 1), s_abort);
         }
         __syncwarp();
-        // With U = 2 an odd block (the LM head) ends in a half unit: its second
-        // row is read from the wave's last slot (stale, in bounds) and its
-        // result is discarded by the epilogue.
-        const int nu = (rows + U - 1) / U;
+        const bool two = g.U == 2;
+        const int nu = two ? (rows + 1) >> 1 : rows;
 #pragma unroll 1
         for (int ub = 0; ub < nu; ub += T) {
             if (ub + warp_team0 >= nu) break;  // warp-uniform
@@ -468,7 +524,7 @@ __device__ __forceinline__ void team_gemv_g(const DecodeParams &p, const Ring &r
             float2 a0 = make_float2(0.0f, 0.0f), b0 = a0, c0 = a0, d0 = a0;
             float2 a1 = a0, b1 = a0, c1 = a0, d1 = a0;
             if (act) {
-                const int row = u * U;
+                const int row = two ? 2 * u : u;
                 const int j = g.rpc == 1 ? row : (int)__umulhi((unsigned)row, g.rpc_magic);
                 int s = cur.slot + j;
                 if (s >= rg.nslot) s -= rg.nslot;
@@ -483,7 +539,7 @@ __device__ __forceinline__ void team_gemv_g(const DecodeParams &p, const Ring &r
                     const uint4 v = *reinterpret_cast<const uint4 *>(w0 + (size_t)(c + G) * 16);
                     chunk_dot2<WF>(w, x, a0, b0);
                     chunk_dot2<WF>(v, y, c0, d0);
-                    if (U == 2) {
+                    if (two) {
                         const uint4 w1 = *reinterpret_cast<const uint4 *>(w0 + g.stride + (size_t)c * 16);
                         const uint4 v1 = *reinterpret_cast<const uint4 *>(w0 + g.stride + (size_t)(c + G) * 16);
                         chunk_dot2<WF>(w1, x, a1, b1);
@@ -496,7 +552,7 @@ __device__ __forceinline__ void team_gemv_g(const DecodeParams &p, const Ring &r
                     for (int q = 0; q < Q; ++q) x[q] = x4[q * C + c];
                     const uint4 w = *reinterpret_cast<const uint4 *>(w0 + (size_t)c * 16);
                     chunk_dot2<WF>(w, x, a0, b0);
-                    if (U == 2) {
+                    if (two) {
                         const uint4 w1 = *reinterpret_cast<const uint4 *>(w0 + g.stride + (size_t)c * 16);
                         chunk_dot2<WF>(w1, x, a1, b1);
                     }
@@ -504,12 +560,28 @@ __device__ __forceinline__ void team_gemv_g(const DecodeParams &p, const Ring &r
             }
             float s0 = ((a0.x + a0.y) + (b0.x + b0.y)) + ((c0.x + c0.y) + (d0.x + d0.y));
             float s1 = ((a1.x + a1.y) + (b1.x + b1.y)) + ((c1.x + c1.y) + (d1.x + d1.y));
-#pragma unroll
+#pragma unroll 1
             for (int off = G >> 1; off; off >>= 1) {
                 s0 += __shfl_xor_sync(FULL, s0, off);
-                if (U == 2) s1 += __shfl_xor_sync(FULL, s1, off);
+                s1 += __shfl_xor_sync(FULL, s1, off);
             }
-            if (act && lt == 0) epi(r0 + u * U, s0, s1);
+            if (act && lt == 0) {
+                const int r = r0 + (two ? 2 * u : u);
+                if (e.kind == EPI_GU) {
+                    float gv = s0, uv = s1;
+                    if (WF == WF_I8) {
+                        gv = gv * e.rv[r];
+                        uv = uv * e.rv[r + 1];
+                    }
+                    const float a = silu1(gv) * uv;
+                    publish(e.out + (r >> 1), a);
+                    flag_nonfinite(ctrl, gv);
+                    flag_nonfinite(ctrl, a);
+                } else {
+                    epi_row(e, WF == WF_I8, n, r, s0, ctrl);
+                    if (two && r + 1 < n) epi_row(e, WF == WF_I8, n, r + 1, s1, ctrl);
+                }
+            }
         }
         __syncwarp();
         if (lane == 0) {
@@ -525,24 +597,7 @@ __device__ __forceinline__ void team_gemv_g(const DecodeParams &p, const Ring &r
         if (cur.slot >= rg.nslot) { cur.slot -= rg.nslot; ++cur.round; }
         r0 += rows;
     }
-}
-
-// y_r = dot(W_r, x) for the n rows of one streamed block.  The block is
-// consumed in waves of up to g.wave ring slots: every warp waits for the
-// wave's slots, then teams of G = 2^g.lgG threads take units of U rows
-// round-robin; a team's threads stride the row's chunks, accumulate in FP32
-// and meet in a shuffle butterfly, and the team's first thread hands the U
-// results to `epi(row, y0, y1)`.  Each warp frees the wave's slots as soon
-// as it is done with them.  A failed wait (timeout) leaves the abort flag
-// set; the caller tests it after its next CTA barrier.
-// Team sizes are restricted to G in {4, 8, 32} to bound the kernel's code
-// size; the host picks among them.  (The LM head streams through lm_stream.)
-template <int WF, int U, class Epi>
-__device__ __forceinline__ void team_gemv(const DecodeParams &p, const Ring &rg, Cursor &cur, const KindGeom &g,
-                                          int n, const float *xs, volatile int *s_abort, Epi &&epi) {
-    if (g.lgG == 2) team_gemv_g<WF, U, 2>(p, rg, cur, g, n, xs, s_abort, epi);
-    else if (g.lgG == 3) team_gemv_g<WF, U, 3>(p, rg, cur, g, n, xs, s_abort, epi);
-    else team_gemv_g<WF, U, 5>(p, rg, cur, g, n, xs, s_abort, epi);
+    return cur;
 }
 
 // The LM head's stream: the CTA's table rows arrive slot by slot, and each
@@ -622,12 +677,6 @@ __device__ __forceinline__ float *xv(const DecodeParams &p, float *xcur, int l, 
     return xcur + (size_t)l * p.xl + off;
 }
 
-// Publishes v in an exchange slot of this step.
-__device__ __forceinline__ void publish(float *slot, float v) {
-    uint32_t b = __float_as_uint(v);
-    if (b == kNotReady) b = 0x7fffffffu;
-    st_relaxed_b32(slot, b);
-}
 
 // Resets this CTA's share of the other parity (the next step's exchange)
 // to kNotReady; nothing reads or writes that parity during this step.  Run
@@ -809,11 +858,6 @@ __device__ __forceinline__ void stage_after_attention(const DecodeParams &p, flo
     }
 }
 
-__device__ __forceinline__ float silu1(float v) {
-    if (v >= 0.0f) return v / (1.0f + expf(-v));
-    const float e = expf(v);
-    return v * e / (1.0f + e);
-}
 
 // Element offset of the row of (KV head g, position q) in a layer's page
 // pool; `ptab` is the page table staged in shared memory.
@@ -1080,18 +1124,28 @@ __device__ __forceinline__ void attention_context(const DecodeParams &p, const D
 
 // ------------------------------------------------------------ phases ----
 //
-// Each phase has a `prep` that stages its small read-only vectors -- `gain`
-// (norm gains) and `rv` (row scales and biases) -- into shared memory, and a
-// `run` that polls the phase's inputs from the exchange, computes and
-// publishes.  The weights arrive through the ring.
+// Each phase has a `prep` that stages its small read-only vectors -- norm
+// gains and row scales and biases -- into shared memory, and a `run` that
+// polls the phase's inputs from the exchange, computes and publishes.  The
+// weights arrive through the ring.  A phase's prep is issued (cp.async) at
+// the start of the phase before it, into the other half of two double
+// buffers: gains in gain buffer 0 (QKV, final norm) or 1 (gate/up); scales
+// and biases in rv buffer 0 (QKV, gate/up) or 1 (attention, down).
+
+__device__ __forceinline__ float *gain_buf(const DecodeParams &p, float *sm, int b) {
+    return sm + p.sm_gain + b * p.sm_gain_n;
+}
+__device__ __forceinline__ float *rv_buf(const DecodeParams &p, float *sm, int b) {
+    return sm + p.sm_rv + b * p.sm_rv_n;
+}
 
 template <int WF>
 __device__ __forceinline__ void prep_qkv(const DecodeParams &p, const DecodeLayer &Ly, const CtaGeom &cg,
                                          float *sm) {
-    float *gain = sm + p.sm_gain, *rv = sm + p.sm_rv;
-    stage_ro<2>(gain, Ly.attn_norm, p.h);
-    if (WF == WF_I8) stage_ro<1>(rv, Ly.sqkv + cg.qkv_r0, cg.qkv_n);
-    stage_ro<1>(rv + cg.qkv_n, Ly.bqkv + cg.qkv_r0, cg.qkv_n);
+    float *rv = rv_buf(p, sm, 0);
+    stage_async(gain_buf(p, sm, 0), Ly.attn_norm, p.h);
+    if (WF == WF_I8) stage_async(rv, Ly.sqkv + cg.qkv_r0, cg.qkv_n);
+    stage_async(rv + cg.qkv_n, Ly.bqkv + cg.qkv_r0, cg.qkv_n);
 }
 
 template <int WF>
@@ -1099,7 +1153,7 @@ __device__ __forceinline__ void run_qkv(const DecodeParams &p, const CtaGeom &cg
                                         float *sm, const Ring &rg, Cursor &cur, volatile int *s_abort) {
     constexpr int EPC = Fmt<WF>::EPC;
     float *xs = sm + p.sm_xs, *h2 = sm + p.sm_h2;
-    const float *gain = sm + p.sm_gain, *rv = sm + p.sm_rv;
+    const float *gain = gain_buf(p, sm, 0), *rv = rv_buf(p, sm, 0);
     if (l > 0) {
         await_stage(p, h2, xv(p, xcur, l - 1, p.x_hid), p.h, s_abort);
     } else {
@@ -1110,17 +1164,9 @@ __device__ __forceinline__ void run_qkv(const DecodeParams &p, const CtaGeom &cg
     mark_ready(p, 4 * l - 1);
     if (*s_abort) return;
     block_rmsnorm<EPC>(h2, gain, xs, p.h, p.ch, p.eps, sm + p.sm_red);
-    const int R = cg.qkv_n;
-    float *out = xv(p, xcur, l, p.x_qkv) + cg.qkv_r0;
-    const bool pub = !(p.withhold && l == 0 && blockIdx.x == 0);
-    DecodeCtrl *ctrl = p.ctrl;
-    team_gemv<WF, 1>(p, rg, cur, p.kind[K_QKV], R, xs, s_abort, [&](int r, float a, float) {
-        float v = a;
-        if (WF == WF_I8) v = v * rv[r];
-        v = v + rv[R + r];
-        if (pub) publish(out + r, v);
-        flag_nonfinite(ctrl, v);
-    });
+    const Epi e{xv(p, xcur, l, p.x_qkv) + cg.qkv_r0, rv, nullptr, EPI_QKV,
+                !(p.withhold && l == 0 && blockIdx.x == 0)};
+    cur = gemv_pairs<WF>(p, rg, cur, p.kind[K_QKV], cg.qkv_n, xs, s_abort, e);
 }
 
 // The position-split exchange of head hh (split sp of nsp, layer l): this
@@ -1193,33 +1239,28 @@ __device__ __forceinline__ bool split_exchange(const DecodeParams &p, int hh, in
 template <int WF>
 __device__ __forceinline__ void prep_attention(const DecodeParams &p, const DecodeLayer &Ly, const CtaGeom &cg,
                                                float *sm) {
-    if (WF == WF_I8 && cg.natt > 0) stage_ro<1>(sm + p.sm_rv, Ly.so + cg.att_r0[0], cg.att_n[0]);
+    if (WF == WF_I8 && cg.natt > 0) stage_async(rv_buf(p, sm, 1), Ly.so + cg.att_r0[0], cg.att_n[0]);
 }
 
 template <int WF, int KVBF16, int SPLIT>
 __device__ __forceinline__ void run_attention(const DecodeParams &p, const DecodeLayer &Ly, const CtaGeom &cg,
                                               float *xcur, int l, int pos, float *sm, const Ring &rg, Cursor &cur,
                                               volatile int *s_abort) {
-    const float *rv = sm + p.sm_rv, *xs = sm + p.sm_xs;
-    DecodeCtrl *ctrl = p.ctrl;
+    const float *rv = rv_buf(p, sm, 1), *xs = sm + p.sm_xs;
 #pragma unroll 1
     for (int a = 0; a < cg.natt; ++a) {
         const int hh = cg.att_hh[a], r0 = cg.att_r0[a], n = cg.att_n[a];
-        const int nsp = SPLIT && p.att_splits > 1 && pos + 1 >= p.att_split_min ? p.att_splits : 1;
+        const int nsp = att_nsp<SPLIT>(p, pos);
         const int sp = cg.att_sp[a];
         const int lo = nsp > 1 ? (int)((long long)(pos + 1) * sp / nsp) : 0;
         const int hi = nsp > 1 ? (int)((long long)(pos + 1) * (sp + 1) / nsp) : pos + 1;
         attention_context<WF, KVBF16>(p, Ly, xv(p, xcur, l, p.x_qkv), hh, r0 == 0 && hh % p.group == 0, pos, sm,
                                       lo, hi, a == 0 ? 4 * l : -1, s_abort);
         if (SPLIT && nsp > 1 && !split_exchange<WF>(p, hh, sp, nsp, l, sm, s_abort)) return;
-        float *outp = xv(p, xcur, l, p.x_part) + (size_t)hh * p.h + r0;
-        const float *so = Ly.so + r0;
-        team_gemv<WF, 1>(p, rg, cur, p.kind[K_O], n, xs, s_abort, [&](int r, float acc, float) {
-            float v = acc;
-            if (WF == WF_I8) v = v * (a == 0 ? rv[r] : __ldg(so + r));
-            publish(outp + r, v);
-            flag_nonfinite(ctrl, v);
-        });
+        // Row scales: staged in shared memory for the first item, read from
+        // global memory for the others.
+        const Epi e{xv(p, xcur, l, p.x_part) + (size_t)hh * p.h + r0, a == 0 ? rv : Ly.so + r0, nullptr, EPI_O, 1};
+        cur = gemv_pairs<WF>(p, rg, cur, p.kind[K_O], n, xs, s_abort, e);
         if (a + 1 < cg.natt) csync();  // xs is rewritten by the next item
     }
 }
@@ -1227,8 +1268,8 @@ __device__ __forceinline__ void run_attention(const DecodeParams &p, const Decod
 template <int WF>
 __device__ __forceinline__ void prep_gate_up(const DecodeParams &p, const DecodeLayer &Ly, const CtaGeom &cg,
                                              float *sm) {
-    stage_ro<2>(sm + p.sm_gain, Ly.ffn_norm, p.h);
-    if (WF == WF_I8) stage_ro<1>(sm + p.sm_rv, Ly.sgu + 2 * cg.gu_f0, 2 * cg.gu_n);
+    stage_async(gain_buf(p, sm, 1), Ly.ffn_norm, p.h);
+    if (WF == WF_I8) stage_async(rv_buf(p, sm, 0), Ly.sgu + 2 * cg.gu_f0, 2 * cg.gu_n);
 }
 
 template <int WF>
@@ -1236,7 +1277,7 @@ __device__ __forceinline__ void run_gate_up(const DecodeParams &p, const CtaGeom
                                             const Ring &rg, Cursor &cur, volatile int *s_abort) {
     constexpr int EPC = Fmt<WF>::EPC;
     float *xs = sm + p.sm_xs, *h2 = sm + p.sm_h2;
-    const float *gain = sm + p.sm_gain, *rv = sm + p.sm_rv;
+    const float *gain = gain_buf(p, sm, 1), *rv = rv_buf(p, sm, 0);
     stage_after_attention(p, xcur, l, h2, s_abort);
     csync();
     mark_ready(p, 4 * l + 1);
@@ -1244,24 +1285,14 @@ __device__ __forceinline__ void run_gate_up(const DecodeParams &p, const CtaGeom
     if (blockIdx.x == 0)
         for (int i = threadIdx.x; i < p.h; i += NT) flag_nonfinite(p.ctrl, h2[i]);
     block_rmsnorm<EPC>(h2, gain, xs, p.h, p.ch, p.eps, sm + p.sm_red);
-    float *act = xv(p, xcur, l, p.x_act) + cg.gu_f0;
-    DecodeCtrl *ctrl = p.ctrl;
-    team_gemv<WF, 2>(p, rg, cur, p.kind[K_GU], 2 * cg.gu_n, xs, s_abort, [&](int row, float g, float u) {
-        if (WF == WF_I8) {
-            g = g * rv[row];
-            u = u * rv[row + 1];
-        }
-        const float a = silu1(g) * u;
-        publish(act + (row >> 1), a);
-        flag_nonfinite(ctrl, g);
-        flag_nonfinite(ctrl, a);
-    });
+    const Epi e{xv(p, xcur, l, p.x_act) + cg.gu_f0, rv, nullptr, EPI_GU, 1};
+    cur = gemv_pairs<WF>(p, rg, cur, p.kind[K_GU], 2 * cg.gu_n, xs, s_abort, e);
 }
 
 template <int WF>
 __device__ __forceinline__ void prep_down(const DecodeParams &p, const DecodeLayer &Ly, const CtaGeom &cg,
                                           float *sm) {
-    if (WF == WF_I8) stage_ro<1>(sm + p.sm_rv, Ly.sd + cg.dn_r0, cg.dn_n);
+    if (WF == WF_I8) stage_async(rv_buf(p, sm, 1), Ly.sd + cg.dn_r0, cg.dn_n);
 }
 
 template <int WF>
@@ -1313,16 +1344,9 @@ __device__ __forceinline__ void run_down(const DecodeParams &p, const CtaGeom &c
     if (*s_abort) return;
     // h' of this layer is still in shared memory from the gate/up phase of
     // this same CTA (src/kv_cache.rs:437-443: x_next = h' + down(a)).
-    const float *h2 = sm + p.sm_h2 + cg.dn_r0, *rv = sm + p.sm_rv;
-    float *hid = xv(p, xcur, l, p.x_hid) + cg.dn_r0;
-    DecodeCtrl *ctrl = p.ctrl;
-    team_gemv<WF, 1>(p, rg, cur, p.kind[K_DN], cg.dn_n, xs, s_abort, [&](int r, float acc, float) {
-        float v = acc;
-        if (WF == WF_I8) v = v * rv[r];
-        const float o = h2[r] + v;
-        publish(hid + r, o);
-        flag_nonfinite(ctrl, o);
-    });
+    const float *h2 = sm + p.sm_h2 + cg.dn_r0, *rv = rv_buf(p, sm, 1);
+    const Epi e{xv(p, xcur, l, p.x_hid) + cg.dn_r0, rv, h2, EPI_DN, 1};
+    cur = gemv_pairs<WF>(p, rg, cur, p.kind[K_DN], cg.dn_n, xs, s_abort, e);
 }
 
 // Final RMSNorm, this CTA's rows of the (tied) table, logits and the CTA's
@@ -1335,7 +1359,7 @@ __device__ __forceinline__ void run_lm_head(const DecodeParams &p, const CtaGeom
     constexpr int TEPC = Fmt<TF>::EPC;
     const int G = gridDim.x, b = blockIdx.x;
     float *xs = sm + p.sm_xs, *h2 = sm + p.sm_h2;
-    const float *gain = sm + p.sm_gain;
+    const float *gain = gain_buf(p, sm, 0);
     float *rowv = sm + p.sm_sc;
     DecodeCtrl *ctrl = p.ctrl;
     await_stage(p, h2, xv(p, xcur, p.L - 1, p.x_hid), p.h, s_abort);
@@ -1473,27 +1497,38 @@ __global__ void __maxnreg__(128) decode_kernel(const __grid_constant__ DecodePar
 
     Cursor cur{0, 0};
     prep_qkv<WF>(p, lay[0], cg, sm);
+    cp_async_commit();
     bool ok = true;
-    // Each phase: stage the phase's small read-only vectors, poll its inputs
-    // from the exchange, run, publish.  Every exit decision is taken right
-    // after a CTA barrier, so all compute threads agree on it.
+    // Each phase: wait for its own small read-only vectors (issued one
+    // phase earlier), issue the next phase's, poll its inputs from the
+    // exchange, run, publish.  Every exit decision is taken right after a
+    // CTA barrier, so all compute threads agree on it.
 #pragma unroll 1
     for (int l = 0; l < p.L && ok; ++l) {
         const DecodeLayer &Ly = lay[l];
+        cp_async_wait_all();
+        prep_attention<WF>(p, Ly, cg, sm);
+        cp_async_commit();
         run_qkv<WF>(p, cg, xcur, l, token, sm, rg, cur, s_abort);
         if (!(ok = phase_end(p, 4 * l, s_abort))) break;
-        prep_attention<WF>(p, Ly, cg, sm);
+        cp_async_wait_all();
+        prep_gate_up<WF>(p, Ly, cg, sm);
+        cp_async_commit();
         run_attention<WF, KVBF16, SPLIT>(p, Ly, cg, xcur, l, pos, sm, rg, cur, s_abort);
         if (!(ok = phase_end(p, 4 * l + 1, s_abort))) break;
-        prep_gate_up<WF>(p, Ly, cg, sm);
+        cp_async_wait_all();
+        prep_down<WF>(p, Ly, cg, sm);
+        cp_async_commit();
         run_gate_up<WF>(p, cg, xcur, l, sm, rg, cur, s_abort);
         if (!(ok = phase_end(p, 4 * l + 2, s_abort))) break;
-        prep_down<WF>(p, Ly, cg, sm);
+        cp_async_wait_all();
+        if (l + 1 < p.L) prep_qkv<WF>(p, lay[l + 1], cg, sm);
+        else stage_async(gain_buf(p, sm, 0), p.final_norm, p.h);
+        cp_async_commit();
         run_down<WF>(p, cg, xcur, l, sm, rg, cur, s_abort);
         if (!(ok = phase_end(p, 4 * l + 3, s_abort))) break;
-        if (l + 1 < p.L) prep_qkv<WF>(p, lay[l + 1], cg, sm);
-        else stage_ro<2>(sm + p.sm_gain, p.final_norm, p.h);
     }
+    cp_async_wait_all();  // nothing lands in shared memory after an early exit
     if (ok) run_lm_head<TF>(p, cg, xcur, pos, sm, rg, cur, s_abort);
 }
 

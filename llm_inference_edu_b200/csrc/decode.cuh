@@ -137,8 +137,10 @@ struct DecodeParams {
     // xs: the current activation vector in the quad-major layout; h2: the
     // residual stream; gain: norm gains; rv: per-row scales/biases; sc:
     // attention scores or the CTA's logits; q: q, k, v of one head; red:
-    // cross-warp partials; lay: the layer table.
+    // cross-warp partials; lay: the layer table.  gain and rv are double
+    // buffers of sm_gain_n and sm_rv_n floats each.
     int sm_xs, sm_h2, sm_gain, sm_rv, sm_sc, sm_q, sm_red, sm_lay;
+    int sm_gain_n, sm_rv_n;
     // The page table's first ceil(cap / 16) entries, staged by every step.
     int sm_ptab;
     // Weight ring: nslot slots of slot_bytes at sm_ring (128-byte aligned) and

@@ -559,14 +559,15 @@ static uint32_t session_build(Session &s) {
     const int red = r4(std::max(64, 2 * 16 + 16 * p.hd));  // softmax partials, then [warp][hd] context partials
     const int lay = r4((long long)(L * sizeof(DecodeLayer) / 4));
     const int ptb = r4((long long)pages_per_seq(cap + 1));  // staged page table (one int per page)
-    p.sm_xs = 0; p.sm_h2 = xs; p.sm_gain = p.sm_h2 + h4; p.sm_rv = p.sm_gain + h4;
-    p.sm_sc = p.sm_rv + rv; p.sm_q = p.sm_sc + sc; p.sm_red = p.sm_q + q; p.sm_lay = p.sm_red + red;
+    p.sm_xs = 0; p.sm_h2 = xs; p.sm_gain = p.sm_h2 + h4; p.sm_rv = p.sm_gain + 2 * h4;
+    p.sm_gain_n = h4; p.sm_rv_n = rv;
+    p.sm_sc = p.sm_rv + 2 * rv; p.sm_q = p.sm_sc + sc; p.sm_red = p.sm_q + q; p.sm_lay = p.sm_red + red;
     p.sm_ptab = p.sm_lay + lay;
     // Weight ring: slots of at least 16 KB holding whole rows (and whole
     // gate/up pairs), as many as fit the remaining shared memory (at most
     // 16), 128-byte aligned; the full/empty mbarriers (2 per slot, 8 bytes
     // each) precede it.
-    size_t max_row = std::max({2 * m.sh, m.shd, m.sff, m.semb});
+    size_t max_row = std::max({2 * m.sh, m.shd, m.sff, 2 * m.semb});  // gate/up and LM-head rows go in pairs
     p.slot_bytes = (int)std::max<size_t>(16384, (max_row + 127) & ~(size_t)127);
     p.sm_bar = (p.sm_ptab + ptb + 3) & ~3;
     p.sm_ring = (p.sm_bar + 2 * 2 * 16 + 31) & ~31;
@@ -586,20 +587,21 @@ static uint32_t session_build(Session &s) {
         KindGeom &g = p.kind[k];
         g.stride = (int)strides[k];
         g.C = (int)(strides[k] / 16);
-        g.U = (k == K_GU || k == K_LM) ? 2 : 1;  // gate/up pairs; LM rows two at a time
+        // Row pairs (gate/up pairs; elsewhere two rows sharing the activation
+        // loads) where two rows fit a slot, else single rows.
+        g.U = (k == K_GU || k == K_LM || 2 * strides[k] <= (size_t)p.slot_bytes) ? 2 : 1;
         g.rpc = std::max(g.U, (p.slot_bytes / g.stride) / g.U * g.U);
         g.rpc_magic = g.rpc > 1 ? (unsigned)(((1ull << 32) + g.rpc - 1) / g.rpc) : 0u;  // rpc == 1 divides directly
+        if ((size_t)g.rpc * strides[k] > (size_t)p.slot_bytes) return QB_UNSUPPORTED;  // a slot's rows must fit it
         const int block_slots = std::max(1, (rows_max[k] + g.rpc - 1) / g.rpc);
         // A per-layer block is consumed in one wave (its weights are already
         // resident); a longer stream (the LM head) in waves of a third of the
         // ring (at most three slots), so the rest keeps copies in flight.
         g.wave = block_slots <= nslot / 2 ? block_slots : std::max(1, std::min(3, nslot / 3));
-        const int units = std::max(1, std::min(rows_max[k], g.wave * g.rpc) / g.U);
-        static const int lm_set[3] = {3, 4, 5}, set[3] = {2, 3, 5};  // the device's instantiated sizes
-        const int *cand = k == K_LM ? lm_set : set;
+        const int units = std::max(1, (std::min(rows_max[k], g.wave * g.rpc) + g.U - 1) / g.U);
         long long best = -1;
-        for (int ci = 0; ci < 3; ++ci) {
-            const int lg = cand[ci], G = 1 << lg, teams = kDecodeThreads / G;
+        for (int lg = 2; lg <= 5; ++lg) {  // team sizes 4 .. 32 (a run-time value on the device)
+            const int G = 1 << lg, teams = kDecodeThreads / G;
             const long long rounds = (units + teams - 1) / teams;
             const long long cost = rounds * ((long long)((g.C + G - 1) / G) * 4 * g.U + 20 + 2 * lg);
             if (best < 0 || cost < best) { best = cost; g.lgG = lg; }
