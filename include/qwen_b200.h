@@ -402,6 +402,62 @@ uint32_t qb_batch_stream(uint64_t batch, void **stream);
 uint32_t qb_batch_free(uint64_t batch);
 
 /* ------------------------------------------------------------------ */
+/* Tensor parallelism across the GPUs of one box                       */
+/* ------------------------------------------------------------------ */
+/* No counterpart in the reference (one CPU thread, src/kernels.rs:8); these
+ * replace its two full-width reductions per layer -- o_proj
+ * (src/kv_cache.rs:581-585) and down (src/kv_cache.rs:437-443) -- with a
+ * sum over ranks, and its argmax over the vocabulary
+ * (src/sampling.rs:65-70) with one over ranks.  One process per GPU; every
+ * rank makes the same calls in the same order.
+ *
+ * A shard (qb_model_create_tp) of rank r of `size` holds: for size <=
+ * kv_heads, kv_heads / size whole KV groups (their query heads and KV
+ * heads); for larger sizes (a multiple of kv_heads), one KV head replicated
+ * on size / kv_heads ranks that split its group's query heads (e.g. 4 and
+ * 3 of 7); ff_dim / size FFN columns; whole 128-row tiles of the LM-head
+ * rows; the whole embedding table and norms.  qb_model_set_tensor takes
+ * the FULL tensors on every rank (INT8 row scales are those of the whole
+ * rows).  Finiteness of the rows a rank does not keep is checked by the
+ * rank that keeps them.  A shard decodes only through qb_batch_create_tp
+ * (qb_session_create returns QB_UNSUPPORTED). */
+typedef struct {
+    int32_t rank, size;
+    size_t head0, heads;        /* query heads [head0, head0 + heads) */
+    size_t kv_head0, kv_heads;  /* KV heads */
+    size_t ff0, ff;             /* FFN columns */
+    size_t vocab0, vocab;       /* LM-head rows (global ids) */
+} qb_tp_shard;
+
+uint32_t qb_model_create_tp(const qb_model_config *config, uint32_t linear_format,
+                            uint32_t table_format, int device, int tp_rank, int tp_size,
+                            uint64_t *out_model);
+uint32_t qb_model_tp_info(uint64_t model, qb_tp_shard *out);
+/* The shard rank `tp_rank` of `tp_size` would hold (host only, no device
+ * needed); QB_UNSUPPORTED when the shape does not split that way. */
+uint32_t qb_tp_shard_of(const qb_model_config *config, int tp_rank, int tp_size, qb_tp_shard *out);
+
+/* The communicator: one exchange buffer per rank in device memory (flags,
+ * two slots of partial sums [rows][hidden], two slots of argmax pairs),
+ * shared with the other ranks through CUDA IPC.  Create it on the rank's
+ * device for at least the batch's workspace rows (max(sequences, 256)),
+ * export its 64-byte handle, exchange the handles (any host channel), then
+ * connect with all `size` handles in rank order.  Each exchange raises this
+ * rank's flag in every rank's buffer and waits (bounded, 2 s; then
+ * QB_DEVICE_TIMEOUT) for all flags, then reads every rank's data with peer
+ * loads and sums in rank order: every rank gets the same values. */
+uint32_t qb_tp_comm_create(int device, size_t rows, size_t hidden, uint64_t *out_comm);
+uint32_t qb_tp_comm_handle(uint64_t comm, void *out, size_t len /* 64 */);
+uint32_t qb_tp_comm_connect(uint64_t comm, int rank, int size, const void *handles,
+                            size_t len /* size * 64 */);
+uint32_t qb_tp_comm_free(uint64_t comm);
+/* A batch over a shard: as qb_batch_create; greedy ids are global, and
+ * qb_batch_logits returns this rank's rows, [sequences][vocab] of its
+ * qb_tp_shard. */
+uint32_t qb_batch_create_tp(uint64_t model, uint64_t comm, size_t sequences, size_t capacity,
+                            uint32_t kv_dtype, uint64_t *out_batch);
+
+/* ------------------------------------------------------------------ */
 /* Synthetic inputs (host only; no GPU needed)                         */
 /* ------------------------------------------------------------------ */
 

@@ -67,6 +67,14 @@ SIGNATURES = {
     "qb_batch_reset": ([U64], U32),
     "qb_batch_stream": ([U64, P], U32),
     "qb_batch_free": ([U64], U32),
+    "qb_model_create_tp": ([P, U32, U32, C.c_int, C.c_int, C.c_int, P], U32),
+    "qb_model_tp_info": ([U64, P], U32),
+    "qb_tp_shard_of": ([P, C.c_int, C.c_int, P], U32),
+    "qb_tp_comm_create": ([C.c_int, S, S, P], U32),
+    "qb_tp_comm_handle": ([U64, P, S], U32),
+    "qb_tp_comm_connect": ([U64, C.c_int, C.c_int, P, S], U32),
+    "qb_tp_comm_free": ([U64], U32),
+    "qb_batch_create_tp": ([U64, U64, S, S, U32, P], U32),
     "qb_synthetic_normal": ([U64, U64, S, C.c_double, U32, P], U32),
     "qb_synthetic_tokens": ([U64, U64, S, U32, P], U32),
 }
@@ -112,3 +120,8 @@ class GenerationInfo(C.Structure):
 
 class BatchInfo(C.Structure):
     _fields_ = [("sequences", S), ("capacity", S), ("processed", S), ("valid", I32)]
+
+
+class TpShard(C.Structure):
+    _fields_ = [("rank", I32), ("size", I32)] + [(n, S) for n in ("head0", "heads", "kv_head0", "kv_heads",
+                                                                    "ff0", "ff", "vocab0", "vocab")]

@@ -250,7 +250,9 @@ class Decoder:
     as "f32" or "bf16"."""
 
     def __init__(self, config: ModelConfig, weights: dict, linear_format: str = "f32",
-                 table_format: str = "f32", device: int = 0):
+                 table_format: str = "f32", device: int = 0, tp=None):
+        """tp = (rank, size): this process's tensor-parallel shard (the full
+        weight dictionary is passed on every rank; see ``shard``)."""
         self.config = config
         self.linear_format = linear_format
         self.table_format = table_format
@@ -258,9 +260,15 @@ class Decoder:
                               config.query_heads, config.kv_heads, config.head_dim, config.ff_dim,
                               config.max_tokens, config.rope_base, config.norm_epsilon)
         h = C.c_uint64()
-        _check(lib().qb_model_create(C.byref(c), LINEAR_FORMATS[linear_format],
-                                     TABLE_FORMATS[table_format], device, C.byref(h)), ModelError)
+        if tp is None:
+            _check(lib().qb_model_create(C.byref(c), LINEAR_FORMATS[linear_format],
+                                         TABLE_FORMATS[table_format], device, C.byref(h)), ModelError)
+        else:
+            _check(lib().qb_model_create_tp(C.byref(c), LINEAR_FORMATS[linear_format],
+                                            TABLE_FORMATS[table_format], device, int(tp[0]), int(tp[1]),
+                                            C.byref(h)), ModelError)
         self.handle = h.value
+        self.device = device
         try:
             self._set(-1, "embedding", weights["embedding"])
             if weights.get("lm_head") is not None:
@@ -290,6 +298,13 @@ class Decoder:
         if getattr(self, "handle", None):
             lib().qb_model_free(self.handle)
             self.handle = None
+
+    def shard(self) -> dict:
+        """This model's tensor-parallel shard: rank, size and the half-open
+        ranges of query heads, KV heads, FFN columns and LM-head rows."""
+        i = _lib.TpShard()
+        _check(lib().qb_model_tp_info(self.handle, C.byref(i)), ModelError)
+        return _shard_dict(i)
 
     def logical_weight_bytes(self) -> int:
         n = C.c_size_t()
@@ -474,20 +489,74 @@ class CachedSession:
 
 # ---------------------------------------------------------------- batch --
 
+def _shard_dict(i) -> dict:
+    return {"rank": i.rank, "size": i.size, "heads": (i.head0, i.head0 + i.heads),
+            "kv_heads": (i.kv_head0, i.kv_head0 + i.kv_heads), "ff": (i.ff0, i.ff0 + i.ff),
+            "vocab": (i.vocab0, i.vocab0 + i.vocab)}
+
+
+def tp_shard_of(config: ModelConfig, rank: int, size: int) -> dict:
+    """The tensor-parallel shard rank `rank` of `size` holds (host only)."""
+    c = _lib.ModelConfigC(config.vocab_size, config.layers, config.hidden_dim, config.query_heads,
+                          config.kv_heads, config.head_dim, config.ff_dim, config.max_tokens,
+                          config.rope_base, config.norm_epsilon)
+    i = _lib.TpShard()
+    _check(lib().qb_tp_shard_of(C.byref(c), rank, size, C.byref(i)), ModelError)
+    return _shard_dict(i)
+
+
+class TpComm:
+    """A rank's tensor-parallel communicator (no reference counterpart):
+    its exchange buffer, opened by the other ranks through CUDA IPC.
+    ``exchange(handles)`` receives every rank's ``handle()`` in rank order
+    (gathered over any host channel, e.g. torch.distributed)."""
+
+    def __init__(self, device: int, rows: int, hidden: int):
+        h = C.c_uint64()
+        _check(lib().qb_tp_comm_create(device, rows, hidden, C.byref(h)), CacheError)
+        self.handle_id = h.value
+
+    def handle(self) -> bytes:
+        buf = (C.c_uint8 * 64)()
+        _check(lib().qb_tp_comm_handle(self.handle_id, buf, 64), CacheError)
+        return bytes(buf)
+
+    def connect(self, rank: int, handles) -> None:
+        blob = b"".join(handles)
+        buf = (C.c_uint8 * len(blob)).from_buffer_copy(blob)
+        _check(lib().qb_tp_comm_connect(self.handle_id, rank, len(handles), buf, len(blob)), CacheError)
+
+    def __del__(self):
+        if getattr(self, "handle_id", None):
+            lib().qb_tp_comm_free(self.handle_id)
+            self.handle_id = None
+
+
 class BatchSession:
     """`sequences` independent sequences decoded greedily in lockstep, each
     with its own KV cache of `capacity` positions.  No counterpart in the
     reference (one sequence per CachedSession); each row matches a
-    CachedSession fed the same tokens."""
+    CachedSession fed the same tokens.  With a tensor-parallel shard, pass
+    its connected ``comm``; ids are global and ``logits`` holds this rank's
+    vocabulary rows."""
 
-    def __init__(self, model: Decoder, sequences: int, capacity: int, kv_dtype: str = "f32"):
+    def __init__(self, model: Decoder, sequences: int, capacity: int, kv_dtype: str = "f32", comm=None):
         self.model = model
+        self.comm = comm
         h = C.c_uint64()
-        _check(lib().qb_batch_create(model.handle, sequences, capacity, KV_DTYPES[kv_dtype],
-                                     C.byref(h)), CacheError)
+        if comm is None:
+            _check(lib().qb_batch_create(model.handle, sequences, capacity, KV_DTYPES[kv_dtype],
+                                         C.byref(h)), CacheError)
+        else:
+            _check(lib().qb_batch_create_tp(model.handle, comm.handle_id, sequences, capacity,
+                                            KV_DTYPES[kv_dtype], C.byref(h)), CacheError)
         self.handle = h.value
         self.sequences = sequences
-        self.vocab = model.config.vocab_size
+        if comm is None:
+            self.vocab = model.config.vocab_size
+        else:
+            v0, v1 = model.shard()["vocab"]
+            self.vocab = v1 - v0
 
     def __del__(self):
         if getattr(self, "handle", None):

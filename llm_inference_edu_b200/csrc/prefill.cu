@@ -701,14 +701,16 @@ cudaError_t gemm(const PrefillArgs &a, const float *X, int ldx, int n, int N, in
 }
 
 Planes xn_planes(const PrefillArgs &a) { return Planes{a.xnp, (size_t)a.chunk * a.h, TC_NP}; }
-Planes ctx_planes(const PrefillArgs &a) { return Planes{a.ctxp, (size_t)a.chunk * a.h, TC_NP}; }
+Planes ctx_planes(const PrefillArgs &a) { return Planes{a.ctxp, (size_t)a.chunk * a.qd, TC_NP}; }
 Planes act_planes(const PrefillArgs &a) { return Planes{a.actp, (size_t)a.chunk * a.ff, TC_NP}; }
 
 // The four GEMMs of a layer: 0 QKV (+ bias), 1 o_proj (head-blocked K) +
-// residual, 2 (gate, up) pairs -> SwiGLU, 3 down + residual.
+// residual, 2 (gate, up) pairs -> SwiGLU, 3 down + residual.  With `part`
+// set, 1 and 3 write this rank's scaled partial sums there instead (no
+// residual; the tensor-parallel sum adds it).
 template <int WF>
-cudaError_t layer_gemm(int which, const PrefillArgs &a, const DecodeLayer &Ly, int n, cudaStream_t st) {
-    const int kv = a.kvh * a.hd, rq = a.h + 2 * kv;
+cudaError_t layer_gemm(int which, const PrefillArgs &a, const DecodeLayer &Ly, int n, float *part, cudaStream_t st) {
+    const int kv = a.kvh * a.hd, rq = a.qd + 2 * kv;
     const Planes none{nullptr, 0, TC_NP};
     switch (which) {
     case 0: {
@@ -717,7 +719,8 @@ cudaError_t layer_gemm(int which, const PrefillArgs &a, const DecodeLayer &Ly, i
     }
     case 1: {
         GemmW w{Ly.wo, a.shd, (size_t)a.h * a.shd, a.hd, Ly.so, nullptr};
-        return gemm<WF, EPI_RESID>(a, a.ctx, a.h, n, a.h, a.qh * a.hd, w, a.x, a.h, a.h2, a.h, none, st);
+        if (part) return gemm<WF, EPI_QKV>(a, a.ctx, a.qd, n, a.h, a.qd, w, nullptr, 0, part, a.h, none, st);
+        return gemm<WF, EPI_RESID>(a, a.ctx, a.qd, n, a.h, a.qd, w, a.x, a.h, a.h2, a.h, none, st);
     }
     case 2: {
         GemmW w{Ly.wgu, a.sh, 0, a.h, Ly.sgu, nullptr};
@@ -725,6 +728,7 @@ cudaError_t layer_gemm(int which, const PrefillArgs &a, const DecodeLayer &Ly, i
     }
     default: {
         GemmW w{Ly.wd, a.sff, 0, a.ff, Ly.sd, nullptr};
+        if (part) return gemm<WF, EPI_QKV>(a, a.act, a.ff, n, a.h, a.ff, w, nullptr, 0, part, a.h, none, st);
         return gemm<WF, EPI_RESID>(a, a.act, a.ff, n, a.h, a.ff, w, a.h2, a.h, a.x, a.h, none, st);
     }
     }
@@ -738,10 +742,10 @@ bool rope_fused(const PrefillArgs &a) {
 
 // The same GEMMs on the tensor cores (weights in the layer's tensor maps,
 // inputs as BF16 planes).
-cudaError_t layer_gemm_tc(int which, const PrefillArgs &a, int l, int n, cudaStream_t st) {
+cudaError_t layer_gemm_tc(int which, const PrefillArgs &a, int l, int n, float *part, cudaStream_t st) {
     const DecodeLayer &Ly = a.layers[l];
     const TcLayerMaps &M = a.tc->layers[l];
-    const int kv = a.kvh * a.hd, rq = a.h + 2 * kv;
+    const int kv = a.kvh * a.hd, rq = a.qd + 2 * kv;
     const Planes none{nullptr, 0, TC_NP};
     TcJob j;
     RopeKv rk;
@@ -750,31 +754,46 @@ cudaError_t layer_gemm_tc(int which, const PrefillArgs &a, int l, int n, cudaStr
         j = TcJob{EPI_QKV, n, rq, a.h, &M.qkv, &a.tc->xn, GemmW{nullptr, 0, 0, 0, Ly.sqkv, Ly.bqkv},
                   nullptr, 0, a.qkv, rq, none};
         if (rope_fused(a)) {
-            rk = RopeKv{a.pos, a.seq, a.rope, a.kv, l, a.h, a.kvh, a.hd, a.kv_bf16};
+            rk = RopeKv{a.pos, a.seq, a.rope, a.kv, l, a.qd, a.kvh, a.hd, a.kv_bf16};
             j.rk = &rk;
         }
         break;
     case 1:
-        j = TcJob{EPI_RESID, n, a.h, a.qh * a.hd, &M.o, &a.tc->ctx, GemmW{nullptr, 0, 0, 0, Ly.so, nullptr},
-                  a.x, a.h, a.h2, a.h, none};
+        j = part ? TcJob{EPI_QKV, n, a.h, a.qd, &M.o, &a.tc->ctx, GemmW{nullptr, 0, 0, 0, Ly.so, nullptr},
+                         nullptr, 0, part, a.h, none}
+                 : TcJob{EPI_RESID, n, a.h, a.qd, &M.o, &a.tc->ctx, GemmW{nullptr, 0, 0, 0, Ly.so, nullptr},
+                         a.x, a.h, a.h2, a.h, none};
         break;
     case 2:
         j = TcJob{EPI_GU, n, 2 * a.ff, a.h, &M.gu, &a.tc->xn, GemmW{nullptr, 0, 0, 0, Ly.sgu, nullptr},
                   nullptr, 0, a.act, a.ff, act_planes(a)};
         break;
     default:
-        j = TcJob{EPI_RESID, n, a.h, a.ff, &M.down, &a.tc->act, GemmW{nullptr, 0, 0, 0, Ly.sd, nullptr},
-                  a.h2, a.h, a.x, a.h, none};
+        j = part ? TcJob{EPI_QKV, n, a.h, a.ff, &M.down, &a.tc->act, GemmW{nullptr, 0, 0, 0, Ly.sd, nullptr},
+                         nullptr, 0, part, a.h, none}
+                 : TcJob{EPI_RESID, n, a.h, a.ff, &M.down, &a.tc->act, GemmW{nullptr, 0, 0, 0, Ly.sd, nullptr},
+                         a.h2, a.h, a.x, a.h, none};
     }
     return tc_gemm(j, a.err, st);
 }
 
-cudaError_t run_gemm(int which, const PrefillArgs &a, int l, int n, cudaStream_t st) {
-    if (a.tc && !a.tc->layers.empty()) return layer_gemm_tc(which, a, l, n, st);
+cudaError_t run_gemm(int which, const PrefillArgs &a, int l, int n, cudaStream_t st, float *part = nullptr) {
+    if (a.tc && !a.tc->layers.empty()) return layer_gemm_tc(which, a, l, n, part, st);
     const DecodeLayer &Ly = a.layers[l];
-    if (a.wfmt == WF_I8) return layer_gemm<WF_I8>(which, a, Ly, n, st);
-    if (a.wfmt == WF_BF16) return layer_gemm<WF_BF16>(which, a, Ly, n, st);
-    return layer_gemm<WF_F32>(which, a, Ly, n, st);
+    if (a.wfmt == WF_I8) return layer_gemm<WF_I8>(which, a, Ly, n, part, st);
+    if (a.wfmt == WF_BF16) return layer_gemm<WF_BF16>(which, a, Ly, n, part, st);
+    return layer_gemm<WF_F32>(which, a, Ly, n, part, st);
+}
+
+// o_proj (which 1) or down (3) with the tensor-parallel sum: this rank's
+// partial sums into its exchange slot for the next call, then the sum over
+// the ranks plus the residual (R + sum of partials in rank order -> Y).
+cudaError_t run_gemm_tp(int which, const PrefillArgs &a, int l, int n, const float *R, float *Y, cudaStream_t st) {
+    const unsigned q = ++*a.tp_seq;
+    float *part = a.tp->part[a.tp->rank] + (size_t)(q & 1u) * a.tp->rows * a.h;
+    cudaError_t e = run_gemm(which, a, l, n, st, part);
+    if (e != cudaSuccess) return e;
+    return tp_allreduce(*a.tp, q, n, R, Y, a.err, a.tp_timeout_ns, st);
 }
 
 size_t attention_smem(const PrefillArgs &a, int max_pos) { return ((size_t)a.hd + max_pos + 1 + 32) * sizeof(float); }
@@ -817,11 +836,11 @@ cudaError_t attention(const PrefillArgs &a, int n, int l, int max_pos, cudaStrea
                 if (e != cudaSuccess) return e;
                 configured[dev].fetch_or(1u << which);
             }
-            cudaError_t e = launch_pdl(kern, dim3(n, a.kvh, nz), dim3(AT_THREADS), sm, st, a.qkv, a.pos, a.seq, l, a.h,
+            cudaError_t e = launch_pdl(kern, dim3(n, a.kvh, nz), dim3(AT_THREADS), sm, st, a.qkv, a.pos, a.seq, l, a.qd,
                                        a.kvh, a.group, a.kv, a.sqrt_hd, span, a.ctx, ctx_planes(a), a.apart, a.err);
             if (e != cudaSuccess) return e;
             if (nz > 1)
-                return launch_pdl(attn_combine, dim3(n, a.kvh), dim3(128), 0, st, a.apart, nz, a.h, a.kvh, a.hd,
+                return launch_pdl(attn_combine, dim3(n, a.kvh), dim3(128), 0, st, a.apart, nz, a.qd, a.kvh, a.hd,
                                   a.group, a.ctx, ctx_planes(a), a.err);
             return cudaSuccess;
         }
@@ -829,8 +848,8 @@ cudaError_t attention(const PrefillArgs &a, int n, int l, int max_pos, cudaStrea
     const size_t sm = attention_smem(a, max_pos);
     if (a.kv_bf16)
         return launch_pdl(attention_rows<1>, dim3(n * a.qh), dim3(128), sm, st, a.qkv, n, a.pos, a.seq, l, max_pos,
-                          a.h, a.qh, a.kvh, a.hd, a.group, a.kv, a.sqrt_hd, a.ctx, ctx_planes(a), a.err);
-    return launch_pdl(attention_rows<0>, dim3(n * a.qh), dim3(128), sm, st, a.qkv, n, a.pos, a.seq, l, max_pos, a.h,
+                          a.qd, a.qh, a.kvh, a.hd, a.group, a.kv, a.sqrt_hd, a.ctx, ctx_planes(a), a.err);
+    return launch_pdl(attention_rows<0>, dim3(n * a.qh), dim3(128), sm, st, a.qkv, n, a.pos, a.seq, l, max_pos, a.qd,
                       a.qh, a.kvh, a.hd, a.group, a.kv, a.sqrt_hd, a.ctx, ctx_planes(a), a.err);
 }
 
@@ -853,18 +872,18 @@ cudaError_t forward_tokens(const PrefillArgs &a, int n, int max_pos, bool lm_hea
             break;
         if ((e = run_gemm(0, a, l, n, st)) != cudaSuccess) break;
         if (!rope_fused(a) &&
-            (e = launch_pdl(rope_kv, dim3(rows_grid), dim3(128), 0, st, a.qkv, n, a.pos, a.seq, l, a.h, a.qh, a.kvh,
+            (e = launch_pdl(rope_kv, dim3(rows_grid), dim3(128), 0, st, a.qkv, n, a.pos, a.seq, l, a.qd, a.qh, a.kvh,
                             a.hd, a.rope, a.kv, a.kv_bf16, a.err)) !=
                 cudaSuccess)
             break;
         if ((e = attention(a, n, l, max_pos, st)) != cudaSuccess) break;
         if ((e = cudaGetLastError()) != cudaSuccess) break;
         if (l + 1 == a.L && !lm_head) break;  // the last layer's MLP feeds only the logits
-        if ((e = run_gemm(1, a, l, n, st)) != cudaSuccess) break;
+        if ((e = a.tp ? run_gemm_tp(1, a, l, n, a.x, a.h2, st) : run_gemm(1, a, l, n, st)) != cudaSuccess) break;
         if ((e = rmsnorm(a.h2, Ly.ffn_norm, a.xn, xn_planes(a), n, a.h, a.eps, a.err, st)) != cudaSuccess)
             break;
         if ((e = run_gemm(2, a, l, n, st)) != cudaSuccess) break;
-        if ((e = run_gemm(3, a, l, n, st)) != cudaSuccess) break;
+        if ((e = a.tp ? run_gemm_tp(3, a, l, n, a.h2, a.x, st) : run_gemm(3, a, l, n, st)) != cudaSuccess) break;
     }
     if (e != cudaSuccess || !lm_head) return e;
     // Final norm, the LM head (tied table or untied head) and the argmax.
@@ -883,6 +902,7 @@ cudaError_t forward_tokens(const PrefillArgs &a, int n, int max_pos, bool lm_hea
         e = gemm<WF_F32, EPI_PLAIN>(a, a.xn, a.h, n, a.V, a.h, w, nullptr, 0, a.logits, a.V, none, st);
     }
     if (e != cudaSuccess) return e;
+    if (a.tp) return tp_argmax(*a.tp, ++*a.tp_seq, a.logits, n, a.V, a.v0, a.amax, a.err, a.tp_timeout_ns, st);
     if (am_tiles > 0) return launch_pdl(argmax_tiles, dim3(n), dim3(32), 0, st, a.amv, a.ami, am_tiles, n, a.V, a.amax);
     return launch_pdl(argmax_rows, dim3(rows_grid), dim3(256), 0, st, a.logits, n, a.V, a.amax, a.err);
 }

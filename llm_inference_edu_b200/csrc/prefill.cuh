@@ -7,6 +7,7 @@
 #include <stddef.h>
 
 #include "decode.cuh"
+#include "tp.cuh"
 
 namespace qb {
 
@@ -35,7 +36,12 @@ struct KvPages {
 // weights are in the decode layout; its KV pointers are ignored: the cache
 // is `kv`.
 struct PrefillArgs {
+    // With tensor parallelism (tp set) the model is one rank's shard: qh
+    // query heads of head_dim (qd = qh * hd query rows, the context width),
+    // kvh KV heads (group = qh / kvh query heads each), ff FFN columns and
+    // V LM-head rows starting at global id v0; h is always the full width.
     int V, L, h, qh, kvh, hd, ff, cap, group;
+    int qd, v0;
     int wfmt, tfmt, kv_bf16;
     float eps, sqrt_hd;
     size_t sh, shd, sff, semb;
@@ -72,6 +78,12 @@ struct PrefillArgs {
     size_t apart_floats;
     float *amv;
     int *ami;
+    // Tensor parallelism (HOST pointers; tp null without it): the ranks'
+    // exchange buffers and the communicator's call counter (every rank makes
+    // the same calls in the same order).
+    const TpPeers *tp;
+    unsigned *tp_seq;
+    unsigned long long tp_timeout_ns;
 };
 
 // True when the shapes suit the multi-token kernels (else callers evaluate

@@ -20,6 +20,7 @@
 #include "decode.cuh"
 #include "prefill.cuh"
 #include "tc_gemm.cuh"
+#include "tp.cuh"
 
 namespace qb {
 int decode_max_ctas(int wfmt, int tfmt, int kv_bf16, size_t smem);
@@ -136,6 +137,12 @@ struct LayerStore {
 struct Model {
     qb_model_config c{};
     int device = 0;
+    // Tensor-parallel shard (tp_size 1: the whole model): query heads
+    // [head0, head0 + nq), KV heads [kv0, kv0 + nkv), FFN columns
+    // [f0, f0 + nff) and LM-head rows [v0, v0 + nv); the embedding table and
+    // the norms are whole on every rank.
+    int tp_rank = 0, tp_size = 1;
+    size_t head0 = 0, nq = 0, kv0 = 0, nkv = 0, f0 = 0, nff = 0, v0 = 0, nv = 0;
     uint32_t lin = QB_LINEAR_F32, tab = QB_TABLE_F32;
     size_t sh = 0, shd = 0, sff = 0, semb = 0;
     DevBuf emb, head, final_norm;
@@ -146,8 +153,41 @@ struct Model {
     int wf() const { return lin == QB_LINEAR_INT8_ROW ? WF_I8 : (lin == QB_LINEAR_BF16 ? WF_BF16 : WF_F32); }
     size_t esz() const { return lin == QB_LINEAR_INT8_ROW ? 1 : (lin == QB_LINEAR_BF16 ? 2 : 4); }
     size_t tesz() const { return tab == QB_TABLE_BF16 ? 2 : 4; }
-    size_t kv() const { return c.kv_heads * c.head_dim; }
+    size_t kv() const { return nkv * c.head_dim; }   // this shard's K (or V) rows
+    size_t qd() const { return nq * c.head_dim; }    // this shard's Q rows
 };
+
+// The shard of rank `rank` of `size`: KV heads split evenly when size <=
+// kv_heads; beyond that each KV head (and its group of query heads) is
+// replicated on size / kv_heads ranks that split the group's query heads
+// (sizes differ by at most one, e.g. 4 and 3 of 7); FFN columns split
+// evenly; LM-head rows split in whole 128-row tiles.  False when the shape
+// does not split this way.
+static bool tp_split(const qb_model_config &c, int rank, int size, Model &m) {
+    const size_t qh = c.query_heads, kvh = c.kv_heads, grp = qh / kvh, ff = c.ff_dim, V = c.vocab_size;
+    if (size < 1 || size > kMaxTp || rank < 0 || rank >= size) return false;
+    const size_t S = (size_t)size, r = (size_t)rank;
+    if (S <= kvh) {
+        if (kvh % S) return false;
+        m.nkv = kvh / S; m.kv0 = r * m.nkv; m.nq = m.nkv * grp; m.head0 = m.kv0 * grp;
+    } else {
+        if (S % kvh || S / kvh > grp) return false;
+        const size_t per_g = S / kvh, g = r / per_g, j = r % per_g, base = grp / per_g, extra = grp % per_g;
+        m.kv0 = g; m.nkv = 1;
+        m.nq = base + (j < extra ? 1 : 0);
+        m.head0 = g * grp + j * base + std::min(j, extra);
+    }
+    if (ff % S || (ff / S) % 4) return false;
+    m.nff = ff / S; m.f0 = r * m.nff;
+    const size_t tiles = (V + 127) / 128, per = tiles / S, extra = tiles % S;
+    const size_t t0 = r * per + std::min(r, extra), nt = per + (r < extra ? 1 : 0);
+    if (nt == 0) return false;
+    m.v0 = t0 * 128;
+    m.nv = std::min(V, (t0 + nt) * 128) - m.v0;
+    m.tp_rank = rank;
+    m.tp_size = size;
+    return true;
+}
 
 static std::mutex g_mu;
 static uint64_t g_next = 1;
@@ -223,10 +263,36 @@ static uint32_t store_linear(const Model &m, const float *src, size_t rows, size
     return QB_OK;
 }
 
-// o_proj in head-blocked form: block hh holds columns [hh*hd, (hh+1)*hd) of
-// every row, so one head's partial product streams a contiguous block.
+// Columns [c0, c0 + nc) of a row-major [rows, cols] FP32 source, each row
+// quantized (INT8) over all its columns, as the whole matrix would be.
+static uint32_t store_linear_cols(const Model &m, const float *src, size_t rows, size_t cols, size_t c0, size_t nc,
+                                  uint8_t *dst, size_t stride, float *scales) {
+    if (c0 == 0 && nc == cols) return store_linear(m, src, rows, cols, dst, stride, scales, 1);
+    const int wf = m.wf();
+    uint32_t s;
+    if (wf == WF_I8) {
+        DevBuf q, sc;
+        if ((s = q.alloc(rows * cols, false)) || (s = sc.alloc(rows * 4, false))) return s;
+        s = qb_quantize_int8(src, rows * cols, rows, cols, cols, q.as<int8_t>(), sc.as<float>(), nullptr);
+        if (s) return s == QB_NONFINITE_WEIGHT ? QB_NONFINITE : s;
+        relayout_kernel<<<gridn(rows * nc), 256>>>(nullptr, q.as<int8_t>(), rows, cols, c0, nc, dst, stride, WF_I8);
+        QB_CUDA(cudaGetLastError());
+        QB_CUDA(cudaMemcpy(scales, sc.p, rows * 4, cudaMemcpyDeviceToDevice));
+    } else {
+        size_t idx;
+        if ((s = check_finite_dev(src, rows * cols, &idx))) { set_detail(0, 0, 0, idx); return s; }
+        relayout_kernel<<<gridn(rows * nc), 256>>>(src, nullptr, rows, cols, c0, nc, dst, stride, wf);
+        QB_CUDA(cudaGetLastError());
+    }
+    QB_CUDA(cudaDeviceSynchronize());
+    return QB_OK;
+}
+
+// o_proj in head-blocked form: block i holds the columns of query head
+// head0 + i ([hh*hd, (hh+1)*hd)) of every row, so one head's partial
+// product streams a contiguous block; a shard keeps its own heads' blocks.
 static uint32_t store_o_proj(Model &m, LayerStore &L, const float *src) {
-    const size_t h = m.c.hidden_dim, hd = m.c.head_dim, qh = m.c.query_heads;
+    const size_t h = m.c.hidden_dim, hd = m.c.head_dim, qh = m.nq;
     const int wf = m.wf();
     uint32_t s;
     if (wf == WF_I8) {
@@ -235,14 +301,14 @@ static uint32_t store_o_proj(Model &m, LayerStore &L, const float *src) {
         s = qb_quantize_int8(src, h * h, h, h, h, q.as<int8_t>(), sc.as<float>(), nullptr);
         if (s) return s == QB_NONFINITE_WEIGHT ? QB_NONFINITE : s;
         for (size_t hh = 0; hh < qh; ++hh)
-            relayout_kernel<<<gridn(h * hd), 256>>>(nullptr, q.as<int8_t>(), h, h, hh * hd, hd,
+            relayout_kernel<<<gridn(h * hd), 256>>>(nullptr, q.as<int8_t>(), h, h, (m.head0 + hh) * hd, hd,
                                                     L.wo.as<uint8_t>() + hh * h * m.shd, m.shd, WF_I8);
         QB_CUDA(cudaMemcpy(L.so.p, sc.p, h * 4, cudaMemcpyDeviceToDevice));
     } else {
         size_t idx;
         if ((s = check_finite_dev(src, h * h, &idx))) { set_detail(0, 0, 0, idx); return s; }
         for (size_t hh = 0; hh < qh; ++hh)
-            relayout_kernel<<<gridn(h * hd), 256>>>(src, nullptr, h, h, hh * hd, hd,
+            relayout_kernel<<<gridn(h * hd), 256>>>(src, nullptr, h, h, (m.head0 + hh) * hd, hd,
                                                     L.wo.as<uint8_t>() + hh * h * m.shd, m.shd, wf);
     }
     QB_CUDA(cudaGetLastError());
@@ -336,16 +402,21 @@ static uint32_t build_rope(const qb_model_config &c, size_t cap, DevBuf &out) {
 // positions per sequence.
 static void prefill_common(const Model &m, size_t cap, int kv_bf16, PrefillArgs &a) {
     const qb_model_config &c = m.c;
-    a.V = (int)c.vocab_size; a.L = (int)c.layers; a.h = (int)c.hidden_dim; a.qh = (int)c.query_heads;
-    a.kvh = (int)c.kv_heads; a.hd = (int)c.head_dim; a.ff = (int)c.ff_dim; a.cap = (int)cap;
-    a.group = (int)(c.query_heads / c.kv_heads);
+    a.V = (int)m.nv; a.L = (int)c.layers; a.h = (int)c.hidden_dim; a.qh = (int)m.nq;
+    a.kvh = (int)m.nkv; a.hd = (int)c.head_dim; a.ff = (int)m.nff; a.cap = (int)cap;
+    a.group = (int)(m.nq / m.nkv);
+    a.qd = (int)m.qd(); a.v0 = (int)m.v0;
     a.wfmt = m.wf(); a.tfmt = m.tab == QB_TABLE_BF16 ? WF_BF16 : WF_F32; a.kv_bf16 = kv_bf16;
     a.eps = c.norm_epsilon; a.sqrt_hd = sqrtf((float)c.head_dim);
     a.sh = m.sh; a.shd = m.shd; a.sff = m.sff; a.semb = m.semb;
     a.emb = m.emb.as<uint8_t>();
-    a.head = m.head_set ? m.head.as<uint8_t>() : m.emb.as<uint8_t>();
+    // A shard's LM head: its rows of the untied head, or of the tied table.
+    a.head = m.head_set ? m.head.as<uint8_t>() : m.emb.as<uint8_t>() + m.v0 * m.semb;
     a.final_norm = m.final_norm.as<float>();
-    a.kv.kvh = (int)c.kv_heads;
+    a.tp = nullptr;
+    a.tp_seq = nullptr;
+    a.tp_timeout_ns = 2000000000ull;
+    a.kv.kvh = (int)m.nkv;
     a.kv.hd = (int)c.head_dim;
 }
 
@@ -354,16 +425,16 @@ static void prefill_common(const Model &m, size_t cap, int kv_bf16, PrefillArgs 
 // sequences, the error word and the BF16 input planes of the tensor-core
 // GEMMs.
 static uint32_t prefill_workspace(const Model &m, int chunk, DevBuf &ws, PrefillArgs &a) {
-    const size_t h = m.c.hidden_dim, ff = m.c.ff_dim, rq = h + 2 * m.kv(), ch = (size_t)chunk;
+    const size_t h = m.c.hidden_dim, ff = m.nff, rq = m.qd() + 2 * m.kv(), ch = (size_t)chunk;
     const size_t part = 4 * ch * std::max(rq, h);
     const size_t floats = ch * (4 * h + rq + ff) + part + 3 * ch + 64;
     const size_t fbytes = round16(floats * 4);
     const size_t hp = round16((size_t)TC_NP * ch * h * 2), fp = round16((size_t)TC_NP * ch * ff * 2);
     // Attention split partials: every row's full-length splits plus room for
     // the extra splits of small row counts; greedy partials per 128-row tile.
-    const size_t kvh = m.c.kv_heads, grp = m.c.query_heads / kvh, hd = m.c.head_dim;
+    const size_t kvh = m.nkv, grp = m.nq / kvh, hd = m.c.head_dim;
     const size_t apart = (ch * kvh * ((a.cap + 1023) / 1024) + 600) * grp * (hd + 2);
-    const size_t am = ((m.c.vocab_size + 127) / 128) * ch;
+    const size_t am = ((m.nv + 127) / 128) * ch;
     const size_t abytes = round16(apart * 4), ambytes = round16(am * 4);
     if (!ws.p) {
         uint32_t st = ws.alloc(fbytes + 2 * hp + fp + abytes + 2 * ambytes);
@@ -393,12 +464,12 @@ static void tc_prepare(const Model &m, PrefillArgs &a, TcMaps &maps) {
     a.tc = nullptr;
     maps.layers.clear();
     maps.head.wf = -1;
-    if (!tc_encode_planes(maps.xn, a.xnp, a.h, a.chunk) || !tc_encode_planes(maps.ctx, a.ctxp, a.h, a.chunk) ||
-        !tc_encode_planes(maps.act, a.actp, a.ff, a.chunk) || a.qh * a.hd != a.h)
+    if (!tc_encode_planes(maps.xn, a.xnp, a.h, a.chunk) || !tc_encode_planes(maps.ctx, a.ctxp, a.qd, a.chunk) ||
+        !tc_encode_planes(maps.act, a.actp, a.ff, a.chunk))
         return;
     const int wf = m.wf();
     if (wf == WF_I8 || wf == WF_BF16) {
-        const size_t h = a.h, ff = a.ff, rq = h + 2 * (size_t)a.kvh * a.hd;
+        const size_t h = a.h, ff = a.ff, rq = (size_t)a.qd + 2 * (size_t)a.kvh * a.hd;
         maps.layers.resize(a.L);
         bool ok = true;
         for (int l = 0; l < a.L && ok; ++l) {
@@ -793,6 +864,31 @@ static void generation_reset(Generation &g) {
 }
 
 
+// ------------------------------------------------------ tp communicator ----
+
+// One rank's exchange buffer and its view of every rank's (CUDA IPC).
+struct Comm {
+    int device = 0, rank = 0, size = 1, rows = 0, h = 0;
+    DevBuf buf;
+    void *peer_base[kMaxTp] = {};  // opened IPC mappings (null for this rank)
+    bool connected = false;
+    TpPeers view{};
+    unsigned seq = 0;  // exchange calls made (every rank makes the same ones)
+    ~Comm() {
+        DeviceGuard dg(device);
+        for (int r = 0; r < kMaxTp; ++r)
+            if (peer_base[r]) cudaIpcCloseMemHandle(peer_base[r]);
+    }
+};
+
+static std::map<uint64_t, std::shared_ptr<Comm>> g_comms;
+
+static std::shared_ptr<Comm> find_comm(uint64_t h) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = g_comms.find(h);
+    return it == g_comms.end() ? nullptr : it->second;
+}
+
 // ----------------------------------------------------------- batch ----
 
 // B independent sequences decoded in lockstep with the multi-token kernels
@@ -810,6 +906,7 @@ struct Batch {
     TcMaps tcm;
     PrefillArgs a{};
     bool logits_valid = false;
+    std::shared_ptr<Comm> comm;  // tensor-parallel batches
     ~Batch() {
         DeviceGuard dg(device);
         if (stream) cudaStreamDestroy(stream);
@@ -844,7 +941,7 @@ static uint32_t batch_check(Batch &b) {
     cudaError_t e = cudaMemcpyAsync(&herr, b.a.err, sizeof(unsigned), cudaMemcpyDeviceToHost, b.stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(b.stream);
     if (e != cudaSuccess) return batch_fail(b, cuda_status(e));
-    if (herr) return batch_fail(b, QB_NONFINITE);
+    if (herr) return batch_fail(b, (herr & ERR_TIMEOUT) ? QB_DEVICE_TIMEOUT : QB_NONFINITE);
     return QB_OK;
 }
 
@@ -856,8 +953,8 @@ extern "C" {
 
 // ---------------------------------------------------------------- model ----
 
-uint32_t qb_model_create(const qb_model_config *cfg, uint32_t linear_format, uint32_t table_format,
-                         int device, uint64_t *out) {
+static uint32_t model_create(const qb_model_config *cfg, uint32_t linear_format, uint32_t table_format,
+                             int device, int tp_rank, int tp_size, uint64_t *out) {
     clear_detail();
     if (!cfg || !out) return QB_INVALID_PARAMETERS;
     const qb_model_config c = *cfg;
@@ -882,20 +979,21 @@ uint32_t qb_model_create(const qb_model_config *cfg, uint32_t linear_format, uin
     }
     auto m = std::make_shared<Model>();
     m->c = c;
+    if (!tp_split(c, tp_rank, tp_size, *m)) return QB_UNSUPPORTED;
     m->device = device;
     m->lin = linear_format;
     m->tab = table_format;
     m->sh = round16(c.hidden_dim * m->esz());
     m->shd = round16(c.head_dim * m->esz());
-    m->sff = round16(c.ff_dim * m->esz());
+    m->sff = round16(m->nff * m->esz());
     m->semb = round16(c.hidden_dim * m->tesz());
     m->layers.resize(c.layers);
     DeviceGuard dg(device);
-    const size_t h = c.hidden_dim, kv = m->kv(), ff = c.ff_dim, rq = h + 2 * kv;
+    const size_t h = c.hidden_dim, kv = m->kv(), ff = m->nff, rq = m->qd() + 2 * kv;
     uint32_t s;
     for (auto &L : m->layers) {
         if ((s = L.wqkv.alloc(rq * m->sh)) || (s = L.sqkv.alloc(rq * 4)) || (s = L.bqkv.alloc(rq * 4)) ||
-            (s = L.wo.alloc(c.query_heads * h * m->shd)) || (s = L.so.alloc(h * 4)) ||
+            (s = L.wo.alloc(m->nq * h * m->shd)) || (s = L.so.alloc(h * 4)) ||
             (s = L.wgu.alloc(2 * ff * m->sh)) || (s = L.sgu.alloc(2 * ff * 4)) ||
             (s = L.down.w.alloc(h * m->sff)) || (s = L.down.scales.alloc(h * 4)) ||
             (s = L.attn_norm.alloc(h * 4)) || (s = L.ffn_norm.alloc(h * 4)))
@@ -910,6 +1008,38 @@ uint32_t qb_model_create(const qb_model_config *cfg, uint32_t linear_format, uin
     return QB_OK;
 }
 
+uint32_t qb_model_create(const qb_model_config *cfg, uint32_t linear_format, uint32_t table_format,
+                         int device, uint64_t *out) {
+    return model_create(cfg, linear_format, table_format, device, 0, 1, out);
+}
+
+uint32_t qb_model_create_tp(const qb_model_config *cfg, uint32_t linear_format, uint32_t table_format,
+                            int device, int tp_rank, int tp_size, uint64_t *out) {
+    return model_create(cfg, linear_format, table_format, device, tp_rank, tp_size, out);
+}
+
+uint32_t qb_tp_shard_of(const qb_model_config *cfg, int tp_rank, int tp_size, qb_tp_shard *out) {
+    if (!cfg || !out) return QB_INVALID_PARAMETERS;
+    if (!cfg->query_heads || !cfg->kv_heads || cfg->query_heads % cfg->kv_heads || !cfg->vocab_size)
+        return QB_INVALID_CONFIG;
+    Model m;
+    if (!tp_split(*cfg, tp_rank, tp_size, m)) return QB_UNSUPPORTED;
+    out->rank = m.tp_rank; out->size = m.tp_size;
+    out->head0 = m.head0; out->heads = m.nq; out->kv_head0 = m.kv0; out->kv_heads = m.nkv;
+    out->ff0 = m.f0; out->ff = m.nff; out->vocab0 = m.v0; out->vocab = m.nv;
+    return QB_OK;
+}
+
+uint32_t qb_model_tp_info(uint64_t model, qb_tp_shard *out) {
+    auto m = find_model(model);
+    if (!m) return QB_INVALID_HANDLE;
+    if (!out) return QB_INVALID_PARAMETERS;
+    out->rank = m->tp_rank; out->size = m->tp_size;
+    out->head0 = m->head0; out->heads = m->nq; out->kv_head0 = m->kv0; out->kv_heads = m->nkv;
+    out->ff0 = m->f0; out->ff = m->nff; out->vocab0 = m->v0; out->vocab = m->nv;
+    return QB_OK;
+}
+
 uint32_t qb_model_set_tensor(uint64_t model, int64_t layer, uint32_t tensor, uint32_t dtype,
                              const void *data, size_t n) {
     clear_detail();
@@ -918,7 +1048,11 @@ uint32_t qb_model_set_tensor(uint64_t model, int64_t layer, uint32_t tensor, uin
     if (m->finalized) return QB_INVALID_STATE;
     if (!data || (dtype != QB_HOST_F32 && dtype != QB_HOST_BF16)) return QB_INVALID_PARAMETERS;
     const qb_model_config &c = m->c;
-    const size_t h = c.hidden_dim, kv = m->kv(), ff = c.ff_dim, V = c.vocab_size;
+    // Full tensors are passed (every rank of a sharded model reads the same
+    // ones); each stores its shard: kvf / ff / V are the full sizes, qd / kv
+    // / nff / nv the shard's.
+    const size_t h = c.hidden_dim, hd = c.head_dim, kvf = c.kv_heads * hd, ff = c.ff_dim, V = c.vocab_size;
+    const size_t qd = m->qd(), kv = m->kv(), q0 = m->head0 * hd, k0 = m->kv0 * hd;
     DeviceGuard dg(m->device);
     size_t expected = 0;
     bool global = tensor <= QB_T_FINAL_NORM;
@@ -927,9 +1061,9 @@ uint32_t qb_model_set_tensor(uint64_t model, int64_t layer, uint32_t tensor, uin
     switch (tensor) {
     case QB_T_EMBEDDING: case QB_T_LM_HEAD: expected = V * h; break;
     case QB_T_FINAL_NORM: case QB_T_ATTN_NORM: case QB_T_FFN_NORM: case QB_T_Q_BIAS: expected = h; break;
-    case QB_T_K_BIAS: case QB_T_V_BIAS: expected = kv; break;
+    case QB_T_K_BIAS: case QB_T_V_BIAS: expected = kvf; break;
     case QB_T_Q: case QB_T_O: expected = h * h; break;
-    case QB_T_K: case QB_T_V: expected = kv * h; break;
+    case QB_T_K: case QB_T_V: expected = kvf * h; break;
     case QB_T_GATE: case QB_T_UP: case QB_T_DOWN: expected = ff * h; break;
     default: return QB_INVALID_PARAMETERS;
     }
@@ -943,16 +1077,17 @@ uint32_t qb_model_set_tensor(uint64_t model, int64_t layer, uint32_t tensor, uin
         tensor == QB_T_Q_BIAS || tensor == QB_T_K_BIAS || tensor == QB_T_V_BIAS) {
         if ((s = host_vector_finite(data, n, dtype, hv))) return s;
         float *dst = nullptr;
+        size_t from = 0, cnt = n;  // the shard's part of a bias
         if (tensor == QB_T_FINAL_NORM) { dst = m->final_norm.as<float>(); m->fn_set = true; }
         else {
             LayerStore &L = m->layers[layer];
             if (tensor == QB_T_ATTN_NORM) { dst = L.attn_norm.as<float>(); L.an = true; }
             else if (tensor == QB_T_FFN_NORM) { dst = L.ffn_norm.as<float>(); L.fn = true; }
-            else if (tensor == QB_T_Q_BIAS) dst = L.bqkv.as<float>();
-            else if (tensor == QB_T_K_BIAS) dst = L.bqkv.as<float>() + h;
-            else dst = L.bqkv.as<float>() + h + kv;
+            else if (tensor == QB_T_Q_BIAS) { dst = L.bqkv.as<float>(); from = q0; cnt = qd; }
+            else if (tensor == QB_T_K_BIAS) { dst = L.bqkv.as<float>() + qd; from = k0; cnt = kv; }
+            else { dst = L.bqkv.as<float>() + qd + kv; from = k0; cnt = kv; }
         }
-        QB_CUDA(cudaMemcpy(dst, hv.data(), n * 4, cudaMemcpyHostToDevice));
+        QB_CUDA(cudaMemcpy(dst, hv.data() + from, cnt * 4, cudaMemcpyHostToDevice));
         return QB_OK;
     }
     DevBuf src;
@@ -961,9 +1096,11 @@ uint32_t qb_model_set_tensor(uint64_t model, int64_t layer, uint32_t tensor, uin
         size_t idx;
         if ((s = check_finite_dev(src.as<float>(), n, &idx))) { set_detail(tensor, 0, 0, idx); return s; }
         DevBuf *dst = tensor == QB_T_EMBEDDING ? &m->emb : &m->head;
-        if (tensor == QB_T_LM_HEAD && (s = m->head.alloc(V * m->semb))) return s;
-        relayout_kernel<<<gridn(n), 256>>>(src.as<float>(), nullptr, V, h, 0, h, dst->as<uint8_t>(), m->semb,
-                                           m->tab == QB_TABLE_BF16 ? WF_BF16 : WF_F32);
+        // The embedding is whole; an untied head keeps the shard's rows.
+        const size_t r0 = tensor == QB_T_LM_HEAD ? m->v0 : 0, nr = tensor == QB_T_LM_HEAD ? m->nv : V;
+        if (tensor == QB_T_LM_HEAD && (s = m->head.alloc(nr * m->semb))) return s;
+        relayout_kernel<<<gridn(nr * h), 256>>>(src.as<float>() + r0 * h, nullptr, nr, h, 0, h, dst->as<uint8_t>(),
+                                                m->semb, m->tab == QB_TABLE_BF16 ? WF_BF16 : WF_F32);
         QB_CUDA(cudaGetLastError());
         QB_CUDA(cudaDeviceSynchronize());
         if (tensor == QB_T_EMBEDDING) m->emb_set = true; else m->head_set = true;
@@ -972,16 +1109,17 @@ uint32_t qb_model_set_tensor(uint64_t model, int64_t layer, uint32_t tensor, uin
     LayerStore &L = m->layers[layer];
     switch (tensor) {
     case QB_T_Q:
-        s = store_linear(*m, src.as<float>(), h, h, L.wqkv.as<uint8_t>(), m->sh, L.sqkv.as<float>(), 1);
+        s = store_linear(*m, src.as<float>() + q0 * h, qd, h, L.wqkv.as<uint8_t>(), m->sh, L.sqkv.as<float>(), 1);
         if (!s) L.q = true;
         break;
     case QB_T_K:
-        s = store_linear(*m, src.as<float>(), kv, h, L.wqkv.as<uint8_t>() + h * m->sh, m->sh, L.sqkv.as<float>() + h, 1);
+        s = store_linear(*m, src.as<float>() + k0 * h, kv, h, L.wqkv.as<uint8_t>() + qd * m->sh, m->sh,
+                         L.sqkv.as<float>() + qd, 1);
         if (!s) L.k = true;
         break;
     case QB_T_V:
-        s = store_linear(*m, src.as<float>(), kv, h, L.wqkv.as<uint8_t>() + (h + kv) * m->sh, m->sh,
-                         L.sqkv.as<float>() + h + kv, 1);
+        s = store_linear(*m, src.as<float>() + k0 * h, kv, h, L.wqkv.as<uint8_t>() + (qd + kv) * m->sh, m->sh,
+                         L.sqkv.as<float>() + qd + kv, 1);
         if (!s) L.v = true;
         break;
     case QB_T_O:
@@ -989,16 +1127,18 @@ uint32_t qb_model_set_tensor(uint64_t model, int64_t layer, uint32_t tensor, uin
         if (!s) L.o = true;
         break;
     case QB_T_GATE:
-        s = store_linear(*m, src.as<float>(), ff, h, L.wgu.as<uint8_t>(), 2 * m->sh, L.sgu.as<float>(), 2);
+        s = store_linear(*m, src.as<float>() + m->f0 * h, m->nff, h, L.wgu.as<uint8_t>(), 2 * m->sh,
+                         L.sgu.as<float>(), 2);
         if (!s) L.gate = true;
         break;
     case QB_T_UP:
-        s = store_linear(*m, src.as<float>(), ff, h, L.wgu.as<uint8_t>() + m->sh, 2 * m->sh,
+        s = store_linear(*m, src.as<float>() + m->f0 * h, m->nff, h, L.wgu.as<uint8_t>() + m->sh, 2 * m->sh,
                          L.sgu.as<float>() + 1, 2);
         if (!s) L.up = true;
         break;
     case QB_T_DOWN:
-        s = store_linear(*m, src.as<float>(), h, ff, L.down.w.as<uint8_t>(), m->sff, L.down.scales.as<float>(), 1);
+        s = store_linear_cols(*m, src.as<float>(), h, ff, m->f0, m->nff, L.down.w.as<uint8_t>(), m->sff,
+                              L.down.scales.as<float>());
         if (!s) L.down.set = true;
         break;
     }
@@ -1035,7 +1175,8 @@ uint32_t qb_model_finalize(uint64_t model) {
     // INT8 1 B + 4 B per row scale), plus FP32 norms and biases; the tied
     // table counts once (src/model.rs:347-385).
     const qb_model_config &c = m->c;
-    const size_t h = c.hidden_dim, kv = m->kv(), ff = c.ff_dim;
+    // (the whole model's payload, also for a shard)
+    const size_t h = c.hidden_dim, kv = c.kv_heads * c.head_dim, ff = c.ff_dim;
     size_t mats = h * h * 2 + kv * h * 2 + ff * h * 3;
     size_t rows = h + 2 * kv + h + 2 * ff + h;
     size_t per = i8 ? mats + rows * 4 : mats * m->esz();
@@ -1125,6 +1266,7 @@ static uint32_t session_create(uint64_t model, size_t capacity, uint32_t kv_dtyp
     auto m = find_model(model);
     if (!m) return QB_INVALID_HANDLE;
     if (!m->finalized) return QB_INVALID_STATE;
+    if (m->tp_size > 1) return QB_UNSUPPORTED;  // shards decode through qb_batch_create_tp
     const qb_model_config &c = m->c;
     if (capacity == 0 || capacity > c.max_tokens) return QB_INVALID_CAPACITY;
     if (kv_dtype > QB_KV_BF16) return QB_INVALID_PARAMETERS;
@@ -1504,12 +1646,23 @@ uint32_t qb_generation_free(uint64_t gen) {
 
 // ----------------------------------------------------------- batch ABI ----
 
-uint32_t qb_batch_create(uint64_t model, size_t sequences, size_t capacity, uint32_t kv_dtype, uint64_t *out) {
+static uint32_t batch_create(uint64_t model, uint64_t comm, size_t sequences, size_t capacity, uint32_t kv_dtype,
+                             uint64_t *out) {
     clear_detail();
     auto m = find_model(model);
     if (!m) return QB_INVALID_HANDLE;
     if (!m->finalized) return QB_INVALID_STATE;
     if (!out) return QB_INVALID_PARAMETERS;
+    std::shared_ptr<Comm> cm;
+    if (comm) {
+        cm = find_comm(comm);
+        if (!cm) return QB_INVALID_HANDLE;
+        if (!cm->connected || cm->rank != m->tp_rank || cm->size != m->tp_size || cm->device != m->device ||
+            cm->h != (int)m->c.hidden_dim)
+            return QB_INVALID_PARAMETERS;
+    } else if (m->tp_size > 1) {
+        return QB_INVALID_PARAMETERS;  // a shard decodes only with its communicator
+    }
     if (sequences == 0 || capacity == 0 || capacity > m->c.max_tokens) return QB_INVALID_CAPACITY;
     if (kv_dtype > QB_KV_BF16) return QB_INVALID_PARAMETERS;
     auto b = std::make_shared<Batch>();
@@ -1524,6 +1677,7 @@ uint32_t qb_batch_create(uint64_t model, size_t sequences, size_t capacity, uint
     const int chunk = (int)std::max<size_t>(sequences, 256);
     a.chunk = chunk;
     if (!prefill_supported(a) || sequences > (1u << 20)) return QB_UNSUPPORTED;
+    if (cm && cm->rows < chunk) return QB_INVALID_PARAMETERS;
     // One page pool per layer for all sequences; the table interleaves the
     // sequences' pages (sequence s's page j is pool page j B + s).
     const size_t pps = pages_per_seq(capacity), npages = pps * sequences;
@@ -1543,7 +1697,7 @@ uint32_t qb_batch_create(uint64_t model, size_t sequences, size_t capacity, uint
     }
     if ((st = b->kv.alloc(kvb)) || (st = build_rope(m->c, capacity, b->rope)) ||
         (st = prefill_workspace(*m, chunk, b->ws, a)) ||
-        (st = b->logits.alloc(sequences * m->c.vocab_size * 4, false)) || (st = b->amax.alloc(sequences * 4)))
+        (st = b->logits.alloc(sequences * m->nv * 4, false)) || (st = b->amax.alloc(sequences * 4)))
         return st == QB_CUDA_ERROR ? QB_ALLOCATION : st;
     b->hlayers.resize(m->c.layers);
     QB_CUDA(cudaMemcpy(b->hlayers.data(), m->dlayers.p, m->c.layers * sizeof(DecodeLayer), cudaMemcpyDeviceToHost));
@@ -1556,10 +1710,102 @@ uint32_t qb_batch_create(uint64_t model, size_t sequences, size_t capacity, uint
     a.kv.pps = (int)pps;
     a.logits = b->logits.as<float>();
     a.amax = b->amax.as<uint32_t>();
+    if (cm) {
+        b->comm = cm;
+        a.tp = &cm->view;
+        a.tp_seq = &cm->seq;
+    }
     std::lock_guard<std::mutex> lk(g_mu);
     uint64_t id = g_next++;
     g_batches[id] = b;
     *out = id;
+    return QB_OK;
+}
+
+uint32_t qb_batch_create(uint64_t model, size_t sequences, size_t capacity, uint32_t kv_dtype, uint64_t *out) {
+    return batch_create(model, 0, sequences, capacity, kv_dtype, out);
+}
+
+uint32_t qb_batch_create_tp(uint64_t model, uint64_t comm, size_t sequences, size_t capacity, uint32_t kv_dtype,
+                            uint64_t *out) {
+    if (!comm) return QB_INVALID_HANDLE;
+    return batch_create(model, comm, sequences, capacity, kv_dtype, out);
+}
+
+// ------------------------------------------------------------- tp ABI ----
+
+uint32_t qb_tp_comm_create(int device, size_t rows, size_t hidden, uint64_t *out) {
+    clear_detail();
+    if (!out || rows == 0 || hidden == 0 || hidden % 4 || rows > (1u << 20) || hidden > 0xffffff)
+        return QB_INVALID_PARAMETERS;
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev) {
+        cudaGetLastError();
+        return QB_CUDA_ERROR;
+    }
+    auto c = std::make_shared<Comm>();
+    c->device = device;
+    c->rows = (int)rows;
+    c->h = (int)hidden;
+    DeviceGuard dg(device);
+    uint32_t st = c->buf.alloc(tp_buffer_bytes(c->rows, c->h));  // zeroed: no flag is up
+    if (st) return st == QB_CUDA_ERROR ? QB_ALLOCATION : st;
+    std::lock_guard<std::mutex> lk(g_mu);
+    uint64_t id = g_next++;
+    g_comms[id] = c;
+    *out = id;
+    return QB_OK;
+}
+
+uint32_t qb_tp_comm_handle(uint64_t comm, void *out, size_t len) {
+    auto c = find_comm(comm);
+    if (!c) return QB_INVALID_HANDLE;
+    if (!out || len != sizeof(cudaIpcMemHandle_t)) return QB_INVALID_LENGTH;
+    DeviceGuard dg(c->device);
+    cudaIpcMemHandle_t hnd;
+    QB_CUDA(cudaIpcGetMemHandle(&hnd, c->buf.p));
+    memcpy(out, &hnd, sizeof(hnd));
+    return QB_OK;
+}
+
+uint32_t qb_tp_comm_connect(uint64_t comm, int rank, int size, const void *handles, size_t len) {
+    auto c = find_comm(comm);
+    if (!c) return QB_INVALID_HANDLE;
+    if (c->connected) return QB_INVALID_STATE;
+    if (size < 1 || size > kMaxTp || rank < 0 || rank >= size || !handles ||
+        len != (size_t)size * sizeof(cudaIpcMemHandle_t))
+        return QB_INVALID_PARAMETERS;
+    DeviceGuard dg(c->device);
+    TpPeers &v = c->view;
+    v.rank = rank;
+    v.size = size;
+    v.rows = c->rows;
+    v.h = c->h;
+    for (int r = 0; r < size; ++r) {
+        void *base = c->buf.p;
+        if (r != rank) {
+            cudaIpcMemHandle_t hnd;
+            memcpy(&hnd, (const uint8_t *)handles + (size_t)r * sizeof(hnd), sizeof(hnd));
+            cudaError_t e = cudaIpcOpenMemHandle(&base, hnd, cudaIpcMemLazyEnablePeerAccess);
+            if (e != cudaSuccess) {
+                cudaGetLastError();
+                return QB_CUDA_ERROR;
+            }
+            c->peer_base[r] = base;
+        }
+        tp_carve(base, c->rows, c->h, &v.flags[r], &v.part[r], &v.amx[r]);
+    }
+    c->rank = rank;
+    c->size = size;
+    c->connected = true;
+    return QB_OK;
+}
+
+uint32_t qb_tp_comm_free(uint64_t comm) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = g_comms.find(comm);
+    if (it == g_comms.end()) return QB_INVALID_HANDLE;
+    g_comms.erase(it);
     return QB_OK;
 }
 
@@ -1671,8 +1917,8 @@ uint32_t qb_batch_logits(uint64_t batch, float *logits, size_t logits_len) {
     if (!bp) return QB_INVALID_HANDLE;
     Batch &b = *bp;
     if (!b.valid || !b.logits_valid) return QB_NOT_STARTED;
-    if (logits_len != b.nseq * b.m->c.vocab_size) {
-        set_detail(0, b.nseq * b.m->c.vocab_size, logits_len);
+    if (logits_len != b.nseq * b.m->nv) {  // a shard's own vocabulary rows
+        set_detail(0, b.nseq * b.m->nv, logits_len);
         return QB_INVALID_OUTPUT_LENGTH;
     }
     DeviceGuard dg(b.device);
