@@ -465,39 +465,91 @@ def run_decode_config(args, topo, lf):
 QWEN7B_PROMPT = 512
 
 
+def qwen7b_shard_bytes(cfg, shard, kv_bytes_per_pos_rank, L, rows):
+    """HBM bytes one rank moves per decode step of `rows` sequences: its
+    shard's INT8 linears (plus row scales), its LM-head rows (BF16), the
+    norms, and the K/V of its KV heads for every sequence's L cached
+    positions."""
+    h, hd = cfg.hidden_dim, cfg.head_dim
+    qd = (shard["heads"][1] - shard["heads"][0]) * hd
+    kv = (shard["kv_heads"][1] - shard["kv_heads"][0]) * hd
+    ff = shard["ff"][1] - shard["ff"][0]
+    nv = shard["vocab"][1] - shard["vocab"][0]
+    mats = qd * h + 2 * kv * h + h * qd + 2 * ff * h + h * ff
+    rows_sc = qd + 2 * kv + h + 2 * ff + h
+    per_layer = mats + 4 * rows_sc + 4 * (2 * h) + 4 * (qd + 2 * kv)
+    return cfg.layers * per_layer + nv * h * 2 + 4 * h + rows * (L + 1) * kv_bytes_per_pos_rank
+
+
 def run_qwen7b(args, topo):
-    """The Qwen2.5-7B shape (INT8 per-row linears, untied BF16 head, BF16 KV)
-    on one GPU per rank: batch-1 greedy decode after a 512-token prompt
-    (device-timed decode kernel steps, roofline ~7.1 GB per step)."""
+    """The Qwen2.5-7B shape (INT8 per-row linears, untied BF16 head, BF16
+    KV), tensor-parallel over the N GPUs of the run (one shard per rank;
+    partial sums after o_proj and down summed over NVLink peer memory):
+    batch 1 and batch 32 greedy decode after 512-token prompts, each step
+    device-timed (max over ranks).  At N = 1 the same model also runs the
+    persistent decode kernel (``decode_kernel``)."""
+    import numpy as np
+    import torch
+
     import llm_inference_edu_b200 as qb
-    from llm_inference_edu_b200 import presets, synthetic
-    steps = max(4, args.steps // 2)
+    from llm_inference_edu_b200 import dp, presets, synthetic, tp
+    steps = max(4, args.steps // 4)
     cap = QWEN7B_PROMPT + args.warmup + steps + 8
     cfg = presets.qwen_7b(cap)
     w = synthetic.weights(cfg, seed=2, dtype="bf16", lazy=True)
-    model = qb.Decoder(cfg, w, linear_format="int8", table_format="bf16", device=topo.local_rank)
+    model = qb.Decoder(cfg, w, linear_format="int8", table_format="bf16", device=topo.local_rank,
+                       tp=(topo.rank, topo.world))
     del w
-    sess = qb.CachedSession(model, cap, kv_dtype="bf16", budget=0)
-    import torch
-    stream = torch.cuda.ExternalStream(sess.stream())
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    ev0.record(stream)
-    first = sess.prefill_into(synthetic.prompt(cfg.vocab_size, QWEN7B_PROMPT, seed=3 + topo.rank), None)
-    ev1.record(stream)
-    torch.cuda.synchronize()
-    prefill_ms = ev0.elapsed_time(ev1)
-    ids = sess.decode_greedy(first, args.warmup)
-    ms, L0 = decode_timed(sess, ids[-1], steps, topo)
+    shard = model.shard()
     peak, peak_kind = measured_peaks()
-    kv_pos = cfg.layers * 2 * cfg.kv_dim * 2
-    bytes_step = algorithmic_bytes(cfg, "int8", kv_pos, L0 + (steps - 1) / 2.0)
-    achieved = bytes_step / (ms / 1000.0 / steps) / 1e9
-    return {"workload": "qwen2.5-7b-shape int8 batch-1 greedy decode (512-token prompt, bf16 KV), tp1 per rank",
-            "steps": steps, "value": topo.world * steps / (ms / 1000.0), "unit": "tok/s",
-            "ms_per_step": ms / steps, "prefill_tok_per_s": QWEN7B_PROMPT / (prefill_ms / 1000.0),
+    kvh = shard["kv_heads"][1] - shard["kv_heads"][0]
+    kv_pos = cfg.layers * 2 * kvh * cfg.head_dim * 2
+    out = {"workload": "qwen2.5-7b-shape int8 greedy decode (512-token prompts, bf16 kv)",
+           "tp": topo.world, "shard": {k: list(v) if isinstance(v, tuple) else v for k, v in shard.items()}}
+    if topo.world == 1:
+        sess = qb.CachedSession(model, cap, kv_dtype="bf16", budget=0)
+        first = sess.prefill_into(synthetic.prompt(cfg.vocab_size, QWEN7B_PROMPT, seed=3), None)
+        ids = sess.decode_greedy(first, args.warmup)
+        ms, L0 = decode_timed(sess, ids[-1], steps, topo)
+        bytes_step = algorithmic_bytes(cfg, "int8", kv_pos, L0 + (steps - 1) / 2.0)
+        achieved = bytes_step / (ms / 1000.0 / steps) / 1e9
+        out["decode_kernel_batch1"] = {
+            "steps": steps, "value": steps / (ms / 1000.0), "unit": "tok/s", "ms_per_step": ms / steps,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "bytes_per_step": bytes_step, "peak_source": peak_kind}}
+        del sess
+    for B in (1, 32):
+        b = tp.batch(model, max(256, B), B, cap, "bf16", topo.rank, topo.world)
+        prompts = np.stack([synthetic.prompt(cfg.vocab_size, QWEN7B_PROMPT, seed=3 + s)
+                            for s in range(B)]).astype(np.uint32)
+        stream = torch.cuda.ExternalStream(b.stream())
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        dp.barrier(topo)
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        first = b.prefill(prompts)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        prefill_ms = dp.max_over_ranks(topo, ev0.elapsed_time(ev1), device="cuda")
+        ids = b.decode_greedy(first, args.warmup)
+        dp.barrier(topo)
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        b.decode_greedy(ids[-1], steps)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        ms = dp.max_over_ranks(topo, ev0.elapsed_time(ev1), device="cuda")
+        L0 = QWEN7B_PROMPT + args.warmup
+        bytes_step = qwen7b_shard_bytes(cfg, shard, kv_pos, L0 + (steps - 1) / 2.0, B)
+        achieved = bytes_step / (ms / 1000.0 / steps) / 1e9
+        out[f"batch{B}"] = {
+            "steps": steps, "value": B * steps / (ms / 1000.0), "unit": "tok/s", "ms_per_step": ms / steps,
+            "prefill_tok_per_s": B * QWEN7B_PROMPT / (prefill_ms / 1000.0),
+            "roofline_per_rank": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                                  "frac": achieved / peak, "bytes_per_step": bytes_step,
+                                  "peak_source": peak_kind}}
+        del b
+    return out
 
 
 def cpu_baseline(args):

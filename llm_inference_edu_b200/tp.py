@@ -8,7 +8,10 @@ from __future__ import annotations
 
 def connect(comm, rank: int, size: int, group=None) -> None:
     """Gathers every rank's communicator handle (torch.distributed, rank
-    order) and opens the peers' buffers."""
+    order) and opens the peers' buffers.  A single rank needs no channel."""
+    if size == 1:
+        comm.connect(rank, [comm.handle()])
+        return
     import torch.distributed as dist
     handles = [None] * size
     dist.all_gather_object(handles, comm.handle(), group=group)

@@ -53,16 +53,22 @@ def _oracle_ids(oracle, om, cap, prompt, steps):
     return first, ids, lg
 
 
-def test_tp2_qwen05b_matches_single_gpu_and_oracle(oracle, tmp_path):
-    # 0.5B shape (14 query heads, 2 KV heads: one KV group per rank), INT8
-    # linears, BF16 table and KV, two sequences of 48-token prompts, 12
-    # greedy steps.
-    _need_gpus(2)
+HEADS_05B = {2: [(0, 7), (7, 14)], 4: [(0, 4), (4, 7), (7, 11), (11, 14)],
+             8: [(0, 2), (2, 4), (4, 6), (6, 7), (7, 9), (9, 11), (11, 13), (13, 14)]}
+
+
+@pytest.mark.parametrize("size", [2, 4, 8])
+def test_tp_qwen05b_matches_single_gpu_and_oracle(oracle, tmp_path, size):
+    # 0.5B shape (14 query heads, 2 KV heads): at TP=2 one KV group per
+    # rank; at TP=4 and 8 each KV head is replicated on 2 or 4 ranks that
+    # split its 7 query heads unevenly.  INT8 linears, BF16 table and KV,
+    # two sequences of 48-token prompts, 12 greedy steps.
+    _need_gpus(size)
     import llm_inference_edu_b200 as qb
     from helpers import qwen_host_weights
     P, steps, B = 48, 12, 2
-    res = _spawn(2, tmp_path, "0.5b", P, steps, B, "bf16")
-    assert res[0]["heads"].tolist() == [0, 7] and res[1]["heads"].tolist() == [7, 14]
+    res = _spawn(size, tmp_path, "0.5b", P, steps, B, "bf16")
+    assert [tuple(r["heads"].tolist()) for r in res] == HEADS_05B[size]
     for r in res[1:]:
         assert np.array_equal(r["first"], res[0]["first"]) and np.array_equal(r["ids"], res[0]["ids"])
     tp_first, tp_ids = res[0]["first"], res[0]["ids"]
