@@ -327,6 +327,159 @@ __global__ void __launch_bounds__(256) gemm_rows(const float *X, int ldx, int n,
     }
 }
 
+// ----------------------------------------------------------- skinny GEMM ----
+//
+// Y[t][r] = epilogue(sum_k X[t][k] W[r][k]) for n <= GV_MAXT tokens (batched
+// decode of a few sequences, a tensor-parallel rank's batch-1 step): an
+// HBM-bound streaming kernel with no tensor-core setup.  Each warp owns two
+// adjacent rows (the gate/up pairs, or two rows sharing the activation
+// reads); its lanes stride the rows' 16-byte chunks and multiply each with
+// the same K elements of all n tokens, staged in shared memory one K tile at
+// a time.  Every weight byte is read
+// once per call with streaming loads; the first tile's weights are loaded
+// before the dependent-launch wait (they do not depend on earlier kernels).
+constexpr int GV_WARPS = 8, GV_MAXT = 1, GV_TILE_BYTES = 2048;  // measured: two tokens already favour the tensor cores
+
+template <int WF>
+__device__ __forceinline__ const uint8_t *gv_chunk(const GemmW &w, int r, int k) {
+    constexpr int ESZ = WF == WF_I8 ? 1 : (WF == WF_BF16 ? 2 : 4);
+    const int s = k / w.seg_len, kk = k - s * w.seg_len;
+    return w.base + (size_t)s * w.seg_stride + (size_t)r * w.row_stride + (size_t)kk * ESZ;
+}
+
+// acc[t] += sum_e x_t[e] * w[e] over one 16-byte chunk of weights.  The
+// tile's inputs are quad-major: quad q of chunk c of token t is float4
+// (t * Q + q) * CT + c, so lanes reading consecutive chunks read
+// consecutive 16-byte words (no bank conflicts).
+template <int WF, int NT>
+__device__ __forceinline__ void gv_dot(const uint4 &c, const float4 *xs4, int ch, int CT, int n, float *acc) {
+    constexpr int EPC = WF == WF_I8 ? 16 : (WF == WF_BF16 ? 8 : 4);
+    float wv[EPC];
+    const uint32_t u[4] = {c.x, c.y, c.z, c.w};
+    if (WF == WF_I8) {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) wv[e] = u8b_to_f32(u[e >> 2], e & 3);
+    } else if (WF == WF_BF16) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) wv[e] = (e & 1) ? bf16_hi(u[e >> 1]) : bf16_lo(u[e >> 1]);
+    } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) wv[e] = __uint_as_float(u[e]);
+    }
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+        if (t >= n) break;
+#pragma unroll
+        for (int q = 0; q < EPC / 4; ++q) {
+            const float4 x = xs4[((size_t)t * (EPC / 4) + q) * CT + ch];
+            acc[t] = fmaf(x.x, wv[4 * q], acc[t]);
+            acc[t] = fmaf(x.y, wv[4 * q + 1], acc[t]);
+            acc[t] = fmaf(x.z, wv[4 * q + 2], acc[t]);
+            acc[t] = fmaf(x.w, wv[4 * q + 3], acc[t]);
+        }
+    }
+}
+
+template <int WF, int EPI, int NT>
+__global__ void __launch_bounds__(GV_WARPS * 32) gemv_tokens(const float *X, int ldx, int n, int N, int K, GemmW w,
+                                                             const float *R, int ldr, float *Y, int ldy, Planes P,
+                                                             unsigned *err) {
+    constexpr int EPC = WF == WF_I8 ? 16 : (WF == WF_BF16 ? 8 : 4);
+    constexpr int KT = GV_TILE_BYTES / 16 * EPC;   // elements per tile
+    constexpr int CT = GV_TILE_BYTES / 16;         // chunks per row and tile
+    constexpr int CPL = CT / 32;                     // chunks per lane per row and tile
+    constexpr int Q = EPC / 4;                       // quads per chunk
+    constexpr int RW = 2;                            // rows per warp
+    extern __shared__ __align__(16) float xs[];    // [NT][KT]
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int r0 = (blockIdx.x * GV_WARPS + warp) * RW;
+    const bool live = r0 < N;
+    float acc[RW][NT];
+#pragma unroll
+    for (int i = 0; i < RW; ++i)
+#pragma unroll
+        for (int t = 0; t < NT; ++t) acc[i][t] = 0.0f;
+    uint4 wc[RW][CPL];
+    auto load_tile = [&](int k0) {
+#pragma unroll
+        for (int i = 0; i < RW; ++i)
+#pragma unroll
+            for (int j = 0; j < CPL; ++j) {
+                const int k = k0 + (lane + 32 * j) * EPC;
+                wc[i][j] = live && r0 + i < N && k < K ? ld_stream_u4(gv_chunk<WF>(w, r0 + i, k))
+                                                       : make_uint4(0u, 0u, 0u, 0u);
+            }
+    };
+    load_tile(0);
+    pdl_wait();
+    for (int k0 = 0; k0 < K; k0 += KT) {
+        // Stage the tokens' K elements [k0, k0 + KT) quad-major (zero past K).
+        float4 *xs4 = reinterpret_cast<float4 *>(xs);
+        for (int f = threadIdx.x; f < NT * (KT / 4); f += GV_WARPS * 32) {
+            const int t = f / (KT / 4), g = f - t * (KT / 4), c = g / Q, q = g - c * Q;
+            float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (t < n && k0 + 4 * g < K) v = *reinterpret_cast<const float4 *>(X + (size_t)t * ldx + k0 + 4 * g);
+            xs4[((size_t)t * Q + q) * CT + c] = v;
+        }
+        __syncthreads();
+        uint4 cur[RW][CPL];
+#pragma unroll
+        for (int i = 0; i < RW; ++i)
+#pragma unroll
+            for (int j = 0; j < CPL; ++j) cur[i][j] = wc[i][j];
+        if (k0 + KT < K) load_tile(k0 + KT);  // the next tile's weights in flight
+#pragma unroll
+        for (int i = 0; i < RW; ++i)
+#pragma unroll
+            for (int j = 0; j < CPL; ++j) {
+                const int ch = lane + 32 * j;
+                if (k0 + ch * EPC < K) gv_dot<WF, NT>(cur[i][j], xs4, ch, CT, n, acc[i]);
+            }
+        __syncthreads();
+    }
+    // The next kernel may launch now: a dependent grid scheduled earlier would
+    // hold SM slots that this grid's later waves still need.
+    pdl_trigger();
+    // Butterfly sums; lane t runs token t's epilogue.
+#pragma unroll
+    for (int i = 0; i < RW; ++i)
+#pragma unroll
+        for (int t = 0; t < NT; ++t)
+#pragma unroll
+            for (int off = 16; off; off >>= 1) acc[i][t] += __shfl_xor_sync(0xffffffffu, acc[i][t], off);
+    if (!live) return;
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+        if (lane != t || t >= n) continue;
+        if (EPI == EPI_GU) {
+            if (r0 + 1 < N) epilogue_gu(w, t, r0, acc[0][t], acc[1][t], Y, ldy, P, err);
+        } else {
+            epilogue1<EPI>(w, t, r0, acc[0][t], R, ldr, Y, ldy, err);
+            if (r0 + 1 < N) epilogue1<EPI>(w, t, r0 + 1, acc[1][t], R, ldr, Y, ldy, err);
+        }
+    }
+}
+
+template <int WF, int EPI>
+cudaError_t gemv(const float *X, int ldx, int n, int N, int K, const GemmW &w, const float *R, int ldr, float *Y,
+                 int ldy, const Planes &P, unsigned *err, cudaStream_t st) {
+    constexpr int EPC = WF == WF_I8 ? 16 : (WF == WF_BF16 ? 8 : 4);
+    constexpr int KT = GV_TILE_BYTES / 16 * EPC, RW = 2;
+    const int rows = GV_WARPS * RW;
+    const dim3 grid((N + rows - 1) / rows);
+    auto go = [&](auto kern, int nt) -> cudaError_t {
+        const size_t sm = (size_t)nt * KT * sizeof(float);
+        if (sm > 48 * 1024) {
+            cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+            if (e != cudaSuccess) return e;
+        }
+        return launch_pdl(kern, grid, dim3(GV_WARPS * 32), sm, st, X, ldx, n, N, K, w, R, ldr, Y, ldy, P, err);
+    };
+    if (n <= 1) return go(gemv_tokens<WF, EPI, 1>, 1);
+    if (n <= 2) return go(gemv_tokens<WF, EPI, 2>, 2);
+    return go(gemv_tokens<WF, EPI, 4>, 4);
+}
+
 // -------------------------------------------------------------- attention ----
 
 // RoPE of every query and key head of each token (at its own position) with
@@ -342,7 +495,8 @@ __global__ void rope_kv(float *qkv, int n, const int *pos, const int *seqs, int 
         uint8_t *kc = kv.k(l), *vc = kv.v(l);
         float *row = qkv + (size_t)t * rq;
         const float2 *rp = rope + (size_t)p * half;
-        for (int idx = threadIdx.x; idx < qh * half; idx += blockDim.x) {
+        const int i0 = blockIdx.y * blockDim.x + threadIdx.x, istep = gridDim.y * blockDim.x;
+        for (int idx = i0; idx < qh * half; idx += istep) {
             const int hh = idx / half, j = idx - hh * half;
             float *q = row + (size_t)hh * hd;
             const float2 cs = rp[j];
@@ -353,7 +507,7 @@ __global__ void rope_kv(float *qkv, int n, const int *pos, const int *seqs, int 
             flag_bad(err, q0);
             flag_bad(err, q1);
         }
-        for (int idx = threadIdx.x; idx < kvh * half; idx += blockDim.x) {
+        for (int idx = i0; idx < kvh * half; idx += istep) {
             const int g = idx / half, j = idx - g * half;
             const float *k = row + h + (size_t)g * hd;
             const float2 cs = rp[j];
@@ -370,7 +524,7 @@ __global__ void rope_kv(float *qkv, int n, const int *pos, const int *seqs, int 
                 ((float *)kc)[base + j + half] = k1;
             }
         }
-        for (int idx = threadIdx.x; idx < kvh * hd; idx += blockDim.x) {
+        for (int idx = i0; idx < kvh * hd; idx += istep) {
             const int g = idx / hd, i = idx - g * hd;
             const float v = row[h + (size_t)kvh * hd + (size_t)g * hd + i];
             const size_t at = kv.row(seqs[t], g, p) + i;
@@ -734,10 +888,40 @@ cudaError_t layer_gemm(int which, const PrefillArgs &a, const DecodeLayer &Ly, i
     }
 }
 
+// A few tokens (INT8 or BF16 linears) take the streaming skinny GEMM
+// instead of the tensor-core or register-tiled GEMM.
+bool use_gemv(const PrefillArgs &a, int n) { return n <= GV_MAXT && (a.wfmt == WF_I8 || a.wfmt == WF_BF16); }
+
+// The four GEMMs of a layer on the skinny path (the same epilogues as
+// layer_gemm).
+template <int WF>
+cudaError_t layer_gemv(int which, const PrefillArgs &a, const DecodeLayer &Ly, int n, float *part, cudaStream_t st) {
+    const int kv = a.kvh * a.hd, rq = a.qd + 2 * kv;
+    const Planes none{nullptr, 0, TC_NP};
+    switch (which) {
+    case 0:
+        return gemv<WF, EPI_QKV>(a.xn, a.h, n, rq, a.h, GemmW{Ly.wqkv, a.sh, 0, a.h, Ly.sqkv, Ly.bqkv}, nullptr, 0,
+                                 a.qkv, rq, none, a.err, st);
+    case 1: {
+        const GemmW w{Ly.wo, a.shd, (size_t)a.h * a.shd, a.hd, Ly.so, nullptr};
+        if (part) return gemv<WF, EPI_QKV>(a.ctx, a.qd, n, a.h, a.qd, w, nullptr, 0, part, a.h, none, a.err, st);
+        return gemv<WF, EPI_RESID>(a.ctx, a.qd, n, a.h, a.qd, w, a.x, a.h, a.h2, a.h, none, a.err, st);
+    }
+    case 2:
+        return gemv<WF, EPI_GU>(a.xn, a.h, n, 2 * a.ff, a.h, GemmW{Ly.wgu, a.sh, 0, a.h, Ly.sgu, nullptr}, nullptr, 0,
+                                a.act, a.ff, none, a.err, st);
+    default: {
+        const GemmW w{Ly.wd, a.sff, 0, a.ff, Ly.sd, nullptr};
+        if (part) return gemv<WF, EPI_QKV>(a.act, a.ff, n, a.h, a.ff, w, nullptr, 0, part, a.h, none, a.err, st);
+        return gemv<WF, EPI_RESID>(a.act, a.ff, n, a.h, a.ff, w, a.h2, a.h, a.x, a.h, none, a.err, st);
+    }
+    }
+}
+
 // RoPE and the KV write run in the QKV GEMM's epilogue when that GEMM is on
 // the tensor cores and the RoPE partner rows (r ^ hd/2) share a 128-row tile.
-bool rope_fused(const PrefillArgs &a) {
-    return a.tc && !a.tc->layers.empty() && (a.hd == 64 || a.hd == 128);
+bool rope_fused(const PrefillArgs &a, int n) {
+    return a.tc && !a.tc->layers.empty() && (a.hd == 64 || a.hd == 128) && !use_gemv(a, n);
 }
 
 // The same GEMMs on the tensor cores (weights in the layer's tensor maps,
@@ -753,7 +937,7 @@ cudaError_t layer_gemm_tc(int which, const PrefillArgs &a, int l, int n, float *
     case 0:
         j = TcJob{EPI_QKV, n, rq, a.h, &M.qkv, &a.tc->xn, GemmW{nullptr, 0, 0, 0, Ly.sqkv, Ly.bqkv},
                   nullptr, 0, a.qkv, rq, none};
-        if (rope_fused(a)) {
+        if (rope_fused(a, n)) {
             rk = RopeKv{a.pos, a.seq, a.rope, a.kv, l, a.qd, a.kvh, a.hd, a.kv_bf16};
             j.rk = &rk;
         }
@@ -778,6 +962,10 @@ cudaError_t layer_gemm_tc(int which, const PrefillArgs &a, int l, int n, float *
 }
 
 cudaError_t run_gemm(int which, const PrefillArgs &a, int l, int n, cudaStream_t st, float *part = nullptr) {
+    if (use_gemv(a, n)) {
+        if (a.wfmt == WF_I8) return layer_gemv<WF_I8>(which, a, a.layers[l], n, part, st);
+        return layer_gemv<WF_BF16>(which, a, a.layers[l], n, part, st);
+    }
     if (a.tc && !a.tc->layers.empty()) return layer_gemm_tc(which, a, l, n, part, st);
     const DecodeLayer &Ly = a.layers[l];
     if (a.wfmt == WF_I8) return layer_gemm<WF_I8>(which, a, Ly, n, part, st);
@@ -807,7 +995,7 @@ int attention_splits(const PrefillArgs &a, int n, int max_pos, int *span) {
     const int len = max_pos + 1;
     int nz = (len + AT_SPAN - 1) / AT_SPAN;
     const int want = (2 * 148 + n * a.kvh - 1) / (n * a.kvh);
-    nz = std::max(nz, std::min(want, (len + 255) / 256));
+    nz = std::max(nz, std::min(want, n <= GV_MAXT ? (len + 63) / 64 : (len + 255) / 256));
     const size_t per = (size_t)a.group * (a.hd + 2);
     while (nz > 1 && (size_t)n * a.kvh * nz * per > a.apart_floats) --nz;
     int sp = (len + nz - 1) / nz;
@@ -871,8 +1059,9 @@ cudaError_t forward_tokens(const PrefillArgs &a, int n, int max_pos, bool lm_hea
         if ((e = rmsnorm(a.x, Ly.attn_norm, a.xn, xn_planes(a), n, a.h, a.eps, a.err, st)) != cudaSuccess)
             break;
         if ((e = run_gemm(0, a, l, n, st)) != cudaSuccess) break;
-        if (!rope_fused(a) &&
-            (e = launch_pdl(rope_kv, dim3(rows_grid), dim3(128), 0, st, a.qkv, n, a.pos, a.seq, l, a.qd, a.qh, a.kvh,
+        if (!rope_fused(a, n) &&
+            (e = launch_pdl(rope_kv, dim3(rows_grid, n < 16 ? 8 : 1), dim3(128), 0, st, a.qkv, n, a.pos, a.seq, l, a.qd,
+                            a.qh, a.kvh,
                             a.hd, a.rope, a.kv, a.kv_bf16, a.err)) !=
                 cudaSuccess)
             break;
@@ -892,7 +1081,12 @@ cudaError_t forward_tokens(const PrefillArgs &a, int n, int max_pos, bool lm_hea
     const Planes none{nullptr, 0, TC_NP};
     GemmW w{a.head, a.semb, 0, a.h, nullptr, nullptr};
     int am_tiles = 0;
-    if (a.tc && a.tc->head.wf >= 0) {
+    if (n <= GV_MAXT) {
+        e = a.tfmt == WF_BF16 ? gemv<WF_BF16, EPI_PLAIN>(a.xn, a.h, n, a.V, a.h, w, nullptr, 0, a.logits, a.V, none,
+                                                         a.err, st)
+                              : gemv<WF_F32, EPI_PLAIN>(a.xn, a.h, n, a.V, a.h, w, nullptr, 0, a.logits, a.V, none,
+                                                        a.err, st);
+    } else if (a.tc && a.tc->head.wf >= 0) {
         const TcJob j{EPI_PLAIN, n, a.V, a.h, &a.tc->head, &a.tc->xn, w, nullptr, 0, a.logits, a.V, none,
                       a.amv, a.ami};
         e = tc_gemm(j, a.err, st, &am_tiles);
@@ -902,7 +1096,9 @@ cudaError_t forward_tokens(const PrefillArgs &a, int n, int max_pos, bool lm_hea
         e = gemm<WF_F32, EPI_PLAIN>(a, a.xn, a.h, n, a.V, a.h, w, nullptr, 0, a.logits, a.V, none, st);
     }
     if (e != cudaSuccess) return e;
-    if (a.tp) return tp_argmax(*a.tp, ++*a.tp_seq, a.logits, n, a.V, a.v0, a.amax, a.err, a.tp_timeout_ns, st);
+    if (a.tp)  // the per-tile greedy partials' space holds the slice partials
+        return tp_argmax(*a.tp, ++*a.tp_seq, a.logits, n, a.V, a.v0, a.amax, a.amv, a.ami, a.err, a.tp_timeout_ns,
+                         st);
     if (am_tiles > 0) return launch_pdl(argmax_tiles, dim3(n), dim3(32), 0, st, a.amv, a.ami, am_tiles, n, a.V, a.amax);
     return launch_pdl(argmax_rows, dim3(rows_grid), dim3(256), 0, st, a.logits, n, a.V, a.amax, a.err);
 }

@@ -177,7 +177,7 @@ static bool tp_split(const qb_model_config &c, int rank, int size, Model &m) {
         m.nq = base + (j < extra ? 1 : 0);
         m.head0 = g * grp + j * base + std::min(j, extra);
     }
-    if (ff % S || (ff / S) % 4) return false;
+    if (S > 1 && (ff % S || (ff / S) % 4)) return false;
     m.nff = ff / S; m.f0 = r * m.nff;
     const size_t tiles = (V + 127) / 128, per = tiles / S, extra = tiles % S;
     const size_t t0 = r * per + std::min(r, extra), nt = per + (r < extra ? 1 : 0);
@@ -434,7 +434,7 @@ static uint32_t prefill_workspace(const Model &m, int chunk, DevBuf &ws, Prefill
     // the extra splits of small row counts; greedy partials per 128-row tile.
     const size_t kvh = m.nkv, grp = m.nq / kvh, hd = m.c.head_dim;
     const size_t apart = (ch * kvh * ((a.cap + 1023) / 1024) + 600) * grp * (hd + 2);
-    const size_t am = ((m.nv + 127) / 128) * ch;
+    const size_t am = std::max<size_t>((m.nv + 127) / 128, tp_argmax_scratch(1)) * ch;  // tile or slice partials
     const size_t abytes = round16(apart * 4), ambytes = round16(am * 4);
     if (!ws.p) {
         uint32_t st = ws.alloc(fbytes + 2 * hp + fp + abytes + 2 * ambytes);

@@ -85,15 +85,18 @@ __global__ void tp_allreduce_kernel(TpPeers P, unsigned seq, size_t n4, const fl
     }
 }
 
-// Local part of the argmax: one block per token scans its logits row
-// (strict >, so the lowest index wins ties) and leaves (value, v0 + index)
-// in this rank's amx slot.
-__global__ void tp_argmax_local(const float *logits, int nv, int v0, float2 *amx, unsigned *err) {
-    const int t = blockIdx.x;
+// Local part of the argmax: block (t, z) scans slice z of token t's logits
+// row (strict >, so the lowest index wins ties) and leaves (value, v0 +
+// index) in pv / pi [t][z].
+constexpr int AM_SLICES = 64;
+
+__global__ void tp_argmax_local(const float *logits, int nv, int v0, float *pv, int *pi, unsigned *err) {
+    const int t = blockIdx.x, z = blockIdx.y;
+    const int per = (nv + AM_SLICES - 1) / AM_SLICES, lo = z * per, hi = min(nv, lo + per);
     const float *row = logits + (size_t)t * nv;
     float bv = -INFINITY;
     int bi = 0x7fffffff;
-    for (int i = threadIdx.x; i < nv; i += blockDim.x) {
+    for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) {
         const float v = row[i];
         if (!isfinite(v)) atomicOr(err, ERR_NONFINITE);
         if (v > bv) { bv = v; bi = i; }
@@ -111,15 +114,28 @@ __global__ void tp_argmax_local(const float *logits, int nv, int v0, float2 *amx
     if (threadIdx.x == 0) {
         for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
             if (sv[w] > bv || (sv[w] == bv && si[w] < bi)) { bv = sv[w]; bi = si[w]; }
-        if (bi == 0x7fffffff) bi = 0;
-        amx[t] = make_float2(bv, __int_as_float(v0 + bi));
+        pv[(size_t)t * AM_SLICES + z] = bv;
+        pi[(size_t)t * AM_SLICES + z] = bi == 0x7fffffff ? 0x7fffffff : v0 + bi;
     }
 }
 
-__global__ void tp_argmax_combine(TpPeers P, unsigned seq, int n, uint32_t *out, unsigned *err,
-                                  unsigned long long timeout_ns) {
-    if (!tp_sync(P, seq, err, timeout_ns)) return;
+// One block: token t's slice partials in slice order (this rank's best),
+// published in its amx slot; then the exchange and the best over ranks.
+__global__ void tp_argmax_combine(TpPeers P, unsigned seq, int n, const float *pv, const int *pi, uint32_t *out,
+                                  unsigned *err, unsigned long long timeout_ns) {
     const size_t off = (size_t)(seq & 1u) * P.rows;
+    for (int t = threadIdx.x; t < n; t += blockDim.x) {
+        float bv = -INFINITY;
+        int bi = 0x7fffffff;
+        for (int z = 0; z < AM_SLICES; ++z) {
+            const float v = pv[(size_t)t * AM_SLICES + z];
+            const int i = pi[(size_t)t * AM_SLICES + z];
+            if (i != 0x7fffffff && (v > bv || bi == 0x7fffffff)) { bv = v; bi = i; }
+        }
+        P.amx[P.rank][off + t] = make_float2(bv, __int_as_float(bi == 0x7fffffff ? 0 : bi));
+    }
+    __syncthreads();
+    if (!tp_sync(P, seq, err, timeout_ns)) return;
     for (int t = threadIdx.x; t < n; t += blockDim.x) {
         float2 best = ld_peer2(P.amx[0] + off + t);
         for (int r = 1; r < P.size; ++r) {
@@ -153,13 +169,14 @@ cudaError_t tp_allreduce(const TpPeers &P, unsigned seq, int n, const float *R, 
 }
 
 cudaError_t tp_argmax(const TpPeers &P, unsigned seq, const float *logits, int n, int nv, int v0, uint32_t *out,
-                      unsigned *err, unsigned long long timeout_ns, cudaStream_t st) {
-    float2 *mine = P.amx[P.rank] + (size_t)(seq & 1u) * P.rows;
-    tp_argmax_local<<<n, 256, 0, st>>>(logits, nv, v0, mine, err);
+                      float *pv, int *pi, unsigned *err, unsigned long long timeout_ns, cudaStream_t st) {
+    tp_argmax_local<<<dim3(n, AM_SLICES), 256, 0, st>>>(logits, nv, v0, pv, pi, err);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    tp_argmax_combine<<<1, 256, 0, st>>>(P, seq, n, out, err, timeout_ns);
+    tp_argmax_combine<<<1, 256, 0, st>>>(P, seq, n, pv, pi, out, err, timeout_ns);
     return cudaGetLastError();
 }
+
+size_t tp_argmax_scratch(int rows) { return (size_t)rows * AM_SLICES; }
 
 }  // namespace qb

@@ -44,8 +44,10 @@ cudaError_t tp_allreduce(const TpPeers &P, unsigned seq, int n, const float *R, 
 // Each token's greedy id over the whole vocabulary: this rank's logits
 // [n][nv] cover global ids v0 .. v0 + nv - 1; the best (strict >, lowest
 // id) of every rank's slice is combined in rank order (ties keep the lower
-// rank, whose ids are lower).  Writes out[t] on every rank.
+// rank, whose ids are lower).  Writes out[t] on every rank.  pv / pi: the
+// per-slice partials, tp_argmax_scratch(rows) of each.
 cudaError_t tp_argmax(const TpPeers &P, unsigned seq, const float *logits, int n, int nv, int v0, uint32_t *out,
-                      unsigned *err, unsigned long long timeout_ns, cudaStream_t st);
+                      float *pv, int *pi, unsigned *err, unsigned long long timeout_ns, cudaStream_t st);
+size_t tp_argmax_scratch(int rows);
 
 }  // namespace qb
