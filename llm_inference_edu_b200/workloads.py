@@ -20,10 +20,10 @@ import numpy as np
 from . import presets, synthetic
 
 
-def _model(cfg, seed=1):
+def _model(cfg, seed=1, linear="int8"):
     from . import api
     w = synthetic.weights(cfg, seed=seed, dtype="bf16", lazy=True)
-    return api.Decoder(cfg, w, linear_format="int8", table_format="bf16")
+    return api.Decoder(cfg, w, linear_format=linear, table_format="bf16")
 
 
 def _sync():
@@ -51,12 +51,13 @@ def batched(sequences: int, prompt: int, steps: int) -> None:
           f"decode {(t2 - t1) * 1e3 / steps:.3f} ms/step (wall)")
 
 
-def decode(prompt: int, steps: int, profile: bool) -> None:
+def decode(prompt: int, steps: int, profile: bool, linear: str = "int8") -> None:
     from . import api
     cap = prompt + steps + 8
     cfg = presets.qwen_0_5b(cap)
-    m = _model(cfg)
-    s = api.CachedSession(m, cap, kv_dtype="bf16", budget=0)
+    m = _model(cfg, linear=linear)
+    # BF16 linears run with the reference's FP32 cache (the BF16 benchmark leg)
+    s = api.CachedSession(m, cap, kv_dtype="bf16" if linear == "int8" else "f32", budget=0)
     tok = s.prefill_into(synthetic.prompt(cfg.vocab_size, prompt, seed=1), None)
     if not profile:
         _sync()
@@ -115,11 +116,12 @@ def main(argv=None) -> int:
     ap.add_argument("--prompt", type=int, default=None)
     ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--profile", action="store_true")
+    ap.add_argument("--linear", choices=["int8", "bf16"], default="int8")
     a = ap.parse_args(argv)
     if a.workload == "batched":
         batched(a.sequences, a.prompt or 2, a.steps or 4)
     elif a.workload == "decode":
-        decode(a.prompt or 128, a.steps or 8, a.profile)
+        decode(a.prompt or 128, a.steps or 8, a.profile, a.linear)
     elif a.workload == "long":
         long(a.prompt or 8192, a.steps or 128)
     else:
