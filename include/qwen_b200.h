@@ -76,7 +76,15 @@ enum {
     QB_EMPTY_PROMPT = 36,
     QB_OUTPUT_LIMIT = 37,
     QB_INVALID_LAYER_COUNT = 38,
-    QB_UNSUPPORTED = 39
+    QB_UNSUPPORTED = 39,
+    /* LoadError (src/weights.rs:72-88) variants without an earlier code;
+     * its InvalidShape, NonFinite, DimensionOverflow, ResourceBudget and
+     * Allocation map to 5, 11, 2, 19 and 8. */
+    QB_LOAD_FORMAT = 40,
+    QB_LOAD_UNSUPPORTED_CONFIG = 41,
+    QB_LOAD_MISSING_TENSOR = 42,
+    QB_LOAD_UNEXPECTED_TENSOR = 43,
+    QB_LOAD_INVALID_DTYPE = 44
 };
 
 /* Detail of the calling thread's last error: which buffer (argument order),
@@ -400,6 +408,57 @@ uint32_t qb_batch_info_get(uint64_t batch, qb_batch_info *out);
 uint32_t qb_batch_reset(uint64_t batch);
 uint32_t qb_batch_stream(uint64_t batch, void **stream);
 uint32_t qb_batch_free(uint64_t batch);
+
+/* ------------------------------------------------------------------ */
+/* Checkpoint loading: safetensors (src/weights.rs:89-264)             */
+/* ------------------------------------------------------------------ */
+/* The HF config.json fields the reference validates (QwenConfig,
+ * src/weights.rs:9-28), parsed by the caller.  `architectures` holds
+ * `architectures_count` strings (the reference requires exactly
+ * ["Qwen2ForCausalLM"]); has_rope_scaling = a rope_scaling key present and
+ * not null. */
+typedef struct {
+    const char *model_type, *hidden_act, *torch_dtype;
+    const char *const *architectures;
+    size_t architectures_count;
+    size_t vocab_size, hidden_size, intermediate_size, num_hidden_layers, num_attention_heads,
+        num_key_value_heads, max_position_embeddings;
+    float rms_norm_eps, rope_theta;
+    int32_t tie_word_embeddings, use_sliding_window, has_rope_scaling;
+} qb_qwen_config;
+
+/* tensor_shapes (src/weights.rs:96-187): validates the config (supported
+ * architecture, positive dimensions, head divisibility, even head width,
+ * finite positive epsilon and base; QB_LOAD_UNSUPPORTED_CONFIG), checks
+ * every dimension product (QB_DIMENSION_OVERFLOW) and the 6 GiB planning
+ * budget of raw BF16 plus FP32 payload (QB_RESOURCE_BUDGET); *count = the
+ * number of expected tensors (12 per layer plus the embedding and final
+ * norm; the tied head has no tensor).  Host only. */
+uint32_t qb_qwen_tensor_count(const qb_qwen_config *config, size_t *count);
+/* inspect_qwen (src/weights.rs:189-221) over a whole safetensors file in
+ * HOST memory: the file format (header length and JSON, known dtypes,
+ * contiguous data offsets covering exactly the data section, sizes that
+ * match the shapes: QB_LOAD_FORMAT), then no unexpected name
+ * (QB_LOAD_UNEXPECTED_TENSOR, detail.index = its position in the header),
+ * then, in sorted-name order, every expected tensor present
+ * (QB_LOAD_MISSING_TENSOR), of its shape (QB_INVALID_SHAPE) and BF16
+ * (QB_LOAD_INVALID_DTYPE), detail.index = its position in the sorted
+ * expected names.  Host only. */
+uint32_t qb_safetensors_inspect(const uint8_t *data, size_t len, const qb_qwen_config *config,
+                                size_t *tensor_count);
+/* decode_qwen (src/weights.rs:226-264) and Decoder creation: inspects,
+ * checks the 6 GiB budget of the decoded payload plus the file
+ * (QB_RESOURCE_BUDGET), rejects any non-finite BF16 value before any
+ * device work (QB_NONFINITE, detail.index = the tensor's sorted position,
+ * detail.actual = the element), then creates and finalizes a device model
+ * (qb_model_create with max_tokens = max_position_embeddings, heads of
+ * hidden_size / num_attention_heads) from the BF16 payload: no partially
+ * loaded model is returned.  The reference's file integrity checks
+ * (inventory sizes and SHA-256, src/weights.rs:266-288) stay with the
+ * caller, which owns the files. */
+uint32_t qb_model_load_safetensors(const uint8_t *data, size_t len, const qb_qwen_config *config,
+                                   uint32_t linear_format, uint32_t table_format, int device,
+                                   uint64_t *out_model);
 
 /* ------------------------------------------------------------------ */
 /* Tensor parallelism across the GPUs of one box                       */

@@ -75,6 +75,9 @@ SIGNATURES = {
     "qb_tp_comm_connect": ([U64, C.c_int, C.c_int, P, S], U32),
     "qb_tp_comm_free": ([U64], U32),
     "qb_batch_create_tp": ([U64, U64, S, S, U32, P], U32),
+    "qb_qwen_tensor_count": ([P, P], U32),
+    "qb_safetensors_inspect": ([P, S, P, P], U32),
+    "qb_model_load_safetensors": ([P, S, P, U32, U32, C.c_int, P], U32),
     "qb_synthetic_normal": ([U64, U64, S, C.c_double, U32, P], U32),
     "qb_synthetic_tokens": ([U64, U64, S, U32, P], U32),
 }
@@ -120,6 +123,15 @@ class GenerationInfo(C.Structure):
 
 class BatchInfo(C.Structure):
     _fields_ = [("sequences", S), ("capacity", S), ("processed", S), ("valid", I32)]
+
+
+class QwenConfigC(C.Structure):
+    _fields_ = [("model_type", C.c_char_p), ("hidden_act", C.c_char_p), ("torch_dtype", C.c_char_p),
+                ("architectures", C.POINTER(C.c_char_p)), ("architectures_count", S)] + \
+               [(n, S) for n in ("vocab_size", "hidden_size", "intermediate_size", "num_hidden_layers",
+                                 "num_attention_heads", "num_key_value_heads", "max_position_embeddings")] + \
+               [("rms_norm_eps", F), ("rope_theta", F), ("tie_word_embeddings", I32),
+                ("use_sliding_window", I32), ("has_rope_scaling", I32)]
 
 
 class TpShard(C.Structure):

@@ -39,7 +39,8 @@ STATUS_NAMES = [
     "InvalidOutputLength", "EmptyInput", "NotEmpty", "Full", "InvalidState", "InvalidConfig",
     "InvalidHandle", "InvalidParameters", "NotStarted", "AlreadyStarted", "Cancelled",
     "EmptyLogits", "CudaError", "DeviceTimeout", "ContextLimit", "TraceLimit", "EmptyPrompt",
-    "OutputLimit", "InvalidLayerCount", "Unsupported"]
+    "OutputLimit", "InvalidLayerCount", "Unsupported", "Format", "UnsupportedConfig", "MissingTensor",
+    "UnexpectedTensor", "InvalidDtype"]
 
 
 class QbError(Exception):
@@ -299,6 +300,30 @@ class Decoder:
             lib().qb_model_free(self.handle)
             self.handle = None
 
+    @classmethod
+    def from_safetensors(cls, data: bytes, config: dict, linear_format: str = "f32",
+                         table_format: str = "f32", device: int = 0) -> "Decoder":
+        """decode_qwen (src/weights.rs:226-264) into a device model: the
+        validated BF16 checkpoint in `data` with its HF config.json
+        dictionary (tied head; max_tokens = max_position_embeddings)."""
+        c, _a, _s = _qwen_config(config)
+        h = C.c_uint64()
+        buf = C.create_string_buffer(bytes(data), len(data)) if data else None
+        _check(lib().qb_model_load_safetensors(buf, len(data), C.byref(c), LINEAR_FORMATS[linear_format],
+                                               TABLE_FORMATS[table_format], device, C.byref(h)), LoadError)
+        self = cls.__new__(cls)
+        self.handle = h.value
+        self.device = device
+        self.linear_format = linear_format
+        self.table_format = table_format
+        from .presets import ModelConfig
+        hd = config["hidden_size"] // config["num_attention_heads"]
+        self.config = ModelConfig(config["vocab_size"], config["num_hidden_layers"], config["hidden_size"],
+                                  config["num_attention_heads"], config["num_key_value_heads"], hd,
+                                  config["intermediate_size"], config["max_position_embeddings"],
+                                  float(config["rope_theta"]), float(config["rms_norm_eps"]), True, True)
+        return self
+
     def shard(self) -> dict:
         """This model's tensor-parallel shard: rank, size and the half-open
         ranges of query heads, KV heads, FFN columns and LM-head rows."""
@@ -488,6 +513,51 @@ class CachedSession:
 
 
 # ---------------------------------------------------------------- batch --
+
+# ------------------------------------------------------- checkpoints --
+
+def _qwen_config(config: dict):
+    """A HF config.json dictionary as the library's qb_qwen_config (the
+    QwenConfig fields of src/weights.rs:9-28); the returned tuple keeps the
+    strings alive."""
+    archs = [a.encode() for a in config.get("architectures", [])]
+    arr = (C.c_char_p * max(1, len(archs)))(*archs)
+    c = _lib.QwenConfigC(
+        str(config.get("model_type", "")).encode(), str(config.get("hidden_act", "")).encode(),
+        str(config.get("torch_dtype", "")).encode(), arr, len(archs),
+        int(config.get("vocab_size", 0)), int(config.get("hidden_size", 0)),
+        int(config.get("intermediate_size", 0)), int(config.get("num_hidden_layers", 0)),
+        int(config.get("num_attention_heads", 0)), int(config.get("num_key_value_heads", 0)),
+        int(config.get("max_position_embeddings", 0)), float(config.get("rms_norm_eps", 0.0)),
+        float(config.get("rope_theta", 0.0)), int(bool(config.get("tie_word_embeddings", False))),
+        int(bool(config.get("use_sliding_window", False))), int(config.get("rope_scaling") is not None))
+    return c, arr, archs
+
+
+class LoadError(QbError):
+    """LoadError (src/weights.rs:72-88): Format, UnsupportedConfig,
+    MissingTensor, UnexpectedTensor, InvalidShape, InvalidDtype, NonFinite,
+    DimensionOverflow, ResourceBudget, Allocation."""
+
+
+def qwen_tensor_count(config: dict) -> int:
+    """tensor_shapes (src/weights.rs:96-187): the config's expected tensor
+    count after its checks."""
+    c, _a, _s = _qwen_config(config)
+    n = C.c_size_t()
+    _check(lib().qb_qwen_tensor_count(C.byref(c), C.byref(n)), LoadError)
+    return n.value
+
+
+def inspect_safetensors(data: bytes, config: dict) -> int:
+    """inspect_qwen (src/weights.rs:189-221): the number of validated
+    tensors of a safetensors file."""
+    c, _a, _s = _qwen_config(config)
+    n = C.c_size_t()
+    buf = C.create_string_buffer(bytes(data), len(data)) if data else None
+    _check(lib().qb_safetensors_inspect(buf, len(data), C.byref(c), C.byref(n)), LoadError)
+    return n.value
+
 
 def _shard_dict(i) -> dict:
     return {"rank": i.rank, "size": i.size, "heads": (i.head0, i.head0 + i.heads),

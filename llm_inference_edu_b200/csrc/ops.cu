@@ -423,7 +423,8 @@ const char *qb_status_name(uint32_t s) {
         "InvalidOutputLength", "EmptyInput", "NotEmpty", "Full", "InvalidState", "InvalidConfig",
         "InvalidHandle", "InvalidParameters", "NotStarted", "AlreadyStarted", "Cancelled",
         "EmptyLogits", "CudaError", "DeviceTimeout", "ContextLimit", "TraceLimit", "EmptyPrompt",
-        "OutputLimit", "InvalidLayerCount", "Unsupported"};
+        "OutputLimit", "InvalidLayerCount", "Unsupported", "Format", "UnsupportedConfig", "MissingTensor",
+        "UnexpectedTensor", "InvalidDtype"};
     return s < sizeof(names) / sizeof(names[0]) ? names[s] : "Unknown";
 }
 
