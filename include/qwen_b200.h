@@ -339,7 +339,41 @@ uint32_t qb_session_stream(uint64_t session, void **stream);
 uint32_t qb_session_free(uint64_t session);
 
 /* ------------------------------------------------------------------ */
-/* GenerationSession (src/generation.rs:98-338), greedy policy         */
+/* Sampling (src/sampling.rs:5-110)                                     */
+/* ------------------------------------------------------------------ */
+
+enum { QB_SAMPLING_GREEDY = 0, QB_SAMPLING_TEMPERATURE = 1 };
+
+/* Sampling::{Greedy, Temperature { temperature, top_k, seed }}
+ * (src/sampling.rs:5-12); temperature, top_k and seed are ignored for
+ * QB_SAMPLING_GREEDY. */
+typedef struct {
+    uint32_t kind;
+    float temperature;
+    uint64_t top_k;
+    uint64_t seed;
+} qb_sampling;
+
+/* Sampler::new, src/sampling.rs:24-42: QB_INVALID_PARAMETERS for a
+ * temperature that is not finite and positive, or top_k = 0.  The
+ * generator (ChaCha8, seeded from `seed`) lives on the host; the selection
+ * runs on CUDA device `device`. */
+uint32_t qb_sampler_create(const qb_sampling *policy, int device, uint64_t *out_sampler);
+/* Sampler::validate_vocab, src/sampling.rs:43-49. */
+uint32_t qb_sampler_validate_vocab(uint64_t sampler, size_t vocab);
+/* Sampler::reset, src/sampling.rs:51-56: the stream restarts from the seed. */
+uint32_t qb_sampler_reset(uint64_t sampler);
+/* Sampler::sample, src/sampling.rs:57-110, over `count` HOST logits (copied
+ * to the device): QB_EMPTY_LOGITS, QB_NONFINITE, QB_INVALID_PARAMETERS
+ * (top_k > count) leave the stream where it was. */
+uint32_t qb_sampler_sample(uint64_t sampler, const float *logits, size_t count, uint32_t *out_id);
+/* The same over DEVICE logits on the sampler's device. */
+uint32_t qb_sampler_sample_device(uint64_t sampler, const float *device_logits, size_t count,
+                                  uint32_t *out_id);
+uint32_t qb_sampler_free(uint64_t sampler);
+
+/* ------------------------------------------------------------------ */
+/* GenerationSession (src/generation.rs:98-338)                         */
 /* ------------------------------------------------------------------ */
 
 enum { QB_STOP_NONE = 0, QB_STOP_TOKEN = 1, QB_STOP_OUTPUT_LIMIT = 2 };
@@ -353,6 +387,14 @@ typedef struct {
 uint32_t qb_generation_create(uint64_t model, size_t capacity, const uint32_t *stops,
                               size_t stop_count, size_t max_new, uint32_t kv_dtype,
                               size_t budget_bytes, uint64_t *out_generation);
+/* GenerationSession::new with a sampling policy (NULL = greedy): the
+ * policy's errors (Sampler::new, validate_vocab against the model's vocab)
+ * are QB_INVALID_PARAMETERS.  next_token samples the device logits of the
+ * last evaluated token; reset and replay_history restart the stream. */
+uint32_t qb_generation_create_sampled(uint64_t model, size_t capacity, const qb_sampling *policy,
+                                      const uint32_t *stops, size_t stop_count, size_t max_new,
+                                      uint32_t kv_dtype, size_t budget_bytes,
+                                      uint64_t *out_generation);
 /* start_with_cancel, src/generation.rs:145-170; `cancel` (HOST, nullable)
  * is polled at token boundaries (nonzero = cancelled). */
 uint32_t qb_generation_start(uint64_t generation, const uint32_t *prompt, size_t count,

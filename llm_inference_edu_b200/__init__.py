@@ -8,7 +8,8 @@ from .presets import ModelConfig, qwen_0_5b, qwen_7b, tiny_b, tiny_r, tiny_r_wei
 from .api import (  # noqa: F401
     BatchSession, CacheError, CachedSession, CancelFlag, Decoder, GenerationSession, GroupwiseInt8, LoadError,
     TpComm, inspect_safetensors, qwen_tensor_count,
-    LinearError, ModelError, OpError, QbError, QuantError, RopeError, Sampling, StateError,
+    LinearError, ModelError, OpError, QbError, QuantError, RopeError, Sampler, Sampling, SamplingError,
+    StateError, Temperature,
     embedding, linear, linear_int8, linear_int8_lanes4, linear_lanes4, masked_softmax,
     residual_add, rmsnorm, rope, silu, softmax, tp_shard_of)
 from . import synthetic  # noqa: F401

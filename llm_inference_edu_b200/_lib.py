@@ -50,6 +50,13 @@ SIGNATURES = {
     "qb_session_stream": ([U64, P], U32),
     "qb_session_free": ([U64], U32),
     "qb_generation_create": ([U64, S, P, S, S, U32, S, P], U32),
+    "qb_generation_create_sampled": ([U64, S, P, P, S, S, U32, S, P], U32),
+    "qb_sampler_create": ([P, I32, P], U32),
+    "qb_sampler_validate_vocab": ([U64, S], U32),
+    "qb_sampler_reset": ([U64], U32),
+    "qb_sampler_sample": ([U64, P, S, P], U32),
+    "qb_sampler_sample_device": ([U64, P, S, P], U32),
+    "qb_sampler_free": ([U64], U32),
     "qb_generation_start": ([U64, P, S, P], U32),
     "qb_generation_next_token": ([U64, P, P, P], U32),
     "qb_generation_append_context": ([U64, P, S, S, P], U32),
@@ -132,6 +139,10 @@ class QwenConfigC(C.Structure):
                                  "num_attention_heads", "num_key_value_heads", "max_position_embeddings")] + \
                [("rms_norm_eps", F), ("rope_theta", F), ("tie_word_embeddings", I32),
                 ("use_sliding_window", I32), ("has_rope_scaling", I32)]
+
+
+class SamplingC(C.Structure):
+    _fields_ = [("kind", U32), ("temperature", C.c_float), ("top_k", C.c_uint64), ("seed", C.c_uint64)]
 
 
 class TpShard(C.Structure):

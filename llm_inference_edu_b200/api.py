@@ -685,10 +685,71 @@ class BatchSession:
 
 # ----------------------------------------------------------- generation --
 
+class SamplingError(QbError):
+    """SamplingError (src/sampling.rs:13-18): InvalidParameters, EmptyLogits,
+    NonFinite."""
+
+
+@dataclass(frozen=True)
+class Temperature:
+    """Sampling::Temperature (src/sampling.rs:7-11)."""
+    temperature: float
+    top_k: int
+    seed: int
+
+
 class Sampling:
-    """Sampling policy.  The device token loop implements Greedy
-    (src/sampling.rs:57-70)."""
+    """Sampling policy (src/sampling.rs:5-12): ``Sampling.Greedy`` or
+    ``Sampling.Temperature(temperature, top_k, seed)``."""
     Greedy = "greedy"
+    Temperature = Temperature
+
+
+def _sampling_c(policy):
+    if policy == Sampling.Greedy:
+        return _lib.SamplingC(0, 1.0, 0, 0)
+    if isinstance(policy, Temperature):
+        k, seed = int(policy.top_k), int(policy.seed)
+        if k < 0 or seed < 0 or seed >= 2**64:
+            raise SamplingError(27)
+        return _lib.SamplingC(1, float(policy.temperature), min(k, 2**64 - 1), seed)
+    raise SamplingError(27)
+
+
+class Sampler:
+    """Sampler (src/sampling.rs:19-110): the ChaCha8 generator on the host,
+    the top-k selection and the walk on CUDA device ``device``.  ``sample``
+    takes host logits (numpy) or a CUDA float32 tensor on that device."""
+
+    def __init__(self, policy, device: int = 0):
+        h = C.c_uint64()
+        c = _sampling_c(policy)
+        _check(lib().qb_sampler_create(C.byref(c), device, C.byref(h)), SamplingError)
+        self.handle = h.value
+        self.device = device
+
+    def __del__(self):
+        if getattr(self, "handle", None):
+            lib().qb_sampler_free(self.handle)
+            self.handle = None
+
+    def validate_vocab(self, vocab: int):
+        _check(lib().qb_sampler_validate_vocab(self.handle, vocab), SamplingError)
+
+    def reset(self):
+        _check(lib().qb_sampler_reset(self.handle), SamplingError)
+
+    def sample(self, logits) -> int:
+        out = C.c_uint32()
+        if hasattr(logits, "is_cuda") and logits.is_cuda:
+            assert logits.dtype.is_floating_point and logits.element_size() == 4 and logits.is_contiguous()
+            _check(lib().qb_sampler_sample_device(self.handle, logits.data_ptr(), logits.numel(), C.byref(out)),
+                   SamplingError)
+        else:
+            a = np.ascontiguousarray(np.asarray(logits, dtype=np.float32))
+            _check(lib().qb_sampler_sample(self.handle, a.ctypes.data_as(C.c_void_p) if a.size else None,
+                                           a.size, C.byref(out)), SamplingError)
+        return int(out.value)
 
 
 STOP_REASONS = {0: None, 1: "StopToken", 2: "OutputLimit"}
@@ -711,22 +772,25 @@ class CancelFlag:
 
 
 class GenerationSession:
-    """History plus KV-cached greedy generation (src/generation.rs:98-338)."""
+    """History plus KV-cached generation (src/generation.rs:98-338), greedy
+    or seeded temperature/top-k sampling."""
 
     def __init__(self, model: Decoder, capacity: int, policy=Sampling.Greedy,
                  stops: Sequence[int] = (), max_new: int = 1, kv_dtype: str = "f32",
                  budget: int = REFERENCE_BUDGET):
-        if policy != Sampling.Greedy:
+        try:
+            pc = _sampling_c(policy)
+        except SamplingError:
             raise StateError(27)
         st = np.ascontiguousarray(np.asarray(list(stops), dtype=np.int64))
         if st.size and (st.min() < 0 or st.max() >= 2**32):
             raise StateError(27)
         st = st.astype(np.uint32)
         h = C.c_uint64()
-        _check(lib().qb_generation_create(model.handle, capacity,
-                                          st.ctypes.data_as(C.c_void_p) if st.size else None,
-                                          st.size, max_new, KV_DTYPES[kv_dtype], budget,
-                                          C.byref(h)), StateError)
+        _check(lib().qb_generation_create_sampled(model.handle, capacity, C.byref(pc),
+                                                  st.ctypes.data_as(C.c_void_p) if st.size else None,
+                                                  st.size, max_new, KV_DTYPES[kv_dtype], budget,
+                                                  C.byref(h)), StateError)
         self.handle = h.value
         self.vocab = model.config.vocab_size
 

@@ -11,6 +11,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <cmath>
 #include <map>
 #include <memory>
 #include <mutex>
@@ -19,6 +20,7 @@
 #include "common.cuh"
 #include "decode.cuh"
 #include "prefill.cuh"
+#include "sampling.cuh"
 #include "tc_gemm.cuh"
 #include "tp.cuh"
 
@@ -196,6 +198,8 @@ struct Session;
 struct Generation;
 static std::map<uint64_t, std::shared_ptr<Session>> g_sessions;
 static std::map<uint64_t, std::shared_ptr<Generation>> g_generations;
+struct Sampler;
+static std::map<uint64_t, std::shared_ptr<Sampler>> g_samplers;
 
 static std::shared_ptr<Model> find_model(uint64_t h) {
     std::lock_guard<std::mutex> lk(g_mu);
@@ -773,10 +777,92 @@ static uint32_t session_step(Session &s, uint32_t token, float *logits, size_t l
     return st;
 }
 
+// --------------------------------------------------------- sampler ----
+
+// Sampler (src/sampling.rs:19-110): the policy, the host generator and the
+// device buffers of the selection kernel.
+struct Sampler {
+    int device = 0;
+    SamplePolicy policy;
+    uint64_t seed = 0;
+    ChaCha8Rng rng;
+    DevBuf scratch, staged, result;
+    int scratch_n = 0;
+    size_t staged_n = 0;
+    uint32_t *hres = nullptr;  // pinned copy of the result words
+    cudaStream_t stream = nullptr;
+    std::mutex mu;
+    ~Sampler() {
+        DeviceGuard dg(device);
+        if (hres) cudaFreeHost(hres);
+        if (stream) cudaStreamDestroy(stream);
+    }
+};
+
+// Sampler::new, src/sampling.rs:24-42.
+static bool policy_ok(const qb_sampling *p) {
+    if (!p || p->kind == QB_SAMPLING_GREEDY) return true;
+    return p->kind == QB_SAMPLING_TEMPERATURE && std::isfinite(p->temperature) && p->temperature > 0.0f &&
+           p->top_k != 0;
+}
+
+static uint32_t sampler_init(const qb_sampling *p, int device, Sampler &sp) {
+    if (!policy_ok(p)) return QB_INVALID_PARAMETERS;
+    const bool greedy = !p || p->kind == QB_SAMPLING_GREEDY;
+    sp.device = device;
+    sp.policy.greedy = greedy;
+    sp.policy.temperature = greedy ? 1.0f : p->temperature;
+    sp.policy.top_k = greedy ? 1 : (size_t)p->top_k;
+    sp.seed = greedy ? 0 : p->seed;
+    sp.rng.seed_from_u64(sp.seed);
+    DeviceGuard dg(device);
+    QB_CUDA(cudaMallocHost((void **)&sp.hres, 8));
+    return sp.result.alloc(8);
+}
+
+// validate_vocab, src/sampling.rs:43-49.
+static bool sampler_vocab_ok(const Sampler &sp, size_t vocab) {
+    return vocab != 0 && (sp.policy.greedy || sp.policy.top_k <= vocab);
+}
+
+// Sampler::sample, src/sampling.rs:57-110, over device logits on `st` (the
+// sampler's device current).  The reference's checks in its order: empty,
+// non-finite (found by the kernel), top_k > n; on any error the stream is
+// left where it was.
+static uint32_t sampler_run(Sampler &sp, const float *logits, size_t n, cudaStream_t st, uint32_t *id) {
+    if (n == 0) return QB_EMPTY_LOGITS;
+    if (n > (size_t)INT32_MAX) return QB_INVALID_PARAMETERS;
+    if (sp.scratch_n < (int)n) {
+        uint32_t e = sp.scratch.alloc(sample_scratch_bytes((int)n), false);
+        if (e) return e;
+        sp.scratch_n = (int)n;
+    }
+    const bool vocab_ok = sampler_vocab_ok(sp, n);
+    SamplePolicy pol = sp.policy;
+    if (!vocab_ok) pol.greedy = true;  // only the finiteness check runs
+    const ChaCha8Rng saved = sp.rng;
+    const double u = pol.greedy ? 0.0 : sp.rng.next_f64();
+    cudaError_t e = sample_launch(logits, (int)n, pol, u, sp.scratch.p, sp.result.as<uint32_t>(), st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(sp.hres, sp.result.p, 8, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) {
+        sp.rng = saved;
+        return cuda_status(e);
+    }
+    if (sp.hres[1] != 0) {
+        sp.rng = saved;
+        return sp.hres[1];
+    }
+    if (!vocab_ok) return QB_INVALID_PARAMETERS;
+    *id = sp.hres[0];
+    return QB_OK;
+}
+
 // ------------------------------------------------------- generation ----
 
 struct Generation {
     std::shared_ptr<Session> cache;
+    std::unique_ptr<Sampler> sampler;  // null: greedy through the fused argmax
     std::vector<uint32_t> history;
     std::vector<uint32_t> stops;
     size_t max_new = 0, generated = 0;
@@ -854,6 +940,7 @@ static uint32_t evaluate_pending(Generation &g, const volatile int32_t *cancel) 
 }
 
 static void generation_reset(Generation &g) {
+    if (g.sampler) g.sampler->rng.seed_from_u64(g.sampler->seed);
     g.cache->processed = 0;
     g.cache->valid = true;
     g.cache->logits_valid = false;
@@ -1477,8 +1564,8 @@ uint32_t qb_session_free(uint64_t session) {
 
 // ----------------------------------------------------------- generation ----
 
-uint32_t qb_generation_create(uint64_t model, size_t capacity, const uint32_t *stops, size_t nstops,
-                              size_t max_new, uint32_t kv_dtype, size_t budget, uint64_t *out) {
+static uint32_t generation_create(uint64_t model, size_t capacity, const qb_sampling *policy, const uint32_t *stops,
+                                  size_t nstops, size_t max_new, uint32_t kv_dtype, size_t budget, uint64_t *out) {
     clear_detail();
     if (!out) return QB_INVALID_PARAMETERS;
     auto m = find_model(model);
@@ -1487,11 +1574,19 @@ uint32_t qb_generation_create(uint64_t model, size_t capacity, const uint32_t *s
     if (max_new == 0 || max_new >= capacity) return QB_INVALID_PARAMETERS;
     for (size_t i = 0; i < nstops; ++i)
         if (stops[i] >= m->c.vocab_size) return QB_INVALID_PARAMETERS;
+    std::unique_ptr<Sampler> sampler;
+    if (policy && policy->kind != QB_SAMPLING_GREEDY) {
+        sampler.reset(new Sampler());
+        uint32_t st = sampler_init(policy, m->device, *sampler);
+        if (st) return st;
+        if (!sampler_vocab_ok(*sampler, m->c.vocab_size)) return QB_INVALID_PARAMETERS;
+    }
     std::shared_ptr<Session> s;
     uint32_t st = session_create(model, capacity, kv_dtype, budget, s);
     if (st) return st;
     auto g = std::make_shared<Generation>();
     g->cache = s;
+    g->sampler = std::move(sampler);
     g->stops.assign(stops, stops + nstops);
     g->max_new = max_new;
     g->vocab = (uint32_t)m->c.vocab_size;
@@ -1501,6 +1596,17 @@ uint32_t qb_generation_create(uint64_t model, size_t capacity, const uint32_t *s
     g_generations[id] = g;
     *out = id;
     return QB_OK;
+}
+
+uint32_t qb_generation_create(uint64_t model, size_t capacity, const uint32_t *stops, size_t nstops,
+                              size_t max_new, uint32_t kv_dtype, size_t budget, uint64_t *out) {
+    return generation_create(model, capacity, nullptr, stops, nstops, max_new, kv_dtype, budget, out);
+}
+
+uint32_t qb_generation_create_sampled(uint64_t model, size_t capacity, const qb_sampling *policy,
+                                      const uint32_t *stops, size_t nstops, size_t max_new, uint32_t kv_dtype,
+                                      size_t budget, uint64_t *out) {
+    return generation_create(model, capacity, policy, stops, nstops, max_new, kv_dtype, budget, out);
 }
 
 uint32_t qb_generation_start(uint64_t gen, const uint32_t *prompt, size_t n, const volatile int32_t *cancel) {
@@ -1535,6 +1641,14 @@ uint32_t qb_generation_next_token(uint64_t gen, const volatile int32_t *cancel, 
     if (st) return st;
     if (!g.logits_ready) return QB_NOT_STARTED;
     uint32_t next = g.last_argmax;
+    if (g.sampler) {
+        // The temperature policy samples the last token's logits, still on
+        // the device (the decode step kept them).
+        Session &s = *g.cache;
+        DeviceGuard dg(s.device);
+        st = sampler_run(*g.sampler, s.logits.as<float>(), s.m->c.vocab_size, s.stream, &next);
+        if (st) return st;
+    }
     g.history.push_back(next);
     g.generated += 1;
     g.logits_ready = false;
@@ -1643,6 +1757,82 @@ uint32_t qb_generation_free(uint64_t gen) {
     return QB_OK;
 }
 
+
+// -------------------------------------------------------- sampler ABI ----
+
+static std::shared_ptr<Sampler> find_sampler(uint64_t h) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = g_samplers.find(h);
+    return it == g_samplers.end() ? nullptr : it->second;
+}
+
+uint32_t qb_sampler_create(const qb_sampling *policy, int device, uint64_t *out) {
+    clear_detail();
+    if (!policy || !out || !policy_ok(policy)) return QB_INVALID_PARAMETERS;
+    int count = 0;
+    if (cudaGetDeviceCount(&count) != cudaSuccess || device < 0 || device >= count) return QB_INVALID_PARAMETERS;
+    auto sp = std::make_shared<Sampler>();
+    uint32_t st = sampler_init(policy, device, *sp);
+    if (st) return st;
+    DeviceGuard dg(device);
+    QB_CUDA(cudaStreamCreateWithFlags(&sp->stream, cudaStreamNonBlocking));
+    std::lock_guard<std::mutex> lk(g_mu);
+    uint64_t id = g_next++;
+    g_samplers[id] = sp;
+    *out = id;
+    return QB_OK;
+}
+
+uint32_t qb_sampler_validate_vocab(uint64_t h, size_t vocab) {
+    auto sp = find_sampler(h);
+    if (!sp) return QB_INVALID_HANDLE;
+    return sampler_vocab_ok(*sp, vocab) ? QB_OK : QB_INVALID_PARAMETERS;
+}
+
+uint32_t qb_sampler_reset(uint64_t h) {
+    auto sp = find_sampler(h);
+    if (!sp) return QB_INVALID_HANDLE;
+    std::lock_guard<std::mutex> lk(sp->mu);
+    sp->rng.seed_from_u64(sp->seed);
+    return QB_OK;
+}
+
+uint32_t qb_sampler_sample(uint64_t h, const float *logits, size_t n, uint32_t *out) {
+    clear_detail();
+    auto sp = find_sampler(h);
+    if (!sp) return QB_INVALID_HANDLE;
+    if (!out || (n && !logits)) return QB_INVALID_PARAMETERS;
+    if (n == 0) return QB_EMPTY_LOGITS;
+    std::lock_guard<std::mutex> lk(sp->mu);
+    DeviceGuard dg(sp->device);
+    if (sp->staged_n < n) {
+        uint32_t e = sp->staged.alloc(n * 4, false);
+        if (e) return e;
+        sp->staged_n = n;
+    }
+    QB_CUDA(cudaMemcpyAsync(sp->staged.p, logits, n * 4, cudaMemcpyHostToDevice, sp->stream));
+    return sampler_run(*sp, sp->staged.as<float>(), n, sp->stream, out);
+}
+
+uint32_t qb_sampler_sample_device(uint64_t h, const float *logits, size_t n, uint32_t *out) {
+    clear_detail();
+    auto sp = find_sampler(h);
+    if (!sp) return QB_INVALID_HANDLE;
+    if (!out || (n && !logits)) return QB_INVALID_PARAMETERS;
+    std::lock_guard<std::mutex> lk(sp->mu);
+    DeviceGuard dg(sp->device);
+    // The caller's logits may come from another stream: order after all of it.
+    QB_CUDA(cudaDeviceSynchronize());
+    return sampler_run(*sp, logits, n, sp->stream, out);
+}
+
+uint32_t qb_sampler_free(uint64_t h) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = g_samplers.find(h);
+    if (it == g_samplers.end()) return QB_INVALID_HANDLE;
+    g_samplers.erase(it);
+    return QB_OK;
+}
 
 // ----------------------------------------------------------- batch ABI ----
 

@@ -35,6 +35,8 @@ NOT_EMPTY = 22
 FULL = 23
 INVALID_STATE = 24
 CONTEXT_LIMIT = 34
+INVALID_PARAMETERS = 27
+EMPTY_LOGITS = 31
 
 MAT_NONE, MAT_F32, MAT_BF16, MAT_INT8 = -1, 0, 1, 2
 W_EMBEDDING, W_LM_HEAD, W_Q, W_K, W_V, W_O, W_GATE, W_UP, W_DOWN = range(9)
@@ -113,6 +115,15 @@ def lib():
             ("or_round_bf16", [C.c_float], C.c_float),
             ("or_synthetic_normal", [C.c_uint64, C.c_uint64, S, C.c_double, C.c_int, P], C.c_int),
             ("or_synthetic_tokens", [C.c_uint64, C.c_uint64, S, C.c_uint32, P], C.c_int),
+            ("or_chacha_block", [P, C.c_int, P], None),
+            ("or_rng_from_seed", [P, P], None),
+            ("or_rng_seed", [P, C.c_uint64], None),
+            ("or_rng_next_u64", [P], C.c_uint64),
+            ("or_rng_next_f64", [P], C.c_double),
+            ("or_sampler_init", [P, C.c_int, C.c_float, S, C.c_uint64], C.c_int),
+            ("or_sampler_reset", [P], None),
+            ("or_sampler_validate_vocab", [P, S], C.c_int),
+            ("or_sampler_sample", [P, P, S, P], C.c_int),
         ]:
             f = getattr(L, name)
             f.argtypes = args
@@ -434,6 +445,77 @@ class Session:
         if n < 0:
             return -n, None
         return OK, [int(v) for v in out[:n]]
+
+
+class _Rng(C.Structure):
+    _fields_ = [("key", C.c_uint32 * 8), ("counter", C.c_uint64), ("buf", C.c_uint32 * 64), ("index", C.c_size_t)]
+
+
+class _SamplerState(C.Structure):
+    _fields_ = [("greedy", C.c_int), ("temperature", C.c_float), ("top_k", C.c_size_t), ("seed", C.c_uint64),
+                ("rng", _Rng)]
+
+
+def chacha_block(words, rounds):
+    """The ChaCha block function over a 16-word input state."""
+    w = np.ascontiguousarray(words, dtype=np.uint32)
+    out = np.zeros(16, dtype=np.uint32)
+    lib().or_chacha_block(_p(w), rounds, _p(out))
+    return out
+
+
+class Rng:
+    """ChaCha8Rng (rand_chacha 0.9): ``Rng(seed=u64)`` seeds through
+    seed_from_u64, ``Rng(key=bytes32)`` through from_seed."""
+
+    def __init__(self, seed=None, key=None):
+        self.s = _Rng()
+        if key is not None:
+            k = np.frombuffer(bytes(key), dtype=np.uint8).copy()
+            assert k.size == 32
+            lib().or_rng_from_seed(C.byref(self.s), _p(k))
+        else:
+            lib().or_rng_seed(C.byref(self.s), int(seed))
+
+    def next_u64(self):
+        return int(lib().or_rng_next_u64(C.byref(self.s)))
+
+    def next_u32_words(self, n):
+        """n keystream words in order (n even)."""
+        out = []
+        for _ in range(n // 2):
+            v = self.next_u64()
+            out += [v & 0xFFFFFFFF, v >> 32]
+        return out
+
+    def random_f64(self):
+        return float(lib().or_rng_next_f64(C.byref(self.s)))
+
+
+class Sampler:
+    """Sampler (src/sampling.rs:19-110): greedy, or seeded temperature/top-k.
+    Constructor errors raise ValueError with the status code."""
+
+    def __init__(self, temperature=None, top_k=None, seed=0):
+        self.s = _SamplerState()
+        greedy = temperature is None
+        st = lib().or_sampler_init(C.byref(self.s), int(greedy), 0.0 if greedy else float(temperature),
+                                   0 if greedy else int(top_k), int(seed))
+        if st:
+            raise ValueError(st)
+
+    def validate_vocab(self, vocab):
+        return lib().or_sampler_validate_vocab(C.byref(self.s), int(vocab))
+
+    def reset(self):
+        lib().or_sampler_reset(C.byref(self.s))
+
+    def sample(self, logits):
+        """(status, id)"""
+        lg = np.ascontiguousarray(logits, dtype=np.float32)
+        out = C.c_size_t(0)
+        st = lib().or_sampler_sample(C.byref(self.s), _p(lg) if lg.size else None, lg.size, C.byref(out))
+        return st, (int(out.value) if st == OK else None)
 
 
 def int8_model_weights(cfg, w, linear_format):

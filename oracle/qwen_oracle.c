@@ -1274,3 +1274,146 @@ int or_synthetic_tokens(uint64_t seed, uint64_t stream, size_t n, uint32_t vocab
     for (size_t i = 0; i < n; ++i) out[i] = (uint32_t)(syn_mix(base + i) % vocab);
     return OR_OK;
 }
+
+/* ------------------------------------------------------------------ */
+/* seeded temperature / top-k sampling (src/sampling.rs:71-110)        */
+/* ------------------------------------------------------------------ */
+/* The reference draws from rand_chacha 0.9.0's ChaCha8Rng seeded by
+ * rand_core 0.9.5's SeedableRng::seed_from_u64 (neither is vendored in the
+ * reference tree).  Restated from their published algorithms: the ChaCha
+ * block function (RFC 7539 quarter rounds, 8 rounds = 4 double rounds,
+ * 64-bit block counter in words 12-13, stream 0 in words 14-15, key words
+ * little-endian from the 32-byte seed, output = keystream words in block
+ * order); seed_from_u64 fills the seed 4 bytes at a time with a PCG32 step
+ * (state = state * 6364136223846793005 + 11634580027462260723, output
+ * rotr(((state >> 18) ^ state) >> 27, state >> 59), little-endian);
+ * next_u64 = word[i] | word[i + 1] << 32; random::<f64>() =
+ * (next_u64 >> 11) * 2^-53. */
+
+static uint32_t rotl32(uint32_t v, int c) { return (v << c) | (v >> (32 - c)); }
+
+/* The ChaCha block function: `rounds` rounds over `in`, plus the input. */
+void or_chacha_block(const uint32_t in[16], int rounds, uint32_t out[16]) {
+    uint32_t x[16];
+    memcpy(x, in, sizeof(x));
+#define QR(a, b, c, d)                                              \
+    x[a] += x[b]; x[d] ^= x[a]; x[d] = rotl32(x[d], 16);            \
+    x[c] += x[d]; x[b] ^= x[c]; x[b] = rotl32(x[b], 12);            \
+    x[a] += x[b]; x[d] ^= x[a]; x[d] = rotl32(x[d], 8);             \
+    x[c] += x[d]; x[b] ^= x[c]; x[b] = rotl32(x[b], 7);
+    for (int r = 0; r < rounds; r += 2) {
+        QR(0, 4, 8, 12) QR(1, 5, 9, 13) QR(2, 6, 10, 14) QR(3, 7, 11, 15)
+        QR(0, 5, 10, 15) QR(1, 6, 11, 12) QR(2, 7, 8, 13) QR(3, 4, 9, 14)
+    }
+#undef QR
+    for (int i = 0; i < 16; ++i) out[i] = x[i] + in[i];
+}
+
+/* ChaCha8Rng::from_seed: the key words are the seed's little-endian words;
+ * block counter and stream start at 0. */
+void or_rng_from_seed(or_rng *g, const uint8_t seed[32]) {
+    for (int i = 0; i < 8; ++i)
+        g->key[i] = (uint32_t)seed[4 * i] | (uint32_t)seed[4 * i + 1] << 8 | (uint32_t)seed[4 * i + 2] << 16 |
+                    (uint32_t)seed[4 * i + 3] << 24;
+    g->counter = 0;
+    g->index = 64;  /* empty buffer */
+}
+
+void or_rng_seed(or_rng *g, uint64_t seed) {
+    uint8_t bytes[32];
+    uint64_t state = seed;
+    for (int i = 0; i < 8; ++i) {
+        state = state * 6364136223846793005ull + 11634580027462260723ull;
+        uint32_t xs = (uint32_t)(((state >> 18) ^ state) >> 27);
+        uint32_t rot = (uint32_t)(state >> 59);
+        uint32_t x = (xs >> rot) | (xs << ((32 - rot) & 31));
+        for (int b = 0; b < 4; ++b) bytes[4 * i + b] = (uint8_t)(x >> (8 * b));
+    }
+    or_rng_from_seed(g, bytes);
+}
+
+static void rng_refill(or_rng *g) {
+    for (int b = 0; b < 4; ++b) {
+        uint32_t in[16] = {0x61707865u, 0x3320646eu, 0x79622d32u, 0x6b206574u};
+        for (int i = 0; i < 8; ++i) in[4 + i] = g->key[i];
+        uint64_t c = g->counter + (uint64_t)b;
+        in[12] = (uint32_t)c;
+        in[13] = (uint32_t)(c >> 32);
+        in[14] = 0;
+        in[15] = 0;
+        or_chacha_block(in, 8, g->buf + 16 * b);
+    }
+    g->counter += 4;
+    g->index = 0;
+}
+
+uint64_t or_rng_next_u64(or_rng *g) {
+    if (g->index >= 64) rng_refill(g);
+    /* the index is always even here: only whole u64 draws are made */
+    uint64_t v = (uint64_t)g->buf[g->index] | ((uint64_t)g->buf[g->index + 1] << 32);
+    g->index += 2;
+    return v;
+}
+
+double or_rng_next_f64(or_rng *g) { return (double)(or_rng_next_u64(g) >> 11) * (1.0 / 9007199254740992.0); }
+
+/* Sampler::new, src/sampling.rs:23-41 (greedy: temperature ignored). */
+int or_sampler_init(or_sampler *s, int greedy, float temperature, size_t top_k, uint64_t seed) {
+    if (!greedy && (!isfinite(temperature) || temperature <= 0.0f || top_k == 0)) return OR_INVALID_PARAMETERS;
+    s->greedy = greedy;
+    s->temperature = temperature;
+    s->top_k = top_k;
+    s->seed = greedy ? 0 : seed;
+    or_rng_seed(&s->rng, s->seed);
+    return OR_OK;
+}
+
+void or_sampler_reset(or_sampler *s) { or_rng_seed(&s->rng, s->seed); }
+
+/* Sampler::validate_vocab, src/sampling.rs:43-49. */
+int or_sampler_validate_vocab(const or_sampler *s, size_t vocab) {
+    return (vocab == 0 || (!s->greedy && s->top_k > vocab)) ? OR_INVALID_PARAMETERS : OR_OK;
+}
+
+static const float *g_cmp_logits;
+static int cmp_desc_id(const void *pa, const void *pb) {
+    size_t a = *(const size_t *)pa, b = *(const size_t *)pb;
+    float la = g_cmp_logits[a], lb = g_cmp_logits[b];
+    if (lb > la) return 1;  /* logits[b].partial_cmp(&logits[a]) then id order */
+    if (lb < la) return -1;
+    return a < b ? -1 : (a > b ? 1 : 0);
+}
+
+/* Sampler::sample, src/sampling.rs:48-110. */
+int or_sampler_sample(or_sampler *s, const float *logits, size_t n, size_t *out) {
+    if (n == 0) return OR_EMPTY_LOGITS;
+    for (size_t i = 0; i < n; ++i)
+        if (!isfinite(logits[i])) return OR_NONFINITE;
+    if (or_sampler_validate_vocab(s, n)) return OR_INVALID_PARAMETERS;
+    size_t best = 0;
+    for (size_t i = 1; i < n; ++i)
+        if (logits[i] > logits[best]) best = i;
+    if (s->greedy) { *out = best; return OR_OK; }
+    /* The top-k in (logit desc, id asc) order: a full sort's first k equals
+     * select_nth + truncate + sort under the same total order. */
+    size_t *cand = (size_t *)malloc(n * sizeof(size_t));
+    for (size_t i = 0; i < n; ++i) cand[i] = i;
+    g_cmp_logits = logits;
+    qsort(cand, n, sizeof(size_t), cmp_desc_id);
+    size_t k = s->top_k < n ? s->top_k : n;
+    double maximum = (double)logits[best], temp = (double)s->temperature;
+    double total = 0.0;
+    for (size_t i = 0; i < k; ++i) total += exp(((double)logits[cand[i]] - maximum) / temp);
+    double target = or_rng_next_f64(&s->rng) * total;
+    double cumulative = 0.0;
+    size_t last_positive = best;
+    for (size_t i = 0; i < k; ++i) {
+        double w = exp(((double)logits[cand[i]] - maximum) / temp);
+        if (w > 0.0) last_positive = cand[i];
+        cumulative += w;
+        if (target < cumulative) { *out = cand[i]; free(cand); return OR_OK; }
+    }
+    free(cand);
+    *out = last_positive;
+    return OR_OK;
+}

@@ -39,6 +39,8 @@ enum {
     OR_FULL = 23,
     OR_INVALID_STATE = 24,
     OR_INVALID_CONFIG = 25,
+    OR_INVALID_PARAMETERS = 27,
+    OR_EMPTY_LOGITS = 31,
     OR_CONTEXT_LIMIT = 34,
     OR_TRACE_LIMIT = 35,
     OR_EMPTY_PROMPT = 36,
@@ -144,6 +146,31 @@ long or_uncached_greedy(const or_model *m, const size_t *prompt, size_t n, const
  * library.  out_dtype 0 = FP32, 1 = BF16 bits (nearest-even). */
 int or_synthetic_normal(uint64_t seed, uint64_t stream, size_t n, double stddev, int out_dtype,
                         void *out);
+/* Seeded temperature / top-k sampling (src/sampling.rs): ChaCha8 stream of
+ * rand_chacha 0.9 seeded through rand_core 0.9's seed_from_u64. */
+typedef struct {
+    uint32_t key[8];
+    uint64_t counter;  /* next block number */
+    uint32_t buf[64];  /* four blocks of keystream */
+    size_t index;      /* next unread word of buf; 64 = empty */
+} or_rng;
+typedef struct {
+    int greedy;
+    float temperature;
+    size_t top_k;
+    uint64_t seed;
+    or_rng rng;
+} or_sampler;
+void or_chacha_block(const uint32_t in[16], int rounds, uint32_t out[16]);
+void or_rng_from_seed(or_rng *g, const uint8_t seed[32]);
+void or_rng_seed(or_rng *g, uint64_t seed);
+uint64_t or_rng_next_u64(or_rng *g);
+double or_rng_next_f64(or_rng *g);
+int or_sampler_init(or_sampler *s, int greedy, float temperature, size_t top_k, uint64_t seed);
+void or_sampler_reset(or_sampler *s);
+int or_sampler_validate_vocab(const or_sampler *s, size_t vocab);
+int or_sampler_sample(or_sampler *s, const float *logits, size_t n, size_t *out);
+
 int or_synthetic_tokens(uint64_t seed, uint64_t stream, size_t n, uint32_t vocab, uint32_t *out);
 
 #ifdef __cplusplus

@@ -5,6 +5,7 @@ import os
 import re
 
 import numpy as np
+import pytest
 
 from conftest import ROOT
 
@@ -74,3 +75,19 @@ def test_reference_fixture_weights_formula():
     w = presets.tiny_r_weights()
     assert list(w["embedding"][:4]) == [-0.16015625, -0.09375, -0.02734375, 0.0390625]
     assert w["layers"][1]["down"].size == 2048
+
+
+def test_sampler_policy_admission_needs_no_gpu():
+    # Sampler::new (src/sampling.rs:24-42): a temperature that is not finite
+    # and positive, or top_k = 0, is InvalidParameters before any device work.
+    import llm_inference_edu_b200 as qb
+    T = qb.Sampling.Temperature
+    for pol in [T(0.0, 1, 0), T(-1.0, 1, 0), T(float("nan"), 1, 0), T(float("inf"), 1, 0), T(1.0, 0, 0)]:
+        with pytest.raises(qb.SamplingError) as e:
+            qb.Sampler(pol)
+        assert e.value.kind == "InvalidParameters"
+    from llm_inference_edu_b200._lib import lib, SamplingC
+    bad_kind = SamplingC(7, 1.0, 1, 0)
+    h = C.c_uint64()
+    assert lib().qb_sampler_create(C.byref(bad_kind), 0, C.byref(h)) == 27
+    assert lib().qb_sampler_reset(999999) == 26
