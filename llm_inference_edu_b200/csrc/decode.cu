@@ -206,6 +206,70 @@ __device__ __forceinline__ void block_rmsnorm(const float *in, const float *gain
     csync();
 }
 
+// Statistics of the elements one thread staged: sum of squares and max |x|.
+struct NormAcc {
+    float ss = 0.0f, mx = 0.0f;
+    __device__ __forceinline__ void add(float v) {
+        ss = fmaf(v, v, ss);
+        mx = fmaxf(mx, fabsf(v));
+    }
+};
+
+// RMSNorm of `in` (shared, width w, staged by this CTA's threads, whose
+// NormAcc covers exactly the elements each staged) into xs, as
+// block_rmsnorm, starting right after the staging (no CTA barrier needed
+// before the call).  The statistics come from the staging pass: one
+// butterfly of (sum of squares, max) per warp, one CTA barrier, then every
+// thread adds the warps' pairs in warp order and takes
+// rd = 1 / sqrt(sum / w + eps); y = x * rd * gain.  This is the scaled form
+// of src/ops.rs:137-149 without the scaling, equal to it up to rounding
+// while max |x| < 2^58 (no square overflows a float sum of 2^10 terms) and
+// eps >= 2^-60; outside that range the scaled block_rmsnorm runs instead.
+template <int EPC>
+__device__ __forceinline__ void norm_staged(const float *in, const float *gain, float *xs, int w, int C, float eps,
+                                            float *red, NormAcc a) {
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+#pragma unroll
+    for (int off = 16; off; off >>= 1) {
+        a.ss += __shfl_xor_sync(FULL, a.ss, off);
+        a.mx = fmaxf(a.mx, __shfl_xor_sync(FULL, a.mx, off));
+    }
+    if (lane == 0) *reinterpret_cast<float2 *>(red + 2 * warp) = make_float2(a.ss, a.mx);
+    csync();
+    float S = 0.0f, M = 0.0f;
+#pragma unroll
+    for (int k = 0; k < NW; ++k) {
+        const float2 v = *reinterpret_cast<const float2 *>(red + 2 * k);
+        S += v.x;
+        M = fmaxf(M, v.y);
+    }
+    if (!(M < 0x1p58f && eps >= 0x1p-60f)) {  // CTA-uniform
+        csync();  // every thread has read red
+        block_rmsnorm<EPC>(in, gain, xs, w, C, eps, red);
+        return;
+    }
+    const float rd = 1.0f / sqrtf(S / (float)w + eps);
+    const int padded = C * EPC;
+    if ((w & 3) == 0) {
+        float4 *x4 = reinterpret_cast<float4 *>(xs);
+        for (int e = 4 * t; e < padded; e += 4 * NT) {
+            float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (e < w) {
+                const float4 v = *reinterpret_cast<const float4 *>(in + e);
+                const float4 gg = *reinterpret_cast<const float4 *>(gain + e);
+                o.x = (v.x * rd) * gg.x;
+                o.y = (v.y * rd) * gg.y;
+                o.z = (v.z * rd) * gg.z;
+                o.w = (v.w * rd) * gg.w;
+            }
+            x4[((e % EPC) >> 2) * C + e / EPC] = o;
+        }
+    } else {
+        for (int i = t; i < padded; i += NT) xs[xq<EPC>(i, C)] = i < w ? (in[i] * rd) * gain[i] : 0.0f;
+    }
+    csync();
+}
+
 __device__ __forceinline__ void flag_nonfinite(DecodeCtrl *ctrl, float v) {
     if (!isfinite(v)) atomicOr(&ctrl->error, ERR_NONFINITE);
 }
@@ -487,9 +551,29 @@ __device__ __forceinline__ void epi_row(const Epi &e, int WFi8, int n, int r, fl
 // become generic loads and live registers spill around it); the team size
 // is a run-time value, so each phase holds one copy of the loop.  Returns
 // the advanced cursor.
+// The wait of gemv_pairs for the first wave of a block of n rows starting
+// at `cur`: each warp observes those copies (lane j the j-th) before it
+// needs them.  Issued at the start of a phase, before the phase's inputs
+// are polled, so the weights' acquire overlaps the hand-over instead of
+// following it; gemv_pairs is then called with prewaited = true.
+__device__ __forceinline__ void ring_prewait(const DecodeParams &p, const Ring &rg, const Cursor &cur,
+                                             const KindGeom &g, int n, volatile int *s_abort) {
+    const int lane = threadIdx.x & 31;
+    const int rows = min(g.wave * g.rpc, n);
+    const int ns = g.rpc == 1 ? rows : (int)__umulhi((unsigned)(rows + g.rpc - 1), g.rpc_magic);
+#pragma unroll 1
+    for (int j = lane; j < ns; j += 32) {
+        int s = cur.slot + j, rd = cur.round;
+        while (s >= rg.nslot) { s -= rg.nslot; ++rd; }
+        mbar_wait(p, rg.full + s, (uint32_t)(rd & 1), s_abort);
+    }
+    __syncwarp();
+}
+
 template <int WF>
 __device__ __forceinline__ Cursor gemv_pairs(const DecodeParams &p, const Ring rg, Cursor cur, const KindGeom &g,
-                                          int n, const float *xs, volatile int *s_abort, const Epi e) {
+                                          int n, const float *xs, volatile int *s_abort, const Epi e,
+                                          bool prewaited = false) {
     constexpr int Q = Fmt<WF>::EPC / 4;
     const int lg = g.lgG, G = 1 << lg, T = NT >> lg;
     const int t = threadIdx.x, lane = t & 31;
@@ -504,14 +588,17 @@ __device__ __forceinline__ Cursor gemv_pairs(const DecodeParams &p, const Ring r
         const int ns = g.rpc == 1 ? rows : (int)__umulhi((unsigned)(rows + g.rpc - 1), g.rpc_magic);
         // Lane j of each warp observes the completion of the wave's j-th
         // copy (acquire); __syncwarp orders the rest of the warp's reads
-        // after all of them.
+        // after all of them.  The first wave was observed already when the
+        // caller pre-waited.
+        if (!(prewaited && r0 == 0)) {
 #pragma unroll 1
-        for (int j = lane; j < ns; j += 32) {
-            int s = cur.slot + j, rd = cur.round;
-            while (s >= rg.nslot) { s -= rg.nslot; ++rd; }
-            mbar_wait(p, rg.full + s, (uint32_t)(rd & 1), s_abort);
+            for (int j = lane; j < ns; j += 32) {
+                int s = cur.slot + j, rd = cur.round;
+                while (s >= rg.nslot) { s -= rg.nslot; ++rd; }
+                mbar_wait(p, rg.full + s, (uint32_t)(rd & 1), s_abort);
+            }
+            __syncwarp();
         }
-        __syncwarp();
         const bool two = g.U == 2;
         const int nu = two ? (rows + 1) >> 1 : rows;
 #pragma unroll 1
@@ -749,9 +836,10 @@ __device__ __forceinline__ void await4(const DecodeParams &p, const float *a0, c
 }
 
 // dst[i] = src[i], i < n, from an exchange vector (16 bytes per load when
-// n % 4 == 0 and src is 16-byte aligned).
+// n % 4 == 0 and src is 16-byte aligned); acc gathers the statistics of
+// the elements this thread staged (for norm_staged).
 __device__ __forceinline__ void await_stage(const DecodeParams &p, float *dst, const float *src, int n,
-                                            volatile int *s_abort) {
+                                            volatile int *s_abort, NormAcc &acc) {
     if ((n & 3) == 0 && ((uintptr_t)src & 15) == 0) {
         const uint4 *s4 = reinterpret_cast<const uint4 *>(src);
         uint4 *d4 = reinterpret_cast<uint4 *>(dst);
@@ -762,10 +850,18 @@ __device__ __forceinline__ void await_stage(const DecodeParams &p, float *dst, c
 #pragma unroll 1
             while (!ready4(v) && pl.again(p, s_abort)) v = ld_relaxed_v4(s4 + i);
             d4[i] = v;
+            acc.add(__uint_as_float(v.x));
+            acc.add(__uint_as_float(v.y));
+            acc.add(__uint_as_float(v.z));
+            acc.add(__uint_as_float(v.w));
         }
     } else {
 #pragma unroll 1
-        for (int i = threadIdx.x; i < n; i += NT) dst[i] = await1(p, src + i, s_abort);
+        for (int i = threadIdx.x; i < n; i += NT) {
+            const float v = await1(p, src + i, s_abort);
+            dst[i] = v;
+            acc.add(v);
+        }
     }
 }
 
@@ -801,7 +897,7 @@ __device__ __forceinline__ float emb_in(const DecodeParams &p, int token, int i)
 // polled from the exchange, summed in head order, then added.  All of a
 // batch's partials are in flight at once; a pass reloads only the missing.
 __device__ __forceinline__ void stage_after_attention(const DecodeParams &p, float *xcur, int l, float *h2,
-                                                      volatile int *s_abort) {
+                                                      volatile int *s_abort, NormAcc &acc) {
     const float *part = xv(p, xcur, l, p.x_part);
     const size_t stride = (size_t)p.h;
     if ((p.h & 1) == 0) {
@@ -842,7 +938,10 @@ __device__ __forceinline__ void stage_after_attention(const DecodeParams &p, flo
             }
             float2 *h2v = reinterpret_cast<float2 *>(h2) + i;
             const float2 r = *h2v;
-            *h2v = make_float2(r.x + o.x, r.y + o.y);
+            const float2 y = make_float2(r.x + o.x, r.y + o.y);
+            *h2v = y;
+            acc.add(y.x);
+            acc.add(y.y);
         }
         return;
     }
@@ -854,7 +953,9 @@ __device__ __forceinline__ void stage_after_attention(const DecodeParams &p, flo
             const float v = await1(p, part + (size_t)hh * stride + i, s_abort);
             o = hh == 0 ? v : o + v;
         }
-        h2[i] = h2[i] + o;
+        const float y = h2[i] + o;
+        h2[i] = y;
+        acc.add(y);
     }
 }
 
@@ -1154,19 +1255,24 @@ __device__ __forceinline__ void run_qkv(const DecodeParams &p, const CtaGeom &cg
     constexpr int EPC = Fmt<WF>::EPC;
     float *xs = sm + p.sm_xs, *h2 = sm + p.sm_h2;
     const float *gain = gain_buf(p, sm, 0), *rv = rv_buf(p, sm, 0);
+    ring_prewait(p, rg, cur, p.kind[K_QKV], cg.qkv_n, s_abort);
+    NormAcc acc;
     if (l > 0) {
-        await_stage(p, h2, xv(p, xcur, l - 1, p.x_hid), p.h, s_abort);
+        await_stage(p, h2, xv(p, xcur, l - 1, p.x_hid), p.h, s_abort, acc);
     } else {
 #pragma unroll 2
-        for (int i = threadIdx.x; i < p.h; i += NT) h2[i] = emb_in(p, token, i);
+        for (int i = threadIdx.x; i < p.h; i += NT) {
+            const float v = emb_in(p, token, i);
+            h2[i] = v;
+            acc.add(v);
+        }
     }
-    csync();
     mark_ready(p, 4 * l - 1);
+    norm_staged<EPC>(h2, gain, xs, p.h, p.ch, p.eps, sm + p.sm_red, acc);
     if (*s_abort) return;
-    block_rmsnorm<EPC>(h2, gain, xs, p.h, p.ch, p.eps, sm + p.sm_red);
     const Epi e{xv(p, xcur, l, p.x_qkv) + cg.qkv_r0, rv, nullptr, EPI_QKV,
                 !(p.withhold && l == 0 && blockIdx.x == 0)};
-    cur = gemv_pairs<WF>(p, rg, cur, p.kind[K_QKV], cg.qkv_n, xs, s_abort, e);
+    cur = gemv_pairs<WF>(p, rg, cur, p.kind[K_QKV], cg.qkv_n, xs, s_abort, e, true);
 }
 
 // The position-split exchange of head hh (split sp of nsp, layer l): this
@@ -1247,6 +1353,7 @@ __device__ __forceinline__ void run_attention(const DecodeParams &p, const Decod
                                               float *xcur, int l, int pos, float *sm, const Ring &rg, Cursor &cur,
                                               volatile int *s_abort) {
     const float *rv = rv_buf(p, sm, 1), *xs = sm + p.sm_xs;
+    if (cg.natt > 0) ring_prewait(p, rg, cur, p.kind[K_O], cg.att_n[0], s_abort);
 #pragma unroll 1
     for (int a = 0; a < cg.natt; ++a) {
         const int hh = cg.att_hh[a], r0 = cg.att_r0[a], n = cg.att_n[a];
@@ -1260,7 +1367,7 @@ __device__ __forceinline__ void run_attention(const DecodeParams &p, const Decod
         // Row scales: staged in shared memory for the first item, read from
         // global memory for the others.
         const Epi e{xv(p, xcur, l, p.x_part) + (size_t)hh * p.h + r0, a == 0 ? rv : Ly.so + r0, nullptr, EPI_O, 1};
-        cur = gemv_pairs<WF>(p, rg, cur, p.kind[K_O], n, xs, s_abort, e);
+        cur = gemv_pairs<WF>(p, rg, cur, p.kind[K_O], n, xs, s_abort, e, a == 0);
         if (a + 1 < cg.natt) csync();  // xs is rewritten by the next item
     }
 }
@@ -1278,15 +1385,16 @@ __device__ __forceinline__ void run_gate_up(const DecodeParams &p, const CtaGeom
     constexpr int EPC = Fmt<WF>::EPC;
     float *xs = sm + p.sm_xs, *h2 = sm + p.sm_h2;
     const float *gain = gain_buf(p, sm, 1), *rv = rv_buf(p, sm, 0);
-    stage_after_attention(p, xcur, l, h2, s_abort);
-    csync();
+    ring_prewait(p, rg, cur, p.kind[K_GU], 2 * cg.gu_n, s_abort);
+    NormAcc acc;
+    stage_after_attention(p, xcur, l, h2, s_abort, acc);
     mark_ready(p, 4 * l + 1);
+    norm_staged<EPC>(h2, gain, xs, p.h, p.ch, p.eps, sm + p.sm_red, acc);
     if (*s_abort) return;
     if (blockIdx.x == 0)
         for (int i = threadIdx.x; i < p.h; i += NT) flag_nonfinite(p.ctrl, h2[i]);
-    block_rmsnorm<EPC>(h2, gain, xs, p.h, p.ch, p.eps, sm + p.sm_red);
     const Epi e{xv(p, xcur, l, p.x_act) + cg.gu_f0, rv, nullptr, EPI_GU, 1};
-    cur = gemv_pairs<WF>(p, rg, cur, p.kind[K_GU], 2 * cg.gu_n, xs, s_abort, e);
+    cur = gemv_pairs<WF>(p, rg, cur, p.kind[K_GU], 2 * cg.gu_n, xs, s_abort, e, true);
 }
 
 template <int WF>
@@ -1302,6 +1410,7 @@ __device__ __forceinline__ void run_down(const DecodeParams &p, const CtaGeom &c
     float *xs = sm + p.sm_xs;
     const int padded = p.cff * EPC;
     const float *actv = xv(p, xcur, l, p.x_act);
+    ring_prewait(p, rg, cur, p.kind[K_DN], cg.dn_n, s_abort);
     if ((p.ff & 3) == 0) {
         // act -> xs: four consecutive elements are one quad of the layout.
         const uint4 *a4 = reinterpret_cast<const uint4 *>(actv);
@@ -1346,7 +1455,7 @@ __device__ __forceinline__ void run_down(const DecodeParams &p, const CtaGeom &c
     // this same CTA (src/kv_cache.rs:437-443: x_next = h' + down(a)).
     const float *h2 = sm + p.sm_h2 + cg.dn_r0, *rv = rv_buf(p, sm, 1);
     const Epi e{xv(p, xcur, l, p.x_hid) + cg.dn_r0, rv, h2, EPI_DN, 1};
-    cur = gemv_pairs<WF>(p, rg, cur, p.kind[K_DN], cg.dn_n, xs, s_abort, e);
+    cur = gemv_pairs<WF>(p, rg, cur, p.kind[K_DN], cg.dn_n, xs, s_abort, e, true);
 }
 
 // Final RMSNorm, this CTA's rows of the (tied) table, logits and the CTA's
@@ -1362,11 +1471,11 @@ __device__ __forceinline__ void run_lm_head(const DecodeParams &p, const CtaGeom
     const float *gain = gain_buf(p, sm, 0);
     float *rowv = sm + p.sm_sc;
     DecodeCtrl *ctrl = p.ctrl;
-    await_stage(p, h2, xv(p, xcur, p.L - 1, p.x_hid), p.h, s_abort);
-    csync();
+    NormAcc acc;
+    await_stage(p, h2, xv(p, xcur, p.L - 1, p.x_hid), p.h, s_abort, acc);
     mark_ready(p, 4 * p.L - 1);
+    norm_staged<TEPC>(h2, gain, xs, p.h, p.cemb, p.eps, sm + p.sm_red, acc);
     if (*s_abort) return;
-    block_rmsnorm<TEPC>(h2, gain, xs, p.h, p.cemb, p.eps, sm + p.sm_red);
     const int nlm = cg.lm_n;
     lm_stream<TF>(p, rg, cur, p.kind[K_LM], nlm, xs, s_abort, [&](int r, float a0, float a1) {
         rowv[r] = a0;
