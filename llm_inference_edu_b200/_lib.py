@@ -100,7 +100,7 @@ def lib():
             from . import build
             build.build()
         L = C.CDLL(LIB_PATH)
-        for name, (args, res) in SIGNATURES.items():
+        for name, (args, res) in list(SIGNATURES.items()) + list(BRIDGE_SIGNATURES.items()):
             f = getattr(L, name)
             f.argtypes = args
             f.restype = res
@@ -139,6 +139,26 @@ class QwenConfigC(C.Structure):
                                  "num_attention_heads", "num_key_value_heads", "max_position_embeddings")] + \
                [("rms_norm_eps", F), ("rope_theta", F), ("tie_word_embeddings", I32),
                 ("use_sliding_window", I32), ("has_rope_scaling", I32)]
+
+
+# The poll bridge (include/qwen_b200_bridge.h), the reference Apple host's
+# aie_* names.
+BRIDGE_SIGNATURES = {
+    "aie_abi_version": ([], U32),
+    "aie_open": ([U32, P, S, P], U32),
+    "aie_begin_ids": ([U64, P, S, U32], U32),
+    "aie_begin_text": ([U64, P, S, U32], U32),
+    "aie_next": ([U64], U32),
+    "aie_reset": ([U64], U32),
+    "aie_set_cancel": ([U64, U32], U32),
+    "aie_poll": ([U64, P], U32),
+    "aie_poll_text": ([U64, P, P, S, P], U32),
+    "aie_close": ([U64], U32),
+}
+
+
+class AieEvent(C.Structure):
+    _fields_ = [(n, U32) for n in ("kind", "code", "token", "processed", "history")]
 
 
 class SamplingC(C.Structure):

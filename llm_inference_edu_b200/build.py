@@ -14,7 +14,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "libqwen_b200.so")
-SOURCES = ["ops.cu", "decode.cu", "prefill.cu", "tc_gemm.cu", "tp.cu", "sampling.cu", "runtime.cu", "static_scratch.cu", "synthetic.cpp", "loader.cpp"]
+SOURCES = ["ops.cu", "decode.cu", "prefill.cu", "tc_gemm.cu", "tp.cu", "sampling.cu", "runtime.cu", "static_scratch.cu", "synthetic.cpp", "loader.cpp", "bridge.cpp"]
 HEADERS = ["common.cuh", "decode.cuh", "prefill.cuh", "multitoken.cuh", "tc_gemm.cuh", "tp.cuh", "sampling.cuh"]
 
 NVCC_FLAGS = [
@@ -34,6 +34,7 @@ def _stale():
     t = os.path.getmtime(OUT)
     deps = [os.path.join(CSRC, f) for f in SOURCES + HEADERS]
     deps.append(os.path.join(os.path.dirname(HERE), "include", "qwen_b200.h"))
+    deps.append(os.path.join(os.path.dirname(HERE), "include", "qwen_b200_bridge.h"))
     return any(os.path.getmtime(d) > t for d in deps)
 
 
@@ -45,6 +46,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
     # An object is rebuilt when its source, or any shared header, is newer.
     hdrs = [os.path.join(CSRC, f) for f in HEADERS]
     hdrs.append(os.path.join(os.path.dirname(HERE), "include", "qwen_b200.h"))
+    hdrs.append(os.path.join(os.path.dirname(HERE), "include", "qwen_b200_bridge.h"))
     t_hdr = max(os.path.getmtime(h) for h in hdrs)
     objs, procs = [], []
     for src in SOURCES:

@@ -54,3 +54,106 @@ def qwen2_tensor_shapes(cfg):
                     p + "self_attn.o_proj.weight": (h, h), p + "mlp.gate_proj.weight": (ff, h),
                     p + "mlp.up_proj.weight": (ff, h), p + "mlp.down_proj.weight": (h, ff)})
     return out
+
+
+# ----------------------------------------------------------- poll bridge ----
+
+def tiny_model_json(weights=None, config=None) -> bytes:
+    """The reference's tiny model file format (Decoder::from_json,
+    src/model.rs:185; {"config", "weights"}) for the Tiny-R weights."""
+    import json
+    from llm_inference_edu_b200 import presets
+    w = weights or presets.tiny_r_weights()
+    c = config or presets.tiny_r(32)
+    names = dict(attn_norm="attention_norm", q="query", k="key", v="value", o="attention_output",
+                 ffn_norm="ffn_norm", gate="gate", up="up", down="down")
+    doc = {
+        "config": {"vocab_size": c.vocab_size, "layers": c.layers, "hidden_dim": c.hidden_dim,
+                   "query_heads": c.query_heads, "kv_heads": c.kv_heads, "head_dim": c.head_dim,
+                   "ff_dim": c.ff_dim, "max_tokens": c.max_tokens, "rope_base": c.rope_base,
+                   "norm_epsilon": c.norm_epsilon},
+        "weights": {"embedding": [float(x) for x in w["embedding"]],
+                    "layers": [{names[k]: [float(x) for x in v] for k, v in l.items()} for l in w["layers"]],
+                    "final_norm": [float(x) for x in w["final_norm"]]},
+    }
+    return json.dumps(doc).encode()
+
+
+def bridge_event():
+    from llm_inference_edu_b200._lib import AieEvent
+    return AieEvent(99, 99, 99, 99, 99)
+
+
+def ev_tuple(e):
+    return (e.kind, e.code, e.token, e.processed, e.history)
+
+
+def bridge_wait(h, seconds=20.0):
+    """Polls until the worker's event arrives (src/tests.rs:14-28)."""
+    import ctypes as C
+    import time
+    from llm_inference_edu_b200._lib import lib
+    deadline = time.monotonic() + seconds
+    while True:
+        out = bridge_event()
+        st = lib().aie_poll(h, C.byref(out))
+        if st == 0:
+            return out
+        assert st == 1, st  # PENDING
+        assert ev_tuple(out) == (99,) * 5
+        assert time.monotonic() < deadline, "worker event timeout"
+        time.sleep(0.001)
+
+
+def bridge_open(source: bytes, kind: int = 0, seconds=20.0):
+    """aie_open, retrying while a closed worker still releases its model."""
+    import ctypes as C
+    import time
+    from llm_inference_edu_b200._lib import lib
+    h = C.c_uint64(0)
+    deadline = time.monotonic() + seconds
+    while True:
+        st = lib().aie_open(kind, source, len(source), C.byref(h))
+        if st != 4:  # BUSY
+            return st, h.value
+        assert time.monotonic() < deadline, "worker never released"
+        time.sleep(0.005)
+
+
+def _bf16_bits(a):
+    """FP32 values as BF16 bit patterns (round to nearest even; finite)."""
+    import numpy as np
+    a = np.asarray(a)
+    if a.dtype == np.uint16:
+        return a
+    f = np.ascontiguousarray(a, np.float32).view(np.uint32)
+    return ((f + 0x7fff + ((f >> 16) & 1)) >> 16).astype(np.uint16)
+
+
+def small_qwen_checkpoint(seed=5):
+    """A small Qwen2 checkpoint: (HF config.json dict, the matching
+    ModelConfig, its BF16 weight dictionary, the safetensors bytes)."""
+    from llm_inference_edu_b200 import presets, synthetic
+    hf = {"architectures": ["Qwen2ForCausalLM"], "model_type": "qwen2", "hidden_act": "silu",
+          "vocab_size": 256, "hidden_size": 64, "intermediate_size": 128, "num_hidden_layers": 2,
+          "num_attention_heads": 4, "num_key_value_heads": 2, "max_position_embeddings": 64,
+          "rms_norm_eps": 1e-6, "rope_theta": 10000.0, "tie_word_embeddings": True,
+          "torch_dtype": "bfloat16", "use_sliding_window": False}
+    cfg = presets.ModelConfig(256, 2, 64, 4, 2, 16, 128, 64, 10000.0, 1e-6, True, True)
+    w = synthetic.weights(cfg, seed=seed, dtype="bf16", bias_std=0.02, norm_std=0.1)
+    w = {"embedding": _bf16_bits(w["embedding"]), "final_norm": _bf16_bits(w["final_norm"]),
+         "layers": [{k: _bf16_bits(v) for k, v in L.items()} for L in w["layers"]]}
+    names = {"attn_norm": "input_layernorm.weight", "ffn_norm": "post_attention_layernorm.weight",
+             "q": "self_attn.q_proj.weight", "q_bias": "self_attn.q_proj.bias", "k": "self_attn.k_proj.weight",
+             "k_bias": "self_attn.k_proj.bias", "v": "self_attn.v_proj.weight", "v_bias": "self_attn.v_proj.bias",
+             "o": "self_attn.o_proj.weight", "gate": "mlp.gate_proj.weight", "up": "mlp.up_proj.weight",
+             "down": "mlp.down_proj.weight"}
+    shapes = {"q": (64, 64), "k": (32, 64), "v": (32, 64), "o": (64, 64), "gate": (128, 64), "up": (128, 64),
+              "down": (64, 128)}
+    t = {"model.embed_tokens.weight": ("BF16", (256, 64), w["embedding"].astype("<u2").tobytes()),
+         "model.norm.weight": ("BF16", (64,), w["final_norm"].astype("<u2").tobytes())}
+    for l, L in enumerate(w["layers"]):
+        for k, v in L.items():
+            t[f"model.layers.{l}.{names[k]}"] = ("BF16", shapes.get(k, (v.size,)), v.astype("<u2").tobytes())
+    data = safetensors_bytes(t)
+    return hf, cfg, w, data
