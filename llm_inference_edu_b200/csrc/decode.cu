@@ -59,6 +59,10 @@ __device__ __forceinline__ float ldcg(const float *p) { return __ldcg(p); }
 
 // Barrier among the compute warps only (the producer warp never joins).
 __device__ __forceinline__ void csync() { asm volatile("bar.sync 1, %0;" ::"n"(NT) : "memory"); }
+// Barrier of the warps of one GEMV team wider than a warp (ids 2..15).
+__device__ __forceinline__ void team_sync(int id, int threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
 
 // ------------------------------------------------------ activations ----
 //
@@ -573,7 +577,7 @@ __device__ __forceinline__ void ring_prewait(const DecodeParams &p, const Ring &
 template <int WF>
 __device__ __forceinline__ Cursor gemv_pairs(const DecodeParams &p, const Ring rg, Cursor cur, const KindGeom &g,
                                           int n, const float *xs, volatile int *s_abort, const Epi e,
-                                          bool prewaited = false) {
+                                          bool prewaited, float *tscr) {
     constexpr int Q = Fmt<WF>::EPC / 4;
     const int lg = g.lgG, G = 1 << lg, T = NT >> lg;
     const int t = threadIdx.x, lane = t & 31;
@@ -603,7 +607,7 @@ __device__ __forceinline__ Cursor gemv_pairs(const DecodeParams &p, const Ring r
         const int nu = two ? (rows + 1) >> 1 : rows;
 #pragma unroll 1
         for (int ub = 0; ub < nu; ub += T) {
-            if (ub + warp_team0 >= nu) break;  // warp-uniform
+            if (warp_team0 >= T || ub + warp_team0 >= nu) break;  // warp-uniform
             const int u = ub + tm;
             const bool act = u < nu;
             // Four independent partial-sum chains per row: two per chunk,
@@ -648,9 +652,33 @@ __device__ __forceinline__ Cursor gemv_pairs(const DecodeParams &p, const Ring r
             float s0 = ((a0.x + a0.y) + (b0.x + b0.y)) + ((c0.x + c0.y) + (d0.x + d0.y));
             float s1 = ((a1.x + a1.y) + (b1.x + b1.y)) + ((c1.x + c1.y) + (d1.x + d1.y));
 #pragma unroll 1
-            for (int off = G >> 1; off; off >>= 1) {
+            for (int off = (G < 32 ? G : 32) >> 1; off; off >>= 1) {
                 s0 += __shfl_xor_sync(FULL, s0, off);
                 s1 += __shfl_xor_sync(FULL, s1, off);
+            }
+            if (G > 32) {
+                // A team of W = G / 32 warps (a long row over more lanes):
+                // each warp's lane 0 leaves its sums in the team's scratch,
+                // the team meets at its own barrier, and its first thread
+                // adds them in warp order.  The second barrier frees the
+                // scratch for the next round.
+                const int W = G >> 5, wi = (t >> 5) & (W - 1);
+                float *ts = tscr + 2 * W * tm;
+                if (lane == 0) {
+                    ts[2 * wi] = s0;
+                    ts[2 * wi + 1] = s1;
+                }
+                team_sync(2 + tm, G);
+                if (lt == 0) {
+                    s0 = ts[0];
+                    s1 = ts[1];
+#pragma unroll 1
+                    for (int w = 1; w < W; ++w) {
+                        s0 += ts[2 * w];
+                        s1 += ts[2 * w + 1];
+                    }
+                }
+                team_sync(2 + tm, G);
             }
             if (act && lt == 0) {
                 const int r = r0 + (two ? 2 * u : u);
@@ -1272,7 +1300,7 @@ __device__ __forceinline__ void run_qkv(const DecodeParams &p, const CtaGeom &cg
     if (*s_abort) return;
     const Epi e{xv(p, xcur, l, p.x_qkv) + cg.qkv_r0, rv, nullptr, EPI_QKV,
                 !(p.withhold && l == 0 && blockIdx.x == 0)};
-    cur = gemv_pairs<WF>(p, rg, cur, p.kind[K_QKV], cg.qkv_n, xs, s_abort, e, true);
+    cur = gemv_pairs<WF>(p, rg, cur, p.kind[K_QKV], cg.qkv_n, xs, s_abort, e, true, sm + p.sm_red);
 }
 
 // The position-split exchange of head hh (split sp of nsp, layer l): this
@@ -1367,7 +1395,7 @@ __device__ __forceinline__ void run_attention(const DecodeParams &p, const Decod
         // Row scales: staged in shared memory for the first item, read from
         // global memory for the others.
         const Epi e{xv(p, xcur, l, p.x_part) + (size_t)hh * p.h + r0, a == 0 ? rv : Ly.so + r0, nullptr, EPI_O, 1};
-        cur = gemv_pairs<WF>(p, rg, cur, p.kind[K_O], n, xs, s_abort, e, a == 0);
+        cur = gemv_pairs<WF>(p, rg, cur, p.kind[K_O], n, xs, s_abort, e, a == 0, sm + p.sm_red);
         if (a + 1 < cg.natt) csync();  // xs is rewritten by the next item
     }
 }
@@ -1394,7 +1422,7 @@ __device__ __forceinline__ void run_gate_up(const DecodeParams &p, const CtaGeom
     if (blockIdx.x == 0)
         for (int i = threadIdx.x; i < p.h; i += NT) flag_nonfinite(p.ctrl, h2[i]);
     const Epi e{xv(p, xcur, l, p.x_act) + cg.gu_f0, rv, nullptr, EPI_GU, 1};
-    cur = gemv_pairs<WF>(p, rg, cur, p.kind[K_GU], 2 * cg.gu_n, xs, s_abort, e, true);
+    cur = gemv_pairs<WF>(p, rg, cur, p.kind[K_GU], 2 * cg.gu_n, xs, s_abort, e, true, sm + p.sm_red);
 }
 
 template <int WF>
@@ -1455,7 +1483,7 @@ __device__ __forceinline__ void run_down(const DecodeParams &p, const CtaGeom &c
     // this same CTA (src/kv_cache.rs:437-443: x_next = h' + down(a)).
     const float *h2 = sm + p.sm_h2 + cg.dn_r0, *rv = rv_buf(p, sm, 1);
     const Epi e{xv(p, xcur, l, p.x_hid) + cg.dn_r0, rv, h2, EPI_DN, 1};
-    cur = gemv_pairs<WF>(p, rg, cur, p.kind[K_DN], cg.dn_n, xs, s_abort, e, true);
+    cur = gemv_pairs<WF>(p, rg, cur, p.kind[K_DN], cg.dn_n, xs, s_abort, e, true, sm + p.sm_red);
 }
 
 // Final RMSNorm, this CTA's rows of the (tied) table, logits and the CTA's

@@ -62,7 +62,7 @@ struct KindGeom {
     int stride;  // bytes per padded row
     int C;       // 16-byte chunks per row
     int rpc;     // rows per ring slot (a multiple of U)
-    int lgG;     // log2 of the threads per unit (0..5)
+    int lgG;     // log2 of the threads per unit (2..7; above 5 a unit spans warps)
     int U;       // rows per unit
     int wave;    // ring slots waited for and released together (<= nslot / 2 or the block)
     unsigned rpc_magic;  // ceil(2^32 / rpc) when rpc > 1: r / rpc == umulhi(r, rpc_magic) for r < 2^16

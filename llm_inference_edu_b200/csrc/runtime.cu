@@ -674,12 +674,31 @@ static uint32_t session_build(Session &s) {
         // ring (at most three slots), so the rest keeps copies in flight.
         g.wave = block_slots <= nslot / 2 ? block_slots : std::max(1, std::min(3, nslot / 3));
         const int units = std::max(1, (std::min(rows_max[k], g.wave * g.rpc) + g.U - 1) / g.U);
-        long long best = -1;
-        for (int lg = 2; lg <= 5; ++lg) {  // team sizes 4 .. 32 (a run-time value on the device)
-            const int G = 1 << lg, teams = kDecodeThreads / G;
-            const long long rounds = (units + teams - 1) / teams;
-            const long long cost = rounds * ((long long)((g.C + G - 1) / G) * 4 * g.U + 20 + 2 * lg);
-            if (best < 0 || cost < best) { best = cost; g.lgG = lg; }
+        if (k == K_LM) {
+            long long best = -1;
+            for (int lg = 2; lg <= 5; ++lg) {  // team sizes 4 .. 32 (a run-time value on the device)
+                const int G = 1 << lg, teams = kDecodeThreads / G;
+                const long long rounds = (units + teams - 1) / teams;
+                const long long cost = rounds * ((long long)((g.C + G - 1) / G) * 4 * g.U + 20 + 2 * lg);
+                if (best < 0 || cost < best) { best = cost; g.lgG = lg; }
+            }
+        } else {
+            // Per-layer blocks: the fewest rounds, then the most lanes with
+            // chunks to multiply (one warp per SM sub-partition leaves its
+            // dependent chains exposed; more busy warps hide them), then the
+            // smaller team.  Teams of 64 or 128 threads span warps and meet
+            // at a named barrier.
+            long long best_rounds = -1, best_busy = -1;
+            for (int lg = 2; lg <= 7; ++lg) {
+                const int G = 1 << lg, teams = kDecodeThreads / G;
+                const long long rounds = (units + teams - 1) / teams;
+                const long long busy = (long long)std::min(units, teams) * std::min(G, g.C);
+                if (best_rounds < 0 || rounds < best_rounds || (rounds == best_rounds && busy > best_busy)) {
+                    best_rounds = rounds;
+                    best_busy = busy;
+                    g.lgG = lg;
+                }
+            }
         }
     }
     size_t smem = decode_smem_bytes(p);
