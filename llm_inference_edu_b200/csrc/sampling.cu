@@ -44,9 +44,63 @@ __device__ __forceinline__ unsigned pow2_ceil(unsigned v) {
     return p;
 }
 
+// Visits every element once: f(i, x, ok) for this thread's elements, in
+// batches of four 16-byte loads all in flight before the first use (the
+// passes are bound by load latency, not bandwidth).  Every thread of the
+// block makes the same calls (ok = false past the end), so f may use
+// warp-collective operations.  A base that is not 16-byte aligned takes
+// the scalar path.
+constexpr int kVisitBatch = 4;
+template <class F>
+__device__ __forceinline__ void visit(const float *__restrict__ logits, int n, F &&f) {
+    const int tid = threadIdx.x;
+    if (((uintptr_t)logits & 15) == 0) {
+        const float4 *l4 = reinterpret_cast<const float4 *>(logits);
+        const int n4 = n >> 2, iters = (n4 + SAMPLE_THREADS - 1) / SAMPLE_THREADS;
+#pragma unroll 1
+        for (int it = 0; it < iters; it += kVisitBatch) {
+            float4 v[kVisitBatch];
+#pragma unroll
+            for (int b = 0; b < kVisitBatch; ++b) {
+                const int f4 = (it + b) * SAMPLE_THREADS + tid;
+                v[b] = f4 < n4 ? __ldcg(l4 + f4) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            }
+#pragma unroll
+            for (int b = 0; b < kVisitBatch; ++b) {
+                const int f4 = (it + b) * SAMPLE_THREADS + tid;
+                const bool ok = f4 < n4;
+                f(4 * f4, v[b].x, ok);
+                f(4 * f4 + 1, v[b].y, ok);
+                f(4 * f4 + 2, v[b].z, ok);
+                f(4 * f4 + 3, v[b].w, ok);
+            }
+        }
+        const int i = 4 * n4 + tid;  // the last n % 4 elements
+        const bool ok = i < n;
+        f(i, ok ? __ldcg(logits + i) : 0.0f, ok);
+    } else {
+        const int iters = (n + SAMPLE_THREADS - 1) / SAMPLE_THREADS;
+#pragma unroll 1
+        for (int it = 0; it < iters; it += kVisitBatch) {
+            float v[kVisitBatch];
+#pragma unroll
+            for (int b = 0; b < kVisitBatch; ++b) {
+                const int i = (it + b) * SAMPLE_THREADS + tid;
+                v[b] = i < n ? __ldcg(logits + i) : 0.0f;
+            }
+#pragma unroll
+            for (int b = 0; b < kVisitBatch; ++b) {
+                const int i = (it + b) * SAMPLE_THREADS + tid;
+                f(i, v[b], i < n);
+            }
+        }
+    }
+}
+
 // Adds 1 to hist[bin] for every lane whose bin != kNoBin, one shared atomic
-// per distinct bin of the warp.
+// per distinct bin of the warp (nothing when no lane has a bin).
 __device__ __forceinline__ void warp_hist_add(unsigned *hist, unsigned bin) {
+    if (!__any_sync(0xffffffffu, bin != kNoBin)) return;
     const unsigned peers = __match_any_sync(0xffffffffu, bin);
     const int lane = threadIdx.x & 31;
     if (bin != kNoBin && lane == __ffs(peers) - 1) atomicAdd(&hist[bin], __popc(peers));
@@ -118,18 +172,17 @@ sample_kernel(const float *__restrict__ logits, int n, int greedy, float tempera
     float bv = 0.0f;
     int bi = INT_MAX;
     bool bad = false;
-    const int iters = (n + SAMPLE_THREADS - 1) / SAMPLE_THREADS;
-    for (int it = 0; it < iters; ++it) {
-        const int i = it * SAMPLE_THREADS + tid;
+    // Each thread meets its elements in increasing index order, so strict >
+    // keeps the lowest index among equal values.
+    visit(logits, n, [&](int i, float x, bool ok) {
         unsigned bin = kNoBin;
-        if (i < n) {
-            const float x = logits[i];
+        if (ok) {
             if (!isfinite(x)) bad = true;
             if (bi == INT_MAX || x > bv) { bv = x; bi = i; }
             bin = rank_key(x) >> 24;
         }
         if (!greedy) warp_hist_add(hist, bin);
-    }
+    });
     if (bad) s_bad = 1;
 #pragma unroll
     for (int off = 16; off; off >>= 1) {
@@ -170,15 +223,14 @@ sample_kernel(const float *__restrict__ logits, int n, int greedy, float tempera
         __syncthreads();  // everyone has read s_bin / s_before
         if (tid < 256) hist[tid] = 0;
         __syncthreads();
-        for (int it = 0; it < iters; ++it) {
-            const int i = it * SAMPLE_THREADS + tid;
+        visit(logits, n, [&](int, float x, bool ok) {
             unsigned bin = kNoBin;
-            if (i < n) {
-                const unsigned key = rank_key(logits[i]);
+            if (ok) {
+                const unsigned key = rank_key(x);
                 if ((key & pmask) == prefix) bin = (key >> (shift - 8)) & 0xffu;
             }
             warp_hist_add(hist, bin);
-        }
+        });
         __syncthreads();
     }
     // prefix = the k-th key; the gather takes (k - rem) keys before it and
@@ -190,20 +242,16 @@ sample_kernel(const float *__restrict__ logits, int n, int greedy, float tempera
     double *mass = k <= SAMPLE_SMEM_WORDS ? smass : gmass;
     if (tid == 0) s_fill = 0;
     __syncthreads();
-    for (int it = 0; it < iters; ++it) {
-        const int i = it * SAMPLE_THREADS + tid;
-        unsigned key = 0;
-        bool take = false;
-        if (i < n) {
-            key = rank_key(logits[i]);
-            take = key <= kth;
-        }
+    visit(logits, n, [&](int i, float x, bool ok) {
+        const unsigned key = ok ? rank_key(x) : 0xffffffffu;
+        const bool take = ok && key <= kth;
         const unsigned vote = __ballot_sync(0xffffffffu, take);
+        if (!vote) return;
         unsigned base = 0;
-        if (lane == 0 && vote) base = atomicAdd(&s_fill, __popc(vote));
+        if (lane == 0) base = atomicAdd(&s_fill, __popc(vote));
         base = __shfl_sync(0xffffffffu, base, 0);
         if (take) cand[base + __popc(vote & ((1u << lane) - 1u))] = (unsigned long long)key << 32 | (unsigned)i;
-    }
+    });
     for (unsigned j = m + tid; j < P; j += SAMPLE_THREADS) cand[j] = ~0ull;
     __syncthreads();
     bitonic_sort(cand, P);

@@ -4,6 +4,7 @@
     python -m llm_inference_edu_b200.workloads decode [--prompt 128] [--steps 8] [--profile]
     python -m llm_inference_edu_b200.workloads long [--prompt 8192] [--steps 128]
     python -m llm_inference_edu_b200.workloads qwen7b [--prompt 512] [--steps 64]
+    python -m llm_inference_edu_b200.workloads sample [--steps 64] [--top-k 40]
 
 Each builds the model on cuda:0 (0.5B INT8 with a BF16 table and KV unless
 noted), runs the workload through the public API and prints one line of
@@ -109,14 +110,35 @@ def qwen7b(prompt: int, steps: int) -> None:
     print(f"qwen7b: prefill {prompt / (t1 - t0):.0f} tok/s, decode {(t2 - t1) * 1e3 / steps:.2f} ms/token (wall)")
 
 
+def sample(steps: int, top_k: int) -> None:
+    """Seeded temperature/top-k sampling (T = 0.8) over Qwen-sized logits
+    (151,936 values, N(0, 2.5^2), new per draw) resident on the device; the
+    per-draw time includes the host generator and the result's read-back."""
+    import torch
+    from . import api
+    V = 151936
+    s = api.Sampler(api.Sampling.Temperature(0.8, top_k, 7))
+    g = torch.Generator(device="cuda").manual_seed(3)
+    rows = [torch.randn(V, device="cuda", generator=g) * 2.5 for _ in range(8)]
+    for i in range(4):
+        s.sample(rows[i % 8])
+    _sync()
+    t0 = time.perf_counter()
+    ids = [s.sample(rows[i % 8]) for i in range(steps)]
+    _sync()
+    print(f"sample: top-k {top_k}, {(time.perf_counter() - t0) * 1e6 / steps:.1f} us/draw (wall), "
+          f"last id {ids[-1]}")
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("workload", choices=["batched", "decode", "long", "qwen7b"])
+    ap.add_argument("workload", choices=["batched", "decode", "long", "qwen7b", "sample"])
     ap.add_argument("--sequences", type=int, default=64)
     ap.add_argument("--prompt", type=int, default=None)
     ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--profile", action="store_true")
     ap.add_argument("--linear", choices=["int8", "bf16"], default="int8")
+    ap.add_argument("--top-k", type=int, default=40)
     a = ap.parse_args(argv)
     if a.workload == "batched":
         batched(a.sequences, a.prompt or 2, a.steps or 4)
@@ -124,6 +146,8 @@ def main(argv=None) -> int:
         decode(a.prompt or 128, a.steps or 8, a.profile, a.linear)
     elif a.workload == "long":
         long(a.prompt or 8192, a.steps or 128)
+    elif a.workload == "sample":
+        sample(a.steps or 64, a.top_k)
     else:
         qwen7b(a.prompt or 512, a.steps or 64)
     return 0
