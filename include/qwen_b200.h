@@ -84,7 +84,14 @@ enum {
     QB_LOAD_UNSUPPORTED_CONFIG = 41,
     QB_LOAD_MISSING_TENSOR = 42,
     QB_LOAD_UNEXPECTED_TENSOR = 43,
-    QB_LOAD_INVALID_DTYPE = 44
+    QB_LOAD_INVALID_DTYPE = 44,
+    /* TokenizerError (src/tokenizer.rs:27-35) */
+    QB_TOKENIZER_JSON = 45,
+    QB_TOKENIZER_ENCODING = 46,
+    QB_TOKENIZER_UNSUPPORTED_ASSETS = 47,
+    QB_TOKENIZER_EMPTY_MESSAGES = 48,
+    QB_TOKENIZER_INVALID_TOKEN = 49,
+    QB_TOKENIZER_INVALID_STREAM = 50
 };
 
 /* Detail of the calling thread's last error: which buffer (argument order),
@@ -501,6 +508,53 @@ uint32_t qb_safetensors_inspect(const uint8_t *data, size_t len, const qb_qwen_c
 uint32_t qb_model_load_safetensors(const uint8_t *data, size_t len, const qb_qwen_config *config,
                                    uint32_t linear_format, uint32_t table_format, int device,
                                    uint64_t *out_model);
+
+/* ------------------------------------------------------------------ */
+/* Tokenizer and chat template (src/tokenizer.rs), host only           */
+/* ------------------------------------------------------------------ */
+/* The Qwen2 byte-level BPE of a tokenizer.json (NFC, the Qwen2 split
+ * pattern, ByteLevel pre-tokenizer and decoder, unnormalized added tokens);
+ * other configurations are QB_TOKENIZER_UNSUPPORTED_ASSETS, malformed JSON
+ * QB_TOKENIZER_JSON.  Text is UTF-8 (QB_TOKENIZER_ENCODING otherwise).
+ * Outputs: counts/lengths are always written; QB_INVALID_OUTPUT_LENGTH when
+ * the capacity is short (nothing copied). */
+enum { QB_ROLE_SYSTEM = 0, QB_ROLE_USER = 1, QB_ROLE_ASSISTANT = 2 };
+
+/* Tokenizer::from_bytes of a tokenizer.json (no chat checks). */
+uint32_t qb_tokenizer_from_json(const uint8_t *json, size_t len, uint64_t *out_tokenizer);
+/* ChatTokenizer::load, src/tokenizer.rs:68-124, from the three files'
+ * contents: tokenizer_config.json (Qwen2Tokenizer, no BOS, <|im_end|> EOS),
+ * generation_config.json (stop ids [151645, 151643]) and tokenizer.json
+ * (<|im_start|> 151644, <|im_end|> 151645, <|endoftext|> 151643).  The
+ * reference's inventory hash check of the files stays with the caller. */
+uint32_t qb_tokenizer_load_chat(const uint8_t *tokenizer_json, size_t tokenizer_len,
+                                const uint8_t *tokenizer_config_json, size_t config_len,
+                                const uint8_t *generation_config_json, size_t generation_len,
+                                uint64_t *out_tokenizer);
+/* ChatTokenizer::encode, src/tokenizer.rs:125-131 (no special tokens added). */
+uint32_t qb_tokenizer_encode(uint64_t tokenizer, const uint8_t *text, size_t len, uint32_t *ids,
+                             size_t capacity, size_t *count);
+/* ChatTokenizer::decode, src/tokenizer.rs:139-154: QB_TOKENIZER_INVALID_TOKEN
+ * (detail.actual = the id) for an id with no token. */
+uint32_t qb_tokenizer_decode(uint64_t tokenizer, const uint32_t *ids, size_t count,
+                             int32_t skip_special, char *text, size_t capacity, size_t *len);
+/* ChatTokenizer::stop_tokens (empty for qb_tokenizer_from_json). */
+uint32_t qb_tokenizer_stop_tokens(uint64_t tokenizer, uint32_t *ids, size_t capacity, size_t *count);
+uint32_t qb_tokenizer_free(uint64_t tokenizer);
+/* TextStream (src/tokenizer.rs:168-214): push writes the newly completed
+ * text (*has_text = 1) or nothing while a UTF-8 sequence is incomplete;
+ * special tokens print nothing; an unknown id is QB_TOKENIZER_INVALID_TOKEN
+ * and leaves the stream as it was. */
+uint32_t qb_tokenizer_stream_create(uint64_t tokenizer, uint64_t *out_stream);
+uint32_t qb_tokenizer_stream_push(uint64_t stream, uint32_t id, char *text, size_t capacity,
+                                  size_t *len, int32_t *has_text);
+uint32_t qb_tokenizer_stream_pending(uint64_t stream, size_t *pending);
+uint32_t qb_tokenizer_stream_free(uint64_t stream);
+/* render_chat, src/tokenizer.rs:40-63: messages as (role, UTF-8 content)
+ * triples; QB_TOKENIZER_EMPTY_MESSAGES for none. */
+uint32_t qb_render_chat(const uint32_t *roles, const uint8_t *const *contents, const size_t *lengths,
+                        size_t count, int32_t generation_prompt, char *text, size_t capacity,
+                        size_t *len);
 
 /* ------------------------------------------------------------------ */
 /* Tensor parallelism across the GPUs of one box                       */

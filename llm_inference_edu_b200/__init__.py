@@ -9,7 +9,7 @@ from .api import (  # noqa: F401
     BatchSession, CacheError, CachedSession, CancelFlag, Decoder, GenerationSession, GroupwiseInt8, LoadError,
     TpComm, inspect_safetensors, qwen_tensor_count,
     LinearError, ModelError, OpError, QbError, QuantError, RopeError, Sampler, Sampling, SamplingError,
-    StateError, Temperature,
+    StateError, Temperature, Role, TextStream, Tokenizer, TokenizerError, render_chat,
     embedding, linear, linear_int8, linear_int8_lanes4, linear_lanes4, masked_softmax,
     residual_add, rmsnorm, rope, silu, softmax, tp_shard_of)
 from . import synthetic  # noqa: F401

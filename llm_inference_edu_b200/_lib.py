@@ -51,6 +51,17 @@ SIGNATURES = {
     "qb_session_free": ([U64], U32),
     "qb_generation_create": ([U64, S, P, S, S, U32, S, P], U32),
     "qb_generation_create_sampled": ([U64, S, P, P, S, S, U32, S, P], U32),
+    "qb_tokenizer_from_json": ([P, S, P], U32),
+    "qb_tokenizer_load_chat": ([P, S, P, S, P, S, P], U32),
+    "qb_tokenizer_encode": ([U64, P, S, P, S, P], U32),
+    "qb_tokenizer_decode": ([U64, P, S, I32, P, S, P], U32),
+    "qb_tokenizer_stop_tokens": ([U64, P, S, P], U32),
+    "qb_tokenizer_free": ([U64], U32),
+    "qb_tokenizer_stream_create": ([U64, P], U32),
+    "qb_tokenizer_stream_push": ([U64, U32, P, S, P, P], U32),
+    "qb_tokenizer_stream_pending": ([U64, P], U32),
+    "qb_tokenizer_stream_free": ([U64], U32),
+    "qb_render_chat": ([P, P, P, S, I32, P, S, P], U32),
     "qb_sampler_create": ([P, I32, P], U32),
     "qb_sampler_validate_vocab": ([U64, S], U32),
     "qb_sampler_reset": ([U64], U32),

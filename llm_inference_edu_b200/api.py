@@ -40,7 +40,8 @@ STATUS_NAMES = [
     "InvalidHandle", "InvalidParameters", "NotStarted", "AlreadyStarted", "Cancelled",
     "EmptyLogits", "CudaError", "DeviceTimeout", "ContextLimit", "TraceLimit", "EmptyPrompt",
     "OutputLimit", "InvalidLayerCount", "Unsupported", "Format", "UnsupportedConfig", "MissingTensor",
-    "UnexpectedTensor", "InvalidDtype"]
+    "UnexpectedTensor", "InvalidDtype", "Json", "Encoding", "UnsupportedAssets", "EmptyMessages",
+    "InvalidToken", "InvalidStream"]
 
 
 class QbError(Exception):
@@ -684,6 +685,127 @@ class BatchSession:
 
 
 # ----------------------------------------------------------- generation --
+
+class TokenizerError(QbError):
+    """TokenizerError (src/tokenizer.rs:27-35): Json, Encoding,
+    UnsupportedAssets, EmptyMessages, InvalidToken (the id in .actual),
+    InvalidStream."""
+
+
+class Role:
+    """src/tokenizer.rs:8-22."""
+    System, User, Assistant = 0, 1, 2
+
+
+def _out_text(call, cap=1 << 16):
+    """Calls call(buf, cap, len_ptr) and grows the buffer once if needed."""
+    n = C.c_size_t()
+    buf = C.create_string_buffer(cap)
+    st = call(buf, cap, C.byref(n))
+    if st == 20 and n.value > cap:  # InvalidOutputLength: retry with the reported size
+        cap = n.value
+        buf = C.create_string_buffer(cap)
+        st = call(buf, cap, C.byref(n))
+    _check(st, TokenizerError)
+    return buf.raw[:n.value].decode("utf-8")
+
+
+def render_chat(messages, generation_prompt: bool) -> str:
+    """render_chat (src/tokenizer.rs:40-63): messages as (Role, content)."""
+    n = len(messages)
+    roles = (C.c_uint32 * max(n, 1))(*[r for r, _ in messages])
+    data = [c.encode() for _, c in messages]
+    ptrs = (C.c_char_p * max(n, 1))(*data)
+    lens = (C.c_size_t * max(n, 1))(*[len(d) for d in data])
+    return _out_text(lambda buf, cap, ln: lib().qb_render_chat(roles, ptrs, lens, n, int(generation_prompt),
+                                                                buf, cap, ln))
+
+
+class Tokenizer:
+    """ChatTokenizer (src/tokenizer.rs:64-166) over the host tokenizer of
+    the library: ``Tokenizer.load(directory)`` with the reference's checks,
+    or ``Tokenizer.from_json(bytes)`` for a bare tokenizer.json."""
+
+    def __init__(self, handle):
+        self.handle = handle
+
+    @classmethod
+    def from_json(cls, data: bytes) -> "Tokenizer":
+        h = C.c_uint64()
+        _check(lib().qb_tokenizer_from_json(data, len(data), C.byref(h)), TokenizerError)
+        return cls(h.value)
+
+    @classmethod
+    def load_files(cls, tokenizer_json: bytes, tokenizer_config: bytes, generation_config: bytes) -> "Tokenizer":
+        h = C.c_uint64()
+        _check(lib().qb_tokenizer_load_chat(tokenizer_json, len(tokenizer_json), tokenizer_config,
+                                            len(tokenizer_config), generation_config, len(generation_config),
+                                            C.byref(h)), TokenizerError)
+        return cls(h.value)
+
+    @classmethod
+    def load(cls, directory) -> "Tokenizer":
+        import os
+        read = lambda n: open(os.path.join(directory, n), "rb").read()
+        return cls.load_files(read("tokenizer.json"), read("tokenizer_config.json"),
+                              read("generation_config.json"))
+
+    def __del__(self):
+        if getattr(self, "handle", None):
+            lib().qb_tokenizer_free(self.handle)
+            self.handle = None
+
+    def encode(self, text: str) -> list:
+        b = text.encode("utf-8")
+        n = C.c_size_t()
+        _check(lib().qb_tokenizer_encode(self.handle, b, len(b), None, 0, C.byref(n)) if not b else 0,
+               TokenizerError)
+        cap = max(1, 2 * len(b) + 8)
+        out = (C.c_uint32 * cap)()
+        _check(lib().qb_tokenizer_encode(self.handle, b, len(b), out, cap, C.byref(n)), TokenizerError)
+        return list(out[:n.value])
+
+    def chat(self, messages, generation_prompt: bool) -> list:
+        return self.encode(render_chat(messages, generation_prompt))
+
+    def decode(self, ids, skip_special: bool) -> str:
+        a = (C.c_uint32 * max(len(ids), 1))(*ids)
+        return _out_text(lambda buf, cap, ln: lib().qb_tokenizer_decode(self.handle, a, len(ids),
+                                                                         int(skip_special), buf, cap, ln))
+
+    def stop_tokens(self) -> list:
+        out, n = (C.c_uint32 * 8)(), C.c_size_t()
+        _check(lib().qb_tokenizer_stop_tokens(self.handle, out, 8, C.byref(n)), TokenizerError)
+        return list(out[:n.value])
+
+    def text_stream(self) -> "TextStream":
+        h = C.c_uint64()
+        _check(lib().qb_tokenizer_stream_create(self.handle, C.byref(h)), TokenizerError)
+        return TextStream(h.value, self)
+
+
+class TextStream:
+    """TextStream (src/tokenizer.rs:168-214)."""
+
+    def __init__(self, handle, owner):
+        self.handle, self._owner = handle, owner
+
+    def __del__(self):
+        if getattr(self, "handle", None):
+            lib().qb_tokenizer_stream_free(self.handle)
+            self.handle = None
+
+    def push(self, token: int):
+        buf, n, has = C.create_string_buffer(4096), C.c_size_t(), C.c_int32()
+        _check(lib().qb_tokenizer_stream_push(self.handle, token, buf, 4096, C.byref(n), C.byref(has)),
+               TokenizerError)
+        return buf.raw[:n.value].decode("utf-8") if has.value else None
+
+    def pending_tokens(self) -> int:
+        n = C.c_size_t()
+        _check(lib().qb_tokenizer_stream_pending(self.handle, C.byref(n)), TokenizerError)
+        return n.value
+
 
 class SamplingError(QbError):
     """SamplingError (src/sampling.rs:13-18): InvalidParameters, EmptyLogits,

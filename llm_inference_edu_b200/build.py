@@ -14,8 +14,8 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "libqwen_b200.so")
-SOURCES = ["ops.cu", "decode.cu", "prefill.cu", "tc_gemm.cu", "tp.cu", "sampling.cu", "runtime.cu", "static_scratch.cu", "synthetic.cpp", "loader.cpp", "bridge.cpp"]
-HEADERS = ["common.cuh", "decode.cuh", "prefill.cuh", "multitoken.cuh", "tc_gemm.cuh", "tp.cuh", "sampling.cuh"]
+SOURCES = ["ops.cu", "decode.cu", "prefill.cu", "tc_gemm.cu", "tp.cu", "sampling.cu", "runtime.cu", "static_scratch.cu", "synthetic.cpp", "loader.cpp", "bridge.cpp", "tokenizer.cpp"]
+HEADERS = ["common.cuh", "decode.cuh", "prefill.cuh", "multitoken.cuh", "tc_gemm.cuh", "tp.cuh", "sampling.cuh", "json.h", "unicode_tables.inc"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

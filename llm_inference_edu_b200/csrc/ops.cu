@@ -424,7 +424,8 @@ const char *qb_status_name(uint32_t s) {
         "InvalidHandle", "InvalidParameters", "NotStarted", "AlreadyStarted", "Cancelled",
         "EmptyLogits", "CudaError", "DeviceTimeout", "ContextLimit", "TraceLimit", "EmptyPrompt",
         "OutputLimit", "InvalidLayerCount", "Unsupported", "Format", "UnsupportedConfig", "MissingTensor",
-        "UnexpectedTensor", "InvalidDtype"};
+        "UnexpectedTensor", "InvalidDtype", "Json", "Encoding", "UnsupportedAssets", "EmptyMessages",
+        "InvalidToken", "InvalidStream"};
     return s < sizeof(names) / sizeof(names[0]) ? names[s] : "Unknown";
 }
 

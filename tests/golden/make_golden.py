@@ -6,8 +6,8 @@ Run in a container that has the reference checkout:
 
 Two kinds of files are written:
 
-1. The reference's own golden vectors (``fixtures/t01..t04``, ``t25``,
-   ``t28``) copied byte-for-byte.  They were produced by the reference's
+1. The reference's own golden vectors (``fixtures/t01..t04``, ``t06``,
+   ``t25``, ``t28``) copied byte-for-byte.  They were produced by the reference's
    independent NumPy equations and are the vectors its Rust tests assert.
 2. ``tinyb-numpy.json``: golden logits and greedy ids for the Tiny-B
    workload (hidden 64, 4/2 heads, head_dim 16, ff 128, vocab 256, 2 layers,
@@ -33,7 +33,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
 COPIED = ["t01-inputs.json", "t01-expected.json", "t02-inputs.json", "t02-expected.json",
           "t03-inputs.json", "t03-expected.json", "t04-inputs.json", "t04-expected.json",
-          "t25-continuation.json", "t28-tiny-context.json"]
+          "t25-continuation.json", "t28-tiny-context.json", "t06-tokenizer.json"]
 
 
 def copy_reference_vectors(ref):
