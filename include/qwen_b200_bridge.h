@@ -17,11 +17,14 @@
  *      rejected), at most 8 MiB, held as FP32 on the device;
  *   1  a Qwen2 directory (UTF-8 path, at most 4096 bytes) holding config.json
  *      and model.safetensors (BF16), loaded as qb_model_load_safetensors does
- *      with a 32-position context, FP32 on the device.  The reference also
- *      verifies the files against its pinned inventory hashes and loads the
- *      tokenizer; here file integrity is the caller's, and with no tokenizer
- *      aie_begin_text is answered by an AIE_INVALID_INPUT event (as the
- *      reference answers it for tiny models).
+ *      with a 32-position context, FP32 on the device, and the chat
+ *      tokenizer's tokenizer.json, tokenizer_config.json and
+ *      generation_config.json (qb_tokenizer_load_chat): text prompts are
+ *      encoded on the worker, generation stops at the tokenizer's stop ids,
+ *      and token events carry the stream decoder's text.  The reference also
+ *      verifies the files against its pinned inventory hashes; here file
+ *      integrity is the caller's.  For tiny models aie_begin_text is
+ *      answered by an AIE_INVALID_INPUT event, as in the reference.
  * Models with max_tokens above 32 or a vocabulary above 151,936 are refused
  * (AIE_MODEL_FAILED), as the reference's bridge refuses them.
  */
@@ -62,7 +65,8 @@ uint32_t aie_open(uint32_t kind, const uint8_t *bytes, size_t length, uint64_t *
  * (8 positions for a Qwen directory), checked on the worker. */
 uint32_t aie_begin_ids(uint64_t handle, const uint32_t *ids, size_t count, uint32_t max_new);
 /* aie_begin_text, llm_cpu_bridge.h:41 (src/lib.rs:227-247): UTF-8, at most
- * 65,536 bytes; with no tokenizer the worker answers AIE_INVALID_INPUT. */
+ * 65,536 bytes; encoded by the source's tokenizer on the worker (a tiny
+ * model has none: AIE_INVALID_INPUT). */
 uint32_t aie_begin_text(uint64_t handle, const uint8_t *bytes, size_t length, uint32_t max_new);
 /* aie_next / aie_reset, llm_cpu_bridge.h:42-43: one greedy token (event
  * AIE_TOKEN, then AIE_STOPPED once stopped) / reset of history, cache and
@@ -76,8 +80,8 @@ uint32_t aie_set_cancel(uint64_t handle, uint32_t enabled);
  * event and opens command admission; AIE_PENDING and errors write nothing. */
 uint32_t aie_poll(uint64_t handle, AieEvent *out_event);
 /* aie_poll_text, llm_cpu_bridge.h:56-57 (src/lib.rs:288-323): as aie_poll
- * plus the event's text (a token event's "<id> "); `capacity` must be
- * exactly 4096. */
+ * plus the event's text (a token event's newly decoded text, or "<id> "
+ * for a tiny model); `capacity` must be exactly 4096. */
 uint32_t aie_poll_text(uint64_t handle, AieEvent *out_event, uint8_t *text, size_t capacity,
                        size_t *out_length);
 /* aie_close, llm_cpu_bridge.h:60 (src/lib.rs:324-339): invalidates the handle

@@ -148,10 +148,27 @@ bool read_file(const std::string &path, std::vector<uint8_t> &out) {
     return ok;
 }
 
-// load_qwen + Decoder::from_qwen(weights, 32) (src/worker.rs:85-95): the
-// directory's config.json and model.safetensors through the checkpoint
-// loader, a 32-position context, FP32 linears and table.
-bool load_qwen_dir(const std::string &dir, int device, ModelHandle &m, qb_model_config &c) {
+struct TokHandle {
+    uint64_t h = 0;
+    ~TokHandle() {
+        if (h) qb_tokenizer_free(h);
+    }
+};
+struct StreamHandle {
+    uint64_t h = 0;
+    ~StreamHandle() { reset(0); }
+    void reset(uint64_t nh) {
+        if (h) qb_tokenizer_stream_free(h);
+        h = nh;
+    }
+};
+
+// load_qwen + Decoder::from_qwen(weights, 32) + ChatTokenizer::load
+// (src/worker.rs:85-99): the directory's config.json and model.safetensors
+// through the checkpoint loader (a 32-position context, FP32 linears and
+// table), then tokenizer.json, tokenizer_config.json and
+// generation_config.json through the chat tokenizer's checks.
+bool load_qwen_dir(const std::string &dir, int device, ModelHandle &m, qb_model_config &c, TokHandle &tok) {
     std::vector<uint8_t> cfg_bytes, st;
     if (!read_file(dir + "/config.json", cfg_bytes)) return false;
     JVal cfg;
@@ -208,7 +225,12 @@ bool load_qwen_dir(const std::string &dir, int device, ModelHandle &m, qb_model_
     c = qb_model_config{};
     c.vocab_size = q.vocab_size;
     c.max_tokens = q.max_position_embeddings;
-    return true;
+    std::vector<uint8_t> tj, tc, gc;
+    if (!read_file(dir + "/tokenizer.json", tj) || !read_file(dir + "/tokenizer_config.json", tc) ||
+        !read_file(dir + "/generation_config.json", gc))
+        return false;
+    return qb_tokenizer_load_chat(tj.data(), tj.size(), tc.data(), tc.size(), gc.data(), gc.size(), &tok.h) ==
+           QB_OK;
 }
 
 bool valid_utf8(const uint8_t *s, size_t n) {
@@ -325,10 +347,11 @@ struct Source {
 // worker::run (src/worker.rs:68-243).
 void run(const Source &src, Engine &e, int device) {
     ModelHandle model;
+    TokHandle tok;
     qb_model_config c{};
     const bool loaded = src.kind == 0 ? load_tiny(src.bytes, device, model, c)
                                       : load_qwen_dir(std::string(src.bytes.begin(), src.bytes.end()), device,
-                                                      model, c);
+                                                      model, c, tok);
     if (!loaded || c.max_tokens > kBridgeContext || c.vocab_size > kBridgeVocab) {
         e.fatal.store(true);
         deliver(e, snapshot(nullptr, AIE_ERROR, AIE_MODEL_FAILED, -1), std::string());
@@ -336,9 +359,19 @@ void run(const Source &src, Engine &e, int device) {
     }
     if (!deliver(e, snapshot(nullptr, AIE_READY, AIE_OK, -1), std::string())) return;
     GenHandle gen;
-    const bool has_tokenizer = false;  // no tokenizer is built: text prompts are refused
-    const size_t admitted = src.kind == 1 ? kQwenAdmitted : c.max_tokens;
+    StreamHandle stream;
+    const bool has_tokenizer = tok.h != 0;
+    const size_t admitted = has_tokenizer ? kQwenAdmitted : c.max_tokens;
     const size_t capacity = c.max_tokens;
+    uint32_t stop_ids[8];
+    size_t nstops = 0;
+    if (has_tokenizer && qb_tokenizer_stop_tokens(tok.h, stop_ids, 8, &nstops) != QB_OK) nstops = 0;
+    auto new_stream = [&]() {
+        uint64_t sh = 0;
+        if (has_tokenizer && qb_tokenizer_stream_create(tok.h, &sh) != QB_OK) sh = 0;
+        stream.reset(sh);
+    };
+    new_stream();
     for (;;) {
         Command cmd;
         {
@@ -357,8 +390,21 @@ void run(const Source &src, Engine &e, int device) {
             bool ok = !started;
             std::vector<uint32_t> ids;
             if (ok) {
-                if (cmd.kind == Cmd::BeginIds) ids = cmd.ids;
-                else ok = has_tokenizer;
+                if (cmd.kind == Cmd::BeginIds) {
+                    ids = cmd.ids;
+                } else if (!has_tokenizer) {
+                    ok = false;
+                } else {
+                    // ChatTokenizer::encode of the plain text on the worker.
+                    size_t n = 0;
+                    const uint8_t *tb = (const uint8_t *)cmd.text.data();
+                    uint32_t st = qb_tokenizer_encode(tok.h, tb, cmd.text.size(), nullptr, 0, &n);
+                    if (st == QB_INVALID_OUTPUT_LENGTH || st == QB_OK) {
+                        ids.resize(n);
+                        st = qb_tokenizer_encode(tok.h, tb, cmd.text.size(), ids.data(), n, &n);
+                    }
+                    ok = st == QB_OK;
+                }
             }
             if (ok) {
                 ok = !ids.empty() && ids.size() <= admitted && cmd.max_new <= admitted - ids.size();
@@ -368,8 +414,8 @@ void run(const Source &src, Engine &e, int device) {
                 ev = snapshot(&gen, AIE_ERROR, AIE_INVALID_INPUT, -1);
             } else {
                 uint64_t cand = 0;
-                const uint32_t st = qb_generation_create(model.h, capacity, nullptr, 0, cmd.max_new, QB_KV_F32,
-                                                         kBudget, &cand);
+                const uint32_t st = qb_generation_create(model.h, capacity, nstops ? stop_ids : nullptr, nstops,
+                                                         cmd.max_new, QB_KV_F32, kBudget, &cand);
                 if (st != QB_OK) {
                     ev = failure(&gen, st);
                 } else {
@@ -378,8 +424,12 @@ void run(const Source &src, Engine &e, int device) {
                     // failed evaluation resumes or reports from it); one
                     // refused before admission leaves the previous state.
                     qb_generation_info ci{};
-                    if (qb_generation_info_get(cand, &ci) == QB_OK && ci.history_len > 0) gen.reset(cand);
-                    else qb_generation_free(cand);
+                    if (qb_generation_info_get(cand, &ci) == QB_OK && ci.history_len > 0) {
+                        gen.reset(cand);
+                        new_stream();
+                    } else {
+                        qb_generation_free(cand);
+                    }
                     ev = r == QB_OK ? snapshot(&gen, AIE_STARTED, AIE_OK, -1) : failure(&gen, r);
                 }
             }
@@ -387,20 +437,36 @@ void run(const Source &src, Engine &e, int device) {
             if (!gen.h) {
                 ev = snapshot(nullptr, AIE_ERROR, AIE_INVALID_INPUT, -1);
             } else {
-                uint32_t tok = 0;
+                uint32_t tid = 0;
                 int32_t has = 0;
-                const uint32_t r = qb_generation_next_token(gen.h, cancel, &tok, &has);
+                const uint32_t r = qb_generation_next_token(gen.h, cancel, &tid, &has);
                 if (r != QB_OK) {
                     ev = failure(&gen, r);
                 } else if (has) {
-                    text = std::to_string(tok) + " ";  // ids, as the reference emits without a tokenizer
-                    ev = snapshot(&gen, AIE_TOKEN, AIE_OK, tok);
+                    bool decoded = true;
+                    if (stream.h) {
+                        // TextStream::push: the newly completed text (or none yet).
+                        char buf[kMaxText];
+                        size_t n = 0;
+                        int32_t has_text = 0;
+                        decoded = qb_tokenizer_stream_push(stream.h, tid, buf, kMaxText, &n, &has_text) == QB_OK;
+                        if (decoded && has_text) text.assign(buf, n);
+                    } else {
+                        text = std::to_string(tid) + " ";  // ids, as the reference emits without a tokenizer
+                    }
+                    if (decoded) {
+                        ev = snapshot(&gen, AIE_TOKEN, AIE_OK, tid);
+                    } else {
+                        ev = snapshot(&gen, AIE_ERROR, AIE_EXECUTION_FAILED, -1);
+                        ev.processed = 0;  // terminal: no valid cache is exposed
+                    }
                 } else {
                     ev = snapshot(&gen, AIE_STOPPED, AIE_OK, -1);
                 }
             }
         } else {  // Reset
             if (gen.h) qb_generation_reset(gen.h);
+            new_stream();
             set_cancel(e, false);
             ev = snapshot(&gen, AIE_RESET_EVENT, AIE_OK, -1);
         }

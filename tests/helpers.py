@@ -130,16 +130,16 @@ def _bf16_bits(a):
     return ((f + 0x7fff + ((f >> 16) & 1)) >> 16).astype(np.uint16)
 
 
-def small_qwen_checkpoint(seed=5):
+def small_qwen_checkpoint(seed=5, vocab=256):
     """A small Qwen2 checkpoint: (HF config.json dict, the matching
     ModelConfig, its BF16 weight dictionary, the safetensors bytes)."""
     from llm_inference_edu_b200 import presets, synthetic
     hf = {"architectures": ["Qwen2ForCausalLM"], "model_type": "qwen2", "hidden_act": "silu",
-          "vocab_size": 256, "hidden_size": 64, "intermediate_size": 128, "num_hidden_layers": 2,
+          "vocab_size": vocab, "hidden_size": 64, "intermediate_size": 128, "num_hidden_layers": 2,
           "num_attention_heads": 4, "num_key_value_heads": 2, "max_position_embeddings": 64,
           "rms_norm_eps": 1e-6, "rope_theta": 10000.0, "tie_word_embeddings": True,
           "torch_dtype": "bfloat16", "use_sliding_window": False}
-    cfg = presets.ModelConfig(256, 2, 64, 4, 2, 16, 128, 64, 10000.0, 1e-6, True, True)
+    cfg = presets.ModelConfig(vocab, 2, 64, 4, 2, 16, 128, 64, 10000.0, 1e-6, True, True)
     w = synthetic.weights(cfg, seed=seed, dtype="bf16", bias_std=0.02, norm_std=0.1)
     w = {"embedding": _bf16_bits(w["embedding"]), "final_norm": _bf16_bits(w["final_norm"]),
          "layers": [{k: _bf16_bits(v) for k, v in L.items()} for L in w["layers"]]}
@@ -150,10 +150,38 @@ def small_qwen_checkpoint(seed=5):
              "down": "mlp.down_proj.weight"}
     shapes = {"q": (64, 64), "k": (32, 64), "v": (32, 64), "o": (64, 64), "gate": (128, 64), "up": (128, 64),
               "down": (64, 128)}
-    t = {"model.embed_tokens.weight": ("BF16", (256, 64), w["embedding"].astype("<u2").tobytes()),
+    t = {"model.embed_tokens.weight": ("BF16", (vocab, 64), w["embedding"].astype("<u2").tobytes()),
          "model.norm.weight": ("BF16", (64,), w["final_norm"].astype("<u2").tobytes())}
     for l, L in enumerate(w["layers"]):
         for k, v in L.items():
             t[f"model.layers.{l}.{names[k]}"] = ("BF16", shapes.get(k, (v.size,)), v.astype("<u2").tobytes())
     data = safetensors_bytes(t)
     return hf, cfg, w, data
+
+
+def chat_tokenizer_files(directory, **over):
+    """tokenizer.json, tokenizer_config.json and generation_config.json of a
+    chat tokenizer in `directory`: the synthetic golden tokenizer padded to
+    151,643 vocabulary entries so that its three special tokens take Qwen's
+    ids 151643-151645 (in the Qwen file they are added tokens past the
+    vocabulary).  `over` replaces config fields ("cfg" / "gen" dicts)."""
+    import json
+    import os
+    here = os.path.dirname(os.path.abspath(__file__))
+    doc = json.loads(open(os.path.join(here, "golden", "tokenizer-synthetic.json"), encoding="utf-8").read())
+    vocab = doc["model"]["vocab"]
+    order = {"<|endoftext|>": 0, "<|im_start|>": 1, "<|im_end|>": 2}
+    for a in doc["added_tokens"]:
+        vocab.pop(a["content"], None)
+    doc["added_tokens"] = sorted(doc["added_tokens"], key=lambda a: order[a["content"]])
+    for k in range(len(vocab), 151643):
+        vocab[f"<pad{k}>"] = k
+    cfg = {"tokenizer_class": "Qwen2Tokenizer", "add_bos_token": False, "bos_token": None,
+           "eos_token": "<|im_end|>"}
+    gen = {"eos_token_id": [151645, 151643]}
+    cfg.update(over.get("cfg", {}))
+    gen.update(over.get("gen", {}))
+    for name, obj in (("tokenizer.json", doc), ("tokenizer_config.json", cfg), ("generation_config.json", gen)):
+        with open(os.path.join(str(directory), name), "w") as f:
+            json.dump(obj, f)
+    return directory

@@ -158,37 +158,58 @@ def test_failure_after_the_kv_write_leaves_no_valid_prefix():
     assert L.aie_close(h) == OK
 
 
-def test_qwen_directory_source_decodes_like_the_checkpoint(tmp_path):
-    # Source kind 1: config.json and model.safetensors of a small Qwen2
-    # checkpoint; the greedy ids equal those of the same file loaded with
-    # qb_model_load_safetensors (FP32 linears and table) in this process.
+def test_qwen_directory_source_with_tokenizer(tmp_path):
+    # Source kind 1 (src/worker.rs:85-99): config.json and model.safetensors
+    # of a small Qwen2 checkpoint with the vocabulary of its chat tokenizer
+    # (151,646 ids), and the tokenizer's three files.  A text prompt is
+    # encoded on the worker; the greedy ids equal those of the same file
+    # loaded directly (token by token, as the worker evaluates a prompt it
+    # may cancel); each token event carries the stream decoder's text.
     import llm_inference_edu_b200 as qb
+    from helpers import chat_tokenizer_files
     L = _L()
-    hf, _cfg, _w, data = small_qwen_checkpoint(seed=9)
+    hf, _cfg, _w, data = small_qwen_checkpoint(seed=9, vocab=151646)
     (tmp_path / "config.json").write_text(json.dumps(hf))
     (tmp_path / "model.safetensors").write_bytes(data)
-    prompt = [3, 17, 200]
+    chat_tokenizer_files(tmp_path)
+    tok = qb.Tokenizer.load(tmp_path)
+    prompt = tok.encode("Hello!")
+    assert 0 < len(prompt) <= 5
     m = qb.Decoder.from_safetensors(data, hf)
     s = qb.CachedSession(m, 32)
-    # token by token, as the worker evaluates a prompt it may cancel
     for t in prompt:
         lg = s.step(t)
     want = [int(np.argmax(lg))]
-    for _ in range(4):
+    for _ in range(2):
         want.append(int(np.argmax(s.step(want[-1]))))
+    stream = tok.text_stream()
+    texts = [stream.push(t) or "" for t in want]
     h = _ready(str(tmp_path).encode(), kind=1)
-    assert L.aie_begin_ids(h, _ids(*prompt), 3, 6) == OK  # 3 + 6 > 8 admitted positions
+    assert L.aie_begin_text(h, b"Hello! Hello! Hello!", 20, 3) == OK  # more than 8 positions
     assert bridge_wait(h).code == INVALID_INPUT
-    assert L.aie_begin_ids(h, _ids(*prompt), 3, 5) == OK
-    assert bridge_wait(h).kind == STARTED
-    got = []
-    for _ in range(5):
+    assert L.aie_begin_text(h, b"Hello!", 6, 3) == OK
+    ev = bridge_wait(h)
+    assert (ev.kind, ev.processed, ev.history) == (STARTED, len(prompt), len(prompt))
+    out, length = bridge_event(), C.c_size_t()
+    text = (C.c_uint8 * 4096)()
+    import time
+    for k in range(3):
         assert L.aie_next(h) == OK
-        ev = bridge_wait(h)
-        assert ev.kind == TOKEN
-        got.append(ev.token)
-    assert got == want
+        deadline = time.monotonic() + 20
+        while (st := L.aie_poll_text(h, C.byref(out), text, 4096, C.byref(length))) == PENDING:
+            assert time.monotonic() < deadline
+            time.sleep(0.001)
+        assert st == OK and out.kind == TOKEN and out.token == want[k]
+        assert bytes(text[:length.value]).decode() == texts[k]
+    assert L.aie_next(h) == OK
+    assert bridge_wait(h).kind == STOPPED
     assert L.aie_close(h) == OK
-    st, bad = bridge_open(str(tmp_path / "missing").encode(), kind=1)
+    # Without the tokenizer's files the source does not load (the reference
+    # loads its tokenizer with the weights).
+    bare = tmp_path / "bare"
+    bare.mkdir()
+    (bare / "config.json").write_text(json.dumps(hf))
+    (bare / "model.safetensors").write_bytes(data)
+    st, bad = bridge_open(str(bare).encode(), kind=1)
     assert st == OK and bridge_wait(bad).code == MODEL_FAILED
     assert L.aie_close(bad) == OK

@@ -17,6 +17,7 @@ import os
 import pytest
 
 from conftest import GOLDEN, golden
+from helpers import chat_tokenizer_files
 
 SYN = os.path.join(GOLDEN, "tokenizer-synthetic.json")
 
@@ -88,38 +89,12 @@ def test_render_chat_matches_the_reference_fixture():
     assert e.value.kind == "EmptyMessages"
 
 
-def _chat_files(tmp_path, **over):
-    # The synthetic tokenizer padded to 151,643 vocabulary entries so that
-    # its three special tokens take Qwen's ids 151643-151645.
-    doc = json.loads(open(SYN, encoding="utf-8").read())
-    vocab = doc["model"]["vocab"]
-    specials = [a["content"] for a in doc["added_tokens"]]
-    for c in specials:  # in the Qwen file they are added tokens only, past the vocabulary
-        vocab.pop(c, None)
-    order = {"<|endoftext|>": 0, "<|im_start|>": 1, "<|im_end|>": 2}
-    doc["added_tokens"] = sorted(doc["added_tokens"], key=lambda a: order[a["content"]])
-    n = len(vocab)
-    for k in range(n, 151643):
-        vocab[f"<pad{k}>"] = k
-    assert sorted(specials, key=order.get) == ["<|endoftext|>", "<|im_start|>", "<|im_end|>"]
-    cfg = {"tokenizer_class": "Qwen2Tokenizer", "add_bos_token": False, "bos_token": None,
-           "eos_token": "<|im_end|>"}
-    gen = {"eos_token_id": [151645, 151643]}
-    cfg.update(over.get("cfg", {}))
-    gen.update(over.get("gen", {}))
-    files = {"tokenizer.json": json.dumps(doc), "tokenizer_config.json": json.dumps(cfg),
-             "generation_config.json": json.dumps(gen)}
-    for name, text in files.items():
-        (tmp_path / name).write_text(text)
-    return tmp_path
-
-
 def test_chat_tokenizer_load_checks(tmp_path):
     # src/tokenizer.rs:68-124
     import llm_inference_edu_b200 as qb
     ok = tmp_path / "ok"
     ok.mkdir()
-    t = qb.Tokenizer.load(_chat_files(ok))
+    t = qb.Tokenizer.load(chat_tokenizer_files(ok))
     assert t.stop_tokens() == [151645, 151643]
     assert t.encode("<|im_start|>user\nx<|im_end|>\n")[0] == 151644
     assert t.encode("<|im_start|>user\nx<|im_end|>\n")[-2] == 151645
@@ -129,11 +104,11 @@ def test_chat_tokenizer_load_checks(tmp_path):
         d = tmp_path / f"bad{k}"
         d.mkdir()
         with pytest.raises(qb.TokenizerError) as e:
-            qb.Tokenizer.load(_chat_files(d, **over))
+            qb.Tokenizer.load(chat_tokenizer_files(d, **over))
         assert e.value.kind == "UnsupportedAssets", over
     d = tmp_path / "json"
     d.mkdir()
-    _chat_files(d)
+    chat_tokenizer_files(d)
     (d / "tokenizer.json").write_text("{not json")
     with pytest.raises(qb.TokenizerError) as e:
         qb.Tokenizer.load(d)
