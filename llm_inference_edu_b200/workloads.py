@@ -3,7 +3,7 @@
     python -m llm_inference_edu_b200.workloads batched [--sequences 64] [--prompt 2] [--steps 4]
     python -m llm_inference_edu_b200.workloads decode [--prompt 128] [--steps 8] [--profile]
     python -m llm_inference_edu_b200.workloads long [--prompt 8192] [--steps 128]
-    python -m llm_inference_edu_b200.workloads qwen7b [--prompt 512] [--steps 64]
+    python -m llm_inference_edu_b200.workloads qwen7b [--prompt 512] [--steps 64] [--layers 28]
     python -m llm_inference_edu_b200.workloads sample [--steps 64] [--top-k 40]
 
 Each builds the model on cuda:0 (0.5B INT8 with a BF16 table and KV unless
@@ -93,10 +93,12 @@ def long(prompt: int, steps: int) -> None:
     decode(prompt, steps, profile=False)
 
 
-def qwen7b(prompt: int, steps: int) -> None:
+def qwen7b(prompt: int, steps: int, layers: int = 28) -> None:
+    """The 7B shape (fewer layers for a small profiling case)."""
+    from dataclasses import replace
     from . import api
     cap = prompt + steps + 8
-    cfg = presets.qwen_7b(cap)
+    cfg = replace(presets.qwen_7b(cap), layers=layers)
     m = _model(cfg, seed=2)
     s = api.CachedSession(m, cap, kv_dtype="bf16", budget=0)
     _sync()
@@ -107,7 +109,8 @@ def qwen7b(prompt: int, steps: int) -> None:
     s.decode_greedy(tok, steps)
     _sync()
     t2 = time.perf_counter()
-    print(f"qwen7b: prefill {prompt / (t1 - t0):.0f} tok/s, decode {(t2 - t1) * 1e3 / steps:.2f} ms/token (wall)")
+    print(f"qwen7b ({layers} layers): prefill {prompt / (t1 - t0):.0f} tok/s, "
+          f"decode {(t2 - t1) * 1e3 / steps:.2f} ms/token (wall)")
 
 
 def sample(steps: int, top_k: int) -> None:
@@ -139,6 +142,7 @@ def main(argv=None) -> int:
     ap.add_argument("--profile", action="store_true")
     ap.add_argument("--linear", choices=["int8", "bf16"], default="int8")
     ap.add_argument("--top-k", type=int, default=40)
+    ap.add_argument("--layers", type=int, default=28)
     a = ap.parse_args(argv)
     if a.workload == "batched":
         batched(a.sequences, a.prompt or 2, a.steps or 4)
@@ -149,7 +153,7 @@ def main(argv=None) -> int:
     elif a.workload == "sample":
         sample(a.steps or 64, a.top_k)
     else:
-        qwen7b(a.prompt or 512, a.steps or 64)
+        qwen7b(a.prompt or 512, a.steps or 64, a.layers)
     return 0
 
 
