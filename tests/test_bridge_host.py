@@ -88,3 +88,20 @@ def test_poll_text_checks_its_outputs_first():
     ev = bridge_wait(h)  # the event is still there
     assert ev.code == MODEL_FAILED
     assert L.aie_close(h) == OK
+
+
+def test_qwen_directory_without_files_fails_on_the_worker(tmp_path):
+    # Source kind 1 reads config.json, model.safetensors and the tokenizer's
+    # files on the worker; a directory without them is AIE_MODEL_FAILED
+    # (src/worker.rs:85-104), decided before any device work.
+    L = lib()
+    st, h = bridge_open(str(tmp_path / "absent").encode(), kind=1)
+    assert st == OK
+    ev = bridge_wait(h)
+    assert (ev.kind, ev.code) == (ERROR, MODEL_FAILED)
+    assert L.aie_begin_text(h, b"hi", 2, 4) == EXECUTION_FAILED
+    assert L.aie_close(h) == OK
+    (tmp_path / "config.json").write_text('{"model_type": "qwen2"}')
+    st, h = bridge_open(str(tmp_path).encode(), kind=1)
+    assert st == OK and bridge_wait(h).code == MODEL_FAILED
+    assert L.aie_close(h) == OK
