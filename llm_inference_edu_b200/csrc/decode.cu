@@ -437,12 +437,14 @@ __device__ void prefetch_phase(const DecodeParams &p, const DecodeLayer *lay, co
         return;
     }
     const DecodeLayer &Ly = lay[k >> 2];
+    const size_t cap = (size_t)p.pf_cap;
     switch (k & 3) {
-    case 0: prefetch_rows(Ly.wqkv + (size_t)cg.qkv_r0 * p.sh, (size_t)cg.qkv_n * p.sh); break;
+    case 0: prefetch_rows(Ly.wqkv + (size_t)cg.qkv_r0 * p.sh, min((size_t)cg.qkv_n * p.sh, cap)); break;
     case 1: {
         const size_t esz = p.kv_bf16 ? 2 : 4;
         for (int a = 0; a < cg.natt; ++a) {
-            prefetch_rows(Ly.wo + ((size_t)cg.att_hh[a] * p.h + cg.att_r0[a]) * p.shd, (size_t)cg.att_n[a] * p.shd);
+            prefetch_rows(Ly.wo + ((size_t)cg.att_hh[a] * p.h + cg.att_r0[a]) * p.shd,
+                          min((size_t)cg.att_n[a] * p.shd, cap));
             const int g = cg.att_hh[a] / p.group;
             // The group's block of every page that holds cached positions.
             const int *ptab = (const int *)(sm + p.sm_ptab);
@@ -457,8 +459,8 @@ __device__ void prefetch_phase(const DecodeParams &p, const DecodeLayer *lay, co
         }
         break;
     }
-    case 2: prefetch_rows(Ly.wgu + (size_t)2 * cg.gu_f0 * p.sh, (size_t)2 * cg.gu_n * p.sh); break;
-    default: prefetch_rows(Ly.wd + (size_t)cg.dn_r0 * p.sff, (size_t)cg.dn_n * p.sff); break;
+    case 2: prefetch_rows(Ly.wgu + (size_t)2 * cg.gu_f0 * p.sh, min((size_t)2 * cg.gu_n * p.sh, cap)); break;
+    default: prefetch_rows(Ly.wd + (size_t)cg.dn_r0 * p.sff, min((size_t)cg.dn_n * p.sff, cap)); break;
     }
 }
 

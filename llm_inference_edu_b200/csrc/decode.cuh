@@ -121,6 +121,7 @@ struct DecodeParams {
     unsigned long long *trace;
     unsigned long long timeout_ns;
     int prefetch;             // L2 prefetch of upcoming weights by the producer warp
+    unsigned long long pf_cap;  // bytes of one block a CTA prefetches (the grid's share of L2 per phase)
     // Fault-path test hook: nonzero = CTA 0 does not publish its layer-0 QKV
     // outputs, so the polls that read them run out (ERR_TIMEOUT).  0 in
     // every normal step.

@@ -575,6 +575,11 @@ static uint32_t session_build(Session &s) {
     p.ctrl = s.ctrl.as<DecodeCtrl>();
     p.timeout_ns = 2000000000ull;
     p.prefetch = 1;
+    // Three phases are prefetched ahead: each may hold 24 MB of L2 across
+    // the grid, so larger blocks (the 7B shape's gate/up and down) are
+    // prefetched only in part instead of evicting themselves before their
+    // copies read them.
+    p.pf_cap = (24ull << 20) / (unsigned long long)std::max(1, s.grid);
     p.withhold = 0;
     // Rows each CTA owns in every phase (floor(n * b / G) splits), and its
     // attention items: (query head, o_proj row range) pairs wi = b + m * G.
