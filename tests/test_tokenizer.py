@@ -134,3 +134,32 @@ def test_unsupported_configurations_and_bad_text():
     n = C.c_size_t()
     assert lib().qb_tokenizer_encode(t.handle, b"\xff", 1, None, 0, C.byref(n)) == 46  # Encoding
     assert lib().qb_tokenizer_encode(t.handle, b"Hello!", 6, None, 0, C.byref(n)) == 20 and n.value == 5
+
+
+def test_random_texts_match_hf_tokenizers():
+    # Differential check against the library the reference wraps, on 600
+    # seeded random strings drawn from every class the split pattern and NFC
+    # distinguish: letters of several scripts (with case), digits and other
+    # numbers, combining marks in both orders, Hangul jamo, spaces, tabs,
+    # newlines and other Unicode whitespace, apostrophe contractions,
+    # symbols, emoji and the special tokens.
+    tokenizers = pytest.importorskip("tokenizers")
+    import random
+    hf = tokenizers.Tokenizer.from_file(SYN)
+    t = _tok()
+    pool = (list("abcXYZ") + list("éüñÅ") + list("приВЕТ") + list("世界中") + list("καλΩ") + list("0123")
+            + ["٣", "½", "Ⅷ"] + ["́", "̈", "̣", "̇", "̊"]
+            + ["ᄀ", "ᅡ", "ᆨ", "각"] + [" ", " ", "  ", "\t", "\n", "\r\n", " ", "　",
+                                                          " ", "\u0085"]
+            + ["'s", "'T", "'re", "'VE", "'m", "'LL", "'d", "'ſ", "'"] + list("!?.,;:-()#$%&*+/<=>@[]^_`{|}~")
+            + ["🙂", "🌍", "👩‍💻", "‍"] + ["<|im_start|>", "<|im_end|>", "<|endoftext|>", "<|im_"])
+    rng = random.Random(1234)
+    for k in range(600):
+        text = "".join(rng.choice(pool) for _ in range(rng.randint(0, 24)))
+        want = hf.encode(text, add_special_tokens=False).ids
+        got = t.encode(text)
+        assert got == want, (k, text)
+        assert t.decode(got, False) == hf.decode(want, skip_special_tokens=False), (k, text)
+        assert t.decode(got, True) == hf.decode(want, skip_special_tokens=True), (k, text)
+        ds, s = tokenizers.decoders.DecodeStream(skip_special_tokens=True), t.text_stream()
+        assert [s.push(i) for i in got] == [ds.step(hf, i) for i in want], (k, text)
