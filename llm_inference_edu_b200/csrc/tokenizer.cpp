@@ -11,7 +11,8 @@
 //                 (no prefix space, no regex): each piece's UTF-8 bytes as
 //                 the GPT-2 byte alphabet;
 //   model         BPE: the piece's symbols merged pair by pair, lowest merge
-//                 rank first (leftmost among equals), then looked up;
+//                 rank first (leftmost among equals; a heap of candidate
+//                 pairs), then looked up;
 //   decoder       ByteLevel: tokens back to bytes, then lossy UTF-8;
 //   stream        step_decode_stream: text is emitted only when the decoded
 //                 suffix no longer ends in U+FFFD.
@@ -24,6 +25,7 @@
 #include <map>
 #include <memory>
 #include <mutex>
+#include <queue>
 #include <string>
 #include <unordered_map>
 #include <vector>
@@ -398,22 +400,45 @@ struct Tokenizer {
             if (it == vocab.end()) return QB_TOKENIZER_ENCODING;  // no unknown token in this model
             sym.push_back(it->second);
         }
-        for (;;) {
-            uint32_t best_rank = 0xffffffffu, best_id = 0;
-            size_t best = (size_t)-1;
-            for (size_t i = 0; i + 1 < sym.size(); ++i) {
-                auto it = merges.find((uint64_t)sym[i] << 32 | sym[i + 1]);
-                if (it != merges.end() && it->second.first < best_rank) {
-                    best_rank = it->second.first;
-                    best_id = it->second.second;
-                    best = i;
-                }
-            }
-            if (best == (size_t)-1) break;
-            sym[best] = best_id;
-            sym.erase(sym.begin() + (long)best + 1);
+        // Merges in (rank, position) order through a min-heap of candidate
+        // pairs over a linked list of symbols; an entry whose pair has
+        // changed since it was pushed is skipped.  Positions are the left
+        // symbols' original indices, so "lowest position" is "leftmost".
+        const size_t n = sym.size();
+        std::vector<long> prev(n), next(n);
+        std::vector<uint8_t> alive(n, 1);
+        for (size_t i = 0; i < n; ++i) {
+            prev[i] = (long)i - 1;
+            next[i] = i + 1 < n ? (long)i + 1 : -1;
         }
-        ids.insert(ids.end(), sym.begin(), sym.end());
+        struct Cand {
+            uint32_t rank, new_id;
+            size_t pos;
+            bool operator>(const Cand &o) const { return rank != o.rank ? rank > o.rank : pos > o.pos; }
+        };
+        std::priority_queue<Cand, std::vector<Cand>, std::greater<Cand>> q;
+        auto push = [&](size_t i) {
+            if (next[i] < 0) return;
+            auto it = merges.find((uint64_t)sym[i] << 32 | sym[(size_t)next[i]]);
+            if (it != merges.end()) q.push(Cand{it->second.first, it->second.second, i});
+        };
+        for (size_t i = 0; i + 1 < n; ++i) push(i);
+        while (!q.empty()) {
+            const Cand c = q.top();
+            q.pop();
+            if (!alive[c.pos] || next[c.pos] < 0) continue;
+            const size_t r = (size_t)next[c.pos];
+            auto it = merges.find((uint64_t)sym[c.pos] << 32 | sym[r]);
+            if (it == merges.end() || it->second.second != c.new_id) continue;  // stale entry
+            sym[c.pos] = c.new_id;
+            alive[r] = 0;
+            next[c.pos] = next[r];
+            if (next[r] >= 0) prev[(size_t)next[r]] = (long)c.pos;
+            if (prev[c.pos] >= 0) push((size_t)prev[c.pos]);
+            push(c.pos);
+        }
+        for (size_t i = 0; i < n; ++i)
+            if (alive[i]) ids.push_back(sym[i]);
         return QB_OK;
     }
 

@@ -163,3 +163,16 @@ def test_random_texts_match_hf_tokenizers():
         assert t.decode(got, True) == hf.decode(want, skip_special_tokens=True), (k, text)
         ds, s = tokenizers.decoders.DecodeStream(skip_special_tokens=True), t.text_stream()
         assert [s.push(i) for i in got] == [ds.step(hf, i) for i in want], (k, text)
+
+
+def test_long_word_matches_hf_tokenizers():
+    # One 64,000-character word (the bridge admits 64 KiB of text): the merge
+    # order over a long symbol list equals the library's, in linearithmic
+    # time.
+    tokenizers = pytest.importorskip("tokenizers")
+    import random
+    hf = tokenizers.Tokenizer.from_file(SYN)
+    t = _tok()
+    rng = random.Random(3)
+    word = "".join(rng.choice("abcdefghijklmnopqrstuvwxyzéñ") for _ in range(64000))
+    assert t.encode(word) == hf.encode(word, add_special_tokens=False).ids
