@@ -119,16 +119,18 @@ std::vector<uint32_t> nfc(const std::vector<uint32_t> &in) {
     std::vector<uint32_t> d;
     d.reserve(in.size() + 8);
     for (uint32_t c : in) decompose(c, d);
-    for (size_t i = 1; i < d.size(); ++i) {  // stable insertion sort of each non-starter run by class
-        const uint32_t cc = ccc(d[i]);
-        if (cc == 0) continue;
-        size_t j = i;
-        while (j > 0) {
-            const uint32_t pc = ccc(d[j - 1]);
-            if (pc == 0 || pc <= cc) break;
-            std::swap(d[j - 1], d[j]);
-            --j;
+    // Canonical ordering: each run of non-starters stably sorted by class.
+    for (size_t i = 0; i < d.size();) {
+        if (ccc(d[i]) == 0) {
+            ++i;
+            continue;
         }
+        size_t j = i;
+        while (j < d.size() && ccc(d[j]) != 0) ++j;
+        if (j - i > 1)
+            std::stable_sort(d.begin() + (long)i, d.begin() + (long)j,
+                             [](uint32_t a, uint32_t b) { return ccc(a) < ccc(b); });
+        i = j;
     }
     std::vector<uint32_t> out;
     out.reserve(d.size());
