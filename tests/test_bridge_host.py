@@ -105,3 +105,33 @@ def test_qwen_directory_without_files_fails_on_the_worker(tmp_path):
     st, h = bridge_open(str(tmp_path).encode(), kind=1)
     assert st == OK and bridge_wait(h).code == MODEL_FAILED
     assert L.aie_close(h) == OK
+
+
+def test_malformed_model_files_fail_on_the_worker():
+    # Decoder::from_json's serde rules (src/model.rs:185-189): exact fields,
+    # integer sizes, arrays of numbers, no trailing content.  Each of these
+    # files is refused on the worker (AIE_MODEL_FAILED); all but the one with
+    # non-numeric weights fail while the file is read, before any device work.
+    import json
+    good_cfg = {"vocab_size": 2, "layers": 1, "hidden_dim": 2, "query_heads": 1, "kv_heads": 1, "head_dim": 2,
+                "ff_dim": 2, "max_tokens": 2, "rope_base": 10000.0, "norm_epsilon": 1e-5}
+    bad = [
+        b'{"config": {}, "config": {}, "weights": {}}',                          # duplicate key
+        json.dumps({"config": dict(good_cfg, layers=-1), "weights": {}}).encode(),  # negative size
+        json.dumps({"config": dict(good_cfg, layers=1.5), "weights": {}}).encode(),  # fractional size
+        json.dumps({"config": dict(good_cfg, rope_base="x"), "weights": {}}).encode(),  # wrong type
+        json.dumps({"config": good_cfg}).encode(),                                   # missing weights
+        json.dumps({"config": good_cfg, "weights": {"embedding": [0.0], "layers": 3,
+                                                    "final_norm": [1.0]}}).encode(),  # layers not a list
+        json.dumps({"config": good_cfg, "weights": {"embedding": ["a"], "layers": [],
+                                                    "final_norm": [1.0]}}).encode(),  # not numbers
+        b'{"config": {}, "weights": {}} trailing',                                   # trailing content
+        b"[" * 100 + b"]" * 100,                                                     # nesting too deep
+    ]
+    L = lib()
+    for src in bad:
+        st, h = bridge_open(src)
+        assert st == OK, src
+        ev = bridge_wait(h)
+        assert (ev.kind, ev.code) == (ERROR, MODEL_FAILED), src
+        assert L.aie_close(h) == OK
